@@ -1,0 +1,317 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 hot path: ocrs page detection (benchmark config 1), pages/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--pages B] [--impl b200|reference]
+
+A step is one pass of the detection hot path (RGB page -> grey/pad/resize -> U-Net -> mask
+resize/threshold/bit-pack, `Detector::detect_page`, src/gpu.rs:1393-1422) over a batch of B
+synthetic 2550 x 3300 pages per GPU.  Pages shard across GPUs with no collective (weak scaling):
+one process per GPU (torchrun), timed on the device with CUDA events, max over ranks.
+
+  value  - pages/s with the pages already in HBM (B pages = 303 MB > L2 per step)
+  e2e    - pages/s through the public API (`wocr_detect_pages`) from pinned host memory, the
+           host->device copy of the pages and the device->host copy of the masks inside the
+           timed region
+  roofline - the kernel with the largest share of device time, from a CUDA-event profile of the
+           same workload: algorithmic FLOPs (or bytes) per launch / its mean launch time
+  cpu_baseline - the CPU oracle (a C restatement of the reference's arithmetic, OpenMP) on a
+           bounded sample of pages, on this host's cores
+
+`--impl reference` times the reference's CPU implementation stand-in (the oracle; the reference
+itself is Rust + wgpu and cannot run here) on the same workload, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "wgpu-ocr_b200"))
+
+W_PAGE, H_PAGE = 2550, 3300
+THRESHOLD = 0.5
+WORKLOAD = "config 1: ocrs detection U-Net (16/32/64/128 ch, 800x600 model input, He-normal seed 1), " \
+           "2550x3300 RGB u8 synthetic pages, threshold 0.5, bit-mask output"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--pages", type=int, default=12, help="pages per GPU per step")
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
+    return p.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(path))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = "index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, bus_id: str | None):
+        self.bus = (bus_id or "").lower()
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = [r.split(", ") for r in self.lines if r]
+        mine = [r for r in rows if len(r) >= 10 and self.bus and self.bus.endswith(r[1].lower()[-12:])] or \
+               [r for r in rows if len(r) >= 10 and r[0] == "0"]
+        sm = sorted(float(r[2]) for r in mine if r[2].replace(".", "").isdigit())
+        mx = max((float(r[3]) for r in mine if r[3].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in mine for i in range(4) if r[6 + i].strip().lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(sm)}
+
+
+def dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def make_pages(rank: int, n: int):
+    import numpy as np
+    from wocr import synth
+    return np.stack([synth.page(1000 * (rank + 1) + k, W_PAGE, H_PAGE) for k in range(n)])
+
+
+def cpu_baseline(sample: int):
+    """The oracle on `sample` pages with all host threads: pages/s."""
+    from oracle import ref
+    from wocr import synth
+    m = synth.ocrs_det_model()
+    pgs = [synth.page(7000 + k, W_PAGE, H_PAGE) for k in range(sample + 1)]
+    ref.set_threads(os.cpu_count() or 1)
+    ref.detect_page(m, pgs[0], THRESHOLD)            # warm-up (library load, page-in)
+    t0 = time.perf_counter()
+    for p in pgs[1:]:
+        ref.detect_page(m, p, THRESHOLD)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "pages/s", "cores": ref.threads(), "kind": "port",
+            "sample": f"{sample} pages of config 1 through the C oracle (grey/resize, U-Net, mask), "
+                      f"{dt:.2f} s"}
+
+
+def run_reference(args):
+    world, rank, _ = dist()
+    if rank != 0:
+        return 0
+    from oracle import ref
+    from wocr import synth
+    m = synth.ocrs_det_model()
+    page = synth.page(7000, W_PAGE, H_PAGE)
+    ref.set_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        ref.detect_page(m, page, THRESHOLD)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        ref.detect_page(m, page, THRESHOLD)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    line = {"impl": "reference", "metric": "pages/s", "value": v, "unit": "pages/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "step": "1 page per step (bounded CPU sample)",
+                       "parallelism": "host threads"},
+            "cpu_baseline": {"value": v, "unit": "pages/s", "cores": ref.threads(), "kind": "port",
+                             "sample": "1 page per step through the C oracle (the reference is Rust + wgpu over "
+                                       "Vulkan and cannot run here)"},
+            "e2e": {"value": v, "unit": "pages/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args):
+    import numpy as np
+    import torch
+    import torch.distributed as tdist
+
+    import wocr
+    from wocr import synth
+
+    world, rank, local = dist()
+    if world > 1:
+        from datetime import timedelta
+        tdist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B = args.pages
+    words = (W_PAGE + 31) // 32
+
+    gpu = wocr.Gpu(lines=8, device=local)
+    det = wocr.Detector(gpu, synth.ocrs_det_model())
+    host_pages = make_pages(rank, B)
+    d_rgb = torch.from_numpy(host_pages).to(dev)
+    d_mask = torch.empty(B * H_PAGE * words, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.ExternalStream(gpu.stream, device=dev)
+
+    def step():
+        det.detect_pages_device(d_rgb.data_ptr(), B, W_PAGE, H_PAGE, THRESHOLD, d_mask.data_ptr())
+
+    def barrier():
+        if world > 1:
+            tdist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident throughput --------------------------------------------------
+    for _ in range(max(args.warmup, 3)):
+        step()
+    gpu.submit_wait()
+    barrier()
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+    except Exception:
+        bus = None
+    clocks = Clocks(bus)
+    clocks.start()
+    l0 = gpu.launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    launches = gpu.launches() - l0
+    clk = clocks.stop()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    value = world * B * args.steps / (ms / 1e3)
+
+    # ---- per-kernel profile of the same workload (separate pass) -----------------------
+    psteps = min(args.steps, 5)
+    gpu.profile(True)
+    for _ in range(psteps):
+        step()
+    rep = gpu.profile_report()
+    gpu.profile(False)
+    total_ms = sum(r["ms"] for r in rep) or 1.0
+    top = max(rep, key=lambda r: r["ms"])
+    pk = peaks()
+    per_launch_ms = top["ms"] / top["launches"]
+    if top["flops"] > 0:
+        achieved = (top["flops"] / top["launches"]) / (per_launch_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / pk["bf16_tflops"]}
+    else:
+        achieved = (top["bytes"] / top["launches"]) / (per_launch_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"]}
+    roof.update({"kernel": top["kernel"], "share": top["ms"] / total_ms, "traffic": None,
+                 "peak_source": pk["src"] + (" (dense bf16 cuBLAS burst)" if roof["bound"] == "tensor" else
+                                             " (copy bandwidth)")})
+    kernels = {r["kernel"]: {"launches": r["launches"] // psteps, "ms_per_step": r["ms"] / psteps,
+                             "share": r["ms"] / total_ms} for r in rep}
+
+    # ---- end to end through the public API, pinned host buffers -------------------------
+    import ctypes
+    nbytes = host_pages.nbytes
+    hp = ctypes.c_void_p()
+    wocr.lib().wocr_host_alloc(nbytes, ctypes.byref(hp))
+    hm = ctypes.c_void_p()
+    mbytes = B * H_PAGE * words * 4
+    wocr.lib().wocr_host_alloc(mbytes, ctypes.byref(hm))
+    ctypes.memmove(hp.value, host_pages.ctypes.data, nbytes)
+
+    def e2e_step():
+        wocr._lib.check(wocr.lib().wocr_detect_pages(det.h, hp, B, W_PAGE, H_PAGE, THRESHOLD, hm))
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    wall = time.perf_counter() - t0
+    ems = max_over_ranks(max(e0.elapsed_time(e1), 1e3 * wall))
+    e2e = {"value": world * B * args.steps / (ems / 1e3), "unit": "pages/s", "h2d_bytes_per_step": int(nbytes),
+           "d2h_bytes_per_step": int(mbytes)}
+    wocr.lib().wocr_host_free(hp)
+    wocr.lib().wocr_host_free(hm)
+
+    cpu = None
+    if rank == 0 and world == 1:
+        cpu = cpu_baseline(args.cpu_sample)
+
+    flops_step, _ = det.stats()
+    if rank == 0:
+        line = {"metric": "pages/s", "value": value, "unit": "pages/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "pages_per_gpu_per_step": B, "global_batch": B * world,
+                           "parallelism": f"pages sharded over {world} GPU(s), no collective",
+                           "l2": f"inputs {B * W_PAGE * H_PAGE * 3 / 1e6:.0f} MB per GPU per step > 126 MB L2"},
+                "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu,
+                "clocks": clk, "kernels": kernels,
+                "algorithmic_gflop_per_page": det.stats()[0] / B / 1e9 if flops_step else None}
+        print(json.dumps(line), flush=True)
+    det.close()
+    gpu.close()
+    if world > 1:
+        tdist.barrier(device_ids=[local])
+        tdist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_b200(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,207 @@
+/*
+ * wocr: the inference hot path of huppiflupp/wgpu-ocr (ocrs detector + GRU recogniser, PP-OCR
+ * N-D graph executor) as hand-written CUDA for B200 (sm_100a), behind a plain C ABI.
+ *
+ * Every entry point mirrors a public function of the reference crate (paths are inside the
+ * reference repository).  The reference is Rust; its functions return Result<T, String>.  Here
+ * each call returns a status code (WOCR_OK = 0) and the message of the last failure on the
+ * calling thread is available from wocr_last_error().  Nothing panics or aborts across the ABI.
+ *
+ * Threading: one wocr_ctx is used by one host thread at a time (the reference's Gpu is not Sync,
+ * src/gpu.rs:835-839).  Different contexts, on the same or different GPUs, run concurrently.
+ * Ownership: all host buffers are the caller's; weights are copied in at create time, so the
+ * caller may free its model description right after a *_create call returns.
+ */
+#ifndef WOCR_H
+#define WOCR_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------------------- */
+enum {
+    WOCR_OK = 0,
+    WOCR_ERR_INVALID = 1,     /* bad argument (null pointer, size out of range)            */
+    WOCR_ERR_UNSUPPORTED = 2, /* op or attribute the executor does not implement, as the
+                                 reference's "unsupported op" errors, src/gpu.rs:1137-1226,
+                                 src/nd.rs:1165                                             */
+    WOCR_ERR_SHAPE = 3,       /* shapes that do not fit (src/gpu.rs:1322, src/nd.rs:1287)  */
+    WOCR_ERR_OOM = 4,         /* device or pinned host allocation failed                   */
+    WOCR_ERR_CUDA = 5,        /* a CUDA runtime error                                      */
+    WOCR_ERR_TIMEOUT = 6,     /* a bounded wait gave up                                    */
+    WOCR_ERR_MISSING = 7,     /* a value or weight the graph names does not exist          */
+    WOCR_ERR_CAPACITY = 8     /* an output buffer given by the caller is too small         */
+};
+
+/* The message of the last failing call on this thread ("" if none). */
+const char *wocr_last_error(void);
+
+/* ---- model description: the loaded ONNX graph --------------------------------------------
+ * Mirrors `Onnx` (src/onnx.rs:44-56, filled by Onnx::load src/onnx.rs:88-123): the node list
+ * in graph order, float initializers, int64 constants, the graph input and output names.
+ * `Constant` nodes are expected already turned into initializers, as Onnx::load does.      */
+enum { WOCR_ATTR_INT = 1, WOCR_ATTR_FLOAT = 2, WOCR_ATTR_STRING = 3, WOCR_ATTR_INTS = 4, WOCR_ATTR_FLOATS = 5 };
+
+typedef struct {
+    const char *name;
+    int32_t kind;         /* WOCR_ATTR_*                                                  */
+    int64_t i;            /* WOCR_ATTR_INT                                                */
+    float f;              /* WOCR_ATTR_FLOAT                                              */
+    const char *s;        /* WOCR_ATTR_STRING                                             */
+    const int64_t *ints;  /* WOCR_ATTR_INTS, `count` values                               */
+    const float *floats;  /* WOCR_ATTR_FLOATS, `count` values                             */
+    int64_t count;
+} wocr_attr;
+
+typedef struct {
+    const char *op;                   /* ONNX op_type                                     */
+    const char *const *inputs;        /* value names ("" for an omitted optional input)    */
+    int32_t n_inputs;
+    const char *const *outputs;
+    int32_t n_outputs;
+    const wocr_attr *attrs;
+    int32_t n_attrs;
+} wocr_node;
+
+/* dtype: 1 = float32, 7 = int64 (ONNX TensorProto codes, src/onnx.rs:58-59). */
+typedef struct {
+    const char *name;
+    int32_t dtype;
+    const int64_t *dims;
+    int32_t rank;
+    const void *data;                 /* prod(dims) values of `dtype`                      */
+} wocr_initializer;
+
+typedef struct {
+    const wocr_node *nodes;
+    int32_t n_nodes;
+    const wocr_initializer *inits;
+    int32_t n_inits;
+    const char *input;                /* first non-initializer graph input (onnx.rs:119)    */
+    const char *output;               /* first graph output (onnx.rs:120)                   */
+} wocr_model;
+
+/* ---- device context: `Gpu` (src/gpu.rs:825-1056) -------------------------------------- */
+typedef struct wocr_ctx wocr_ctx;
+
+/* Gpu::new(lines) src/gpu.rs:850: `lines` = lines per GRU recurrence group (LINES, default 8,
+ * src/bin/ocr-bench.rs:135).  `device` = CUDA ordinal. */
+int32_t wocr_ctx_create(int32_t device, int32_t lines, wocr_ctx **out);
+void wocr_ctx_destroy(wocr_ctx *ctx);
+/* Device name and capability, as Gpu::adapter (src/gpu.rs:915). */
+int32_t wocr_ctx_describe(wocr_ctx *ctx, char *buf, int32_t cap);
+/* The CUDA stream (cudaStream_t) all work of this context runs on, as an opaque pointer. */
+void *wocr_ctx_stream(wocr_ctx *ctx);
+/* Wait for all queued work (Gpu::submit_wait, src/gpu.rs:1005-1008), bounded by timeout_ms
+ * (<= 0: no bound).  WOCR_ERR_TIMEOUT when the bound is reached. */
+int32_t wocr_ctx_sync(wocr_ctx *ctx, int32_t timeout_ms);
+/* Device bytes held by the context's pool (Gpu::pool_bytes, src/gpu.rs:840-845). */
+int64_t wocr_ctx_pool_bytes(wocr_ctx *ctx);
+/* Number of kernels this context has launched since creation (instrumentation). */
+int64_t wocr_ctx_launches(wocr_ctx *ctx);
+/* Per-kernel timing (the reference's OPPROFILE/NDPROFILE timers, src/gpu.rs:1247-1368,
+ * src/nd.rs:18-27, but with CUDA events on the context stream instead of a wait after every
+ * node).  on != 0 starts recording (clearing earlier records), 0 stops. */
+int32_t wocr_ctx_profile(wocr_ctx *ctx, int32_t on);
+/* Waits for the recorded launches and writes a JSON array of
+ * {"kernel", "launches", "ms", "flops", "bytes"} per kernel name into buf (capacity cap). */
+int32_t wocr_ctx_profile_report(wocr_ctx *ctx, char *buf, int32_t cap);
+/* Page-locked host memory for fast copies (the caller's staging buffers). */
+int32_t wocr_host_alloc(size_t bytes, void **out);
+void wocr_host_free(void *p);
+
+/* ---- ocrs detector: `Detector` (src/gpu.rs:1380-1431) --------------------------------- */
+typedef struct wocr_detector wocr_detector;
+
+/* Detector::new (src/gpu.rs:1384-1387): the whole model lowered by Graph::build
+ * (src/gpu.rs:1104-1240). */
+int32_t wocr_detector_create(wocr_ctx *ctx, const wocr_model *model, wocr_detector **out);
+void wocr_detector_destroy(wocr_detector *det);
+
+/* Detector::detect_page (src/gpu.rs:1393-1422): packed RGB bytes of a w x h page in, the
+ * thresholded bit mask out: h rows of ceil(w / 32) words, bit b of word wx = pixel 32 wx + b. */
+int32_t wocr_detect_page(wocr_detector *det, const uint8_t *rgb, int32_t w, int32_t h, float threshold,
+                         uint32_t *mask_out);
+
+/* Detector::detect (src/gpu.rs:1425-1430): the model output of a [1, 1, h, w] input, copied to
+ * prob_out (capacity `cap` floats; nullable to query the size), its height and width to
+ * out_h / out_w. */
+int32_t wocr_detect(wocr_detector *det, const float *input, int32_t h, int32_t w, float *prob_out, int64_t cap,
+                    int32_t *out_h, int32_t *out_w);
+
+/* Several pages of one size in one pass (the model runs with batch n): `rgb` holds n pages
+ * back to back, `mask_out` n masks back to back.  B200 batching of detect_page. */
+int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int32_t w, int32_t h,
+                          float threshold, uint32_t *mask_out);
+
+/* The same on device memory, queued on the context stream without waiting: `d_rgb` and
+ * `d_mask_out` are device pointers. */
+int32_t wocr_detect_pages_device(wocr_detector *det, const uint8_t *d_rgb, int32_t n, int32_t w,
+                                 int32_t h, float threshold, uint32_t *d_mask_out);
+
+/* ---- ocrs recogniser: `Recognizer` (src/gpu.rs:1433-1603) ----------------------------- */
+typedef struct wocr_recognizer wocr_recognizer;
+
+/* Recognizer::new (src/gpu.rs:1452-1506): trunk up to the AveragePool, two bidirectional GRU
+ * layers (hidden 256, linear_before_reset = 1), MatMul + bias Add output layer. */
+int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t lines, wocr_recognizer **out);
+void wocr_recognizer_destroy(wocr_recognizer *rec);
+
+/* Output dimensions of a wocr_recognize call on these batches (without running it). */
+int32_t wocr_recognizer_dims(wocr_recognizer *rec, const int32_t *batch_n, const int32_t *batch_w,
+                             int32_t n_batches, int32_t *tmax, int32_t *ntot, int32_t *classes);
+
+/* Recognizer::recognize (src/gpu.rs:1510-1602).  Batch b is batch_n[b] line images of
+ * 1 x 64 x batch_w[b] floats at batches[b].  Outputs, each nullable:
+ *   logits [tmax][ntot][classes] (rows t >= lens[line] are unspecified, as in the reference),
+ *   lens   [ntot] (each line's sequence length = its batch's trunk width),
+ *   best   [tmax][ntot] arg-max class per step (ties -> the last index, as Rust's max_by),
+ * and tmax.  `logits_cap` = capacity of `logits` in floats. */
+int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const int32_t *batch_n,
+                       const int32_t *batch_w, int32_t n_batches, float *logits, int64_t logits_cap,
+                       int32_t *lens, uint32_t *best, int32_t *tmax_out);
+
+/* ---- N-D graph executor: `NdGraph` (src/nd.rs:428-1394) -------------------------------- */
+typedef struct wocr_ndgraph wocr_ndgraph;
+
+/* NdGraph::new (src/nd.rs:505-817), with the same load-time fusions. */
+int32_t wocr_ndgraph_create(wocr_ctx *ctx, const wocr_model *model, int32_t stop_before_softmax,
+                            wocr_ndgraph **out);
+void wocr_ndgraph_destroy(wocr_ndgraph *g);
+
+/* NdGraph::run (src/nd.rs:834-1195) on a host tensor; the output is copied to `out`
+ * (capacity `out_cap` floats), its shape to out_shape[0..*out_rank) (capacity 6). */
+int32_t wocr_ndgraph_run(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank, float *out,
+                         int64_t out_cap, int64_t *out_shape, int32_t *out_rank);
+
+/* NdGraph::run + NdGraph::argmax (src/nd.rs:1383-1393): the arg-max over the last axis of the
+ * output per row (ties -> the lowest index).  Optionally (nullable) the row maximum and
+ * log-sum-exp, so that the softmax probability of the chosen class is exp(max - lse).
+ * rows_out = number of rows; `cap` = capacity of each output array. */
+int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank,
+                                uint32_t *best, float *row_max, float *row_lse, int64_t cap,
+                                int64_t *rows_out, int64_t *out_shape, int32_t *out_rank);
+
+/* NdGraph::det_input (src/nd.rs:1353-1369): the PP-OCR detection input of an RGB page,
+ * [1, 3, oh, ow] planar floats, sized as ppdet::det_input (src/ppdet.rs:29-33). */
+int32_t wocr_det_input(wocr_ctx *ctx, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, float *out,
+                       int64_t out_cap, int32_t *ow, int32_t *oh, float *to_page);
+
+/* The PP-OCR detection pass of the reference's GPU thread (src/bin/ocr-bench.rs:186-200):
+ * det_input + NdGraph::run on the page, probability map [oh][ow] read back. */
+int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side,
+                        float *prob, int64_t prob_cap, int32_t *ow, int32_t *oh, float *to_page);
+
+/* Algorithmic work of the last run of a graph handle (detector, recogniser or N-D graph):
+ * floating-point operations of its convolutions and matrix products (2 per multiply-add)
+ * and the launch count. */
+int32_t wocr_last_run_stats(void *handle, int32_t kind, double *flops, int64_t *launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WOCR_H */

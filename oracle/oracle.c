@@ -1,0 +1,476 @@
+/*
+ * CPU oracle for the wgpu-ocr inference hot path -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement (fp32 storage, fp32 arithmetic, NCHW layout) of the arithmetic of the
+ * reference's WGSL kernels and of the ONNX operator semantics its executors implement.  Each
+ * function cites the reference code it follows (paths inside huppiflupp/wgpu-ocr).  Only the
+ * tests, the smoke check and the benchmark's CPU-baseline leg may load this library; the
+ * product path (the CUDA library) never does.
+ *
+ * Parity pinning: the reference ships no golden vectors and cannot run here (Rust + wgpu over a
+ * graphics API; its rten CPU path is an un-vendored crates.io dependency, rten =0.26.0).  The
+ * oracle is therefore "parity unpinned" against the reference itself; it is cross-checked
+ * against an independent implementation (PyTorch CPU: conv2d, conv_transpose2d, max/avg pool,
+ * nn.GRU, layer_norm, softmax) in tests/test_oracle.py.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* Abramowitz & Stegun 7.1.26 erf, as the reference's kernels compute it
+ * (src/gpu.rs:19-27, src/nd.rs:70-76). */
+static float erf_as(float v) {
+    float s = (v > 0.f) - (v < 0.f);
+    float a = fabsf(v);
+    float t = 1.0f / (1.0f + 0.3275911f * a);
+    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    return s * (1.0f - poly * expf(-a * a));
+}
+
+/* Activation codes of the reference's epilogue (src/gpu.rs:28-34):
+ * 0 none, 1 Relu, 2 Sigmoid, 3 GELU (erf form), 4 SiLU. */
+static float act_f(float v, int act) {
+    switch (act) {
+    case 1: return v > 0.f ? v : 0.f;
+    case 2: return 1.0f / (1.0f + expf(-v));
+    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
+    case 4: return v / (1.0f + expf(-v));
+    default: return v;
+    }
+}
+
+float oracle_erf(float v) { return erf_as(v); }
+float oracle_act(float v, int act) { return act_f(v, act); }
+
+void oracle_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+int oracle_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
+
+/*
+ * Dense or grouped convolution, zero padding (pt, pl leading; pb, pr trailing), strides
+ * (sh, sw), weights in ONNX order [cout][cin/group][kh][kw].  Epilogue as the reference's
+ * `put` (src/gpu.rs:58-73): act(acc + b) then + res when given.  `insc` [n][cin] scales the
+ * input before the multiply (squeeze-excitation input scale, src/gpu.rs:95-97, src/nd.rs:552-571).
+ * Output size (h + pt + pb - kh) / sh + 1 (src/nd.rs:1279-1280).
+ */
+void oracle_conv2d(const float *x, int n, int cin, int h, int w,
+                   const float *wt, const float *b, int cout, int group, int kh, int kw,
+                   int sh, int sw, int pt, int pl, int pb, int pr, int act,
+                   const float *res, const float *insc, float *y) {
+    int oh = (h + pt + pb - kh) / sh + 1;
+    int ow = (w + pl + pr - kw) / sw + 1;
+    int cin_g = cin / group, cout_g = cout / group;
+    long plane = (long)h * w, oplane = (long)oh * ow;
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int nb = 0; nb < n; nb++) {
+        for (int co = 0; co < cout; co++) {
+            float *yp = y + ((long)nb * cout + co) * oplane;
+            float bias = b ? b[co] : 0.f;
+            for (long i = 0; i < oplane; i++) yp[i] = 0.f;
+            int g = co / cout_g;
+            for (int cg = 0; cg < cin_g; cg++) {
+                int ci = g * cin_g + cg;
+                const float *xp = x + ((long)nb * cin + ci) * plane;
+                float sc = insc ? insc[(long)nb * cin + ci] : 1.f;
+                for (int ky = 0; ky < kh; ky++) {
+                    for (int kx = 0; kx < kw; kx++) {
+                        float wv = wt[(((long)co * cin_g + cg) * kh + ky) * kw + kx];
+                        /* ox range with 0 <= ox*sw + kx - pl < w */
+                        int ox0 = 0, ox1 = ow;
+                        while (ox0 < ow && ox0 * sw + kx - pl < 0) ox0++;
+                        while (ox1 > ox0 && (ox1 - 1) * sw + kx - pl >= w) ox1--;
+                        for (int oy = 0; oy < oh; oy++) {
+                            int iy = oy * sh + ky - pt;
+                            if (iy < 0 || iy >= h) continue;
+                            const float *xr = xp + (long)iy * w + kx - pl;
+                            float *yr = yp + (long)oy * ow;
+                            if (insc) {
+                                for (int ox = ox0; ox < ox1; ox++) yr[ox] += (xr[ox * sw] * sc) * wv;
+                            } else if (sw == 1) {
+                                for (int ox = ox0; ox < ox1; ox++) yr[ox] += xr[ox] * wv;
+                            } else {
+                                for (int ox = ox0; ox < ox1; ox++) yr[ox] += xr[ox * sw] * wv;
+                            }
+                        }
+                    }
+                }
+            }
+            const float *rp = res ? res + ((long)nb * cout + co) * oplane : NULL;
+            for (long i = 0; i < oplane; i++) {
+                float r = act_f(yp[i] + bias, act);
+                if (rp) r += rp[i];
+                yp[i] = r;
+            }
+        }
+    }
+}
+
+/*
+ * ConvTranspose, group 1, no pads/output_padding: out (h - 1) * s + k (src/gpu.rs:424-460,
+ * src/nd.rs:874-886).  Weights [cin][cout][kh][kw]; y = act(b + sum of the taps).
+ */
+void oracle_convt(const float *x, int n, int cin, int h, int w, const float *wt, const float *b,
+                  int cout, int kh, int kw, int s, int act, float *y) {
+    int oh = (h - 1) * s + kh, ow = (w - 1) * s + kw;
+    long plane = (long)h * w, oplane = (long)oh * ow;
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int nb = 0; nb < n; nb++) {
+        for (int co = 0; co < cout; co++) {
+            float *yp = y + ((long)nb * cout + co) * oplane;
+            for (long i = 0; i < oplane; i++) yp[i] = 0.f;
+            for (int ci = 0; ci < cin; ci++) {
+                const float *xp = x + ((long)nb * cin + ci) * plane;
+                for (int ky = 0; ky < kh; ky++)
+                    for (int kx = 0; kx < kw; kx++) {
+                        float wv = wt[(((long)ci * cout + co) * kh + ky) * kw + kx];
+                        for (int iy = 0; iy < h; iy++) {
+                            float *yr = yp + (long)(iy * s + ky) * ow + kx;
+                            const float *xr = xp + (long)iy * w;
+                            for (int ix = 0; ix < w; ix++) yr[ix * s] += xr[ix] * wv;
+                        }
+                    }
+            }
+            float bias = b ? b[co] : 0.f;
+            for (long i = 0; i < oplane; i++) yp[i] = act_f(yp[i] + bias, act);
+        }
+    }
+}
+
+/*
+ * Max or average pooling with strides and leading padding; padding is never counted
+ * (src/nd.rs:246-275, 1319-1349).  The ocrs MaxPool (kernel = stride, no pad, src/gpu.rs:462-482)
+ * is the special case pt = pl = 0, sh = kh, sw = kw.  oh, ow given by the caller.
+ */
+void oracle_pool(const float *x, int nc, int h, int w, int oh, int ow, int kh, int kw, int sh, int sw,
+                 int pt, int pl, int avg, float *y) {
+#pragma omp parallel for schedule(static)
+    for (int c = 0; c < nc; c++) {
+        for (int oy = 0; oy < oh; oy++)
+            for (int ox = 0; ox < ow; ox++) {
+                float m = -3.4e38f, s = 0.f, cnt = 0.f;
+                for (int ky = 0; ky < kh; ky++) {
+                    int iy = oy * sh + ky - pt;
+                    if (iy < 0 || iy >= h) continue;
+                    for (int kx = 0; kx < kw; kx++) {
+                        int ix = ox * sw + kx - pl;
+                        if (ix < 0 || ix >= w) continue;
+                        float v = x[((long)c * h + iy) * w + ix];
+                        m = v > m ? v : m;
+                        s += v;
+                        cnt += 1.f;
+                    }
+                }
+                y[((long)c * oh + oy) * ow + ox] = avg ? s / (cnt > 1.f ? cnt : 1.f) : m;
+            }
+    }
+}
+
+/* Linear interpolation as WGSL `mix(a, b, t)` = a * (1 - t) + b * t. */
+static inline float mixf(float a, float b, float t) { return a * (1.0f - t) + b * t; }
+
+static inline float byte_at(const uint8_t *rgb, long i) { return (float)rgb[i]; }
+
+/* ocrs grey value of page pixel (x, y), -0.5 outside the page (src/gpu.rs:537-542). */
+static inline float grey_px(const uint8_t *rgb, int w, int h, int x, int yy) {
+    if (x >= w || yy >= h) return -0.5f;
+    long i = ((long)yy * w + x) * 3;
+    return -0.5f + byte_at(rgb, i) * (0.299f / 255.0f) + byte_at(rgb, i + 1) * (0.587f / 255.0f) +
+           byte_at(rgb, i + 2) * (0.114f / 255.0f);
+}
+
+/*
+ * Detector input: RGB page -> ocrs grey, padded with -0.5 to (ph, pw) = (max(h, oh), max(w, ow)),
+ * half-pixel bilinear resize (clamped, x then y) to oh x ow (src/gpu.rs:530-561, 1394-1411).
+ */
+void oracle_grey_resize(const uint8_t *rgb, int w, int h, int ow, int oh, float *y) {
+    int ph = h > oh ? h : oh, pw = w > ow ? w : ow;
+    float sx = (float)pw / (float)ow, sy = (float)ph / (float)oh;
+#pragma omp parallel for schedule(static)
+    for (int oy = 0; oy < oh; oy++) {
+        for (int ox = 0; ox < ow; ox++) {
+            float iy = sy * ((float)oy + 0.5f) - 0.5f;
+            float ix = sx * ((float)ox + 0.5f) - 0.5f;
+            iy = iy < 0.f ? 0.f : (iy > (float)ph - 1.f ? (float)ph - 1.f : iy);
+            ix = ix < 0.f ? 0.f : (ix > (float)pw - 1.f ? (float)pw - 1.f : ix);
+            int y1 = (int)iy, x1 = (int)ix;
+            int y2 = y1 + 1 < ph - 1 ? y1 + 1 : ph - 1;
+            int x2 = x1 + 1 < pw - 1 ? x1 + 1 : pw - 1;
+            float wy = iy - (float)y1, wx = ix - (float)x1;
+            float top = mixf(grey_px(rgb, w, h, x1, y1), grey_px(rgb, w, h, x2, y1), wx);
+            float bot = mixf(grey_px(rgb, w, h, x1, y2), grey_px(rgb, w, h, x2, y2), wx);
+            y[(long)oy * ow + ox] = mixf(top, bot, wy);
+        }
+    }
+}
+
+/*
+ * Detector output: the valid vh x vw part of the model's map (row stride `stride`), half-pixel
+ * bilinear to the page (w x h), `> thr`, 32 pixels to a word, bit b = pixel 32 * wx + b
+ * (src/gpu.rs:563-593, 1414-1418).  `prob` (nullable) receives the page-level interpolated
+ * probabilities [h][w], for the threshold tie band of the parity tests.
+ */
+void oracle_mask_up(const float *m, int stride, int vw, int vh, int w, int h, float thr,
+                    uint32_t *bits, float *prob) {
+    int words = (w + 31) / 32;
+    float sx = (float)vw / (float)w, sy = (float)vh / (float)h;
+#pragma omp parallel for schedule(static)
+    for (int oy = 0; oy < h; oy++) {
+        float iy = sy * ((float)oy + 0.5f) - 0.5f;
+        iy = iy < 0.f ? 0.f : (iy > (float)vh - 1.f ? (float)vh - 1.f : iy);
+        int y1 = (int)iy;
+        int y2 = y1 + 1 < vh - 1 ? y1 + 1 : vh - 1;
+        float fy = iy - (float)y1;
+        for (int wx = 0; wx < words; wx++) {
+            uint32_t v = 0;
+            for (int b = 0; b < 32; b++) {
+                int ox = wx * 32 + b;
+                if (ox >= w) break;
+                float ix = sx * ((float)ox + 0.5f) - 0.5f;
+                ix = ix < 0.f ? 0.f : (ix > (float)vw - 1.f ? (float)vw - 1.f : ix);
+                int x1 = (int)ix;
+                int x2 = x1 + 1 < vw - 1 ? x1 + 1 : vw - 1;
+                float fx = ix - (float)x1;
+                float top = mixf(m[(long)y1 * stride + x1], m[(long)y1 * stride + x2], fx);
+                float bot = mixf(m[(long)y2 * stride + x1], m[(long)y2 * stride + x2], fx);
+                float p = mixf(top, bot, fy);
+                if (prob) prob[(long)oy * w + ox] = p;
+                if (p > thr) v |= 1u << b;
+            }
+            bits[(long)oy * words + wx] = v;
+        }
+    }
+}
+
+/*
+ * PP-OCR detection input: RGB page -> half-pixel bilinear to ow x oh (clamped), BGR planes,
+ * (v / 255 - mean) / std with the ImageNet constants (src/nd.rs:172-204, 1353-1369).
+ */
+void oracle_det_prep(const uint8_t *rgb, int w, int h, int ow, int oh, float *y) {
+    const float mean[3] = {0.485f, 0.456f, 0.406f};
+    const float dev[3] = {0.229f, 0.224f, 0.225f};
+    float sx = (float)w / (float)ow, sy = (float)h / (float)oh;
+#pragma omp parallel for schedule(static)
+    for (int oy = 0; oy < oh; oy++) {
+        for (int ox = 0; ox < ow; ox++) {
+            float ix = sx * ((float)ox + 0.5f) - 0.5f;
+            float iy = sy * ((float)oy + 0.5f) - 0.5f;
+            ix = ix < 0.f ? 0.f : (ix > (float)w - 1.f ? (float)w - 1.f : ix);
+            iy = iy < 0.f ? 0.f : (iy > (float)h - 1.f ? (float)h - 1.f : iy);
+            int x1 = (int)ix, y1 = (int)iy;
+            int x2 = x1 + 1 < w - 1 ? x1 + 1 : w - 1;
+            int y2 = y1 + 1 < h - 1 ? y1 + 1 : h - 1;
+            float fx = ix - (float)x1, fy = iy - (float)y1;
+            for (int c = 0; c < 3; c++) {
+                int k = 2 - c; /* BGR: output channel 0 is blue, byte 2 */
+                float a = mixf(byte_at(rgb, ((long)y1 * w + x1) * 3 + k), byte_at(rgb, ((long)y1 * w + x2) * 3 + k), fx);
+                float bb = mixf(byte_at(rgb, ((long)y2 * w + x1) * 3 + k), byte_at(rgb, ((long)y2 * w + x2) * 3 + k), fx);
+                y[((long)c * oh + oy) * ow + ox] = (mixf(a, bb, fy) / 255.0f - mean[c]) / dev[c];
+            }
+        }
+    }
+}
+
+/* Nearest Resize, asymmetric, floor: in = min(floor(out / scale), size - 1) (src/nd.rs:155-170). */
+void oracle_resize_nearest(const float *x, int nc, int h, int w, int oh, int ow, float sy, float sx,
+                           float *y) {
+#pragma omp parallel for schedule(static)
+    for (int c = 0; c < nc; c++)
+        for (int oy = 0; oy < oh; oy++) {
+            int iy = (int)floorf((float)oy / sy);
+            if (iy > h - 1) iy = h - 1;
+            for (int ox = 0; ox < ow; ox++) {
+                int ix = (int)floorf((float)ox / sx);
+                if (ix > w - 1) ix = w - 1;
+                y[((long)c * oh + oy) * ow + ox] = x[((long)c * h + iy) * w + ix];
+            }
+        }
+}
+
+/*
+ * y[m, k] = x[m, :] . wt[:, k] + b[k], wt stored [i][k] (src/gpu.rs:616-678); with act
+ * (src/nd.rs:291-358 with zero batch strides).
+ */
+void oracle_gemm(const float *x, const float *wt, const float *b, int m, int k, int i, int act, float *y) {
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < m; r++) {
+        float *yr = y + (long)r * k;
+        for (int c = 0; c < k; c++) yr[c] = 0.f;
+        for (int j = 0; j < i; j++) {
+            float xv = x[(long)r * i + j];
+            const float *wr = wt + (long)j * k;
+            for (int c = 0; c < k; c++) yr[c] += xv * wr[c];
+        }
+        for (int c = 0; c < k; c++) yr[c] = act_f(yr[c] + (b ? b[c] : 0.f), act);
+    }
+}
+
+static inline float sigm(float v) { return 1.0f / (1.0f + expf(-v)); }
+
+/*
+ * ONNX GRU, linear_before_reset = 1, gate order z, r, h (src/gpu.rs:680-819).
+ *   g  [tmax][ntot][2][768]  = W x + Wb   (input projection, both directions)
+ *   r  [2][768][hid]         recurrent weights (rows z | r | h)
+ *   rb [2][768]              recurrent bias
+ *   lens[ntot]               each line's length; the backward direction starts at len - 1
+ *   y  [tmax][ntot][2][hid]  only t < len is written
+ * hid is 256 in the reference (hidden_size check, src/gpu.rs:1461).
+ */
+void oracle_gru(const float *g, const float *r, const float *rb, const int *lens, int tmax, int ntot,
+                int hid, float *y) {
+    int G = 3 * hid;
+#pragma omp parallel for collapse(2) schedule(dynamic)
+    for (int dir = 0; dir < 2; dir++) {
+        for (int line = 0; line < ntot; line++) {
+            float *h = (float *)calloc((size_t)hid, sizeof(float));
+            float *acc = (float *)malloc((size_t)G * sizeof(float));
+            const float *R = r + (long)dir * G * hid;
+            const float *RB = rb + (long)dir * G;
+            int len = lens[line];
+            for (int s = 0; s < len && s < tmax; s++) {
+                int t = dir == 0 ? s : len - 1 - s;
+                for (int row = 0; row < G; row++) {
+                    const float *rr = R + (long)row * hid;
+                    float a = 0.f;
+                    for (int q = 0; q < hid; q++) a += rr[q] * h[q];
+                    acc[row] = a;
+                }
+                const float *gb = g + ((long)t * ntot + line) * 2 * G + (long)dir * G;
+                float *yo = y + ((long)t * ntot + line) * 2 * hid + (long)dir * hid;
+                for (int j = 0; j < hid; j++) {
+                    float z = sigm(gb[j] + acc[j] + RB[j]);
+                    float rr = sigm(gb[hid + j] + acc[hid + j] + RB[hid + j]);
+                    float c = tanhf(gb[2 * hid + j] + rr * (acc[2 * hid + j] + RB[2 * hid + j]));
+                    yo[j] = (1.0f - z) * c + z * h[j];
+                }
+                for (int j = 0; j < hid; j++) h[j] = yo[j];
+            }
+            free(h);
+            free(acc);
+        }
+    }
+}
+
+/* AvgPool (kh, 1) over the whole height to one row, time-major [t][ntot][c] at line offset
+ * `noff` (src/gpu.rs:595-614). */
+void oracle_avgpool_t(const float *x, int n, int c, int h, int w, int kh, int ntot, int noff, float *y) {
+    for (int nb = 0; nb < n; nb++)
+        for (int t = 0; t < w; t++)
+            for (int ch = 0; ch < c; ch++) {
+                float s = 0.f;
+                for (int r = 0; r < kh; r++) s += x[(((long)nb * c + ch) * h + r) * w + t];
+                y[((long)t * ntot + noff + nb) * c + ch] = s / (float)kh;
+            }
+}
+
+/* LayerNorm over the last axis, two-pass (src/nd.rs:135-153). */
+void oracle_layer_norm(const float *x, const float *gamma, const float *beta, long rows, int len, float eps,
+                       float *y) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < rows; i++) {
+        const float *xr = x + i * len;
+        float m = 0.f, v = 0.f;
+        for (int j = 0; j < len; j++) m += xr[j];
+        m /= (float)len;
+        for (int j = 0; j < len; j++) { float d = xr[j] - m; v += d * d; }
+        float inv = 1.0f / sqrtf(v / (float)len + eps);
+        for (int j = 0; j < len; j++) y[i * len + j] = (xr[j] - m) * inv * gamma[j] + beta[j];
+    }
+}
+
+/* Row softmax (src/nd.rs:206-220). */
+void oracle_softmax(const float *x, long rows, long len, float *y) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < rows; i++) {
+        const float *xr = x + i * len;
+        float m = -3.4e38f, s = 0.f;
+        for (long j = 0; j < len; j++) m = xr[j] > m ? xr[j] : m;
+        for (long j = 0; j < len; j++) s += expf(xr[j] - m);
+        for (long j = 0; j < len; j++) y[i * len + j] = expf(xr[j] - m) / s;
+    }
+}
+
+/*
+ * Row arg-max; ties -> the lowest index (src/nd.rs:360-391).  Also, per row, the largest value,
+ * the second largest (for the tie band) and log(sum(exp(v - max))) + max.
+ */
+void oracle_argmax(const float *x, long rows, long len, uint32_t *best, float *top1, float *top2, float *lse) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < rows; i++) {
+        const float *xr = x + i * len;
+        float m1 = -3.4e38f, m2 = -3.4e38f;
+        long at = 0;
+        for (long j = 0; j < len; j++) {
+            float v = xr[j];
+            if (v > m1) { m2 = m1; m1 = v; at = j; }
+            else if (v > m2) m2 = v;
+        }
+        double s = 0.0;
+        for (long j = 0; j < len; j++) s += exp((double)xr[j] - (double)m1);
+        best[i] = (uint32_t)at;
+        if (top1) top1[i] = m1;
+        if (top2) top2[i] = m2;
+        if (lse) lse[i] = (float)(log(s) + (double)m1);
+    }
+}
+
+/* Mean over the trailing `inner` values of each of `outer` rows (src/nd.rs:98-133). */
+void oracle_reduce_mean(const float *x, long outer, long inner, float *y) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < outer; i++) {
+        float s = 0.f;
+        for (long j = 0; j < inner; j++) s += x[i * inner + j];
+        y[i] = s / (float)inner;
+    }
+}
+
+/* Batched y[b] = a[b] (m x k) . c[b] (k x n), row-major, fp32 (src/nd.rs:947-962). */
+void oracle_bmm(const float *a, const float *c, long batch, int m, int k, int n, float *y) {
+#pragma omp parallel for collapse(2) schedule(static)
+    for (long bt = 0; bt < batch; bt++)
+        for (int r = 0; r < m; r++) {
+            const float *ar = a + (bt * m + r) * (long)k;
+            const float *cb = c + bt * (long)k * n;
+            float *yr = y + (bt * m + r) * (long)n;
+            for (int j = 0; j < n; j++) yr[j] = 0.f;
+            for (int q = 0; q < k; q++) {
+                float av = ar[q];
+                const float *cr = cb + (long)q * n;
+                for (int j = 0; j < n; j++) yr[j] += av * cr[j];
+            }
+        }
+}
+
+/* Elementwise unary ops of src/nd.rs:67-96: 1 Relu, 2 Sigmoid, 3 HardSigmoid(alpha, beta),
+ * 4 Erf, 5 Sqrt. */
+void oracle_unary(const float *x, long n, int op, float alpha, float beta, float *y) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < n; i++) {
+        float v = x[i], r = v;
+        switch (op) {
+        case 1: r = v > 0.f ? v : 0.f; break;
+        case 2: r = 1.0f / (1.0f + expf(-v)); break;
+        case 3: r = alpha * v + beta; r = r < 0.f ? 0.f : (r > 1.f ? 1.f : r); break;
+        case 4: r = erf_as(v); break;
+        case 5: r = sqrtf(v); break;
+        default: break;
+        }
+        y[i] = r;
+    }
+}

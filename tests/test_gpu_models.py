@@ -1,0 +1,127 @@
+"""Whole-model parity of the CUDA path against the CPU oracle on the benchmark configurations'
+seeded synthetic models and inputs (tolerances in tests/_helpers.py)."""
+import numpy as np
+import pytest
+
+import wocr
+from oracle import ref
+from wocr import synth
+
+from _helpers import PROB_TOL, argmax_parity, mask_parity, softmax
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def det_model():
+    return synth.ocrs_det_model()
+
+
+@pytest.fixture(scope="module")
+def detector(gpu, det_model):
+    d = wocr.Detector(gpu, det_model)
+    yield d
+    d.close()
+
+
+@pytest.mark.parametrize("w,h", [(2550, 3300), (517, 389), (600, 1700)])
+def test_detect_page(detector, det_model, w, h):
+    """Config 1 (ocrs detection), and pages smaller than the model (padding path, width not a
+    multiple of 32)."""
+    page = synth.page(11, w, h)
+    thr = 0.5
+    bits = detector.detect_page(page, w, h, thr)
+    rbits, prob, _ = ref.detect_page(det_model, page, thr)
+    bad, band = mask_parity(bits, rbits, prob, thr, w)
+    assert bad == 0, f"{bad} mask pixels differ outside the threshold band ({band} in it)"
+
+
+def test_detect_pages_batched_equals_single(detector):
+    pages = np.stack([synth.page(20 + k, 640, 480) for k in range(3)])
+    many = detector.detect_pages(pages, 0.5)
+    for k in range(3):
+        one = detector.detect_page(pages[k], 640, 480, 0.5)
+        assert (many[k] == one).all()
+
+
+def test_detect_prob_map(detector, det_model):
+    x = ref.grey_resize(synth.page(5, 1275, 1650)).reshape(1, 1, 800, 600)
+    got = detector.detect(x)
+    want = ref.detect(det_model, x)[0, 0]
+    assert np.abs(got - want).max() < 1e-4
+
+
+@pytest.fixture(scope="module")
+def rec_model():
+    return synth.ocrs_rec_model()
+
+
+@pytest.mark.parametrize("n", [1, 9, 64])
+def test_recognize(gpu, rec_model, n):
+    """Config 0 (ocrs recognition): per-line lengths, lines batched as ocr-bench batches them."""
+    lines = synth.ocrs_lines(0, n=n)
+    batches, order, widths = synth.ocrs_batches(lines)
+    rec = wocr.Recognizer(gpu, rec_model)
+    try:
+        logits, tmax, lens, best = rec.recognize(batches)
+    finally:
+        rec.close()
+    rlogits, rtmax, rlens = ref.recognize(rec_model, batches)
+    assert tmax == rtmax and lens == rlens
+    for line in range(len(lens)):
+        t = lens[line]
+        g, r = logits[:t, line], rlogits[:t, line]
+        bad, ties = argmax_parity(best[:t, line], r)
+        assert bad == 0, f"line {line}: {bad} steps choose another class"
+        assert np.abs(softmax(g) - softmax(r)).max() < PROB_TOL
+    # greedy CTC text identical
+    for k, line in enumerate(range(len(lens))):
+        want = ref.ocrs_decode(rlogits, line, lens[line], widths[k], synth.OCRS_ALPHABET)
+        got = wocr.ocrs_decode(best[:, line], lens[line], widths[k], synth.OCRS_ALPHABET)
+        assert got == want
+
+
+@pytest.fixture(scope="module")
+def pp_model():
+    return synth.pp_rec_model()
+
+
+def test_pp_recognition(gpu, pp_model):
+    """Config 3 (PP-OCRv6-style recognition, 18,709 classes): arg-max per step and the chosen
+    class's probability, on 2 of the 16 batches (the shortest and the longest)."""
+    lines = synth.pp_lines(2, n=256)
+    batches, order = synth.pp_batches(lines)
+    g = wocr.NdGraph(gpu, pp_model, stop_before_softmax=True)
+    try:
+        for data, n, w in (batches[0], batches[-1]):
+            best, mx, lse, shape = g.argmax(data)
+            logits = ref.run_onnx(pp_model, data, stop_before_softmax=True)
+            assert shape == logits.shape
+            flat = logits.reshape(-1, logits.shape[-1])
+            bad, ties = argmax_parity(best, flat)
+            assert bad == 0, f"{bad} of {len(best)} steps choose another class ({ties} near-ties)"
+            rb, t1, _, rlse = ref.argmax(flat)
+            p_gpu = np.exp(mx - lse)
+            p_ref = np.exp(t1 - rlse)
+            assert np.abs(p_gpu - p_ref).max() < PROB_TOL
+    finally:
+        g.close()
+
+
+def test_pp_detection(gpu):
+    """Config 4 (PP-OCRv6-style DB detection): det_input on the device and the probability map."""
+    m = synth.pp_det_model()
+    page = synth.page(3, 2550, 3300)
+    x, tp = wocr.NdGraph.det_input(gpu, page, 2550, 3300, 960)
+    rx, rtp = ref.det_input(page, 960)
+    assert x.shape == rx.shape == (1, 3, 960, 736)
+    assert np.abs(x - rx).max() < 1e-5
+    assert np.allclose(tp, rtp)
+    g = wocr.NdGraph(gpu, m)
+    try:
+        prob, tp2 = g.ppdet_page(page, 2550, 3300, 960)
+    finally:
+        g.close()
+    want = ref.run_onnx(m, rx)[0, 0]
+    assert prob.shape == want.shape
+    assert np.abs(prob - want).max() < 1e-4

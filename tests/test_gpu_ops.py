@@ -1,0 +1,154 @@
+"""Per-operator parity of the CUDA path against the CPU oracle, through the C ABI, on small
+and odd shapes (non-multiples of the tiles, one input channel, strides (2, 1), asymmetric pads,
+channel slices).  Each case is a tiny ONNX-style graph run by NdGraph (src/nd.rs) or by the
+ocrs Graph executor behind Detector::detect (src/gpu.rs)."""
+import numpy as np
+import pytest
+
+import wocr
+from oracle import ref
+from wocr.synth import _Builder
+
+pytestmark = pytest.mark.gpu
+
+RNG = np.random.default_rng(7)
+
+
+def rnd(*s):
+    return RNG.standard_normal(s).astype(np.float32)
+
+
+def close(a, b, tol=2e-4):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    scale = max(1.0, float(np.abs(b).max()))
+    err = float(np.abs(a - b).max()) / scale
+    assert err < tol, f"max relative error {err}"
+
+
+def run_nd(gpu, m, x, stop=False):
+    g = wocr.NdGraph(gpu, m, stop)
+    try:
+        return g.run(x)
+    finally:
+        g.close()
+
+
+@pytest.mark.parametrize("cin,cout,k,stride,pads,group,act", [
+    (3, 32, 3, (2, 2), [1, 1, 1, 1], 1, "relu"),
+    (16, 24, 3, (1, 1), [1, 1, 1, 1], 1, None),
+    (32, 64, 1, (1, 1), [0, 0, 0, 0], 1, "relu"),
+    (64, 64, 3, (2, 2), [1, 1, 1, 1], 64, "relu"),     # depthwise s2
+    (24, 24, 3, (2, 1), [1, 1, 1, 1], 24, None),       # depthwise (2, 1)
+    (5, 7, 3, (2, 2), [0, 0, 1, 1], 1, None),          # asymmetric pads, generic K decode
+    (8, 130, 3, (1, 1), [1, 1, 1, 1], 1, "relu"),      # N not a multiple of the tile
+])
+def test_conv(gpu, cin, cout, k, stride, pads, group, act):
+    b = _Builder(3)
+    y = b.conv("x", cin, cout, k, stride=stride, pads=pads, group=group)
+    if act:
+        y = b.op("Relu", [y])
+    m = b.model("x", y)
+    x = rnd(2, cin, 19, 37)
+    close(run_nd(gpu, m, x), ref.run_onnx(m, x))
+
+
+def test_conv_fusions(gpu):
+    """bias Add + GELU chain + residual Add, and the squeeze-excitation input scale."""
+    b = _Builder(4)
+    c = b.conv("x", 16, 16, 3, bias=False)
+    c = b.op("Add", [c, b.w("B", RNG.standard_normal((1, 16, 1, 1)))])
+    g = b.gelu(c)
+    r = b.op("Add", [g, "x"])
+    s = b.se(r, 16)
+    y = b.op("Relu", [b.conv(s, 16, 32, 1, pads=[0, 0, 0, 0])])
+    m = b.model("x", y)
+    x = rnd(2, 16, 12, 20)
+    close(run_nd(gpu, m, x), ref.run_onnx(m, x))
+
+
+def test_convt_batchnorm_resize_concat(gpu):
+    b = _Builder(5)
+    t = b.op("Relu", [b.batchnorm(b.convt("x", 12, 8, 2, 2), 8)])    # ConvT GEMM path + BN
+    u = b.op("Sigmoid", [b.convt("x", 12, 4, 3, 2)])                 # general ConvT (gather)
+    u = b.op("Slice", [u, b.i("s", [0, 0]), b.i("e", [14, 26]), b.i("a", [2, 3])])
+    sc = b.w("scales", np.array([1, 1, 2, 2], np.float32))
+    r = b.op("Resize", ["x", "", sc], {"mode": "nearest", "coordinate_transformation_mode": "asymmetric"})
+    r = b.conv(r, 12, 4, 1, pads=[0, 0, 0, 0])
+    y = b.op("Concat", [t, u, r], {"axis": 1})
+    y = b.op("MaxPool", [y], {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1]})
+    m = b.model("x", y)
+    x = rnd(1, 12, 7, 13)
+    close(run_nd(gpu, m, x), ref.run_onnx(m, x))
+
+
+def test_svtr_block(gpu):
+    """LayerNorm chain, Linear + bias, attention via Reshape/Transpose/Slice/MatMul/Softmax,
+    Linear + SiLU; the stop before the final Softmax."""
+    from wocr.synth import _svtr_block
+    b = _Builder(6)
+    x = _svtr_block(b, "x")
+    y = b.layer_norm(x, 120)
+    y = b.linear(y, 120, 37)
+    y = b.op("Softmax", [y], {"axis": 2})
+    m = b.model("x", y)
+    x = rnd(3, 11, 120)
+    close(run_nd(gpu, m, x), ref.run_onnx(m, x))
+    close(run_nd(gpu, m, x, stop=True), ref.run_onnx(m, x, stop_before_softmax=True))
+
+
+def test_int_shape_ops_and_pools(gpu):
+    b = _Builder(8)
+    p = b.op("AveragePool", ["x"], {"kernel_shape": [3, 3], "strides": [2, 2], "auto_pad": "SAME_UPPER"})
+    p = b.op("HardSigmoid", [p], {"alpha": 0.3, "beta": 0.4})
+    gp = b.op("GlobalAveragePool", [p])
+    shp = b.op("Shape", [p])
+    nb = b.op("Unsqueeze", [b.op("Gather", [shp, b.i("i", [0])]), b.i("ax", [0])])
+    tgt = b.op("Concat", [nb, b.i("rest", [-1])], {"axis": 0})
+    flat = b.op("Reshape", [p, tgt])
+    red = b.op("ReduceMean", [flat], {"axes": [-1], "keepdims": 0})
+    y = b.op("Mul", [b.op("Reshape", [gp, b.i("s2", [0, -1])]), b.op("Unsqueeze", [red, b.i("a2", [1])])])
+    y = b.op("Pow", [b.op("Sub", [y, b.scalar("c", 0.1)]), b.scalar("two", 2.0)])
+    y = b.op("Div", [b.op("Sqrt", [y]), b.scalar("d", 3.0)])
+    m = b.model("x", y)
+    x = rnd(2, 6, 9, 14)
+    close(run_nd(gpu, m, x), ref.run_onnx(m, x))
+
+
+def test_graph_executor_ops(gpu):
+    """The ocrs executor: Direct conv + fused MaxPool, dense convs, standalone MaxPool, zero Pad,
+    Slice, ConvTranspose + Relu, channel Concat, standalone Sigmoid."""
+    b = _Builder(9)
+    d = b.maxpool(b.conv_relu("image", 1, 16, 3), 2, 2)
+    c = b.conv_relu(d, 16, 32, 3)
+    p = b.maxpool(c, 2, 2)
+    p = b.op("Pad", [p, b.i("pads", [0] * 8)])
+    u = b.op("Relu", [b.convt(p, 32, 16, 2, 2)])
+    u = b.op("Slice", [u, b.i("st", [0]), b.i("en", [16]), b.i("ax", [1])])
+    y = b.op("Concat", [u, d], {"axis": 1})
+    y = b.op("Sigmoid", [b.conv(y, 32, 1, 1, pads=[0, 0, 0, 0])])
+    m = b.model("image", y)
+    x = rnd(1, 1, 44, 60)
+    det = wocr.Detector(gpu, m)
+    try:
+        close(det.detect(x), ref.run_onnx(m, x)[0, 0])
+    finally:
+        det.close()
+
+
+def test_unsupported_and_shape_errors(gpu):
+    b = _Builder(10)
+    y = b.op("LeakyRelu", ["x"])
+    with pytest.raises(wocr.WocrError) as e:
+        run_nd(gpu, b.model("x", y), rnd(1, 2, 3, 4))
+    assert e.value.code == 2 and "unsupported op LeakyRelu" in e.value.message
+    b = _Builder(11)
+    y = b.conv("x", 4, 4, 3)
+    with pytest.raises(wocr.WocrError) as e:
+        run_nd(gpu, b.model("x", y), rnd(1, 3, 8, 8))           # 3 channels into a 4-channel conv
+    assert e.value.code == 3
+    b = _Builder(12)
+    y = b.conv("image", 2, 4, 3, group=2)                           # grouped, not depthwise
+    with pytest.raises(wocr.WocrError) as e:
+        wocr.Detector(gpu, b.model("image", y))
+    assert e.value.code == 2

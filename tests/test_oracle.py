@@ -1,0 +1,196 @@
+"""The CPU oracle against an independent implementation (PyTorch CPU), and its restatement of
+the reference's coordinate formulas, on small seeded cases.  No GPU needed."""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle import ref
+from wocr import synth
+
+RNG = np.random.default_rng(1234)
+
+
+def rnd(*shape):
+    return RNG.standard_normal(shape).astype(np.float32)
+
+
+@pytest.mark.parametrize("cin,cout,k,stride,pads,group", [
+    (3, 5, 3, (1, 1), (1, 1, 1, 1), 1),
+    (4, 6, 3, (2, 2), (1, 1, 1, 1), 1),
+    (8, 8, 3, (2, 1), (1, 1, 1, 1), 8),     # depthwise, stride (2, 1)
+    (1, 4, 5, (1, 1), (2, 2, 2, 2), 1),
+    (6, 3, 1, (1, 1), (0, 0, 0, 0), 1),
+    (4, 4, 3, (2, 2), (0, 0, 1, 1), 1),     # asymmetric (SAME_UPPER-like) padding
+])
+def test_conv2d_vs_torch(cin, cout, k, stride, pads, group):
+    x = rnd(2, cin, 11, 13)
+    w = rnd(cout, cin // group, k, k)
+    b = rnd(cout)
+    y = ref.conv2d(x, w, b, group=group, strides=stride, pads=pads)
+    xp = F.pad(torch.from_numpy(x), (pads[1], pads[3], pads[0], pads[2]))
+    yt = F.conv2d(xp, torch.from_numpy(w), torch.from_numpy(b), stride=stride, groups=group).numpy()
+    assert y.shape == yt.shape
+    assert np.abs(y - yt).max() < 1e-4
+
+
+def test_conv2d_epilogue_residual_scale():
+    x, w, b = rnd(2, 4, 7, 9), rnd(5, 4, 3, 3), rnd(5)
+    res, sc = rnd(2, 5, 7, 9), rnd(2, 4)
+    y = ref.conv2d(x, w, b, pads=(1, 1, 1, 1), act=1, res=res, insc=sc)
+    xs = torch.from_numpy(x) * torch.from_numpy(sc)[:, :, None, None]
+    yt = torch.relu(F.conv2d(xs, torch.from_numpy(w), torch.from_numpy(b), padding=1)) + torch.from_numpy(res)
+    assert np.abs(y - yt.numpy()).max() < 1e-4
+
+
+@pytest.mark.parametrize("act", [0, 1, 2, 3, 4])
+def test_activations(act):
+    v = np.linspace(-6, 6, 97).astype(np.float32)
+    got = np.array([ref.lib().oracle_act(float(x), act) for x in v], np.float32)
+    t = torch.from_numpy(v)
+    want = {0: t, 1: torch.relu(t), 2: torch.sigmoid(t), 3: F.gelu(t), 4: F.silu(t)}[act].numpy()
+    assert np.abs(got - want).max() < 2e-6
+
+
+def test_erf_as_bound():
+    v = np.linspace(-4, 4, 801)
+    got = np.array([ref.lib().oracle_erf(float(x)) for x in v])
+    want = np.array([math.erf(x) for x in v])
+    assert np.abs(got - want).max() < 5e-7   # A&S 7.1.26: 1.5e-7 plus float rounding
+
+
+def test_convt_vs_torch():
+    x, w, b = rnd(2, 6, 5, 7), rnd(6, 4, 2, 2), rnd(4)
+    y = ref.convt(x, w, b, stride=2, act=1)
+    yt = torch.relu(F.conv_transpose2d(torch.from_numpy(x), torch.from_numpy(w), torch.from_numpy(b), stride=2))
+    assert np.abs(y - yt.numpy()).max() < 1e-4
+    w3 = rnd(6, 4, 3, 3)
+    y3 = ref.convt(x, w3, None, stride=2)
+    yt3 = F.conv_transpose2d(torch.from_numpy(x), torch.from_numpy(w3), stride=2)
+    assert np.abs(y3 - yt3.numpy()).max() < 1e-4
+
+
+def test_pool_vs_torch():
+    x = rnd(2, 3, 9, 12)
+    y = ref.pool(x, 2, 2, 2, 2)
+    assert np.abs(y - F.max_pool2d(torch.from_numpy(x), 2).numpy()).max() == 0
+    y = ref.pool(x, 3, 1, 3, 1)
+    assert np.abs(y - F.max_pool2d(torch.from_numpy(x), (3, 1)).numpy()).max() == 0
+    y = ref.pool(x, 3, 3, 2, 2, pads=(1, 1, 1, 1), avg=True)
+    yt = F.avg_pool2d(torch.from_numpy(x), 3, 2, padding=1, count_include_pad=False).numpy()
+    assert np.abs(y - yt).max() < 1e-5
+
+
+def test_gru_vs_torch():
+    """ONNX GRU (z, r, h; linear_before_reset = 1) == torch GRU (r, z, n) after a gate reorder."""
+    T, n, inp, hid = 7, 3, 16, 256
+    X = rnd(T, n, inp) * 0.5
+    W = RNG.uniform(-1 / 16, 1 / 16, (2, 3 * hid, inp)).astype(np.float32)
+    R = RNG.uniform(-1 / 16, 1 / 16, (2, 3 * hid, hid)).astype(np.float32)
+    B = RNG.uniform(-1 / 16, 1 / 16, (2, 6 * hid)).astype(np.float32)
+    Y = ref._onnx_gru(X, W, R, B, hid)                       # [T, 2, n, hid]
+    g = torch.nn.GRU(inp, hid, bidirectional=True)
+    order = lambda a: np.concatenate([a[hid:2 * hid], a[:hid], a[2 * hid:]])  # z,r,h -> r,z,n
+    with torch.no_grad():
+        for d, sfx in ((0, ""), (1, "_reverse")):
+            getattr(g, "weight_ih_l0" + sfx).copy_(torch.from_numpy(order(W[d])))
+            getattr(g, "weight_hh_l0" + sfx).copy_(torch.from_numpy(order(R[d])))
+            getattr(g, "bias_ih_l0" + sfx).copy_(torch.from_numpy(order(B[d, :3 * hid])))
+            getattr(g, "bias_hh_l0" + sfx).copy_(torch.from_numpy(order(B[d, 3 * hid:])))
+        yt, _ = g(torch.from_numpy(X))
+    yt = yt.numpy().reshape(T, n, 2, hid).transpose(0, 2, 1, 3)
+    assert np.abs(Y - yt).max() < 1e-5
+
+
+def test_gru_lengths():
+    """Per-line lengths: steps t >= len are not written, the backward pass starts at len - 1."""
+    hid, tmax = 256, 6
+    g = rnd(tmax, 2, 2 * 3 * hid) * 0.3
+    r = RNG.uniform(-1 / 16, 1 / 16, (2, 3 * hid, hid)).astype(np.float32)
+    rb = RNG.uniform(-1 / 16, 1 / 16, (2, 3 * hid)).astype(np.float32)
+    y = ref.gru(g, r, rb, [6, 3], hid)
+    assert np.isnan(y[3:, 1]).all() and not np.isnan(y[:3, 1]).any() and not np.isnan(y).any(axis=2)[:, 0].any()
+    # line 1 alone with tmax 3 gives the same first 3 steps
+    y1 = ref.gru(g[:3, 1:2], r, rb, [3], hid)
+    assert np.abs(y1[:, 0] - y[:3, 1]).max() == 0
+
+
+def test_layer_norm_softmax_argmax():
+    x = rnd(5, 120)
+    g, b = rnd(120), rnd(120)
+    y = ref.layer_norm(x, g, b, 1e-6)
+    yt = F.layer_norm(torch.from_numpy(x), (120,), torch.from_numpy(g), torch.from_numpy(b), 1e-6).numpy()
+    assert np.abs(y - yt).max() < 1e-4
+    s = ref.softmax(x)
+    assert np.abs(s - torch.softmax(torch.from_numpy(x), -1).numpy()).max() < 1e-6
+    xt = x.copy()
+    xt[0, 7] = xt[0, 9] = 100.0
+    best, t1, t2, lse = ref.argmax(xt)
+    assert best[0] == 7 and t1[0] == 100.0 and t2[0] == 100.0          # ties -> lowest index
+    assert ref.ocrs_best(xt[0]) == 9                                    # Rust max_by -> last index
+    assert np.abs(lse - torch.logsumexp(torch.from_numpy(xt), -1).numpy()).max() < 1e-4
+
+
+def test_grey_resize_formula():
+    """Identity-size resize reproduces the grey formula; out-of-page pixels are -0.5."""
+    rgb = RNG.integers(0, 256, (800, 600, 3), dtype=np.uint8)
+    g = ref.grey_resize(rgb)
+    want = -0.5 + rgb[..., 0] * (0.299 / 255) + rgb[..., 1] * (0.587 / 255) + rgb[..., 2] * (0.114 / 255)
+    assert np.abs(g - want).max() < 1e-5
+    small = RNG.integers(0, 256, (400, 300, 3), dtype=np.uint8)       # padded to 800 x 600
+    g2 = ref.grey_resize(small)
+    assert (g2[450:, :] == -0.5).all() and (g2[:, 350:] == -0.5).all()
+
+
+def test_mask_bits_layout():
+    m = np.zeros((800, 600), np.float32)
+    m[:, :300] = 1.0
+    bits, prob = ref.mask_up(m, 600, 800, 70, 40, 0.5)     # page 70 x 40: 3 words per row
+    assert bits.shape == (40, 3)
+    for y in range(40):
+        row = [(bits[y, x // 32] >> (x % 32)) & 1 for x in range(70)]
+        assert row == [int(p > 0.5) for p in prob[y]]
+    assert (bits[:, 2] >> 6).max() == 0                     # bits past the page width stay 0
+
+
+def test_det_input_sizes():
+    # the config-4 page: 2550 x 3300 at max_side 960 -> 736 x 960
+    assert ref.det_input_size(2550, 3300, 960) == (736, 960)
+    assert ref.det_input_size(100, 50, 960) == (96, 64)
+    assert ref.det_input_size(10, 10, 960) == (32, 32)
+
+
+def test_resize_nearest_vs_torch():
+    x = rnd(1, 3, 5, 7)
+    y = ref.resize_nearest(x, 2.0, 2.0)
+    yt = F.interpolate(torch.from_numpy(x), scale_factor=2, mode="nearest").numpy()
+    assert np.abs(y - yt).max() == 0
+
+
+def test_run_onnx_shapes():
+    """The interpreter runs every synthetic architecture end to end with the expected shapes."""
+    m = synth.ocrs_rec_model()
+    lines = synth.ocrs_lines(n=3, wmin=64, wmax=96)
+    batches, order, widths = synth.ocrs_batches(lines)
+    out = ref.run_onnx(m, batches[0][0])
+    assert out.shape == (batches[0][2] // 4, batches[0][1], 97)
+    pm = synth.pp_rec_model(classes=50)
+    x = np.zeros((2, 3, 48, 64), np.float32)
+    y = ref.run_onnx(pm, x)
+    assert y.shape == (2, 8, 50) and np.allclose(y.sum(-1), 1.0, atol=1e-5)
+    logits = ref.run_onnx(pm, x, stop_before_softmax=True)
+    assert np.abs(ref.softmax(logits) - y).max() < 1e-6
+    dm = synth.pp_det_model()
+    z = ref.run_onnx(dm, np.zeros((1, 3, 64, 96), np.float32))
+    assert z.shape == (1, 1, 64, 96)
+
+
+def test_synth_determinism():
+    a, b = synth.page(3, 300, 200), synth.page(3, 300, 200)
+    assert (a == b).all()
+    la, lb = synth.ocrs_lines(5, n=4), synth.ocrs_lines(5, n=4)
+    assert all((x == y).all() for x, y in zip(la, lb))
+    ma, mb = synth.ocrs_det_model(), synth.ocrs_det_model()
+    assert all((ma.weights[k] == mb.weights[k]).all() for k in ma.weights)

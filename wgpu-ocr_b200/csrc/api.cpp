@@ -1,0 +1,690 @@
+// The C ABI of include/wocr.h: status codes at the boundary, exceptions inside.
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <thread>
+
+#include "exec.h"
+
+using namespace wocr;
+
+namespace wocr {
+const std::string &last_error();
+}
+
+struct wocr_ctx {
+    Ctx c;
+};
+
+struct Stats {
+    double flops = 0;
+    int64_t launches = 0;
+};
+
+struct wocr_detector {
+    wocr_ctx *ctx;
+    std::unique_ptr<Executor> graph;
+    Stats last;
+};
+
+struct GruLayer {
+    DevW w_t, wb, r, rb;  // w_t [in][1536], wb [2][768] (input bias), r [2][768][256], rb [2][768]
+    int input = 0;
+};
+
+struct wocr_recognizer {
+    wocr_ctx *ctx;
+    std::unique_ptr<Executor> trunk;
+    int pool_kh = 1;
+    GruLayer layers[2];
+    DevW lin_w, lin_b;  // [512][ldw], bias [ldw]
+    int classes = 0, ldw = 0;
+    int lines = 8;
+    Stats last;
+};
+
+struct wocr_ndgraph {
+    wocr_ctx *ctx;
+    std::unique_ptr<Executor> graph;
+    Stats last;
+};
+
+namespace {
+
+template <typename F>
+int32_t guard(F &&f) {
+    try {
+        f();
+        set_last_error("");
+        return WOCR_OK;
+    } catch (const Error &e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc &) {
+        set_last_error("host out of memory");
+        return WOCR_ERR_OOM;
+    } catch (const std::exception &e) {
+        set_last_error(e.what());
+        return WOCR_ERR_INVALID;
+    }
+}
+
+struct RunScope {
+    Ctx *c;
+    Stats *out;
+    double f0;
+    int64_t l0;
+    RunScope(Ctx *ctx, Stats *s) : c(ctx), out(s), f0(ctx->flops), l0(ctx->launches) { WOCR_CUDA(cudaSetDevice(ctx->device)); }
+    ~RunScope() {
+        out->flops = c->flops - f0;
+        out->launches = c->launches - l0;
+    }
+};
+
+void sync_bounded(Ctx *c, int timeout_ms) {
+    if (timeout_ms <= 0) {
+        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        return;
+    }
+    auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        cudaError_t e = cudaStreamQuery(c->stream);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) WOCR_CUDA(e);
+        auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
+        if (ms > timeout_ms) fail(WOCR_ERR_TIMEOUT, "stream did not finish within " + std::to_string(timeout_ms) + " ms");
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+void d2h(Ctx *c, void *dst, const void *src, size_t bytes) {
+    if (bytes) WOCR_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *wocr_last_error(void) { return last_error().c_str(); }
+
+int32_t wocr_ctx_create(int32_t device, int32_t lines, wocr_ctx **out) {
+    return guard([&] {
+        if (!out) fail(WOCR_ERR_INVALID, "null out");
+        int n = 0;
+        WOCR_CUDA(cudaGetDeviceCount(&n));
+        if (device < 0 || device >= n) fail(WOCR_ERR_INVALID, "no CUDA device " + std::to_string(device));
+        WOCR_CUDA(cudaSetDevice(device));
+        cudaDeviceProp prop;
+        WOCR_CUDA(cudaGetDeviceProperties(&prop, device));
+        if (prop.major < 10) fail(WOCR_ERR_UNSUPPORTED, std::string("sm_100a kernels need a B200-class GPU, found ") + prop.name);
+        auto *h = new wocr_ctx();
+        h->c.device = device;
+        h->c.lines = lines > 0 ? lines : 8;
+        h->c.sm_count = prop.multiProcessorCount;
+        h->c.name = std::string(prop.name) + " (sm_" + std::to_string(prop.major) + std::to_string(prop.minor) + ", " +
+                    std::to_string(prop.multiProcessorCount) + " SMs)";
+        cudaError_t e = cudaStreamCreateWithFlags(&h->c.stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) {
+            delete h;
+            WOCR_CUDA(e);
+        }
+        cudaMemPool_t pool;
+        WOCR_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+        uint64_t thr = UINT64_MAX;
+        WOCR_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr));
+        h->c.pool = pool;
+        *out = h;
+    });
+}
+
+void wocr_ctx_destroy(wocr_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->c.device);
+    cudaStreamSynchronize(ctx->c.stream);
+    cudaStreamDestroy(ctx->c.stream);
+    delete ctx;
+}
+
+int32_t wocr_ctx_describe(wocr_ctx *ctx, char *buf, int32_t cap) {
+    return guard([&] {
+        if (!ctx || !buf || cap <= 0) fail(WOCR_ERR_INVALID, "null argument");
+        std::snprintf(buf, (size_t)cap, "%s", ctx->c.name.c_str());
+    });
+}
+
+void *wocr_ctx_stream(wocr_ctx *ctx) { return ctx ? (void *)ctx->c.stream : nullptr; }
+
+int32_t wocr_ctx_sync(wocr_ctx *ctx, int32_t timeout_ms) {
+    return guard([&] {
+        if (!ctx) fail(WOCR_ERR_INVALID, "null ctx");
+        WOCR_CUDA(cudaSetDevice(ctx->c.device));
+        sync_bounded(&ctx->c, timeout_ms);
+    });
+}
+
+int64_t wocr_ctx_pool_bytes(wocr_ctx *ctx) {
+    if (!ctx) return -1;
+    uint64_t v = 0;
+    if (cudaMemPoolGetAttribute(ctx->c.pool, cudaMemPoolAttrReservedMemCurrent, &v) != cudaSuccess) return -1;
+    return (int64_t)v;
+}
+
+int64_t wocr_ctx_launches(wocr_ctx *ctx) { return ctx ? ctx->c.launches : -1; }
+
+int32_t wocr_ctx_profile(wocr_ctx *ctx, int32_t on) {
+    return guard([&] {
+        if (!ctx) fail(WOCR_ERR_INVALID, "null ctx");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        for (auto &r : c->recs) {
+            c->spare.push_back(r.a);
+            c->spare.push_back(r.b);
+        }
+        c->recs.clear();
+        c->prof = on != 0;
+    });
+}
+
+int32_t wocr_ctx_profile_report(wocr_ctx *ctx, char *buf, int32_t cap) {
+    return guard([&] {
+        if (!ctx || !buf || cap <= 0) fail(WOCR_ERR_INVALID, "null argument");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        struct Agg {
+            int64_t n = 0;
+            double ms = 0, flops = 0, bytes = 0;
+        };
+        std::map<std::string, Agg> agg;
+        for (auto &r : c->recs) {
+            float ms = 0;
+            WOCR_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+            Agg &a = agg[r.name];
+            a.n++;
+            a.ms += ms;
+            a.flops += r.flops;
+            a.bytes += r.bytes;
+        }
+        std::string s = "[";
+        for (auto &kv : agg) {
+            char tmp[512];
+            std::snprintf(tmp, sizeof tmp, "%s{\"kernel\": \"%s\", \"launches\": %lld, \"ms\": %.6f, \"flops\": %.6e, \"bytes\": %.6e}",
+                          s.size() > 1 ? ", " : "", kv.first.c_str(), (long long)kv.second.n, kv.second.ms,
+                          kv.second.flops, kv.second.bytes);
+            s += tmp;
+        }
+        s += "]";
+        if ((int64_t)s.size() + 1 > cap) fail(WOCR_ERR_CAPACITY, "report needs " + std::to_string(s.size() + 1) + " bytes");
+        std::memcpy(buf, s.c_str(), s.size() + 1);
+    });
+}
+
+int32_t wocr_host_alloc(size_t bytes, void **out) {
+    return guard([&] {
+        if (!out) fail(WOCR_ERR_INVALID, "null out");
+        WOCR_CUDA(cudaHostAlloc(out, bytes ? bytes : 16, cudaHostAllocPortable));
+    });
+}
+
+void wocr_host_free(void *p) {
+    if (p) cudaFreeHost(p);
+}
+
+// ---- detector ---------------------------------------------------------------------------
+int32_t wocr_detector_create(wocr_ctx *ctx, const wocr_model *model, wocr_detector **out) {
+    return guard([&] {
+        if (!ctx || !out) fail(WOCR_ERR_INVALID, "null argument");
+        WOCR_CUDA(cudaSetDevice(ctx->c.device));
+        Model m = model_from_c(model);
+        auto *d = new wocr_detector();
+        d->ctx = ctx;
+        try {
+            d->graph = build_graph(&ctx->c, m, nullptr, nullptr);
+            WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
+        } catch (...) {
+            delete d;
+            throw;
+        }
+        *out = d;
+    });
+}
+
+void wocr_detector_destroy(wocr_detector *det) {
+    if (!det) return;
+    cudaSetDevice(det->ctx->c.device);
+    cudaStreamSynchronize(det->ctx->c.stream);
+    delete det;
+}
+
+static void detect_pages_dev(wocr_detector *det, const uint8_t *d_rgb, int n, int w, int h, float thr,
+                             uint32_t *d_mask) {
+    Ctx *c = &det->ctx->c;
+    if (n <= 0 || w <= 0 || h <= 0) fail(WOCR_ERR_INVALID, "empty page");
+    const int mh = 800, mw = 600;  // the model size (src/gpu.rs:1394)
+    int ph = std::max(h, mh), pw = std::max(w, mw);
+    DT in = new_nhwc(c, n, 1, mh, mw);
+    k::grey_resize(c, d_rgb, (int64_t)w * h * 3, n, w, h, mh, mw, in.p);
+    DT m = det->graph->run(in);
+    if (m.rank() != 4 || m.shape[0] != n || m.shape[1] != 1)
+        fail(WOCR_ERR_SHAPE, "detection output " + shape_str(m.shape));
+    int vh = mh - (ph - h) * mh / ph, vw = mw - (pw - w) * mw / pw;
+    if (m.shape[2] < vh || m.shape[3] < vw) fail(WOCR_ERR_SHAPE, "detection output " + shape_str(m.shape));
+    // C = 1: row stride strides[2], plane strides[0]
+    k::mask_up(c, m.p, (int)m.strides[2], m.strides[0], n, vw, vh, w, h, thr, d_mask);
+}
+
+int32_t wocr_detect_pages_device(wocr_detector *det, const uint8_t *d_rgb, int32_t n, int32_t w, int32_t h,
+                                 float threshold, uint32_t *d_mask_out) {
+    return guard([&] {
+        if (!det || !d_rgb || !d_mask_out) fail(WOCR_ERR_INVALID, "null argument");
+        RunScope rs(&det->ctx->c, &det->last);
+        detect_pages_dev(det, d_rgb, n, w, h, threshold, d_mask_out);
+    });
+}
+
+int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int32_t w, int32_t h, float threshold,
+                          uint32_t *mask_out) {
+    return guard([&] {
+        if (!det || !rgb || !mask_out) fail(WOCR_ERR_INVALID, "null argument");
+        if (n <= 0 || w <= 0 || h <= 0) fail(WOCR_ERR_INVALID, "empty page");
+        Ctx *c = &det->ctx->c;
+        RunScope rs(c, &det->last);
+        size_t in_bytes = (size_t)n * w * h * 3;
+        size_t out_words = (size_t)n * h * ((w + 31) / 32);
+        BufP src = alloc(c, in_bytes), dst = alloc(c, out_words * 4);
+        WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, in_bytes, cudaMemcpyHostToDevice, c->stream));
+        detect_pages_dev(det, (const uint8_t *)src->p, n, w, h, threshold, (uint32_t *)dst->p);
+        d2h(c, mask_out, dst->p, out_words * 4);
+        sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_detect_page(wocr_detector *det, const uint8_t *rgb, int32_t w, int32_t h, float threshold,
+                         uint32_t *mask_out) {
+    return wocr_detect_pages(det, rgb, 1, w, h, threshold, mask_out);
+}
+
+int32_t wocr_detect(wocr_detector *det, const float *input, int32_t h, int32_t w, float *prob_out, int64_t cap,
+                    int32_t *out_h, int32_t *out_w) {
+    return guard([&] {
+        if (!det || !input || h <= 0 || w <= 0) fail(WOCR_ERR_INVALID, "bad argument");
+        Ctx *c = &det->ctx->c;
+        RunScope rs(c, &det->last);
+        DT x = from_host(c, input, {1, 1, h, w});
+        DT out = to_rowmajor(c, det->graph->run(x));
+        if (out.rank() != 4) fail(WOCR_ERR_SHAPE, "detection output " + shape_str(out.shape));
+        if (out_h) *out_h = (int32_t)out.shape[2];
+        if (out_w) *out_w = (int32_t)out.shape[3];
+        if (prob_out) {
+            if (cap < out.numel()) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(out.shape));
+            d2h(c, prob_out, out.p, (size_t)out.numel() * 4);
+        }
+        sync_bounded(c, 0);
+    });
+}
+
+// ---- recogniser -------------------------------------------------------------------------
+int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t lines, wocr_recognizer **out) {
+    return guard([&] {
+        if (!ctx || !out) fail(WOCR_ERR_INVALID, "null argument");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        Model m = model_from_c(model);
+        auto *r = new wocr_recognizer();
+        r->ctx = ctx;
+        r->lines = lines > 0 ? lines : c->lines;
+        try {
+            Node pool;
+            r->trunk = build_graph(c, m, "AveragePool", &pool);
+            if (pool.op.empty()) fail(WOCR_ERR_UNSUPPORTED, "no AveragePool in the recognition model");
+            auto kv = pool.ints("kernel_shape");
+            if (!kv) fail(WOCR_ERR_UNSUPPORTED, "AveragePool without kernel_shape");
+            auto sv = pool.ints("strides");
+            if (kv->size() != 2 || (*kv)[1] != 1 || !sv || *sv != *kv)
+                fail(WOCR_ERR_UNSUPPORTED, "unsupported AveragePool " + shape_str(*kv));
+            r->pool_kh = (int)(*kv)[0];
+            int nl = 0;
+            for (auto &n : m.nodes) {
+                if (n.op != "GRU") continue;
+                if (n.int_("hidden_size").value_or(0) != 256 || n.int_("linear_before_reset").value_or(0) != 1 ||
+                    n.str("direction").value_or("") != "bidirectional")
+                    fail(WOCR_ERR_UNSUPPORTED, "unsupported GRU attributes");
+                if (nl >= 2) {
+                    nl++;
+                    continue;
+                }
+                const HostW &W = m.weight(n.in(1)), &R = m.weight(n.in(2)), &B = m.weight(n.in(3));
+                if (W.dims.size() != 3 || W.dims[0] != 2 || W.dims[1] != 768 || R.data.size() != 2 * 768 * 256 ||
+                    B.data.size() != 2 * 1536)
+                    fail(WOCR_ERR_SHAPE, "GRU weights " + shape_str(W.dims));
+                int input = (int)W.dims[2];
+                // W [2][768][in] as rows of the projection -> [in][1536] (src/gpu.rs:1466-1472)
+                std::vector<float> wt((size_t)input * 1536);
+                for (int row = 0; row < 1536; row++)
+                    for (int i = 0; i < input; i++) wt[(size_t)i * 1536 + row] = W.data[(size_t)row * input + i];
+                std::vector<float> wb, rb;
+                for (int dir = 0; dir < 2; dir++) {
+                    wb.insert(wb.end(), B.data.begin() + dir * 1536, B.data.begin() + dir * 1536 + 768);
+                    rb.insert(rb.end(), B.data.begin() + dir * 1536 + 768, B.data.begin() + dir * 1536 + 1536);
+                }
+                GruLayer &L = r->layers[nl];
+                L.input = input;
+                L.w_t = upload(c, wt);
+                L.wb = upload(c, wb);
+                L.r = upload(c, R.data);
+                L.rb = upload(c, rb);
+                nl++;
+            }
+            if (nl != 2) fail(WOCR_ERR_UNSUPPORTED, std::to_string(nl) + " GRU layers");
+            const Node *mm = nullptr;
+            for (auto &n : m.nodes)
+                if (n.op == "MatMul") {
+                    mm = &n;
+                    break;
+                }
+            if (!mm) fail(WOCR_ERR_UNSUPPORTED, "no MatMul");
+            const HostW &lin = m.weight(mm->in(1));  // [512][classes]
+            if (lin.dims.size() != 2 || lin.dims[0] != 512) fail(WOCR_ERR_SHAPE, "output layer " + shape_str(lin.dims));
+            const Node *add = nullptr;
+            for (auto &n : m.nodes)
+                if (n.op == "Add" && std::find(n.inputs.begin(), n.inputs.end(), mm->outputs[0]) != n.inputs.end()) {
+                    add = &n;
+                    break;
+                }
+            if (!add) fail(WOCR_ERR_UNSUPPORTED, "no bias Add");
+            const HostW *bias = nullptr;
+            for (auto &i : add->inputs)
+                if (m.weights.count(i)) {
+                    bias = &m.weights.at(i);
+                    break;
+                }
+            if (!bias) fail(WOCR_ERR_UNSUPPORTED, "no bias weight");
+            r->classes = (int)lin.dims[1];
+            r->ldw = (r->classes + 3) / 4 * 4;
+            std::vector<float> lw((size_t)512 * r->ldw, 0.f), lb(r->ldw, 0.f);
+            for (int i = 0; i < 512; i++)
+                for (int q = 0; q < r->classes; q++) lw[(size_t)i * r->ldw + q] = lin.data[(size_t)i * r->classes + q];
+            for (int q = 0; q < r->classes && q < (int)bias->data.size(); q++) lb[q] = bias->data[q];
+            r->lin_w = upload(c, lw);
+            r->lin_b = upload(c, lb);
+            WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        } catch (...) {
+            delete r;
+            throw;
+        }
+        *out = r;
+    });
+}
+
+void wocr_recognizer_destroy(wocr_recognizer *rec) {
+    if (!rec) return;
+    cudaSetDevice(rec->ctx->c.device);
+    cudaStreamSynchronize(rec->ctx->c.stream);
+    delete rec;
+}
+
+// Trunk output width of a batch of width w: follows the trunk's pooling/strides exactly by
+// running shape arithmetic of the lowered steps.
+static int trunk_width(wocr_recognizer *rec, int w, int *h_out) {
+    int64_t h = 64, wd = w;
+    for (auto &s : rec->trunk->steps) {
+        switch (s.kind) {
+        case Step::G_DIRECT:
+            h = (h + 2 * s.conv.pads[0] - s.conv.kh + 1) / s.conv.pool_h;
+            wd = (wd + 2 * s.conv.pads[0] - s.conv.kw + 1) / s.conv.pool_w;
+            break;
+        case Step::G_CONV:
+        case Step::G_DEPTHWISE:
+            h = (h + 2 * s.conv.pads[0] - s.conv.kh) / s.conv.sh + 1;
+            wd = (wd + 2 * s.conv.pads[0] - s.conv.kw) / s.conv.sw + 1;
+            break;
+        case Step::G_CONVT:
+            h = (h - 1) * s.convt.s + s.convt.kh;
+            wd = (wd - 1) * s.convt.s + s.convt.kw;
+            break;
+        case Step::G_MAXPOOL:
+            h /= s.conv.kh;
+            wd /= s.conv.kw;
+            break;
+        default:
+            break;
+        }
+    }
+    if (h_out) *h_out = (int)h;
+    return (int)wd;
+}
+
+int32_t wocr_recognizer_dims(wocr_recognizer *rec, const int32_t *batch_n, const int32_t *batch_w, int32_t n_batches,
+                             int32_t *tmax, int32_t *ntot, int32_t *classes) {
+    return guard([&] {
+        if (!rec || (n_batches > 0 && (!batch_n || !batch_w))) fail(WOCR_ERR_INVALID, "null argument");
+        int tm = 0, nt = 0;
+        for (int b = 0; b < n_batches; b++) {
+            tm = std::max(tm, trunk_width(rec, batch_w[b], nullptr));
+            nt += batch_n[b];
+        }
+        if (tmax) *tmax = tm;
+        if (ntot) *ntot = nt;
+        if (classes) *classes = rec->classes;
+    });
+}
+
+int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const int32_t *batch_n,
+                       const int32_t *batch_w, int32_t n_batches, float *logits, int64_t logits_cap, int32_t *lens,
+                       uint32_t *best, int32_t *tmax_out) {
+    return guard([&] {
+        if (!rec || n_batches <= 0 || !batches || !batch_n || !batch_w) fail(WOCR_ERR_INVALID, "no batches");
+        Ctx *c = &rec->ctx->c;
+        RunScope rs(c, &rec->last);
+        // the trunks first (src/gpu.rs:1516-1526)
+        std::vector<DT> trunks;
+        for (int b = 0; b < n_batches; b++) {
+            if (batch_n[b] <= 0 || batch_w[b] <= 0 || !batches[b]) fail(WOCR_ERR_INVALID, "empty batch");
+            DT x = from_host(c, batches[b], {batch_n[b], 1, 64, batch_w[b]});
+            trunks.push_back(rec->trunk->run(x));
+        }
+        int ntot = 0, tmax = 0;
+        for (auto &t : trunks) {
+            ntot += (int)t.shape[0];
+            tmax = std::max(tmax, (int)t.shape[3]);
+        }
+        int ch = (int)trunks[0].shape[1];
+        if (ch != rec->layers[0].input)
+            fail(WOCR_ERR_SHAPE, "trunk gives " + std::to_string(ch) + " features, GRU takes " +
+                                     std::to_string(rec->layers[0].input));
+        int64_t m = (int64_t)tmax * ntot;
+        DT x = new_rowmajor(c, {tmax, ntot, ch});
+        WOCR_CUDA(cudaMemsetAsync(x.p, 0, (size_t)x.numel() * 4, c->stream));
+        std::vector<int> hl;
+        int noff = 0;
+        for (auto &t : trunks) {
+            int n = (int)t.shape[0], tc = (int)t.shape[1], h = (int)t.shape[2], w = (int)t.shape[3];
+            if (tc != ch) fail(WOCR_ERR_SHAPE, "trunk channels differ between batches");
+            if ((h - rec->pool_kh) / rec->pool_kh + 1 != 1 || h < rec->pool_kh)
+                fail(WOCR_ERR_SHAPE, "trunk height " + std::to_string(h) + " does not pool to one row");
+            DT tn = to_nhwc(c, t);
+            k::avgpool_t(c, tn.p, tn.strides[0], tn.pix(), n, ch, h, w, rec->pool_kh, ntot, noff, x.p);
+            for (int q = 0; q < n; q++) hl.push_back(w);
+            noff += n;
+        }
+        BufP lens_d = alloc(c, hl.size() * sizeof(int));
+        WOCR_CUDA(cudaMemcpyAsync(lens_d->p, hl.data(), hl.size() * sizeof(int), cudaMemcpyHostToDevice, c->stream));
+        DT in = x;
+        for (int l = 0; l < 2; l++) {
+            GruLayer &L = rec->layers[l];
+            DT gates = linear_run(c, in, L.w_t, L.wb, L.input, 1536, 1536, 0);
+            DT yo = new_rowmajor(c, {tmax, ntot, 512});
+            WOCR_CUDA(cudaMemsetAsync(yo.p, 0, (size_t)yo.numel() * 4, c->stream));
+            k::gru_layer(c, gates.p, L.r.p, L.rb.p, (const int *)lens_d->p, tmax, ntot, yo.p);
+            in = yo;
+        }
+        DT lg = linear_run(c, in, rec->lin_w, rec->lin_b, 512, rec->classes, rec->ldw, 0);  // [tmax][ntot][classes]
+        if (logits) {
+            if (logits_cap < m * rec->classes) fail(WOCR_ERR_CAPACITY, "logits buffer too small");
+            d2h(c, logits, lg.p, (size_t)m * rec->classes * 4);
+        }
+        BufP bd;
+        if (best) {
+            bd = alloc(c, (size_t)m * 4);
+            k::argmax(c, lg.p, m, rec->classes, rec->classes, (uint32_t *)bd->p, nullptr, nullptr, 1);
+            d2h(c, best, bd->p, (size_t)m * 4);
+        }
+        sync_bounded(c, 0);
+        if (lens) std::memcpy(lens, hl.data(), hl.size() * sizeof(int));
+        if (tmax_out) *tmax_out = tmax;
+    });
+}
+
+// ---- N-D graph ----------------------------------------------------------------------------
+int32_t wocr_ndgraph_create(wocr_ctx *ctx, const wocr_model *model, int32_t stop_before_softmax, wocr_ndgraph **out) {
+    return guard([&] {
+        if (!ctx || !out) fail(WOCR_ERR_INVALID, "null argument");
+        WOCR_CUDA(cudaSetDevice(ctx->c.device));
+        Model m = model_from_c(model);
+        auto *g = new wocr_ndgraph();
+        g->ctx = ctx;
+        try {
+            g->graph = build_ndgraph(&ctx->c, m, stop_before_softmax != 0);
+            WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
+        } catch (...) {
+            delete g;
+            throw;
+        }
+        *out = g;
+    });
+}
+
+void wocr_ndgraph_destroy(wocr_ndgraph *g) {
+    if (!g) return;
+    cudaSetDevice(g->ctx->c.device);
+    cudaStreamSynchronize(g->ctx->c.stream);
+    delete g;
+}
+
+static DT nd_input(Ctx *c, const float *x, const int64_t *shape, int32_t rank) {
+    if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
+    std::vector<int64_t> s(shape, shape + rank);
+    for (auto d : s)
+        if (d <= 0) fail(WOCR_ERR_INVALID, "empty input tensor");
+    return from_host(c, x, s);
+}
+
+static void put_shape(const DT &t, int64_t *out_shape, int32_t *out_rank) {
+    if (out_rank) *out_rank = t.rank();
+    if (out_shape)
+        for (int d = 0; d < t.rank(); d++) out_shape[d] = t.shape[d];
+}
+
+int32_t wocr_ndgraph_run(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank, float *out,
+                         int64_t out_cap, int64_t *out_shape, int32_t *out_rank) {
+    return guard([&] {
+        if (!g) fail(WOCR_ERR_INVALID, "null graph");
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        DT y = g->graph->run(nd_input(c, x, shape, rank));
+        put_shape(y, out_shape, out_rank);
+        if (out) {
+            if (out_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(y.shape));
+            y = to_rowmajor(c, y);
+            d2h(c, out, y.p, (size_t)y.numel() * 4);
+        }
+        sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank, uint32_t *best,
+                                float *row_max, float *row_lse, int64_t cap, int64_t *rows_out, int64_t *out_shape,
+                                int32_t *out_rank) {
+    return guard([&] {
+        if (!g) fail(WOCR_ERR_INVALID, "null graph");
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        DT y = to_rowmajor(c, g->graph->run(nd_input(c, x, shape, rank)));
+        put_shape(y, out_shape, out_rank);
+        int64_t len = y.shape.empty() ? 1 : y.shape.back();
+        int64_t rows = y.numel() / std::max<int64_t>(len, 1);
+        if (rows_out) *rows_out = rows;
+        if (cap < rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
+        BufP b = alloc(c, (size_t)rows * 4), mx = alloc(c, (size_t)rows * 4), ls = alloc(c, (size_t)rows * 4);
+        k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr, 0);
+        if (best) d2h(c, best, b->p, (size_t)rows * 4);
+        if (row_max) d2h(c, row_max, mx->p, (size_t)rows * 4);
+        if (row_lse) d2h(c, row_lse, ls->p, (size_t)rows * 4);
+        sync_bounded(c, 0);
+    });
+}
+
+static void det_input_sizes(int w, int h, int max_side, int *ow, int *oh) {
+    float ratio = std::max(w, h) > max_side ? (float)max_side / (float)std::max(w, h) : 1.0f;
+    auto rnd = [](float v) { return std::max((int)std::round(v / 32.0f) * 32, 32); };
+    *ow = rnd((float)w * ratio);
+    *oh = rnd((float)h * ratio);
+}
+
+int32_t wocr_det_input(wocr_ctx *ctx, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, float *out,
+                       int64_t out_cap, int32_t *ow_out, int32_t *oh_out, float *to_page) {
+    return guard([&] {
+        if (!ctx || !rgb || w <= 0 || h <= 0 || max_side <= 0) fail(WOCR_ERR_INVALID, "bad argument");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        int ow, oh;
+        det_input_sizes(w, h, max_side, &ow, &oh);
+        if (ow_out) *ow_out = ow;
+        if (oh_out) *oh_out = oh;
+        if (to_page) {
+            to_page[0] = (float)w / (float)ow;
+            to_page[1] = (float)h / (float)oh;
+        }
+        if (!out) return;
+        if (out_cap < (int64_t)3 * ow * oh) fail(WOCR_ERR_CAPACITY, "det_input buffer too small");
+        BufP src = alloc(c, (size_t)w * h * 3);
+        WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, (size_t)w * h * 3, cudaMemcpyHostToDevice, c->stream));
+        DT y = new_rowmajor(c, {1, 3, oh, ow});
+        k::det_prep(c, (const uint8_t *)src->p, w, h, ow, oh, 1, y.p);
+        d2h(c, out, y.p, (size_t)y.numel() * 4);
+        sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, float *prob,
+                        int64_t prob_cap, int32_t *ow_out, int32_t *oh_out, float *to_page) {
+    return guard([&] {
+        if (!g || !rgb || w <= 0 || h <= 0 || max_side <= 0) fail(WOCR_ERR_INVALID, "bad argument");
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        int ow, oh;
+        det_input_sizes(w, h, max_side, &ow, &oh);
+        if (ow_out) *ow_out = ow;
+        if (oh_out) *oh_out = oh;
+        if (to_page) {
+            to_page[0] = (float)w / (float)ow;
+            to_page[1] = (float)h / (float)oh;
+        }
+        BufP src = alloc(c, (size_t)w * h * 3);
+        WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, (size_t)w * h * 3, cudaMemcpyHostToDevice, c->stream));
+        DT x = new_nhwc(c, 1, 3, oh, ow);
+        k::det_prep(c, (const uint8_t *)src->p, w, h, ow, oh, 0, x.p);
+        DT y = to_rowmajor(c, g->graph->run(x));
+        if (prob) {
+            if (prob_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "probability buffer too small");
+            d2h(c, prob, y.p, (size_t)y.numel() * 4);
+        }
+        sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_last_run_stats(void *handle, int32_t kind, double *flops, int64_t *launches) {
+    return guard([&] {
+        if (!handle) fail(WOCR_ERR_INVALID, "null handle");
+        Stats *s = nullptr;
+        if (kind == 1) s = &((wocr_detector *)handle)->last;
+        else if (kind == 2) s = &((wocr_recognizer *)handle)->last;
+        else if (kind == 3) s = &((wocr_ndgraph *)handle)->last;
+        else fail(WOCR_ERR_INVALID, "kind must be 1 (detector), 2 (recogniser) or 3 (N-D graph)");
+        if (flops) *flops = s->flops;
+        if (launches) *launches = s->launches;
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,113 @@
+// Graph executors: the lowering and fusion passes of the reference's two executors and the
+// run loop that issues the sm_100a kernels.
+//   Graph   - src/gpu.rs:1058-1378 (4-D convolutional graphs of the ocrs models)
+//   NdGraph - src/nd.rs:428-1394  (N-D graphs of PP-OCR, with load-time fusions)
+#pragma once
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.h"
+#include "kernels.h"
+#include "model.h"
+
+namespace wocr {
+
+// A weight uploaded to the device.
+struct DevW {
+    BufP buf;
+    float *p = nullptr;
+    int64_t n = 0;
+};
+DevW upload(Ctx *c, const std::vector<float> &v);
+DevW upload(Ctx *c, const float *v, int64_t n);
+
+// A lowered convolution (dense, depthwise or Cin = 1 direct), weights laid out for its kernel.
+struct ConvW {
+    enum Kind { DENSE, DEPTHWISE, DIRECT } kind = DENSE;
+    DevW w, b;
+    int cout = 0, cin = 0, group = 1, kh = 1, kw = 1, sh = 1, sw = 1;
+    int pads[4] = {0, 0, 0, 0};  // top, left, bottom, right
+    bool same_upper = false;
+    int ldw = 0;                 // DENSE: columns of the [K][ldw] weight matrix
+    int pool_h = 1, pool_w = 1;  // DIRECT: fused MaxPool
+};
+
+// A lowered ConvTranspose: kernel == stride runs as one GEMM with a scatter epilogue.
+struct ConvTW {
+    DevW w, b;  // gemm: [cin][ldw] with column (ky*s + kx)*cout + co; else [cin][cout][kh][kw]
+    int cin = 0, cout = 0, kh = 0, kw = 0, s = 1, ldw = 0;
+    bool gemm = false;
+};
+
+ConvW lower_conv_dense(Ctx *c, const HostW &w, const std::vector<float> &bias, int group);
+ConvTW lower_convt(Ctx *c, const HostW &w, const std::vector<float> &bias, int stride);
+
+// A value while a graph runs: a device float tensor or a host integer tensor (src/nd.rs:448).
+struct Value {
+    bool is_int = false;
+    DT f;
+    std::vector<int64_t> iv;
+    std::vector<int64_t> ishape;
+};
+
+// One executed step of a lowered graph.
+struct Step {
+    enum Kind {
+        // Graph (src/gpu.rs:1088-1098)
+        G_CONV, G_DIRECT, G_DEPTHWISE, G_CONVT, G_MAXPOOL, G_SLICE, G_CONCAT, G_ACT, G_IDENTITY,
+        // NdGraph fused kinds (src/nd.rs:467-479); other NdGraph nodes run as N_GENERIC
+        N_CONV, N_CONVT, N_LINEAR, N_AFFINE, N_LAYERNORM, N_GENERIC
+    } kind;
+    int node = -1;                        // index into the (rewritten) node list
+    std::vector<std::string> inputs;
+    std::string output;
+    ConvW conv;
+    ConvTW convt;
+    int act = 0;
+    std::string residual, scale;          // N_CONV fusions
+    DevW lw, lb;                          // N_LINEAR [K][ldw] + bias
+    int lk = 0, ln = 0, ldw = 0;
+    DevW st;                              // N_AFFINE scale|shift, N_LAYERNORM gamma|beta
+    int ln_len = 0;
+    float eps = 1e-5f;
+    std::vector<int64_t> starts, ends, axes;  // G_SLICE
+};
+
+class Executor {
+  public:
+    Ctx *ctx;
+    Model model;                          // nodes rewritten by the fusion pass
+    std::vector<Step> steps;
+    std::map<std::string, DT> weights;    // float initializers read by generic steps
+    std::string input, output;
+    std::map<std::string, int> last_use;  // value -> last step reading it
+
+    explicit Executor(Ctx *c) : ctx(c) {}
+    // Run on `x`; returns the output tensor.
+    DT run(const DT &x);
+    void finalize();  // uploads generic weights, computes last uses
+
+  protected:
+    Value get(std::map<std::string, Value> &vals, const std::string &name);
+    DT getf(std::map<std::string, Value> &vals, const std::string &name);
+    void exec_step(const Step &s, std::map<std::string, Value> &vals);
+    void exec_generic(const Node &n, std::map<std::string, Value> &vals);
+};
+
+// Graph::build (src/gpu.rs:1104-1240): the graph up to (not including) the first node of type
+// `stop`, if given; `stop_node` receives that node.
+std::unique_ptr<Executor> build_graph(Ctx *c, const Model &m, const char *stop, Node *stop_node);
+// NdGraph::new (src/nd.rs:505-817).
+std::unique_ptr<Executor> build_ndgraph(Ctx *c, const Model &m, bool stop_before_softmax);
+
+// Helpers shared with the API layer.
+DT to_nhwc(Ctx *c, const DT &x);
+DT to_rowmajor(Ctx *c, const DT &x);
+DT conv_run(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale);
+DT linear_run(Ctx *c, const DT &x, const DevW &w, const DevW &b, int K, int N, int ldw, int act);
+DT from_host(Ctx *c, const float *x, const std::vector<int64_t> &shape);
+
+}  // namespace wocr

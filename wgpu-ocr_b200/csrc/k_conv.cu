@@ -1,0 +1,396 @@
+// Convolution family on channels-last tensors: implicit-GEMM dense conv / linear / strided
+// ConvTranspose (CUDA-core fp32 path), Cin = 1 direct conv with fused MaxPool, depthwise conv,
+// general ConvTranspose.
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+
+namespace wocr {
+namespace k {
+
+namespace {
+
+__device__ __forceinline__ float erf_as(float v) {
+    float s = (v > 0.f) - (v < 0.f);
+    float a = fabsf(v);
+    float t = 1.0f / (1.0f + 0.3275911f * a);
+    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    return s * (1.0f - poly * expf(-a * a));
+}
+
+__device__ __forceinline__ float act_f(float v, int act) {
+    switch (act) {
+    case 1: return fmaxf(v, 0.f);
+    case 2: return 1.0f / (1.0f + expf(-v));
+    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
+    case 4: return v / (1.0f + expf(-v));
+    default: return v;
+    }
+}
+
+constexpr int BM = 128, BN = 64, BK = 16;
+
+// 256 threads; thread (tx, ty) = (tid % 16, tid / 16) owns pixels tx*8..+8 and channels
+// ty*4..+4 of the 128 x 64 tile.  A tile is staged k-major so the FMA loop reads it as float4.
+// VEC: cin % 8 == 0 and 16-byte aligned rows, so a thread's 8 consecutive k (one tap, 8 input
+// channels) load as two float4.
+template <bool VEC>
+__global__ void __launch_bounds__(256) k_conv_gemm(ConvP p) {
+    __shared__ __align__(16) float As[BK][BM + 4];
+    __shared__ __align__(16) float Bs[BK][BN];
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int64_t M = (int64_t)p.n * p.oh * p.ow;
+    const int64_t m0 = (int64_t)blockIdx.x * BM;
+    const int n0 = blockIdx.y * BN;
+    const int K = p.kh * p.kw * p.cin;
+
+    // A loader: pixel am of the tile, k slice ak .. ak + 8
+    const int am = tid & (BM - 1);
+    const int ak = (tid >> 7) * 8;
+    const int64_t m = m0 + am;
+    const bool mvalid = m < M;
+    int ox = 0, oy = 0, nb = 0;
+    if (mvalid) {
+        ox = (int)(m % p.ow);
+        int64_t t = m / p.ow;
+        oy = (int)(t % p.oh);
+        nb = (int)(t / p.oh);
+    }
+    const int iy0 = oy * p.sh - p.pt, ix0 = ox * p.sw - p.pl;
+    const float *xb = p.x + (int64_t)nb * p.x_n;
+    const float *scb = p.insc ? p.insc + (int64_t)nb * p.cin : nullptr;
+    // B loader: k row tid / 16, channels (tid % 16) * 4 .. + 4
+    const int bk = tid >> 4, bc = (tid & 15) * 4;
+
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
+
+    for (int k0 = 0; k0 < K; k0 += BK) {
+        float av[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) av[e] = 0.f;
+        if (VEC) {
+            int kq = k0 + ak;
+            if (mvalid && kq < K) {
+                int tap = kq / p.cin, ci = kq - tap * p.cin;
+                int ky = tap / p.kw, kx = tap - ky * p.kw;
+                int iy = iy0 + ky, ix = ix0 + kx;
+                if (iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
+                    const float4 *src = reinterpret_cast<const float4 *>(xb + ((int64_t)iy * p.w + ix) * p.x_pix + ci);
+                    float4 v0 = src[0], v1 = src[1];
+                    av[0] = v0.x; av[1] = v0.y; av[2] = v0.z; av[3] = v0.w;
+                    av[4] = v1.x; av[5] = v1.y; av[6] = v1.z; av[7] = v1.w;
+                    if (scb) {
+#pragma unroll
+                        for (int e = 0; e < 8; e++) av[e] *= scb[ci + e];
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                int kq = k0 + ak + e;
+                if (mvalid && kq < K) {
+                    int tap = kq / p.cin, ci = kq - tap * p.cin;
+                    int ky = tap / p.kw, kx = tap - ky * p.kw;
+                    int iy = iy0 + ky, ix = ix0 + kx;
+                    if (iy >= 0 && iy < p.h && ix >= 0 && ix < p.w) {
+                        float v = xb[((int64_t)iy * p.w + ix) * p.x_pix + ci];
+                        if (scb) v *= scb[ci];
+                        av[e] = v;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) As[ak + e][am] = av[e];
+        {
+            float4 bv = make_float4(0.f, 0.f, 0.f, 0.f);
+            int kq = k0 + bk;
+            if (kq < K && n0 + bc < p.ldw) bv = *reinterpret_cast<const float4 *>(p.wt + (int64_t)kq * p.ldw + n0 + bc);
+            *reinterpret_cast<float4 *>(&Bs[bk][bc]) = bv;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < BK; kk++) {
+            float4 a0 = *reinterpret_cast<const float4 *>(&As[kk][tx * 8]);
+            float4 a1 = *reinterpret_cast<const float4 *>(&As[kk][tx * 8 + 4]);
+            float4 b = *reinterpret_cast<const float4 *>(&Bs[kk][ty * 4]);
+            float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] += a[i] * bb[j];
+        }
+        __syncthreads();
+    }
+
+    // epilogue: bias, activation, residual; channels-last stores
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int64_t mm = m0 + tx * 8 + i;
+        if (mm >= M) continue;
+        int eox = (int)(mm % p.ow);
+        int64_t t = mm / p.ow;
+        int eoy = (int)(t % p.oh);
+        int enb = (int)(t / p.oh);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            int col = n0 + ty * 4 + j;
+            if (col >= p.cout) continue;
+            if (p.scatter) {
+                int s = p.scatter;
+                int co = col % p.scat_cout, tap = col / p.scat_cout;
+                int ky = tap / s, kx = tap % s;
+                int yy = eoy * s + ky, xx = eox * s + kx;
+                int ow2 = p.ow * s;
+                float v = act_f(acc[i][j] + (p.bias ? p.bias[co] : 0.f), p.act);
+                p.y[(int64_t)enb * p.y_n + ((int64_t)yy * ow2 + xx) * p.y_pix + co] = v;
+            } else {
+                float v = act_f(acc[i][j] + (p.bias ? p.bias[col] : 0.f), p.act);
+                int64_t pix = (int64_t)eoy * p.ow + eox;
+                if (p.res) v += p.res[(int64_t)enb * p.res_n + pix * p.res_pix + col];
+                p.y[(int64_t)enb * p.y_n + pix * p.y_pix + col] = v;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Cin = 1 direct conv: one thread per output pixel (after the fused pool), all channels.
+template <int COUT>
+__global__ void k_conv_direct(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int n, int h, int w,
+                              const float *__restrict__ wt, const float *__restrict__ bias, int kh, int kw, int pad,
+                              int act, int ph, int pw, float *__restrict__ y, int64_t y_n, int64_t y_pix, int oh,
+                              int ow) {
+    __shared__ float ws[7 * 7 * COUT];
+    __shared__ float bs[COUT];
+    for (int i = threadIdx.x; i < kh * kw * COUT; i += blockDim.x) ws[i] = wt[i];
+    for (int i = threadIdx.x; i < COUT; i += blockDim.x) bs[i] = bias[i];
+    __syncthreads();
+    int64_t total = (int64_t)n * oh * ow;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int ox = (int)(i % ow);
+        int oy = (int)((i / ow) % oh);
+        int nb = (int)(i / ((int64_t)ow * oh));
+        const float *xb = x + nb * x_n;
+        float best[COUT];
+#pragma unroll
+        for (int c = 0; c < COUT; c++) best[c] = -3.4e38f;
+        for (int py = 0; py < ph; py++)
+            for (int px = 0; px < pw; px++) {
+                int cy = oy * ph + py, cx = ox * pw + px;
+                float acc[COUT];
+#pragma unroll
+                for (int c = 0; c < COUT; c++) acc[c] = bs[c];
+                for (int ky = 0; ky < kh; ky++) {
+                    int iy = cy + ky - pad;
+                    if (iy < 0 || iy >= h) continue;
+                    for (int kx = 0; kx < kw; kx++) {
+                        int ix = cx + kx - pad;
+                        if (ix < 0 || ix >= w) continue;
+                        float v = xb[((int64_t)iy * w + ix) * x_pix];
+                        const float *wr = ws + (ky * kw + kx) * COUT;
+#pragma unroll
+                        for (int c = 0; c < COUT; c++) acc[c] += v * wr[c];
+                    }
+                }
+#pragma unroll
+                for (int c = 0; c < COUT; c++) best[c] = fmaxf(best[c], act_f(acc[c], act));
+            }
+        float *yo = y + nb * y_n + ((int64_t)oy * ow + ox) * y_pix;
+#pragma unroll
+        for (int c = 0; c < COUT; c++) yo[c] = best[c];
+    }
+}
+
+// Generic-cout direct conv: one thread per (output pixel, channel).
+__global__ void k_conv_direct_any(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int n, int h, int w,
+                                  const float *__restrict__ wt, const float *__restrict__ bias, int cout, int kh,
+                                  int kw, int pad, int act, int ph, int pw, float *__restrict__ y, int64_t y_n,
+                                  int64_t y_pix, int oh, int ow) {
+    int64_t total = (int64_t)n * oh * ow * cout;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int c = (int)(i % cout);
+        int64_t pix = i / cout;
+        int ox = (int)(pix % ow);
+        int oy = (int)((pix / ow) % oh);
+        int nb = (int)(pix / ((int64_t)ow * oh));
+        const float *xb = x + nb * x_n;
+        float best = -3.4e38f;
+        for (int py = 0; py < ph; py++)
+            for (int px = 0; px < pw; px++) {
+                int cy = oy * ph + py, cx = ox * pw + px;
+                float acc = bias[c];
+                for (int ky = 0; ky < kh; ky++) {
+                    int iy = cy + ky - pad;
+                    if (iy < 0 || iy >= h) continue;
+                    for (int kx = 0; kx < kw; kx++) {
+                        int ix = cx + kx - pad;
+                        if (ix < 0 || ix >= w) continue;
+                        acc += xb[((int64_t)iy * w + ix) * x_pix] * wt[(ky * kw + kx) * cout + c];
+                    }
+                }
+                best = fmaxf(best, act_f(acc, act));
+            }
+        y[nb * y_n + ((int64_t)oy * ow + ox) * y_pix + c] = best;
+    }
+}
+
+// Depthwise: one thread per (output pixel, 4 channels) when c % 4 == 0, else per channel.
+template <bool VEC4>
+__global__ void k_depthwise(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int n, int h, int w, int ch,
+                            const float *__restrict__ wt, const float *__restrict__ bias, int kh, int kw, int sh, int sw,
+                            int pt, int pl, int oh, int ow, int act, float *__restrict__ y, int64_t y_n, int64_t y_pix) {
+    const int cv = VEC4 ? ch / 4 : ch;
+    int64_t total = (int64_t)n * oh * ow * cv;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int cq = (int)(i % cv);
+        int64_t pix = i / cv;
+        int ox = (int)(pix % ow);
+        int oy = (int)((pix / ow) % oh);
+        int nb = (int)(pix / ((int64_t)ow * oh));
+        const float *xb = x + nb * x_n;
+        if (VEC4) {
+            int c = cq * 4;
+            float4 acc = *reinterpret_cast<const float4 *>(bias + c);
+            for (int ky = 0; ky < kh; ky++) {
+                int iy = oy * sh + ky - pt;
+                if (iy < 0 || iy >= h) continue;
+                for (int kx = 0; kx < kw; kx++) {
+                    int ix = ox * sw + kx - pl;
+                    if (ix < 0 || ix >= w) continue;
+                    float4 v = *reinterpret_cast<const float4 *>(xb + ((int64_t)iy * w + ix) * x_pix + c);
+                    float4 wv = *reinterpret_cast<const float4 *>(wt + (int64_t)(ky * kw + kx) * ch + c);
+                    acc.x += v.x * wv.x; acc.y += v.y * wv.y; acc.z += v.z * wv.z; acc.w += v.w * wv.w;
+                }
+            }
+            float4 o = make_float4(act_f(acc.x, act), act_f(acc.y, act), act_f(acc.z, act), act_f(acc.w, act));
+            *reinterpret_cast<float4 *>(y + nb * y_n + ((int64_t)oy * ow + ox) * y_pix + c) = o;
+        } else {
+            int c = cq;
+            float acc = bias[c];
+            for (int ky = 0; ky < kh; ky++) {
+                int iy = oy * sh + ky - pt;
+                if (iy < 0 || iy >= h) continue;
+                for (int kx = 0; kx < kw; kx++) {
+                    int ix = ox * sw + kx - pl;
+                    if (ix < 0 || ix >= w) continue;
+                    acc += xb[((int64_t)iy * w + ix) * x_pix + c] * wt[(int64_t)(ky * kw + kx) * ch + c];
+                }
+            }
+            y[nb * y_n + ((int64_t)oy * ow + ox) * y_pix + c] = act_f(acc, act);
+        }
+    }
+}
+
+// General ConvTranspose: each output gathers only the taps of its parity (src/gpu.rs:443-456).
+__global__ void k_convt_gather(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int n, int h, int w, int cin,
+                               const float *__restrict__ wt, const float *__restrict__ bias, int cout, int kh, int kw,
+                               int s, int act, float *__restrict__ y, int64_t y_n, int64_t y_pix, int oh, int ow) {
+    int64_t total = (int64_t)n * oh * ow * cout;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int co = (int)(i % cout);
+        int64_t pix = i / cout;
+        int ox = (int)(pix % ow);
+        int oy = (int)((pix / ow) % oh);
+        int nb = (int)(pix / ((int64_t)ow * oh));
+        float acc = bias ? bias[co] : 0.f;
+        for (int ky = oy % s; ky < kh && ky <= oy; ky += s) {
+            int iy = (oy - ky) / s;
+            if (iy >= h) continue;
+            for (int kx = ox % s; kx < kw && kx <= ox; kx += s) {
+                int ix = (ox - kx) / s;
+                if (ix >= w) continue;
+                const float *xr = x + nb * x_n + ((int64_t)iy * w + ix) * x_pix;
+                for (int ci = 0; ci < cin; ci++) acc += xr[ci] * wt[(((int64_t)ci * cout + co) * kh + ky) * kw + kx];
+            }
+        }
+        y[nb * y_n + ((int64_t)oy * ow + ox) * y_pix + co] = act_f(acc, act);
+    }
+}
+
+inline int grid_for(Ctx *c, int64_t work, int per_block = 256) {
+    int64_t g = (work + per_block - 1) / per_block;
+    int64_t cap = (int64_t)c->sm_count * 16;
+    if (g > cap) g = cap;
+    if (g < 1) g = 1;
+    return (int)g;
+}
+
+}  // namespace
+
+void conv_gemm(Ctx *c, const ConvP &p) {
+    int64_t M = (int64_t)p.n * p.oh * p.ow;
+    if (M == 0 || p.cout == 0) return;
+    dim3 grid((unsigned)((M + BM - 1) / BM), (unsigned)((p.cout + BN - 1) / BN));
+    Prof pf(c, p.scatter ? "convt_gemm" : "conv_gemm", 2.0 * (double)M * p.cout * p.kh * p.kw * p.cin,
+            4.0 * ((double)p.n * p.h * p.w * p.cin + (double)p.kh * p.kw * p.cin * p.cout + (double)M * p.cout));
+    bool vec = (p.cin % 8 == 0) && (p.x_pix % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0) &&
+               (p.x_n % 4 == 0);
+    if (vec) k_conv_gemm<true><<<grid, 256, 0, c->stream>>>(p);
+    else k_conv_gemm<false><<<grid, 256, 0, c->stream>>>(p);
+    WOCR_LAUNCHED(c);
+    c->flops += 2.0 * (double)M * p.cout * p.kh * p.kw * p.cin;
+}
+
+void conv_direct(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, const float *wt,
+                 const float *bias, int cout, int kh, int kw, int pad, int act, int ph, int pw, float *y,
+                 int64_t y_n, int64_t y_pix, int oh, int ow) {
+    int64_t pix = (int64_t)n * oh * ow;
+    if (pix == 0) return;
+    Prof pf(c, "conv_direct", 2.0 * (double)pix * ph * pw * cout * kh * kw,
+            4.0 * ((double)n * h * w + (double)pix * cout));
+    if (kh * kw <= 49 && (cout == 16 || cout == 32)) {
+        if (cout == 16)
+            k_conv_direct<16><<<grid_for(c, pix), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, kh, kw, pad,
+                                                                       act, ph, pw, y, y_n, y_pix, oh, ow);
+        else
+            k_conv_direct<32><<<grid_for(c, pix), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, kh, kw, pad,
+                                                                       act, ph, pw, y, y_n, y_pix, oh, ow);
+    } else {
+        k_conv_direct_any<<<grid_for(c, pix * cout), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, cout, kh,
+                                                                          kw, pad, act, ph, pw, y, y_n, y_pix, oh, ow);
+    }
+    WOCR_LAUNCHED(c);
+    c->flops += 2.0 * (double)pix * ph * pw * cout * kh * kw;
+}
+
+void depthwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, int ch, const float *wt,
+               const float *bias, int kh, int kw, int sh, int sw, int pt, int pl, int oh, int ow, int act, float *y,
+               int64_t y_n, int64_t y_pix) {
+    int64_t pix = (int64_t)n * oh * ow;
+    if (pix == 0) return;
+    Prof pf(c, "depthwise", 2.0 * (double)pix * ch * kh * kw, 4.0 * ch * ((double)n * h * w + (double)pix));
+    bool vec = ch % 4 == 0 && x_pix % 4 == 0 && y_pix % 4 == 0 && x_n % 4 == 0 && y_n % 4 == 0 &&
+               ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+    if (vec)
+        k_depthwise<true><<<grid_for(c, pix * ch / 4), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, ch, wt, bias, kh,
+                                                                            kw, sh, sw, pt, pl, oh, ow, act, y, y_n, y_pix);
+    else
+        k_depthwise<false><<<grid_for(c, pix * ch), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, ch, wt, bias, kh, kw,
+                                                                         sh, sw, pt, pl, oh, ow, act, y, y_n, y_pix);
+    WOCR_LAUNCHED(c);
+    c->flops += 2.0 * (double)pix * ch * kh * kw;
+}
+
+void convt_gather(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, int cin, const float *wt,
+                  const float *bias, int cout, int kh, int kw, int s, int act, float *y, int64_t y_n, int64_t y_pix,
+                  int oh, int ow) {
+    int64_t total = (int64_t)n * oh * ow * cout;
+    if (total == 0) return;
+    Prof pf(c, "convt_gather", 2.0 * (double)n * h * w * cin * cout * kh * kw,
+            4.0 * ((double)n * h * w * cin + (double)total));
+    k_convt_gather<<<grid_for(c, total), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, cin, wt, bias, cout, kh, kw, s,
+                                                             act, y, y_n, y_pix, oh, ow);
+    WOCR_LAUNCHED(c);
+    c->flops += 2.0 * (double)n * h * w * cin * cout * kh * kw;
+}
+
+}  // namespace k
+}  // namespace wocr

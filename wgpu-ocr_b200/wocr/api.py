@@ -1,0 +1,307 @@
+"""The reference crate's public API for the hot path, over the C ABI.
+
+  Gpu         - src/gpu.rs:825-1056   (`Gpu::new(lines)`, submit_wait, pool)
+  Detector    - src/gpu.rs:1380-1431  (`new`, `detect_page`, `detect`)
+  Recognizer  - src/gpu.rs:1433-1603  (`new`, `recognize`)
+  NdGraph     - src/nd.rs:428-1394    (`new`, `run`, `argmax`, `det_input`)
+
+Errors are raised as `WocrError` (the reference returns `Err(String)` from the same calls).
+All work runs in hand-written sm_100a kernels of libwocr.so; nothing here computes on the CPU
+except the greedy CTC decode, which the reference also runs on the host.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import _lib as L
+from .model import Model
+
+
+class Gpu:
+    """`Gpu::new(lines)` (src/gpu.rs:850): one CUDA device, one stream, a pooled allocator."""
+
+    def __init__(self, lines: int = 8, device: int = 0):
+        h = ctypes.c_void_p()
+        L.check(L.lib().wocr_ctx_create(int(device), int(lines), ctypes.byref(h)))
+        self.h = h
+        self.device = device
+        self.lines = lines
+
+    @property
+    def adapter(self) -> str:
+        buf = ctypes.create_string_buffer(256)
+        L.check(L.lib().wocr_ctx_describe(self.h, buf, 256))
+        return buf.value.decode()
+
+    @property
+    def stream(self) -> int:
+        """The cudaStream_t all work of this device context runs on."""
+        return int(L.lib().wocr_ctx_stream(self.h) or 0)
+
+    def submit_wait(self, timeout_ms: int = 0):
+        """Wait for all queued work (src/gpu.rs:1005-1008), optionally bounded."""
+        L.check(L.lib().wocr_ctx_sync(self.h, int(timeout_ms)))
+
+    def pool_bytes(self) -> int:
+        return int(L.lib().wocr_ctx_pool_bytes(self.h))
+
+    def launches(self) -> int:
+        return int(L.lib().wocr_ctx_launches(self.h))
+
+    def profile(self, on: bool):
+        """Start (clearing earlier records) or stop per-kernel CUDA-event timing."""
+        L.check(L.lib().wocr_ctx_profile(self.h, int(bool(on))))
+
+    def profile_report(self):
+        """[{kernel, launches, ms, flops, bytes}] of the launches recorded since profile(True)."""
+        import json
+        buf = ctypes.create_string_buffer(1 << 16)
+        L.check(L.lib().wocr_ctx_profile_report(self.h, buf, len(buf)))
+        return json.loads(buf.value.decode())
+
+    def close(self):
+        if self.h:
+            L.lib().wocr_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class _Handle:
+    kind = 0
+
+    def stats(self) -> Tuple[float, int]:
+        """(FLOPs of convolutions/matmuls, kernel launches) of the last run of this handle."""
+        f, n = ctypes.c_double(), ctypes.c_int64()
+        L.check(L.lib().wocr_last_run_stats(self.h, self.kind, ctypes.byref(f), ctypes.byref(n)))
+        return f.value, n.value
+
+
+class Detector(_Handle):
+    """`Detector` (src/gpu.rs:1380-1431): the ocrs detection model lowered by Graph::build."""
+
+    kind = 1
+
+    def __init__(self, gpu: Gpu, model: Model):
+        self.gpu = gpu
+        holder = L.CModelHolder(model)
+        h = ctypes.c_void_p()
+        L.check(L.lib().wocr_detector_create(gpu.h, holder.ref(), ctypes.byref(h)))
+        self.h = h
+
+    def detect_page(self, rgb: np.ndarray, w: int, h: int, threshold: float) -> np.ndarray:
+        """RGB bytes of a w x h page -> bit mask [h, ceil(w/32)] u32 (src/gpu.rs:1393-1422)."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        if rgb.size < w * h * 3:
+            raise ValueError("rgb smaller than w * h * 3")
+        out = np.empty((h, (w + 31) // 32), np.uint32)
+        L.check(L.lib().wocr_detect_page(self.h, L.ptr(rgb), w, h, float(threshold), L.ptr(out)))
+        return out
+
+    def detect_pages(self, rgb: np.ndarray, threshold: float) -> np.ndarray:
+        """n pages [n, h, w, 3] u8 of one size in one pass -> masks [n, h, ceil(w/32)]."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        n, h, w, _ = rgb.shape
+        out = np.empty((n, h, (w + 31) // 32), np.uint32)
+        L.check(L.lib().wocr_detect_pages(self.h, L.ptr(rgb), n, w, h, float(threshold), L.ptr(out)))
+        return out
+
+    def detect_pages_device(self, d_rgb: int, n: int, w: int, h: int, threshold: float, d_mask: int):
+        """The same on device pointers, queued on the context stream (no wait)."""
+        L.check(L.lib().wocr_detect_pages_device(self.h, ctypes.c_void_p(d_rgb), n, w, h, float(threshold),
+                                                 ctypes.c_void_p(d_mask)))
+
+    def detect(self, inp: np.ndarray) -> np.ndarray:
+        """The probability map of a [1, 1, h, w] input (src/gpu.rs:1425-1430)."""
+        inp = np.ascontiguousarray(inp, np.float32)
+        h, w = inp.shape[-2:]
+        oh, ow = ctypes.c_int32(), ctypes.c_int32()
+        out = np.empty(h * w, np.float32)
+        st = L.lib().wocr_detect(self.h, L.ptr(inp), h, w, L.ptr(out), out.size, ctypes.byref(oh), ctypes.byref(ow))
+        if st == 8:  # larger output than input: once more with the size it reported
+            out = np.empty(oh.value * ow.value, np.float32)
+            st = L.lib().wocr_detect(self.h, L.ptr(inp), h, w, L.ptr(out), out.size, ctypes.byref(oh),
+                                     ctypes.byref(ow))
+        L.check(st)
+        return out[: oh.value * ow.value].reshape(oh.value, ow.value)
+
+    def close(self):
+        if getattr(self, "h", None):
+            L.lib().wocr_detector_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Recognizer(_Handle):
+    """`Recognizer` (src/gpu.rs:1433-1603): conv trunk, 2 bidirectional GRU layers, output layer."""
+
+    kind = 2
+
+    def __init__(self, gpu: Gpu, model: Model, lines: int = 8):
+        self.gpu = gpu
+        holder = L.CModelHolder(model)
+        h = ctypes.c_void_p()
+        L.check(L.lib().wocr_recognizer_create(gpu.h, holder.ref(), int(lines), ctypes.byref(h)))
+        self.h = h
+
+    def dims(self, batches) -> Tuple[int, int, int]:
+        bn = (ctypes.c_int32 * len(batches))(*[int(b[1]) for b in batches])
+        bw = (ctypes.c_int32 * len(batches))(*[int(b[2]) for b in batches])
+        t, n, c = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        L.check(L.lib().wocr_recognizer_dims(self.h, bn, bw, len(batches), ctypes.byref(t), ctypes.byref(n),
+                                             ctypes.byref(c)))
+        return t.value, n.value, c.value
+
+    def recognize(self, batches: Sequence[Tuple[np.ndarray, int, int]], want_logits: bool = True):
+        """Batches of (data [n, 1, 64, w] f32, n, w) -> (logits [tmax, ntot, classes] or None,
+        tmax, lens, best [tmax, ntot]).  Rows t >= lens[line] of logits/best are unspecified."""
+        tmax, ntot, classes = self.dims(batches)
+        datas = [np.ascontiguousarray(b[0], np.float32) for b in batches]
+        ptrs = (ctypes.c_void_p * len(batches))(*[d.ctypes.data for d in datas])
+        bn = (ctypes.c_int32 * len(batches))(*[int(b[1]) for b in batches])
+        bw = (ctypes.c_int32 * len(batches))(*[int(b[2]) for b in batches])
+        logits = np.empty((tmax, ntot, classes), np.float32) if want_logits else None
+        best = np.empty((tmax, ntot), np.uint32)
+        lens = (ctypes.c_int32 * ntot)()
+        tm = ctypes.c_int32()
+        L.check(L.lib().wocr_recognize(self.h, ptrs, bn, bw, len(batches),
+                                       L.ptr(logits) if logits is not None else None,
+                                       logits.size if logits is not None else 0, lens, L.ptr(best), ctypes.byref(tm)))
+        return logits, tm.value, list(lens), best
+
+    def close(self):
+        if getattr(self, "h", None):
+            L.lib().wocr_recognizer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class NdGraph(_Handle):
+    """`NdGraph` (src/nd.rs:428-1394): the N-D executor with its load-time fusions."""
+
+    kind = 3
+
+    def __init__(self, gpu: Gpu, model: Model, stop_before_softmax: bool = False):
+        self.gpu = gpu
+        holder = L.CModelHolder(model)
+        h = ctypes.c_void_p()
+        L.check(L.lib().wocr_ndgraph_create(gpu.h, holder.ref(), int(bool(stop_before_softmax)), ctypes.byref(h)))
+        self.h = h
+        self._cap = 1 << 20
+
+    def run(self, x: np.ndarray) -> np.ndarray:
+        """NdGraph::run (src/nd.rs:834-1195) on a host tensor; the output read back."""
+        x = np.ascontiguousarray(x, np.float32)
+        shp = (ctypes.c_int64 * x.ndim)(*x.shape)
+        oshape = (ctypes.c_int64 * 6)()
+        orank = ctypes.c_int32()
+        while True:
+            out = np.empty(self._cap, np.float32)
+            st = L.lib().wocr_ndgraph_run(self.h, L.ptr(x), shp, x.ndim, L.ptr(out), out.size, oshape,
+                                          ctypes.byref(orank))
+            shape = tuple(oshape[i] for i in range(orank.value))
+            if st == 8 and orank.value > 0:
+                self._cap = int(np.prod(shape))
+                continue
+            L.check(st)
+            return out[: int(np.prod(shape))].reshape(shape)
+
+    def argmax(self, x: np.ndarray):
+        """run + arg-max over the last axis per row (ties -> lowest index, src/nd.rs:360-391).
+        Returns (best [rows], row_max [rows], row_lse [rows], output shape)."""
+        x = np.ascontiguousarray(x, np.float32)
+        shp = (ctypes.c_int64 * x.ndim)(*x.shape)
+        cap = max(int(np.prod(x.shape)), 1 << 16)
+        while True:
+            best = np.empty(cap, np.uint32)
+            mx = np.empty(cap, np.float32)
+            lse = np.empty(cap, np.float32)
+            rows = ctypes.c_int64()
+            oshape = (ctypes.c_int64 * 6)()
+            orank = ctypes.c_int32()
+            st = L.lib().wocr_ndgraph_run_argmax(self.h, L.ptr(x), shp, x.ndim, L.ptr(best), L.ptr(mx), L.ptr(lse),
+                                                 cap, ctypes.byref(rows), oshape, ctypes.byref(orank))
+            if st == 8 and rows.value > cap:
+                cap = rows.value
+                continue
+            L.check(st)
+            r = rows.value
+            shape = tuple(oshape[i] for i in range(orank.value))
+            return best[:r], mx[:r], lse[:r], shape
+
+    def ppdet_page(self, rgb: np.ndarray, w: int, h: int, max_side: int):
+        """det_input + run on one page (src/bin/ocr-bench.rs:186-200): (prob [oh, ow], to_page)."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        ow, oh = ctypes.c_int32(), ctypes.c_int32()
+        tp = (ctypes.c_float * 2)()
+        L.check(L.lib().wocr_det_input(self.gpu.h, L.ptr(rgb), w, h, max_side, None, 0, ctypes.byref(ow),
+                                       ctypes.byref(oh), tp))
+        prob = np.empty((oh.value, ow.value), np.float32)
+        L.check(L.lib().wocr_ppdet_page(self.h, L.ptr(rgb), w, h, max_side, L.ptr(prob), prob.size,
+                                        ctypes.byref(ow), ctypes.byref(oh), tp))
+        return prob, (tp[0], tp[1])
+
+    @staticmethod
+    def det_input(gpu: Gpu, rgb: np.ndarray, w: int, h: int, max_side: int):
+        """NdGraph::det_input (src/nd.rs:1353-1369): ([1, 3, oh, ow] f32, to_page factors)."""
+        rgb = np.ascontiguousarray(rgb, np.uint8)
+        ow, oh = ctypes.c_int32(), ctypes.c_int32()
+        tp = (ctypes.c_float * 2)()
+        L.check(L.lib().wocr_det_input(gpu.h, L.ptr(rgb), w, h, max_side, None, 0, ctypes.byref(ow),
+                                       ctypes.byref(oh), tp))
+        out = np.empty((1, 3, oh.value, ow.value), np.float32)
+        L.check(L.lib().wocr_det_input(gpu.h, L.ptr(rgb), w, h, max_side, L.ptr(out), out.size, ctypes.byref(ow),
+                                       ctypes.byref(oh), tp))
+        return out, (tp[0], tp[1])
+
+    def close(self):
+        if getattr(self, "h", None):
+            L.lib().wocr_ndgraph_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---- host-side greedy CTC (the reference also decodes on the CPU) ----------------------------
+def ocrs_decode(best_col: Sequence[int], steps: int, width: int, alphabet: str) -> str:
+    """Greedy CTC of src/bin/ocr-bench.rs:62-74 over per-step best classes of one line: blank 0
+    dropped, repeats merged, characters starting at t*4 >= width (in the padding) dropped."""
+    s, prev = [], 0
+    for t in range(steps):
+        b = int(best_col[t])
+        if b != 0 and b != prev and t * 4 < width:
+            s.append(alphabet[b - 1])
+        prev = b
+    return "".join(s)
+
+
+def pp_decode(best: Sequence[int], chars: List[str]) -> str:
+    """`Dictionary::decode` (src/ppocr.rs:23-33): repeats merged, blanks dropped."""
+    out, prev = [], 0
+    for c in best:
+        c = int(c)
+        if c != 0 and c != prev:
+            out.append(chars[c] if c < len(chars) else "")
+        prev = c
+    return "".join(out)
