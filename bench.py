@@ -66,8 +66,8 @@ class Clocks:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
-    def __init__(self, bus_id: str | None):
-        self.bus = (bus_id or "").lower()
+    def __init__(self, bus_id):
+        self.bus = bus_id if isinstance(bus_id, int) else None   # torch's pci_bus_id (an int)
         self.proc = None
         self.lines = []
 
@@ -94,7 +94,13 @@ class Clocks:
         except Exception:
             self.proc.kill()
         rows = [r.split(", ") for r in self.lines if r]
-        mine = [r for r in rows if len(r) >= 10 and self.bus and self.bus.endswith(r[1].lower()[-12:])] or \
+
+        def bus_of(field):  # "00000000:1B:00.0" -> 0x1b
+            try:
+                return int(field.split(":")[1], 16)
+            except Exception:
+                return None
+        mine = [r for r in rows if len(r) >= 10 and self.bus is not None and bus_of(r[1]) == self.bus] or \
                [r for r in rows if len(r) >= 10 and r[0] == "0"]
         sm = sorted(float(r[2]) for r in mine if r[2].replace(".", "").isdigit())
         mx = max((float(r[3]) for r in mine if r[3].replace(".", "").isdigit()), default=None)

@@ -152,3 +152,15 @@ def test_unsupported_and_shape_errors(gpu):
     with pytest.raises(wocr.WocrError) as e:
         wocr.Detector(gpu, b.model("image", y))
     assert e.value.code == 2
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 120, 97), (300, 120, 360), (257, 512, 1536), (130, 120, 18709),
+                                   (64, 240, 120), (7, 256, 1536)])
+def test_linear_shapes(gpu, m, k, n):
+    """MatMul with a constant [K, N] weight + bias (the tensor-core GEMM with K padded to 64 and
+    N over several tiles), against the oracle's fp32 GEMM."""
+    b = _Builder(20 + n)
+    y = b.linear("x", k, n, init="he")
+    mdl = b.model("x", y)
+    x = rnd(m, k)
+    close(run_nd(gpu, mdl, x), ref.run_onnx(mdl, x), tol=5e-5)

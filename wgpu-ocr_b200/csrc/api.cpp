@@ -30,6 +30,7 @@ struct wocr_detector {
 struct GruLayer {
     DevW w_t, wb, r, rb;  // w_t [in][1536], wb [2][768] (input bias), r [2][768][256], rb [2][768]
     int input = 0;
+    std::shared_ptr<k::UmmaW> uw;  // the projection on the tensor cores
 };
 
 struct wocr_recognizer {
@@ -38,6 +39,7 @@ struct wocr_recognizer {
     int pool_kh = 1;
     GruLayer layers[2];
     DevW lin_w, lin_b;  // [512][ldw], bias [ldw]
+    std::shared_ptr<k::UmmaW> lin_uw;
     int classes = 0, ldw = 0;
     int lines = 8;
     Stats last;
@@ -81,15 +83,30 @@ struct RunScope {
     }
 };
 
+// The device error word of bounded kernel waits: read (and cleared) after a synchronisation.
+void check_status(Ctx *c) {
+    if (!c->status) return;
+    int v = 0;
+    WOCR_CUDA(cudaMemcpy(&v, c->status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != 0) {
+        WOCR_CUDA(cudaMemset(c->status, 0, sizeof(int)));
+        fail(WOCR_ERR_TIMEOUT, "a kernel wait gave up (code " + std::to_string(v) + "); its results are invalid");
+    }
+}
+
 void sync_bounded(Ctx *c, int timeout_ms) {
     if (timeout_ms <= 0) {
         WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        check_status(c);
         return;
     }
     auto t0 = std::chrono::steady_clock::now();
     while (true) {
         cudaError_t e = cudaStreamQuery(c->stream);
-        if (e == cudaSuccess) return;
+        if (e == cudaSuccess) {
+            check_status(c);
+            return;
+        }
         if (e != cudaErrorNotReady) WOCR_CUDA(e);
         auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
         if (ms > timeout_ms) fail(WOCR_ERR_TIMEOUT, "stream did not finish within " + std::to_string(timeout_ms) + " ms");
@@ -371,6 +388,7 @@ int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t l
                 GruLayer &L = r->layers[nl];
                 L.input = input;
                 L.w_t = upload(c, wt);
+                L.uw = linear_umma(c, wt.data(), input, 1536);
                 L.wb = upload(c, wb);
                 L.r = upload(c, R.data);
                 L.rb = upload(c, rb);
@@ -407,6 +425,7 @@ int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t l
                 for (int q = 0; q < r->classes; q++) lw[(size_t)i * r->ldw + q] = lin.data[(size_t)i * r->classes + q];
             for (int q = 0; q < r->classes && q < (int)bias->data.size(); q++) lb[q] = bias->data[q];
             r->lin_w = upload(c, lw);
+            r->lin_uw = linear_umma(c, lin.data.data(), 512, r->classes);
             r->lin_b = upload(c, lb);
             WOCR_CUDA(cudaStreamSynchronize(c->stream));
         } catch (...) {
@@ -513,13 +532,14 @@ int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const 
         DT in = x;
         for (int l = 0; l < 2; l++) {
             GruLayer &L = rec->layers[l];
-            DT gates = linear_run(c, in, L.w_t, L.wb, L.input, 1536, 1536, 0);
+            DT gates = linear_run(c, in, L.w_t, L.wb, L.input, 1536, 1536, 0, L.uw.get());
             DT yo = new_rowmajor(c, {tmax, ntot, 512});
             WOCR_CUDA(cudaMemsetAsync(yo.p, 0, (size_t)yo.numel() * 4, c->stream));
             k::gru_layer(c, gates.p, L.r.p, L.rb.p, (const int *)lens_d->p, tmax, ntot, yo.p);
             in = yo;
         }
-        DT lg = linear_run(c, in, rec->lin_w, rec->lin_b, 512, rec->classes, rec->ldw, 0);  // [tmax][ntot][classes]
+        DT lg = linear_run(c, in, rec->lin_w, rec->lin_b, 512, rec->classes, rec->ldw, 0,
+                           rec->lin_uw.get());  // [tmax][ntot][classes]
         if (logits) {
             if (logits_cap < m * rec->classes) fail(WOCR_ERR_CAPACITY, "logits buffer too small");
             d2h(c, logits, lg.p, (size_t)m * rec->classes * 4);

@@ -66,6 +66,9 @@ struct Ctx {
     bool prof = false;
     std::vector<ProfRec> recs;
     std::vector<cudaEvent_t> spare;
+    // device error word written by kernels whose bounded waits gave up (0 = fine)
+    int *status = nullptr;
+    std::shared_ptr<struct Buf> status_buf;
 };
 
 // Brackets one kernel launch with events when the context profiles; records its algorithmic

@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <set>
 
 namespace wocr {
@@ -21,6 +22,25 @@ DevW upload(Ctx *c, const float *v, int64_t n) {
 DevW upload(Ctx *c, const std::vector<float> &v) { return upload(c, v.data(), (int64_t)v.size()); }
 
 static int round4(int v) { return (v + 3) / 4 * 4; }
+
+// Dense convolutions and matrix products run on the tcgen05 tensor-core kernel; WOCR_SIMT_GEMM=1
+// selects the CUDA-core fp32 kernel instead (a diagnosis switch for comparing the two).
+static bool use_umma() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = std::getenv("WOCR_SIMT_GEMM");
+        v = (e && e[0] == '1') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+std::shared_ptr<k::UmmaW> linear_umma(Ctx *c, const float *w_kn, int K, int N) {
+    if (!use_umma()) return nullptr;
+    std::vector<float> nk((size_t)N * K);
+    for (int kk = 0; kk < K; kk++)
+        for (int n = 0; n < N; n++) nk[(size_t)n * K + kk] = w_kn[(size_t)kk * N + n];
+    return std::make_shared<k::UmmaW>(k::make_umma_weights(c, nk, N, K));
+}
 
 // [cout][cin/g][kh][kw] -> the layout of the kernel the conv runs on.
 ConvW lower_conv_dense(Ctx *c, const HostW &w, const std::vector<float> &bias, int group) {
@@ -46,6 +66,16 @@ ConvW lower_conv_dense(Ctx *c, const HostW &w, const std::vector<float> &bias, i
                         t[(size_t)((ky * kw + kx) * cin_g + ci) * cw.ldw + co] =
                             w.data[(((size_t)co * cin_g + ci) * kh + ky) * kw + kx];
         cw.w = upload(c, t);
+        if (use_umma()) {
+            std::vector<float> nk((size_t)cout * K);
+            for (int co = 0; co < cout; co++)
+                for (int ci = 0; ci < cin_g; ci++)
+                    for (int ky = 0; ky < kh; ky++)
+                        for (int kx = 0; kx < kw; kx++)
+                            nk[(size_t)co * K + (ky * kw + kx) * cin_g + ci] =
+                                w.data[(((size_t)co * cin_g + ci) * kh + ky) * kw + kx];
+            cw.uw = std::make_shared<k::UmmaW>(k::make_umma_weights(c, nk, cout, K));
+        }
     } else {
         // depthwise: [kh][kw][c]
         cw.kind = ConvW::DEPTHWISE;
@@ -99,6 +129,12 @@ ConvTW lower_convt(Ctx *c, const HostW &w, const std::vector<float> &bias, int s
                         m[(size_t)ci * t.ldw + (ky * stride + kx) * t.cout + co] =
                             w.data[(((size_t)ci * t.cout + co) * t.kh + ky) * t.kw + kx];
         t.w = upload(c, m);
+        if (use_umma()) {
+            std::vector<float> nk((size_t)N * t.cin);
+            for (int ci = 0; ci < t.cin; ci++)
+                for (int j = 0; j < N; j++) nk[(size_t)j * t.cin + ci] = m[(size_t)ci * t.ldw + j];
+            t.uw = std::make_shared<k::UmmaW>(k::make_umma_weights(c, nk, N, t.cin));
+        }
     } else {
         t.w = upload(c, w.data);
     }
@@ -234,6 +270,39 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
         s = to_rowmajor(c, *scale);
         p.insc = s.p;
     }
+    if (cw.uw) {
+        k::UmmaP u;
+        u.mode = 1;
+        u.x = p.x;
+        u.x_n = p.x_n;
+        u.x_pix = p.x_pix;
+        u.n = p.n;
+        u.h = p.h;
+        u.w = p.w;
+        u.cin = p.cin;
+        u.kh = p.kh;
+        u.kw = p.kw;
+        u.sh = p.sh;
+        u.sw = p.sw;
+        u.pt = p.pt;
+        u.pl = p.pl;
+        u.oh = p.oh;
+        u.ow = p.ow;
+        u.insc = p.insc;
+        u.vec = (p.cin % 8 == 0) && (p.x_pix % 4 == 0) && (p.x_n % 4 == 0) &&
+                ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
+        u.M = (int64_t)p.n * p.oh * p.ow;
+        u.bias = p.bias;
+        u.act = p.act;
+        u.y = p.y;
+        u.y_n = p.y_n;
+        u.y_pix = p.y_pix;
+        u.res = p.res;
+        u.res_n = p.res_n;
+        u.res_pix = p.res_pix;
+        k::umma_gemm(c, *cw.uw, u);
+        return y;
+    }
     k::conv_gemm(c, p);
     return y;
 }
@@ -266,7 +335,32 @@ static DT convt_run(Ctx *c, const DT &xin, const ConvTW &t, int act) {
         p.act = act;
         p.scatter = t.s;
         p.scat_cout = t.cout;
-        k::conv_gemm(c, p);
+        if (t.uw) {
+            k::UmmaP u;
+            u.mode = 1;
+            u.x = p.x;
+            u.x_n = p.x_n;
+            u.x_pix = p.x_pix;
+            u.n = p.n;
+            u.h = p.h;
+            u.w = p.w;
+            u.cin = p.cin;
+            u.oh = p.oh;
+            u.ow = p.ow;
+            u.vec = (p.cin % 8 == 0) && (p.x_pix % 4 == 0) && (p.x_n % 4 == 0) &&
+                    ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
+            u.M = (int64_t)p.n * p.oh * p.ow;
+            u.bias = p.bias;
+            u.act = p.act;
+            u.y = p.y;
+            u.y_n = p.y_n;
+            u.y_pix = p.y_pix;
+            u.scatter = t.s;
+            u.scat_cout = t.cout;
+            k::umma_gemm(c, *t.uw, u);
+        } else {
+            k::conv_gemm(c, p);
+        }
     } else {
         k::convt_gather(c, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, (int)cin, t.w.p, t.b.p, t.cout, t.kh,
                         t.kw, t.s, act, y.p, y.strides[0], y.pix(), (int)oh, (int)ow);
@@ -274,7 +368,8 @@ static DT convt_run(Ctx *c, const DT &xin, const ConvTW &t, int act) {
     return y;
 }
 
-DT linear_run(Ctx *c, const DT &xin, const DevW &w, const DevW &b, int K, int N, int ldw, int act) {
+DT linear_run(Ctx *c, const DT &xin, const DevW &w, const DevW &b, int K, int N, int ldw, int act,
+              const k::UmmaW *uw) {
     if (xin.shape.empty() || xin.shape.back() != K)
         fail(WOCR_ERR_SHAPE, "MatMul: " + shape_str(xin.shape) + " by [" + std::to_string(K) + ", " +
                                  std::to_string(N) + "]");
@@ -301,6 +396,20 @@ DT linear_run(Ctx *c, const DT &xin, const DevW &w, const DevW &b, int K, int N,
     p.y_n = M * N;
     p.y_pix = N;
     p.act = act;
+    if (uw) {
+        k::UmmaP u;
+        u.mode = 0;
+        u.x = x.p;
+        u.lda = K;
+        u.vec = (K % 4 == 0) && ((reinterpret_cast<uintptr_t>(x.p) & 15) == 0);
+        u.M = M;
+        u.bias = b.p;
+        u.act = act;
+        u.y = y.p;
+        u.ldy = N;
+        k::umma_gemm(c, *uw, u);
+        return y;
+    }
     k::conv_gemm(c, p);
     return y;
 }
@@ -473,7 +582,7 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
         out = get(vals, s.inputs[0]);
         break;
     case Step::N_LINEAR:
-        out.f = linear_run(ctx, getf(vals, s.inputs[0]), s.lw, s.lb, s.lk, s.ln, s.ldw, s.act);
+        out.f = linear_run(ctx, getf(vals, s.inputs[0]), s.lw, s.lb, s.lk, s.ln, s.ldw, s.act, s.luw.get());
         break;
     case Step::N_AFFINE: {
         DT x = getf(vals, s.inputs[0]);
@@ -1292,6 +1401,7 @@ std::unique_ptr<Executor> build_ndgraph(Ctx *c, const Model &m, bool stop_before
             for (int r = 0; r < K; r++)
                 for (int q = 0; q < N; q++) t[(size_t)r * st.ldw + q] = w.data[(size_t)r * N + q];
             st.lw = upload(c, t);
+            st.luw = linear_umma(c, w.data.data(), K, N);
             b.resize(st.ldw, 0.f);
             st.lb = upload(c, b);
             st.act = act;

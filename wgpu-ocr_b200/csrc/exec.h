@@ -12,6 +12,7 @@
 #include "common.h"
 #include "kernels.h"
 #include "model.h"
+#include "umma.h"
 
 namespace wocr {
 
@@ -33,6 +34,7 @@ struct ConvW {
     bool same_upper = false;
     int ldw = 0;                 // DENSE: columns of the [K][ldw] weight matrix
     int pool_h = 1, pool_w = 1;  // DIRECT: fused MaxPool
+    std::shared_ptr<k::UmmaW> uw;  // DENSE: the tensor-core operand (split bf16, TMA maps)
 };
 
 // A lowered ConvTranspose: kernel == stride runs as one GEMM with a scatter epilogue.
@@ -40,6 +42,7 @@ struct ConvTW {
     DevW w, b;  // gemm: [cin][ldw] with column (ky*s + kx)*cout + co; else [cin][cout][kh][kw]
     int cin = 0, cout = 0, kh = 0, kw = 0, s = 1, ldw = 0;
     bool gemm = false;
+    std::shared_ptr<k::UmmaW> uw;  // gemm: the tensor-core operand
 };
 
 ConvW lower_conv_dense(Ctx *c, const HostW &w, const std::vector<float> &bias, int group);
@@ -70,6 +73,7 @@ struct Step {
     std::string residual, scale;          // N_CONV fusions
     DevW lw, lb;                          // N_LINEAR [K][ldw] + bias
     int lk = 0, ln = 0, ldw = 0;
+    std::shared_ptr<k::UmmaW> luw;        // N_LINEAR tensor-core operand
     DevW st;                              // N_AFFINE scale|shift, N_LAYERNORM gamma|beta
     int ln_len = 0;
     float eps = 1e-5f;
@@ -107,7 +111,10 @@ std::unique_ptr<Executor> build_ndgraph(Ctx *c, const Model &m, bool stop_before
 DT to_nhwc(Ctx *c, const DT &x);
 DT to_rowmajor(Ctx *c, const DT &x);
 DT conv_run(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale);
-DT linear_run(Ctx *c, const DT &x, const DevW &w, const DevW &b, int K, int N, int ldw, int act);
+DT linear_run(Ctx *c, const DT &x, const DevW &w, const DevW &b, int K, int N, int ldw, int act,
+              const k::UmmaW *uw = nullptr);
+// [K][N] row-major fp32 weights -> the tensor-core operand of y = x W.
+std::shared_ptr<k::UmmaW> linear_umma(Ctx *c, const float *w_kn, int K, int N);
 DT from_host(Ctx *c, const float *x, const std::vector<int64_t> &shape);
 
 }  // namespace wocr

@@ -1,0 +1,530 @@
+// Tensor-core GEMM / implicit-GEMM convolution on the 5th-generation tensor cores (tcgen05,
+// sm_100a): the B200 path of the reference's dense conv (K1-K4, src/gpu.rs:37-350), its GEMM
+// (K15, src/gpu.rs:616-678), the linear layers of nd_bgemm (K29, src/nd.rs:291-358) and the
+// kernel == stride ConvTranspose (K7, src/gpu.rs:424-460).
+//
+// Precision: the reference computes in fp32.  Each operand is split into two bf16 parts,
+// x = hi + lo (hi = bf16(x), lo = bf16(x - hi)), and the product is accumulated in fp32 in
+// tensor memory as hi*hi + hi*lo + lo*hi: three kind::f16 MMAs per K step, relative error of a
+// product about 2^-16 (the dropped lo*lo term and the rounding of lo), against 2^-8 for plain
+// bf16 and 2^-11 for tf32.
+//
+// One CTA computes a 128 x BN output tile:
+//   warps 0-3  produce A: 128 rows (output pixels / rows of x) x 64 k per stage, fp32 loads
+//              (implicit im2col for convolutions, zero padding, SE input scale), split to
+//              bf16 hi/lo, written in the 128-byte-swizzled K-major layout the MMA reads;
+//   warp 8     issues the TMA loads of the pre-split weight tiles (B hi/lo, BN x 64 each);
+//   warp 9     allocates tensor memory and (one thread) issues tcgen05.mma + tcgen05.commit;
+//   warps 4-7  the epilogue: tcgen05.ld of the fp32 accumulator, bias, activation, residual,
+//              channels-last stores (or the ConvTranspose scatter).
+// Stages are handed over with mbarriers.  Every wait is bounded by a clock budget; on expiry
+// the kernel records an error code in `status`, drains its own TMA loads and MMAs, frees its
+// tensor memory and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "kernels.h"
+#include "umma.h"
+
+namespace wocr {
+namespace k {
+
+namespace {
+
+constexpr int BM = 128, BK = 64;
+constexpr int kProducers = 128;          // warps 0-3
+constexpr int kThreads = 320;            // 10 warps
+constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (about 2 s) per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false (and an error code in *status) when the budget runs out or another role
+// has already given up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
+                                          int code) {
+    long long t0 = clock64();
+    while (!mbar_try(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitBudget) {
+            *abort_flag = 1;
+            atomicCAS(status, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// K-major operand tile in the 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16, D fp32, A and B bf16, both K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t instr_desc(int bn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float erf_as(float v) {
+    float s = (v > 0.f) - (v < 0.f);
+    float a = fabsf(v);
+    float t = 1.0f / (1.0f + 0.3275911f * a);
+    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    return s * (1.0f - poly * expf(-a * a));
+}
+
+__device__ __forceinline__ float act_f(float v, int act) {
+    switch (act) {
+    case 1: return fmaxf(v, 0.f);
+    case 2: return 1.0f / (1.0f + expf(-v));
+    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
+    case 4: return v / (1.0f + expf(-v));
+    default: return v;
+    }
+}
+
+// Split 8 fp32 values into bf16 hi and lo parts, packed 2 per word.
+__device__ __forceinline__ void split8(const float (&v)[8], uint4 &hi, uint4 &lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        float2 hf = __bfloat1622float2(hv);
+        __nv_bfloat162 lv = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+        h[i] = *reinterpret_cast<uint32_t *>(&hv);
+        l[i] = *reinterpret_cast<uint32_t *>(&lv);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+struct Smem {
+    // per stage: A hi, A lo (128 x 64 bf16 = 16 KB each), B hi, B lo (BN x 64 bf16 each)
+    static constexpr int a_bytes = BM * BK * 2;
+};
+
+template <int BN, int STAGES>
+struct Layout {
+    static constexpr int b_bytes = BN * BK * 2;
+    static constexpr int stage_bytes = 2 * Smem::a_bytes + 2 * b_bytes;
+    static constexpr int bar_off = STAGES * stage_bytes;
+    static constexpr int total = bar_off + 256 + 1024;  // barriers + tmem slot, + alignment slack
+};
+
+// Loads 8 consecutive k values of row `m` of A (fp32) for k0 .. k0 + 8.
+struct ARow {
+    bool valid;
+    int iy0, ix0;
+    const float *xb;
+    const float *scb;
+};
+
+__device__ __forceinline__ void load8(const UmmaP &p, const ARow &r, int k0, float (&v)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = 0.f;
+    if (!r.valid || k0 >= p.K) return;
+    if (p.mode == 0) {  // row-major A
+        const float *src = r.xb + k0;
+        if (p.vec && k0 + 8 <= p.K) {
+            float4 a = *reinterpret_cast<const float4 *>(src);
+            float4 b = *reinterpret_cast<const float4 *>(src + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (k0 + i < p.K) v[i] = src[i];
+        }
+        return;
+    }
+    if (p.vec) {  // cin % 8 == 0: one tap, 8 consecutive channels
+        int tap = k0 / p.cin, ci = k0 - tap * p.cin;
+        int ky = tap / p.kw, kx = tap - ky * p.kw;
+        int iy = r.iy0 + ky, ix = r.ix0 + kx;
+        if (iy < 0 || iy >= p.h || ix < 0 || ix >= p.w) return;
+        const float4 *src = reinterpret_cast<const float4 *>(r.xb + ((int64_t)iy * p.w + ix) * p.x_pix + ci);
+        float4 a = src[0], b = src[1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        if (r.scb) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] *= r.scb[ci + i];
+        }
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        int k = k0 + i;
+        if (k >= p.K) break;
+        int tap = k / p.cin, ci = k - tap * p.cin;
+        int ky = tap / p.kw, kx = tap - ky * p.kw;
+        int iy = r.iy0 + ky, ix = r.ix0 + kx;
+        if (iy < 0 || iy >= p.h || ix < 0 || ix >= p.w) continue;
+        float x = r.xb[((int64_t)iy * p.w + ix) * p.x_pix + ci];
+        if (r.scb) x *= r.scb[ci];
+        v[i] = x;
+    }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo, UmmaP p) {
+    using Lay = Layout<BN, STAGES>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *afull = reinterpret_cast<uint64_t *>(smem + Lay::bar_off);
+    uint64_t *bfull = afull + STAGES;
+    uint64_t *empty = bfull + STAGES;
+    uint64_t *accum = empty + STAGES;
+    uint64_t *drain = accum + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t m0 = (int64_t)blockIdx.x * BM;
+    const int n0 = blockIdx.y * BN;
+    const int nk = p.Kpad / BK;
+    constexpr uint32_t kCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&afull[s], kProducers);
+            mbar_init(&bfull[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp == 9) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < 4) {
+        // ---------------- A producers: one tile row per thread ----------------
+        const int row = threadIdx.x;
+        const int64_t m = m0 + row;
+        ARow r;
+        r.valid = m < p.M;
+        r.iy0 = r.ix0 = 0;
+        r.xb = p.x;
+        r.scb = nullptr;
+        if (r.valid) {
+            if (p.mode == 0) {
+                r.xb = p.x + m * p.lda;
+            } else {
+                int ox = (int)(m % p.ow);
+                int64_t t = m / p.ow;
+                int oy = (int)(t % p.oh);
+                int nb = (int)(t / p.oh);
+                r.iy0 = oy * p.sh - p.pt;
+                r.ix0 = ox * p.sw - p.pl;
+                r.xb = p.x + (int64_t)nb * p.x_n;
+                r.scb = p.insc ? p.insc + (int64_t)nb * p.cin : nullptr;
+            }
+        }
+        const int sw = row & 7;
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % STAGES;
+            const uint32_t par = ((kb / STAGES) & 1) ^ 1;
+            if (!mbar_wait(&empty[s], par, p.status, abort_flag, 11)) break;
+            uint8_t *ahi = smem + s * Lay::stage_bytes;
+            uint8_t *alo = ahi + Smem::a_bytes;
+            uint8_t *rhi = ahi + (row >> 3) * 1024 + (row & 7) * 128;
+            uint8_t *rlo = alo + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll 2
+            for (int c = 0; c < 8; c++) {
+                float v[8];
+                load8(p, r, kb * BK + c * 8, v);
+                uint4 hi, lo;
+                split8(v, hi, lo);
+                *reinterpret_cast<uint4 *>(rhi + ((c ^ sw) << 4)) = hi;
+                *reinterpret_cast<uint4 *>(rlo + ((c ^ sw) << 4)) = lo;
+            }
+            fence_async_smem();
+            mbar_arrive(&afull[s]);
+        }
+    } else if (warp == 8) {
+        // ---------------- B loader: TMA of the pre-split weight tiles ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < nk; kb++) {
+                const int s = kb % STAGES;
+                const uint32_t par = ((kb / STAGES) & 1) ^ 1;
+                if (!mbar_wait(&empty[s], par, p.status, abort_flag, 12)) break;
+                uint8_t *bhi = smem + s * Lay::stage_bytes + 2 * Smem::a_bytes;
+                uint8_t *blo = bhi + Lay::b_bytes;
+                mbar_expect_tx(&bfull[s], 2 * Lay::b_bytes);
+                tma_load_2d(bhi, &tm_hi, &bfull[s], kb * BK, n0);
+                tma_load_2d(blo, &tm_lo, &bfull[s], kb * BK, n0);
+                issued = kb + 1;
+            }
+            // drain: every issued copy lands before the CTA may exit (bounded)
+            for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; kb++) {
+                long long t0 = clock64();
+                while (!mbar_try(&bfull[kb % STAGES], (kb / STAGES) & 1) && clock64() - t0 < kWaitBudget) {
+                }
+            }
+        }
+    } else if (warp == 9) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(BN);
+            bool ok = true;
+            for (int kb = 0; kb < nk && ok; kb++) {
+                const int s = kb % STAGES;
+                const uint32_t par = (kb / STAGES) & 1;
+                ok = mbar_wait(&afull[s], par, p.status, abort_flag, 13) &&
+                     mbar_wait(&bfull[s], par, p.status, abort_flag, 14);
+                if (!ok) break;
+                tc_fence_after();
+                uint8_t *base = smem + s * Lay::stage_bytes;
+                const uint32_t ahi = smem_u32(base), alo = ahi + Smem::a_bytes;
+                const uint32_t bhi = alo + Smem::a_bytes, blo = bhi + Lay::b_bytes;
+#pragma unroll
+                for (int kk = 0; kk < BK / 16; kk++) {
+                    const uint32_t off = kk * 32;
+                    umma(tmem, smem_desc(ahi + off), smem_desc(bhi + off), idesc, (kb | kk) != 0);
+                    umma(tmem, smem_desc(ahi + off), smem_desc(blo + off), idesc, 1);
+                    umma(tmem, smem_desc(alo + off), smem_desc(bhi + off), idesc, 1);
+                }
+                umma_commit(&empty[s]);
+            }
+            umma_commit(ok ? accum : drain);
+            if (!ok) {  // wait for the MMAs already issued before the memory goes away
+                long long t0 = clock64();
+                while (!mbar_try(drain, 0) && clock64() - t0 < kWaitBudget) {
+                }
+            }
+        }
+    } else {
+        // ---------------- epilogue: warps 4-7, TMEM lanes 32 * (warp - 4) ----------------
+        const int q = warp - 4;
+        const int row = q * 32 + lane;
+        const int64_t m = m0 + row;
+        bool ok = mbar_wait(accum, 0, p.status, abort_flag, 15);
+        tc_fence_after();
+        if (ok) {
+            int ox = 0, oy = 0, nb = 0;
+            int64_t pix = 0;
+            if (p.mode == 1 && m < p.M) {
+                ox = (int)(m % p.ow);
+                int64_t t = m / p.ow;
+                oy = (int)(t % p.oh);
+                nb = (int)(t / p.oh);
+                pix = (int64_t)oy * p.ow + ox;
+            }
+#pragma unroll 1
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                float v[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
+                if (m >= p.M) continue;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int col = n0 + c0 + j;
+                    if (col >= p.N) break;
+                    if (p.scatter) {
+                        const int s = p.scatter;
+                        const int co = col % p.scat_cout, tap = col / p.scat_cout;
+                        const int yy = oy * s + tap / s, xx = ox * s + tap % s;
+                        float o = act_f(v[j] + (p.bias ? p.bias[co] : 0.f), p.act);
+                        p.y[(int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co] = o;
+                    } else if (p.mode == 1) {
+                        float o = act_f(v[j] + (p.bias ? p.bias[col] : 0.f), p.act);
+                        if (p.res) o += p.res[(int64_t)nb * p.res_n + pix * p.res_pix + col];
+                        p.y[(int64_t)nb * p.y_n + pix * p.y_pix + col] = o;
+                    } else {
+                        float o = act_f(v[j] + (p.bias ? p.bias[col] : 0.f), p.act);
+                        p.y[m * p.ldy + col] = o;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+    }
+}
+
+// ---- host side ------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+void make_map(CUtensorMap *map, void *base, int N, int Kpad, int bn) {
+    auto fn = encode_fn();
+    if (!fn) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)Kpad, (cuuint64_t)N};
+    cuuint64_t strides[1] = {(cuuint64_t)Kpad * 2};
+    cuuint32_t box[2] = {BK, (cuuint32_t)bn};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+template <int BN, int STAGES>
+void launch(Ctx *c, const UmmaW &w, const UmmaP &p) {
+    using Lay = Layout<BN, STAGES>;
+    static bool set[64] = {false};
+    if (!set[c->device]) {
+        WOCR_CUDA(cudaFuncSetAttribute(k_umma<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::total));
+        set[c->device] = true;
+    }
+    dim3 grid((unsigned)((p.M + BM - 1) / BM), (unsigned)((p.N + BN - 1) / BN));
+    k_umma<BN, STAGES><<<grid, kThreads, Lay::total, c->stream>>>(w.map_hi, w.map_lo, p);
+    WOCR_LAUNCHED(c);
+}
+
+}  // namespace
+
+int umma_bn(int N) {
+    if (N <= 16) return 16;
+    if (N <= 32) return 32;
+    if (N <= 64) return 64;
+    if (N <= 128) return 128;
+    return 256;
+}
+
+UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K) {
+    // wnk: [N][K] fp32 (row n = output channel, k in the A operand's order)
+    UmmaW w;
+    w.N = N;
+    w.K = K;
+    w.Kpad = (K + BK - 1) / BK * BK;
+    w.bn = umma_bn(N);
+    const int Npad = (N + w.bn - 1) / w.bn * w.bn;  // every TMA box lies inside the tensor
+    std::vector<__nv_bfloat16> hi((size_t)Npad * w.Kpad, __float2bfloat16_rn(0.f)), lo = hi;
+    for (int n = 0; n < N; n++)
+        for (int k = 0; k < K; k++) {
+            float v = wnk[(size_t)n * K + k];
+            __nv_bfloat16 h = __float2bfloat16_rn(v);
+            hi[(size_t)n * w.Kpad + k] = h;
+            lo[(size_t)n * w.Kpad + k] = __float2bfloat16_rn(v - __bfloat162float(h));
+        }
+    size_t bytes = (size_t)Npad * w.Kpad * 2;
+    w.hi = alloc(c, bytes);
+    w.lo = alloc(c, bytes);
+    WOCR_CUDA(cudaMemcpyAsync(w.hi->p, hi.data(), bytes, cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaMemcpyAsync(w.lo->p, lo.data(), bytes, cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    make_map(&w.map_hi, w.hi->p, Npad, w.Kpad, w.bn);
+    make_map(&w.map_lo, w.lo->p, Npad, w.Kpad, w.bn);
+    return w;
+}
+
+void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
+    if (p.M == 0 || p.N == 0) return;
+    if (!c->status) {
+        c->status_buf = alloc(c, 16);
+        c->status = (int *)c->status_buf->p;
+        WOCR_CUDA(cudaMemsetAsync(c->status, 0, 16, c->stream));
+    }
+    p.status = c->status;
+    p.K = w.K;
+    p.Kpad = w.Kpad;
+    p.N = w.N;
+    double flops = 2.0 * (double)p.M * w.N * w.K;
+    double bytes = 4.0 * ((double)p.M * w.K / (p.mode == 1 ? (double)p.kh * p.kw : 1.0) + (double)p.M * w.N) +
+                   4.0 * (double)w.N * w.Kpad;
+    Prof pf(c, p.scatter ? "umma_convt" : (p.mode == 1 ? "umma_conv" : "umma_linear"), flops, bytes);
+    switch (w.bn) {
+    case 16: launch<16, 4>(c, w, p); break;
+    case 32: launch<32, 4>(c, w, p); break;
+    case 64: launch<64, 3>(c, w, p); break;
+    case 128: launch<128, 3>(c, w, p); break;
+    default: launch<256, 2>(c, w, p); break;
+    }
+    c->flops += flops;
+}
+
+}  // namespace k
+}  // namespace wocr

@@ -1,0 +1,47 @@
+// The tcgen05 tensor-core GEMM (k_umma.cu): parameters and pre-split weights.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.h"
+
+namespace wocr {
+namespace k {
+
+// Weights of one GEMM as the tensor cores read them: B = W^T, [N][Kpad] bf16 K-major, split into
+// hi = bf16(w) and lo = bf16(w - hi), rows padded with zeros to a multiple of the N tile, with
+// their TMA descriptors (128-byte swizzle, 64 x bn boxes).
+struct UmmaW {
+    BufP hi, lo;
+    CUtensorMap map_hi, map_lo;
+    int N = 0, K = 0, Kpad = 0, bn = 0;
+};
+
+struct UmmaP {
+    int mode = 0;                 // 0: A row-major [M][lda]; 1: implicit im2col of an NHWC tensor
+    const float *x = nullptr;
+    int64_t x_n = 0, x_pix = 0;
+    int n = 0, h = 0, w = 0, cin = 0;
+    int kh = 1, kw = 1, sh = 1, sw = 1, pt = 0, pl = 0, oh = 0, ow = 0;
+    const float *insc = nullptr;  // [n][cin] squeeze-excitation input scale
+    int64_t lda = 0;
+    int vec = 0;                  // 8-wide aligned loads are valid
+    int64_t M = 0;
+    int K = 0, Kpad = 0, N = 0;
+    const float *bias = nullptr;
+    int act = 0;
+    float *y = nullptr;
+    int64_t y_n = 0, y_pix = 0, ldy = 0;
+    const float *res = nullptr;
+    int64_t res_n = 0, res_pix = 0;
+    int scatter = 0, scat_cout = 0;
+    int *status = nullptr;        // device error word (bounded waits that gave up)
+};
+
+int umma_bn(int N);
+// wnk: [N][K] fp32, k in the order the A operand is produced (ky, kx, ci for convolutions).
+UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K);
+void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p);
+
+}  // namespace k
+}  // namespace wocr
