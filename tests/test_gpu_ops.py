@@ -164,3 +164,16 @@ def test_linear_shapes(gpu, m, k, n):
     mdl = b.model("x", y)
     x = rnd(m, k)
     close(run_nd(gpu, mdl, x), ref.run_onnx(mdl, x), tol=5e-5)
+
+
+def test_handles_outlive_their_context():
+    """Destroying the device context before the graphs made from it is safe: the context is
+    released with its last handle (Python may collect them in any order)."""
+    g = wocr.Gpu()
+    b = _Builder(30)
+    m = b.model("x", b.op("Relu", [b.conv("x", 8, 16, 3)]))
+    nd = wocr.NdGraph(g, m)
+    g.close()
+    x = rnd(1, 8, 9, 11)
+    close(nd.run(x), ref.run_onnx(m, x))
+    nd.close()

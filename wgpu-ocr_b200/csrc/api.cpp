@@ -12,9 +12,14 @@ namespace wocr {
 const std::string &last_error();
 }
 
+// The context lives until the caller's handle and every detector / recogniser / graph made
+// from it are destroyed, in any order.
 struct wocr_ctx {
     Ctx c;
+    int refs = 1;
 };
+
+static void ctx_release(wocr_ctx *ctx);
 
 struct Stats {
     double flops = 0;
@@ -120,6 +125,27 @@ void d2h(Ctx *c, void *dst, const void *src, size_t bytes) {
 
 }  // namespace
 
+static void ctx_release(wocr_ctx *ctx) {
+    if (--ctx->refs > 0) return;
+    Ctx &c = ctx->c;
+    cudaSetDevice(c.device);
+    cudaStreamSynchronize(c.stream);
+    // everything freed on the stream goes before the stream itself
+    c.status_buf.reset();
+    c.status = nullptr;
+    for (auto &r : c.recs) {
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    for (auto e : c.spare) cudaEventDestroy(e);
+    c.recs.clear();
+    c.spare.clear();
+    cudaStreamSynchronize(c.stream);
+    cudaStreamDestroy(c.stream);
+    c.stream = nullptr;
+    delete ctx;
+}
+
 extern "C" {
 
 const char *wocr_last_error(void) { return last_error().c_str(); }
@@ -156,10 +182,7 @@ int32_t wocr_ctx_create(int32_t device, int32_t lines, wocr_ctx **out) {
 
 void wocr_ctx_destroy(wocr_ctx *ctx) {
     if (!ctx) return;
-    cudaSetDevice(ctx->c.device);
-    cudaStreamSynchronize(ctx->c.stream);
-    cudaStreamDestroy(ctx->c.stream);
-    delete ctx;
+    ctx_release(ctx);
 }
 
 int32_t wocr_ctx_describe(wocr_ctx *ctx, char *buf, int32_t cap) {
@@ -256,11 +279,13 @@ int32_t wocr_detector_create(wocr_ctx *ctx, const wocr_model *model, wocr_detect
         Model m = model_from_c(model);
         auto *d = new wocr_detector();
         d->ctx = ctx;
+        ctx->refs++;
         try {
             d->graph = build_graph(&ctx->c, m, nullptr, nullptr);
             WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
         } catch (...) {
             delete d;
+            ctx_release(ctx);
             throw;
         }
         *out = d;
@@ -269,9 +294,11 @@ int32_t wocr_detector_create(wocr_ctx *ctx, const wocr_model *model, wocr_detect
 
 void wocr_detector_destroy(wocr_detector *det) {
     if (!det) return;
-    cudaSetDevice(det->ctx->c.device);
-    cudaStreamSynchronize(det->ctx->c.stream);
+    wocr_ctx *ctx = det->ctx;
+    cudaSetDevice(ctx->c.device);
+    cudaStreamSynchronize(ctx->c.stream);
     delete det;
+    ctx_release(ctx);
 }
 
 static void detect_pages_dev(wocr_detector *det, const uint8_t *d_rgb, int n, int w, int h, float thr,
@@ -350,6 +377,7 @@ int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t l
         Model m = model_from_c(model);
         auto *r = new wocr_recognizer();
         r->ctx = ctx;
+        ctx->refs++;
         r->lines = lines > 0 ? lines : c->lines;
         try {
             Node pool;
@@ -430,6 +458,7 @@ int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t l
             WOCR_CUDA(cudaStreamSynchronize(c->stream));
         } catch (...) {
             delete r;
+            ctx_release(ctx);
             throw;
         }
         *out = r;
@@ -438,9 +467,11 @@ int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t l
 
 void wocr_recognizer_destroy(wocr_recognizer *rec) {
     if (!rec) return;
-    cudaSetDevice(rec->ctx->c.device);
-    cudaStreamSynchronize(rec->ctx->c.stream);
+    wocr_ctx *ctx = rec->ctx;
+    cudaSetDevice(ctx->c.device);
+    cudaStreamSynchronize(ctx->c.stream);
     delete rec;
+    ctx_release(ctx);
 }
 
 // Trunk output width of a batch of width w: follows the trunk's pooling/strides exactly by
@@ -564,11 +595,13 @@ int32_t wocr_ndgraph_create(wocr_ctx *ctx, const wocr_model *model, int32_t stop
         Model m = model_from_c(model);
         auto *g = new wocr_ndgraph();
         g->ctx = ctx;
+        ctx->refs++;
         try {
             g->graph = build_ndgraph(&ctx->c, m, stop_before_softmax != 0);
             WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
         } catch (...) {
             delete g;
+            ctx_release(ctx);
             throw;
         }
         *out = g;
@@ -577,9 +610,11 @@ int32_t wocr_ndgraph_create(wocr_ctx *ctx, const wocr_model *model, int32_t stop
 
 void wocr_ndgraph_destroy(wocr_ndgraph *g) {
     if (!g) return;
-    cudaSetDevice(g->ctx->c.device);
-    cudaStreamSynchronize(g->ctx->c.stream);
+    wocr_ctx *ctx = g->ctx;
+    cudaSetDevice(ctx->c.device);
+    cudaStreamSynchronize(ctx->c.stream);
     delete g;
+    ctx_release(ctx);
 }
 
 static DT nd_input(Ctx *c, const float *x, const int64_t *shape, int32_t rank) {

@@ -502,7 +502,7 @@ UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K) {
 }
 
 void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
-    if (p.M == 0 || p.N == 0) return;
+    if (p.M == 0 || w.N == 0) return;
     if (!c->status) {
         c->status_buf = alloc(c, 16);
         c->status = (int *)c->status_buf->p;
