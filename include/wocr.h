@@ -186,6 +186,21 @@ int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *
                                 uint32_t *best, float *row_max, float *row_lse, int64_t cap,
                                 int64_t *rows_out, int64_t *out_shape, int32_t *out_rank);
 
+/* No counterpart in the reference.  The arg-max of wocr_ndgraph_run_argmax for callers that
+ * cannot let the library allocate device memory (a host program whose own allocator owns the
+ * GPU, a process under a device-memory cap, a latency-critical path that avoids cudaMalloc's
+ * implicit synchronisation).  The caller passes the device logits d_logits [rows][len] (ordered
+ * before this call on the context's stream or by a device synchronisation) and host outputs:
+ * best [rows] (ties -> the lowest index), and nullable row_max / row_lse [rows].  Results are
+ * staged in a fixed 768 KiB array in the library's device memory, for at most 65,536 rows
+ * (more rows: WOCR_ERR_CAPACITY); every GPU that loads the library holds that array until the
+ * process exits.  Nothing is allocated: no cudaMalloc, cudaFree or allocating routine.  The
+ * first call on a device looks up the array's device address (once per device), so make that
+ * first call before any stream capture.  All calls share the array: calls that overlap on the
+ * GPU (several contexts or threads at once) race on it. */
+int32_t wocr_argmax_rows_noalloc(wocr_ctx *ctx, const float *d_logits, int64_t rows, int64_t len, uint32_t *best,
+                                 float *row_max, float *row_lse);
+
 /* NdGraph::det_input (src/nd.rs:1353-1369): the PP-OCR detection input of an RGB page,
  * [1, 3, oh, ow] planar floats, sized as ppdet::det_input (src/ppdet.rs:29-33). */
 int32_t wocr_det_input(wocr_ctx *ctx, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, float *out,

@@ -88,6 +88,9 @@ struct RunScope {
     }
 };
 
+}  // namespace
+
+namespace wocr {
 // The device error word of bounded kernel waits: read (and cleared) after a synchronisation.
 void check_status(Ctx *c) {
     if (!c->status) return;
@@ -118,6 +121,11 @@ void sync_bounded(Ctx *c, int timeout_ms) {
         std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
+
+Ctx *ctx_of(wocr_ctx *h) { return h ? &h->c : nullptr; }
+}  // namespace wocr
+
+namespace {
 
 void d2h(Ctx *c, void *dst, const void *src, size_t bytes) {
     if (bytes) WOCR_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->stream));

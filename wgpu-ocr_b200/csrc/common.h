@@ -120,6 +120,11 @@ struct DT {
     int64_t pix() const { return strides[3]; }  // NHWC pixel stride
 };
 
+// Waits for the context stream (bounded when timeout_ms > 0) and raises the device error word.
+void sync_bounded(Ctx *c, int timeout_ms);
+// The context behind a C-ABI handle.
+Ctx *ctx_of(wocr_ctx *h);
+
 std::vector<int64_t> rowmajor_strides(const std::vector<int64_t> &shape);
 DT new_rowmajor(Ctx *c, const std::vector<int64_t> &shape);
 DT new_nhwc(Ctx *c, int64_t n, int64_t ch, int64_t h, int64_t w);

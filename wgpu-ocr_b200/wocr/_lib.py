@@ -89,6 +89,7 @@ _SIGS = [
     ("wocr_ndgraph_run", c_i32, [c_void_p, c_void_p, P(c_i64), c_i32, c_void_p, c_i64, P(c_i64), P(c_i32)]),
     ("wocr_ndgraph_run_argmax", c_i32, [c_void_p, c_void_p, P(c_i64), c_i32, c_void_p, c_void_p, c_void_p, c_i64,
                                         P(c_i64), P(c_i64), P(c_i32)]),
+    ("wocr_argmax_rows_noalloc", c_i32, [c_void_p, c_void_p, c_i64, c_i64, c_void_p, c_void_p, c_void_p]),
     ("wocr_det_input", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_void_p, c_i64, P(c_i32), P(c_i32),
                                P(c_f32)]),
     ("wocr_ppdet_page", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_void_p, c_i64, P(c_i32), P(c_i32),
