@@ -25,7 +25,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -60,53 +59,56 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi samples of the SM clock and throttle reasons while the timed region runs."""
-
-    FIELDS = "index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    """SM clock and throttle reasons of this process's GPU, sampled every 200 ms by NVML in a
+    thread while the timed region runs (nvidia-smi's own 100 ms loop over every GPU of the box
+    was seen to stall the timed kernels)."""
 
     def __init__(self, bus_id):
         self.bus = bus_id if isinstance(bus_id, int) else None   # torch's pci_bus_id (an int)
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.stop_flag = threading.Event()
+        self.err = None
+
+    def _handle(self, nv):
+        n = nv.nvmlDeviceGetCount()
+        for i in range(n):
+            h = nv.nvmlDeviceGetHandleByIndex(i)
+            if self.bus is None or nv.nvmlDeviceGetPciInfo(h).bus == self.bus:
+                return h
+        return nv.nvmlDeviceGetHandleByIndex(0)
+
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            bits = {"hw_slowdown": nv.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": nv.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": nv.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": nv.nvmlClocksEventReasonSwPowerCap}
+            while not self.stop_flag.is_set():
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((mhz, [k for k, b in bits.items() if r & b]))
+                self.stop_flag.wait(0.2)
+            nv.nvmlShutdown()
+        except Exception as e:  # no NVML: report it instead of clocks
+            self.err = str(e)
 
     def start(self):
-        try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
-
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        rows = [r.split(", ") for r in self.lines if r]
-
-        def bus_of(field):  # "00000000:1B:00.0" -> 0x1b
-            try:
-                return int(field.split(":")[1], 16)
-            except Exception:
-                return None
-        mine = [r for r in rows if len(r) >= 10 and self.bus is not None and bus_of(r[1]) == self.bus] or \
-               [r for r in rows if len(r) >= 10 and r[0] == "0"]
-        sm = sorted(float(r[2]) for r in mine if r[2].replace(".", "").isdigit())
-        mx = max((float(r[3]) for r in mine if r[3].replace(".", "").isdigit()), default=None)
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in mine for i in range(4) if r[6 + i].strip().lower() == "active"})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+        time.sleep(0.05)
+        self.stop_flag.set()
+        self.t.join(timeout=5)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"], "samples": 0}
+        sm = sorted(s[0] for s in self.samples)
+        reasons = sorted({r for s in self.samples for r in s[1]})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": getattr(self, "max_mhz", None), "reasons": reasons,
                 "samples": len(sm)}
 
 

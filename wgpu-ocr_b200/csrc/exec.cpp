@@ -133,7 +133,8 @@ ConvTW lower_convt(Ctx *c, const HostW &w, const std::vector<float> &bias, int s
             std::vector<float> nk((size_t)N * t.cin);
             for (int ci = 0; ci < t.cin; ci++)
                 for (int j = 0; j < N; j++) nk[(size_t)j * t.cin + ci] = m[(size_t)ci * t.ldw + j];
-            t.uw = std::make_shared<k::UmmaW>(k::make_umma_weights(c, nk, N, t.cin));
+            const int max_bn = (t.cout % 16 == 0 && t.cout <= 256) ? t.cout : 256;  // one tap per N tile
+            t.uw = std::make_shared<k::UmmaW>(k::make_umma_weights(c, nk, N, t.cin, max_bn));
         }
     } else {
         t.w = upload(c, w.data);
@@ -193,7 +194,7 @@ static DT view(const DT &x, std::vector<int64_t> shape, std::vector<int64_t> str
 // =========================================================================================
 // convolution runs
 // =========================================================================================
-DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale) {
+DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale, const OutAlloc *out) {
     DT x = to_nhwc(c, xin);
     int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
     int pt, pl, pb, pr;
@@ -210,7 +211,7 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
         if (ch <= 0 || cwd <= 0) fail(WOCR_ERR_SHAPE, "conv input " + shape_str(x.shape) + " smaller than its kernel");
         if (cin != 1) fail(WOCR_ERR_SHAPE, "direct conv expects 1 channel, has " + std::to_string(cin));
         int64_t oh = ch / cw.pool_h, ow = cwd / cw.pool_w;
-        DT y = new_nhwc(c, n, cw.cout, oh, ow);
+        DT y = out ? (*out)(n, cw.cout, oh, ow) : new_nhwc(c, n, cw.cout, oh, ow);
         k::conv_direct(c, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, cw.w.p, cw.b.p, cw.cout, cw.kh, cw.kw,
                        pt, act, cw.pool_h, cw.pool_w, y.p, y.strides[0], y.pix(), (int)oh, (int)ow);
         return y;
@@ -225,7 +226,7 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
     if (scale && scale->numel() != n * cin)
         fail(WOCR_ERR_SHAPE, "input scale " + shape_str(scale->shape) + " for " + shape_str(x.shape));
     if ((res || scale) && cw.kind != ConvW::DENSE) fail(WOCR_ERR_UNSUPPORTED, "residual after a grouped conv");
-    DT y = new_nhwc(c, n, cw.cout, oh, ow);
+    DT y = out ? (*out)(n, cw.cout, oh, ow) : new_nhwc(c, n, cw.cout, oh, ow);
     if (cw.kind == ConvW::DEPTHWISE) {
         if (cin != cw.cout || cw.group != cin)
             fail(WOCR_ERR_UNSUPPORTED, "grouped conv with group " + std::to_string(cw.group));
@@ -307,13 +308,13 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
     return y;
 }
 
-static DT convt_run(Ctx *c, const DT &xin, const ConvTW &t, int act) {
+static DT convt_run(Ctx *c, const DT &xin, const ConvTW &t, int act, const OutAlloc *out = nullptr) {
     DT x = to_nhwc(c, xin);
     int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
     if (cin != t.cin) fail(WOCR_ERR_SHAPE, "ConvTranspose expects " + std::to_string(t.cin) + " channels, has " +
                                                std::to_string(cin));
     int64_t oh = (h - 1) * t.s + t.kh, ow = (w - 1) * t.s + t.kw;
-    DT y = new_nhwc(c, n, t.cout, oh, ow);
+    DT y = out ? (*out)(n, t.cout, oh, ow) : new_nhwc(c, n, t.cout, oh, ow);
     if (t.gemm) {
         k::ConvP p;
         p.x = x.p;
@@ -463,9 +464,73 @@ void Executor::finalize() {
     last_use.clear();
     for (int i = 0; i < (int)steps.size(); i++)
         for (auto &n : steps[i].inputs) last_use[n] = i;
+    // Channel Concats whose parts all come from convolution steps: those steps write straight
+    // into their channel slice of the Concat output, and the Concat itself copies nothing.
+    concat_slot.clear();
+    std::map<std::string, int> producer;
+    for (int i = 0; i < (int)steps.size(); i++) producer[steps[i].output] = i;
+    for (auto &st : steps) {
+        bool channel_concat = st.kind == Step::G_CONCAT;
+        if (st.kind == Step::N_GENERIC) {
+            const Node &n = model.nodes[st.node];
+            channel_concat = n.op == "Concat" && n.int_("axis").value_or(0) == 1;
+        }
+        if (!channel_concat) continue;
+        std::vector<std::pair<std::string, int>> parts;
+        bool ok = true;
+        std::set<std::string> seen;
+        for (auto &nm : st.inputs) {
+            auto pi = producer.find(nm);
+            if (pi == producer.end() || nm == input || nm == output || !seen.insert(nm).second ||
+                concat_slot.count(nm)) {
+                ok = false;
+                break;
+            }
+            const Step &ps = steps[pi->second];
+            int c = 0;
+            if (ps.kind == Step::G_CONV || ps.kind == Step::G_DIRECT || ps.kind == Step::G_DEPTHWISE ||
+                ps.kind == Step::N_CONV)
+                c = ps.conv.cout;
+            else if (ps.kind == Step::G_CONVT || ps.kind == Step::N_CONVT)
+                c = ps.convt.cout;
+            if (c <= 0) {
+                ok = false;
+                break;
+            }
+            parts.push_back({nm, c});
+        }
+        if (!ok || parts.size() < 2) continue;
+        int64_t ctot = 0;
+        for (auto &pp : parts) ctot += pp.second;
+        int64_t off = 0;
+        for (auto &pp : parts) {
+            concat_slot[pp.first] = {st.output, off, ctot};
+            off += pp.second;
+        }
+    }
+}
+
+// The output of a step registered in concat_slot: a channel slice of the Concat buffer (made on
+// first use with the producing step's batch and spatial size).
+DT Executor::slot_output(const std::string &name, int64_t n, int64_t c, int64_t h, int64_t w) {
+    auto si = concat_slot.find(name);
+    if (si == concat_slot.end() || !cbufs) return new_nhwc(ctx, n, c, h, w);
+    const ConcatSlot &sl = si->second;
+    auto bi = cbufs->find(sl.concat);
+    if (bi == cbufs->end()) bi = cbufs->emplace(sl.concat, new_nhwc(ctx, n, sl.ctot, h, w)).first;
+    const DT &b = bi->second;
+    if (b.shape[0] != n || b.shape[2] != h || b.shape[3] != w || sl.offset + c > sl.ctot)
+        return new_nhwc(ctx, n, c, h, w);  // shapes differ: the Concat will copy this part
+    return view(b, {n, c, h, w}, b.strides, sl.offset);
 }
 
 DT Executor::run(const DT &x) {
+    std::map<std::string, DT> concat_bufs;
+    cbufs = &concat_bufs;
+    struct Reset {
+        std::map<std::string, DT> **p;
+        ~Reset() { *p = nullptr; }
+    } reset{&cbufs};
     std::map<std::string, Value> vals;
     Value in;
     in.f = x;
@@ -483,13 +548,41 @@ DT Executor::run(const DT &x) {
     return it->second.f;
 }
 
+// Channel Concat of NHWC parts: parts already written into their slice of the registered
+// buffer are not copied again (src/gpu.rs:1317-1330 copies every part).
+DT Executor::concat_channels(const std::vector<DT> &parts, const std::string &out_name) {
+    const DT &a = parts[0];
+    int64_t ctot = 0;
+    for (auto &t : parts) ctot += t.shape[1];
+    DT y;
+    bool reuse = false;
+    if (cbufs) {
+        auto bi = cbufs->find(out_name);
+        if (bi != cbufs->end() && bi->second.shape == std::vector<int64_t>{a.shape[0], ctot, a.shape[2], a.shape[3]}) {
+            y = bi->second;
+            reuse = true;
+        }
+    }
+    if (!reuse) y = new_nhwc(ctx, a.shape[0], ctot, a.shape[2], a.shape[3]);
+    int64_t off = 0;
+    for (auto &t : parts) {
+        DT dst = view(y, t.shape, y.strides, off);
+        if (!(reuse && t.p == dst.p && t.strides == dst.strides)) copy_into(ctx, t, dst);
+        off += t.shape[1];
+    }
+    return y;
+}
+
 void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
     Value out;
+    const OutAlloc alloc_out = [&](int64_t n, int64_t c, int64_t h, int64_t w) {
+        return slot_output(s.output, n, c, h, w);
+    };
     switch (s.kind) {
     case Step::G_CONV:
     case Step::G_DIRECT:
     case Step::G_DEPTHWISE:
-        out.f = conv_run(ctx, getf(vals, s.inputs[0]), s.conv, s.act, nullptr, nullptr);
+        out.f = conv_run(ctx, getf(vals, s.inputs[0]), s.conv, s.act, nullptr, nullptr, &alloc_out);
         break;
     case Step::N_CONV: {
         DT r, sc;
@@ -504,14 +597,14 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
         }
         DT x = getf(vals, s.inputs[0]);
         if (x.rank() != 4) fail(WOCR_ERR_SHAPE, "Conv input " + shape_str(x.shape));
-        out.f = conv_run(ctx, x, s.conv, s.act, rp, sp);
+        out.f = conv_run(ctx, x, s.conv, s.act, rp, sp, &alloc_out);
         break;
     }
     case Step::G_CONVT:
     case Step::N_CONVT: {
         DT x = getf(vals, s.inputs[0]);
         if (x.rank() != 4) fail(WOCR_ERR_SHAPE, "ConvTranspose input " + shape_str(x.shape));
-        out.f = convt_run(ctx, x, s.convt, s.act);
+        out.f = convt_run(ctx, x, s.convt, s.act, &alloc_out);
         break;
     }
     case Step::G_MAXPOOL: {
@@ -557,14 +650,7 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
             }
             ctot += t.shape[1];
         }
-        DT y = new_nhwc(ctx, a.shape[0], ctot, a.shape[2], a.shape[3]);
-        int64_t off = 0;
-        for (auto &t : parts) {
-            DT dst = view(y, t.shape, y.strides, off);
-            copy_into(ctx, t, dst);
-            off += t.shape[1];
-        }
-        out.f = y;
+        out.f = concat_channels(parts, s.output);
         break;
     }
     case Step::G_ACT: {
@@ -858,6 +944,13 @@ void Executor::exec_generic(const Node &n, std::map<std::string, Value> &vals) {
                 shape[ax] += p.f.shape[ax];
             }
             bool nh = r == 4 && ax == 1;
+            if (nh) {
+                std::vector<DT> ts;
+                for (auto &p : parts) ts.push_back(p.f);
+                out.f = concat_channels(ts, n.outputs[0]);
+                vals[n.outputs[0]] = out;
+                return;
+            }
             DT y = nh ? new_nhwc(ctx, shape[0], shape[1], shape[2], shape[3]) : new_rowmajor(ctx, shape);
             int64_t off = 0;
             for (auto &p : parts) {

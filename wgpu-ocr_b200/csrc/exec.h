@@ -88,6 +88,12 @@ class Executor {
     std::map<std::string, DT> weights;    // float initializers read by generic steps
     std::string input, output;
     std::map<std::string, int> last_use;  // value -> last step reading it
+    struct ConcatSlot {
+        std::string concat;               // the Concat output this value is a channel slice of
+        int64_t offset, ctot;
+    };
+    std::map<std::string, ConcatSlot> concat_slot;
+    std::map<std::string, DT> *cbufs = nullptr;  // Concat buffers of the current run
 
     explicit Executor(Ctx *c) : ctx(c) {}
     // Run on `x`; returns the output tensor.
@@ -95,6 +101,8 @@ class Executor {
     void finalize();  // uploads generic weights, computes last uses
 
   protected:
+    DT slot_output(const std::string &name, int64_t n, int64_t c, int64_t h, int64_t w);
+    DT concat_channels(const std::vector<DT> &parts, const std::string &out_name);
     Value get(std::map<std::string, Value> &vals, const std::string &name);
     DT getf(std::map<std::string, Value> &vals, const std::string &name);
     void exec_step(const Step &s, std::map<std::string, Value> &vals);
@@ -110,7 +118,9 @@ std::unique_ptr<Executor> build_ndgraph(Ctx *c, const Model &m, bool stop_before
 // Helpers shared with the API layer.
 DT to_nhwc(Ctx *c, const DT &x);
 DT to_rowmajor(Ctx *c, const DT &x);
-DT conv_run(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale);
+using OutAlloc = std::function<DT(int64_t n, int64_t c, int64_t h, int64_t w)>;
+DT conv_run(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale,
+            const OutAlloc *out = nullptr);
 DT linear_run(Ctx *c, const DT &x, const DevW &w, const DevW &b, int K, int N, int ldw, int act,
               const k::UmmaW *uw = nullptr);
 // [K][N] row-major fp32 weights -> the tensor-core operand of y = x W.

@@ -9,14 +9,17 @@
 // product about 2^-16 (the dropped lo*lo term and the rounding of lo), against 2^-8 for plain
 // bf16 and 2^-11 for tf32.
 //
-// One CTA computes a 128 x BN output tile:
-//   warps 0-3  produce A: 128 rows (output pixels / rows of x) x 64 k per stage, fp32 loads
-//              (implicit im2col for convolutions, zero padding, SE input scale), split to
-//              bf16 hi/lo, written in the 128-byte-swizzled K-major layout the MMA reads;
-//   warp 8     issues the TMA loads of the pre-split weight tiles (B hi/lo, BN x 64 each);
-//   warp 9     allocates tensor memory and (one thread) issues tcgen05.mma + tcgen05.commit;
-//   warps 4-7  the epilogue: tcgen05.ld of the fp32 accumulator, bias, activation, residual,
-//              channels-last stores (or the ConvTranspose scatter).
+// Persistent: one CTA per SM loops over 128 x BN output tiles; the shared-memory stage ring runs
+// on across tile boundaries and the fp32 accumulator in tensor memory is double-buffered, so
+// loads of the next tile and the epilogue of the last one overlap the MMAs of the current one.
+//   warps 0-7   produce A: two threads per tile row, 64 k per stage, fp32 loads (implicit
+//               im2col for convolutions, zero padding, SE input scale), split to bf16 hi/lo,
+//               written in the 128-byte-swizzled K-major layout the MMA reads;
+//   warp 12     issues the TMA loads of the pre-split weight tiles (B hi/lo, BN x 64 each);
+//   warp 13     allocates tensor memory and (one thread) issues tcgen05.mma + tcgen05.commit;
+//   warps 8-11  the epilogue: tcgen05.ld of the accumulator, bias, activation, residual,
+//               channels-last stores (or the ConvTranspose scatter), then hand the accumulator
+//               buffer back to the MMA warp.
 // Stages are handed over with mbarriers.  Every wait is bounded by a clock budget; on expiry
 // the kernel records an error code in `status`, drains its own TMA loads and MMAs, frees its
 // tensor memory and returns.
@@ -25,6 +28,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "kernels.h"
@@ -36,8 +40,6 @@ namespace k {
 namespace {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kProducers = 128;          // warps 0-3
-constexpr int kThreads = 320;            // 10 warps
 constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (about 2 s) per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -177,10 +179,10 @@ struct Layout {
     static constexpr int b_bytes = BN * BK * 2;
     static constexpr int stage_bytes = 2 * Smem::a_bytes + 2 * b_bytes;
     static constexpr int bar_off = STAGES * stage_bytes;
-    static constexpr int total = bar_off + 256 + 1024;  // barriers + tmem slot, + alignment slack
+    static constexpr int total = bar_off + 512 + 1024;  // barriers + tmem slot, + alignment slack
 };
 
-// Loads 8 consecutive k values of row `m` of A (fp32) for k0 .. k0 + 8.
+// The fp32 source of one row of A (an output pixel of a convolution, or a row of x).
 struct ARow {
     bool valid;
     int iy0, ix0;
@@ -188,6 +190,30 @@ struct ARow {
     const float *scb;
 };
 
+__device__ __forceinline__ ARow a_row(const UmmaP &p, int64_t m) {
+    ARow r;
+    r.valid = m < p.M;
+    r.iy0 = r.ix0 = 0;
+    r.xb = p.x;
+    r.scb = nullptr;
+    if (r.valid) {
+        if (p.mode == 0) {
+            r.xb = p.x + m * p.lda;
+        } else {
+            int ox = (int)(m % p.ow);
+            int64_t t = m / p.ow;
+            int oy = (int)(t % p.oh);
+            int nb = (int)(t / p.oh);
+            r.iy0 = oy * p.sh - p.pt;
+            r.ix0 = ox * p.sw - p.pl;
+            r.xb = p.x + (int64_t)nb * p.x_n;
+            r.scb = p.insc ? p.insc + (int64_t)nb * p.cin : nullptr;
+        }
+    }
+    return r;
+}
+
+// Loads 8 consecutive k values of one row of A (fp32) for k0 .. k0 + 8; zeros outside.
 __device__ __forceinline__ void load8(const UmmaP &p, const ARow &r, int k0, float (&v)[8]) {
 #pragma unroll
     for (int i = 0; i < 8; i++) v[i] = 0.f;
@@ -195,8 +221,8 @@ __device__ __forceinline__ void load8(const UmmaP &p, const ARow &r, int k0, flo
     if (p.mode == 0) {  // row-major A
         const float *src = r.xb + k0;
         if (p.vec && k0 + 8 <= p.K) {
-            float4 a = *reinterpret_cast<const float4 *>(src);
-            float4 b = *reinterpret_cast<const float4 *>(src + 4);
+            float4 a = __ldg(reinterpret_cast<const float4 *>(src));
+            float4 b = __ldg(reinterpret_cast<const float4 *>(src + 4));
             v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         } else {
 #pragma unroll
@@ -211,7 +237,7 @@ __device__ __forceinline__ void load8(const UmmaP &p, const ARow &r, int k0, flo
         int iy = r.iy0 + ky, ix = r.ix0 + kx;
         if (iy < 0 || iy >= p.h || ix < 0 || ix >= p.w) return;
         const float4 *src = reinterpret_cast<const float4 *>(r.xb + ((int64_t)iy * p.w + ix) * p.x_pix + ci);
-        float4 a = src[0], b = src[1];
+        float4 a = __ldg(src), b = __ldg(src + 1);
         v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
         if (r.scb) {
 #pragma unroll
@@ -233,8 +259,15 @@ __device__ __forceinline__ void load8(const UmmaP &p, const ARow &r, int k0, flo
     }
 }
 
+// Warp roles of the persistent kernel (448 threads):
+constexpr int kProdWarps = 8;   // warps 0-7: A producers, two threads per tile row
+constexpr int kEpiWarp0 = 8;    // warps 8-11: epilogue (TMEM lane quadrant = warp % 4)
+constexpr int kTmaWarp = 12;    // warp 12: B tiles by TMA
+constexpr int kMmaWarp = 13;    // warp 13: TMEM allocation, MMA issue
+constexpr int kAllThreads = 14 * 32;
+
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kAllThreads, 1)
     k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo, UmmaP p) {
     using Lay = Layout<BN, STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -242,30 +275,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *afull = reinterpret_cast<uint64_t *>(smem + Lay::bar_off);
     uint64_t *bfull = afull + STAGES;
     uint64_t *empty = bfull + STAGES;
-    uint64_t *accum = empty + STAGES;
-    uint64_t *drain = accum + 1;
+    uint64_t *tfull = empty + STAGES;   // [2] accumulator ready (tcgen05.commit)
+    uint64_t *tempty = tfull + 2;       // [2] accumulator drained by the epilogue (128 arrivals)
+    uint64_t *drain = tempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m0 = (int64_t)blockIdx.x * BM;
-    const int n0 = blockIdx.y * BN;
     const int nk = p.Kpad / BK;
-    constexpr uint32_t kCols = BN <= 32 ? 32 : (BN <= 64 ? 64 : (BN <= 128 ? 128 : 256));
+    const int ntn = (p.N + BN - 1) / BN;
+    const int64_t ntiles = ((p.M + BM - 1) / BM) * ntn;
+    // two accumulators of BN fp32 columns each
+    constexpr uint32_t kCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(&afull[s], kProducers);
+            mbar_init(&afull[s], kProdWarps * 32);
             mbar_init(&bfull[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum, 1);
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -275,150 +313,195 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < 4) {
-        // ---------------- A producers: one tile row per thread ----------------
-        const int row = threadIdx.x;
-        const int64_t m = m0 + row;
-        ARow r;
-        r.valid = m < p.M;
-        r.iy0 = r.ix0 = 0;
-        r.xb = p.x;
-        r.scb = nullptr;
-        if (r.valid) {
-            if (p.mode == 0) {
-                r.xb = p.x + m * p.lda;
-            } else {
-                int ox = (int)(m % p.ow);
-                int64_t t = m / p.ow;
-                int oy = (int)(t % p.oh);
-                int nb = (int)(t / p.oh);
-                r.iy0 = oy * p.sh - p.pt;
-                r.ix0 = ox * p.sw - p.pl;
-                r.xb = p.x + (int64_t)nb * p.x_n;
-                r.scb = p.insc ? p.insc + (int64_t)nb * p.cin : nullptr;
-            }
-        }
+    if (warp < kProdWarps) {
+        // ---------------- A producers: thread pair per tile row, 4 chunks of 8 k each ----------------
+        const int row = threadIdx.x & (BM - 1);
+        const int half = threadIdx.x >> 7;  // 0: chunks 0-3, 1: chunks 4-7
         const int sw = row & 7;
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % STAGES;
-            const uint32_t par = ((kb / STAGES) & 1) ^ 1;
-            if (!mbar_wait(&empty[s], par, p.status, abort_flag, 11)) break;
-            uint8_t *ahi = smem + s * Lay::stage_bytes;
-            uint8_t *alo = ahi + Smem::a_bytes;
-            uint8_t *rhi = ahi + (row >> 3) * 1024 + (row & 7) * 128;
-            uint8_t *rlo = alo + (row >> 3) * 1024 + (row & 7) * 128;
-#pragma unroll 2
-            for (int c = 0; c < 8; c++) {
-                float v[8];
-                load8(p, r, kb * BK + c * 8, v);
-                uint4 hi, lo;
-                split8(v, hi, lo);
-                *reinterpret_cast<uint4 *>(rhi + ((c ^ sw) << 4)) = hi;
-                *reinterpret_cast<uint4 *>(rlo + ((c ^ sw) << 4)) = lo;
+        int it = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            const int64_t m0 = (t / ntn) * BM;
+            const ARow r = a_row(p, m0 + row);
+            for (int kb = 0; kb < nk; kb++, it++) {
+                const int s = it % STAGES;
+                if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 11)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *ahi = smem + s * Lay::stage_bytes;
+                uint8_t *rhi = ahi + (row >> 3) * 1024 + (row & 7) * 128;
+                uint8_t *rlo = rhi + Smem::a_bytes;
+                float v[4][8];
+#pragma unroll
+                for (int c = 0; c < 4; c++) load8(p, r, kb * BK + (half * 4 + c) * 8, v[c]);
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    uint4 hi, lo;
+                    split8(v[c], hi, lo);
+                    const int ch = half * 4 + c;
+                    *reinterpret_cast<uint4 *>(rhi + ((ch ^ sw) << 4)) = hi;
+                    *reinterpret_cast<uint4 *>(rlo + ((ch ^ sw) << 4)) = lo;
+                }
+                fence_async_smem();
+                mbar_arrive(&afull[s]);
             }
-            fence_async_smem();
-            mbar_arrive(&afull[s]);
         }
-    } else if (warp == 8) {
+    } else if (warp == kTmaWarp) {
         // ---------------- B loader: TMA of the pre-split weight tiles ----------------
         if (lane == 0) {
-            int issued = 0;
-            for (int kb = 0; kb < nk; kb++) {
-                const int s = kb % STAGES;
-                const uint32_t par = ((kb / STAGES) & 1) ^ 1;
-                if (!mbar_wait(&empty[s], par, p.status, abort_flag, 12)) break;
-                uint8_t *bhi = smem + s * Lay::stage_bytes + 2 * Smem::a_bytes;
-                uint8_t *blo = bhi + Lay::b_bytes;
-                mbar_expect_tx(&bfull[s], 2 * Lay::b_bytes);
-                tma_load_2d(bhi, &tm_hi, &bfull[s], kb * BK, n0);
-                tma_load_2d(blo, &tm_lo, &bfull[s], kb * BK, n0);
-                issued = kb + 1;
+            int it = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int n0 = (int)(t % ntn) * BN;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 12)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *bhi = smem + s * Lay::stage_bytes + 2 * Smem::a_bytes;
+                    uint8_t *blo = bhi + Lay::b_bytes;
+                    mbar_expect_tx(&bfull[s], 2 * Lay::b_bytes);
+                    tma_load_2d(bhi, &tm_hi, &bfull[s], kb * BK, n0);
+                    tma_load_2d(blo, &tm_lo, &bfull[s], kb * BK, n0);
+                }
             }
-            // drain: every issued copy lands before the CTA may exit (bounded)
-            for (int kb = (issued > STAGES ? issued - STAGES : 0); kb < issued; kb++) {
+            // drain: the last STAGES issued copies land before the CTA may exit (bounded)
+            for (int j = (it > STAGES ? it - STAGES : 0); j < it; j++) {
                 long long t0 = clock64();
-                while (!mbar_try(&bfull[kb % STAGES], (kb / STAGES) & 1) && clock64() - t0 < kWaitBudget) {
+                while (!mbar_try(&bfull[j % STAGES], (j / STAGES) & 1) && clock64() - t0 < kWaitBudget) {
                 }
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = instr_desc(BN);
             bool ok = true;
-            for (int kb = 0; kb < nk && ok; kb++) {
-                const int s = kb % STAGES;
-                const uint32_t par = (kb / STAGES) & 1;
-                ok = mbar_wait(&afull[s], par, p.status, abort_flag, 13) &&
-                     mbar_wait(&bfull[s], par, p.status, abort_flag, 14);
+            int it = 0, lt = 0;
+            for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
+                const int ab = lt & 1;
+                const uint32_t dcol = tmem + ab * BN;
+                ok = mbar_wait(&tempty[ab], ((lt >> 1) & 1) ^ 1, p.status, abort_flag, 16);
                 if (!ok) break;
                 tc_fence_after();
-                uint8_t *base = smem + s * Lay::stage_bytes;
-                const uint32_t ahi = smem_u32(base), alo = ahi + Smem::a_bytes;
-                const uint32_t bhi = alo + Smem::a_bytes, blo = bhi + Lay::b_bytes;
+                for (int kb = 0; kb < nk; kb++, it++) {
+                    const int s = it % STAGES;
+                    const uint32_t par = (it / STAGES) & 1;
+                    ok = mbar_wait(&afull[s], par, p.status, abort_flag, 13) &&
+                         mbar_wait(&bfull[s], par, p.status, abort_flag, 14);
+                    if (!ok) break;
+                    tc_fence_after();
+                    uint8_t *base = smem + s * Lay::stage_bytes;
+                    const uint32_t ahi = smem_u32(base), alo = ahi + Smem::a_bytes;
+                    const uint32_t bhi = alo + Smem::a_bytes, blo = bhi + Lay::b_bytes;
 #pragma unroll
-                for (int kk = 0; kk < BK / 16; kk++) {
-                    const uint32_t off = kk * 32;
-                    umma(tmem, smem_desc(ahi + off), smem_desc(bhi + off), idesc, (kb | kk) != 0);
-                    umma(tmem, smem_desc(ahi + off), smem_desc(blo + off), idesc, 1);
-                    umma(tmem, smem_desc(alo + off), smem_desc(bhi + off), idesc, 1);
+                    for (int kk = 0; kk < BK / 16; kk++) {
+                        const uint32_t off = kk * 32;
+                        umma(dcol, smem_desc(ahi + off), smem_desc(bhi + off), idesc, (kb | kk) != 0);
+                        umma(dcol, smem_desc(ahi + off), smem_desc(blo + off), idesc, 1);
+                        umma(dcol, smem_desc(alo + off), smem_desc(bhi + off), idesc, 1);
+                    }
+                    umma_commit(&empty[s]);
                 }
-                umma_commit(&empty[s]);
+                if (ok) umma_commit(&tfull[ab]);
             }
-            umma_commit(ok ? accum : drain);
-            if (!ok) {  // wait for the MMAs already issued before the memory goes away
-                long long t0 = clock64();
-                while (!mbar_try(drain, 0) && clock64() - t0 < kWaitBudget) {
-                }
+            // every issued MMA completes before the shared and tensor memory go away (bounded)
+            umma_commit(drain);
+            long long t0 = clock64();
+            while (!mbar_try(drain, 0) && clock64() - t0 < kWaitBudget) {
             }
         }
     } else {
-        // ---------------- epilogue: warps 4-7, TMEM lanes 32 * (warp - 4) ----------------
-        const int q = warp - 4;
+        // ---------------- epilogue: warps 8-11, TMEM lanes 32 * (warp % 4) ----------------
+        const int q = warp & 3;
         const int row = q * 32 + lane;
-        const int64_t m = m0 + row;
-        bool ok = mbar_wait(accum, 0, p.status, abort_flag, 15);
-        tc_fence_after();
-        if (ok) {
+        int lt = 0;
+        for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
+            const int ab = lt & 1;
+            if (!mbar_wait(&tfull[ab], (lt >> 1) & 1, p.status, abort_flag, 15)) break;
+            tc_fence_after();
+            const int64_t m = (t / ntn) * BM + row;
+            const int n0 = (int)(t % ntn) * BN;
             int ox = 0, oy = 0, nb = 0;
             int64_t pix = 0;
             if (p.mode == 1 && m < p.M) {
                 ox = (int)(m % p.ow);
-                int64_t t = m / p.ow;
-                oy = (int)(t % p.oh);
-                nb = (int)(t / p.oh);
+                int64_t tt = m / p.ow;
+                oy = (int)(tt % p.oh);
+                nb = (int)(tt / p.oh);
                 pix = (int64_t)oy * p.ow + ox;
             }
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float v[16];
-                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
-                if (m >= p.M) continue;
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ab * BN + c0, v);
+                if (m >= p.M || n0 + c0 >= p.N) continue;
+                if (p.scatter && p.scat_cout == BN) {
+                    // one tap per N tile: 16 consecutive channels of output pixel (s oy + ky, s ox + kx)
+                    const int s = p.scatter, tap = n0 / BN;
+                    const int yy = oy * s + tap / s, xx = ox * s + tap % s;
+                    float *dst = p.y + (int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + c0;
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int col = n0 + c0 + j;
-                    if (col >= p.N) break;
-                    if (p.scatter) {
-                        const int s = p.scatter;
+                    for (int j = 0; j < 16; j++) v[j] = act_f(v[j] + (p.bias ? p.bias[c0 + j] : 0.f), p.act);
+                    if (p.out_vec) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+                            d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; j++) dst[j] = v[j];
+                    }
+                    continue;
+                }
+                if (p.scatter) {
+                    const int s = p.scatter;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int col = n0 + c0 + j;
+                        if (col >= p.N) break;
                         const int co = col % p.scat_cout, tap = col / p.scat_cout;
                         const int yy = oy * s + tap / s, xx = ox * s + tap % s;
                         float o = act_f(v[j] + (p.bias ? p.bias[co] : 0.f), p.act);
                         p.y[(int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co] = o;
-                    } else if (p.mode == 1) {
-                        float o = act_f(v[j] + (p.bias ? p.bias[col] : 0.f), p.act);
-                        if (p.res) o += p.res[(int64_t)nb * p.res_n + pix * p.res_pix + col];
-                        p.y[(int64_t)nb * p.y_n + pix * p.y_pix + col] = o;
-                    } else {
-                        float o = act_f(v[j] + (p.bias ? p.bias[col] : 0.f), p.act);
-                        p.y[m * p.ldy + col] = o;
                     }
+                    continue;
+                }
+                float *dst;
+                const float *rsrc = nullptr;
+                if (p.mode == 1) {
+                    dst = p.y + (int64_t)nb * p.y_n + pix * p.y_pix + n0 + c0;
+                    if (p.res) rsrc = p.res + (int64_t)nb * p.res_n + pix * p.res_pix + n0 + c0;
+                } else {
+                    dst = p.y + m * p.ldy + n0 + c0;
+                }
+                const float *bsrc = p.bias ? p.bias + n0 + c0 : nullptr;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    float o = act_f(v[j] + (bsrc ? bsrc[j] : 0.f), p.act);
+                    if (rsrc && n0 + c0 + j < p.N) o += rsrc[j];
+                    v[j] = o;
+                }
+                const bool full = n0 + c0 + 16 <= p.N && p.out_vec;
+                if (full) {
+                    float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (n0 + c0 + j < p.N) dst[j] = v[j];
                 }
             }
+            tc_fence_before();
+            mbar_arrive(&tempty[ab]);
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
     }
@@ -459,8 +542,9 @@ void launch(Ctx *c, const UmmaW &w, const UmmaP &p) {
         WOCR_CUDA(cudaFuncSetAttribute(k_umma<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::total));
         set[c->device] = true;
     }
-    dim3 grid((unsigned)((p.M + BM - 1) / BM), (unsigned)((p.N + BN - 1) / BN));
-    k_umma<BN, STAGES><<<grid, kThreads, Lay::total, c->stream>>>(w.map_hi, w.map_lo, p);
+    int64_t tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+    unsigned grid = (unsigned)std::min<int64_t>(tiles, c->sm_count);
+    k_umma<BN, STAGES><<<grid, kAllThreads, Lay::total, c->stream>>>(w.map_hi, w.map_lo, p);
     WOCR_LAUNCHED(c);
 }
 
@@ -474,13 +558,13 @@ int umma_bn(int N) {
     return 256;
 }
 
-UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K) {
+UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int max_bn) {
     // wnk: [N][K] fp32 (row n = output channel, k in the A operand's order)
     UmmaW w;
     w.N = N;
     w.K = K;
     w.Kpad = (K + BK - 1) / BK * BK;
-    w.bn = umma_bn(N);
+    w.bn = umma_bn(std::min(N, max_bn));
     const int Npad = (N + w.bn - 1) / w.bn * w.bn;  // every TMA box lies inside the tensor
     std::vector<__nv_bfloat16> hi((size_t)Npad * w.Kpad, __float2bfloat16_rn(0.f)), lo = hi;
     for (int n = 0; n < N; n++)
@@ -509,6 +593,8 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
         WOCR_CUDA(cudaMemsetAsync(c->status, 0, 16, c->stream));
     }
     p.status = c->status;
+    const bool al = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0;
+    p.out_vec = p.mode == 1 ? (al && p.y_pix % 4 == 0 && p.y_n % 4 == 0) : (al && p.ldy % 4 == 0);
     p.K = w.K;
     p.Kpad = w.Kpad;
     p.N = w.N;
@@ -517,9 +603,9 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
                    4.0 * (double)w.N * w.Kpad;
     Prof pf(c, p.scatter ? "umma_convt" : (p.mode == 1 ? "umma_conv" : "umma_linear"), flops, bytes);
     switch (w.bn) {
-    case 16: launch<16, 4>(c, w, p); break;
-    case 32: launch<32, 4>(c, w, p); break;
-    case 64: launch<64, 3>(c, w, p); break;
+    case 16: launch<16, 6>(c, w, p); break;
+    case 32: launch<32, 5>(c, w, p); break;
+    case 64: launch<64, 4>(c, w, p); break;
     case 128: launch<128, 3>(c, w, p); break;
     default: launch<256, 2>(c, w, p); break;
     }

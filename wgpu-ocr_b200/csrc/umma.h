@@ -32,6 +32,7 @@ struct UmmaP {
     int act = 0;
     float *y = nullptr;
     int64_t y_n = 0, y_pix = 0, ldy = 0;
+    int out_vec = 0;              // 16-byte aligned output rows: float4 stores
     const float *res = nullptr;
     int64_t res_n = 0, res_pix = 0;
     int scatter = 0, scat_cout = 0;
@@ -40,7 +41,9 @@ struct UmmaP {
 
 int umma_bn(int N);
 // wnk: [N][K] fp32, k in the order the A operand is produced (ky, kx, ci for convolutions).
-UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K);
+// max_bn caps the N tile (a ConvTranspose with kernel == stride uses its cout, so each N tile
+// is one tap and the scatter epilogue stores contiguous channels).
+UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int max_bn = 256);
 void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p);
 
 }  // namespace k
