@@ -110,6 +110,9 @@ int32_t wocr_ctx_profile(wocr_ctx *ctx, int32_t on);
 /* Waits for the recorded launches and writes a JSON array of
  * {"kernel", "launches", "ms", "flops", "bytes"} per kernel name into buf (capacity cap). */
 int32_t wocr_ctx_profile_report(wocr_ctx *ctx, char *buf, int32_t cap);
+/* The same records launch by launch, in launch order: a JSON array of
+ * {"kernel", "ms", "flops", "bytes"}. */
+int32_t wocr_ctx_profile_launches(wocr_ctx *ctx, char *buf, int32_t cap);
 /* Page-locked host memory for fast copies (the caller's staging buffers). */
 int32_t wocr_host_alloc(size_t bytes, void **out);
 void wocr_host_free(void *p);

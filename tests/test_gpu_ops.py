@@ -42,6 +42,8 @@ def run_nd(gpu, m, x, stop=False):
     (24, 24, 3, (2, 1), [1, 1, 1, 1], 24, None),       # depthwise (2, 1)
     (5, 7, 3, (2, 2), [0, 0, 1, 1], 1, None),          # asymmetric pads, generic K decode
     (8, 130, 3, (1, 1), [1, 1, 1, 1], 1, "relu"),      # N not a multiple of the tile
+    (16, 1, 1, (1, 1), [0, 0, 0, 0], 1, None),         # narrow 1 x 1 head: pointwise kernel
+    (13, 5, 1, (1, 1), [0, 0, 0, 0], 1, "relu"),       # pointwise, cin not a multiple of 4
 ])
 def test_conv(gpu, cin, cout, k, stride, pads, group, act):
     b = _Builder(3)
@@ -79,6 +81,17 @@ def test_convt_batchnorm_resize_concat(gpu):
     y = b.op("MaxPool", [y], {"kernel_shape": [3, 3], "strides": [2, 2], "pads": [1, 1, 1, 1]})
     m = b.model("x", y)
     x = rnd(1, 12, 7, 13)
+    close(run_nd(gpu, m, x), ref.run_onnx(m, x))
+
+
+@pytest.mark.parametrize("cin,cout", [(32, 16), (64, 32), (24, 48)])
+def test_convt_scatter_full_taps(gpu, cin, cout):
+    """ConvTranspose k == s == 2 as one GEMM whose N tile spans all four taps; the scatter
+    epilogue stores 16 contiguous channels per chunk (cout a multiple of 16)."""
+    b = _Builder(8)
+    y = b.op("Relu", [b.convt("x", cin, cout, 2, 2)])
+    m = b.model("x", y)
+    x = rnd(2, cin, 9, 23)
     close(run_nd(gpu, m, x), ref.run_onnx(m, x))
 
 

@@ -268,6 +268,27 @@ int32_t wocr_ctx_profile_report(wocr_ctx *ctx, char *buf, int32_t cap) {
     });
 }
 
+int32_t wocr_ctx_profile_launches(wocr_ctx *ctx, char *buf, int32_t cap) {
+    return guard([&] {
+        if (!ctx || !buf || cap <= 0) fail(WOCR_ERR_INVALID, "null argument");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        std::string s = "[";
+        for (auto &r : c->recs) {
+            float ms = 0;
+            WOCR_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+            char tmp[256];
+            std::snprintf(tmp, sizeof tmp, "%s{\"kernel\": \"%s\", \"ms\": %.6f, \"flops\": %.6e, \"bytes\": %.6e}",
+                          s.size() > 1 ? ", " : "", r.name, ms, r.flops, r.bytes);
+            s += tmp;
+        }
+        s += "]";
+        if ((int64_t)s.size() + 1 > cap) fail(WOCR_ERR_CAPACITY, "report needs " + std::to_string(s.size() + 1) + " bytes");
+        std::memcpy(buf, s.c_str(), s.size() + 1);
+    });
+}
+
 int32_t wocr_host_alloc(size_t bytes, void **out) {
     return guard([&] {
         if (!out) fail(WOCR_ERR_INVALID, "null out");

@@ -133,8 +133,7 @@ ConvTW lower_convt(Ctx *c, const HostW &w, const std::vector<float> &bias, int s
             std::vector<float> nk((size_t)N * t.cin);
             for (int ci = 0; ci < t.cin; ci++)
                 for (int j = 0; j < N; j++) nk[(size_t)j * t.cin + ci] = m[(size_t)ci * t.ldw + j];
-            const int max_bn = (t.cout % 16 == 0 && t.cout <= 256) ? t.cout : 256;  // one tap per N tile
-            t.uw = std::make_shared<k::UmmaW>(k::make_umma_weights(c, nk, N, t.cin, max_bn));
+            t.uw = std::make_shared<k::UmmaW>(k::make_umma_weights(c, nk, N, t.cin));
         }
     } else {
         t.w = upload(c, w.data);
@@ -236,6 +235,13 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
     }
     if (cw.cin != cin)
         fail(WOCR_ERR_SHAPE, "Conv expects " + std::to_string(cw.cin) + " channels, has " + std::to_string(cin));
+    if (cw.cout < 16 && cw.kh == 1 && cw.kw == 1 && cw.sh == 1 && cw.sw == 1 && pt == 0 && pl == 0 && pb == 0 && pr == 0 && !res && !scale &&
+        cin <= 4096) {
+        // too narrow for a tensor-core tile: a memory-bound pass over the pixels
+        k::pointwise(c, x.p, x.strides[0], x.pix(), h * w, (int)n, (int)cin, cw.w.p, cw.ldw, cw.b.p, cw.cout, act, y.p,
+                     y.strides[0], y.pix());
+        return y;
+    }
     DT r, s;
     k::ConvP p;
     p.x = x.p;

@@ -3,6 +3,8 @@
 // general ConvTranspose.
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "kernels.h"
 
 namespace wocr {
@@ -315,6 +317,49 @@ __global__ void k_convt_gather(const float *__restrict__ x, int64_t x_n, int64_t
     }
 }
 
+
+// 1 x 1 convolution with few output channels (< 16, e.g. a detector head): memory-bound, one
+// thread per pixel, weights [cin][cout] in shared memory.  The tensor-core tile would be mostly
+// empty for such an N.
+template <int COUT, bool VEC>
+__global__ void k_pointwise(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin,
+                            const float *__restrict__ wt, int ldw, const float *__restrict__ bias, int cout, int act,
+                            float *__restrict__ y, int64_t y_n, int64_t y_pix) {
+    extern __shared__ float ws[];  // [cin][COUT]
+    for (int i = threadIdx.x; i < cin * COUT; i += blockDim.x) {
+        int ci = i / COUT, co = i % COUT;
+        ws[i] = co < cout ? wt[(int64_t)ci * ldw + co] : 0.f;
+    }
+    __syncthreads();
+    const int64_t total = (int64_t)n * hw;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t nb = i / hw, pix = i - nb * hw;
+        const float *xp = x + nb * x_n + pix * x_pix;
+        float acc[COUT];
+#pragma unroll
+        for (int co = 0; co < COUT; co++) acc[co] = co < cout ? bias[co] : 0.f;
+        if (VEC) {
+            for (int ci = 0; ci < cin; ci += 4) {
+                float4 v = __ldg(reinterpret_cast<const float4 *>(xp + ci));
+                const float *w0 = ws + ci * COUT;
+#pragma unroll
+                for (int co = 0; co < COUT; co++)
+                    acc[co] += v.x * w0[co] + v.y * w0[COUT + co] + v.z * w0[2 * COUT + co] + v.w * w0[3 * COUT + co];
+            }
+        } else {
+            for (int ci = 0; ci < cin; ci++) {
+                float v = xp[ci];
+#pragma unroll
+                for (int co = 0; co < COUT; co++) acc[co] += v * ws[ci * COUT + co];
+            }
+        }
+        float *yp = y + nb * y_n + pix * y_pix;
+#pragma unroll
+        for (int co = 0; co < COUT; co++)
+            if (co < cout) yp[co] = act_f(acc[co], act);
+    }
+}
+
 inline int grid_for(Ctx *c, int64_t work, int per_block = 256) {
     int64_t g = (work + per_block - 1) / per_block;
     int64_t cap = (int64_t)c->sm_count * 16;
@@ -337,6 +382,32 @@ void conv_gemm(Ctx *c, const ConvP &p) {
     else k_conv_gemm<false><<<grid, 256, 0, c->stream>>>(p);
     WOCR_LAUNCHED(c);
     c->flops += 2.0 * (double)M * p.cout * p.kh * p.kw * p.cin;
+}
+
+void pointwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin, const float *wt, int ldw,
+               const float *bias, int cout, int act, float *y, int64_t y_n, int64_t y_pix) {
+    const int64_t total = (int64_t)n * hw;
+    if (total == 0) return;
+    Prof pf(c, "pointwise", 2.0 * (double)total * cin * cout, 4.0 * (double)total * (cin + cout));
+    const bool vec = cin % 4 == 0 && x_pix % 4 == 0 && x_n % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const int grid = grid_for(c, total);
+    auto go = [&](auto cout_tag) {
+        constexpr int CO = decltype(cout_tag)::value;
+        const size_t smem = sizeof(float) * cin * CO;
+        if (vec)
+            k_pointwise<CO, true><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias, cout, act,
+                                                                   y, y_n, y_pix);
+        else
+            k_pointwise<CO, false><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias, cout, act,
+                                                                    y, y_n, y_pix);
+    };
+    if (cout <= 1) go(std::integral_constant<int, 1>());
+    else if (cout <= 2) go(std::integral_constant<int, 2>());
+    else if (cout <= 4) go(std::integral_constant<int, 4>());
+    else if (cout <= 8) go(std::integral_constant<int, 8>());
+    else go(std::integral_constant<int, 16>());
+    WOCR_LAUNCHED(c);
+    c->flops += 2.0 * (double)total * cin * cout;
 }
 
 void conv_direct(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, const float *wt,

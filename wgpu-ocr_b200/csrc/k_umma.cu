@@ -10,14 +10,14 @@
 // bf16 and 2^-11 for tf32.
 //
 // Persistent: one CTA per SM loops over 128 x BN output tiles; the shared-memory stage ring runs
-// on across tile boundaries and the fp32 accumulator in tensor memory is double-buffered, so
-// loads of the next tile and the epilogue of the last one overlap the MMAs of the current one.
-//   warps 0-7   produce A: two threads per tile row, 64 k per stage, fp32 loads (implicit
+// on across tile boundaries and the fp32 accumulators in tensor memory are multi-buffered (up to
+// 8 tiles), so loads of the next tiles and the epilogues of earlier ones overlap the MMAs.
+//   warps 0-15  produce A: four threads per tile row, 64 k per stage, fp32 loads (implicit
 //               im2col for convolutions, zero padding, SE input scale), split to bf16 hi/lo,
 //               written in the 128-byte-swizzled K-major layout the MMA reads;
-//   warp 12     issues the TMA loads of the pre-split weight tiles (B hi/lo, BN x 64 each);
-//   warp 13     allocates tensor memory and (one thread) issues tcgen05.mma + tcgen05.commit;
-//   warps 8-11  the epilogue: tcgen05.ld of the accumulator, bias, activation, residual,
+//   warp 20     issues the TMA loads of the pre-split weight tiles (B hi/lo, BN x 64 each);
+//   warp 21     allocates tensor memory and (one thread) issues tcgen05.mma + tcgen05.commit;
+//   warps 16-19 the epilogue: tcgen05.ld of the accumulator, bias, activation, residual,
 //               channels-last stores (or the ConvTranspose scatter), then hand the accumulator
 //               buffer back to the MMA warp.
 // Stages are handed over with mbarriers.  Every wait is bounded by a clock budget; on expiry
@@ -40,6 +40,7 @@ namespace k {
 namespace {
 
 constexpr int BM = 128, BK = 64;
+constexpr int kTapTable = 1024;  // 8-wide k chunks described in shared memory (K <= 8192)
 constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (about 2 s) per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -71,12 +72,26 @@ __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// The same, but the thread is suspended (not spinning, so it leaves the issue slots to the warps
+// doing work) until the phase completes or about 0.5 ms pass.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait: false (and an error code in *status) when the budget runs out or another role
 // has already given up.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
                                           int code) {
     long long t0 = clock64();
-    while (!mbar_try(bar, parity)) {
+    while (!mbar_try_sleep(bar, parity)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > kWaitBudget) {
             *abort_flag = 1;
@@ -85,6 +100,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
         }
     }
     return true;
+}
+
+// One lane polls, the warp follows: a warp-uniform outcome for warp-wide code after the wait.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
+                                          int code) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, abort_flag, code);
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -179,7 +202,8 @@ struct Layout {
     static constexpr int b_bytes = BN * BK * 2;
     static constexpr int stage_bytes = 2 * Smem::a_bytes + 2 * b_bytes;
     static constexpr int bar_off = STAGES * stage_bytes;
-    static constexpr int total = bar_off + 512 + 1024;  // barriers + tmem slot, + alignment slack
+    static constexpr int tab_off = bar_off + 1024;   // barriers and tmem slot first
+    static constexpr int total = tab_off + 4 * kTapTable + 1024;  // + tap table + alignment slack
 };
 
 // The fp32 source of one row of A (an output pixel of a convolution, or a row of x).
@@ -200,10 +224,11 @@ __device__ __forceinline__ ARow a_row(const UmmaP &p, int64_t m) {
         if (p.mode == 0) {
             r.xb = p.x + m * p.lda;
         } else {
-            int ox = (int)(m % p.ow);
-            int64_t t = m / p.ow;
-            int oy = (int)(t % p.oh);
-            int nb = (int)(t / p.oh);
+            const int mi = (int)m;  // M < 2^31 (checked on the host)
+            const int ox = mi % p.ow;
+            const int t = mi / p.ow;
+            const int oy = t % p.oh;
+            const int nb = t / p.oh;
             r.iy0 = oy * p.sh - p.pt;
             r.ix0 = ox * p.sw - p.pl;
             r.xb = p.x + (int64_t)nb * p.x_n;
@@ -260,24 +285,63 @@ __device__ __forceinline__ void load8(const UmmaP &p, const ARow &r, int k0, flo
 }
 
 // Warp roles of the persistent kernel (448 threads):
-constexpr int kProdWarps = 8;   // warps 0-7: A producers, two threads per tile row
-constexpr int kEpiWarp0 = 8;    // warps 8-11: epilogue (TMEM lane quadrant = warp % 4)
-constexpr int kTmaWarp = 12;    // warp 12: B tiles by TMA
-constexpr int kMmaWarp = 13;    // warp 13: TMEM allocation, MMA issue
-constexpr int kAllThreads = 14 * 32;
+constexpr int kProdWarps = 16;  // warps 0-15: A producers, four threads per tile row
+constexpr int kEpiWarp0 = 16;   // warps 16-19: epilogue (TMEM lane quadrant = warp % 4)
+constexpr int kTmaWarp = 20;    // warp 20: B tiles by TMA
+constexpr int kMmaWarp = 21;    // warp 21: TMEM allocation, MMA issue
+constexpr int kAllThreads = 22 * 32;
+
+// Accumulator buffers in tensor memory: as many BN-column fp32 tiles as fit its 512 columns, at
+// most 8, so the MMA warp can run that many tiles ahead of the epilogue.
+template <int BN>
+struct Acc {
+    // Independent accumulation chains per tile: consecutive MMAs into one accumulator serialise
+    // on its read-modify-write, so narrow tiles (whose MMAs are short) spread the 12 MMAs of a
+    // stage over several accumulators and the epilogue adds them up.
+    static constexpr int chains = BN <= 16 ? 6 : (BN <= 32 ? 4 : (BN <= 64 ? 2 : 1));
+    static constexpr int cols = BN * chains;  // TMEM columns of one tile
+    static constexpr int n = 512 / cols < 8 ? 512 / cols : 8;
+};
+
+// The im2col source of one 8-wide k chunk of a convolution, precomputed per CTA: tap row (bits
+// 24-31), tap column (16-23) and first input channel (0-15); 0xffffffff past K.
+__device__ __forceinline__ uint32_t tap_entry(const UmmaP &p, int g) {
+    const int k0 = g * 8;
+    if (k0 >= p.K) return 0xffffffffu;
+    const int tap = k0 / p.cin, ci = k0 - tap * p.cin;
+    const int ky = tap / p.kw, kx = tap - ky * p.kw;
+    return ((uint32_t)ky << 24) | ((uint32_t)kx << 16) | (uint32_t)ci;
+}
+
+// load8 for convolutions with cin % 8 == 0 through the tap table: no divisions.
+__device__ __forceinline__ void load8_tab(const UmmaP &p, const ARow &r, uint32_t e, float (&v)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = 0.f;
+    if (!r.valid || e == 0xffffffffu) return;
+    const int iy = r.iy0 + (int)(e >> 24), ix = r.ix0 + (int)((e >> 16) & 0xff), ci = (int)(e & 0xffff);
+    if (iy < 0 || iy >= p.h || ix < 0 || ix >= p.w) return;
+    const float4 *src = reinterpret_cast<const float4 *>(r.xb + ((int64_t)iy * p.w + ix) * p.x_pix + ci);
+    float4 a = __ldg(src), b = __ldg(src + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    if (r.scb) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] *= r.scb[ci + i];
+    }
+}
 
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(kAllThreads, 1)
     k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo, UmmaP p) {
     using Lay = Layout<BN, STAGES>;
+    constexpr int NACC = Acc<BN>::n;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *afull = reinterpret_cast<uint64_t *>(smem + Lay::bar_off);
     uint64_t *bfull = afull + STAGES;
     uint64_t *empty = bfull + STAGES;
-    uint64_t *tfull = empty + STAGES;   // [2] accumulator ready (tcgen05.commit)
-    uint64_t *tempty = tfull + 2;       // [2] accumulator drained by the epilogue (128 arrivals)
-    uint64_t *drain = tempty + 2;
+    uint64_t *tfull = empty + STAGES;   // [NACC] accumulator ready (tcgen05.commit)
+    uint64_t *tempty = tfull + NACC;    // [NACC] accumulator drained by the epilogue (4 warps)
+    uint64_t *drain = tempty + NACC;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -286,23 +350,28 @@ __global__ void __launch_bounds__(kAllThreads, 1)
     const int ntn = (p.N + BN - 1) / BN;
     const int64_t ntiles = ((p.M + BM - 1) / BM) * ntn;
     // two accumulators of BN fp32 columns each
-    constexpr uint32_t kCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+    constexpr int NCH = Acc<BN>::chains, TCOLS = Acc<BN>::cols;
+    constexpr uint32_t kCols = NACC * TCOLS <= 32 ? 32 : (NACC * TCOLS <= 64 ? 64 : (NACC * TCOLS <= 128 ? 128 : (NACC * TCOLS <= 256 ? 256 : 512)));
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(&afull[s], kProdWarps * 32);
+            mbar_init(&afull[s], kProdWarps);
             mbar_init(&bfull[s], 1);
             mbar_init(&empty[s], 1);
         }
-        for (int a = 0; a < 2; a++) {
+        for (int a = 0; a < NACC; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], 4);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
+    uint32_t *taps = reinterpret_cast<uint32_t *>(smem + Lay::tab_off);
+    const bool use_tab = p.mode == 1 && p.vec && p.Kpad / 8 <= kTapTable;
+    if (use_tab)
+        for (int g = threadIdx.x; g < p.Kpad / 8; g += blockDim.x) taps[g] = tap_entry(p, g);
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kCols));
@@ -314,37 +383,62 @@ __global__ void __launch_bounds__(kAllThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp < kProdWarps) {
-        // ---------------- A producers: thread pair per tile row, 4 chunks of 8 k each ----------------
+        // ---------------- A producers: four threads per tile row, 2 chunks of 8 k each ----------------
+        // Software-pipelined: the loads of the next k block are issued before waiting for a free
+        // stage and converting the current one, so two k blocks of loads are in flight.
         const int row = threadIdx.x & (BM - 1);
-        const int half = threadIdx.x >> 7;  // 0: chunks 0-3, 1: chunks 4-7
+        const int quarter = threadIdx.x >> 7;  // chunks 2 quarter, 2 quarter + 1
         const int sw = row & 7;
-        int it = 0;
-        bool ok = true;
-        for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            const int64_t m0 = (t / ntn) * BM;
-            const ARow r = a_row(p, m0 + row);
-            for (int kb = 0; kb < nk; kb++, it++) {
-                const int s = it % STAGES;
-                if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 11)) {
-                    ok = false;
-                    break;
+        int64_t t = blockIdx.x;
+        int kb = 0, it = 0;
+        auto load_pair = [&](const ARow &r, int kbl, float (&v)[2][8]) {
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                const int g = kbl * (BK / 8) + quarter * 2 + c;
+                if (use_tab) load8_tab(p, r, taps[g], v[c]);
+                else load8(p, r, g * 8, v[c]);
+            }
+        };
+        if (t < ntiles) {
+            ARow r = a_row(p, (t / ntn) * BM + row);
+            float cur[2][8], nxt[2][8];
+            load_pair(r, 0, cur);
+            while (true) {
+                // the (tile, k block) after this one
+                int64_t t2 = t;
+                int kb2 = kb + 1;
+                if (kb2 == nk) {
+                    kb2 = 0;
+                    t2 = t + gridDim.x;
                 }
-                uint8_t *ahi = smem + s * Lay::stage_bytes;
-                uint8_t *rhi = ahi + (row >> 3) * 1024 + (row & 7) * 128;
+                const bool more = t2 < ntiles;
+                if (more) {
+                    if (t2 != t) r = a_row(p, (t2 / ntn) * BM + row);
+                    load_pair(r, kb2, nxt);
+                }
+                const int s = it % STAGES;
+                if (!warp_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 11)) break;
+                uint8_t *rhi = smem + s * Lay::stage_bytes + (row >> 3) * 1024 + (row & 7) * 128;
                 uint8_t *rlo = rhi + Smem::a_bytes;
-                float v[4][8];
 #pragma unroll
-                for (int c = 0; c < 4; c++) load8(p, r, kb * BK + (half * 4 + c) * 8, v[c]);
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
+                for (int c = 0; c < 2; c++) {
                     uint4 hi, lo;
-                    split8(v[c], hi, lo);
-                    const int ch = half * 4 + c;
+                    split8(cur[c], hi, lo);
+                    const int ch = quarter * 2 + c;
                     *reinterpret_cast<uint4 *>(rhi + ((ch ^ sw) << 4)) = hi;
                     *reinterpret_cast<uint4 *>(rlo + ((ch ^ sw) << 4)) = lo;
                 }
                 fence_async_smem();
-                mbar_arrive(&afull[s]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&afull[s]);  // one arrival per warp
+                it++;
+                if (!more) break;
+                t = t2;
+                kb = kb2;
+#pragma unroll
+                for (int c = 0; c < 2; c++)
+#pragma unroll
+                    for (int e = 0; e < 8; e++) cur[c][e] = nxt[c][e];
             }
         }
     } else if (warp == kTmaWarp) {
@@ -381,9 +475,9 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             bool ok = true;
             int it = 0, lt = 0;
             for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
-                const int ab = lt & 1;
-                const uint32_t dcol = tmem + ab * BN;
-                ok = mbar_wait(&tempty[ab], ((lt >> 1) & 1) ^ 1, p.status, abort_flag, 16);
+                const int ab = lt % NACC;
+                const uint32_t dcol = tmem + ab * TCOLS;
+                ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 16);
                 if (!ok) break;
                 tc_fence_after();
                 for (int kb = 0; kb < nk; kb++, it++) {
@@ -399,9 +493,15 @@ __global__ void __launch_bounds__(kAllThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++) {
                         const uint32_t off = kk * 32;
-                        umma(dcol, smem_desc(ahi + off), smem_desc(bhi + off), idesc, (kb | kk) != 0);
-                        umma(dcol, smem_desc(ahi + off), smem_desc(blo + off), idesc, 1);
-                        umma(dcol, smem_desc(alo + off), smem_desc(bhi + off), idesc, 1);
+                        // MMA number j = 3 kk + {0, 1, 2} goes to chain j % NCH; a chain's first
+                        // MMA of the tile overwrites, the others accumulate
+                        const int j0 = 3 * kk;
+                        const uint32_t d0 = dcol + ((j0 + 0) % NCH) * BN;
+                        const uint32_t d1 = dcol + ((j0 + 1) % NCH) * BN;
+                        const uint32_t d2 = dcol + ((j0 + 2) % NCH) * BN;
+                        umma(d0, smem_desc(ahi + off), smem_desc(bhi + off), idesc, kb > 0 || j0 + 0 >= NCH);
+                        umma(d1, smem_desc(ahi + off), smem_desc(blo + off), idesc, kb > 0 || j0 + 1 >= NCH);
+                        umma(d2, smem_desc(alo + off), smem_desc(bhi + off), idesc, kb > 0 || j0 + 2 >= NCH);
                     }
                     umma_commit(&empty[s]);
                 }
@@ -414,37 +514,48 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             }
         }
     } else {
-        // ---------------- epilogue: warps 8-11, TMEM lanes 32 * (warp % 4) ----------------
+        // ---------------- epilogue: warps 16-19, TMEM lanes 32 * (warp % 4) ----------------
         const int q = warp & 3;
         const int row = q * 32 + lane;
         int lt = 0;
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
-            const int ab = lt & 1;
-            if (!mbar_wait(&tfull[ab], (lt >> 1) & 1, p.status, abort_flag, 15)) break;
+            const int ab = lt % NACC;
+            if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 15)) break;
             tc_fence_after();
             const int64_t m = (t / ntn) * BM + row;
             const int n0 = (int)(t % ntn) * BN;
             int ox = 0, oy = 0, nb = 0;
             int64_t pix = 0;
             if (p.mode == 1 && m < p.M) {
-                ox = (int)(m % p.ow);
-                int64_t tt = m / p.ow;
-                oy = (int)(tt % p.oh);
-                nb = (int)(tt / p.oh);
+                const int mi = (int)m;  // M < 2^31 (checked on the host)
+                ox = mi % p.ow;
+                const int tt = mi / p.ow;
+                oy = tt % p.oh;
+                nb = tt / p.oh;
                 pix = (int64_t)oy * p.ow + ox;
             }
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float v[16];
-                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ab * BN + c0, v);
-                if (m >= p.M || n0 + c0 >= p.N) continue;
-                if (p.scatter && p.scat_cout == BN) {
-                    // one tap per N tile: 16 consecutive channels of output pixel (s oy + ky, s ox + kx)
-                    const int s = p.scatter, tap = n0 / BN;
-                    const int yy = oy * s + tap / s, xx = ox * s + tap % s;
-                    float *dst = p.y + (int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + c0;
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + c0;
+                tmem_ld16(tbase, v);
+#pragma unroll 1
+                for (int ch = 1; ch < NCH; ch++) {
+                    float w[16];
+                    tmem_ld16(tbase + ch * BN, w);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] = act_f(v[j] + (p.bias ? p.bias[c0 + j] : 0.f), p.act);
+                    for (int j = 0; j < 16; j++) v[j] += w[j];
+                }
+                if (m >= p.M || n0 + c0 >= p.N) continue;
+                if (p.scatter && p.scat_cout % 16 == 0) {
+                    // a 16-column chunk lies in one tap: 16 consecutive channels of output pixel
+                    // (s oy + ky, s ox + kx)
+                    const int s = p.scatter, col = n0 + c0;
+                    const int tap = col / p.scat_cout, co0 = col - tap * p.scat_cout;
+                    const int yy = oy * s + tap / s, xx = ox * s + tap % s;
+                    float *dst = p.y + (int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co0;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = act_f(v[j] + (p.bias ? p.bias[co0 + j] : 0.f), p.act);
                     if (p.out_vec) {
                         float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
@@ -480,7 +591,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 const float *bsrc = p.bias ? p.bias + n0 + c0 : nullptr;
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
-                    float o = act_f(v[j] + (bsrc ? bsrc[j] : 0.f), p.act);
+                    float o = act_f(v[j] + (bsrc && n0 + c0 + j < p.N ? bsrc[j] : 0.f), p.act);
                     if (rsrc && n0 + c0 + j < p.N) o += rsrc[j];
                     v[j] = o;
                 }
@@ -496,7 +607,8 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[ab]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[ab]);  // one arrival per warp
         }
     }
     tc_fence_before();
@@ -587,6 +699,7 @@ UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int
 
 void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
     if (p.M == 0 || w.N == 0) return;
+    if (p.M >= (int64_t)INT32_MAX - BM) fail(WOCR_ERR_UNSUPPORTED, "GEMM with 2^31 rows or more");
     if (!c->status) {
         c->status_buf = alloc(c, 16);
         c->status = (int *)c->status_buf->p;

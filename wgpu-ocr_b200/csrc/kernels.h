@@ -42,6 +42,10 @@ void conv_direct(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int 
                  const float *bias, int cout, int kh, int kw, int pad, int act, int ph, int pw, float *y,
                  int64_t y_n, int64_t y_pix, int oh, int ow);
 
+// 1 x 1, stride 1 convolution with cout < 16 (a detector head), memory-bound; wt [cin][ldw].
+void pointwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin, const float *wt, int ldw,
+               const float *bias, int cout, int act, float *y, int64_t y_n, int64_t y_pix);
+
 // Depthwise convolution (K5, src/gpu.rs:356-383): wt [kh][kw][c], NHWC.
 void depthwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, int ch, const float *wt,
                const float *bias, int kh, int kw, int sh, int sw, int pt, int pl, int oh, int ow, int act, float *y,

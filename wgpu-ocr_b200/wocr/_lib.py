@@ -71,6 +71,7 @@ _SIGS = [
     ("wocr_ctx_launches", c_i64, [c_void_p]),
     ("wocr_ctx_profile", c_i32, [c_void_p, c_i32]),
     ("wocr_ctx_profile_report", c_i32, [c_void_p, c_char_p, c_i32]),
+    ("wocr_ctx_profile_launches", c_i32, [c_void_p, c_char_p, c_i32]),
     ("wocr_host_alloc", c_i32, [c_size_t, P(c_void_p)]),
     ("wocr_host_free", None, [c_void_p]),
     ("wocr_detector_create", c_i32, [c_void_p, P(CModel), P(c_void_p)]),

@@ -62,6 +62,13 @@ class Gpu:
         L.check(L.lib().wocr_ctx_profile_report(self.h, buf, len(buf)))
         return json.loads(buf.value.decode())
 
+    def profile_launches(self):
+        """[{kernel, ms, flops, bytes}] per recorded launch, in launch order."""
+        import json
+        buf = ctypes.create_string_buffer(1 << 22)
+        L.check(L.lib().wocr_ctx_profile_launches(self.h, buf, len(buf)))
+        return json.loads(buf.value.decode())
+
     def close(self):
         if self.h:
             L.lib().wocr_ctx_destroy(self.h)
