@@ -149,6 +149,52 @@ def test_graph_executor_ops(gpu):
         det.close()
 
 
+def _det_parity(gpu, m, x):
+    det = wocr.Detector(gpu, m)
+    try:
+        close(det.detect(x), ref.run_onnx(m, x)[0, 0])
+    finally:
+        det.close()
+
+
+def test_graph_split_activations(gpu):
+    """Values between the convolutions stored split (bf16 hi | lo) and read by the tap
+    convolution: 3 x 3 and 5 x 5 kernels, a partial 16-channel chunk (24 channels) and a
+    partial 32-channel chunk (40), N below one column chunk (8), the ConvTranspose scatter,
+    a split Concat, split MaxPool, the pointwise head; a cin = 8 conv takes the fp32 path."""
+    b = _Builder(12)
+    d = b.maxpool(b.conv_relu("image", 1, 16, 3), 2, 2)                  # 26 x 36
+    a = b.conv_relu(d, 16, 24, 3)
+    a2 = b.op("Relu", [b.conv(a, 24, 32, 5, pads=[2, 2, 2, 2])])
+    p = b.maxpool(a2, 2, 2)                                              # 13 x 18
+    u = b.op("Relu", [b.convt(p, 32, 16, 2, 2)])                         # 26 x 36
+    y = b.op("Concat", [u, a], {"axis": 1})                              # 40 channels
+    e = b.conv_relu(y, 40, 8, 3)
+    f = b.conv_relu(e, 8, 16, 1)
+    g = b.conv_relu(f, 16, 20, 3)
+    out = b.op("Sigmoid", [b.conv(g, 20, 1, 1, pads=[0, 0, 0, 0])])
+    m = b.model("image", out)
+    _det_parity(gpu, m, rnd(1, 1, 52, 72))
+    _det_parity(gpu, m, rnd(1, 1, 36, 44))
+
+
+def test_graph_split_fallbacks(gpu):
+    """Split values whose slices break the TMA alignment (a Concat of 16 + 12 + 24 channels puts
+    the 24-channel part at channel 28) and a ConvTranspose with cout % 16 != 0 (per-channel
+    scatter stores): these run through the fp32 conversions."""
+    b = _Builder(13)
+    d = b.maxpool(b.conv_relu("image", 1, 16, 3), 2, 2)
+    a = b.conv_relu(d, 16, 24, 3)
+    p = b.maxpool(b.conv_relu(a, 24, 32, 3), 2, 2)
+    u = b.op("Relu", [b.convt(p, 32, 16, 2, 2)])
+    v = b.op("Relu", [b.convt(p, 32, 12, 2, 2)])
+    y = b.op("Concat", [u, v, a], {"axis": 1})                           # 52 channels
+    g = b.conv_relu(y, 52, 16, 3)
+    out = b.op("Sigmoid", [b.conv(g, 16, 1, 1, pads=[0, 0, 0, 0])])
+    m = b.model("image", out)
+    _det_parity(gpu, m, rnd(1, 1, 40, 56))
+
+
 def test_unsupported_and_shape_errors(gpu):
     b = _Builder(10)
     y = b.op("LeakyRelu", ["x"])

@@ -116,6 +116,16 @@ DT new_nhwc(Ctx *c, int64_t n, int64_t ch, int64_t h, int64_t w) {
     return t;
 }
 
+DT new_nhwc_split(Ctx *c, int64_t n, int64_t ch, int64_t h, int64_t w) {
+    DT t;
+    t.shape = {n, ch, h, w};
+    t.strides = {h * w * 2 * ch, 1, w * 2 * ch, 2 * ch};
+    t.buf = alloc(c, (size_t)std::max<int64_t>(n * ch * h * w, 1) * 2 * sizeof(uint16_t));
+    t.p = (float *)t.buf->p;
+    t.split = true;
+    return t;
+}
+
 std::string shape_str(const std::vector<int64_t> &s) {
     std::ostringstream o;
     o << "[";

@@ -102,11 +102,17 @@ constexpr int kMaxRank = 6;  // src/nd.rs:30
 // tensors produced by the convolution kernels are channels-last (NHWC): strides
 // {H*W*P, 1, W*P, P} with the pixel stride P >= C (P > C when the tensor is a channel slice
 // of a wider buffer, e.g. one part of a Concat).
+//
+// A split tensor (`split`) is an NHWC activation stored for the tensor cores: per pixel the bf16
+// hi parts (bf16(v)) of all channels of its buffer, then their lo parts (bf16(v - hi)), the same
+// 4 bytes a value as fp32.  Its strides count bf16 elements, `p` addresses the hi part of the
+// view's first channel, and a channel's lo part lies pix() / 2 elements after its hi part.
 struct DT {
     float *p = nullptr;
     std::vector<int64_t> shape;
     std::vector<int64_t> strides;
     BufP buf;
+    bool split = false;
 
     int rank() const { return (int)shape.size(); }
     int64_t numel() const {
@@ -128,6 +134,7 @@ Ctx *ctx_of(wocr_ctx *h);
 std::vector<int64_t> rowmajor_strides(const std::vector<int64_t> &shape);
 DT new_rowmajor(Ctx *c, const std::vector<int64_t> &shape);
 DT new_nhwc(Ctx *c, int64_t n, int64_t ch, int64_t h, int64_t w);
+DT new_nhwc_split(Ctx *c, int64_t n, int64_t ch, int64_t h, int64_t w);
 std::string shape_str(const std::vector<int64_t> &s);
 
 }  // namespace wocr

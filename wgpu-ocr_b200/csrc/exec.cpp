@@ -142,6 +142,31 @@ ConvTW lower_convt(Ctx *c, const HostW &w, const std::vector<float> &bias, int s
     return t;
 }
 
+// The tap-convolution operand of a stride-1 dense convolution: [cout][ky][kx][ci].
+void attach_tconv(Ctx *c, ConvW &cw, const HostW &w) {
+    const int cout = (int)w.dims[0], cin = (int)w.dims[1], kh = (int)w.dims[2], kw = (int)w.dims[3];
+    std::vector<float> nk((size_t)cout * kh * kw * cin);
+    for (int co = 0; co < cout; co++)
+        for (int ci = 0; ci < cin; ci++)
+            for (int ky = 0; ky < kh; ky++)
+                for (int kx = 0; kx < kw; kx++)
+                    nk[(((size_t)co * kh + ky) * kw + kx) * cin + ci] = w.data[(((size_t)co * cin + ci) * kh + ky) * kw + kx];
+    cw.tw = std::make_shared<k::TconvW>(k::make_tconv_weights(c, nk, cout, kh * kw, cin));
+}
+
+// ... of a ConvTranspose with kernel == stride s: one 1 x 1 tap, row (ky*s + kx)*cout + co.
+void attach_tconv(Ctx *c, ConvTW &t, const HostW &w) {
+    const int s = t.s, N = t.cout * s * s;
+    std::vector<float> nk((size_t)N * t.cin);
+    for (int ci = 0; ci < t.cin; ci++)
+        for (int co = 0; co < t.cout; co++)
+            for (int ky = 0; ky < s; ky++)
+                for (int kx = 0; kx < s; kx++)
+                    nk[(size_t)((ky * s + kx) * t.cout + co) * t.cin + ci] =
+                        w.data[(((size_t)ci * t.cout + co) * t.kh + ky) * t.kw + kx];
+    t.tw = std::make_shared<k::TconvW>(k::make_tconv_weights(c, nk, N, 1, t.cin));
+}
+
 // =========================================================================================
 // tensor helpers
 // =========================================================================================
@@ -184,16 +209,134 @@ DT from_host(Ctx *c, const float *x, const std::vector<int64_t> &shape) {
 static DT view(const DT &x, std::vector<int64_t> shape, std::vector<int64_t> strides, int64_t offset = 0) {
     DT v;
     v.buf = x.buf;
-    v.p = x.p + offset;
+    v.p = x.split ? reinterpret_cast<float *>(reinterpret_cast<uint16_t *>(x.p) + offset) : x.p + offset;
     v.shape = std::move(shape);
     v.strides = std::move(strides);
+    v.split = x.split;
     return v;
+}
+
+static void strides4(const DT &t, int64_t (&s)[4]) {
+    for (int d = 0; d < 4; d++) s[d] = t.strides[d];
+}
+
+// x (any format, 4-D) into the same-shaped view y (any format).
+static void copy_any(Ctx *c, const DT &x, const DT &y) {
+    if (!x.split && !y.split) {
+        copy_into(c, x, y);
+        return;
+    }
+    int64_t xs[4], ys[4], dims[4] = {x.shape[0], x.shape[1], x.shape[2], x.shape[3]};
+    if (x.split && y.split) {
+        DT t = new_nhwc(c, x.shape[0], x.shape[1], x.shape[2], x.shape[3]);
+        copy_any(c, x, t);
+        copy_any(c, t, y);
+        return;
+    }
+    strides4(x, xs);
+    strides4(y, ys);
+    if (x.split)
+        k::unsplit(c, reinterpret_cast<const uint16_t *>(x.p), xs, x.strides[3] / 2, y.p, ys, dims);
+    else
+        k::resplit(c, x.p, xs, reinterpret_cast<uint16_t *>(y.p), ys, y.strides[3] / 2, dims);
+}
+
+DT to_f32(Ctx *c, const DT &x) {
+    if (!x.split) return x;
+    DT y = new_nhwc(c, x.shape[0], x.shape[1], x.shape[2], x.shape[3]);
+    copy_any(c, x, y);
+    return y;
+}
+
+// The output of a kernel that may or may not write split tensors: `y` is what it writes (the
+// step's own output when formats agree, else an fp32 temporary converted into it by done()).
+struct KOut {
+    DT y, target;
+    bool convert = false;
+};
+
+static KOut kout(Ctx *c, const OutAlloc *out, int64_t n, int64_t ch, int64_t h, int64_t w, bool kernel_splits) {
+    KOut o;
+    o.target = out ? (*out)(n, ch, h, w) : new_nhwc(c, n, ch, h, w);
+    if (o.target.split && !kernel_splits) {
+        o.y = new_nhwc(c, n, ch, h, w);
+        o.convert = true;
+    } else {
+        o.y = o.target;
+    }
+    return o;
+}
+
+static DT done(Ctx *c, const KOut &o) {
+    if (o.convert) copy_any(c, o.y, o.target);
+    return o.target;
 }
 
 // =========================================================================================
 // convolution runs
 // =========================================================================================
+// A convolution whose input is a split tensor: the tap convolution (stride 1, dense) or the
+// pointwise kernel; false when neither applies (the caller converts the input to fp32).
+static bool conv_split(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale,
+                       const OutAlloc *out, DT &y) {
+    if (res || scale || cw.kind != ConvW::DENSE || !x.nhwc()) return false;
+    int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
+    if (cw.cin != cin)
+        fail(WOCR_ERR_SHAPE, "Conv expects " + std::to_string(cw.cin) + " channels, has " + std::to_string(cin));
+    int pt, pl, pb, pr;
+    if (cw.same_upper) {
+        int64_t oh = (h + cw.sh - 1) / cw.sh, ow = (w + cw.sw - 1) / cw.sw;
+        int64_t th = std::max<int64_t>((oh - 1) * cw.sh + cw.kh - h, 0);
+        int64_t tw = std::max<int64_t>((ow - 1) * cw.sw + cw.kw - w, 0);
+        pt = (int)(th / 2), pl = (int)(tw / 2), pb = (int)(th - th / 2), pr = (int)(tw - tw / 2);
+    } else {
+        pt = cw.pads[0], pl = cw.pads[1], pb = cw.pads[2], pr = cw.pads[3];
+    }
+    if (h + pt + pb < cw.kh || w + pl + pr < cw.kw)
+        fail(WOCR_ERR_SHAPE, "conv input " + shape_str(x.shape) + " smaller than its kernel");
+    const uint16_t *xp = reinterpret_cast<const uint16_t *>(x.p);
+    if (cw.cout < 16 && cw.kh == 1 && cw.kw == 1 && cw.sh == 1 && cw.sw == 1 && pt == 0 && pl == 0 && pb == 0 &&
+        pr == 0 && cin <= 4096) {
+        KOut o = kout(c, out, n, cw.cout, h, w, false);
+        k::pointwise(c, xp, x.strides[0], x.pix(), h * w, (int)n, (int)cin, cw.w.p, cw.ldw, cw.b.p, cw.cout, act,
+                     o.y.p, o.y.strides[0], o.y.pix(), 1);
+        y = done(c, o);
+        return true;
+    }
+    if (!cw.tw || cw.sh != 1 || cw.sw != 1 || !k::tconv_input_ok(xp, x.strides[0], x.pix())) return false;
+    const int64_t oh = h + pt + pb - cw.kh + 1, ow = w + pl + pr - cw.kw + 1;
+    KOut o = kout(c, out, n, cw.cout, oh, ow, true);
+    k::TconvP p;
+    p.x = xp;
+    p.x_n = x.strides[0];
+    p.x_pix = x.pix();
+    p.n = (int)n;
+    p.h = (int)h;
+    p.w = (int)w;
+    p.cin = (int)cin;
+    p.kh = cw.kh;
+    p.kw = cw.kw;
+    p.pt = pt;
+    p.pl = pl;
+    p.oh = (int)oh;
+    p.ow = (int)ow;
+    p.bias = cw.b.p;
+    p.act = act;
+    p.y = o.y.p;
+    p.split_out = o.y.split;
+    p.y_n = o.y.strides[0];
+    p.y_pix = o.y.pix();
+    k::tconv(c, *cw.tw, p);
+    y = done(c, o);
+    return true;
+}
+
 DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale, const OutAlloc *out) {
+    if (xin.split) {
+        DT y;
+        if (conv_split(c, xin, cw, act, res, scale, out, y)) return y;
+        return conv_run(c, to_f32(c, xin), cw, act, res, scale, out);
+    }
     DT x = to_nhwc(c, xin);
     int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
     int pt, pl, pb, pr;
@@ -210,10 +353,12 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
         if (ch <= 0 || cwd <= 0) fail(WOCR_ERR_SHAPE, "conv input " + shape_str(x.shape) + " smaller than its kernel");
         if (cin != 1) fail(WOCR_ERR_SHAPE, "direct conv expects 1 channel, has " + std::to_string(cin));
         int64_t oh = ch / cw.pool_h, ow = cwd / cw.pool_w;
-        DT y = out ? (*out)(n, cw.cout, oh, ow) : new_nhwc(c, n, cw.cout, oh, ow);
+        const bool splits = (cw.cout == 16 || cw.cout == 32) && cw.kh * cw.kw <= 49;
+        KOut o = kout(c, out, n, cw.cout, oh, ow, splits);
         k::conv_direct(c, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, cw.w.p, cw.b.p, cw.cout, cw.kh, cw.kw,
-                       pt, act, cw.pool_h, cw.pool_w, y.p, y.strides[0], y.pix(), (int)oh, (int)ow);
-        return y;
+                       pt, act, cw.pool_h, cw.pool_w, o.y.p, o.y.strides[0], o.y.pix(), (int)oh, (int)ow,
+                       o.y.split ? 1 : 0);
+        return done(c, o);
     }
     if (h + pt + pb < cw.kh || w + pl + pr < cw.kw)
         fail(WOCR_ERR_SHAPE, "conv input " + shape_str(x.shape) + " smaller than its kernel");
@@ -225,13 +370,14 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
     if (scale && scale->numel() != n * cin)
         fail(WOCR_ERR_SHAPE, "input scale " + shape_str(scale->shape) + " for " + shape_str(x.shape));
     if ((res || scale) && cw.kind != ConvW::DENSE) fail(WOCR_ERR_UNSUPPORTED, "residual after a grouped conv");
-    DT y = out ? (*out)(n, cw.cout, oh, ow) : new_nhwc(c, n, cw.cout, oh, ow);
+    KOut o = kout(c, out, n, cw.cout, oh, ow, false);
+    const DT &y = o.y;
     if (cw.kind == ConvW::DEPTHWISE) {
         if (cin != cw.cout || cw.group != cin)
             fail(WOCR_ERR_UNSUPPORTED, "grouped conv with group " + std::to_string(cw.group));
         k::depthwise(c, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, (int)cin, cw.w.p, cw.b.p, cw.kh, cw.kw,
                      cw.sh, cw.sw, pt, pl, (int)oh, (int)ow, act, y.p, y.strides[0], y.pix());
-        return y;
+        return done(c, o);
     }
     if (cw.cin != cin)
         fail(WOCR_ERR_SHAPE, "Conv expects " + std::to_string(cw.cin) + " channels, has " + std::to_string(cin));
@@ -240,7 +386,7 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
         // too narrow for a tensor-core tile: a memory-bound pass over the pixels
         k::pointwise(c, x.p, x.strides[0], x.pix(), h * w, (int)n, (int)cin, cw.w.p, cw.ldw, cw.b.p, cw.cout, act, y.p,
                      y.strides[0], y.pix());
-        return y;
+        return done(c, o);
     }
     DT r, s;
     k::ConvP p;
@@ -308,19 +454,49 @@ DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, cons
         u.res_n = p.res_n;
         u.res_pix = p.res_pix;
         k::umma_gemm(c, *cw.uw, u);
-        return y;
+        return done(c, o);
     }
     k::conv_gemm(c, p);
-    return y;
+    return done(c, o);
 }
 
 static DT convt_run(Ctx *c, const DT &xin, const ConvTW &t, int act, const OutAlloc *out = nullptr) {
+    if (xin.split) {
+        const uint16_t *xp = reinterpret_cast<const uint16_t *>(xin.p);
+        if (!t.tw || !xin.nhwc() || !k::tconv_input_ok(xp, xin.strides[0], xin.pix()))
+            return convt_run(c, to_f32(c, xin), t, act, out);
+        int64_t n = xin.shape[0], cin = xin.shape[1], h = xin.shape[2], w = xin.shape[3];
+        if (cin != t.cin) fail(WOCR_ERR_SHAPE, "ConvTranspose expects " + std::to_string(t.cin) + " channels, has " +
+                                                   std::to_string(cin));
+        KOut o = kout(c, out, n, t.cout, h * t.s, w * t.s, true);
+        k::TconvP p;
+        p.x = xp;
+        p.x_n = xin.strides[0];
+        p.x_pix = xin.pix();
+        p.n = (int)n;
+        p.h = (int)h;
+        p.w = (int)w;
+        p.cin = (int)cin;
+        p.oh = (int)h;
+        p.ow = (int)w;
+        p.bias = t.b.p;
+        p.act = act;
+        p.y = o.y.p;
+        p.split_out = o.y.split;
+        p.y_n = o.y.strides[0];
+        p.y_pix = o.y.pix();
+        p.scatter = t.s;
+        p.scat_cout = t.cout;
+        k::tconv(c, *t.tw, p);
+        return done(c, o);
+    }
     DT x = to_nhwc(c, xin);
     int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
     if (cin != t.cin) fail(WOCR_ERR_SHAPE, "ConvTranspose expects " + std::to_string(t.cin) + " channels, has " +
                                                std::to_string(cin));
     int64_t oh = (h - 1) * t.s + t.kh, ow = (w - 1) * t.s + t.kw;
-    DT y = out ? (*out)(n, t.cout, oh, ow) : new_nhwc(c, n, t.cout, oh, ow);
+    KOut o = kout(c, out, n, t.cout, oh, ow, false);
+    const DT &y = o.y;
     if (t.gemm) {
         k::ConvP p;
         p.x = x.p;
@@ -372,7 +548,7 @@ static DT convt_run(Ctx *c, const DT &xin, const ConvTW &t, int act, const OutAl
         k::convt_gather(c, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, (int)cin, t.w.p, t.b.p, t.cout, t.kh,
                         t.kw, t.s, act, y.p, y.strides[0], y.pix(), (int)oh, (int)ow);
     }
-    return y;
+    return done(c, o);
 }
 
 DT linear_run(Ctx *c, const DT &xin, const DevW &w, const DevW &b, int K, int N, int ldw, int act,
@@ -444,10 +620,69 @@ Value Executor::get(std::map<std::string, Value> &vals, const std::string &name)
     fail(WOCR_ERR_MISSING, "missing value " + name);
 }
 
-DT Executor::getf(std::map<std::string, Value> &vals, const std::string &name) {
+DT Executor::getx(std::map<std::string, Value> &vals, const std::string &name) {
     Value v = get(vals, name);
     if (v.is_int) fail(WOCR_ERR_SHAPE, name + " is not float");
     return v.f;
+}
+
+DT Executor::getf(std::map<std::string, Value> &vals, const std::string &name) {
+    return to_f32(ctx, getx(vals, name));
+}
+
+// Which step outputs are stored split: those whose kernel can write them so (a Cin = 1 direct
+// conv, a tap convolution or tap ConvTranspose fed split, a MaxPool, Concat or Identity of split
+// values) and whose every reader takes them (tap convolutions, the pointwise head, MaxPool,
+// split Concats and Identities).  The graph output never is.  Fixed point from above.
+void Executor::plan_split() {
+    for (auto &st : steps) st.split_out = false;
+    if (!allow_split) return;
+    std::map<std::string, std::vector<int>> readers;
+    for (int i = 0; i < (int)steps.size(); i++)
+        for (auto &nm : steps[i].inputs) readers[nm].push_back(i);
+    auto pointwise_head = [](const ConvW &cw) {
+        return cw.kind == ConvW::DENSE && cw.cout < 16 && cw.kh == 1 && cw.kw == 1 && cw.sh == 1 && cw.sw == 1 &&
+               !cw.same_upper && cw.pads[0] == 0 && cw.pads[1] == 0 && cw.pads[2] == 0 && cw.pads[3] == 0;
+    };
+    std::set<std::string> sp;
+    for (auto &st : steps) {
+        bool capable = false;
+        switch (st.kind) {
+        case Step::G_DIRECT: capable = (st.conv.cout == 16 || st.conv.cout == 32) && st.conv.kh * st.conv.kw <= 49; break;
+        case Step::G_CONV: capable = (bool)st.conv.tw; break;
+        case Step::G_CONVT: capable = (bool)st.convt.tw; break;
+        case Step::G_MAXPOOL:
+        case Step::G_CONCAT:
+        case Step::G_IDENTITY: capable = true; break;
+        default: break;
+        }
+        if (capable && st.output != output && st.output != input) sp.insert(st.output);
+    }
+    auto accepts = [&](const Step &st) {
+        switch (st.kind) {
+        case Step::G_CONV: return (bool)st.conv.tw || pointwise_head(st.conv);
+        case Step::G_CONVT: return (bool)st.convt.tw;
+        case Step::G_MAXPOOL: return true;
+        case Step::G_CONCAT:
+        case Step::G_IDENTITY: return sp.count(st.output) > 0;
+        default: return false;
+        }
+    };
+    for (bool changed = true; changed;) {
+        changed = false;
+        for (auto &st : steps) {
+            if (!sp.count(st.output)) continue;
+            bool ok = true;
+            if (st.kind != Step::G_DIRECT)
+                for (auto &nm : st.inputs) ok = ok && sp.count(nm) > 0;
+            for (int r : readers[st.output]) ok = ok && accepts(steps[r]);
+            if (!ok) {
+                sp.erase(st.output);
+                changed = true;
+            }
+        }
+    }
+    for (auto &st : steps) st.split_out = sp.count(st.output) > 0;
 }
 
 void Executor::finalize() {
@@ -514,19 +749,21 @@ void Executor::finalize() {
             off += pp.second;
         }
     }
+    plan_split();
 }
 
 // The output of a step registered in concat_slot: a channel slice of the Concat buffer (made on
 // first use with the producing step's batch and spatial size).
-DT Executor::slot_output(const std::string &name, int64_t n, int64_t c, int64_t h, int64_t w) {
+DT Executor::slot_output(const std::string &name, int64_t n, int64_t c, int64_t h, int64_t w, bool split) {
+    auto fresh = [&](int64_t ch) { return split ? new_nhwc_split(ctx, n, ch, h, w) : new_nhwc(ctx, n, ch, h, w); };
     auto si = concat_slot.find(name);
-    if (si == concat_slot.end() || !cbufs) return new_nhwc(ctx, n, c, h, w);
+    if (si == concat_slot.end() || !cbufs) return fresh(c);
     const ConcatSlot &sl = si->second;
     auto bi = cbufs->find(sl.concat);
-    if (bi == cbufs->end()) bi = cbufs->emplace(sl.concat, new_nhwc(ctx, n, sl.ctot, h, w)).first;
+    if (bi == cbufs->end()) bi = cbufs->emplace(sl.concat, fresh(sl.ctot)).first;
     const DT &b = bi->second;
-    if (b.shape[0] != n || b.shape[2] != h || b.shape[3] != w || sl.offset + c > sl.ctot)
-        return new_nhwc(ctx, n, c, h, w);  // shapes differ: the Concat will copy this part
+    if (b.shape[0] != n || b.shape[2] != h || b.shape[3] != w || sl.offset + c > sl.ctot || b.split != split)
+        return fresh(c);  // shapes or formats differ: the Concat will copy this part
     return view(b, {n, c, h, w}, b.strides, sl.offset);
 }
 
@@ -551,12 +788,12 @@ DT Executor::run(const DT &x) {
     auto it = vals.find(output);
     if (it == vals.end()) fail(WOCR_ERR_MISSING, "graph output " + output + " not computed");
     if (it->second.is_int) fail(WOCR_ERR_SHAPE, "output " + output + " not computed");
-    return it->second.f;
+    return to_f32(ctx, it->second.f);
 }
 
 // Channel Concat of NHWC parts: parts already written into their slice of the registered
 // buffer are not copied again (src/gpu.rs:1317-1330 copies every part).
-DT Executor::concat_channels(const std::vector<DT> &parts, const std::string &out_name) {
+DT Executor::concat_channels(const std::vector<DT> &parts, const std::string &out_name, bool split) {
     const DT &a = parts[0];
     int64_t ctot = 0;
     for (auto &t : parts) ctot += t.shape[1];
@@ -569,11 +806,13 @@ DT Executor::concat_channels(const std::vector<DT> &parts, const std::string &ou
             reuse = true;
         }
     }
-    if (!reuse) y = new_nhwc(ctx, a.shape[0], ctot, a.shape[2], a.shape[3]);
+    if (!reuse)
+        y = split ? new_nhwc_split(ctx, a.shape[0], ctot, a.shape[2], a.shape[3])
+                  : new_nhwc(ctx, a.shape[0], ctot, a.shape[2], a.shape[3]);
     int64_t off = 0;
     for (auto &t : parts) {
         DT dst = view(y, t.shape, y.strides, off);
-        if (!(reuse && t.p == dst.p && t.strides == dst.strides)) copy_into(ctx, t, dst);
+        if (!(reuse && t.p == dst.p && t.strides == dst.strides && t.split == dst.split)) copy_any(ctx, t, dst);
         off += t.shape[1];
     }
     return y;
@@ -582,13 +821,13 @@ DT Executor::concat_channels(const std::vector<DT> &parts, const std::string &ou
 void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
     Value out;
     const OutAlloc alloc_out = [&](int64_t n, int64_t c, int64_t h, int64_t w) {
-        return slot_output(s.output, n, c, h, w);
+        return slot_output(s.output, n, c, h, w, s.split_out);
     };
     switch (s.kind) {
     case Step::G_CONV:
     case Step::G_DIRECT:
     case Step::G_DEPTHWISE:
-        out.f = conv_run(ctx, getf(vals, s.inputs[0]), s.conv, s.act, nullptr, nullptr, &alloc_out);
+        out.f = conv_run(ctx, getx(vals, s.inputs[0]), s.conv, s.act, nullptr, nullptr, &alloc_out);
         break;
     case Step::N_CONV: {
         DT r, sc;
@@ -608,25 +847,36 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
     }
     case Step::G_CONVT:
     case Step::N_CONVT: {
-        DT x = getf(vals, s.inputs[0]);
+        DT x = getx(vals, s.inputs[0]);
         if (x.rank() != 4) fail(WOCR_ERR_SHAPE, "ConvTranspose input " + shape_str(x.shape));
         out.f = convt_run(ctx, x, s.convt, s.act, &alloc_out);
         break;
     }
     case Step::G_MAXPOOL: {
-        DT x = to_nhwc(ctx, getf(vals, s.inputs[0]));
+        DT x = getx(vals, s.inputs[0]);
+        if (x.rank() != 4) fail(WOCR_ERR_SHAPE, "MaxPool input " + shape_str(x.shape));
+        if (x.split && !x.nhwc()) x = to_f32(ctx, x);
         int64_t n = x.shape[0], ch = x.shape[1], h = x.shape[2], w = x.shape[3];
         int kh = s.conv.kh, kw = s.conv.kw;
         int64_t oh = h / kh, ow = w / kw;
-        DT y = new_nhwc(ctx, n, ch, oh, ow);
+        if (x.split) {
+            DT y = s.split_out ? new_nhwc_split(ctx, n, ch, oh, ow) : new_nhwc(ctx, n, ch, oh, ow);
+            k::maxpool_split(ctx, reinterpret_cast<const uint16_t *>(x.p), x.strides[0], x.pix(), (int)n, (int)h,
+                             (int)w, (int)ch, kh, kw, (int)oh, (int)ow, y.p, y.strides[0], y.pix(), y.split ? 1 : 0);
+            out.f = y;
+            break;
+        }
+        x = to_nhwc(ctx, x);
+        KOut o = kout(ctx, nullptr, n, ch, oh, ow, false);
+        if (s.split_out) o.target = new_nhwc_split(ctx, n, ch, oh, ow), o.y = new_nhwc(ctx, n, ch, oh, ow), o.convert = true;
         k::pool(ctx, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, (int)ch, kh, kw, kh, kw, 0, 0, (int)oh,
-                (int)ow, 0, y.p, y.strides[0], y.pix());
-        out.f = y;
+                (int)ow, 0, o.y.p, o.y.strides[0], o.y.pix());
+        out.f = done(ctx, o);
         break;
     }
     case Step::G_SLICE: {
         // 4-D box (src/gpu.rs:1303-1315)
-        DT a = getf(vals, s.inputs[0]);
+        DT a = getx(vals, s.inputs[0]);
         if (a.rank() != 4) fail(WOCR_ERR_SHAPE, "Slice input " + shape_str(a.shape));
         std::vector<int64_t> lo(4, 0), shp = a.shape;
         for (size_t q = 0; q < s.starts.size() && q < s.ends.size() && q < s.axes.size(); q++) {
@@ -645,7 +895,7 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
     }
     case Step::G_CONCAT: {
         std::vector<DT> parts;
-        for (auto &nm : s.inputs) parts.push_back(getf(vals, nm));
+        for (auto &nm : s.inputs) parts.push_back(getx(vals, nm));
         DT a = parts[0];
         int64_t ctot = 0;
         for (auto &t : parts) {
@@ -656,7 +906,7 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
             }
             ctot += t.shape[1];
         }
-        out.f = concat_channels(parts, s.output);
+        out.f = concat_channels(parts, s.output, s.split_out);
         break;
     }
     case Step::G_ACT: {
@@ -953,7 +1203,7 @@ void Executor::exec_generic(const Node &n, std::map<std::string, Value> &vals) {
             if (nh) {
                 std::vector<DT> ts;
                 for (auto &p : parts) ts.push_back(p.f);
-                out.f = concat_channels(ts, n.outputs[0]);
+                out.f = concat_channels(ts, n.outputs[0], false);
                 vals[n.outputs[0]] = out;
                 return;
             }
@@ -1158,6 +1408,7 @@ std::unique_ptr<Executor> build_graph(Ctx *c, const Model &m, const char *stop, 
             }
             st.conv.sh = st.conv.sw = stride;
             for (int q = 0; q < 4; q++) st.conv.pads[q] = pad;
+            if (st.kind == Step::G_CONV && stride == 1 && cin_g >= 16 && use_umma()) attach_tconv(c, st.conv, w);
             st.act = fused;
         } else if (n.op == "ConvTranspose") {
             const HostW &w = m.weight(n.in(1));
@@ -1167,6 +1418,7 @@ std::unique_ptr<Executor> build_graph(Ctx *c, const Model &m, const char *stop, 
                 fail(WOCR_ERR_UNSUPPORTED, "unsupported ConvTranspose attributes");
             st.kind = Step::G_CONVT;
             st.convt = lower_convt(c, w, bias_or_zero(m, n, 2, (int)w.dims[1]), (int)symmetric(n, "strides", 1));
+            if (st.convt.gemm && st.convt.cin >= 16 && use_umma()) attach_tconv(c, st.convt, w);
             st.act = fused;
         } else if (n.op == "MaxPool") {
             auto kv = n.ints("kernel_shape");
@@ -1223,6 +1475,7 @@ std::unique_ptr<Executor> build_graph(Ctx *c, const Model &m, const char *stop, 
     }
     ex->input = m.input;
     ex->output = stopped ? sn.in(0) : m.output;
+    ex->allow_split = use_umma() && !std::getenv("WOCR_NO_SPLIT");
     if (stop_node && stopped) *stop_node = sn;
     if (stop && !stopped && stop_node) stop_node->op.clear();
     ex->finalize();

@@ -12,6 +12,7 @@
 #include "common.h"
 #include "kernels.h"
 #include "model.h"
+#include "tconv.h"
 #include "umma.h"
 
 namespace wocr {
@@ -35,6 +36,7 @@ struct ConvW {
     int ldw = 0;                 // DENSE: columns of the [K][ldw] weight matrix
     int pool_h = 1, pool_w = 1;  // DIRECT: fused MaxPool
     std::shared_ptr<k::UmmaW> uw;  // DENSE: the tensor-core operand (split bf16, TMA maps)
+    std::shared_ptr<k::TconvW> tw;  // DENSE, stride 1: the tap-convolution operand (split inputs)
 };
 
 // A lowered ConvTranspose: kernel == stride runs as one GEMM with a scatter epilogue.
@@ -43,10 +45,15 @@ struct ConvTW {
     int cin = 0, cout = 0, kh = 0, kw = 0, s = 1, ldw = 0;
     bool gemm = false;
     std::shared_ptr<k::UmmaW> uw;  // gemm: the tensor-core operand
+    std::shared_ptr<k::TconvW> tw;  // gemm: the tap-convolution operand (split inputs)
 };
 
 ConvW lower_conv_dense(Ctx *c, const HostW &w, const std::vector<float> &bias, int group);
 ConvTW lower_convt(Ctx *c, const HostW &w, const std::vector<float> &bias, int stride);
+// Tap-convolution operands (split inputs): a stride-1 dense convolution, a kernel == stride
+// ConvTranspose.
+void attach_tconv(Ctx *c, ConvW &cw, const HostW &w);
+void attach_tconv(Ctx *c, ConvTW &t, const HostW &w);
 
 // A value while a graph runs: a device float tensor or a host integer tensor (src/nd.rs:448).
 struct Value {
@@ -78,6 +85,7 @@ struct Step {
     int ln_len = 0;
     float eps = 1e-5f;
     std::vector<int64_t> starts, ends, axes;  // G_SLICE
+    bool split_out = false;               // the output is stored as a split tensor
 };
 
 class Executor {
@@ -94,6 +102,9 @@ class Executor {
     };
     std::map<std::string, ConcatSlot> concat_slot;
     std::map<std::string, DT> *cbufs = nullptr;  // Concat buffers of the current run
+    // Values between the convolutional steps of a Graph may be stored split (bf16 hi | lo, as
+    // the tap convolution reads them); plan_split() marks the steps whose output is.
+    bool allow_split = false;
 
     explicit Executor(Ctx *c) : ctx(c) {}
     // Run on `x`; returns the output tensor.
@@ -101,10 +112,12 @@ class Executor {
     void finalize();  // uploads generic weights, computes last uses
 
   protected:
-    DT slot_output(const std::string &name, int64_t n, int64_t c, int64_t h, int64_t w);
-    DT concat_channels(const std::vector<DT> &parts, const std::string &out_name);
+    void plan_split();
+    DT slot_output(const std::string &name, int64_t n, int64_t c, int64_t h, int64_t w, bool split);
+    DT concat_channels(const std::vector<DT> &parts, const std::string &out_name, bool split);
     Value get(std::map<std::string, Value> &vals, const std::string &name);
-    DT getf(std::map<std::string, Value> &vals, const std::string &name);
+    DT getf(std::map<std::string, Value> &vals, const std::string &name);  // fp32 (converts split)
+    DT getx(std::map<std::string, Value> &vals, const std::string &name);  // as stored
     void exec_step(const Step &s, std::map<std::string, Value> &vals);
     void exec_generic(const Node &n, std::map<std::string, Value> &vals);
 };
@@ -117,6 +130,7 @@ std::unique_ptr<Executor> build_ndgraph(Ctx *c, const Model &m, bool stop_before
 
 // Helpers shared with the API layer.
 DT to_nhwc(Ctx *c, const DT &x);
+DT to_f32(Ctx *c, const DT &x);  // a split tensor as fp32 NHWC; others unchanged
 DT to_rowmajor(Ctx *c, const DT &x);
 using OutAlloc = std::function<DT(int64_t n, int64_t c, int64_t h, int64_t w)>;
 DT conv_run(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale,

@@ -1,6 +1,7 @@
 // Convolution family on channels-last tensors: implicit-GEMM dense conv / linear / strided
 // ConvTranspose (CUDA-core fp32 path), Cin = 1 direct conv with fused MaxPool, depthwise conv,
 // general ConvTranspose.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <type_traits>
@@ -165,11 +166,37 @@ __global__ void __launch_bounds__(256) k_conv_gemm(ConvP p) {
 
 // ---------------------------------------------------------------------------------------
 // Cin = 1 direct conv: one thread per output pixel (after the fused pool), all channels.
-template <int COUT>
+// Split activations (bf16 hi = bf16(v), lo = bf16(v - hi)) as the tap-convolution kernel reads them.
+__device__ __forceinline__ void split1(float v, uint16_t &h, uint16_t &l) {
+    __nv_bfloat16 hb = __float2bfloat16_rn(v);
+    __nv_bfloat16 lb = __float2bfloat16_rn(v - __bfloat162float(hb));
+    h = *reinterpret_cast<uint16_t *>(&hb);
+    l = *reinterpret_cast<uint16_t *>(&lb);
+}
+
+__device__ __forceinline__ void split8v(const float *v, uint4 &hi, uint4 &lo) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        uint16_t h0, l0, h1, l1;
+        split1(v[2 * i], h0, l0);
+        split1(v[2 * i + 1], h1, l1);
+        hw[i] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        lw[i] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+    }
+    hi = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    lo = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
+
+__device__ __forceinline__ float unsplit1(const uint16_t *hp, int64_t lo_off) {
+    return __uint_as_float((uint32_t)hp[0] << 16) + __uint_as_float((uint32_t)hp[lo_off] << 16);
+}
+
+template <int COUT, int SPLIT>
 __global__ void k_conv_direct(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int n, int h, int w,
                               const float *__restrict__ wt, const float *__restrict__ bias, int kh, int kw, int pad,
-                              int act, int ph, int pw, float *__restrict__ y, int64_t y_n, int64_t y_pix, int oh,
-                              int ow) {
+                              int act, int ph, int pw, void *__restrict__ yv, int64_t y_n, int64_t y_pix, int oh,
+                              int ow, int vec) {
     __shared__ float ws[7 * 7 * COUT];
     __shared__ float bs[COUT];
     for (int i = threadIdx.x; i < kh * kw * COUT; i += blockDim.x) ws[i] = wt[i];
@@ -205,9 +232,27 @@ __global__ void k_conv_direct(const float *__restrict__ x, int64_t x_n, int64_t 
 #pragma unroll
                 for (int c = 0; c < COUT; c++) best[c] = fmaxf(best[c], act_f(acc[c], act));
             }
-        float *yo = y + nb * y_n + ((int64_t)oy * ow + ox) * y_pix;
+        const int64_t off = nb * y_n + ((int64_t)oy * ow + ox) * y_pix;
+        if (SPLIT) {
+            // split activations: bf16 hi parts of the pixel's channels, lo parts y_pix / 2 later
+            uint16_t *yo = reinterpret_cast<uint16_t *>(yv) + off;
+            if (vec) {
 #pragma unroll
-        for (int c = 0; c < COUT; c++) yo[c] = best[c];
+                for (int c = 0; c < COUT; c += 8) {
+                    uint4 hi, lo;
+                    split8v(best + c, hi, lo);
+                    *reinterpret_cast<uint4 *>(yo + c) = hi;
+                    *reinterpret_cast<uint4 *>(yo + y_pix / 2 + c) = lo;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < COUT; c++) split1(best[c], yo[c], yo[y_pix / 2 + c]);
+            }
+        } else {
+            float *yo = reinterpret_cast<float *>(yv) + off;
+#pragma unroll
+            for (int c = 0; c < COUT; c++) yo[c] = best[c];
+        }
     }
 }
 
@@ -321,8 +366,8 @@ __global__ void k_convt_gather(const float *__restrict__ x, int64_t x_n, int64_t
 // 1 x 1 convolution with few output channels (< 16, e.g. a detector head): memory-bound, one
 // thread per pixel, weights [cin][cout] in shared memory.  The tensor-core tile would be mostly
 // empty for such an N.
-template <int COUT, bool VEC>
-__global__ void k_pointwise(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin,
+template <int COUT, bool VEC, bool SPLIT_IN>
+__global__ void k_pointwise(const void *__restrict__ xv, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin,
                             const float *__restrict__ wt, int ldw, const float *__restrict__ bias, int cout, int act,
                             float *__restrict__ y, int64_t y_n, int64_t y_pix) {
     extern __shared__ float ws[];  // [cin][COUT]
@@ -334,11 +379,36 @@ __global__ void k_pointwise(const float *__restrict__ x, int64_t x_n, int64_t x_
     const int64_t total = (int64_t)n * hw;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t nb = i / hw, pix = i - nb * hw;
-        const float *xp = x + nb * x_n + pix * x_pix;
         float acc[COUT];
 #pragma unroll
         for (int co = 0; co < COUT; co++) acc[co] = co < cout ? bias[co] : 0.f;
-        if (VEC) {
+        if (SPLIT_IN) {
+            const uint16_t *xp = reinterpret_cast<const uint16_t *>(xv) + nb * x_n + pix * x_pix;
+            const int64_t lo = x_pix / 2;
+            if (VEC) {
+                for (int ci = 0; ci < cin; ci += 8) {
+                    uint4 h = __ldg(reinterpret_cast<const uint4 *>(xp + ci));
+                    uint4 l = __ldg(reinterpret_cast<const uint4 *>(xp + lo + ci));
+                    const uint32_t hw4[4] = {h.x, h.y, h.z, h.w}, lw4[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const uint32_t hb = (hw4[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+                        const uint32_t lb = (lw4[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+                        const float v = __uint_as_float(hb << 16) + __uint_as_float(lb << 16);
+                        const float *w0 = ws + (ci + e) * COUT;
+#pragma unroll
+                        for (int co = 0; co < COUT; co++) acc[co] += v * w0[co];
+                    }
+                }
+            } else {
+                for (int ci = 0; ci < cin; ci++) {
+                    float v = unsplit1(xp + ci, lo);
+#pragma unroll
+                    for (int co = 0; co < COUT; co++) acc[co] += v * ws[ci * COUT + co];
+                }
+            }
+        } else if (VEC) {
+            const float *xp = reinterpret_cast<const float *>(xv) + nb * x_n + pix * x_pix;
             for (int ci = 0; ci < cin; ci += 4) {
                 float4 v = __ldg(reinterpret_cast<const float4 *>(xp + ci));
                 const float *w0 = ws + ci * COUT;
@@ -347,6 +417,7 @@ __global__ void k_pointwise(const float *__restrict__ x, int64_t x_n, int64_t x_
                     acc[co] += v.x * w0[co] + v.y * w0[COUT + co] + v.z * w0[2 * COUT + co] + v.w * w0[3 * COUT + co];
             }
         } else {
+            const float *xp = reinterpret_cast<const float *>(xv) + nb * x_n + pix * x_pix;
             for (int ci = 0; ci < cin; ci++) {
                 float v = xp[ci];
 #pragma unroll
@@ -384,22 +455,30 @@ void conv_gemm(Ctx *c, const ConvP &p) {
     c->flops += 2.0 * (double)M * p.cout * p.kh * p.kw * p.cin;
 }
 
-void pointwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin, const float *wt, int ldw,
-               const float *bias, int cout, int act, float *y, int64_t y_n, int64_t y_pix) {
+void pointwise(Ctx *c, const void *x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin, const float *wt, int ldw,
+               const float *bias, int cout, int act, float *y, int64_t y_n, int64_t y_pix, int split_in) {
     const int64_t total = (int64_t)n * hw;
     if (total == 0) return;
     Prof pf(c, "pointwise", 2.0 * (double)total * cin * cout, 4.0 * (double)total * (cin + cout));
-    const bool vec = cin % 4 == 0 && x_pix % 4 == 0 && x_n % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const bool al = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    const bool vec = split_in ? (al && cin % 8 == 0 && x_pix % 16 == 0 && x_n % 8 == 0)
+                              : (al && cin % 4 == 0 && x_pix % 4 == 0 && x_n % 4 == 0);
     const int grid = grid_for(c, total);
     auto go = [&](auto cout_tag) {
         constexpr int CO = decltype(cout_tag)::value;
         const size_t smem = sizeof(float) * cin * CO;
-        if (vec)
-            k_pointwise<CO, true><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias, cout, act,
-                                                                   y, y_n, y_pix);
+        if (split_in && vec)
+            k_pointwise<CO, true, true><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias, cout,
+                                                                         act, y, y_n, y_pix);
+        else if (split_in)
+            k_pointwise<CO, false, true><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias, cout,
+                                                                          act, y, y_n, y_pix);
+        else if (vec)
+            k_pointwise<CO, true, false><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias, cout,
+                                                                          act, y, y_n, y_pix);
         else
-            k_pointwise<CO, false><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias, cout, act,
-                                                                    y, y_n, y_pix);
+            k_pointwise<CO, false, false><<<grid, 256, smem, c->stream>>>(x, x_n, x_pix, hw, n, cin, wt, ldw, bias,
+                                                                           cout, act, y, y_n, y_pix);
     };
     if (cout <= 1) go(std::integral_constant<int, 1>());
     else if (cout <= 2) go(std::integral_constant<int, 2>());
@@ -411,20 +490,27 @@ void pointwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int64_t hw, i
 }
 
 void conv_direct(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, const float *wt,
-                 const float *bias, int cout, int kh, int kw, int pad, int act, int ph, int pw, float *y,
-                 int64_t y_n, int64_t y_pix, int oh, int ow) {
+                 const float *bias, int cout, int kh, int kw, int pad, int act, int ph, int pw, void *yv,
+                 int64_t y_n, int64_t y_pix, int oh, int ow, int split_out) {
     int64_t pix = (int64_t)n * oh * ow;
     if (pix == 0) return;
     Prof pf(c, "conv_direct", 2.0 * (double)pix * ph * pw * cout * kh * kw,
             4.0 * ((double)n * h * w + (double)pix * cout));
     if (kh * kw <= 49 && (cout == 16 || cout == 32)) {
-        if (cout == 16)
-            k_conv_direct<16><<<grid_for(c, pix), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, kh, kw, pad,
-                                                                       act, ph, pw, y, y_n, y_pix, oh, ow);
-        else
-            k_conv_direct<32><<<grid_for(c, pix), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, kh, kw, pad,
-                                                                       act, ph, pw, y, y_n, y_pix, oh, ow);
+        const int vec = (reinterpret_cast<uintptr_t>(yv) & 15) == 0 && y_pix % 16 == 0 && y_n % 8 == 0;
+        auto go = [&](auto co_tag, auto split_tag) {
+            constexpr int CO = decltype(co_tag)::value, SP = decltype(split_tag)::value;
+            k_conv_direct<CO, SP><<<grid_for(c, pix), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, kh, kw,
+                                                                           pad, act, ph, pw, yv, y_n, y_pix, oh, ow,
+                                                                           vec);
+        };
+        if (cout == 16 && split_out) go(std::integral_constant<int, 16>(), std::integral_constant<int, 1>());
+        else if (cout == 16) go(std::integral_constant<int, 16>(), std::integral_constant<int, 0>());
+        else if (split_out) go(std::integral_constant<int, 32>(), std::integral_constant<int, 1>());
+        else go(std::integral_constant<int, 32>(), std::integral_constant<int, 0>());
     } else {
+        if (split_out) fail(WOCR_ERR_UNSUPPORTED, "split output of a direct conv with " + std::to_string(cout) + " channels");
+        float *y = reinterpret_cast<float *>(yv);
         k_conv_direct_any<<<grid_for(c, pix * cout), 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, cout, kh,
                                                                           kw, pad, act, ph, pw, y, y_n, y_pix, oh, ow);
     }

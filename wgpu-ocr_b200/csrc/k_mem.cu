@@ -1,6 +1,7 @@
 // Memory-bound kernels of the hot path: page pre/post-processing, pooling, elementwise,
 // row reductions.  Channels-last (NHWC) for 4-D image tensors; vectorised where the layout
 // allows.  Grid sizes are multiples of the SM count with grid-stride loops.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -160,6 +161,133 @@ __global__ void k_pool(const float *__restrict__ x, int64_t x_n, int64_t x_pix, 
             }
         }
         y[nb * y_n + ((int64_t)oy * ow + ox) * y_pix + c] = avg ? s / fmaxf(cnt, 1.f) : m;
+    }
+}
+
+// ---- split activations -------------------------------------------------------------------
+__device__ __forceinline__ float bf_f(uint32_t b) { return __uint_as_float(b << 16); }
+
+__device__ __forceinline__ void split_f(float v, uint16_t &h, uint16_t &l) {
+    __nv_bfloat16 hb = __float2bfloat16_rn(v);
+    __nv_bfloat16 lb = __float2bfloat16_rn(v - __bfloat162float(hb));
+    h = *reinterpret_cast<uint16_t *>(&hb);
+    l = *reinterpret_cast<uint16_t *>(&lb);
+}
+
+// One thread per (output pixel, 8 channels) when VEC (16-byte aligned hi / lo vectors), else per
+// channel.  The maximum is taken over hi + lo; its hi and lo parts are copied unchanged.
+template <bool VEC>
+__global__ void k_maxpool_split(const uint16_t *__restrict__ x, int64_t x_n, int64_t x_pix, int n, int h, int w,
+                                int ch, int kh, int kw, int oh, int ow, void *__restrict__ y, int64_t y_n,
+                                int64_t y_pix, int split_out) {
+    const int cv = VEC ? ch / 8 : ch;
+    const int64_t total = (int64_t)n * oh * ow * cv;
+    const int64_t xlo = x_pix / 2, ylo = y_pix / 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int cq = (int)(i % cv);
+        const int64_t pix = i / cv;
+        const int ox = (int)(pix % ow);
+        const int oy = (int)((pix / ow) % oh);
+        const int nb = (int)(pix / ((int64_t)ow * oh));
+        const uint16_t *xb = x + nb * x_n;
+        const int64_t yoff = nb * y_n + ((int64_t)oy * ow + ox) * y_pix;
+        if (VEC) {
+            const int c = cq * 8;
+            float best[8];
+            uint32_t bh[8], bl[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                best[e] = -3.4e38f;
+                bh[e] = bl[e] = 0;
+            }
+            for (int ky = 0; ky < kh; ky++)
+                for (int kx = 0; kx < kw; kx++) {
+                    const int iy = oy * kh + ky, ix = ox * kw + kx;
+                    if (iy >= h || ix >= w) continue;
+                    const uint16_t *src = xb + ((int64_t)iy * w + ix) * x_pix + c;
+                    const uint4 hv = *reinterpret_cast<const uint4 *>(src);
+                    const uint4 lv = *reinterpret_cast<const uint4 *>(src + xlo);
+                    const uint32_t hw4[4] = {hv.x, hv.y, hv.z, hv.w}, lw4[4] = {lv.x, lv.y, lv.z, lv.w};
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        const uint32_t hb = (hw4[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+                        const uint32_t lb = (lw4[e >> 1] >> ((e & 1) * 16)) & 0xffffu;
+                        const float v = bf_f(hb) + bf_f(lb);
+                        if (v > best[e]) {
+                            best[e] = v;
+                            bh[e] = hb;
+                            bl[e] = lb;
+                        }
+                    }
+                }
+            if (split_out) {
+                uint16_t *yo = reinterpret_cast<uint16_t *>(y) + yoff + c;
+                *reinterpret_cast<uint4 *>(yo) = make_uint4(bh[0] | bh[1] << 16, bh[2] | bh[3] << 16,
+                                                            bh[4] | bh[5] << 16, bh[6] | bh[7] << 16);
+                *reinterpret_cast<uint4 *>(yo + ylo) = make_uint4(bl[0] | bl[1] << 16, bl[2] | bl[3] << 16,
+                                                                  bl[4] | bl[5] << 16, bl[6] | bl[7] << 16);
+            } else {
+                float *yo = reinterpret_cast<float *>(y) + yoff + c;
+#pragma unroll
+                for (int e = 0; e < 8; e++) yo[e] = best[e];
+            }
+        } else {
+            const int c = cq;
+            float best = -3.4e38f;
+            uint16_t bh = 0, bl = 0;
+            for (int ky = 0; ky < kh; ky++)
+                for (int kx = 0; kx < kw; kx++) {
+                    const int iy = oy * kh + ky, ix = ox * kw + kx;
+                    if (iy >= h || ix >= w) continue;
+                    const uint16_t *src = xb + ((int64_t)iy * w + ix) * x_pix + c;
+                    const float v = bf_f(src[0]) + bf_f(src[xlo]);
+                    if (v > best) {
+                        best = v;
+                        bh = src[0];
+                        bl = src[xlo];
+                    }
+                }
+            if (split_out) {
+                uint16_t *yo = reinterpret_cast<uint16_t *>(y) + yoff + c;
+                yo[0] = bh;
+                yo[ylo] = bl;
+            } else {
+                reinterpret_cast<float *>(y)[yoff + c] = best;
+            }
+        }
+    }
+}
+
+struct Dims4 {
+    int64_t d[4], xs[4], ys[4];
+};
+
+__device__ __forceinline__ void index4(const Dims4 &g, int64_t i, int64_t &xo, int64_t &yo) {
+    xo = yo = 0;
+#pragma unroll
+    for (int k = 3; k >= 0; k--) {
+        const int64_t q = i % g.d[k];
+        i /= g.d[k];
+        xo += q * g.xs[k];
+        yo += q * g.ys[k];
+    }
+}
+
+__global__ void k_unsplit(const uint16_t *__restrict__ x, int64_t lo_off, float *__restrict__ y, Dims4 g,
+                          int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t xo, yo;
+        index4(g, i, xo, yo);
+        y[yo] = bf_f(x[xo]) + bf_f(x[xo + lo_off]);
+    }
+}
+
+__global__ void k_resplit(const float *__restrict__ x, uint16_t *__restrict__ y, int64_t lo_off, Dims4 g,
+                          int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t xo, yo;
+        index4(g, i, xo, yo);
+        split_f(x[xo], y[yo], y[yo + lo_off]);
     }
 }
 
@@ -463,6 +591,55 @@ void pool(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int 
     int64_t total = (int64_t)n * oh * ow * ch;
     k_pool<<<grid_for(c, total), kThreads, 0, c->stream>>>(x, x_n, x_pix, n, h, w, ch, kh, kw, sh, sw, pt, pl, oh, ow,
                                                           avg, y, y_n, y_pix);
+    WOCR_LAUNCHED(c);
+}
+
+void maxpool_split(Ctx *c, const uint16_t *x, int64_t x_n, int64_t x_pix, int n, int h, int w, int ch, int kh, int kw,
+                   int oh, int ow, void *y, int64_t y_n, int64_t y_pix, int split_out) {
+    Prof pf(c, "maxpool_split", 0, 4.0 * n * ch * ((double)h * w + (double)oh * ow));
+    const bool al = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+    const bool vec = al && ch % 8 == 0 && x_pix % 16 == 0 && x_n % 8 == 0 &&
+                     (split_out ? (y_pix % 16 == 0 && y_n % 8 == 0) : true);
+    const int64_t total = (int64_t)n * oh * ow * (vec ? ch / 8 : ch);
+    if (total == 0) return;
+    if (vec)
+        k_maxpool_split<true><<<grid_for(c, total), kThreads, 0, c->stream>>>(x, x_n, x_pix, n, h, w, ch, kh, kw, oh,
+                                                                              ow, y, y_n, y_pix, split_out);
+    else
+        k_maxpool_split<false><<<grid_for(c, total), kThreads, 0, c->stream>>>(x, x_n, x_pix, n, h, w, ch, kh, kw, oh,
+                                                                               ow, y, y_n, y_pix, split_out);
+    WOCR_LAUNCHED(c);
+}
+
+void unsplit(Ctx *c, const uint16_t *x, const int64_t (&xs)[4], int64_t lo_off, float *y, const int64_t (&ys)[4],
+             const int64_t (&dims)[4]) {
+    Dims4 g;
+    int64_t total = 1;
+    for (int k = 0; k < 4; k++) {
+        g.d[k] = dims[k];
+        g.xs[k] = xs[k];
+        g.ys[k] = ys[k];
+        total *= dims[k];
+    }
+    if (total == 0) return;
+    Prof pf(c, "unsplit", 0, 8.0 * total);
+    k_unsplit<<<grid_for(c, total), kThreads, 0, c->stream>>>(x, lo_off, y, g, total);
+    WOCR_LAUNCHED(c);
+}
+
+void resplit(Ctx *c, const float *x, const int64_t (&xs)[4], uint16_t *y, const int64_t (&ys)[4], int64_t lo_off,
+             const int64_t (&dims)[4]) {
+    Dims4 g;
+    int64_t total = 1;
+    for (int k = 0; k < 4; k++) {
+        g.d[k] = dims[k];
+        g.xs[k] = xs[k];
+        g.ys[k] = ys[k];
+        total *= dims[k];
+    }
+    if (total == 0) return;
+    Prof pf(c, "resplit", 0, 8.0 * total);
+    k_resplit<<<grid_for(c, total), kThreads, 0, c->stream>>>(x, y, lo_off, g, total);
     WOCR_LAUNCHED(c);
 }
 

@@ -1,0 +1,627 @@
+// Tap convolution: a stride-1 convolution (or a ConvTranspose with kernel == stride, as a 1 x 1
+// GEMM with a scatter epilogue) on tcgen05 tensor cores, for activations stored split: bf16 hi |
+// lo parts written so by the producing kernel's epilogue, so filling the A operand is a plain
+// copy.  A tile is 128 output pixels, 16 image rows of 8; its input is loaded ONCE as a halo of
+// (16 + kh - 1) x (8 + kw - 1) pixels per cg-channel chunk (cg = 16 or 32), coalesced 16-byte
+// cp.async copies into 8-channel planes (pixel p of a plane at 16 p bytes, zeros outside the
+// image).  That is the tensor cores' unswizzled K-major layout: every tap (ky, kx) of the kernel
+// is the same halo seen from another start address, (ky * halo_width + kx) * 16 bytes further,
+// with the 8-row groups (the tile's image rows) one halo row apart.  So the halo is read once
+// for all taps instead of once per tap.
+//   B hi, B lo: the tap's chunk of the pre-split weights for bn output channels (128-byte or
+//               smaller swizzle), by TMA, resident for the whole kernel when it fits, else
+//               through a ring of per-tap stages.
+// Per tap the MMA thread issues hi.hi + hi.lo + lo.hi per 16-channel step (fp32-accurate
+// products, as in k_umma.cu) into tensor memory.  Reference kernels: the implicit-GEMM
+// convolution K1-K4 (src/gpu.rs:37-350) and the ConvTranspose K7 (src/gpu.rs:424-460).
+//
+// Warp roles (448 threads, one CTA per SM, persistent over tiles):
+//   warps 0-3   halo producers (cp.async, up to kLagMax stages in flight per thread);
+//   warps 4-11  epilogue: tcgen05.ld (lane quadrant warp % 4, column half), bias, activation,
+//               split (or fp32) stores, plain or ConvTranspose scatter;
+//   warp 12     B by TMA;
+//   warp 13     tensor-memory allocation and MMA issue.
+// Every wait is bounded; on expiry the kernel records an error code, drains its own copies and
+// MMAs, frees its tensor memory and returns.
+#include "kernels.h"
+#include "tc.h"
+#include "tconv.h"
+
+#include <algorithm>
+
+namespace wocr {
+namespace k {
+
+namespace {
+
+using namespace tc;
+
+constexpr int kProd = 4, kEpi0 = 4, kEpiWarps = 8, kTmaW = 12, kMmaW = 13, kThreads = 448;
+constexpr int kLagMax = 4;        // cp.async stages in flight per producer thread
+constexpr int kSmemBudget = 220 * 1024;
+constexpr int TP = 8, TR = 16;    // tile: TR image rows of TP pixels (an 8-row group per image row)
+
+struct TcP {
+    const uint16_t *x;
+    int64_t x_n, x_pix;
+    int h, w, cin;
+    int n, oh, ow;              // GEMM output grid (ConvTranspose: its input grid)
+    int tiles_x, tiles_y, ntn;
+    int64_t ntiles;
+    int N, nchunk, taps, kw, pt, pl, cin_pad;
+    int two_acc;                // the tile's MMAs alternate between two accumulators
+    int hw_w, halo_px;          // halo row length and pixel count
+    uint32_t plane, a_stage;    // bytes of one 8-channel halo plane, of one A stage
+    int SA, SB, lag, b_res;     // A stages, B ring stages, cp.async stages in flight, B resident
+    uint32_t b_off, bar_off;    // shared-memory offsets of the B region and the barriers
+    const float *bias;
+    int act;
+    void *y;
+    int split_out, out_vec;
+    int64_t y_n, y_pix;
+    int ow_out;                 // pixels per output row
+    int scatter, scat_cout;
+    int *status;
+};
+
+struct Tile {
+    int nb, oy0, ox0, nt;
+};
+
+__device__ __forceinline__ Tile decode(const TcP &p, int64_t t) {
+    Tile r;
+    r.nt = (int)(t % p.ntn);
+    int64_t sp = t / p.ntn;
+    const int tx = (int)(sp % p.tiles_x);
+    sp /= p.tiles_x;
+    const int ty = (int)(sp % p.tiles_y);
+    r.nb = (int)(sp / p.tiles_y);
+    r.oy0 = ty * TR;
+    r.ox0 = tx * TP;
+    return r;
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait(int n) {
+    switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+    }
+}
+
+// 16 fp32 values -> bf16 hi and lo parts, 8 per uint4
+__device__ __forceinline__ void split16(const float (&v)[16], uint4 (&hi)[2], uint4 (&lo)[2]) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) t[j] = v[8 * h + j];
+        split8(t, hi[h], lo[h]);
+    }
+}
+
+__device__ __forceinline__ void store1(const TcP &p, int64_t off, float o) {
+    if (p.split_out) {
+        uint16_t *y = reinterpret_cast<uint16_t *>(p.y);
+        __nv_bfloat16 h = __float2bfloat16_rn(o);
+        __nv_bfloat16 l = __float2bfloat16_rn(o - __bfloat162float(h));
+        y[off] = *reinterpret_cast<uint16_t *>(&h);
+        y[off + p.y_pix / 2] = *reinterpret_cast<uint16_t *>(&l);
+    } else {
+        reinterpret_cast<float *>(p.y)[off] = o;
+    }
+}
+
+// 16 consecutive channels at element offset `off` (all valid)
+__device__ __forceinline__ void store16(const TcP &p, int64_t off, const float (&v)[16]) {
+    if (p.split_out) {
+        uint16_t *y = reinterpret_cast<uint16_t *>(p.y);
+        if (p.out_vec) {
+            uint4 hi[2], lo[2];
+            split16(v, hi, lo);
+            uint4 *dh = reinterpret_cast<uint4 *>(y + off);
+            uint4 *dl = reinterpret_cast<uint4 *>(y + off + p.y_pix / 2);
+            dh[0] = hi[0];
+            dh[1] = hi[1];
+            dl[0] = lo[0];
+            dl[1] = lo[1];
+            return;
+        }
+    } else if (p.out_vec) {
+        float4 *d4 = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.y) + off);
+#pragma unroll
+        for (int j = 0; j < 4; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j++) store1(p, off + j, v[j]);
+}
+
+template <int BN, int CG>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_tconv(const __grid_constant__ CUtensorMap wb_hi, const __grid_constant__ CUtensorMap wb_lo, TcP p) {
+    constexpr int RB = CG * 2;                 // bytes of one B row
+    constexpr uint32_t B_BYTES = BN * RB;      // B hi (or lo) of one tap chunk
+    constexpr int NPL = CG / 8;                // 8-channel planes per split part
+    constexpr int PPP = 2 * NPL;               // 16-byte pieces per halo pixel
+    constexpr int PXS = kProd * 32 / PPP;      // halo pixels per pass of the producer threads
+    // accumulator buffers in tensor memory: NACC tiles of two BN-column accumulators each (the MMAs
+    // after a commit inside a tile go to the other one, so they never wait on the committed ones)
+    constexpr int TCOLS = 2 * BN;
+    constexpr int NACC = 512 / TCOLS < 8 ? 512 / TCOLS : 8;
+    constexpr uint32_t kCols = NACC * TCOLS <= 32 ? 32 : (NACC * TCOLS <= 64 ? 64 : (NACC * TCOLS <= 128 ? 128 : (NACC * TCOLS <= 256 ? 256 : 512)));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int SA = p.SA, SB = p.SB;
+    uint8_t *bsm = smem + p.b_off;
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + p.bar_off);
+    uint64_t *emptyA = fullA + SA;
+    uint64_t *fullB = emptyA + SA;
+    uint64_t *emptyB = fullB + SB;
+    uint64_t *tfull = emptyB + SB;
+    uint64_t *tempty = tfull + NACC;
+    uint64_t *drain = tempty + NACC;
+    uint64_t *bres = drain + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bres + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SA; s++) {
+            mbar_init(&fullA[s], kProd);
+            mbar_init(&emptyA[s], 1);
+        }
+        for (int s = 0; s < SB; s++) {
+            mbar_init(&fullB[s], 1);
+            mbar_init(&emptyB[s], 1);
+        }
+        for (int a = 0; a < NACC; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        mbar_init(bres, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp == kMmaW) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp < kProd) {
+        // ---------------- halo producers ----------------
+        // thread: piece (split part, plane) of every PXS-th halo pixel, consecutive threads on
+        // consecutive 16-byte pieces of a pixel (coalesced)
+        const int piece = threadIdx.x % PPP, part = piece / NPL, jpl = piece % NPL;
+        const int hp0 = threadIdx.x / PPP;
+        const int64_t part_off = part ? p.x_pix / 2 : 0;
+        int s = 0, ph = 0, sa = 0, inflight = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+            const Tile tl = decode(p, t);
+            const int iy0 = tl.oy0 - p.pt, ix0 = tl.ox0 - p.pl;
+            const uint16_t *xb = p.x + (int64_t)tl.nb * p.x_n + part_off;
+            for (int ch = 0; ch < p.nchunk; ch++) {
+                if (!warp_wait(&emptyA[s], ph ^ 1, p.status, abort_flag, 21)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *a = smem + (uint32_t)s * p.a_stage + (uint32_t)(part * NPL + jpl) * p.plane;
+                const int c = ch * CG + jpl * 8;
+                const int left = (p.cin - c) * 2;
+                const uint32_t cbytes = left <= 0 ? 0u : (left < 16 ? (uint32_t)left : 16u);
+                int hy = hp0 / p.hw_w, hx = hp0 - (hp0 / p.hw_w) * p.hw_w;
+                for (int hp = hp0; hp < p.halo_px; hp += PXS) {
+                    const int iy = iy0 + hy, ix = ix0 + hx;
+                    const bool v = cbytes && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+                    const uint16_t *src = v ? xb + ((int64_t)iy * p.w + ix) * p.x_pix + c : p.x;
+                    cp_async16(a + hp * 16, src, v ? cbytes : 0u);
+                    hx += PXS;
+                    while (hx >= p.hw_w) {
+                        hx -= p.hw_w;
+                        hy++;
+                    }
+                }
+                cp_async_commit();
+                if (inflight == p.lag) {
+                    // the oldest stage in flight has landed: publish it to the tensor cores
+                    cp_async_wait(p.lag);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&fullA[sa]);
+                    if (++sa == SA) sa = 0;
+                } else {
+                    inflight++;
+                }
+                if (++s == SA) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+        }
+        // the stages still in flight
+        cp_async_wait(0);
+        fence_async_smem();
+        __syncwarp();
+        for (; inflight > 0; inflight--) {
+            if (lane == 0) mbar_arrive(&fullA[sa]);
+            if (++sa == SA) sa = 0;
+        }
+    } else if (warp == kTmaW) {
+        // ---------------- B loader ----------------
+        if (lane == 0) {
+            if (p.b_res) {
+                // every (N tile, tap, chunk) of the weights, once
+                mbar_expect_tx(bres, (uint32_t)p.ntn * p.taps * p.nchunk * 2 * B_BYTES);
+                for (int nt = 0; nt < p.ntn; nt++)
+                    for (int tap = 0; tap < p.taps; tap++)
+                        for (int ch = 0; ch < p.nchunk; ch++) {
+                            uint8_t *dst = bsm + (uint32_t)((nt * p.taps + tap) * p.nchunk + ch) * 2 * B_BYTES;
+                            const int kx0 = tap * p.cin_pad + ch * CG;
+                            tma_load_2d(dst, &wb_hi, bres, kx0, nt * BN);
+                            tma_load_2d(dst + B_BYTES, &wb_lo, bres, kx0, nt * BN);
+                        }
+                long long t0 = clock64();
+                while (!mbar_try(bres, 0) && clock64() - t0 < kWaitBudget) {
+                }
+            } else {
+                int s = 0, ph = 0, issued = 0;
+                bool ok = true;
+                for (int64_t t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+                    const Tile tl = decode(p, t);
+                    for (int ch = 0; ch < p.nchunk && ok; ch++)
+                        for (int tap = 0; tap < p.taps; tap++, issued++) {
+                            if (!mbar_wait(&emptyB[s], ph ^ 1, p.status, abort_flag, 22)) {
+                                ok = false;
+                                break;
+                            }
+                            uint8_t *dst = bsm + (uint32_t)s * 2 * B_BYTES;
+                            mbar_expect_tx(&fullB[s], 2 * B_BYTES);
+                            const int kx0 = tap * p.cin_pad + ch * CG;
+                            tma_load_2d(dst, &wb_hi, &fullB[s], kx0, tl.nt * BN);
+                            tma_load_2d(dst + B_BYTES, &wb_lo, &fullB[s], kx0, tl.nt * BN);
+                            if (++s == SB) {
+                                s = 0;
+                                ph ^= 1;
+                            }
+                        }
+                }
+                // drain: the last SB issued loads land before the CTA may exit (bounded)
+                for (int j = (issued > SB ? issued - SB : 0); j < issued; j++) {
+                    long long t0 = clock64();
+                    while (!mbar_try(&fullB[j % SB], (j / SB) & 1) && clock64() - t0 < kWaitBudget) {
+                    }
+                }
+            }
+        }
+    } else if (warp == kMmaW) {
+        // ---------------- MMA issue ----------------
+        // Descriptors are built once per stage and advanced by adding 16-byte units to their start
+        // address field, so the issuing thread spends a few instructions per MMA.
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(BN);
+            const uint32_t plane16 = p.plane >> 4, b16 = B_BYTES >> 4;
+            const uint32_t sbo = (uint32_t)p.hw_w * 16;  // one halo row per 8-row group
+            const uint32_t bsm32 = smem_u32(bsm);
+            const uint32_t tap_b16 = (uint32_t)p.nchunk * 2 * b16;  // resident B: next tap
+            bool ok = !p.b_res || mbar_wait(bres, 0, p.status, abort_flag, 27);
+            int sa = 0, pha = 0, sb = 0, phb = 0, lt = 0;
+            for (int64_t t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x, lt++) {
+                const int ab = lt % NACC;
+                const uint32_t dtile = tmem + ab * TCOLS;
+                const int nt = (int)(t % p.ntn);
+                ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 26);
+                if (!ok) break;
+                tc_fence_after();
+                int par = 0;
+                uint32_t fresh = 3;  // accumulators not yet written in this tile
+                for (int ch = 0; ch < p.nchunk && ok; ch++) {
+                    ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 23);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
+                    uint64_t dbr = p.b_res ? smem_desc_sw(bsm32 + (uint32_t)(nt * p.taps * p.nchunk + ch) * 2 * B_BYTES, RB)
+                                           : 0;
+                    uint32_t toff = 0;
+                    int kx = 0;
+                    for (int tap = 0; tap < p.taps; tap++) {
+                        uint64_t db;
+                        if (p.b_res) {
+                            db = dbr;
+                            dbr += tap_b16;
+                        } else {
+                            ok = mbar_wait(&fullB[sb], phb, p.status, abort_flag, 24);
+                            if (!ok) break;
+                            tc_fence_after();
+                            db = smem_desc_sw(bsm32 + (uint32_t)sb * 2 * B_BYTES, RB);
+                        }
+                        const uint64_t da = da0 + toff;
+                        const uint32_t d = dtile + par * BN;
+                        uint32_t acc = (fresh >> par) & 1 ? 0u : 1u;
+                        fresh &= ~(1u << par);
+#pragma unroll
+                        for (int kk = 0; kk < CG / 16; kk++) {
+                            const uint64_t ah = da + 2 * kk * plane16, al = da + (NPL + 2 * kk) * plane16;
+                            umma(d, ah, db + 2 * kk, idesc, acc);
+                            umma(d, ah, db + b16 + 2 * kk, idesc, 1u);
+                            umma(d, al, db + 2 * kk, idesc, 1u);
+                            acc = 1u;
+                        }
+                        if (!p.b_res) {
+                            umma_commit(&emptyB[sb]);
+                            par ^= 1;
+                            if (++sb == SB) {
+                                sb = 0;
+                                phb ^= 1;
+                            }
+                        }
+                        toff++;
+                        if (++kx == p.kw) {
+                            kx = 0;
+                            toff += p.hw_w - p.kw;
+                        }
+                    }
+                    if (!ok) break;
+                    umma_commit(&emptyA[sa]);
+                    if (p.b_res) par ^= 1;
+                    if (++sa == SA) {
+                        sa = 0;
+                        pha ^= 1;
+                    }
+                }
+                if (ok) umma_commit(&tfull[ab]);
+            }
+            // every issued MMA completes before the shared and tensor memory go away (bounded)
+            umma_commit(drain);
+            long long t0 = clock64();
+            while (!mbar_try(drain, 0) && clock64() - t0 < kWaitBudget) {
+            }
+        }
+    } else {
+        // ---------------- epilogue: warps 4-11, lane quadrant warp % 4, column half ----------------
+        const int q = warp & 3, half = (warp - kEpi0) >> 2;
+        const int row = q * 32 + lane;
+        const int r = row / TP, pc = row % TP;
+        int lt = 0;
+        for (int64_t t = blockIdx.x; t < p.ntiles; t += gridDim.x, lt++) {
+            const int ab = lt % NACC;
+            if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 25)) break;
+            tc_fence_after();
+            const Tile tl = decode(p, t);
+            const int oy = tl.oy0 + r, ox = tl.ox0 + pc;
+            const bool valid = oy < p.oh && ox < p.ow;
+#pragma unroll 1
+            for (int c0 = half * 16; c0 < BN; c0 += 32) {
+                float v[16];
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + c0;
+                if (p.two_acc) tmem_ld16_sum2(tbase, tbase + BN, v);
+                else tmem_ld16(tbase, v);
+                const int col = tl.nt * BN + c0;
+                if (!valid || col >= p.N) continue;
+                if (p.scatter) {
+                    const int sc = p.scatter;
+                    if (p.scat_cout % 16 == 0) {
+                        // a 16-column chunk lies in one tap: 16 channels of pixel (s oy + ky, s ox + kx)
+                        const int tap = col / p.scat_cout, co0 = col - tap * p.scat_cout;
+                        const int yy = oy * sc + tap / sc, xx = ox * sc + tap % sc;
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj++) v[jj] = act_f(v[jj] + p.bias[co0 + jj], p.act);
+                        store16(p, (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + co0, v);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj++) {
+                            if (col + jj >= p.N) continue;
+                            const int cc = col + jj, tap = cc / p.scat_cout, co = cc - tap * p.scat_cout;
+                            const int yy = oy * sc + tap / sc, xx = ox * sc + tap % sc;
+                            store1(p, (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + co,
+                                   act_f(v[jj] + p.bias[co], p.act));
+                        }
+                    }
+                    continue;
+                }
+                const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
+                if (col + 16 <= p.N) {
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++) v[jj] = act_f(v[jj] + p.bias[col + jj], p.act);
+                    store16(p, off, v);
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++)
+                        if (col + jj < p.N) store1(p, off + jj, act_f(v[jj] + p.bias[col + jj], p.act));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[ab]);  // one arrival per warp
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaW) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+    }
+}
+
+CUtensorMapSwizzle swizzle_of(int cg) {
+    return cg == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : (cg == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+void encode(CUtensorMap *map, int rank, void *base, const cuuint64_t *dims, const cuuint64_t *strides,
+            const cuuint32_t *box, int cg) {
+    auto fn = encode_fn();
+    if (!fn) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle_of(cg), CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+}
+
+template <int BN, int CG>
+void launch(Ctx *c, const TconvW &w, const TcP &p, int smem) {
+    static bool set[64] = {false};
+    if (!set[c->device]) {
+        WOCR_CUDA(cudaFuncSetAttribute(k_tconv<BN, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 2048));
+        set[c->device] = true;
+    }
+    unsigned grid = (unsigned)std::min<int64_t>(p.ntiles, c->sm_count);
+    k_tconv<BN, CG><<<grid, kThreads, smem, c->stream>>>(w.map_hi, w.map_lo, p);
+    WOCR_LAUNCHED(c);
+}
+
+template <int CG>
+void launch_bn(Ctx *c, const TconvW &w, const TcP &p, int smem) {
+    switch (w.bn) {
+    case 16: launch<16, CG>(c, w, p, smem); break;
+    case 32: launch<32, CG>(c, w, p, smem); break;
+    case 64: launch<64, CG>(c, w, p, smem); break;
+    default: launch<128, CG>(c, w, p, smem); break;
+    }
+}
+
+int tconv_bn(int N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128; }
+
+}  // namespace
+
+TconvW make_tconv_weights(Ctx *c, const std::vector<float> &wnk, int N, int taps, int cin) {
+    TconvW w;
+    w.N = N;
+    w.taps = taps;
+    w.cin = cin;
+    // the widest chunk that fits in cin (a last partial chunk reads zeros past cin)
+    if (cin < 16) fail(WOCR_ERR_UNSUPPORTED, "tap convolution with fewer than 16 input channels");
+    w.cg = cin >= 32 ? 32 : 16;
+    w.cin_pad = (cin + w.cg - 1) / w.cg * w.cg;
+    w.bn = tconv_bn(N);
+    const int Npad = (N + w.bn - 1) / w.bn * w.bn;  // every TMA box lies inside the tensor
+    const int64_t K = (int64_t)taps * w.cin_pad;
+    std::vector<__nv_bfloat16> hi((size_t)Npad * K, __float2bfloat16_rn(0.f)), lo = hi;
+    for (int n = 0; n < N; n++)
+        for (int t = 0; t < taps; t++)
+            for (int ci = 0; ci < cin; ci++) {
+                float v = wnk[((size_t)n * taps + t) * cin + ci];
+                __nv_bfloat16 h = __float2bfloat16_rn(v);
+                size_t o = (size_t)n * K + (size_t)t * w.cin_pad + ci;
+                hi[o] = h;
+                lo[o] = __float2bfloat16_rn(v - __bfloat162float(h));
+            }
+    size_t bytes = (size_t)Npad * K * 2;
+    w.hi = alloc(c, bytes);
+    w.lo = alloc(c, bytes);
+    WOCR_CUDA(cudaMemcpyAsync(w.hi->p, hi.data(), bytes, cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaMemcpyAsync(w.lo->p, lo.data(), bytes, cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)Npad};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {(cuuint32_t)w.cg, (cuuint32_t)w.bn};
+    encode(&w.map_hi, 2, w.hi->p, dims, strides, box, w.cg);
+    encode(&w.map_lo, 2, w.lo->p, dims, strides, box, w.cg);
+    return w;
+}
+
+bool tconv_input_ok(const uint16_t *x, int64_t x_n, int64_t x_pix) {
+    // 16-byte copies: base, lo part and pixel / image strides 16-byte aligned
+    return (reinterpret_cast<uintptr_t>(x) & 15) == 0 && x_pix % 16 == 0 && x_n % 8 == 0;
+}
+
+void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
+    const int64_t M = (int64_t)q.n * q.oh * q.ow;
+    if (M == 0 || w.N == 0) return;
+    if (q.cin != w.cin || q.kh * q.kw != w.taps) fail(WOCR_ERR_SHAPE, "tap convolution weights do not match");
+    if (!tconv_input_ok(q.x, q.x_n, q.x_pix)) fail(WOCR_ERR_UNSUPPORTED, "tap convolution input not 16-byte aligned");
+    if (q.scatter && (q.kh != 1 || q.kw != 1)) fail(WOCR_ERR_UNSUPPORTED, "scatter tap convolution with a kernel");
+    if (!c->status) {
+        c->status_buf = alloc(c, 16);
+        c->status = (int *)c->status_buf->p;
+        WOCR_CUDA(cudaMemsetAsync(c->status, 0, 16, c->stream));
+    }
+    TcP p{};
+    p.x = q.x;
+    p.x_n = q.x_n;
+    p.x_pix = q.x_pix;
+    p.h = q.h;
+    p.w = q.w;
+    p.cin = q.cin;
+    p.n = q.n;
+    p.oh = q.oh;
+    p.ow = q.ow;
+    p.tiles_x = (q.ow + TP - 1) / TP;
+    p.tiles_y = (q.oh + TR - 1) / TR;
+    p.ntn = (w.N + w.bn - 1) / w.bn;
+    p.ntiles = (int64_t)q.n * p.tiles_x * p.tiles_y * p.ntn;
+    p.N = w.N;
+    p.nchunk = w.cin_pad / w.cg;
+    p.taps = w.taps;
+    p.kw = q.kw;
+    p.pt = q.pt;
+    p.pl = q.pl;
+    p.cin_pad = w.cin_pad;
+    p.hw_w = TP + q.kw - 1;
+    p.halo_px = (TR + q.kh - 1) * p.hw_w;
+    p.plane = (uint32_t)p.halo_px * 16;
+    p.a_stage = (2 * (w.cg / 8) * p.plane + 1023) / 1024 * 1024;
+
+    // shared memory: A stages, then B (resident or a ring of tap chunks), then the barriers
+    const int b_half = w.bn * w.cg * 2;
+    const int b_all = p.ntn * w.taps * p.nchunk * 2 * b_half;
+    int SA, SB;
+    if (b_all <= 96 * 1024) {
+        p.b_res = 1;
+        SB = 1;
+        const int b_region = (b_all + 1023) / 1024 * 1024;
+        SA = std::min(8, (kSmemBudget - b_region) / (int)p.a_stage);
+        p.b_off = (uint32_t)SA * p.a_stage;
+        p.bar_off = p.b_off + (uint32_t)b_region;
+    } else {
+        p.b_res = 0;
+        SB = std::min(8, std::max(2, (kSmemBudget / 2) / (2 * b_half)));
+        SA = std::min(8, (kSmemBudget - SB * 2 * b_half) / (int)p.a_stage);
+        p.b_off = (uint32_t)SA * p.a_stage;
+        p.bar_off = p.b_off + (uint32_t)((SB * 2 * b_half + 1023) / 1024 * 1024);
+    }
+    if (SA < 2) fail(WOCR_ERR_UNSUPPORTED, "tap convolution halo does not fit twice");
+    // a second accumulator is written when a tile has a commit before its last MMA
+    p.two_acc = p.b_res ? (p.nchunk > 1) : (w.taps * p.nchunk > 1);
+    p.SA = SA;
+    p.SB = SB;
+    p.lag = std::min(kLagMax, SA - 2);
+    const int smem = (int)p.bar_off + 1024 + 1024;  // barriers + alignment slack
+
+    p.bias = q.bias;
+    p.act = q.act;
+    p.y = q.y;
+    p.split_out = q.split_out;
+    const bool al = (reinterpret_cast<uintptr_t>(q.y) & 15) == 0;
+    p.out_vec = q.split_out ? (al && q.y_pix % 16 == 0 && q.y_n % 8 == 0) : (al && q.y_pix % 4 == 0 && q.y_n % 4 == 0);
+    p.y_n = q.y_n;
+    p.y_pix = q.y_pix;
+    p.scatter = q.scatter;
+    p.scat_cout = q.scat_cout;
+    p.ow_out = q.scatter ? q.ow * q.scatter : q.ow;
+    p.status = c->status;
+
+    const double flops = 2.0 * (double)M * w.N * w.taps * w.cin;
+    const double bytes = 4.0 * ((double)q.n * q.h * q.w * q.cin + (double)M * w.N) + 4.0 * (double)w.N * w.taps * w.cin;
+    Prof pf(c, q.scatter ? "tconv_convt" : "tconv", flops, bytes);
+    if (w.cg == 16) launch_bn<16>(c, w, p, smem);
+    else launch_bn<32>(c, w, p, smem);
+    c->flops += flops;
+}
+
+}  // namespace k
+}  // namespace wocr

@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "kernels.h"
+#include "tc.h"
 #include "umma.h"
 
 namespace wocr {
@@ -39,158 +40,9 @@ namespace k {
 
 namespace {
 
-constexpr int BM = 128, BK = 64;
+constexpr int BK = 64;
 constexpr int kTapTable = 1024;  // 8-wide k chunks described in shared memory (K <= 8192)
-constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (about 2 s) per wait
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// The same, but the thread is suspended (not spinning, so it leaves the issue slots to the warps
-// doing work) until the phase completes or about 0.5 ms pass.
-__device__ __forceinline__ bool mbar_try_sleep(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait: false (and an error code in *status) when the budget runs out or another role
-// has already given up.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
-                                          int code) {
-    long long t0 = clock64();
-    while (!mbar_try_sleep(bar, parity)) {
-        if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitBudget) {
-            *abort_flag = 1;
-            atomicCAS(status, 0, code);
-            return false;
-        }
-    }
-    return true;
-}
-
-// One lane polls, the warp follows: a warp-uniform outcome for warp-wide code after the wait.
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
-                                          int code) {
-    int ok = 1;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, abort_flag, code);
-    return __shfl_sync(0xffffffffu, ok, 0) != 0;
-}
-
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-}
-
-// K-major operand tile in the 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// kind::f16, D fp32, A and B bf16, both K-major, M = 128, N = bn.
-__host__ __device__ constexpr uint32_t instr_desc(int bn) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ float erf_as(float v) {
-    float s = (v > 0.f) - (v < 0.f);
-    float a = fabsf(v);
-    float t = 1.0f / (1.0f + 0.3275911f * a);
-    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-    return s * (1.0f - poly * expf(-a * a));
-}
-
-__device__ __forceinline__ float act_f(float v, int act) {
-    switch (act) {
-    case 1: return fmaxf(v, 0.f);
-    case 2: return 1.0f / (1.0f + expf(-v));
-    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
-    case 4: return v / (1.0f + expf(-v));
-    default: return v;
-    }
-}
-
-// Split 8 fp32 values into bf16 hi and lo parts, packed 2 per word.
-__device__ __forceinline__ void split8(const float (&v)[8], uint4 &hi, uint4 &lo) {
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-        float2 hf = __bfloat1622float2(hv);
-        __nv_bfloat162 lv = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
-        h[i] = *reinterpret_cast<uint32_t *>(&hv);
-        l[i] = *reinterpret_cast<uint32_t *>(&lv);
-    }
-    hi = make_uint4(h[0], h[1], h[2], h[3]);
-    lo = make_uint4(l[0], l[1], l[2], l[3]);
-}
+using namespace tc;
 
 struct Smem {
     // per stage: A hi, A lo (128 x 64 bf16 = 16 KB each), B hi, B lo (BN x 64 bf16 each)
@@ -291,17 +143,6 @@ constexpr int kTmaWarp = 20;    // warp 20: B tiles by TMA
 constexpr int kMmaWarp = 21;    // warp 21: TMEM allocation, MMA issue
 constexpr int kAllThreads = 22 * 32;
 
-// Accumulator buffers in tensor memory: as many BN-column fp32 tiles as fit its 512 columns, at
-// most 8, so the MMA warp can run that many tiles ahead of the epilogue.
-template <int BN>
-struct Acc {
-    // Independent accumulation chains per tile: consecutive MMAs into one accumulator serialise
-    // on its read-modify-write, so narrow tiles (whose MMAs are short) spread the 12 MMAs of a
-    // stage over several accumulators and the epilogue adds them up.
-    static constexpr int chains = BN <= 16 ? 6 : (BN <= 32 ? 4 : (BN <= 64 ? 2 : 1));
-    static constexpr int cols = BN * chains;  // TMEM columns of one tile
-    static constexpr int n = 512 / cols < 8 ? 512 / cols : 8;
-};
 
 // The im2col source of one 8-wide k chunk of a convolution, precomputed per CTA: tap row (bits
 // 24-31), tap column (16-23) and first input channel (0-15); 0xffffffff past K.
@@ -620,18 +461,6 @@ __global__ void __launch_bounds__(kAllThreads, 1)
 }
 
 // ---- host side ------------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
 
 void make_map(CUtensorMap *map, void *base, int N, int Kpad, int bn) {
     auto fn = encode_fn();

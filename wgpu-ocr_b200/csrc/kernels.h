@@ -38,13 +38,30 @@ void conv_gemm(Ctx *c, const ConvP &p);
 
 // Cin = 1, stride 1 convolution with its activation and an optional fused MaxPool (ph, pw)
 // (K6, src/gpu.rs:385-422).  wt [kh][kw][cout]; output NHWC with pixel stride y_pix.
+// split_out: y is a split tensor (bf16 hi | lo per pixel, strides in bf16 elements; cout 16
+// or 32 only).
 void conv_direct(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, const float *wt,
-                 const float *bias, int cout, int kh, int kw, int pad, int act, int ph, int pw, float *y,
-                 int64_t y_n, int64_t y_pix, int oh, int ow);
+                 const float *bias, int cout, int kh, int kw, int pad, int act, int ph, int pw, void *y,
+                 int64_t y_n, int64_t y_pix, int oh, int ow, int split_out = 0);
 
 // 1 x 1, stride 1 convolution with cout < 16 (a detector head), memory-bound; wt [cin][ldw].
-void pointwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin, const float *wt, int ldw,
-               const float *bias, int cout, int act, float *y, int64_t y_n, int64_t y_pix);
+// split_in: x is a split tensor (strides in bf16 elements).  y fp32 NHWC.
+void pointwise(Ctx *c, const void *x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin, const float *wt, int ldw,
+               const float *bias, int cout, int act, float *y, int64_t y_n, int64_t y_pix, int split_in = 0);
+
+// Split activations: per pixel the bf16 hi parts of the buffer's channels, then their lo parts
+// (hi = bf16(v), lo = bf16(v - hi)); views carry strides in bf16 elements, and the lo part of a
+// channel lies x_pix / 2 elements after its hi part.
+// Max pool with kernel == stride, no padding (K8, src/gpu.rs:462), on a split input; the output
+// is split (split_out) or fp32.
+void maxpool_split(Ctx *c, const uint16_t *x, int64_t x_n, int64_t x_pix, int n, int h, int w, int ch, int kh, int kw,
+                   int oh, int ow, void *y, int64_t y_n, int64_t y_pix, int split_out);
+// split <-> fp32 conversions of 4-D views [n][c][h][w] with any strides (xs, ys in elements of
+// each side; a split side has channel stride 1 and its lo part at lo_off elements).
+void unsplit(Ctx *c, const uint16_t *x, const int64_t (&xs)[4], int64_t lo_off, float *y, const int64_t (&ys)[4],
+             const int64_t (&dims)[4]);
+void resplit(Ctx *c, const float *x, const int64_t (&xs)[4], uint16_t *y, const int64_t (&ys)[4], int64_t lo_off,
+             const int64_t (&dims)[4]);
 
 // Depthwise convolution (K5, src/gpu.rs:356-383): wt [kh][kw][c], NHWC.
 void depthwise(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int h, int w, int ch, const float *wt,

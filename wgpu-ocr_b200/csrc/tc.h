@@ -1,0 +1,231 @@
+// Device helpers shared by the tcgen05 kernels (k_umma.cu, k_tconv.cu): mbarriers with bounded
+// waits, TMA loads, shared-memory matrix descriptors, tcgen05.mma / commit / ld, the epilogue
+// activations and the bf16 hi/lo split.  All inline PTX for sm_100a.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace wocr {
+namespace k {
+namespace tc {
+
+constexpr int BM = 128;  // rows of every tensor-core tile (one TMEM lane each)
+constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (about 2 s) per wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// The same, but the thread is suspended (not spinning, so it leaves the issue slots to the warps
+// doing work) until the phase completes or about 0.5 ms pass.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(500000u)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false (and an error code in *status) when the budget runs out or another role
+// has already given up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
+                                          int code) {
+    long long t0 = clock64();
+    while (!mbar_try_sleep(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitBudget) {
+            *abort_flag = 1;
+            atomicCAS(status, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+// One lane polls, the warp follows: a warp-uniform outcome for warp-wide code after the wait.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
+                                          int code) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, abort_flag, code);
+    return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// K-major operand tile in the 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// kind::f16, D fp32, A and B bf16, both K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t instr_desc(int bn) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Two 16-column loads, one wait: v = columns at a0 + columns at a1.
+__device__ __forceinline__ void tmem_ld16_sum2(uint32_t a0, uint32_t a1, float (&v)[16]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(a0), "r"(a1)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]) + __uint_as_float(r[16 + i]);
+}
+
+__device__ __forceinline__ float erf_as(float v) {
+    float s = (v > 0.f) - (v < 0.f);
+    float a = fabsf(v);
+    float t = 1.0f / (1.0f + 0.3275911f * a);
+    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
+    return s * (1.0f - poly * expf(-a * a));
+}
+
+__device__ __forceinline__ float act_f(float v, int act) {
+    switch (act) {
+    case 1: return fmaxf(v, 0.f);
+    case 2: return 1.0f / (1.0f + expf(-v));
+    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
+    case 4: return v / (1.0f + expf(-v));
+    default: return v;
+    }
+}
+
+// Split 8 fp32 values into bf16 hi and lo parts, packed 2 per word.
+__device__ __forceinline__ void split8(const float (&v)[8], uint4 &hi, uint4 &lo) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        __nv_bfloat162 hv = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        float2 hf = __bfloat1622float2(hv);
+        __nv_bfloat162 lv = __floats2bfloat162_rn(v[2 * i] - hf.x, v[2 * i + 1] - hf.y);
+        h[i] = *reinterpret_cast<uint32_t *>(&hv);
+        l[i] = *reinterpret_cast<uint32_t *>(&lv);
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// K-major operand tile with rows of `row_bytes` (32, 64 or 128) in the matching TMA swizzle:
+// 8-row atoms of 8 * row_bytes bytes (the stride byte offset), layout codes 6 / 4 / 2.
+__device__ __forceinline__ uint64_t smem_desc_sw(uint32_t addr, int row_bytes) {
+    const uint64_t layout = row_bytes == 32 ? 6 : (row_bytes == 64 ? 4 : 2);
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)((8 * row_bytes) >> 4) << 32) |
+           ((uint64_t)1 << 46) | (layout << 61);
+}
+
+// K-major operand without swizzle: 8 x 16-byte core matrices (8 rows of 8 bf16, 128 contiguous
+// bytes); `lbo` bytes between the two core matrices of a 16-element K step, `sbo` bytes between
+// consecutive 8-row groups.  Start, lbo and sbo are multiples of 16 bytes.
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+}
+
+// Accumulator buffers in tensor memory: as many BN-column fp32 tiles as fit its 512 columns, at
+// most 8, so the MMA warp can run that many tiles ahead of the epilogue.
+template <int BN>
+struct Acc {
+    // Independent accumulation chains per tile: consecutive MMAs into one accumulator serialise
+    // on its read-modify-write, so narrow tiles (whose MMAs are short) spread the 12 MMAs of a
+    // stage over several accumulators and the epilogue adds them up.
+    static constexpr int chains = BN <= 16 ? 6 : (BN <= 32 ? 4 : (BN <= 64 ? 2 : 1));
+    static constexpr int cols = BN * chains;  // TMEM columns of one tile
+    static constexpr int n = 512 / cols < 8 ? 512 / cols : 8;
+};
+
+inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+}  // namespace tc
+}  // namespace k
+}  // namespace wocr

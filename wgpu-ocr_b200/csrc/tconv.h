@@ -1,0 +1,44 @@
+// Tap convolution on split activations (k_tconv.cu): parameters and pre-split weights.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.h"
+
+namespace wocr {
+namespace k {
+
+// Weights of a stride-1 convolution as tap-major GEMM operand: [Npad][taps][cin_pad] bf16,
+// split into hi = bf16(w) and lo = bf16(w - hi), with TMA descriptors whose boxes are one tap's
+// cg-channel chunk (cg = 16, 32 or 64, the swizzle span of its rows) of bn output channels.
+struct TconvW {
+    BufP hi, lo;
+    CUtensorMap map_hi, map_lo;
+    int N = 0, taps = 0, cin = 0, cin_pad = 0, cg = 0, bn = 0;
+};
+
+// wnk: [N][taps][cin] fp32 (taps in (ky, kx) order).
+TconvW make_tconv_weights(Ctx *c, const std::vector<float> &wnk, int N, int taps, int cin);
+
+// One launch.  The input is a split NHWC tensor: per pixel the bf16 hi parts of all channels of
+// its buffer, then their lo parts; x points at the hi part of channel 0 of this view, strides
+// are in bf16 elements and the lo part of a channel sits x_pix / 2 elements after its hi part.
+struct TconvP {
+    const uint16_t *x = nullptr;
+    int64_t x_n = 0, x_pix = 0;
+    int n = 0, h = 0, w = 0, cin = 0;
+    int kh = 1, kw = 1, pt = 0, pl = 0, oh = 0, ow = 0;  // stride 1
+    const float *bias = nullptr;
+    int act = 0;
+    void *y = nullptr;
+    int split_out = 0;               // 1: y split like x (bf16 elements); 0: fp32 NHWC
+    int64_t y_n = 0, y_pix = 0;
+    int scatter = 0, scat_cout = 0;  // ConvTranspose kernel == stride s: N = cout * s * s
+};
+
+// The input view meets the TMA rules (16-byte aligned base, lo part and strides).
+bool tconv_input_ok(const uint16_t *x, int64_t x_n, int64_t x_pix);
+void tconv(Ctx *c, const TconvW &w, const TconvP &p);
+
+}  // namespace k
+}  // namespace wocr
