@@ -38,7 +38,7 @@ using namespace tc;
 
 constexpr int kProd = 4, kEpi0 = 4, kEpiWarps = 8, kTmaW = 12, kMmaW = 13, kThreads = 448;
 constexpr int kLagMax = 4;        // cp.async stages in flight per producer thread
-constexpr int kSmemBudget = 220 * 1024;
+constexpr int kSmemBudget = 212 * 1024;  // stages and B; barriers and bias after it
 constexpr int TP = 8, TR = 16;    // tile: TR image rows of TP pixels (an 8-row group per image row)
 
 struct TcP {
@@ -47,7 +47,8 @@ struct TcP {
     int h, w, cin;
     int n, oh, ow;              // GEMM output grid (ConvTranspose: its input grid)
     int tiles_x, tiles_y, ntn;
-    int64_t ntiles;
+    int ntiles;                 // < 2^31 (checked on the host)
+    FastDiv div_ntn, div_tx, div_ty;
     int N, nchunk, taps, kw, pt, pl, cin_pad;
     int two_acc;                // the tile's MMAs alternate between two accumulators
     int hw_w, halo_px;          // halo row length and pixel count
@@ -55,6 +56,8 @@ struct TcP {
     int SA, SB, lag, b_res;     // A stages, B ring stages, cp.async stages in flight, B resident
     uint32_t b_off, bar_off;    // shared-memory offsets of the B region and the barriers
     const float *bias;
+    int bias_n;                 // bias values copied to shared memory at bias_off
+    uint32_t bias_off;
     int act;
     void *y;
     int split_out, out_vec;
@@ -68,17 +71,27 @@ struct Tile {
     int nb, oy0, ox0, nt;
 };
 
-__device__ __forceinline__ Tile decode(const TcP &p, int64_t t) {
+// tile t -> (image, tile row, tile column, N tile), N tile fastest
+__device__ __forceinline__ Tile decode(const TcP &p, int t) {
     Tile r;
-    r.nt = (int)(t % p.ntn);
-    int64_t sp = t / p.ntn;
-    const int tx = (int)(sp % p.tiles_x);
-    sp /= p.tiles_x;
-    const int ty = (int)(sp % p.tiles_y);
-    r.nb = (int)(sp / p.tiles_y);
-    r.oy0 = ty * TR;
-    r.ox0 = tx * TP;
+    const uint32_t q1 = p.div_ntn.div((uint32_t)t), q2 = p.div_tx.div(q1), q3 = p.div_ty.div(q2);
+    r.nt = t - (int)(q1 * p.div_ntn.d);
+    r.ox0 = (int)(q1 - q2 * p.div_tx.d) * TP;
+    r.oy0 = (int)(q2 - q3 * p.div_ty.d) * TR;
+    r.nb = (int)q3;
     return r;
+}
+
+// activation of 16 values (uniform branch on the code)
+__device__ __forceinline__ void act16(float (&v)[16], int act) {
+    if (act == 0) return;
+    if (act == 1) {
+#pragma unroll
+        for (int j = 0; j < 16; j++) v[j] = fmaxf(v[j], 0.f);
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 16; j++) v[j] = act_f(v[j], act);
 }
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
@@ -144,7 +157,8 @@ __device__ __forceinline__ void store16(const TcP &p, int64_t off, const float (
     for (int j = 0; j < 16; j++) store1(p, off + j, v[j]);
 }
 
-template <int BN, int CG>
+// TAPS: 9 (3 x 3 kernel), 1 (1 x 1) or 0 (any kernel, taps counted at run time).
+template <int BN, int CG, int TAPS>
 __global__ void __launch_bounds__(kThreads, 1)
     k_tconv(const __grid_constant__ CUtensorMap wb_hi, const __grid_constant__ CUtensorMap wb_lo, TcP p) {
     constexpr int RB = CG * 2;                 // bytes of one B row
@@ -152,10 +166,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int NPL = CG / 8;                // 8-channel planes per split part
     constexpr int PPP = 2 * NPL;               // 16-byte pieces per halo pixel
     constexpr int PXS = kProd * 32 / PPP;      // halo pixels per pass of the producer threads
-    // accumulator buffers in tensor memory: NACC tiles of two BN-column accumulators each (the MMAs
-    // after a commit inside a tile go to the other one, so they never wait on the committed ones)
-    constexpr int TCOLS = 2 * BN;
+    // STACK (BN <= 64): B hi and lo are one 2 BN-row operand, so one MMA of N = 2 BN (no slower
+    // than N = BN up to 128) gives hi.hi in columns [0, BN) and hi.lo in [BN, 2 BN), and a second
+    // MMA adds lo.hi to [0, BN): two MMAs per 16-channel step instead of three.
+    constexpr bool STACK = BN <= 64;
+    constexpr int ACCW = STACK ? 2 * BN : BN;  // columns of one accumulator
+    // accumulator buffers in tensor memory: NACC tiles of two accumulators each (the MMAs after a
+    // commit inside a tile go to the other one, so they never wait on the committed ones)
+    constexpr int TCOLS = 2 * ACCW;
     constexpr int NACC = 512 / TCOLS < 8 ? 512 / TCOLS : 8;
+    constexpr int KW = TAPS == 9 ? 3 : 1;       // kernel width when TAPS is fixed
     constexpr uint32_t kCols = NACC * TCOLS <= 32 ? 32 : (NACC * TCOLS <= 64 ? 64 : (NACC * TCOLS <= 128 ? 128 : (NACC * TCOLS <= 256 ? 256 : 512)));
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -171,7 +191,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *bres = drain + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bres + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *bias_s = reinterpret_cast<float *>(smem + p.bias_off);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < p.bias_n; i += blockDim.x) bias_s[i] = p.bias[i];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SA; s++) {
@@ -204,36 +226,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp < kProd) {
         // ---------------- halo producers ----------------
-        // thread: piece (split part, plane) of every PXS-th halo pixel, consecutive threads on
-        // consecutive 16-byte pieces of a pixel (coalesced)
+        // thread: one 16-byte piece (split part, plane) of one halo column, every rstep-th halo
+        // row; consecutive threads take consecutive pieces of a pixel, then consecutive pixels
+        // (coalesced).  Threads past rstep * hw_w pixel slots idle.
         const int piece = threadIdx.x % PPP, part = piece / NPL, jpl = piece % NPL;
-        const int hp0 = threadIdx.x / PPP;
+        const int slot = threadIdx.x / PPP, rstep = PXS / p.hw_w;
+        const int col = slot % p.hw_w, row0 = slot / p.hw_w;
+        const bool active = slot < rstep * p.hw_w;
+        const int halo_h = p.halo_px / p.hw_w;
         const int64_t part_off = part ? p.x_pix / 2 : 0;
+        const int64_t row_step = (int64_t)rstep * p.w * p.x_pix;
+        const uint32_t dst_step = (uint32_t)(rstep * p.hw_w * 16);
         int s = 0, ph = 0, sa = 0, inflight = 0;
         bool ok = true;
-        for (int64_t t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+        for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
             const Tile tl = decode(p, t);
-            const int iy0 = tl.oy0 - p.pt, ix0 = tl.ox0 - p.pl;
-            const uint16_t *xb = p.x + (int64_t)tl.nb * p.x_n + part_off;
+            const int iy0 = tl.oy0 - p.pt + row0, ix = tl.ox0 - p.pl + col;
+            const bool colv = active && ix >= 0 && ix < p.w;
+            const uint16_t *xrow = p.x + (int64_t)tl.nb * p.x_n + part_off + ((int64_t)iy0 * p.w + ix) * p.x_pix;
             for (int ch = 0; ch < p.nchunk; ch++) {
                 if (!warp_wait(&emptyA[s], ph ^ 1, p.status, abort_flag, 21)) {
                     ok = false;
                     break;
                 }
-                uint8_t *a = smem + (uint32_t)s * p.a_stage + (uint32_t)(part * NPL + jpl) * p.plane;
                 const int c = ch * CG + jpl * 8;
                 const int left = (p.cin - c) * 2;
                 const uint32_t cbytes = left <= 0 ? 0u : (left < 16 ? (uint32_t)left : 16u);
-                int hy = hp0 / p.hw_w, hx = hp0 - (hp0 / p.hw_w) * p.hw_w;
-                for (int hp = hp0; hp < p.halo_px; hp += PXS) {
-                    const int iy = iy0 + hy, ix = ix0 + hx;
-                    const bool v = cbytes && iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
-                    const uint16_t *src = v ? xb + ((int64_t)iy * p.w + ix) * p.x_pix + c : p.x;
-                    cp_async16(a + hp * 16, src, v ? cbytes : 0u);
-                    hx += PXS;
-                    while (hx >= p.hw_w) {
-                        hx -= p.hw_w;
-                        hy++;
+                if (active) {
+                    uint8_t *dst = smem + (uint32_t)s * p.a_stage + (uint32_t)(part * NPL + jpl) * p.plane +
+                                   (uint32_t)(row0 * p.hw_w + col) * 16;
+                    const uint16_t *src = xrow + c;
+                    int iy = iy0;
+                    for (int hy = row0; hy < halo_h; hy += rstep) {
+                        const bool v = colv && cbytes && iy >= 0 && iy < p.h;
+                        cp_async16(dst, v ? src : p.x, v ? cbytes : 0u);
+                        dst += dst_step;
+                        src += row_step;
+                        iy += rstep;
                     }
                 }
                 cp_async_commit();
@@ -281,7 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
                 int s = 0, ph = 0, issued = 0;
                 bool ok = true;
-                for (int64_t t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
+                for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
                     const Tile tl = decode(p, t);
                     for (int ch = 0; ch < p.nchunk && ok; ch++)
                         for (int tap = 0; tap < p.taps; tap++, issued++) {
@@ -311,19 +340,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaW) {
         // ---------------- MMA issue ----------------
         // Descriptors are built once per stage and advanced by adding 16-byte units to their start
-        // address field, so the issuing thread spends a few instructions per MMA.
+        // address field; with TAPS fixed the tap loop unrolls into constant offsets.
         if (lane == 0) {
-            const uint32_t idesc = instr_desc(BN);
+            const uint32_t idesc = instr_desc(BN), idesc2 = instr_desc(STACK ? 2 * BN : BN);
             const uint32_t plane16 = p.plane >> 4, b16 = B_BYTES >> 4;
             const uint32_t sbo = (uint32_t)p.hw_w * 16;  // one halo row per 8-row group
             const uint32_t bsm32 = smem_u32(bsm);
             const uint32_t tap_b16 = (uint32_t)p.nchunk * 2 * b16;  // resident B: next tap
+            const int taps = TAPS ? TAPS : p.taps, kw = TAPS ? KW : p.kw, hw_w = TAPS ? KW + TP - 1 : p.hw_w;
             bool ok = !p.b_res || mbar_wait(bres, 0, p.status, abort_flag, 27);
             int sa = 0, pha = 0, sb = 0, phb = 0, lt = 0;
-            for (int64_t t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x, lt++) {
+            for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x, lt++) {
                 const int ab = lt % NACC;
                 const uint32_t dtile = tmem + ab * TCOLS;
-                const int nt = (int)(t % p.ntn);
+                const int nt = t - (int)(p.div_ntn.div((uint32_t)t) * p.div_ntn.d);
                 ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 26);
                 if (!ok) break;
                 tc_fence_after();
@@ -334,31 +364,35 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!ok) break;
                     tc_fence_after();
                     const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
-                    uint64_t dbr = p.b_res ? smem_desc_sw(bsm32 + (uint32_t)(nt * p.taps * p.nchunk + ch) * 2 * B_BYTES, RB)
-                                           : 0;
-                    uint32_t toff = 0;
-                    int kx = 0;
-                    for (int tap = 0; tap < p.taps; tap++) {
+                    const uint64_t dbr = p.b_res ? smem_desc_sw(bsm32 + (uint32_t)(nt * taps * p.nchunk + ch) * 2 * B_BYTES, RB)
+                                                 : 0;
+#pragma unroll
+                    for (int tap = 0; tap < (TAPS ? TAPS : 64); tap++) {
+                        if (!TAPS && tap >= taps) break;
                         uint64_t db;
                         if (p.b_res) {
-                            db = dbr;
-                            dbr += tap_b16;
+                            db = dbr + (uint64_t)tap * tap_b16;
                         } else {
                             ok = mbar_wait(&fullB[sb], phb, p.status, abort_flag, 24);
                             if (!ok) break;
                             tc_fence_after();
                             db = smem_desc_sw(bsm32 + (uint32_t)sb * 2 * B_BYTES, RB);
                         }
-                        const uint64_t da = da0 + toff;
-                        const uint32_t d = dtile + par * BN;
+                        const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw);
+                        const uint32_t d = dtile + par * ACCW;
                         uint32_t acc = (fresh >> par) & 1 ? 0u : 1u;
                         fresh &= ~(1u << par);
 #pragma unroll
                         for (int kk = 0; kk < CG / 16; kk++) {
                             const uint64_t ah = da + 2 * kk * plane16, al = da + (NPL + 2 * kk) * plane16;
-                            umma(d, ah, db + 2 * kk, idesc, acc);
-                            umma(d, ah, db + b16 + 2 * kk, idesc, 1u);
-                            umma(d, al, db + 2 * kk, idesc, 1u);
+                            if (STACK) {
+                                umma(d, ah, db + 2 * kk, idesc2, acc);  // hi . [hi; lo]
+                                umma(d, al, db + 2 * kk, idesc, 1u);    // lo . hi
+                            } else {
+                                umma(d, ah, db + 2 * kk, idesc, acc);
+                                umma(d, ah, db + b16 + 2 * kk, idesc, 1u);
+                                umma(d, al, db + 2 * kk, idesc, 1u);
+                            }
                             acc = 1u;
                         }
                         if (!p.b_res) {
@@ -368,11 +402,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 sb = 0;
                                 phb ^= 1;
                             }
-                        }
-                        toff++;
-                        if (++kx == p.kw) {
-                            kx = 0;
-                            toff += p.hw_w - p.kw;
                         }
                     }
                     if (!ok) break;
@@ -397,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = q * 32 + lane;
         const int r = row / TP, pc = row % TP;
         int lt = 0;
-        for (int64_t t = blockIdx.x; t < p.ntiles; t += gridDim.x, lt++) {
+        for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, lt++) {
             const int ab = lt % NACC;
             if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 25)) break;
             tc_fence_after();
@@ -408,8 +437,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c0 = half * 16; c0 < BN; c0 += 32) {
                 float v[16];
                 const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + c0;
-                if (p.two_acc) tmem_ld16_sum2(tbase, tbase + BN, v);
-                else tmem_ld16(tbase, v);
+                if (STACK) {
+                    if (p.two_acc) tmem_ld16_sum4(tbase, tbase + BN, tbase + ACCW, tbase + ACCW + BN, v);
+                    else tmem_ld16_sum2(tbase, tbase + BN, v);
+                } else {
+                    if (p.two_acc) tmem_ld16_sum2(tbase, tbase + ACCW, v);
+                    else tmem_ld16(tbase, v);
+                }
                 const int col = tl.nt * BN + c0;
                 if (!valid || col >= p.N) continue;
                 if (p.scatter) {
@@ -419,7 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int tap = col / p.scat_cout, co0 = col - tap * p.scat_cout;
                         const int yy = oy * sc + tap / sc, xx = ox * sc + tap % sc;
 #pragma unroll
-                        for (int jj = 0; jj < 16; jj++) v[jj] = act_f(v[jj] + p.bias[co0 + jj], p.act);
+                        for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[co0 + jj];
+                        act16(v, p.act);
                         store16(p, (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + co0, v);
                     } else {
 #pragma unroll
@@ -428,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             const int cc = col + jj, tap = cc / p.scat_cout, co = cc - tap * p.scat_cout;
                             const int yy = oy * sc + tap / sc, xx = ox * sc + tap % sc;
                             store1(p, (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + co,
-                                   act_f(v[jj] + p.bias[co], p.act));
+                                   act_f(v[jj] + bias_s[co], p.act));
                         }
                     }
                     continue;
@@ -436,12 +471,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
                 if (col + 16 <= p.N) {
 #pragma unroll
-                    for (int jj = 0; jj < 16; jj++) v[jj] = act_f(v[jj] + p.bias[col + jj], p.act);
+                    for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[col + jj];
+                    act16(v, p.act);
                     store16(p, off, v);
                 } else {
 #pragma unroll
                     for (int jj = 0; jj < 16; jj++)
-                        if (col + jj < p.N) store1(p, off + jj, act_f(v[jj] + p.bias[col + jj], p.act));
+                        if (col + jj < p.N) store1(p, off + jj, act_f(v[jj] + bias_s[col + jj], p.act));
                 }
             }
             tc_fence_before();
@@ -472,26 +508,33 @@ void encode(CUtensorMap *map, int rank, void *base, const cuuint64_t *dims, cons
     if (r != CUDA_SUCCESS) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 
-template <int BN, int CG>
+template <int BN, int CG, int TAPS>
 void launch(Ctx *c, const TconvW &w, const TcP &p, int smem) {
     static bool set[64] = {false};
     if (!set[c->device]) {
-        WOCR_CUDA(cudaFuncSetAttribute(k_tconv<BN, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 2048));
+        WOCR_CUDA(cudaFuncSetAttribute(k_tconv<BN, CG, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         set[c->device] = true;
     }
     unsigned grid = (unsigned)std::min<int64_t>(p.ntiles, c->sm_count);
-    k_tconv<BN, CG><<<grid, kThreads, smem, c->stream>>>(w.map_hi, w.map_lo, p);
+    k_tconv<BN, CG, TAPS><<<grid, kThreads, smem, c->stream>>>(w.map_hi, w.map_lo, p);
     WOCR_LAUNCHED(c);
 }
 
-template <int CG>
+template <int CG, int TAPS>
 void launch_bn(Ctx *c, const TconvW &w, const TcP &p, int smem) {
     switch (w.bn) {
-    case 16: launch<16, CG>(c, w, p, smem); break;
-    case 32: launch<32, CG>(c, w, p, smem); break;
-    case 64: launch<64, CG>(c, w, p, smem); break;
-    default: launch<128, CG>(c, w, p, smem); break;
+    case 16: launch<16, CG, TAPS>(c, w, p, smem); break;
+    case 32: launch<32, CG, TAPS>(c, w, p, smem); break;
+    case 64: launch<64, CG, TAPS>(c, w, p, smem); break;
+    default: launch<128, CG, TAPS>(c, w, p, smem); break;
     }
+}
+
+template <int CG>
+void launch_taps(Ctx *c, const TconvW &w, const TcP &p, int smem, int kh, int kw) {
+    if (kh == 3 && kw == 3) launch_bn<CG, 9>(c, w, p, smem);
+    else if (kh == 1 && kw == 1) launch_bn<CG, 1>(c, w, p, smem);
+    else launch_bn<CG, 0>(c, w, p, smem);
 }
 
 int tconv_bn(int N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128; }
@@ -563,7 +606,12 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.tiles_x = (q.ow + TP - 1) / TP;
     p.tiles_y = (q.oh + TR - 1) / TR;
     p.ntn = (w.N + w.bn - 1) / w.bn;
-    p.ntiles = (int64_t)q.n * p.tiles_x * p.tiles_y * p.ntn;
+    const int64_t ntiles = (int64_t)q.n * p.tiles_x * p.tiles_y * p.ntn;
+    if (ntiles >= (int64_t)INT32_MAX) fail(WOCR_ERR_UNSUPPORTED, "tap convolution with 2^31 tiles or more");
+    p.ntiles = (int)ntiles;
+    p.div_ntn = FastDiv((uint32_t)p.ntn);
+    p.div_tx = FastDiv((uint32_t)p.tiles_x);
+    p.div_ty = FastDiv((uint32_t)p.tiles_y);
     p.N = w.N;
     p.nchunk = w.cin_pad / w.cg;
     p.taps = w.taps;
@@ -572,6 +620,7 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.pl = q.pl;
     p.cin_pad = w.cin_pad;
     p.hw_w = TP + q.kw - 1;
+    if (p.hw_w > 128 / (4 * w.cg / 16)) fail(WOCR_ERR_UNSUPPORTED, "tap convolution kernel too wide");
     p.halo_px = (TR + q.kh - 1) * p.hw_w;
     p.plane = (uint32_t)p.halo_px * 16;
     p.a_stage = (2 * (w.cg / 8) * p.plane + 1023) / 1024 * 1024;
@@ -600,7 +649,10 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.SA = SA;
     p.SB = SB;
     p.lag = std::min(kLagMax, SA - 2);
-    const int smem = (int)p.bar_off + 1024 + 1024;  // barriers + alignment slack
+    p.bias_n = q.scatter ? q.scat_cout : w.N;
+    p.bias_off = p.bar_off + 1024;
+    const int smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + 1024;  // + alignment slack
+    if (smem > 227 * 1024) fail(WOCR_ERR_UNSUPPORTED, "tap convolution bias too large");
 
     p.bias = q.bias;
     p.act = q.act;
@@ -618,8 +670,8 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     const double flops = 2.0 * (double)M * w.N * w.taps * w.cin;
     const double bytes = 4.0 * ((double)q.n * q.h * q.w * q.cin + (double)M * w.N) + 4.0 * (double)w.N * w.taps * w.cin;
     Prof pf(c, q.scatter ? "tconv_convt" : "tconv", flops, bytes);
-    if (w.cg == 16) launch_bn<16>(c, w, p, smem);
-    else launch_bn<32>(c, w, p, smem);
+    if (w.cg == 16) launch_taps<16>(c, w, p, smem, q.kh, q.kw);
+    else launch_taps<32>(c, w, p, smem, q.kh, q.kw);
     c->flops += flops;
 }
 

@@ -15,6 +15,25 @@ namespace k {
 namespace tc {
 
 constexpr int BM = 128;  // rows of every tensor-core tile (one TMEM lane each)
+
+// Division of 0 <= x < 2^31 by a divisor fixed at launch, as a multiply-high, an add and a shift
+// (Granlund and Montgomery, "Division by invariant integers using multiplication", 1994):
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1, x / d = (mulhi(x, m) + x) >> l.
+struct FastDiv {
+    uint32_t d = 1, m = 1, l = 0;
+    FastDiv() = default;
+    explicit FastDiv(uint32_t dv) : d(dv) {
+        while ((1ull << l) < d) l++;
+        m = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+    }
+    __host__ __device__ __forceinline__ uint32_t div(uint32_t x) const {
+#ifdef __CUDA_ARCH__
+        return (__umulhi(x, m) + x) >> l;
+#else
+        return (uint32_t)((((uint64_t)x * m) >> 32) + x) >> l;
+#endif
+    }
+};
 constexpr long long kWaitBudget = 4000000000LL;  // clock cycles (about 2 s) per wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -150,6 +169,15 @@ __device__ __forceinline__ void tmem_ld16_sum2(uint32_t a0, uint32_t a1, float (
         : "memory");
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]) + __uint_as_float(r[16 + i]);
+}
+
+// Four 16-column loads, one wait: v = the sum of the four.
+__device__ __forceinline__ void tmem_ld16_sum4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, float (&v)[16]) {
+    float u[16], w[16];
+    tmem_ld16_sum2(a0, a1, u);
+    tmem_ld16_sum2(a2, a3, w);
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = u[i] + w[i];
 }
 
 __device__ __forceinline__ float erf_as(float v) {
