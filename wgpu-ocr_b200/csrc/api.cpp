@@ -1,6 +1,8 @@
 // The C ABI of include/wocr.h: status codes at the boundary, exceptions inside.
+#include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -30,6 +32,15 @@ struct wocr_detector {
     wocr_ctx *ctx;
     std::unique_ptr<Executor> graph;
     Stats last;
+    // page uploads of wocr_detect_pages on their own stream, overlapped with detection:
+    // ready (buffers allocated), up[slot] (chunk uploaded), done[slot] (chunk detected)
+    cudaStream_t copy = nullptr;
+    cudaEvent_t ready = nullptr, up[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr};
+    ~wocr_detector() {
+        if (copy) cudaStreamDestroy(copy);
+        for (cudaEvent_t e : {ready, up[0], up[1], done[0], done[1]})
+            if (e) cudaEventDestroy(e);
+    }
 };
 
 struct GruLayer {
@@ -356,6 +367,16 @@ int32_t wocr_detect_pages_device(wocr_detector *det, const uint8_t *d_rgb, int32
     });
 }
 
+// Pages per chunk of wocr_detect_pages: the upload of one chunk overlaps the detection of the
+// previous one.  WOCR_DETECT_CHUNK overrides (0 = one chunk).
+static int detect_chunk(int n) {
+    if (const char *e = std::getenv("WOCR_DETECT_CHUNK")) {
+        int v = std::atoi(e);
+        return v <= 0 ? n : std::min(v, n);
+    }
+    return std::max(1, (n + 2) / 3);  // three chunks
+}
+
 int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int32_t w, int32_t h, float threshold,
                           uint32_t *mask_out) {
     return guard([&] {
@@ -363,12 +384,35 @@ int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int
         if (n <= 0 || w <= 0 || h <= 0) fail(WOCR_ERR_INVALID, "empty page");
         Ctx *c = &det->ctx->c;
         RunScope rs(c, &det->last);
-        size_t in_bytes = (size_t)n * w * h * 3;
-        size_t out_words = (size_t)n * h * ((w + 31) / 32);
-        BufP src = alloc(c, in_bytes), dst = alloc(c, out_words * 4);
-        WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, in_bytes, cudaMemcpyHostToDevice, c->stream));
-        detect_pages_dev(det, (const uint8_t *)src->p, n, w, h, threshold, (uint32_t *)dst->p);
-        d2h(c, mask_out, dst->p, out_words * 4);
+        const size_t page_bytes = (size_t)w * h * 3, page_words = (size_t)h * ((w + 31) / 32);
+        const int chunk = detect_chunk(n), nchunks = (n + chunk - 1) / chunk;
+        if (!det->copy) {
+            WOCR_CUDA(cudaStreamCreateWithFlags(&det->copy, cudaStreamNonBlocking));
+            for (cudaEvent_t *e : {&det->ready, &det->up[0], &det->up[1], &det->done[0], &det->done[1]})
+                WOCR_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
+        }
+        BufP src[2], dst = alloc(c, (size_t)n * page_words * 4);
+        for (int b = 0; b < std::min(nchunks, 2); b++) src[b] = alloc(c, (size_t)chunk * page_bytes);
+        // nothing of the upload stream may still run when the buffers go back to the pool
+        struct Drain {
+            cudaStream_t s;
+            ~Drain() { cudaStreamSynchronize(s); }
+        } drain{det->copy};
+        WOCR_CUDA(cudaEventRecord(det->ready, c->stream));
+        WOCR_CUDA(cudaStreamWaitEvent(det->copy, det->ready, 0));
+        for (int i = 0; i < nchunks; i++) {
+            const int slot = i & 1, k0 = i * chunk, kn = std::min(chunk, n - k0);
+            // the slot's buffer is free once the detection of chunk i - 2 has read it
+            if (i >= 2) WOCR_CUDA(cudaStreamWaitEvent(det->copy, det->done[slot], 0));
+            WOCR_CUDA(cudaMemcpyAsync(src[slot]->p, rgb + (size_t)k0 * page_bytes, (size_t)kn * page_bytes,
+                                      cudaMemcpyHostToDevice, det->copy));
+            WOCR_CUDA(cudaEventRecord(det->up[slot], det->copy));
+            WOCR_CUDA(cudaStreamWaitEvent(c->stream, det->up[slot], 0));
+            detect_pages_dev(det, (const uint8_t *)src[slot]->p, kn, w, h, threshold,
+                             (uint32_t *)dst->p + (size_t)k0 * page_words);
+            WOCR_CUDA(cudaEventRecord(det->done[slot], c->stream));
+        }
+        d2h(c, mask_out, dst->p, (size_t)n * page_words * 4);
         sync_bounded(c, 0);
     });
 }

@@ -346,9 +346,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t plane16 = p.plane >> 4, b16 = B_BYTES >> 4;
             const uint32_t sbo = (uint32_t)p.hw_w * 16;  // one halo row per 8-row group
             const uint32_t bsm32 = smem_u32(bsm);
-            const uint32_t tap_b16 = (uint32_t)p.nchunk * 2 * b16;  // resident B: next tap
+            const uint64_t tap_b16 = (uint64_t)p.nchunk * 2 * b16;  // resident B: next tap
             const int taps = TAPS ? TAPS : p.taps, kw = TAPS ? KW : p.kw, hw_w = TAPS ? KW + TP - 1 : p.hw_w;
             bool ok = !p.b_res || mbar_wait(bres, 0, p.status, abort_flag, 27);
+            // A start offsets (16-byte units) of the hi and lo planes of each 16-channel step
+            uint32_t ahi_off[CG / 16], alo_off[CG / 16];
+#pragma unroll
+            for (int kk = 0; kk < CG / 16; kk++) {
+                ahi_off[kk] = 2 * kk * plane16;
+                alo_off[kk] = (NPL + 2 * kk) * plane16;
+            }
             int sa = 0, pha = 0, sb = 0, phb = 0, lt = 0;
             for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x, lt++) {
                 const int ab = lt % NACC;
@@ -357,45 +364,71 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 26);
                 if (!ok) break;
                 tc_fence_after();
-                int par = 0;
-                uint32_t fresh = 3;  // accumulators not yet written in this tile
-                for (int ch = 0; ch < p.nchunk && ok; ch++) {
-                    ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 23);
-                    if (!ok) break;
-                    tc_fence_after();
-                    const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
-                    const uint64_t dbr = p.b_res ? smem_desc_sw(bsm32 + (uint32_t)(nt * taps * p.nchunk + ch) * 2 * B_BYTES, RB)
-                                                 : 0;
+                if (p.b_res) {
+                    // resident B: the only commits inside a tile end a chunk; chunks alternate
+                    // between the two accumulators, the first two chunks start them
+                    for (int ch = 0; ch < p.nchunk && ok; ch++) {
+                        ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 23);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
+                        uint64_t db = smem_desc_sw(bsm32 + (uint32_t)(nt * taps * p.nchunk + ch) * 2 * B_BYTES, RB);
+                        const uint32_t d = dtile + (ch & 1) * ACCW;
+                        const uint32_t acc0 = ch >= 2 ? 1u : 0u;
 #pragma unroll
-                    for (int tap = 0; tap < (TAPS ? TAPS : 64); tap++) {
-                        if (!TAPS && tap >= taps) break;
-                        uint64_t db;
-                        if (p.b_res) {
-                            db = dbr + (uint64_t)tap * tap_b16;
-                        } else {
+                        for (int tap = 0; tap < (TAPS ? TAPS : 64); tap++) {
+                            if (!TAPS && tap >= taps) break;
+                            const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw);
+#pragma unroll
+                            for (int kk = 0; kk < CG / 16; kk++) {
+                                const uint32_t acc = tap == 0 && kk == 0 ? acc0 : 1u;
+                                if (STACK) {
+                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc2, acc);  // hi . [hi; lo]
+                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);    // lo . hi
+                                } else {
+                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc, acc);
+                                    umma(d, da + ahi_off[kk], db + b16 + 2 * kk, idesc, 1u);
+                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                                }
+                            }
+                            db += tap_b16;
+                        }
+                        umma_commit(&emptyA[sa]);
+                        if (++sa == SA) {
+                            sa = 0;
+                            pha ^= 1;
+                        }
+                    }
+                } else {
+                    // B through the ring: a commit after every tap, which alternates the accumulator
+                    int par = 0;
+                    uint32_t fresh = 3;  // accumulators not yet written in this tile
+                    for (int ch = 0; ch < p.nchunk && ok; ch++) {
+                        ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 23);
+                        if (!ok) break;
+                        tc_fence_after();
+                        const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
+                        for (int tap = 0; tap < taps; tap++) {
                             ok = mbar_wait(&fullB[sb], phb, p.status, abort_flag, 24);
                             if (!ok) break;
                             tc_fence_after();
-                            db = smem_desc_sw(bsm32 + (uint32_t)sb * 2 * B_BYTES, RB);
-                        }
-                        const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw);
-                        const uint32_t d = dtile + par * ACCW;
-                        uint32_t acc = (fresh >> par) & 1 ? 0u : 1u;
-                        fresh &= ~(1u << par);
+                            const uint64_t db = smem_desc_sw(bsm32 + (uint32_t)sb * 2 * B_BYTES, RB);
+                            const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw);
+                            const uint32_t d = dtile + par * ACCW;
+                            uint32_t acc = (fresh >> par) & 1 ? 0u : 1u;
+                            fresh &= ~(1u << par);
 #pragma unroll
-                        for (int kk = 0; kk < CG / 16; kk++) {
-                            const uint64_t ah = da + 2 * kk * plane16, al = da + (NPL + 2 * kk) * plane16;
-                            if (STACK) {
-                                umma(d, ah, db + 2 * kk, idesc2, acc);  // hi . [hi; lo]
-                                umma(d, al, db + 2 * kk, idesc, 1u);    // lo . hi
-                            } else {
-                                umma(d, ah, db + 2 * kk, idesc, acc);
-                                umma(d, ah, db + b16 + 2 * kk, idesc, 1u);
-                                umma(d, al, db + 2 * kk, idesc, 1u);
+                            for (int kk = 0; kk < CG / 16; kk++) {
+                                if (STACK) {
+                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc2, acc);
+                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                                } else {
+                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc, acc);
+                                    umma(d, da + ahi_off[kk], db + b16 + 2 * kk, idesc, 1u);
+                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                                }
+                                acc = 1u;
                             }
-                            acc = 1u;
-                        }
-                        if (!p.b_res) {
                             umma_commit(&emptyB[sb]);
                             par ^= 1;
                             if (++sb == SB) {
@@ -403,13 +436,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 phb ^= 1;
                             }
                         }
-                    }
-                    if (!ok) break;
-                    umma_commit(&emptyA[sa]);
-                    if (p.b_res) par ^= 1;
-                    if (++sa == SA) {
-                        sa = 0;
-                        pha ^= 1;
+                        if (!ok) break;
+                        umma_commit(&emptyA[sa]);
+                        if (++sa == SA) {
+                            sa = 0;
+                            pha ^= 1;
+                        }
                     }
                 }
                 if (ok) umma_commit(&tfull[ab]);
