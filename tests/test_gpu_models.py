@@ -44,6 +44,24 @@ def test_detect_pages_batched_equals_single(detector):
         assert (many[k] == one).all()
 
 
+def test_detect_pages_graph_replay(detector, monkeypatch):
+    """Repeated calls replay captured CUDA graphs (the upload chunks and a last, shorter one);
+    the masks equal those of direct launches, and changing the input between replays is seen."""
+    pages = np.stack([synth.page(30 + k, 700, 560) for k in range(7)])
+    first = detector.detect_pages(pages, 0.5)
+    again = detector.detect_pages(pages, 0.5)
+    assert (first == again).all()
+    other = np.ascontiguousarray(pages[::-1])
+    swapped = detector.detect_pages(other, 0.5)
+    assert (swapped == first[::-1]).all()
+    monkeypatch.setenv("WOCR_NO_GRAPH", "1")
+    direct = detector.detect_pages(pages, 0.5)
+    assert (direct == first).all()
+    monkeypatch.setenv("WOCR_DETECT_CHUNK", "0")
+    whole = detector.detect_pages(pages, 0.5)
+    assert (whole == first).all()
+
+
 def test_detect_prob_map(detector, det_model):
     x = ref.grey_resize(synth.page(5, 1275, 1650)).reshape(1, 1, 800, 600)
     got = detector.detect(x)

@@ -28,15 +28,41 @@ struct Stats {
     int64_t launches = 0;
 };
 
+// One detection pass (detect_pages_dev) captured as a CUDA graph for a given page count, size,
+// threshold and pair of device buffers, then replayed with one launch: the executor's host work
+// (lowering lookups, stream-ordered allocations, twenty-odd launches) is paid at capture only.
+struct DetGraph {
+    int n = 0, w = 0, h = 0;
+    float thr = 0;
+    const uint8_t *rgb = nullptr;
+    uint32_t *mask = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    double flops = 0;
+    int64_t launches = 0;
+    uint64_t used = 0;  // last use (least recently used is replaced)
+    void reset() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+        exec = nullptr;
+        graph = nullptr;
+        n = 0;
+    }
+};
+
 struct wocr_detector {
     wocr_ctx *ctx;
     std::unique_ptr<Executor> graph;
     Stats last;
+    DetGraph graphs[4];
+    uint64_t uses = 0;
+    BufP up_buf[2], mask_buf;  // wocr_detect_pages: upload slots and the mask, kept between calls
     // page uploads of wocr_detect_pages on their own stream, overlapped with detection:
     // ready (buffers allocated), up[slot] (chunk uploaded), done[slot] (chunk detected)
     cudaStream_t copy = nullptr;
     cudaEvent_t ready = nullptr, up[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr};
     ~wocr_detector() {
+        for (auto &g : graphs) g.reset();
         if (copy) cudaStreamDestroy(copy);
         for (cudaEvent_t e : {ready, up[0], up[1], done[0], done[1]})
             if (e) cudaEventDestroy(e);
@@ -195,6 +221,11 @@ int32_t wocr_ctx_create(int32_t device, int32_t lines, wocr_ctx **out) {
         uint64_t thr = UINT64_MAX;
         WOCR_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr));
         h->c.pool = pool;
+        // the device error word of bounded waits, allocated before any graph capture
+        h->c.status_buf = alloc(&h->c, 16);
+        h->c.status = (int *)h->c.status_buf->p;
+        WOCR_CUDA(cudaMemsetAsync(h->c.status, 0, 16, h->c.stream));
+        WOCR_CUDA(cudaStreamSynchronize(h->c.stream));
         *out = h;
     });
 }
@@ -358,12 +389,59 @@ static void detect_pages_dev(wocr_detector *det, const uint8_t *d_rgb, int n, in
     k::mask_up(c, m.p, (int)m.strides[2], m.strides[0], n, vw, vh, w, h, thr, d_mask);
 }
 
+// detect_pages_dev through the detector's graph cache (direct when profiling, or with
+// WOCR_NO_GRAPH set).
+static void detect_pages_run(wocr_detector *det, const uint8_t *d_rgb, int n, int w, int h, float thr,
+                             uint32_t *d_mask) {
+    Ctx *c = &det->ctx->c;
+    if (c->prof || std::getenv("WOCR_NO_GRAPH")) {
+        detect_pages_dev(det, d_rgb, n, w, h, thr, d_mask);
+        return;
+    }
+    DetGraph *g = nullptr;
+    for (auto &e : det->graphs)
+        if (e.exec && e.n == n && e.w == w && e.h == h && e.thr == thr && e.rgb == d_rgb && e.mask == d_mask) g = &e;
+    if (!g) {
+        g = &det->graphs[0];
+        for (auto &e : det->graphs)
+            if (!e.exec || e.used < g->used) g = &e;
+        g->reset();
+        const double f0 = c->flops;
+        const int64_t l0 = c->launches;
+        WOCR_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+        try {
+            detect_pages_dev(det, d_rgb, n, w, h, thr, d_mask);
+        } catch (...) {
+            cudaGraph_t dead = nullptr;
+            cudaStreamEndCapture(c->stream, &dead);
+            if (dead) cudaGraphDestroy(dead);
+            throw;
+        }
+        WOCR_CUDA(cudaStreamEndCapture(c->stream, &g->graph));
+        WOCR_CUDA(cudaGraphInstantiate(&g->exec, g->graph, 0));
+        g->n = n;
+        g->w = w;
+        g->h = h;
+        g->thr = thr;
+        g->rgb = d_rgb;
+        g->mask = d_mask;
+        g->flops = c->flops - f0;
+        g->launches = c->launches - l0;
+        c->flops = f0;
+        c->launches = l0;
+    }
+    g->used = ++det->uses;
+    WOCR_CUDA(cudaGraphLaunch(g->exec, c->stream));
+    c->flops += g->flops;
+    c->launches += g->launches;
+}
+
 int32_t wocr_detect_pages_device(wocr_detector *det, const uint8_t *d_rgb, int32_t n, int32_t w, int32_t h,
                                  float threshold, uint32_t *d_mask_out) {
     return guard([&] {
         if (!det || !d_rgb || !d_mask_out) fail(WOCR_ERR_INVALID, "null argument");
         RunScope rs(&det->ctx->c, &det->last);
-        detect_pages_dev(det, d_rgb, n, w, h, threshold, d_mask_out);
+        detect_pages_run(det, d_rgb, n, w, h, threshold, d_mask_out);
     });
 }
 
@@ -374,7 +452,7 @@ static int detect_chunk(int n) {
         int v = std::atoi(e);
         return v <= 0 ? n : std::min(v, n);
     }
-    return std::max(1, (n + 2) / 3);  // three chunks
+    return std::max(1, (n + 5) / 6);  // six chunks (two pages each for a batch of 12)
 }
 
 int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int32_t w, int32_t h, float threshold,
@@ -391,8 +469,13 @@ int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int
             for (cudaEvent_t *e : {&det->ready, &det->up[0], &det->up[1], &det->done[0], &det->done[1]})
                 WOCR_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
         }
-        BufP src[2], dst = alloc(c, (size_t)n * page_words * 4);
-        for (int b = 0; b < std::min(nchunks, 2); b++) src[b] = alloc(c, (size_t)chunk * page_bytes);
+        // upload slots and the mask persist between calls (stable addresses for the graph cache)
+        for (int b = 0; b < std::min(nchunks, 2); b++)
+            if (!det->up_buf[b] || det->up_buf[b]->bytes < (size_t)chunk * page_bytes)
+                det->up_buf[b] = alloc(c, (size_t)chunk * page_bytes);
+        if (!det->mask_buf || det->mask_buf->bytes < (size_t)n * page_words * 4)
+            det->mask_buf = alloc(c, (size_t)n * page_words * 4);
+        BufP src[2] = {det->up_buf[0], det->up_buf[1]}, dst = det->mask_buf;
         // nothing of the upload stream may still run when the buffers go back to the pool
         struct Drain {
             cudaStream_t s;
@@ -408,7 +491,7 @@ int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int
                                       cudaMemcpyHostToDevice, det->copy));
             WOCR_CUDA(cudaEventRecord(det->up[slot], det->copy));
             WOCR_CUDA(cudaStreamWaitEvent(c->stream, det->up[slot], 0));
-            detect_pages_dev(det, (const uint8_t *)src[slot]->p, kn, w, h, threshold,
+            detect_pages_run(det, (const uint8_t *)src[slot]->p, kn, w, h, threshold,
                              (uint32_t *)dst->p + (size_t)k0 * page_words);
             WOCR_CUDA(cudaEventRecord(det->done[slot], c->stream));
         }

@@ -256,6 +256,98 @@ __global__ void k_conv_direct(const float *__restrict__ x, int64_t x_n, int64_t 
     }
 }
 
+// 3 x 3, Cin = 1 convolution on 16 x 16 tiles of conv outputs (one per block): the input halo
+// in shared memory, weights read 4 output channels at a time; POOL 2 fuses a 2 x 2 MaxPool.
+template <int COUT, int SPLIT, int POOL>
+__global__ void __launch_bounds__(256) k_conv3_cin1(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int n,
+                                                    int h, int w, const float *__restrict__ wt,
+                                                    const float *__restrict__ bias, int pad, int act,
+                                                    void *__restrict__ yv, int64_t y_n, int64_t y_pix, int oh, int ow,
+                                                    int ch, int cw, int tiles_x, int tiles_y, int vec) {
+    __shared__ __align__(16) float ws[9 * COUT];
+    __shared__ float bs[COUT];
+    __shared__ float tile[18][19];
+    __shared__ __align__(16) float pooled[POOL == 2 ? 256 * COUT : 1];
+    for (int i = threadIdx.x; i < 9 * COUT; i += 256) ws[i] = wt[i];
+    for (int i = threadIdx.x; i < COUT; i += 256) bs[i] = bias[i];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    for (int64_t b = blockIdx.x; b < (int64_t)n * tiles_y * tiles_x; b += gridDim.x) {
+        const int bx = (int)(b % tiles_x);
+        const int64_t r = b / tiles_x;
+        const int by = (int)(r % tiles_y), nb = (int)(r / tiles_y);
+        const int cy0 = by * 16, cx0 = bx * 16;
+        const float *xb = x + nb * x_n;
+        __syncthreads();  // the previous tile's readers are done
+        for (int i = threadIdx.x; i < 18 * 18; i += 256) {
+            const int yy = i / 18, xx = i - (i / 18) * 18;
+            const int iy = cy0 + yy - pad, ix = cx0 + xx - pad;
+            tile[yy][xx] = iy >= 0 && iy < h && ix >= 0 && ix < w ? xb[((int64_t)iy * w + ix) * x_pix] : 0.f;
+        }
+        __syncthreads();
+        float acc[COUT];
+#pragma unroll
+        for (int c = 0; c < COUT; c++) acc[c] = bs[c];
+#pragma unroll
+        for (int ky = 0; ky < 3; ky++)
+#pragma unroll
+            for (int kx = 0; kx < 3; kx++) {
+                const float v = tile[ty + ky][tx + kx];
+                const float4 *w4 = reinterpret_cast<const float4 *>(ws + (ky * 3 + kx) * COUT);
+#pragma unroll
+                for (int c4 = 0; c4 < COUT / 4; c4++) {
+                    const float4 q = w4[c4];
+                    acc[4 * c4] += v * q.x;
+                    acc[4 * c4 + 1] += v * q.y;
+                    acc[4 * c4 + 2] += v * q.z;
+                    acc[4 * c4 + 3] += v * q.w;
+                }
+            }
+#pragma unroll
+        for (int c = 0; c < COUT; c++) acc[c] = act_f(acc[c], act);
+        int oy = cy0 + ty, ox = cx0 + tx;
+        bool store = oy < ch && ox < cw;
+        if (POOL == 2) {
+            float4 *ps = reinterpret_cast<float4 *>(pooled + threadIdx.x * COUT);
+#pragma unroll
+            for (int c4 = 0; c4 < COUT / 4; c4++)
+                ps[c4] = make_float4(acc[4 * c4], acc[4 * c4 + 1], acc[4 * c4 + 2], acc[4 * c4 + 3]);
+            __syncthreads();
+            store = false;
+            if (threadIdx.x < 64) {
+                const int py = threadIdx.x >> 3, px = threadIdx.x & 7;
+                oy = by * 8 + py;
+                ox = bx * 8 + px;
+                store = oy < oh && ox < ow;
+                const float *q0 = pooled + ((2 * py) * 16 + 2 * px) * COUT;
+#pragma unroll
+                for (int c = 0; c < COUT; c++)
+                    acc[c] = fmaxf(fmaxf(q0[c], q0[COUT + c]), fmaxf(q0[16 * COUT + c], q0[17 * COUT + c]));
+            }
+        }
+        if (!store) continue;
+        const int64_t off = nb * y_n + ((int64_t)oy * ow + ox) * y_pix;
+        if (SPLIT) {
+            uint16_t *yo = reinterpret_cast<uint16_t *>(yv) + off;
+            if (vec) {
+#pragma unroll
+                for (int c = 0; c < COUT; c += 8) {
+                    uint4 hi, lo;
+                    split8v(acc + c, hi, lo);
+                    *reinterpret_cast<uint4 *>(yo + c) = hi;
+                    *reinterpret_cast<uint4 *>(yo + y_pix / 2 + c) = lo;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < COUT; c++) split1(acc[c], yo[c], yo[y_pix / 2 + c]);
+            }
+        } else {
+            float *yo = reinterpret_cast<float *>(yv) + off;
+#pragma unroll
+            for (int c = 0; c < COUT; c++) yo[c] = acc[c];
+        }
+    }
+}
+
 // Generic-cout direct conv: one thread per (output pixel, channel).
 __global__ void k_conv_direct_any(const float *__restrict__ x, int64_t x_n, int64_t x_pix, int n, int h, int w,
                                   const float *__restrict__ wt, const float *__restrict__ bias, int cout, int kh,
@@ -496,7 +588,32 @@ void conv_direct(Ctx *c, const float *x, int64_t x_n, int64_t x_pix, int n, int 
     if (pix == 0) return;
     Prof pf(c, "conv_direct", 2.0 * (double)pix * ph * pw * cout * kh * kw,
             4.0 * ((double)n * h * w + (double)pix * cout));
-    if (kh * kw <= 49 && (cout == 16 || cout == 32)) {
+    if (kh == 3 && kw == 3 && (cout == 16 || cout == 32) && ph == pw && (ph == 1 || ph == 2)) {
+        // 16 x 16 conv-output tiles in shared memory
+        const int vec = (reinterpret_cast<uintptr_t>(yv) & 15) == 0 && y_pix % 16 == 0 && y_n % 8 == 0;
+        const int cch = h + 2 * pad - 2, ccw = w + 2 * pad - 2;  // conv output before the pool
+        const int tiles_x = (ccw + 15) / 16, tiles_y = (cch + 15) / 16;
+        const int64_t blocks = (int64_t)n * tiles_x * tiles_y;
+        const int grid = (int)std::min<int64_t>(blocks, (int64_t)c->sm_count * 8);
+        auto go = [&](auto co_tag, auto split_tag, auto pool_tag) {
+            constexpr int CO = decltype(co_tag)::value, SP = decltype(split_tag)::value,
+                          PL = decltype(pool_tag)::value;
+            k_conv3_cin1<CO, SP, PL><<<grid, 256, 0, c->stream>>>(x, x_n, x_pix, n, h, w, wt, bias, pad, act, yv, y_n,
+                                                                  y_pix, oh, ow, cch, ccw, tiles_x, tiles_y, vec);
+        };
+        using I1 = std::integral_constant<int, 1>;
+        using I0 = std::integral_constant<int, 0>;
+        using I2 = std::integral_constant<int, 2>;
+        using C16 = std::integral_constant<int, 16>;
+        using C32 = std::integral_constant<int, 32>;
+        if (cout == 16) {
+            if (ph == 1) split_out ? go(C16(), I1(), I1()) : go(C16(), I0(), I1());
+            else split_out ? go(C16(), I1(), I2()) : go(C16(), I0(), I2());
+        } else {
+            if (ph == 1) split_out ? go(C32(), I1(), I1()) : go(C32(), I0(), I1());
+            else split_out ? go(C32(), I1(), I2()) : go(C32(), I0(), I2());
+        }
+    } else if (kh * kw <= 49 && (cout == 16 || cout == 32)) {
         const int vec = (reinterpret_cast<uintptr_t>(yv) & 15) == 0 && y_pix % 16 == 0 && y_n % 8 == 0;
         auto go = [&](auto co_tag, auto split_tag) {
             constexpr int CO = decltype(co_tag)::value, SP = decltype(split_tag)::value;
