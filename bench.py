@@ -58,6 +58,50 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
+def traffic_per_launch(kernel: str):
+    """DRAM bytes per launch of `kernel` (dram__bytes_read.sum + dram__bytes_write.sum averaged
+    over one step's launches) from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "tconv_config1.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic per launch (bytes):"):
+                for item in line.split(":", 1)[1].split():
+                    name, _, val = item.partition("=")
+                    if name == kernel:
+                        return float(val)
+    except OSError:
+        pass
+    return None
+
+
+def roofline(top, total_ms: float):
+    """Roofline of the dominant kernel: algorithmic FLOPs and bytes per launch over its average
+    launch time (CUDA events).  The bound is the resource whose peak would take longer for that
+    work (HBM at the measured copy bandwidth, or the tensor cores at the measured dense bf16
+    rate); the other one is reported beside it."""
+    pk = peaks()
+    n = max(top["launches"], 1)
+    t = top["ms"] / n / 1e3
+    flops, nbytes = top["flops"] / n, top["bytes"] / n
+    hbm = {"achieved": nbytes / t / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s"}
+    hbm["frac"] = hbm["achieved"] / hbm["peak"]
+    ten = {"achieved": flops / t / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s"}
+    ten["frac"] = ten["achieved"] / ten["peak"]
+    t_hbm = nbytes / (pk["hbm_gbs"] * 1e9)
+    t_ten = flops / (pk["bf16_tflops"] * 1e12)
+    if flops > 0 and t_ten > t_hbm:
+        roof, other, oname = dict(bound="tensor", **ten), hbm, "hbm"
+        src = " (dense bf16 cuBLAS burst)"
+    else:
+        roof, other, oname = dict(bound="hbm", **hbm), ten, "tensor"
+        src = " (copy bandwidth)"
+    tr = traffic_per_launch(top["kernel"])
+    roof.update({"traffic": tr, "kernel": top["kernel"], "share": top["ms"] / total_ms,
+                 "algorithmic_bytes_per_launch": nbytes, "algorithmic_flops_per_launch": flops,
+                 "peak_source": pk["src"] + src, oname: other})
+    return roof
+
+
 class Clocks:
     """SM clock and throttle reasons of this process's GPU, sampled every 200 ms by NVML in a
     thread while the timed region runs (nvidia-smi's own 100 ms loop over every GPU of the box
@@ -120,9 +164,11 @@ def dist():
 
 
 def make_pages(rank: int, n: int):
+    """This rank's pages (weak scaling: n per rank, global page g from seed 1000 + g)."""
     import numpy as np
     from wocr import synth
-    return np.stack([synth.page(1000 * (rank + 1) + k, W_PAGE, H_PAGE) for k in range(n)])
+    from wocr.shard import weak_pages_of
+    return np.stack([synth.page(1000 + g, W_PAGE, H_PAGE) for g in weak_pages_of(rank, n)])
 
 
 def cpu_baseline(sample: int):
@@ -199,17 +245,14 @@ def run_b200(args):
     def step():
         det.detect_pages_device(d_rgb.data_ptr(), B, W_PAGE, H_PAGE, THRESHOLD, d_mask.data_ptr())
 
+    from wocr import shard
+
     def barrier():
-        if world > 1:
-            tdist.barrier(device_ids=[local])
+        shard.barrier(local)
         torch.cuda.synchronize(dev)
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(v, dev)
 
     # ---- device-resident throughput --------------------------------------------------
     for _ in range(max(args.warmup, 3)):
@@ -245,19 +288,7 @@ def run_b200(args):
     gpu.profile(False)
     total_ms = sum(r["ms"] for r in rep) or 1.0
     top = max(rep, key=lambda r: r["ms"])
-    pk = peaks()
-    per_launch_ms = top["ms"] / top["launches"]
-    if top["flops"] > 0:
-        achieved = (top["flops"] / top["launches"]) / (per_launch_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / pk["bf16_tflops"]}
-    else:
-        achieved = (top["bytes"] / top["launches"]) / (per_launch_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"]}
-    roof.update({"kernel": top["kernel"], "share": top["ms"] / total_ms, "traffic": None,
-                 "peak_source": pk["src"] + (" (dense bf16 cuBLAS burst)" if roof["bound"] == "tensor" else
-                                             " (copy bandwidth)")})
+    roof = roofline(top, total_ms)
     kernels = {r["kernel"]: {"launches": r["launches"] // psteps, "ms_per_step": r["ms"] / psteps,
                              "share": r["ms"] / total_ms} for r in rep}
 
