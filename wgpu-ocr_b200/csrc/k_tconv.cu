@@ -39,7 +39,7 @@ using namespace tc;
 constexpr int kProd = 4, kEpi0 = 4, kEpiWarps = 8, kTmaW = 12, kMmaW = 13, kThreads = 448;
 constexpr int kLagMax = 4;        // cp.async stages in flight per producer thread
 constexpr int kSmemBudget = 212 * 1024;  // stages and B; barriers and bias after it
-constexpr int TP = 8, TR = 16;    // tile: TR image rows of TP pixels (an 8-row group per image row)
+constexpr int TP = 8, TR = 16;    // an MMA block: TR image rows of TP pixels (an 8-row group per image row)
 
 struct TcP {
     const uint16_t *x;
@@ -47,6 +47,7 @@ struct TcP {
     int h, w, cin;
     int n, oh, ow;              // GEMM output grid (ConvTranspose: its input grid)
     int tiles_x, tiles_y, ntn;
+    int trows;                  // image rows of a tile: TR * MB
     int ntiles;                 // < 2^31 (checked on the host)
     FastDiv div_ntn, div_tx, div_ty;
     int N, nchunk, taps, kw, pt, pl, cin_pad;
@@ -77,7 +78,7 @@ __device__ __forceinline__ Tile decode(const TcP &p, int t) {
     const uint32_t q1 = p.div_ntn.div((uint32_t)t), q2 = p.div_tx.div(q1), q3 = p.div_ty.div(q2);
     r.nt = t - (int)(q1 * p.div_ntn.d);
     r.ox0 = (int)(q1 - q2 * p.div_tx.d) * TP;
-    r.oy0 = (int)(q2 - q3 * p.div_ty.d) * TR;
+    r.oy0 = (int)(q2 - q3 * p.div_ty.d) * p.trows;
     r.nb = (int)q3;
     return r;
 }
@@ -158,14 +159,17 @@ __device__ __forceinline__ void store16(const TcP &p, int64_t off, const float (
 }
 
 // TAPS: 9 (3 x 3 kernel), 1 (1 x 1) or 0 (any kernel, taps counted at run time).
-template <int BN, int CG, int TAPS>
+// MB: 128-pixel MMA blocks per tile (2 for the narrow layers: one halo, the per-tile waits and
+// commits shared by 256 pixels).
+template <int BN, int CG, int TAPS, int MB>
 __global__ void __launch_bounds__(kThreads, 1)
     k_tconv(const __grid_constant__ CUtensorMap wb_hi, const __grid_constant__ CUtensorMap wb_lo, TcP p) {
     constexpr int RB = CG * 2;                 // bytes of one B row
     constexpr uint32_t B_BYTES = BN * RB;      // B hi (or lo) of one tap chunk
     constexpr int NPL = CG / 8;                // 8-channel planes per split part
-    constexpr int PPP = 2 * NPL;               // 16-byte pieces per halo pixel
-    constexpr int PXS = kProd * 32 / PPP;      // halo pixels per pass of the producer threads
+    // BN = 16: one 16-column chunk per tile, so the two halves of the epilogue take alternate
+    // tiles instead of alternate chunks
+    constexpr bool TSPLIT = BN == 16 && MB == 1;
     // STACK (BN <= 64): B hi and lo are one 2 BN-row operand, so one MMA of N = 2 BN (no slower
     // than N = BN up to 128) gives hi.hi in columns [0, BN) and hi.lo in [BN, 2 BN), and a second
     // MMA adds lo.hi to [0, BN): two MMAs per 16-channel step instead of three.
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int ACCW = STACK ? 2 * BN : BN;  // columns of one accumulator
     // accumulator buffers in tensor memory: NACC tiles of two accumulators each (the MMAs after a
     // commit inside a tile go to the other one, so they never wait on the committed ones)
-    constexpr int TCOLS = 2 * ACCW;
+    constexpr int TCOLS = MB * 2 * ACCW;
     constexpr int NACC = 512 / TCOLS < 8 ? 512 / TCOLS : 8;
     constexpr int KW = TAPS == 9 ? 3 : 1;       // kernel width when TAPS is fixed
     constexpr uint32_t kCols = NACC * TCOLS <= 32 ? 32 : (NACC * TCOLS <= 64 ? 64 : (NACC * TCOLS <= 128 ? 128 : (NACC * TCOLS <= 256 ? 256 : 512)));
@@ -206,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < NACC; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], kEpiWarps);
+            mbar_init(&tempty[a], TSPLIT ? kEpiWarps / 2 : kEpiWarps);
         }
         mbar_init(drain, 1);
         mbar_init(bres, 1);
@@ -226,43 +230,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp < kProd) {
         // ---------------- halo producers ----------------
-        // thread: one 16-byte piece (split part, plane) of one halo column, every rstep-th halo
-        // row; consecutive threads take consecutive pieces of a pixel, then consecutive pixels
-        // (coalesced).  Threads past rstep * hw_w pixel slots idle.
-        const int piece = threadIdx.x % PPP, part = piece / NPL, jpl = piece % NPL;
-        const int slot = threadIdx.x / PPP, rstep = PXS / p.hw_w;
-        const int col = slot % p.hw_w, row0 = slot / p.hw_w;
-        const bool active = slot < rstep * p.hw_w;
-        const int halo_h = p.halo_px / p.hw_w;
-        const int64_t part_off = part ? p.x_pix / 2 : 0;
-        const int64_t row_step = (int64_t)rstep * p.w * p.x_pix;
-        const uint32_t dst_step = (uint32_t)(rstep * p.hw_w * 16);
+        // thread: whole halo pixels hp = threadIdx.x + 128 i (all 2 NPL 16-byte pieces, hi then
+        // lo, each to its plane); consecutive threads take consecutive pixels (coalesced), the
+        // pixel slots' halo coordinates are fixed for the launch
+        constexpr int kSlots = 4;  // halo pixels per thread (halo_px <= 512, checked on the host)
+        int sy[kSlots], sx[kSlots];
+#pragma unroll
+        for (int i = 0; i < kSlots; i++) {
+            const int hp = threadIdx.x + i * kProd * 32;
+            sy[i] = hp < p.halo_px ? hp / p.hw_w : -1;  // -1: no pixel
+            sx[i] = hp < p.halo_px ? hp - (hp / p.hw_w) * p.hw_w : 0;
+        }
+        const int64_t xlo = p.x_pix / 2;
         int s = 0, ph = 0, sa = 0, inflight = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
             const Tile tl = decode(p, t);
-            const int iy0 = tl.oy0 - p.pt + row0, ix = tl.ox0 - p.pl + col;
-            const bool colv = active && ix >= 0 && ix < p.w;
-            const uint16_t *xrow = p.x + (int64_t)tl.nb * p.x_n + part_off + ((int64_t)iy0 * p.w + ix) * p.x_pix;
+            const int iy0 = tl.oy0 - p.pt, ix0 = tl.ox0 - p.pl;
+            const uint16_t *xb = p.x + (int64_t)tl.nb * p.x_n;
             for (int ch = 0; ch < p.nchunk; ch++) {
                 if (!warp_wait(&emptyA[s], ph ^ 1, p.status, abort_flag, 21)) {
                     ok = false;
                     break;
                 }
-                const int c = ch * CG + jpl * 8;
-                const int left = (p.cin - c) * 2;
-                const uint32_t cbytes = left <= 0 ? 0u : (left < 16 ? (uint32_t)left : 16u);
-                if (active) {
-                    uint8_t *dst = smem + (uint32_t)s * p.a_stage + (uint32_t)(part * NPL + jpl) * p.plane +
-                                   (uint32_t)(row0 * p.hw_w + col) * 16;
-                    const uint16_t *src = xrow + c;
-                    int iy = iy0;
-                    for (int hy = row0; hy < halo_h; hy += rstep) {
-                        const bool v = colv && cbytes && iy >= 0 && iy < p.h;
-                        cp_async16(dst, v ? src : p.x, v ? cbytes : 0u);
-                        dst += dst_step;
-                        src += row_step;
-                        iy += rstep;
+                uint8_t *a = smem + (uint32_t)s * p.a_stage;
+#pragma unroll
+                for (int i = 0; i < kSlots; i++) {
+                    if (sy[i] < 0) continue;
+                    const int iy = iy0 + sy[i], ix = ix0 + sx[i];
+                    const bool v = iy >= 0 && iy < p.h && ix >= 0 && ix < p.w;
+                    const uint16_t *src = v ? xb + ((int64_t)iy * p.w + ix) * p.x_pix + ch * CG : p.x;
+                    uint8_t *dst = a + (uint32_t)(threadIdx.x + i * kProd * 32) * 16;
+#pragma unroll
+                    for (int j = 0; j < NPL; j++) {
+                        const int left = (p.cin - (ch * CG + j * 8)) * 2;
+                        const uint32_t nb = v && left > 0 ? (left < 16 ? (uint32_t)left : 16u) : 0u;
+                        cp_async16(dst + (uint32_t)j * p.plane, nb ? src + j * 8 : p.x, nb);
+                        cp_async16(dst + (uint32_t)(NPL + j) * p.plane, nb ? src + xlo + j * 8 : p.x, nb);
                     }
                 }
                 cp_async_commit();
@@ -345,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t idesc = instr_desc(BN), idesc2 = instr_desc(STACK ? 2 * BN : BN);
             const uint32_t plane16 = p.plane >> 4, b16 = B_BYTES >> 4;
             const uint32_t sbo = (uint32_t)p.hw_w * 16;  // one halo row per 8-row group
+            const uint32_t blk16 = (uint32_t)(TR * p.hw_w);  // next MMA block: TR halo rows further
             const uint32_t bsm32 = smem_u32(bsm);
             const uint64_t tap_b16 = (uint64_t)p.nchunk * 2 * b16;  // resident B: next tap
             const int taps = TAPS ? TAPS : p.taps, kw = TAPS ? KW : p.kw, hw_w = TAPS ? KW + TP - 1 : p.hw_w;
@@ -378,17 +383,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int tap = 0; tap < (TAPS ? TAPS : 64); tap++) {
                             if (!TAPS && tap >= taps) break;
-                            const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw);
 #pragma unroll
-                            for (int kk = 0; kk < CG / 16; kk++) {
-                                const uint32_t acc = tap == 0 && kk == 0 ? acc0 : 1u;
-                                if (STACK) {
-                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc2, acc);  // hi . [hi; lo]
-                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);    // lo . hi
-                                } else {
-                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc, acc);
-                                    umma(d, da + ahi_off[kk], db + b16 + 2 * kk, idesc, 1u);
-                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                            for (int b = 0; b < MB; b++) {
+                                const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw) + b * blk16;
+                                const uint32_t db_d = d + b * 2 * ACCW;
+#pragma unroll
+                                for (int kk = 0; kk < CG / 16; kk++) {
+                                    const uint32_t acc = tap == 0 && kk == 0 ? acc0 : 1u;
+                                    if (STACK) {
+                                        umma(db_d, da + ahi_off[kk], db + 2 * kk, idesc2, acc);  // hi . [hi; lo]
+                                        umma(db_d, da + alo_off[kk], db + 2 * kk, idesc, 1u);    // lo . hi
+                                    } else {
+                                        umma(db_d, da + ahi_off[kk], db + 2 * kk, idesc, acc);
+                                        umma(db_d, da + ahi_off[kk], db + b16 + 2 * kk, idesc, 1u);
+                                        umma(db_d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                                    }
                                 }
                             }
                             db += tap_b16;
@@ -413,21 +422,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (!ok) break;
                             tc_fence_after();
                             const uint64_t db = smem_desc_sw(bsm32 + (uint32_t)sb * 2 * B_BYTES, RB);
-                            const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw);
                             const uint32_t d = dtile + par * ACCW;
-                            uint32_t acc = (fresh >> par) & 1 ? 0u : 1u;
+                            const uint32_t acc0 = (fresh >> par) & 1 ? 0u : 1u;
                             fresh &= ~(1u << par);
 #pragma unroll
-                            for (int kk = 0; kk < CG / 16; kk++) {
-                                if (STACK) {
-                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc2, acc);
-                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
-                                } else {
-                                    umma(d, da + ahi_off[kk], db + 2 * kk, idesc, acc);
-                                    umma(d, da + ahi_off[kk], db + b16 + 2 * kk, idesc, 1u);
-                                    umma(d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                            for (int b = 0; b < MB; b++) {
+                                const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw) + b * blk16;
+                                const uint32_t db_d = d + b * 2 * ACCW;
+                                uint32_t acc = acc0;
+#pragma unroll
+                                for (int kk = 0; kk < CG / 16; kk++) {
+                                    if (STACK) {
+                                        umma(db_d, da + ahi_off[kk], db + 2 * kk, idesc2, acc);
+                                        umma(db_d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                                    } else {
+                                        umma(db_d, da + ahi_off[kk], db + 2 * kk, idesc, acc);
+                                        umma(db_d, da + ahi_off[kk], db + b16 + 2 * kk, idesc, 1u);
+                                        umma(db_d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
+                                    }
+                                    acc = 1u;
                                 }
-                                acc = 1u;
                             }
                             umma_commit(&emptyB[sb]);
                             par ^= 1;
@@ -456,9 +470,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- epilogue: warps 4-11, lane quadrant warp % 4, column half ----------------
         const int q = warp & 3, half = (warp - kEpi0) >> 2;
         const int row = q * 32 + lane;
-        const int r = row / TP, pc = row % TP;
+        // MB = 2: half h takes MMA block h (image rows 16 h .. 16 h + 15 of the tile), all columns
+        const int blk = MB == 2 ? half : 0;
+        const int r = row / TP + TR * blk, pc = row % TP;
         int lt = 0;
         for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, lt++) {
+            if (TSPLIT && (lt & 1) != half) continue;
             const int ab = lt % NACC;
             if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 25)) break;
             tc_fence_after();
@@ -466,9 +483,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int oy = tl.oy0 + r, ox = tl.ox0 + pc;
             const bool valid = oy < p.oh && ox < p.ow;
 #pragma unroll 1
-            for (int c0 = half * 16; c0 < BN; c0 += 32) {
+            for (int c0 = TSPLIT || MB == 2 ? 0 : half * 16; c0 < BN; c0 += TSPLIT || MB == 2 ? 16 : 32) {
                 float v[16];
-                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + c0;
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + blk * 2 * ACCW + c0;
                 if (STACK) {
                     if (p.two_acc) tmem_ld16_sum4(tbase, tbase + BN, tbase + ACCW, tbase + ACCW + BN, v);
                     else tmem_ld16_sum2(tbase, tbase + BN, v);
@@ -540,25 +557,27 @@ void encode(CUtensorMap *map, int rank, void *base, const cuuint64_t *dims, cons
     if (r != CUDA_SUCCESS) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 
-template <int BN, int CG, int TAPS>
+template <int BN, int CG, int TAPS, int MB>
 void launch(Ctx *c, const TconvW &w, const TcP &p, int smem) {
     static bool set[64] = {false};
     if (!set[c->device]) {
-        WOCR_CUDA(cudaFuncSetAttribute(k_tconv<BN, CG, TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        WOCR_CUDA(cudaFuncSetAttribute(k_tconv<BN, CG, TAPS, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024));
         set[c->device] = true;
     }
     unsigned grid = (unsigned)std::min<int64_t>(p.ntiles, c->sm_count);
-    k_tconv<BN, CG, TAPS><<<grid, kThreads, smem, c->stream>>>(w.map_hi, w.map_lo, p);
+    k_tconv<BN, CG, TAPS, MB><<<grid, kThreads, smem, c->stream>>>(w.map_hi, w.map_lo, p);
     WOCR_LAUNCHED(c);
 }
 
 template <int CG, int TAPS>
 void launch_bn(Ctx *c, const TconvW &w, const TcP &p, int smem) {
+    const bool two = p.trows == 2 * TR;
     switch (w.bn) {
-    case 16: launch<16, CG, TAPS>(c, w, p, smem); break;
-    case 32: launch<32, CG, TAPS>(c, w, p, smem); break;
-    case 64: launch<64, CG, TAPS>(c, w, p, smem); break;
-    default: launch<128, CG, TAPS>(c, w, p, smem); break;
+    case 16: two ? launch<16, CG, TAPS, 2>(c, w, p, smem) : launch<16, CG, TAPS, 1>(c, w, p, smem); break;
+    case 32: two ? launch<32, CG, TAPS, 2>(c, w, p, smem) : launch<32, CG, TAPS, 1>(c, w, p, smem); break;
+    case 64: launch<64, CG, TAPS, 1>(c, w, p, smem); break;
+    default: launch<128, CG, TAPS, 1>(c, w, p, smem); break;
     }
 }
 
@@ -635,8 +654,11 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.n = q.n;
     p.oh = q.oh;
     p.ow = q.ow;
+    // two MMA blocks per tile for the narrow layers when there are tiles to spare
+    const int mb = w.bn <= 32 && (int64_t)q.n * q.oh * q.ow >= (int64_t)c->sm_count * 256 * 8 ? 2 : 1;
+    p.trows = TR * mb;
     p.tiles_x = (q.ow + TP - 1) / TP;
-    p.tiles_y = (q.oh + TR - 1) / TR;
+    p.tiles_y = (q.oh + p.trows - 1) / p.trows;
     p.ntn = (w.N + w.bn - 1) / w.bn;
     const int64_t ntiles = (int64_t)q.n * p.tiles_x * p.tiles_y * p.ntn;
     if (ntiles >= (int64_t)INT32_MAX) fail(WOCR_ERR_UNSUPPORTED, "tap convolution with 2^31 tiles or more");
@@ -652,8 +674,8 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.pl = q.pl;
     p.cin_pad = w.cin_pad;
     p.hw_w = TP + q.kw - 1;
-    if (p.hw_w > 128 / (4 * w.cg / 16)) fail(WOCR_ERR_UNSUPPORTED, "tap convolution kernel too wide");
-    p.halo_px = (TR + q.kh - 1) * p.hw_w;
+    if ((p.trows + q.kh - 1) * p.hw_w > 512) fail(WOCR_ERR_UNSUPPORTED, "tap convolution kernel too large");
+    p.halo_px = (p.trows + q.kh - 1) * p.hw_w;
     p.plane = (uint32_t)p.halo_px * 16;
     p.a_stage = (2 * (w.cg / 8) * p.plane + 1023) / 1024 * 1024;
 
