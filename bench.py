@@ -46,6 +46,9 @@ def parse():
     p.add_argument("--pages", type=int, default=12, help="pages per GPU per step")
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
+    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4"],
+                   help="det1 (default, the driver's line): config 1 detection; rec0 / pp3 / ppdet4: configs "
+                        "0, 3 and 4 through their public calls (secondary measurements)")
     return p.parse_args()
 
 
@@ -74,7 +77,7 @@ def traffic_per_launch(kernel: str):
     return None
 
 
-def roofline(top, total_ms: float):
+def roofline(top, total_ms: float, with_traffic: bool = True):
     """Roofline of the dominant kernel: algorithmic FLOPs and bytes per launch over its average
     launch time (CUDA events).  The bound is the resource whose peak would take longer for that
     work (HBM at the measured copy bandwidth, or the tensor cores at the measured dense bf16
@@ -95,7 +98,7 @@ def roofline(top, total_ms: float):
     else:
         roof, other, oname = dict(bound="hbm", **hbm), ten, "tensor"
         src = " (copy bandwidth)"
-    tr = traffic_per_launch(top["kernel"])
+    tr = traffic_per_launch(top["kernel"]) if with_traffic else None
     roof.update({"traffic": tr, "kernel": top["kernel"], "share": top["ms"] / total_ms,
                  "algorithmic_bytes_per_launch": nbytes, "algorithmic_flops_per_launch": flops,
                  "peak_source": pk["src"] + src, oname: other})
@@ -345,10 +348,125 @@ def run_b200(args):
     return 0
 
 
+def run_workload(args):
+    """Configs 0, 3 and 4 through the public calls a user makes (host inputs, as the reference's
+    Recognizer::recognize, NdGraph::run + argmax and the PP detection page take them).  `value`:
+    units over the context stream's busy time (CUDA events; the H2D copies the call makes are
+    inside); `e2e`: the same over wall-clock time of the calls."""
+    import numpy as np
+    import torch
+
+    import wocr
+    from oracle import ref
+    from wocr import synth
+
+    world, rank, local = dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    gpu = wocr.Gpu(lines=8, device=local)
+    stream = torch.cuda.ExternalStream(gpu.stream, device=dev)
+    ref.set_threads(os.cpu_count() or 1)
+    if args.workload == "rec0":
+        model = synth.ocrs_rec_model()
+        batches, _, _ = synth.ocrs_batches(synth.ocrs_lines(0, n=64))
+        handle = wocr.Recognizer(gpu, model)
+        units, unit, workload = 64, "lines/s", ("config 0: ocrs recognition, 64 lines 1x64xW (W ~ U{64..1024}), "
+                                                "conv trunk + 2-layer biGRU(256) + Linear 512->97, seed 0")
+        tmax, ntot, classes = handle.dims(batches)
+        h2d = sum(b[0].nbytes for b in batches)
+        d2h = tmax * ntot * (classes + 1) * 4
+
+        def step():
+            handle.recognize(batches, want_logits=True)
+
+        sample = batches[:1]
+
+        def cpu():
+            ref.recognize(model, sample)
+            return sum(b[1] for b in sample), f"{sum(b[1] for b in sample)} lines (the first width bucket)"
+    elif args.workload == "pp3":
+        model = synth.pp_rec_model()
+        batches, _ = synth.pp_batches(synth.pp_lines(2, n=256))
+        handle = wocr.NdGraph(gpu, model, stop_before_softmax=True)
+        units, unit, workload = 256, "lines/s", ("config 3: PP-OCRv6-style recognition, 256 lines 3x48xW "
+                                                 "(W ~ U{96..1280}), trunk + 2 SVTR blocks + CTC head 120->18709, "
+                                                 "seed 2, arg-max per step")
+        h2d = sum(b[0].nbytes for b in batches)
+        d2h = sum(b[1] * (b[2] // 8) * 12 for b in batches)
+
+        def step():
+            for data, _, _ in batches:
+                handle.argmax(data)
+
+        def cpu():
+            data, n, _ = batches[0]
+            logits = ref.run_onnx(model, data, stop_before_softmax=True)
+            ref.argmax(logits.reshape(-1, logits.shape[-1]))
+            return n, f"{n} lines (the narrowest batch)"
+    else:
+        model = synth.pp_det_model()
+        page = synth.page(3, W_PAGE, H_PAGE)
+        handle = wocr.NdGraph(gpu, model)
+        units, unit, workload = 1, "pages/s", ("config 4 detection: PP-OCRv6-style DB detector on a 2550x3300 "
+                                               "page resized to 3x960x736, seed 3, probability map read back")
+        h2d, d2h = page.nbytes, 960 * 736 * 4
+
+        def step():
+            handle.ppdet_page(page, W_PAGE, H_PAGE, 960)
+
+        def cpu():
+            x, _ = ref.det_input(page, 960)
+            ref.run_onnx(model, x)
+            return 1, "1 page"
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    gpu.submit_wait()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = gpu.launches()
+    e0.record(stream)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    wall = time.perf_counter() - t0
+    launches = gpu.launches() - l0
+    ms = e0.elapsed_time(e1)
+    gpu.profile(True)
+    step()
+    rep = gpu.profile_report()
+    gpu.profile(False)
+    total_ms = sum(r["ms"] for r in rep) or 1.0
+    top = max(rep, key=lambda r: r["ms"])
+    roof = roofline(top, total_ms, with_traffic=False)  # the committed ncu traffic is config 1's
+    cpu_v = None
+    if rank == 0:
+        c0 = time.perf_counter()
+        n, what = cpu()
+        dt = time.perf_counter() - c0
+        cpu_v = {"value": n / dt, "unit": unit, "cores": ref.threads(), "kind": "port",
+                 "sample": f"{what} through the CPU oracle, {dt:.2f} s"}
+        line = {"metric": unit, "value": units * args.steps / (ms / 1e3), "unit": unit, "n_gpus": 1,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic", "config": {"workload": workload, "units_per_step": units},
+                "e2e": {"value": units * args.steps / wall, "unit": unit, "h2d_bytes_per_step": int(h2d),
+                        "d2h_bytes_per_step": int(d2h)},
+                "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu_v,
+                "kernels": {r["kernel"]: {"launches": r["launches"], "ms_per_step": r["ms"],
+                                          "share": r["ms"] / total_ms} for r in rep}}
+        print(json.dumps(line), flush=True)
+    handle.close()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload != "det1":
+        return run_workload(args)
     return run_b200(args)
 
 

@@ -143,3 +143,45 @@ def test_pp_detection(gpu):
     want = ref.run_onnx(m, rx)[0, 0]
     assert prob.shape == want.shape
     assert np.abs(prob - want).max() < 1e-4
+
+
+def test_ndgraph_replay(gpu, pp_model, monkeypatch):
+    """NdGraph calls of a known shape replay a captured CUDA graph (run, arg-max and the PP
+    detection page): the results equal direct runs, and new input values are seen."""
+    from wocr.synth import _Builder, _svtr_block
+    b = _Builder(21)
+    y = b.linear(b.layer_norm(_svtr_block(b, "x"), 120), 120, 37)
+    m = b.model("x", y)
+    rng = np.random.default_rng(5)
+    x1 = rng.standard_normal((2, 9, 120)).astype(np.float32)
+    x2 = rng.standard_normal((2, 9, 120)).astype(np.float32)
+    g = wocr.NdGraph(gpu, m)
+    try:
+        outs = [g.run(x) for x in (x1, x1, x2, x1)]          # direct, capture, replay, replay
+    finally:
+        g.close()
+    assert (outs[0] == outs[1]).all() and (outs[0] == outs[3]).all()
+    assert np.abs(outs[2] - ref.run_onnx(m, x2)).max() < 2e-4 * max(1.0, float(np.abs(outs[2]).max()))
+
+    data = synth.pp_batches(synth.pp_lines(2, n=16))[0][0][0]
+    g = wocr.NdGraph(gpu, pp_model, stop_before_softmax=True)
+    try:
+        r1, r2, r3 = (g.argmax(data) for _ in range(3))
+    finally:
+        g.close()
+    for a, b2 in ((r1, r2), (r1, r3)):
+        assert all((u == v).all() for u, v in zip(a[:3], b2[:3])) and a[3] == b2[3]
+
+    det = synth.pp_det_model()
+    page = synth.page(4, 1275, 1650)
+    g = wocr.NdGraph(gpu, det)
+    try:
+        p1, _ = g.ppdet_page(page, 1275, 1650, 960)
+        p2, _ = g.ppdet_page(page, 1275, 1650, 960)
+        other = synth.page(9, 1275, 1650)
+        p3, _ = g.ppdet_page(other, 1275, 1650, 960)
+        monkeypatch.setenv("WOCR_NO_GRAPH", "1")
+        p4, _ = g.ppdet_page(other, 1275, 1650, 960)
+    finally:
+        g.close()
+    assert (p1 == p2).all() and (p3 == p4).all()

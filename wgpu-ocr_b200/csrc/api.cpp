@@ -87,10 +87,43 @@ struct wocr_recognizer {
     Stats last;
 };
 
+// One NdGraph call for one input shape, replayed from a CUDA graph: the input is uploaded into a
+// persistent buffer, the captured run writes persistent outputs (the full output, or the row
+// arg-max with its maximum and log-sum-exp).  The first call of a shape runs directly and
+// records the output shape; the second captures.
+struct NdReplay {
+    std::vector<int64_t> in_shape, out_shape;
+    int mode = -1;  // 0 wocr_ndgraph_run, 1 wocr_ndgraph_run_argmax
+    int64_t rows = 0, len = 0;
+    BufP in, out, best, mx, lse;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    double flops = 0;
+    int64_t launches = 0;
+    uint64_t used = 0;
+    void reset() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+        exec = nullptr;
+        graph = nullptr;
+        mode = -1;
+        in.reset();
+        out.reset();
+        best.reset();
+        mx.reset();
+        lse.reset();
+    }
+};
+
 struct wocr_ndgraph {
     wocr_ctx *ctx;
     std::unique_ptr<Executor> graph;
     Stats last;
+    NdReplay replays[8];
+    uint64_t uses = 0;
+    ~wocr_ndgraph() {
+        for (auto &r : replays) r.reset();
+    }
 };
 
 namespace {
@@ -787,19 +820,118 @@ static void put_shape(const DT &t, int64_t *out_shape, int32_t *out_rank) {
         for (int d = 0; d < t.rank(); d++) out_shape[d] = t.shape[d];
 }
 
+// The replay entry of (shape, mode), or null on a first call (which then records one).
+static NdReplay *nd_replay(wocr_ndgraph *g, const std::vector<int64_t> &shape, int mode, bool *first) {
+    *first = false;
+    if (g->ctx->c.prof || std::getenv("WOCR_NO_GRAPH")) return nullptr;
+    for (auto &r : g->replays)
+        if (r.mode == mode && r.in_shape == shape) {
+            r.used = ++g->uses;
+            return &r;
+        }
+    NdReplay *r = &g->replays[0];
+    for (auto &e : g->replays)
+        if (e.mode < 0 || e.used < r->used) r = &e;
+    r->reset();
+    r->mode = mode;
+    r->in_shape = shape;
+    r->used = ++g->uses;
+    *first = true;
+    return r;
+}
+
+// Capture the run (+ arg-max) from r->in into r's persistent outputs, once.
+static void nd_capture(wocr_ndgraph *g, NdReplay *r) {
+    if (r->exec) return;
+    Ctx *c = &g->ctx->c;
+    int64_t n = 1;
+    for (auto d : r->in_shape) n *= d;
+    r->in = alloc(c, (size_t)n * 4);
+    if (r->mode == 0) {
+        int64_t m = 1;
+        for (auto d : r->out_shape) m *= d;
+        r->out = alloc(c, (size_t)std::max<int64_t>(m, 1) * 4);
+    } else {
+        r->best = alloc(c, (size_t)r->rows * 4);
+        r->mx = alloc(c, (size_t)r->rows * 4);
+        r->lse = alloc(c, (size_t)r->rows * 4);
+    }
+    const double f0 = c->flops;
+    const int64_t l0 = c->launches;
+    WOCR_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+    try {
+        DT x;
+        x.buf = r->in;
+        x.p = (float *)r->in->p;
+        x.shape = r->in_shape;
+        x.strides = rowmajor_strides(x.shape);
+        DT y = to_rowmajor(c, g->graph->run(x));
+        if (y.shape != r->out_shape) fail(WOCR_ERR_SHAPE, "NdGraph output shape changed between runs");
+        if (r->mode == 0) {
+            if (y.numel() > 0)
+                WOCR_CUDA(cudaMemcpyAsync(r->out->p, y.p, (size_t)y.numel() * 4, cudaMemcpyDeviceToDevice, c->stream));
+        } else {
+            k::argmax(c, y.p, r->rows, r->len, r->len, (uint32_t *)r->best->p, (float *)r->mx->p, (float *)r->lse->p,
+                      0);
+        }
+    } catch (...) {
+        cudaGraph_t dead = nullptr;
+        cudaStreamEndCapture(c->stream, &dead);
+        if (dead) cudaGraphDestroy(dead);
+        r->reset();
+        throw;
+    }
+    WOCR_CUDA(cudaStreamEndCapture(c->stream, &r->graph));
+    WOCR_CUDA(cudaGraphInstantiate(&r->exec, r->graph, 0));
+    r->flops = c->flops - f0;
+    r->launches = c->launches - l0;
+    c->flops = f0;
+    c->launches = l0;
+}
+
+static void nd_replay_launch(wocr_ndgraph *g, NdReplay *r, const float *x) {
+    Ctx *c = &g->ctx->c;
+    WOCR_CUDA(cudaMemcpyAsync(r->in->p, x, r->in->bytes, cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaGraphLaunch(r->exec, c->stream));
+    c->flops += r->flops;
+    c->launches += r->launches;
+}
+
+static void put_dims(const std::vector<int64_t> &s, int64_t *out_shape, int32_t *out_rank) {
+    if (out_rank) *out_rank = (int32_t)s.size();
+    if (out_shape)
+        for (size_t d = 0; d < s.size(); d++) out_shape[d] = s[d];
+}
+
 int32_t wocr_ndgraph_run(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank, float *out,
                          int64_t out_cap, int64_t *out_shape, int32_t *out_rank) {
     return guard([&] {
         if (!g) fail(WOCR_ERR_INVALID, "null graph");
         Ctx *c = &g->ctx->c;
         RunScope rs(c, &g->last);
-        DT y = g->graph->run(nd_input(c, x, shape, rank));
-        put_shape(y, out_shape, out_rank);
-        if (out) {
-            if (out_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(y.shape));
-            y = to_rowmajor(c, y);
-            d2h(c, out, y.p, (size_t)y.numel() * 4);
+        if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
+        bool first = false;
+        NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 0, &first);
+        if (!r || first) {
+            DT y = g->graph->run(nd_input(c, x, shape, rank));
+            put_shape(y, out_shape, out_rank);
+            if (r) r->out_shape = y.shape;
+            if (out) {
+                if (out_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(y.shape));
+                y = to_rowmajor(c, y);
+                d2h(c, out, y.p, (size_t)y.numel() * 4);
+            }
+            sync_bounded(c, 0);
+            return;
         }
+        put_dims(r->out_shape, out_shape, out_rank);
+        int64_t m = 1;
+        for (auto d : r->out_shape) m *= d;
+        if (!out) return;
+        if (out_cap < m) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(r->out_shape));
+        nd_capture(g, r);
+        nd_replay_launch(g, r, x);
+        d2h(c, out, r->out->p, (size_t)m * 4);
         sync_bounded(c, 0);
     });
 }
@@ -811,17 +943,37 @@ int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *
         if (!g) fail(WOCR_ERR_INVALID, "null graph");
         Ctx *c = &g->ctx->c;
         RunScope rs(c, &g->last);
-        DT y = to_rowmajor(c, g->graph->run(nd_input(c, x, shape, rank)));
-        put_shape(y, out_shape, out_rank);
-        int64_t len = y.shape.empty() ? 1 : y.shape.back();
-        int64_t rows = y.numel() / std::max<int64_t>(len, 1);
-        if (rows_out) *rows_out = rows;
-        if (cap < rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
-        BufP b = alloc(c, (size_t)rows * 4), mx = alloc(c, (size_t)rows * 4), ls = alloc(c, (size_t)rows * 4);
-        k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr, 0);
-        if (best) d2h(c, best, b->p, (size_t)rows * 4);
-        if (row_max) d2h(c, row_max, mx->p, (size_t)rows * 4);
-        if (row_lse) d2h(c, row_lse, ls->p, (size_t)rows * 4);
+        if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
+        bool first = false;
+        NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 1, &first);
+        if (!r || first) {
+            DT y = to_rowmajor(c, g->graph->run(nd_input(c, x, shape, rank)));
+            put_shape(y, out_shape, out_rank);
+            int64_t len = y.shape.empty() ? 1 : y.shape.back();
+            int64_t rows = y.numel() / std::max<int64_t>(len, 1);
+            if (rows_out) *rows_out = rows;
+            if (r) {
+                r->out_shape = y.shape;
+                r->rows = rows;
+                r->len = len;
+            }
+            if (cap < rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
+            BufP b = alloc(c, (size_t)rows * 4), mx = alloc(c, (size_t)rows * 4), ls = alloc(c, (size_t)rows * 4);
+            k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr, 0);
+            if (best) d2h(c, best, b->p, (size_t)rows * 4);
+            if (row_max) d2h(c, row_max, mx->p, (size_t)rows * 4);
+            if (row_lse) d2h(c, row_lse, ls->p, (size_t)rows * 4);
+            sync_bounded(c, 0);
+            return;
+        }
+        put_dims(r->out_shape, out_shape, out_rank);
+        if (rows_out) *rows_out = r->rows;
+        if (cap < r->rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
+        nd_capture(g, r);
+        nd_replay_launch(g, r, x);
+        if (best) d2h(c, best, r->best->p, (size_t)r->rows * 4);
+        if (row_max) d2h(c, row_max, r->mx->p, (size_t)r->rows * 4);
+        if (row_lse) d2h(c, row_lse, r->lse->p, (size_t)r->rows * 4);
         sync_bounded(c, 0);
     });
 }
@@ -872,14 +1024,55 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
             to_page[0] = (float)w / (float)ow;
             to_page[1] = (float)h / (float)oh;
         }
-        BufP src = alloc(c, (size_t)w * h * 3);
-        WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, (size_t)w * h * 3, cudaMemcpyHostToDevice, c->stream));
-        DT x = new_nhwc(c, 1, 3, oh, ow);
-        k::det_prep(c, (const uint8_t *)src->p, w, h, ow, oh, 0, x.p);
-        DT y = to_rowmajor(c, g->graph->run(x));
+        // replayed from a CUDA graph after the first call of a page size (mode 2 of the cache)
+        bool first = false;
+        NdReplay *r = nd_replay(g, {h, w, 3, max_side}, 2, &first);
+        if (!r || first) {
+            BufP src = alloc(c, (size_t)w * h * 3);
+            WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, (size_t)w * h * 3, cudaMemcpyHostToDevice, c->stream));
+            DT x = new_nhwc(c, 1, 3, oh, ow);
+            k::det_prep(c, (const uint8_t *)src->p, w, h, ow, oh, 0, x.p);
+            DT y = to_rowmajor(c, g->graph->run(x));
+            if (r) r->out_shape = y.shape;
+            if (prob) {
+                if (prob_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "probability buffer too small");
+                d2h(c, prob, y.p, (size_t)y.numel() * 4);
+            }
+            sync_bounded(c, 0);
+            return;
+        }
+        int64_t m = 1;
+        for (auto d : r->out_shape) m *= d;
+        if (!r->exec) {
+            r->in = alloc(c, (size_t)w * h * 3);
+            r->out = alloc(c, (size_t)std::max<int64_t>(m, 1) * 4);
+            const double f0 = c->flops;
+            const int64_t l0 = c->launches;
+            WOCR_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+            try {
+                DT x = new_nhwc(c, 1, 3, oh, ow);
+                k::det_prep(c, (const uint8_t *)r->in->p, w, h, ow, oh, 0, x.p);
+                DT y = to_rowmajor(c, g->graph->run(x));
+                if (y.shape != r->out_shape) fail(WOCR_ERR_SHAPE, "NdGraph output shape changed between runs");
+                WOCR_CUDA(cudaMemcpyAsync(r->out->p, y.p, (size_t)m * 4, cudaMemcpyDeviceToDevice, c->stream));
+            } catch (...) {
+                cudaGraph_t dead = nullptr;
+                cudaStreamEndCapture(c->stream, &dead);
+                if (dead) cudaGraphDestroy(dead);
+                r->reset();
+                throw;
+            }
+            WOCR_CUDA(cudaStreamEndCapture(c->stream, &r->graph));
+            WOCR_CUDA(cudaGraphInstantiate(&r->exec, r->graph, 0));
+            r->flops = c->flops - f0;
+            r->launches = c->launches - l0;
+            c->flops = f0;
+            c->launches = l0;
+        }
+        nd_replay_launch(g, r, reinterpret_cast<const float *>(rgb));
         if (prob) {
-            if (prob_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "probability buffer too small");
-            d2h(c, prob, y.p, (size_t)y.numel() * 4);
+            if (prob_cap < m) fail(WOCR_ERR_CAPACITY, "probability buffer too small");
+            d2h(c, prob, r->out->p, (size_t)m * 4);
         }
         sync_bounded(c, 0);
     });
