@@ -9,6 +9,8 @@ import wocr
 from oracle import ref
 from wocr.synth import _Builder
 
+from _helpers import argmax_parity
+
 pytestmark = pytest.mark.gpu
 
 RNG = np.random.default_rng(7)
@@ -108,6 +110,33 @@ def test_svtr_block(gpu):
     x = rnd(3, 11, 120)
     close(run_nd(gpu, m, x), ref.run_onnx(m, x))
     close(run_nd(gpu, m, x, stop=True), ref.run_onnx(m, x, stop_before_softmax=True))
+
+
+@pytest.mark.parametrize("classes", [37, 700, 1031])
+def test_linear_argmax_fused(gpu, classes, monkeypatch):
+    """A final linear layer with the row arg-max in its epilogue (per N tile partials merged):
+    one tile, several tiles, a last partial tile; equals the oracle's arg-max, maximum and
+    log-sum-exp, and the unfused path's arg-max and maximum exactly."""
+    b = _Builder(14)
+    y = b.linear(b.layer_norm("x", 120), 120, classes)
+    m = b.model("x", y)
+    x = rnd(3, 50, 120)
+    g = wocr.NdGraph(gpu, m)
+    try:
+        best, mx, lse, shape = g.argmax(x)
+        monkeypatch.setenv("WOCR_UNFUSED_ARGMAX", "1")
+        monkeypatch.setenv("WOCR_NO_GRAPH", "1")
+        ub, umx, ulse, ushape = g.argmax(x)
+    finally:
+        g.close()
+    assert shape == ushape == (3, 50, classes)
+    assert (best == ub).all() and (mx == umx).all()
+    assert np.abs(lse - ulse).max() < 1e-4
+    logits = ref.run_onnx(m, x).reshape(-1, classes)
+    bad, _ = argmax_parity(best, logits)
+    assert bad == 0
+    _, rmx, _, rlse = ref.argmax(logits)
+    assert np.abs(mx - rmx).max() < 1e-4 and np.abs(lse - rlse).max() < 1e-4
 
 
 def test_int_shape_ops_and_pools(gpu):

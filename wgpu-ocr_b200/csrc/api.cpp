@@ -865,14 +865,22 @@ static void nd_capture(wocr_ndgraph *g, NdReplay *r) {
         x.p = (float *)r->in->p;
         x.shape = r->in_shape;
         x.strides = rowmajor_strides(x.shape);
-        DT y = to_rowmajor(c, g->graph->run(x));
-        if (y.shape != r->out_shape) fail(WOCR_ERR_SHAPE, "NdGraph output shape changed between runs");
-        if (r->mode == 0) {
-            if (y.numel() > 0)
-                WOCR_CUDA(cudaMemcpyAsync(r->out->p, y.p, (size_t)y.numel() * 4, cudaMemcpyDeviceToDevice, c->stream));
+        Executor &ex = *g->graph;
+        if (r->mode == 1 && ex.ends_in_linear() && !std::getenv("WOCR_UNFUSED_ARGMAX")) {
+            DT xl = ex.run_to(x, (int)ex.steps.size() - 1);
+            if (ex.linear_argmax(xl, (uint32_t *)r->best->p, (float *)r->mx->p, (float *)r->lse->p) != r->out_shape)
+                fail(WOCR_ERR_SHAPE, "NdGraph output shape changed between runs");
         } else {
-            k::argmax(c, y.p, r->rows, r->len, r->len, (uint32_t *)r->best->p, (float *)r->mx->p, (float *)r->lse->p,
-                      0);
+            DT y = to_rowmajor(c, ex.run(x));
+            if (y.shape != r->out_shape) fail(WOCR_ERR_SHAPE, "NdGraph output shape changed between runs");
+            if (r->mode == 0) {
+                if (y.numel() > 0)
+                    WOCR_CUDA(cudaMemcpyAsync(r->out->p, y.p, (size_t)y.numel() * 4, cudaMemcpyDeviceToDevice,
+                                              c->stream));
+            } else {
+                k::argmax(c, y.p, r->rows, r->len, r->len, (uint32_t *)r->best->p, (float *)r->mx->p,
+                          (float *)r->lse->p, 0);
+            }
         }
     } catch (...) {
         cudaGraph_t dead = nullptr;
@@ -947,19 +955,30 @@ int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *
         bool first = false;
         NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 1, &first);
         if (!r || first) {
-            DT y = to_rowmajor(c, g->graph->run(nd_input(c, x, shape, rank)));
-            put_shape(y, out_shape, out_rank);
-            int64_t len = y.shape.empty() ? 1 : y.shape.back();
-            int64_t rows = y.numel() / std::max<int64_t>(len, 1);
+            Executor &ex = *g->graph;
+            DT in = nd_input(c, x, shape, rank);
+            // a final linear layer (the CTC head) takes the arg-max into its epilogue
+            const bool fused = ex.ends_in_linear() && !std::getenv("WOCR_UNFUSED_ARGMAX");
+            DT y = fused ? ex.run_to(in, (int)ex.steps.size() - 1) : to_rowmajor(c, ex.run(in));
+            std::vector<int64_t> oshape = y.shape;
+            if (fused && !oshape.empty()) oshape.back() = ex.steps.back().ln;
+            put_dims(oshape, out_shape, out_rank);
+            int64_t len = oshape.empty() ? 1 : oshape.back(), rows = 1;
+            for (auto d : oshape) rows *= d;
+            rows /= std::max<int64_t>(len, 1);
             if (rows_out) *rows_out = rows;
             if (r) {
-                r->out_shape = y.shape;
+                r->out_shape = oshape;
                 r->rows = rows;
                 r->len = len;
             }
             if (cap < rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
             BufP b = alloc(c, (size_t)rows * 4), mx = alloc(c, (size_t)rows * 4), ls = alloc(c, (size_t)rows * 4);
-            k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr, 0);
+            if (fused)
+                ex.linear_argmax(y, (uint32_t *)b->p, (float *)mx->p, (float *)ls->p);
+            else
+                k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr,
+                          0);
             if (best) d2h(c, best, b->p, (size_t)rows * 4);
             if (row_max) d2h(c, row_max, mx->p, (size_t)rows * 4);
             if (row_lse) d2h(c, row_lse, ls->p, (size_t)rows * 4);

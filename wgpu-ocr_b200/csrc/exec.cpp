@@ -767,7 +767,10 @@ DT Executor::slot_output(const std::string &name, int64_t n, int64_t c, int64_t 
     return view(b, {n, c, h, w}, b.strides, sl.offset);
 }
 
-DT Executor::run(const DT &x) {
+DT Executor::run(const DT &x) { return run_to(x, (int)steps.size()); }
+
+DT Executor::run_to(const DT &x, int upto) {
+    if (upto < 0 || upto > (int)steps.size()) fail(WOCR_ERR_INVALID, "step index out of range");
     std::map<std::string, DT> concat_bufs;
     cbufs = &concat_bufs;
     struct Reset {
@@ -778,17 +781,57 @@ DT Executor::run(const DT &x) {
     Value in;
     in.f = x;
     vals[input] = in;
-    for (int i = 0; i < (int)steps.size(); i++) {
+    for (int i = 0; i < upto; i++) {
         exec_step(steps[i], vals);
         for (auto &n : steps[i].inputs) {
             auto lu = last_use.find(n);
             if (lu != last_use.end() && lu->second == i && n != output && n != input) vals.erase(n);
         }
     }
-    auto it = vals.find(output);
-    if (it == vals.end()) fail(WOCR_ERR_MISSING, "graph output " + output + " not computed");
-    if (it->second.is_int) fail(WOCR_ERR_SHAPE, "output " + output + " not computed");
+    // the whole graph: its output; a prefix: the first input of step `upto`
+    const std::string &want = upto == (int)steps.size() ? output : steps[upto].inputs[0];
+    auto it = vals.find(want);
+    if (it == vals.end()) fail(WOCR_ERR_MISSING, "value " + want + " not computed");
+    if (it->second.is_int) fail(WOCR_ERR_SHAPE, "value " + want + " is not float");
     return to_f32(ctx, it->second.f);
+}
+
+bool Executor::ends_in_linear() const {
+    if (steps.empty()) return false;
+    const Step &s = steps.back();
+    return s.kind == Step::N_LINEAR && s.act == 0 && s.luw && s.output == output;
+}
+
+// The final linear layer with the row arg-max in its epilogue: per N tile partials, then one
+// merge pass; the logits are never stored (the CTC head, src/nd.rs:291 + 360-391).
+std::vector<int64_t> Executor::linear_argmax(const DT &xin, uint32_t *best, float *row_max, float *row_lse) {
+    const Step &s = steps.back();
+    if (xin.shape.empty() || xin.shape.back() != s.lk)
+        fail(WOCR_ERR_SHAPE, "MatMul: " + shape_str(xin.shape) + " by [" + std::to_string(s.lk) + ", " +
+                                 std::to_string(s.ln) + "]");
+    DT x = to_rowmajor(ctx, xin);
+    const int64_t M = x.numel() / s.lk;
+    const int ntn = k::umma_ntiles(*s.luw);
+    BufP pm = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4), ps = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4),
+         pi = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4);
+    k::UmmaP u;
+    u.mode = 0;
+    u.x = x.p;
+    u.lda = s.lk;
+    u.vec = (s.lk % 4 == 0) && ((reinterpret_cast<uintptr_t>(x.p) & 15) == 0);
+    u.M = M;
+    u.bias = s.lb.p;
+    u.act = 0;
+    u.part_max = (float *)pm->p;
+    u.part_sum = (float *)ps->p;
+    u.part_idx = (uint32_t *)pi->p;
+    u.part_ld = ntn;
+    k::umma_gemm(ctx, *s.luw, u);
+    k::argmax_merge(ctx, (const float *)pm->p, (const float *)ps->p, (const uint32_t *)pi->p, M, ntn, best, row_max,
+                    row_lse);
+    std::vector<int64_t> shape = x.shape;
+    shape.back() = s.ln;
+    return shape;
 }
 
 // Channel Concat of NHWC parts: parts already written into their slice of the registered

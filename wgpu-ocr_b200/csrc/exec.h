@@ -109,6 +109,12 @@ class Executor {
     explicit Executor(Ctx *c) : ctx(c) {}
     // Run on `x`; returns the output tensor.
     DT run(const DT &x);
+    // Run steps [0, upto); returns the first input of step `upto` (the output when upto = all).
+    DT run_to(const DT &x, int upto);
+    // The last step is a linear layer without activation producing the output (a CTC head).
+    bool ends_in_linear() const;
+    // That linear layer on x (its input) with the row arg-max fused; returns the logits' shape.
+    std::vector<int64_t> linear_argmax(const DT &x, uint32_t *best, float *row_max, float *row_lse);
     void finalize();  // uploads generic weights, computes last uses
 
   protected:

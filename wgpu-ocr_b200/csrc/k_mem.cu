@@ -6,6 +6,7 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <cmath>
 
 #include "kernels.h"
 
@@ -288,6 +289,40 @@ __global__ void k_resplit(const float *__restrict__ x, uint16_t *__restrict__ y,
         int64_t xo, yo;
         index4(g, i, xo, yo);
         split_f(x[xo], y[yo], y[yo + lo_off]);
+    }
+}
+
+// One warp per row: the tiles' maxima reduced over the lanes, the lowest tile reaching the
+// maximum gives the column, the sums rescaled to the maximum.
+__global__ void k_argmax_merge(const float *__restrict__ pmax, const float *__restrict__ psum,
+                               const uint32_t *__restrict__ pidx, int64_t rows, int ntiles, uint32_t *best,
+                               float *row_max, float *row_lse) {
+    const int lane = threadIdx.x & 31;
+    const int64_t wid = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = wid; r < rows; r += nw) {
+        const float *pm = pmax + r * ntiles;
+        float m = -INFINITY;
+        for (int t = lane; t < ntiles; t += 32) m = fmaxf(m, pm[t]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        int first = ntiles;
+        float s = 0.f;
+        for (int t = lane; t < ntiles; t += 32) {
+            const float v = pm[t];
+            if (v == m && t < first) first = t;
+            s += psum[r * ntiles + t] * __expf(v - m);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
+            s += __shfl_xor_sync(0xffffffffu, s, o);
+        }
+        if (lane == 0) {
+            best[r] = first < ntiles ? pidx[r * ntiles + first] : 0u;
+            if (row_max) row_max[r] = m;
+            if (row_lse) row_lse[r] = m + logf(s);
+        }
     }
 }
 
@@ -640,6 +675,15 @@ void resplit(Ctx *c, const float *x, const int64_t (&xs)[4], uint16_t *y, const 
     if (total == 0) return;
     Prof pf(c, "resplit", 0, 8.0 * total);
     k_resplit<<<grid_for(c, total), kThreads, 0, c->stream>>>(x, y, lo_off, g, total);
+    WOCR_LAUNCHED(c);
+}
+
+void argmax_merge(Ctx *c, const float *pmax, const float *psum, const uint32_t *pidx, int64_t rows, int ntiles,
+                  uint32_t *best, float *row_max, float *row_lse) {
+    if (rows == 0) return;
+    Prof pf(c, "argmax_merge", 0, 12.0 * (double)rows * ntiles);
+    k_argmax_merge<<<grid_for(c, rows * 32), kThreads, 0, c->stream>>>(pmax, psum, pidx, rows, ntiles, best,
+                                                                       row_max, row_lse);
     WOCR_LAUNCHED(c);
 }
 

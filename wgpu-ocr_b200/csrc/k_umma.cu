@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "kernels.h"
@@ -375,6 +376,8 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 nb = tt / p.oh;
                 pix = (int64_t)oy * p.ow + ox;
             }
+            float amx = -INFINITY, asum = 0.f;  // arg-max partials of this row over the tile
+            uint32_t aidx = 0;
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float v[16];
@@ -388,6 +391,23 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     for (int j = 0; j < 16; j++) v[j] += w[j];
                 }
                 if (m >= p.M || n0 + c0 >= p.N) continue;
+                if (p.part_max) {
+                    // online arg-max and sum of exponentials (ties keep the lowest column)
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const int col = n0 + c0 + j;
+                        if (col >= p.N) break;
+                        const float o = v[j] + (p.bias ? p.bias[col] : 0.f);
+                        if (o > amx) {
+                            asum = asum * __expf(amx - o) + 1.f;
+                            amx = o;
+                            aidx = (uint32_t)col;
+                        } else {
+                            asum += __expf(o - amx);
+                        }
+                    }
+                    continue;
+                }
                 if (p.scatter && p.scat_cout % 16 == 0) {
                     // a 16-column chunk lies in one tap: 16 consecutive channels of output pixel
                     // (s oy + ky, s ox + kx)
@@ -446,6 +466,12 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     for (int j = 0; j < 16; j++)
                         if (n0 + c0 + j < p.N) dst[j] = v[j];
                 }
+            }
+            if (p.part_max && m < p.M) {
+                const int64_t o = m * p.part_ld + n0 / BN;
+                p.part_max[o] = amx;
+                p.part_sum[o] = asum;
+                p.part_idx[o] = aidx;
             }
             tc_fence_before();
             __syncwarp();
@@ -529,6 +555,8 @@ UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int
 void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
     if (p.M == 0 || w.N == 0) return;
     if (p.M >= (int64_t)INT32_MAX - BM) fail(WOCR_ERR_UNSUPPORTED, "GEMM with 2^31 rows or more");
+    if (p.part_max && (p.mode != 0 || p.part_ld != umma_ntiles(w)))
+        fail(WOCR_ERR_INVALID, "arg-max partials need a row-major GEMM and one slot per N tile");
     if (!c->status) {
         c->status_buf = alloc(c, 16);
         c->status = (int *)c->status_buf->p;

@@ -120,6 +120,12 @@ void softmax(Ctx *c, const float *x, float *y, int64_t rows, int64_t len);
 void argmax(Ctx *c, const float *x, int64_t rows, int64_t len, int64_t ld, uint32_t *best, float *row_max,
             float *row_lse, int tie_last);
 
+// Rows of arg-max partials [rows][ntiles] (per tile: maximum, its lowest column, sum of
+// exp(value - maximum)) -> the row's arg-max (lowest column on ties, as K30), maximum and
+// log-sum-exp.  row_max / row_lse nullable.
+void argmax_merge(Ctx *c, const float *pmax, const float *psum, const uint32_t *pidx, int64_t rows, int ntiles,
+                  uint32_t *best, float *row_max, float *row_lse);
+
 // Batched row-major matmul y[b] = a[b] (m x k) . bm[b] (k x n) (K29 with two activations,
 // src/nd.rs:947-962).
 void bmm(Ctx *c, const float *a, const float *bm, float *y, int64_t batch, int m, int kk, int n);

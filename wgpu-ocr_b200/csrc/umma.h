@@ -36,6 +36,12 @@ struct UmmaP {
     const float *res = nullptr;
     int64_t res_n = 0, res_pix = 0;
     int scatter = 0, scat_cout = 0;
+    // mode 0 only: instead of storing y, each N tile writes its per-row arg-max partials at
+    // [row][tile] (part_ld tiles a row): the maximum, the lowest column reaching it and the sum
+    // of exp(value - maximum) over the tile's columns
+    float *part_max = nullptr, *part_sum = nullptr;
+    uint32_t *part_idx = nullptr;
+    int part_ld = 0;
     int *status = nullptr;        // device error word (bounded waits that gave up)
 };
 
@@ -45,6 +51,7 @@ int umma_bn(int N);
 // is one tap and the scatter epilogue stores contiguous channels).
 UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int max_bn = 256);
 void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p);
+inline int umma_ntiles(const UmmaW &w) { return (w.N + w.bn - 1) / w.bn; }
 
 }  // namespace k
 }  // namespace wocr
