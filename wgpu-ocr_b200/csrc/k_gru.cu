@@ -6,9 +6,11 @@
 // fp32 = 96 KB, padded to 128 KB) in shared memory for the whole sequence.  Every step:
 //   1. each CTA computes its rows' dot products with h for its L lines (thread = unit x k-slice,
 //      R read as one float4 of the unit's z/r/h weights, h broadcast as float4),
-//   2. the 8 k-slices are summed, the gate nonlinearity gives the new h for its 32 units,
+//   2. the 8 k-slices (one warp each) are summed, the gate nonlinearity gives the new h for its
+//      32 units (the step's input gates were loaded during the previous step),
 //   3. the new h is stored into every CTA's next-step buffer through distributed shared memory
-//      and `barrier.cluster` (hardware co-scheduled CTAs: no global-memory spin waits) publishes it.
+//      and `barrier.cluster` (hardware co-scheduled CTAs: no global-memory spin waits) publishes
+//      it: arrive right after the stores, wait before the next step reads h.
 // Each line runs for its own length; the backward direction starts at len - 1 (src/gpu.rs:797-800).
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
@@ -26,12 +28,39 @@ constexpr int kHid = 256;
 constexpr int kCluster = 8;
 constexpr int kUnits = kHid / kCluster;  // 32 hidden units per CTA
 constexpr int kSlices = 8;               // k split over 8 warps
+constexpr int kThreadsG = kSlices * 32;
 constexpr int kSliceLen = kHid / kSlices;
 
 __device__ __forceinline__ float sigm(float v) { return 1.0f / (1.0f + expf(-v)); }
 
+// h of L lines at one k (L consecutive floats, 4 L-byte aligned) as vector loads
 template <int L>
-__global__ void __launch_bounds__(256) k_gru(const float *__restrict__ g, const float *__restrict__ r,
+__device__ __forceinline__ void load_h(const float *p, float (&h)[L]) {
+    if (L % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < L / 4; i++) {
+            const float4 v = reinterpret_cast<const float4 *>(p)[i];
+            h[4 * i] = v.x;
+            h[4 * i + 1] = v.y;
+            h[4 * i + 2] = v.z;
+            h[4 * i + 3] = v.w;
+        }
+    } else if (L == 2) {
+        const float2 v = *reinterpret_cast<const float2 *>(p);
+        h[0] = v.x;
+        h[L - 1] = v.y;
+    } else {
+        h[0] = p[0];
+    }
+}
+
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+template <int L>
+__global__ void __launch_bounds__(kThreadsG) k_gru(const float *__restrict__ g, const float *__restrict__ r,
                                             const float *__restrict__ rb, const int *__restrict__ lens, int tmax,
                                             int ntot, float *__restrict__ y) {
     extern __shared__ __align__(16) float smem[];
@@ -80,6 +109,18 @@ __global__ void __launch_bounds__(256) k_gru(const float *__restrict__ g, const 
     }
     // phase-1 role: unit u1, k-slice sl
     const int u1 = tid % kUnits, sl = tid / kUnits;
+    // the input-gate values of this thread's (unit, line) for the next step, loaded a step ahead
+    auto gate_ptr = [&](int s) {
+        const int t = dir == 0 ? s : mylen - 1 - s;
+        return g + ((size_t)t * ntot + line) * 1536 + dir * 768;
+    };
+    float gz = 0.f, gr = 0.f, gh = 0.f;
+    if (owner && mylen > 0) {
+        const float *gb = gate_ptr(0);
+        gz = gb[j];
+        gr = gb[256 + j];
+        gh = gb[512 + j];
+    }
     cluster.sync();
 
     for (int s = 0; s < steps; s++) {
@@ -92,13 +133,13 @@ __global__ void __launch_bounds__(256) k_gru(const float *__restrict__ g, const 
         for (int kk = 0; kk < kSliceLen; kk++) {
             int k = sl * kSliceLen + kk;
             float4 w = Rs[k * kUnits + u1];
-            const float *hv = hc + k * L;
+            float hv[L];
+            load_h<L>(hc + k * L, hv);
 #pragma unroll
             for (int l = 0; l < L; l++) {
-                float hl = hv[l];
-                az[l] += w.x * hl;
-                ar[l] += w.y * hl;
-                ah[l] += w.z * hl;
+                az[l] += w.x * hv[l];
+                ar[l] += w.y * hv[l];
+                ah[l] += w.z * hv[l];
             }
         }
         float *rd = red + (size_t)sl * 3 * L * kUnits + u1;
@@ -109,9 +150,11 @@ __global__ void __launch_bounds__(256) k_gru(const float *__restrict__ g, const 
             rd[(2 * L + l) * kUnits] = ah[l];
         }
         __syncthreads();
+        float hn = 0.f;
+        bool wrote = false;
         if (l2 < L) {
             float hold = hc[j * L + l2];
-            float hn = hold;
+            hn = hold;
             if (owner && s < mylen) {
                 float pz = 0.f, pr = 0.f, ph = 0.f;
 #pragma unroll
@@ -121,13 +164,11 @@ __global__ void __launch_bounds__(256) k_gru(const float *__restrict__ g, const 
                     pr += rq[(L + l2) * kUnits];
                     ph += rq[(2 * L + l2) * kUnits];
                 }
-                int t = dir == 0 ? s : mylen - 1 - s;
-                const float *gb = g + ((size_t)t * ntot + line) * 1536 + dir * 768;
-                float z = sigm(gb[j] + pz + bz);
-                float rr = sigm(gb[256 + j] + pr + br);
-                float c = tanhf(gb[512 + j] + rr * (ph + bh));
+                float z = sigm(gz + pz + bz);
+                float rr = sigm(gr + pr + br);
+                float c = tanhf(gh + rr * (ph + bh));
                 hn = (1.0f - z) * c + z * hold;
-                y[((size_t)t * ntot + line) * 512 + dir * 256 + j] = hn;
+                wrote = true;
             }
 #pragma unroll
             for (int q = 0; q < kCluster; q++) {
@@ -135,7 +176,20 @@ __global__ void __launch_bounds__(256) k_gru(const float *__restrict__ g, const 
                 *dst = hn;
             }
         }
-        cluster.sync();
+        // publish h (release), then store y and fetch the next step's gates while the other
+        // CTAs catch up, then wait for theirs (acquire)
+        cluster_arrive();
+        if (wrote) {
+            const int t = dir == 0 ? s : mylen - 1 - s;
+            y[((size_t)t * ntot + line) * 512 + dir * 256 + j] = hn;
+            if (s + 1 < mylen) {
+                const float *gb = gate_ptr(s + 1);
+                gz = gb[j];
+                gr = gb[256 + j];
+                gh = gb[512 + j];
+            }
+        }
+        cluster_wait();
     }
 }
 
@@ -156,7 +210,7 @@ void launch_gru(Ctx *c, const float *g, const float *r, const float *rb, const i
     int groups = (ntot + L - 1) / L;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(groups * kCluster, 2, 1);
-    cfg.blockDim = dim3(256, 1, 1);
+    cfg.blockDim = dim3(kThreadsG, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = c->stream;
     cudaLaunchAttribute attr[1];
@@ -178,7 +232,7 @@ int max_clusters(Ctx *c) {
     WOCR_CUDA(cudaFuncSetAttribute(k_gru<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kCluster * 64, 2, 1);
-    cfg.blockDim = dim3(256, 1, 1);
+    cfg.blockDim = dim3(kThreadsG, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
