@@ -185,3 +185,27 @@ def test_ndgraph_replay(gpu, pp_model, monkeypatch):
     finally:
         g.close()
     assert (p1 == p2).all() and (p3 == p4).all()
+
+
+def test_recognize_replay(gpu, rec_model, monkeypatch):
+    """wocr_recognize calls of a known batch layout replay a captured CUDA graph: logits and
+    arg-max equal those of direct runs, with and without logits, and new line images are seen."""
+    batches, _, _ = synth.ocrs_batches(synth.ocrs_lines(3, n=9))
+    other = [(np.ascontiguousarray(d[::-1]), n, w) for d, n, w in batches]
+    rec = wocr.Recognizer(gpu, rec_model)
+    try:
+        a = rec.recognize(batches)                       # direct
+        b = rec.recognize(batches)                       # capture + replay
+        c = rec.recognize(batches)                       # replay
+        o = rec.recognize(other)                         # replay on new data
+        nb = rec.recognize(batches, want_logits=False)   # another layout (no logits)
+        nb2 = rec.recognize(batches, want_logits=False)
+        monkeypatch.setenv("WOCR_NO_GRAPH", "1")
+        od = rec.recognize(other)
+    finally:
+        rec.close()
+    for x in (b, c):
+        assert x[1] == a[1] and x[2] == a[2]
+        assert (x[0] == a[0]).all() and (x[3] == a[3]).all()
+    assert (o[0] == od[0]).all() and (o[3] == od[3]).all()
+    assert (nb[3] == a[3]).all() and (nb2[3] == a[3]).all()

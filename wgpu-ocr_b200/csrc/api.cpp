@@ -75,8 +75,38 @@ struct GruLayer {
     std::shared_ptr<k::UmmaW> uw;  // the projection on the tensor cores
 };
 
+// One wocr_recognize layout (batch sizes and widths, which outputs) replayed from a CUDA graph:
+// the batches are uploaded into a persistent buffer, the captured trunks, GRU layers, output
+// layer and arg-max write persistent outputs.  The first call of a layout runs directly.
+struct RecReplay {
+    std::vector<int32_t> bn, bw;
+    int want = -1;  // bit 0 logits, bit 1 arg-max
+    int ntot = 0, tmax = 0;
+    std::vector<int> lens;
+    BufP in, lens_d, logits, best;
+    std::vector<size_t> in_off;  // element offset of each batch in `in`
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    double flops = 0;
+    int64_t launches = 0;
+    uint64_t used = 0;
+    void reset() {
+        if (exec) cudaGraphExecDestroy(exec);
+        if (graph) cudaGraphDestroy(graph);
+        exec = nullptr;
+        graph = nullptr;
+        want = -1;
+        in.reset();
+        lens_d.reset();
+        logits.reset();
+        best.reset();
+    }
+};
+
 struct wocr_recognizer {
     wocr_ctx *ctx;
+    RecReplay replays[4];
+    uint64_t uses = 0;
     std::unique_ptr<Executor> trunk;
     int pool_kh = 1;
     GruLayer layers[2];
@@ -84,6 +114,9 @@ struct wocr_recognizer {
     std::shared_ptr<k::UmmaW> lin_uw;
     int classes = 0, ldw = 0;
     int lines = 8;
+    ~wocr_recognizer() {
+        for (auto &r : replays) r.reset();
+    }
     Stats last;
 };
 
@@ -709,6 +742,78 @@ int32_t wocr_recognizer_dims(wocr_recognizer *rec, const int32_t *batch_n, const
     });
 }
 
+// The recognition pass on device batches (src/gpu.rs:1510-1602): trunks, time-major pooling, two
+// GRU layers, the output layer, the arg-max.  `lens_d` (optional) holds the line lengths already.
+// Returns the logits [tmax][ntot][classes] (and, with want_best, the arg-max [tmax][ntot], into
+// d_best when given).
+struct RecResult {
+    DT logits;
+    BufP best;
+    int ntot = 0, tmax = 0;
+    std::vector<int> lens;
+};
+
+static RecResult recognize_dev(wocr_recognizer *rec, const std::vector<DT> &xs, const int *lens_d_in, bool want_best,
+                               uint32_t *d_best) {
+    Ctx *c = &rec->ctx->c;
+    std::vector<DT> trunks;
+    for (auto &x : xs) trunks.push_back(rec->trunk->run(x));
+    int ntot = 0, tmax = 0;
+    for (auto &t : trunks) {
+        ntot += (int)t.shape[0];
+        tmax = std::max(tmax, (int)t.shape[3]);
+    }
+    int ch = (int)trunks[0].shape[1];
+    if (ch != rec->layers[0].input)
+        fail(WOCR_ERR_SHAPE, "trunk gives " + std::to_string(ch) + " features, GRU takes " +
+                                 std::to_string(rec->layers[0].input));
+    int64_t m = (int64_t)tmax * ntot;
+    DT x = new_rowmajor(c, {tmax, ntot, ch});
+    WOCR_CUDA(cudaMemsetAsync(x.p, 0, (size_t)x.numel() * 4, c->stream));
+    std::vector<int> hl;
+    int noff = 0;
+    for (auto &t : trunks) {
+        int n = (int)t.shape[0], tc = (int)t.shape[1], h = (int)t.shape[2], w = (int)t.shape[3];
+        if (tc != ch) fail(WOCR_ERR_SHAPE, "trunk channels differ between batches");
+        if ((h - rec->pool_kh) / rec->pool_kh + 1 != 1 || h < rec->pool_kh)
+            fail(WOCR_ERR_SHAPE, "trunk height " + std::to_string(h) + " does not pool to one row");
+        DT tn = to_nhwc(c, t);
+        k::avgpool_t(c, tn.p, tn.strides[0], tn.pix(), n, ch, h, w, rec->pool_kh, ntot, noff, x.p);
+        for (int q = 0; q < n; q++) hl.push_back(w);
+        noff += n;
+    }
+    BufP lens_own;
+    const int *lens_d = lens_d_in;
+    if (!lens_d) {
+        lens_own = alloc(c, hl.size() * sizeof(int));
+        WOCR_CUDA(cudaMemcpyAsync(lens_own->p, hl.data(), hl.size() * sizeof(int), cudaMemcpyHostToDevice,
+                                  c->stream));
+        lens_d = (const int *)lens_own->p;
+    }
+    DT in = x;
+    for (int l = 0; l < 2; l++) {
+        GruLayer &L = rec->layers[l];
+        DT gates = linear_run(c, in, L.w_t, L.wb, L.input, 1536, 1536, 0, L.uw.get());
+        DT yo = new_rowmajor(c, {tmax, ntot, 512});
+        WOCR_CUDA(cudaMemsetAsync(yo.p, 0, (size_t)yo.numel() * 4, c->stream));
+        k::gru_layer(c, gates.p, L.r.p, L.rb.p, lens_d, tmax, ntot, yo.p);
+        in = yo;
+    }
+    RecResult res;
+    res.logits = linear_run(c, in, rec->lin_w, rec->lin_b, 512, rec->classes, rec->ldw, 0, rec->lin_uw.get());
+    if (want_best) {
+        if (!d_best) {
+            res.best = alloc(c, (size_t)std::max<int64_t>(m, 1) * 4);
+            d_best = (uint32_t *)res.best->p;
+        }
+        k::argmax(c, res.logits.p, m, rec->classes, rec->classes, d_best, nullptr, nullptr, 1);
+    }
+    res.ntot = ntot;
+    res.tmax = tmax;
+    res.lens = hl;
+    return res;
+}
+
 int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const int32_t *batch_n,
                        const int32_t *batch_w, int32_t n_batches, float *logits, int64_t logits_cap, int32_t *lens,
                        uint32_t *best, int32_t *tmax_out) {
@@ -716,61 +821,113 @@ int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const 
         if (!rec || n_batches <= 0 || !batches || !batch_n || !batch_w) fail(WOCR_ERR_INVALID, "no batches");
         Ctx *c = &rec->ctx->c;
         RunScope rs(c, &rec->last);
-        // the trunks first (src/gpu.rs:1516-1526)
-        std::vector<DT> trunks;
-        for (int b = 0; b < n_batches; b++) {
+        for (int b = 0; b < n_batches; b++)
             if (batch_n[b] <= 0 || batch_w[b] <= 0 || !batches[b]) fail(WOCR_ERR_INVALID, "empty batch");
-            DT x = from_host(c, batches[b], {batch_n[b], 1, 64, batch_w[b]});
-            trunks.push_back(rec->trunk->run(x));
+        std::vector<int32_t> bn(batch_n, batch_n + n_batches), bw(batch_w, batch_w + n_batches);
+        const int want = (logits ? 1 : 0) | (best ? 2 : 0);
+        // the replay entry of this layout
+        RecReplay *r = nullptr;
+        bool first = false;
+        if (!c->prof && !std::getenv("WOCR_NO_GRAPH")) {
+            for (auto &e : rec->replays)
+                if (e.want == want && e.bn == bn && e.bw == bw) r = &e;
+            if (!r) {
+                r = &rec->replays[0];
+                for (auto &e : rec->replays)
+                    if (e.want < 0 || e.used < r->used) r = &e;
+                r->reset();
+                r->want = want;
+                r->bn = bn;
+                r->bw = bw;
+                first = true;
+            }
+            r->used = ++rec->uses;
         }
         int ntot = 0, tmax = 0;
-        for (auto &t : trunks) {
-            ntot += (int)t.shape[0];
-            tmax = std::max(tmax, (int)t.shape[3]);
-        }
-        int ch = (int)trunks[0].shape[1];
-        if (ch != rec->layers[0].input)
-            fail(WOCR_ERR_SHAPE, "trunk gives " + std::to_string(ch) + " features, GRU takes " +
-                                     std::to_string(rec->layers[0].input));
-        int64_t m = (int64_t)tmax * ntot;
-        DT x = new_rowmajor(c, {tmax, ntot, ch});
-        WOCR_CUDA(cudaMemsetAsync(x.p, 0, (size_t)x.numel() * 4, c->stream));
         std::vector<int> hl;
-        int noff = 0;
-        for (auto &t : trunks) {
-            int n = (int)t.shape[0], tc = (int)t.shape[1], h = (int)t.shape[2], w = (int)t.shape[3];
-            if (tc != ch) fail(WOCR_ERR_SHAPE, "trunk channels differ between batches");
-            if ((h - rec->pool_kh) / rec->pool_kh + 1 != 1 || h < rec->pool_kh)
-                fail(WOCR_ERR_SHAPE, "trunk height " + std::to_string(h) + " does not pool to one row");
-            DT tn = to_nhwc(c, t);
-            k::avgpool_t(c, tn.p, tn.strides[0], tn.pix(), n, ch, h, w, rec->pool_kh, ntot, noff, x.p);
-            for (int q = 0; q < n; q++) hl.push_back(w);
-            noff += n;
+        if (!r || first) {
+            std::vector<DT> xs;
+            for (int b = 0; b < n_batches; b++) xs.push_back(from_host(c, batches[b], {bn[b], 1, 64, bw[b]}));
+            RecResult res = recognize_dev(rec, xs, nullptr, best != nullptr, nullptr);
+            ntot = res.ntot;
+            tmax = res.tmax;
+            hl = res.lens;
+            const int64_t m = (int64_t)tmax * ntot;
+            if (logits) {
+                if (logits_cap < m * rec->classes) fail(WOCR_ERR_CAPACITY, "logits buffer too small");
+                d2h(c, logits, res.logits.p, (size_t)m * rec->classes * 4);
+            }
+            if (best) d2h(c, best, res.best->p, (size_t)m * 4);
+            sync_bounded(c, 0);
+            if (r) {
+                r->ntot = ntot;
+                r->tmax = tmax;
+                r->lens = hl;
+            }
+        } else {
+            ntot = r->ntot;
+            tmax = r->tmax;
+            hl = r->lens;
+            const int64_t m = (int64_t)tmax * ntot;
+            if (logits && logits_cap < m * rec->classes) fail(WOCR_ERR_CAPACITY, "logits buffer too small");
+            if (!r->exec) {
+                size_t total = 0;
+                r->in_off.clear();
+                for (int b = 0; b < n_batches; b++) {
+                    r->in_off.push_back(total);
+                    total += (size_t)bn[b] * 64 * bw[b];
+                }
+                r->in = alloc(c, total * 4);
+                r->lens_d = alloc(c, hl.size() * sizeof(int));
+                WOCR_CUDA(cudaMemcpyAsync(r->lens_d->p, hl.data(), hl.size() * sizeof(int), cudaMemcpyHostToDevice,
+                                          c->stream));
+                if (logits) r->logits = alloc(c, (size_t)m * rec->classes * 4);
+                if (best) r->best = alloc(c, (size_t)m * 4);
+                WOCR_CUDA(cudaStreamSynchronize(c->stream));  // lens uploaded before capture
+                const double f0 = c->flops;
+                const int64_t l0 = c->launches;
+                WOCR_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+                try {
+                    std::vector<DT> xs;
+                    for (int b = 0; b < n_batches; b++) {
+                        DT x;
+                        x.buf = r->in;
+                        x.p = (float *)r->in->p + r->in_off[b];
+                        x.shape = {bn[b], 1, 64, bw[b]};
+                        x.strides = rowmajor_strides(x.shape);
+                        xs.push_back(x);
+                    }
+                    RecResult res = recognize_dev(rec, xs, (const int *)r->lens_d->p, best != nullptr,
+                                                  best ? (uint32_t *)r->best->p : nullptr);
+                    if (res.ntot != ntot || res.tmax != tmax)
+                        fail(WOCR_ERR_SHAPE, "recognition sizes changed between calls");
+                    if (logits)
+                        WOCR_CUDA(cudaMemcpyAsync(r->logits->p, res.logits.p, (size_t)m * rec->classes * 4,
+                                                  cudaMemcpyDeviceToDevice, c->stream));
+                } catch (...) {
+                    cudaGraph_t dead = nullptr;
+                    cudaStreamEndCapture(c->stream, &dead);
+                    if (dead) cudaGraphDestroy(dead);
+                    r->reset();
+                    throw;
+                }
+                WOCR_CUDA(cudaStreamEndCapture(c->stream, &r->graph));
+                WOCR_CUDA(cudaGraphInstantiate(&r->exec, r->graph, 0));
+                r->flops = c->flops - f0;
+                r->launches = c->launches - l0;
+                c->flops = f0;
+                c->launches = l0;
+            }
+            for (int b = 0; b < n_batches; b++)
+                WOCR_CUDA(cudaMemcpyAsync((float *)r->in->p + r->in_off[b], batches[b],
+                                          (size_t)bn[b] * 64 * bw[b] * 4, cudaMemcpyHostToDevice, c->stream));
+            WOCR_CUDA(cudaGraphLaunch(r->exec, c->stream));
+            c->flops += r->flops;
+            c->launches += r->launches;
+            if (logits) d2h(c, logits, r->logits->p, (size_t)m * rec->classes * 4);
+            if (best) d2h(c, best, r->best->p, (size_t)m * 4);
+            sync_bounded(c, 0);
         }
-        BufP lens_d = alloc(c, hl.size() * sizeof(int));
-        WOCR_CUDA(cudaMemcpyAsync(lens_d->p, hl.data(), hl.size() * sizeof(int), cudaMemcpyHostToDevice, c->stream));
-        DT in = x;
-        for (int l = 0; l < 2; l++) {
-            GruLayer &L = rec->layers[l];
-            DT gates = linear_run(c, in, L.w_t, L.wb, L.input, 1536, 1536, 0, L.uw.get());
-            DT yo = new_rowmajor(c, {tmax, ntot, 512});
-            WOCR_CUDA(cudaMemsetAsync(yo.p, 0, (size_t)yo.numel() * 4, c->stream));
-            k::gru_layer(c, gates.p, L.r.p, L.rb.p, (const int *)lens_d->p, tmax, ntot, yo.p);
-            in = yo;
-        }
-        DT lg = linear_run(c, in, rec->lin_w, rec->lin_b, 512, rec->classes, rec->ldw, 0,
-                           rec->lin_uw.get());  // [tmax][ntot][classes]
-        if (logits) {
-            if (logits_cap < m * rec->classes) fail(WOCR_ERR_CAPACITY, "logits buffer too small");
-            d2h(c, logits, lg.p, (size_t)m * rec->classes * 4);
-        }
-        BufP bd;
-        if (best) {
-            bd = alloc(c, (size_t)m * 4);
-            k::argmax(c, lg.p, m, rec->classes, rec->classes, (uint32_t *)bd->p, nullptr, nullptr, 1);
-            d2h(c, best, bd->p, (size_t)m * 4);
-        }
-        sync_bounded(c, 0);
         if (lens) std::memcpy(lens, hl.data(), hl.size() * sizeof(int));
         if (tmax_out) *tmax_out = tmax;
     });
