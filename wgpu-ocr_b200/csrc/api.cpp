@@ -107,6 +107,11 @@ struct wocr_recognizer {
     wocr_ctx *ctx;
     RecReplay replays[4];
     uint64_t uses = 0;
+    // the width buckets' trunks run on these streams inside a captured pass (parallel graph
+    // branches): fork from the context stream, join back before the time-major pooling
+    static constexpr int kSide = 4;
+    cudaStream_t side[kSide] = {};
+    cudaEvent_t fork = nullptr, join[kSide] = {};
     std::unique_ptr<Executor> trunk;
     int pool_kh = 1;
     GruLayer layers[2];
@@ -116,6 +121,11 @@ struct wocr_recognizer {
     int lines = 8;
     ~wocr_recognizer() {
         for (auto &r : replays) r.reset();
+        for (int i = 0; i < kSide; i++) {
+            if (side[i]) cudaStreamDestroy(side[i]);
+            if (join[i]) cudaEventDestroy(join[i]);
+        }
+        if (fork) cudaEventDestroy(fork);
     }
     Stats last;
 };
@@ -754,10 +764,32 @@ struct RecResult {
 };
 
 static RecResult recognize_dev(wocr_recognizer *rec, const std::vector<DT> &xs, const int *lens_d_in, bool want_best,
-                               uint32_t *d_best) {
+                               uint32_t *d_best, bool branches = false) {
     Ctx *c = &rec->ctx->c;
     std::vector<DT> trunks;
-    for (auto &x : xs) trunks.push_back(rec->trunk->run(x));
+    if (branches && xs.size() > 1) {
+        // trunks on the side streams (captured as parallel branches of the graph)
+        cudaStream_t main = c->stream;
+        WOCR_CUDA(cudaEventRecord(rec->fork, main));
+        const int ns = std::min<int>(wocr_recognizer::kSide, (int)xs.size());
+        for (int i = 0; i < ns; i++) WOCR_CUDA(cudaStreamWaitEvent(rec->side[i], rec->fork, 0));
+        struct Restore {
+            Ctx *c;
+            cudaStream_t s;
+            ~Restore() { c->stream = s; }
+        } restore{c, main};
+        for (size_t b = 0; b < xs.size(); b++) {
+            c->stream = rec->side[b % ns];
+            trunks.push_back(rec->trunk->run(xs[b]));
+        }
+        c->stream = main;
+        for (int i = 0; i < ns; i++) {
+            WOCR_CUDA(cudaEventRecord(rec->join[i], rec->side[i]));
+            WOCR_CUDA(cudaStreamWaitEvent(main, rec->join[i], 0));
+        }
+    } else {
+        for (auto &x : xs) trunks.push_back(rec->trunk->run(x));
+    }
     int ntot = 0, tmax = 0;
     for (auto &t : trunks) {
         ntot += (int)t.shape[0];
@@ -884,6 +916,13 @@ int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const 
                 if (logits) r->logits = alloc(c, (size_t)m * rec->classes * 4);
                 if (best) r->best = alloc(c, (size_t)m * 4);
                 WOCR_CUDA(cudaStreamSynchronize(c->stream));  // lens uploaded before capture
+                if (!rec->fork) {
+                    for (int i = 0; i < wocr_recognizer::kSide; i++) {
+                        WOCR_CUDA(cudaStreamCreateWithFlags(&rec->side[i], cudaStreamNonBlocking));
+                        WOCR_CUDA(cudaEventCreateWithFlags(&rec->join[i], cudaEventDisableTiming));
+                    }
+                    WOCR_CUDA(cudaEventCreateWithFlags(&rec->fork, cudaEventDisableTiming));
+                }
                 const double f0 = c->flops;
                 const int64_t l0 = c->launches;
                 WOCR_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
@@ -898,7 +937,7 @@ int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const 
                         xs.push_back(x);
                     }
                     RecResult res = recognize_dev(rec, xs, (const int *)r->lens_d->p, best != nullptr,
-                                                  best ? (uint32_t *)r->best->p : nullptr);
+                                                  best ? (uint32_t *)r->best->p : nullptr, true);
                     if (res.ntot != ntot || res.tmax != tmax)
                         fail(WOCR_ERR_SHAPE, "recognition sizes changed between calls");
                     if (logits)
