@@ -275,10 +275,31 @@ static DT done(Ctx *c, const KOut &o) {
 // =========================================================================================
 // convolution runs
 // =========================================================================================
+// MaxPool with kernel == stride, no padding (src/gpu.rs:462-482), on a split or fp32 input; the
+// output split when `split_out`.
+static DT maxpool_run(Ctx *ctx, DT x, int kh, int kw, bool split_out) {
+    if (x.rank() != 4) fail(WOCR_ERR_SHAPE, "MaxPool input " + shape_str(x.shape));
+    if (x.split && !x.nhwc()) x = to_f32(ctx, x);
+    int64_t n = x.shape[0], ch = x.shape[1], h = x.shape[2], w = x.shape[3];
+    int64_t oh = h / kh, ow = w / kw;
+    if (x.split) {
+        DT y = split_out ? new_nhwc_split(ctx, n, ch, oh, ow) : new_nhwc(ctx, n, ch, oh, ow);
+        k::maxpool_split(ctx, reinterpret_cast<const uint16_t *>(x.p), x.strides[0], x.pix(), (int)n, (int)h, (int)w,
+                         (int)ch, kh, kw, (int)oh, (int)ow, y.p, y.strides[0], y.pix(), y.split ? 1 : 0);
+        return y;
+    }
+    x = to_nhwc(ctx, x);
+    KOut o = kout(ctx, nullptr, n, ch, oh, ow, false);
+    if (split_out) o.target = new_nhwc_split(ctx, n, ch, oh, ow), o.y = new_nhwc(ctx, n, ch, oh, ow), o.convert = true;
+    k::pool(ctx, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, (int)ch, kh, kw, kh, kw, 0, 0, (int)oh, (int)ow,
+            0, o.y.p, o.y.strides[0], o.y.pix());
+    return done(ctx, o);
+}
+
 // A convolution whose input is a split tensor: the tap convolution (stride 1, dense) or the
 // pointwise kernel; false when neither applies (the caller converts the input to fp32).
 static bool conv_split(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale,
-                       const OutAlloc *out, DT &y) {
+                       const OutAlloc *out, DT &y, PoolReq *pool) {
     if (res || scale || cw.kind != ConvW::DENSE || !x.nhwc()) return false;
     int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
     if (cw.cin != cin)
@@ -326,16 +347,35 @@ static bool conv_split(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *
     p.split_out = o.y.split;
     p.y_n = o.y.strides[0];
     p.y_pix = o.y.pix();
+    if (pool && !o.convert && cw.cout % 16 == 0) {
+        // the 2 x 2 MaxPool of this output, from the epilogue
+        pool->out = pool->split ? new_nhwc_split(c, n, cw.cout, oh / 2, ow / 2) : new_nhwc(c, n, cw.cout, oh / 2, ow / 2);
+        p.pool_y = pool->out.p;
+        p.pool_split = pool->out.split ? 1 : 0;
+        p.pool_n = pool->out.strides[0];
+        p.pool_pix = pool->out.pix();
+        pool->done = true;
+    }
     k::tconv(c, *cw.tw, p);
     y = done(c, o);
     return true;
 }
 
-DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale, const OutAlloc *out) {
+DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale, const OutAlloc *out,
+            PoolReq *pool) {
     if (xin.split) {
         DT y;
-        if (conv_split(c, xin, cw, act, res, scale, out, y)) return y;
-        return conv_run(c, to_f32(c, xin), cw, act, res, scale, out);
+        if (conv_split(c, xin, cw, act, res, scale, out, y, pool)) {
+            if (pool && !pool->done) pool->out = maxpool_run(c, y, 2, 2, pool->split), pool->done = true;
+            return y;
+        }
+        return conv_run(c, to_f32(c, xin), cw, act, res, scale, out, pool);
+    }
+    if (pool) {
+        DT y = conv_run(c, xin, cw, act, res, scale, out, nullptr);
+        pool->out = maxpool_run(c, y, 2, 2, pool->split);
+        pool->done = true;
+        return y;
     }
     DT x = to_nhwc(c, xin);
     int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
@@ -750,6 +790,20 @@ void Executor::finalize() {
         }
     }
     plan_split();
+    // 2 x 2 MaxPools computed in the epilogue of the tap convolution producing their input
+    for (auto &st : steps) st.pool_output.clear(), st.pool_fused_away = false;
+    if (allow_split) {
+        for (auto &mp : steps) {
+            if (mp.kind != Step::G_MAXPOOL || mp.conv.kh != 2 || mp.conv.kw != 2) continue;
+            auto pi = producer.find(mp.inputs[0]);
+            if (pi == producer.end()) continue;
+            Step &cs = steps[pi->second];
+            if (cs.kind != Step::G_CONV || !cs.conv.tw || !cs.pool_output.empty() || cs.conv.cout % 16) continue;
+            cs.pool_output = mp.output;
+            cs.pool_split = mp.split_out;
+            mp.pool_fused_away = true;
+        }
+    }
 }
 
 // The output of a step registered in concat_slot: a channel slice of the Concat buffer (made on
@@ -870,6 +924,15 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
     case Step::G_CONV:
     case Step::G_DIRECT:
     case Step::G_DEPTHWISE:
+        if (!s.pool_output.empty()) {
+            PoolReq pr;
+            pr.split = s.pool_split;
+            out.f = conv_run(ctx, getx(vals, s.inputs[0]), s.conv, s.act, nullptr, nullptr, &alloc_out, &pr);
+            Value pv;
+            pv.f = pr.out;
+            vals[s.pool_output] = pv;
+            break;
+        }
         out.f = conv_run(ctx, getx(vals, s.inputs[0]), s.conv, s.act, nullptr, nullptr, &alloc_out);
         break;
     case Step::N_CONV: {
@@ -896,25 +959,8 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
         break;
     }
     case Step::G_MAXPOOL: {
-        DT x = getx(vals, s.inputs[0]);
-        if (x.rank() != 4) fail(WOCR_ERR_SHAPE, "MaxPool input " + shape_str(x.shape));
-        if (x.split && !x.nhwc()) x = to_f32(ctx, x);
-        int64_t n = x.shape[0], ch = x.shape[1], h = x.shape[2], w = x.shape[3];
-        int kh = s.conv.kh, kw = s.conv.kw;
-        int64_t oh = h / kh, ow = w / kw;
-        if (x.split) {
-            DT y = s.split_out ? new_nhwc_split(ctx, n, ch, oh, ow) : new_nhwc(ctx, n, ch, oh, ow);
-            k::maxpool_split(ctx, reinterpret_cast<const uint16_t *>(x.p), x.strides[0], x.pix(), (int)n, (int)h,
-                             (int)w, (int)ch, kh, kw, (int)oh, (int)ow, y.p, y.strides[0], y.pix(), y.split ? 1 : 0);
-            out.f = y;
-            break;
-        }
-        x = to_nhwc(ctx, x);
-        KOut o = kout(ctx, nullptr, n, ch, oh, ow, false);
-        if (s.split_out) o.target = new_nhwc_split(ctx, n, ch, oh, ow), o.y = new_nhwc(ctx, n, ch, oh, ow), o.convert = true;
-        k::pool(ctx, x.p, x.strides[0], x.pix(), (int)n, (int)h, (int)w, (int)ch, kh, kw, kh, kw, 0, 0, (int)oh,
-                (int)ow, 0, o.y.p, o.y.strides[0], o.y.pix());
-        out.f = done(ctx, o);
+        if (s.pool_fused_away) return;  // computed by the producing convolution's epilogue
+        out.f = maxpool_run(ctx, getx(vals, s.inputs[0]), s.conv.kh, s.conv.kw, s.split_out);
         break;
     }
     case Step::G_SLICE: {

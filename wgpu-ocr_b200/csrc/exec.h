@@ -86,6 +86,10 @@ struct Step {
     float eps = 1e-5f;
     std::vector<int64_t> starts, ends, axes;  // G_SLICE
     bool split_out = false;               // the output is stored as a split tensor
+    // a 2 x 2 MaxPool of this convolution's output computed by its epilogue (pool_output named,
+    // split when pool_split); the MaxPool step itself is then skipped (pool_fused_away)
+    std::string pool_output;
+    bool pool_split = false, pool_fused_away = false;
 };
 
 class Executor {
@@ -139,8 +143,14 @@ DT to_nhwc(Ctx *c, const DT &x);
 DT to_f32(Ctx *c, const DT &x);  // a split tensor as fp32 NHWC; others unchanged
 DT to_rowmajor(Ctx *c, const DT &x);
 using OutAlloc = std::function<DT(int64_t n, int64_t c, int64_t h, int64_t w)>;
+// A 2 x 2 / stride 2 MaxPool wanted of a convolution's output: `out` receives it.
+struct PoolReq {
+    bool split = false;
+    bool done = false;
+    DT out;
+};
 DT conv_run(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale,
-            const OutAlloc *out = nullptr);
+            const OutAlloc *out = nullptr, PoolReq *pool = nullptr);
 DT linear_run(Ctx *c, const DT &x, const DevW &w, const DevW &b, int K, int N, int ldw, int act,
               const k::UmmaW *uw = nullptr);
 // [K][N] row-major fp32 weights -> the tensor-core operand of y = x W.

@@ -65,6 +65,9 @@ struct TcP {
     int64_t y_n, y_pix;
     int ow_out;                 // pixels per output row
     int scatter, scat_cout;
+    void *pool_y;               // fused 2 x 2 MaxPool output (null: none), oh / 2 x ow / 2
+    int pool_split, pool_vec;
+    int64_t pool_n, pool_pix;
     int *status;
 };
 
@@ -161,6 +164,41 @@ __device__ __forceinline__ void store16(const TcP &p, int64_t off, const float (
 // TAPS: 9 (3 x 3 kernel), 1 (1 x 1) or 0 (any kernel, taps counted at run time).
 // MB: 128-pixel MMA blocks per tile (2 for the narrow layers: one halo, the per-tile waits and
 // commits shared by 256 pixels).
+// 16 pooled channels at element offset `off` of the MaxPool output
+__device__ __forceinline__ void store_pool(const TcP &p, int64_t off, const float (&v)[16]) {
+    if (p.pool_split) {
+        uint16_t *y = reinterpret_cast<uint16_t *>(p.pool_y);
+        if (p.pool_vec) {
+            uint4 hi[2], lo[2];
+            split16(v, hi, lo);
+            uint4 *dh = reinterpret_cast<uint4 *>(y + off);
+            uint4 *dl = reinterpret_cast<uint4 *>(y + off + p.pool_pix / 2);
+            dh[0] = hi[0];
+            dh[1] = hi[1];
+            dl[0] = lo[0];
+            dl[1] = lo[1];
+            return;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+            __nv_bfloat16 h = __float2bfloat16_rn(v[j]);
+            __nv_bfloat16 l = __float2bfloat16_rn(v[j] - __bfloat162float(h));
+            y[off + j] = *reinterpret_cast<uint16_t *>(&h);
+            y[off + p.pool_pix / 2 + j] = *reinterpret_cast<uint16_t *>(&l);
+        }
+    } else {
+        float *y = reinterpret_cast<float *>(p.pool_y) + off;
+        if (p.pool_vec) {
+            float4 *d4 = reinterpret_cast<float4 *>(y);
+#pragma unroll
+            for (int j = 0; j < 4; j++) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 16; j++) y[j] = v[j];
+        }
+    }
+}
+
 template <int BN, int CG, int TAPS, int MB>
 __global__ void __launch_bounds__(kThreads, 1)
     k_tconv(const __grid_constant__ CUtensorMap wb_hi, const __grid_constant__ CUtensorMap wb_lo, TcP p) {
@@ -494,6 +532,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                     else tmem_ld16(tbase, v);
                 }
                 const int col = tl.nt * BN + c0;
+                if (p.pool_y && col + 16 <= p.N) {
+                    // plain store and the fused 2 x 2 MaxPool: every lane takes part in the
+                    // shuffles (lanes l, l + 1, l + 8, l + 9 hold a window), the window's top-left
+                    // lane stores the maximum
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[col + jj];
+                    act16(v, p.act);
+                    if (valid) store16(p, (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col, v);
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++) {
+                        float a = fmaxf(v[jj], __shfl_down_sync(0xffffffffu, v[jj], 1));
+                        v[jj] = fmaxf(a, __shfl_down_sync(0xffffffffu, a, 8));
+                    }
+                    if (valid && !(oy & 1) && !(ox & 1) && oy + 1 < p.oh && ox + 1 < p.ow)
+                        store_pool(p, (int64_t)tl.nb * p.pool_n + ((int64_t)(oy >> 1) * (p.ow >> 1) + (ox >> 1)) * p.pool_pix +
+                                          col,
+                                   v);
+                    continue;
+                }
                 if (!valid || col >= p.N) continue;
                 if (p.scatter) {
                     const int sc = p.scatter;
@@ -719,6 +776,16 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.scatter = q.scatter;
     p.scat_cout = q.scat_cout;
     p.ow_out = q.scatter ? q.ow * q.scatter : q.ow;
+    p.pool_y = q.pool_y;
+    p.pool_split = q.pool_split;
+    p.pool_n = q.pool_n;
+    p.pool_pix = q.pool_pix;
+    if (q.pool_y) {
+        if (q.scatter || w.N % 16) fail(WOCR_ERR_UNSUPPORTED, "fused MaxPool needs a plain output of 16-channel chunks");
+        const bool pal = (reinterpret_cast<uintptr_t>(q.pool_y) & 15) == 0;
+        p.pool_vec = q.pool_split ? (pal && q.pool_pix % 16 == 0 && q.pool_n % 8 == 0)
+                                  : (pal && q.pool_pix % 4 == 0 && q.pool_n % 4 == 0);
+    }
     p.status = c->status;
 
     const double flops = 2.0 * (double)M * w.N * w.taps * w.cin;

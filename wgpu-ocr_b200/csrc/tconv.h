@@ -34,6 +34,11 @@ struct TconvP {
     int split_out = 0;               // 1: y split like x (bf16 elements); 0: fp32 NHWC
     int64_t y_n = 0, y_pix = 0;
     int scatter = 0, scat_cout = 0;  // ConvTranspose kernel == stride s: N = cout * s * s
+    // fused 2 x 2 / stride 2 MaxPool of the output (null: none): [n][oh/2][ow/2] at pool_y,
+    // split like x (pool_split) or fp32, strides in elements of its format
+    void *pool_y = nullptr;
+    int pool_split = 0;
+    int64_t pool_n = 0, pool_pix = 0;
 };
 
 // The input view meets the TMA rules (16-byte aligned base, lo part and strides).
