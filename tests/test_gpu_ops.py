@@ -224,6 +224,31 @@ def test_graph_split_fallbacks(gpu):
     _det_parity(gpu, m, rnd(1, 1, 40, 56))
 
 
+@pytest.mark.parametrize("hw", [(52, 72), (36, 100), (404, 700)])
+@pytest.mark.parametrize("rows", [True, False])
+def test_graph_narrow_3x3_layers(gpu, hw, rows, monkeypatch):
+    """The narrow 3 x 3 layers (<= 32 output channels, <= 64 input channels) of a small U-Net,
+    by the row kernel (kernel columns stacked along N, the column sums gathered by shuffles)
+    and, with WOCR_NO_ROWS, by the per-tap kernel: 16 -> 16 with a fused MaxPool, 16 -> 32,
+    32 -> 32 with a fused MaxPool, 64 -> 32 and 32 -> 16 behind split Concats.  Widths that are
+    not multiples of the 14-column tile; 404 x 700 (283 K pixels) takes the two-block tiles."""
+    if not rows:
+        monkeypatch.setenv("WOCR_NO_ROWS", "1")
+    b = _Builder(21)
+    x0 = b.conv_relu("image", 1, 16, 3)
+    a0 = b.conv_relu(x0, 16, 16, 3)
+    a1 = b.conv_relu(b.maxpool(a0, 2, 2), 16, 32, 3)
+    a1b = b.conv_relu(a1, 32, 32, 3)
+    a2 = b.conv_relu(b.maxpool(a1b, 2, 2), 32, 64, 3)
+    u1 = b.op("Relu", [b.convt(a2, 64, 32, 2, 2)])
+    d1 = b.conv_relu(b.op("Concat", [u1, a1b], {"axis": 1}), 64, 32, 3)
+    u0 = b.op("Relu", [b.convt(d1, 32, 16, 2, 2)])
+    d0 = b.conv_relu(b.op("Concat", [u0, a0], {"axis": 1}), 32, 16, 3)
+    out = b.op("Sigmoid", [b.conv(d0, 16, 1, 1, pads=[0, 0, 0, 0])])
+    m = b.model("image", out)
+    _det_parity(gpu, m, rnd(1, 1, *hw))
+
+
 def test_unsupported_and_shape_errors(gpu):
     b = _Builder(10)
     y = b.op("LeakyRelu", ["x"])

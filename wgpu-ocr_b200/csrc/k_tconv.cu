@@ -28,6 +28,7 @@
 #include "tconv.h"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace wocr {
 namespace k {
@@ -599,6 +600,297 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Row kernel for the narrow 3 x 3 layers (N <= 32 output channels).  There k_tconv's MMAs are
+// 128 x 16 (or 32) x 16, and the tensor core's fixed cost per instruction, not its arithmetic,
+// sets the pace (18 MMAs per 128-pixel tile at 16 channels in).  Here the three kernel columns
+// kx are stacked along N instead.  An MMA block is RX = 8 image rows of RP = 16 positions
+// (M = 128, 8-position core-matrix groups, so one halo row is 256 bytes and kernel row dy is the
+// same halo RP * dy 16-byte units further); B is [w_hi(kx = 0, 1, 2); w_lo(kx = 0, 1, 2)] for C =
+// 16 or 32 output channels.  Per kernel row and 16-channel step:
+//   LO (C = 16): hi . [hi; lo] (N = 6 C) and lo . hi (N = 3 C, into the hi columns), the
+//                epilogue adding the hi and lo columns: 2 MMAs, 6 C accumulator columns;
+//   else (C = 32): hi . hi, hi . lo and lo . hi into the same 3 C columns: 3 MMAs, 3 C columns.
+// Position j of a row accumulates, per kx, the kernel-row sums for input column x0 + j; output
+// column x0 + i is the sum over kx of those at position i + kx, gathered by the epilogue with two
+// warp shuffles (a warp's 32 lanes are two rows of 16 positions).  Positions 14 and 15 only feed
+// that sum, so tiles advance RV = 14 columns.  The fused 2 x 2 MaxPool is a reduce-scatter over
+// each window's lanes l, l + 1, l + 16, l + 17, after which each of them stores 4 channels.
+//
+// The halo comes by TMA, one 4-D box (channels x RP positions x RX + 2 rows) per split part, in
+// the K-major swizzled layout whose rows are pixels of CG channels (CG = 16, 32, 64: 32-, 64-,
+// 128-byte swizzle): a kernel row is 16 pixel rows, two whole swizzle atoms, further; zeros
+// outside the image and past cin come from the TMA bounds.
+//
+// Warp roles (512 threads): warp 0 halo TMA, warp 1 tensor-memory allocation and MMA issue,
+// warps 4-15 three epilogue groups of four (one per lane quadrant) taking every third tile.  B (at
+// most 72 KB) is copied into shared memory once.
+constexpr int RX = 8, RP = 16, RV = 14;
+constexpr int kRGroups = 3, kRTmaW = 0, kRMmaW = 1, kRThreads = 32 * (4 + 4 * kRGroups);
+
+__device__ __forceinline__ Tile decode_rows(const TcP &p, int t) {
+    Tile r;
+    const uint32_t q1 = p.div_tx.div((uint32_t)t), q2 = p.div_ty.div(q1);
+    r.nt = 0;
+    r.ox0 = (t - (int)(q1 * p.div_tx.d)) * RV;
+    r.oy0 = (int)(q1 - q2 * p.div_ty.d) * RX;
+    r.nb = (int)q2;
+    return r;
+}
+
+// fused 2 x 2 MaxPool of 16 channels held by the lanes of each window (l, l + 1, l + 16, l + 17,
+// l even and below 16): after two exchange-and-max steps lane (odd, upper) holds the window's
+// channels 8 odd + 4 upper .. + 3, which it stores
+__device__ __forceinline__ void pool_rows(const TcP &p, const float (&v)[16], int lane, int64_t off, bool store) {
+    const bool odd = lane & 1, up = lane & 16;
+    float k8[8], k4[4];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float send = odd ? v[i] : v[8 + i];
+        const float got = __shfl_xor_sync(0xffffffffu, send, 1);
+        k8[i] = fmaxf(odd ? v[8 + i] : v[i], got);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float send = up ? k8[i] : k8[4 + i];
+        const float got = __shfl_xor_sync(0xffffffffu, send, 16);
+        k4[i] = fmaxf(up ? k8[4 + i] : k8[i], got);
+    }
+    if (!store) return;
+    off += (odd ? 8 : 0) + (up ? 4 : 0);
+    if (p.pool_split) {
+        uint16_t *y = reinterpret_cast<uint16_t *>(p.pool_y);
+        uint32_t h[2], l[2];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            __nv_bfloat162 hv = __floats2bfloat162_rn(k4[2 * i], k4[2 * i + 1]);
+            float2 hf = __bfloat1622float2(hv);
+            __nv_bfloat162 lv = __floats2bfloat162_rn(k4[2 * i] - hf.x, k4[2 * i + 1] - hf.y);
+            h[i] = *reinterpret_cast<uint32_t *>(&hv);
+            l[i] = *reinterpret_cast<uint32_t *>(&lv);
+        }
+        if (p.pool_vec) {
+            *reinterpret_cast<uint2 *>(y + off) = make_uint2(h[0], h[1]);
+            *reinterpret_cast<uint2 *>(y + off + p.pool_pix / 2) = make_uint2(l[0], l[1]);
+        } else {
+            uint16_t *dh = y + off, *dl = y + off + p.pool_pix / 2;
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                dh[2 * i] = (uint16_t)(h[i] & 0xffffu);
+                dh[2 * i + 1] = (uint16_t)(h[i] >> 16);
+                dl[2 * i] = (uint16_t)(l[i] & 0xffffu);
+                dl[2 * i + 1] = (uint16_t)(l[i] >> 16);
+            }
+        }
+    } else {
+        float *y = reinterpret_cast<float *>(p.pool_y) + off;
+        if (p.pool_vec) {
+            *reinterpret_cast<float4 *>(y) = make_float4(k4[0], k4[1], k4[2], k4[3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) y[i] = k4[i];
+        }
+    }
+}
+
+template <int C, int CG, bool LO>
+__global__ void __launch_bounds__(kRThreads, 1)
+    k_tconv_rows(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo,
+                 const uint16_t *__restrict__ wx, TcP p) {
+    constexpr int NPL = CG / 8;                 // 8-channel planes per split part
+    constexpr int NB = 6 * C;                   // B rows
+    constexpr int TCOLS = LO ? 6 * C : 3 * C;   // accumulator columns of a tile
+    constexpr int NACC = 512 / TCOLS < 8 ? 512 / TCOLS : 8;
+    constexpr uint32_t kCols = NACC * TCOLS <= 128 ? 128 : (NACC * TCOLS <= 256 ? 256 : 512);
+    constexpr uint32_t B_BYTES = 3u * NPL * NB * 16;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int SA = p.SA;
+    uint8_t *bsm = smem + p.b_off;
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + p.bar_off);
+    uint64_t *emptyA = fullA + SA;
+    uint64_t *tfull = emptyA + SA;
+    uint64_t *tempty = tfull + NACC;
+    uint64_t *drain = tempty + NACC;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    float *bias_s = reinterpret_cast<float *>(smem + p.bias_off);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < p.bias_n; i += blockDim.x) bias_s[i] = p.bias[i];
+    {
+        // the stacked weights, resident for the whole kernel: generic stores, made visible to
+        // the tensor cores by each writer's proxy fence before the barrier
+        const uint4 *src = reinterpret_cast<const uint4 *>(wx);
+        uint4 *dst = reinterpret_cast<uint4 *>(bsm);
+        for (int i = threadIdx.x; i < (int)(B_BYTES / 16); i += blockDim.x) dst[i] = src[i];
+        fence_async_smem();
+    }
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SA; s++) {
+            mbar_init(&fullA[s], 1);
+            mbar_init(&emptyA[s], 1);
+        }
+        for (int a = 0; a < NACC; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp == kRMmaW) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kRTmaW) {
+        // ---------------- halo TMA: the hi and the lo part of a tile's halo per stage ----------------
+        if (lane == 0) {
+            const uint32_t part = p.a_stage / 2;
+            int s = 0, ph = 0, issued = 0;
+            for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x) {
+                const Tile tl = decode_rows(p, t);
+                if (!mbar_wait(&emptyA[s], ph ^ 1, p.status, abort_flag, 31)) break;
+                uint8_t *a = smem + (uint32_t)s * p.a_stage;
+                mbar_expect_tx(&fullA[s], p.a_stage);
+                tma_load_4d(a, &x_hi, &fullA[s], 0, tl.ox0 - p.pl, tl.oy0 - p.pt, tl.nb);
+                tma_load_4d(a + part, &x_lo, &fullA[s], 0, tl.ox0 - p.pl, tl.oy0 - p.pt, tl.nb);
+                issued++;
+                if (++s == SA) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+            // the loads still in flight land before the CTA may exit (bounded)
+            for (int k = (issued > SA ? issued - SA : 0); k < issued; k++) {
+                long long t0 = clock64();
+                while (!mbar_try(&fullA[k % SA], (k / SA) & 1) && clock64() - t0 < kWaitBudget) {
+                }
+            }
+        }
+    } else if (warp == kRMmaW) {
+        // ---------------- MMA issue ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc_w = instr_desc(NB), idesc_3 = instr_desc(3 * C);
+            const uint32_t lo16 = p.a_stage >> 5;  // the lo part, half a stage further
+            const uint64_t db0 = smem_desc_plain(smem_u32(bsm), NB * 16, 128);
+            int sa = 0, pha = 0;
+            bool ok = true;
+            for (int t = blockIdx.x, lt = 0; t < p.ntiles && ok; t += gridDim.x, lt++) {
+                const int ab = lt % NACC;
+                ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 36);
+                if (!ok) break;
+                ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 33);
+                if (!ok) break;
+                tc_fence_after();
+                const uint64_t da0 = smem_desc_sw(smem_u32(smem + (uint32_t)sa * p.a_stage), CG * 2);
+                const uint32_t d = tmem + ab * TCOLS;
+#pragma unroll
+                for (int dy = 0; dy < 3; dy++)
+#pragma unroll
+                    for (int kk = 0; kk < CG / 16; kk++) {
+                        // kernel row dy: RP pixel rows of CG * 2 bytes further; 16 channels: 32 bytes
+                        const uint64_t da = da0 + (uint32_t)(dy * RP * CG * 2 / 16) + 2 * kk;
+                        const uint64_t db = db0 + (uint32_t)((dy * NPL + 2 * kk) * NB);
+                        const uint32_t acc = dy == 0 && kk == 0 ? 0u : 1u;
+                        if (LO) {
+                            umma(d, da, db, idesc_w, acc);                     // hi . [hi; lo]
+                            umma(d, da + lo16, db, idesc_3, 1u);               // lo . hi
+                        } else {
+                            umma(d, da, db, idesc_3, acc);                     // hi . hi
+                            umma(d, da, db + 3 * C, idesc_3, 1u);              // hi . lo
+                            umma(d, da + lo16, db, idesc_3, 1u);               // lo . hi
+                        }
+                    }
+                umma_commit(&emptyA[sa]);
+                if (++sa == SA) {
+                    sa = 0;
+                    pha ^= 1;
+                }
+                umma_commit(&tfull[ab]);
+            }
+            umma_commit(drain);
+            long long t0 = clock64();
+            while (!mbar_try(drain, 0) && clock64() - t0 < kWaitBudget) {
+            }
+        }
+    } else {
+        // ---------------- epilogue group g: tiles lt = g (mod 3), lane quadrant warp % 4 ----------------
+        const int q = warp & 3, g = (warp - 4) >> 2;
+        const int r = 2 * q + (lane >> 4), j = lane & 15;
+        int lt = 0;
+        for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, lt++) {
+            if (lt % kRGroups != g) continue;
+            const int ab = lt % NACC;
+            if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 35)) break;
+            tc_fence_after();
+            const Tile tl = decode_rows(p, t);
+            const int oy = tl.oy0 + r, ox = tl.ox0 + j;
+            const bool valid = j < RV && oy < p.oh && ox < p.ow;
+#pragma unroll 1
+            for (int c0 = 0; c0 < C; c0 += 16) {
+                const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + c0;
+                float v[16], s1[16], s2[16];
+                if (LO) {
+                    tmem_ld16_sum2(tb + C, tb + 4 * C, s1);      // kx = 1: hi + lo columns
+                    tmem_ld16_sum2(tb + 2 * C, tb + 5 * C, s2);  // kx = 2
+                    tmem_ld16_sum2(tb, tb + 3 * C, v);           // kx = 0
+                } else {
+                    tmem_ld16x3(tb, tb + C, tb + 2 * C, v, s1, s2);
+                }
+                const int col = c0;
+                const float4 *b4 = reinterpret_cast<const float4 *>(bias_s + col);
+#pragma unroll
+                for (int jj = 0; jj < 16; jj += 2) {
+                    const float2 sh = __fadd2_rn(make_float2(__shfl_down_sync(0xffffffffu, s1[jj], 1),
+                                                             __shfl_down_sync(0xffffffffu, s1[jj + 1], 1)),
+                                                 make_float2(__shfl_down_sync(0xffffffffu, s2[jj], 2),
+                                                             __shfl_down_sync(0xffffffffu, s2[jj + 1], 2)));
+                    const float4 bb = b4[jj >> 2];
+                    const float2 bj = (jj & 2) ? make_float2(bb.z, bb.w) : make_float2(bb.x, bb.y);
+                    const float2 o = __fadd2_rn(__fadd2_rn(make_float2(v[jj], v[jj + 1]), sh), bj);
+                    v[jj] = o.x;
+                    v[jj + 1] = o.y;
+                }
+                act16(v, p.act);
+                const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
+                if (p.pool_y) {
+                    // N % 16 == 0 (checked on the host): every chunk is whole
+                    if (valid) store16(p, off, v);
+                    const bool wv = j < RV && (oy | 1) < p.oh && (ox | 1) < p.ow;
+                    pool_rows(p, v, lane,
+                              (int64_t)tl.nb * p.pool_n + ((int64_t)(oy >> 1) * (p.ow >> 1) + (ox >> 1)) * p.pool_pix + col,
+                              wv);
+                    continue;
+                }
+                if (!valid || col >= p.N) continue;
+                if (col + 16 <= p.N) {
+                    store16(p, off, v);
+                } else {
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++)
+                        if (col + jj < p.N) store1(p, off + jj, v[jj]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[ab]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kRMmaW) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+    }
+}
+
 CUtensorMapSwizzle swizzle_of(int cg) {
     return cg == 16 ? CU_TENSOR_MAP_SWIZZLE_32B : (cg == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
@@ -647,6 +939,69 @@ void launch_taps(Ctx *c, const TconvW &w, const TcP &p, int smem, int kh, int kw
 
 int tconv_bn(int N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128; }
 
+template <int C, int CG>
+void launch_rows(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm) {
+    constexpr bool LO = C == 16;  // 2 MMAs over 6 C columns; C = 32: 3 MMAs over 3 C columns
+    static bool set[64] = {false};
+    if (!set[c->device]) {
+        WOCR_CUDA(cudaFuncSetAttribute(k_tconv_rows<C, CG, LO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       227 * 1024));
+        set[c->device] = true;
+    }
+    unsigned grid = (unsigned)std::min<int64_t>(p.ntiles, c->sm_count);
+    k_tconv_rows<C, CG, LO><<<grid, kRThreads, smem, c->stream>>>(xm[0], xm[1], reinterpret_cast<const uint16_t *>(w.x3->p),
+                                                                   p);
+    WOCR_LAUNCHED(c);
+}
+
+void launch_rows_any(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm) {
+    if (w.x3_cout == 16) {
+        if (w.x3_cg == 16) launch_rows<16, 16>(c, w, p, smem, xm);
+        else if (w.x3_cg == 32) launch_rows<16, 32>(c, w, p, smem, xm);
+        else launch_rows<16, 64>(c, w, p, smem, xm);
+    } else {
+        if (w.x3_cg == 16) launch_rows<32, 16>(c, w, p, smem, xm);
+        else if (w.x3_cg == 32) launch_rows<32, 32>(c, w, p, smem, xm);
+        else launch_rows<32, 64>(c, w, p, smem, xm);
+    }
+}
+
+// The row kernel's launch parameters (geometry, stages); false when its stages do not fit.
+bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap *xm) {
+    const int C = w.x3_cout, CG = w.x3_cg;
+    p.trows = RX;
+    p.tiles_x = (q.ow + RV - 1) / RV;
+    p.tiles_y = (q.oh + RX - 1) / RX;
+    p.ntn = 1;
+    const int64_t ntiles = (int64_t)q.n * p.tiles_x * p.tiles_y;
+    if (ntiles >= (int64_t)INT32_MAX) return false;
+    p.ntiles = (int)ntiles;
+    p.div_ntn = FastDiv(1);
+    p.div_tx = FastDiv((uint32_t)p.tiles_x);
+    p.div_ty = FastDiv((uint32_t)p.tiles_y);
+    p.hw_w = RP;
+    p.halo_px = (RX + 2) * RP;
+    p.plane = 0;
+    p.a_stage = (uint32_t)(2 * p.halo_px * CG * 2);  // hi part, lo part: multiples of 1024 bytes
+    // the halo boxes: [n][h][w][channels < cin] of the hi and of the lo parts, zeros outside
+    const cuuint64_t dims[4] = {(cuuint64_t)q.cin, (cuuint64_t)q.w, (cuuint64_t)q.h, (cuuint64_t)q.n};
+    const cuuint64_t strides[3] = {(cuuint64_t)q.x_pix * 2, (cuuint64_t)q.w * q.x_pix * 2, (cuuint64_t)q.x_n * 2};
+    const cuuint32_t box[4] = {(cuuint32_t)CG, (cuuint32_t)RP, (cuuint32_t)(RX + 2), 1};
+    encode(&xm[0], 4, const_cast<uint16_t *>(q.x), dims, strides, box, CG);
+    encode(&xm[1], 4, const_cast<uint16_t *>(q.x + q.x_pix / 2), dims, strides, box, CG);
+    const int b_region = (3 * (CG / 8) * 6 * C * 16 + 1023) / 1024 * 1024;
+    const int SA = std::min(8, (kSmemBudget - b_region) / (int)p.a_stage);
+    if (SA < 3) return false;
+    p.SA = SA;
+    p.SB = 0;
+    p.lag = std::min(kLagMax, SA - 2);
+    p.b_off = (uint32_t)SA * p.a_stage;
+    p.bar_off = p.b_off + (uint32_t)b_region;
+    p.bias_off = p.bar_off + 1024;
+    smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + 1024;
+    return smem <= 227 * 1024;
+}
+
 }  // namespace
 
 TconvW make_tconv_weights(Ctx *c, const std::vector<float> &wnk, int N, int taps, int cin) {
@@ -682,6 +1037,27 @@ TconvW make_tconv_weights(Ctx *c, const std::vector<float> &wnk, int N, int taps
     cuuint32_t box[2] = {(cuuint32_t)w.cg, (cuuint32_t)w.bn};
     encode(&w.map_hi, 2, w.hi->p, dims, strides, box, w.cg);
     encode(&w.map_lo, 2, w.lo->p, dims, strides, box, w.cg);
+    if (taps == 9 && N <= 32 && cin <= 64) {
+        // the row kernel's operand: [dy][8-channel plane][v 3 C + kx C + n][8], zeros past N
+        // and cin, copied verbatim into shared memory
+        const int C = N <= 16 ? 16 : 32, CG = cin <= 16 ? 16 : (cin <= 32 ? 32 : 64), NPL = CG / 8, NB = 6 * C;
+        std::vector<__nv_bfloat16> b((size_t)3 * NPL * NB * 8, __float2bfloat16_rn(0.f));
+        for (int dy = 0; dy < 3; dy++)
+            for (int kx = 0; kx < 3; kx++)
+                for (int n = 0; n < N; n++)
+                    for (int ci = 0; ci < cin; ci++) {
+                        const float v = wnk[((size_t)n * taps + dy * 3 + kx) * cin + ci];
+                        const __nv_bfloat16 h = __float2bfloat16_rn(v);
+                        const size_t o = ((size_t)(dy * NPL + ci / 8) * NB + kx * C + n) * 8 + ci % 8;
+                        b[o] = h;
+                        b[o + (size_t)3 * C * 8] = __float2bfloat16_rn(v - __bfloat162float(h));
+                    }
+        w.x3 = alloc(c, b.size() * 2);
+        WOCR_CUDA(cudaMemcpyAsync(w.x3->p, b.data(), b.size() * 2, cudaMemcpyHostToDevice, c->stream));
+        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        w.x3_cout = C;
+        w.x3_cg = CG;
+    }
     return w;
 }
 
@@ -711,6 +1087,46 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.n = q.n;
     p.oh = q.oh;
     p.ow = q.ow;
+    p.N = w.N;
+    p.pt = q.pt;
+    p.pl = q.pl;
+    p.bias_n = q.scatter ? q.scat_cout : w.N;
+    p.bias = q.bias;
+    p.act = q.act;
+    p.y = q.y;
+    p.split_out = q.split_out;
+    const bool al = (reinterpret_cast<uintptr_t>(q.y) & 15) == 0;
+    p.out_vec = q.split_out ? (al && q.y_pix % 16 == 0 && q.y_n % 8 == 0) : (al && q.y_pix % 4 == 0 && q.y_n % 4 == 0);
+    p.y_n = q.y_n;
+    p.y_pix = q.y_pix;
+    p.scatter = q.scatter;
+    p.scat_cout = q.scat_cout;
+    p.ow_out = q.scatter ? q.ow * q.scatter : q.ow;
+    p.pool_y = q.pool_y;
+    p.pool_split = q.pool_split;
+    p.pool_n = q.pool_n;
+    p.pool_pix = q.pool_pix;
+    if (q.pool_y) {
+        if (q.scatter || w.N % 16) fail(WOCR_ERR_UNSUPPORTED, "fused MaxPool needs a plain output of 16-channel chunks");
+        const bool pal = (reinterpret_cast<uintptr_t>(q.pool_y) & 15) == 0;
+        p.pool_vec = q.pool_split ? (pal && q.pool_pix % 16 == 0 && q.pool_n % 8 == 0)
+                                  : (pal && q.pool_pix % 4 == 0 && q.pool_n % 4 == 0);
+    }
+    p.status = c->status;
+    const double flops = 2.0 * (double)M * w.N * w.taps * w.cin;
+    const double bytes = 4.0 * ((double)q.n * q.h * q.w * q.cin + (double)M * w.N) + 4.0 * (double)w.N * w.taps * w.cin;
+    // the narrow 3 x 3 layers: kernel columns stacked along N (k_tconv_rows)
+    if (w.x3 && q.kh == 3 && q.kw == 3 && !q.scatter && !std::getenv("WOCR_NO_ROWS")) {
+        TcP pr = p;
+        int smem = 0;
+        CUtensorMap xm[2];
+        if (plan_rows(w, q, pr, smem, xm)) {
+            Prof pf(c, "tconv", flops, bytes);
+            launch_rows_any(c, w, pr, smem, xm);
+            c->flops += flops;
+            return;
+        }
+    }
     // two MMA blocks per tile for the narrow layers when there are tiles to spare
     const int mb = w.bn <= 32 && (int64_t)q.n * q.oh * q.ow >= (int64_t)c->sm_count * 256 * 8 ? 2 : 1;
     p.trows = TR * mb;
@@ -723,12 +1139,9 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.div_ntn = FastDiv((uint32_t)p.ntn);
     p.div_tx = FastDiv((uint32_t)p.tiles_x);
     p.div_ty = FastDiv((uint32_t)p.tiles_y);
-    p.N = w.N;
     p.nchunk = w.cin_pad / w.cg;
     p.taps = w.taps;
     p.kw = q.kw;
-    p.pt = q.pt;
-    p.pl = q.pl;
     p.cin_pad = w.cin_pad;
     p.hw_w = TP + q.kw - 1;
     if ((p.trows + q.kh - 1) * p.hw_w > 512) fail(WOCR_ERR_UNSUPPORTED, "tap convolution kernel too large");
@@ -760,36 +1173,10 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.SA = SA;
     p.SB = SB;
     p.lag = std::min(kLagMax, SA - 2);
-    p.bias_n = q.scatter ? q.scat_cout : w.N;
     p.bias_off = p.bar_off + 1024;
     const int smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + 1024;  // + alignment slack
     if (smem > 227 * 1024) fail(WOCR_ERR_UNSUPPORTED, "tap convolution bias too large");
 
-    p.bias = q.bias;
-    p.act = q.act;
-    p.y = q.y;
-    p.split_out = q.split_out;
-    const bool al = (reinterpret_cast<uintptr_t>(q.y) & 15) == 0;
-    p.out_vec = q.split_out ? (al && q.y_pix % 16 == 0 && q.y_n % 8 == 0) : (al && q.y_pix % 4 == 0 && q.y_n % 4 == 0);
-    p.y_n = q.y_n;
-    p.y_pix = q.y_pix;
-    p.scatter = q.scatter;
-    p.scat_cout = q.scat_cout;
-    p.ow_out = q.scatter ? q.ow * q.scatter : q.ow;
-    p.pool_y = q.pool_y;
-    p.pool_split = q.pool_split;
-    p.pool_n = q.pool_n;
-    p.pool_pix = q.pool_pix;
-    if (q.pool_y) {
-        if (q.scatter || w.N % 16) fail(WOCR_ERR_UNSUPPORTED, "fused MaxPool needs a plain output of 16-channel chunks");
-        const bool pal = (reinterpret_cast<uintptr_t>(q.pool_y) & 15) == 0;
-        p.pool_vec = q.pool_split ? (pal && q.pool_pix % 16 == 0 && q.pool_n % 8 == 0)
-                                  : (pal && q.pool_pix % 4 == 0 && q.pool_n % 4 == 0);
-    }
-    p.status = c->status;
-
-    const double flops = 2.0 * (double)M * w.N * w.taps * w.cin;
-    const double bytes = 4.0 * ((double)q.n * q.h * q.w * q.cin + (double)M * w.N) + 4.0 * (double)w.N * w.taps * w.cin;
     Prof pf(c, q.scatter ? "tconv_convt" : "tconv", flops, bytes);
     if (w.cg == 16) launch_taps<16>(c, w, p, smem, q.kh, q.kw);
     else launch_taps<32>(c, w, p, smem, q.kh, q.kw);

@@ -115,6 +115,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
 // K-major operand tile in the 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
@@ -168,7 +177,40 @@ __device__ __forceinline__ void tmem_ld16_sum2(uint32_t a0, uint32_t a1, float (
         : "r"(a0), "r"(a1)
         : "memory");
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]) + __uint_as_float(r[16 + i]);
+    for (int i = 0; i < 16; i += 2) {
+        const float2 a = __fadd2_rn(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])),
+                                    make_float2(__uint_as_float(r[16 + i]), __uint_as_float(r[17 + i])));
+        v[i] = a.x;
+        v[i + 1] = a.y;
+    }
+}
+
+// Three 16-column loads, one wait.
+__device__ __forceinline__ void tmem_ld16x3(uint32_t a0, uint32_t a1, uint32_t a2, float (&v0)[16], float (&v1)[16],
+                                            float (&v2)[16]) {
+    uint32_t r[48];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%48];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31}, [%49];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, "
+        "%45, %46, %47}, [%50];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47])
+        : "r"(a0), "r"(a1), "r"(a2)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+        v0[i] = __uint_as_float(r[i]);
+        v1[i] = __uint_as_float(r[16 + i]);
+        v2[i] = __uint_as_float(r[32 + i]);
+    }
 }
 
 // Four 16-column loads, one wait: v = the sum of the four.

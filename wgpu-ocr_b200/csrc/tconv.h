@@ -15,6 +15,11 @@ struct TconvW {
     BufP hi, lo;
     CUtensorMap map_hi, map_lo;
     int N = 0, taps = 0, cin = 0, cin_pad = 0, cg = 0, bn = 0;
+    // 3 x 3 kernels with N <= 32 and cin <= 64 also get the column-stacked operand of the row
+    // kernel (k_tconv_rows): per kernel row dy and 8-channel plane, 6 x3_cout rows of 8 bf16, row
+    // v 3 x3_cout + kx x3_cout + n holding the hi (v = 0) or lo (v = 1) part of w[n][dy][kx]
+    BufP x3;
+    int x3_cout = 0, x3_cg = 0;
 };
 
 // wnk: [N][taps][cin] fp32 (taps in (ky, kx) order).
