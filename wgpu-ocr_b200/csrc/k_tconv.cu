@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const Tile tl = decode(p, t);
                     for (int ch = 0; ch < p.nchunk && ok; ch++)
                         for (int tap = 0; tap < p.taps; tap++, issued++) {
-                            if (!mbar_wait(&emptyB[s], ph ^ 1, p.status, abort_flag, 22)) {
+                            if (!mbar_wait_spin(&emptyB[s], ph ^ 1, p.status, abort_flag, 22)) {
                                 ok = false;
                                 break;
                             }
@@ -405,14 +405,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int ab = lt % NACC;
                 const uint32_t dtile = tmem + ab * TCOLS;
                 const int nt = t - (int)(p.div_ntn.div((uint32_t)t) * p.div_ntn.d);
-                ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 26);
+                ok = mbar_wait_spin(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 26);
                 if (!ok) break;
                 tc_fence_after();
                 if (p.b_res) {
                     // resident B: the only commits inside a tile end a chunk; chunks alternate
                     // between the two accumulators, the first two chunks start them
                     for (int ch = 0; ch < p.nchunk && ok; ch++) {
-                        ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 23);
+                        ok = mbar_wait_spin(&fullA[sa], pha, p.status, abort_flag, 23);
                         if (!ok) break;
                         tc_fence_after();
                         const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
@@ -452,12 +452,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int par = 0;
                     uint32_t fresh = 3;  // accumulators not yet written in this tile
                     for (int ch = 0; ch < p.nchunk && ok; ch++) {
-                        ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 23);
+                        ok = mbar_wait_spin(&fullA[sa], pha, p.status, abort_flag, 23);
                         if (!ok) break;
                         tc_fence_after();
                         const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
                         for (int tap = 0; tap < taps; tap++) {
-                            ok = mbar_wait(&fullB[sb], phb, p.status, abort_flag, 24);
+                            ok = mbar_wait_spin(&fullB[sb], phb, p.status, abort_flag, 24);
                             if (!ok) break;
                             tc_fence_after();
                             const uint64_t db = smem_desc_sw(bsm32 + (uint32_t)sb * 2 * B_BYTES, RB);
@@ -620,11 +620,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // The halo comes by TMA, one 4-D box (channels x RP positions x RX + 2 rows) per split part, in
 // the K-major swizzled layout whose rows are pixels of CG channels (CG = 16, 32, 64: 32-, 64-,
 // 128-byte swizzle): a kernel row is 16 pixel rows, two whole swizzle atoms, further; zeros
-// outside the image and past cin come from the TMA bounds.
+// outside the image and past cin come from the TMA bounds.  WHOLE: the view is its whole buffer
+// (a pixel is cin hi parts then cin lo parts, cin = CG <= 32), so one box of whole pixels (64- or
+// 128-byte rows) brings both parts, the lo part CG elements along the row: half the TMA lines,
+// twice as long, whose rate bounds these layers.
 //
 // Warp roles (512 threads): warp 0 halo TMA, warp 1 tensor-memory allocation and MMA issue,
 // warps 4-15 three epilogue groups of four (one per lane quadrant) taking every third tile.  B (at
-// most 72 KB) is copied into shared memory once.
+// most 72 KB) is copied into shared memory once.  Every barrier check or commit on the MMA thread
+// stalls its issue (an MMA is only accepted when the tensor core takes it, so the pipe drains
+// meanwhile: about 100 cycles a check), so the thread has one of each per tile: the TMA thread
+// loads a tile's halo only once the tile's accumulator buffer is free, making the stage's full
+// barrier mean both, and the epilogue group that sees a tile's MMAs complete releases its stage.
 constexpr int RX = 8, RP = 16, RV = 14;
 constexpr int kRGroups = 3, kRTmaW = 0, kRMmaW = 1, kRThreads = 32 * (4 + 4 * kRGroups);
 
@@ -693,7 +700,7 @@ __device__ __forceinline__ void pool_rows(const TcP &p, const float (&v)[16], in
     }
 }
 
-template <int C, int CG, bool LO>
+template <int C, int CG, bool LO, bool WHOLE>
 __global__ void __launch_bounds__(kRThreads, 1)
     k_tconv_rows(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo,
                  const uint16_t *__restrict__ wx, TcP p) {
@@ -756,11 +763,13 @@ __global__ void __launch_bounds__(kRThreads, 1)
             int s = 0, ph = 0, issued = 0;
             for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x) {
                 const Tile tl = decode_rows(p, t);
-                if (!mbar_wait(&emptyA[s], ph ^ 1, p.status, abort_flag, 31)) break;
+                if (!mbar_wait_spin(&emptyA[s], ph ^ 1, p.status, abort_flag, 31)) break;
+                // the tile's accumulator buffer is free (its previous tile's epilogue is done)
+                if (!mbar_wait_spin(&tempty[issued % NACC], ((issued / NACC) & 1) ^ 1, p.status, abort_flag, 36)) break;
                 uint8_t *a = smem + (uint32_t)s * p.a_stage;
                 mbar_expect_tx(&fullA[s], p.a_stage);
                 tma_load_4d(a, &x_hi, &fullA[s], 0, tl.ox0 - p.pl, tl.oy0 - p.pt, tl.nb);
-                tma_load_4d(a + part, &x_lo, &fullA[s], 0, tl.ox0 - p.pl, tl.oy0 - p.pt, tl.nb);
+                if (!WHOLE) tma_load_4d(a + part, &x_lo, &fullA[s], 0, tl.ox0 - p.pl, tl.oy0 - p.pt, tl.nb);
                 issued++;
                 if (++s == SA) {
                     s = 0;
@@ -778,25 +787,26 @@ __global__ void __launch_bounds__(kRThreads, 1)
         // ---------------- MMA issue ----------------
         if (lane == 0) {
             constexpr uint32_t idesc_w = instr_desc(NB), idesc_3 = instr_desc(3 * C);
-            const uint32_t lo16 = p.a_stage >> 5;  // the lo part, half a stage further
+            constexpr int ROWB = WHOLE ? 4 * CG : 2 * CG;  // bytes of a halo pixel row
+            // the lo part: CG elements along the row, or half a stage further
+            const uint32_t lo16 = WHOLE ? CG / 8 : p.a_stage >> 5;
             const uint64_t db0 = smem_desc_plain(smem_u32(bsm), NB * 16, 128);
             int sa = 0, pha = 0;
             bool ok = true;
             for (int t = blockIdx.x, lt = 0; t < p.ntiles && ok; t += gridDim.x, lt++) {
                 const int ab = lt % NACC;
-                ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 36);
-                if (!ok) break;
-                ok = mbar_wait(&fullA[sa], pha, p.status, abort_flag, 33);
+                // the halo has landed and the accumulator buffer is free
+                ok = mbar_wait_spin(&fullA[sa], pha, p.status, abort_flag, 33);
                 if (!ok) break;
                 tc_fence_after();
-                const uint64_t da0 = smem_desc_sw(smem_u32(smem + (uint32_t)sa * p.a_stage), CG * 2);
+                const uint64_t da0 = smem_desc_sw(smem_u32(smem + (uint32_t)sa * p.a_stage), ROWB);
                 const uint32_t d = tmem + ab * TCOLS;
 #pragma unroll
                 for (int dy = 0; dy < 3; dy++)
 #pragma unroll
                     for (int kk = 0; kk < CG / 16; kk++) {
-                        // kernel row dy: RP pixel rows of CG * 2 bytes further; 16 channels: 32 bytes
-                        const uint64_t da = da0 + (uint32_t)(dy * RP * CG * 2 / 16) + 2 * kk;
+                        // kernel row dy: RP pixel rows further; 16 channels: 32 bytes
+                        const uint64_t da = da0 + (uint32_t)(dy * RP * ROWB / 16) + 2 * kk;
                         const uint64_t db = db0 + (uint32_t)((dy * NPL + 2 * kk) * NB);
                         const uint32_t acc = dy == 0 && kk == 0 ? 0u : 1u;
                         if (LO) {
@@ -808,12 +818,11 @@ __global__ void __launch_bounds__(kRThreads, 1)
                             umma(d, da + lo16, db, idesc_3, 1u);               // lo . hi
                         }
                     }
-                umma_commit(&emptyA[sa]);
                 if (++sa == SA) {
                     sa = 0;
                     pha ^= 1;
                 }
-                umma_commit(&tfull[ab]);
+                umma_commit(&tfull[ab]);  // the epilogue group then releases the stage
             }
             umma_commit(drain);
             long long t0 = clock64();
@@ -830,6 +839,8 @@ __global__ void __launch_bounds__(kRThreads, 1)
             const int ab = lt % NACC;
             if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 35)) break;
             tc_fence_after();
+            // the tile's MMAs are complete: its halo stage may be refilled
+            if (q == 0 && lane == 0) mbar_arrive(&emptyA[lt % SA]);
             const Tile tl = decode_rows(p, t);
             const int oy = tl.oy0 + r, ox = tl.ox0 + j;
             const bool valid = j < RV && oy < p.oh && ox < p.ow;
@@ -939,35 +950,35 @@ void launch_taps(Ctx *c, const TconvW &w, const TcP &p, int smem, int kh, int kw
 
 int tconv_bn(int N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128; }
 
-template <int C, int CG>
+template <int C, int CG, bool WHOLE>
 void launch_rows(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm) {
     constexpr bool LO = C == 16;  // 2 MMAs over 6 C columns; C = 32: 3 MMAs over 3 C columns
     static bool set[64] = {false};
     if (!set[c->device]) {
-        WOCR_CUDA(cudaFuncSetAttribute(k_tconv_rows<C, CG, LO>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        WOCR_CUDA(cudaFuncSetAttribute(k_tconv_rows<C, CG, LO, WHOLE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        227 * 1024));
         set[c->device] = true;
     }
     unsigned grid = (unsigned)std::min<int64_t>(p.ntiles, c->sm_count);
-    k_tconv_rows<C, CG, LO><<<grid, kRThreads, smem, c->stream>>>(xm[0], xm[1], reinterpret_cast<const uint16_t *>(w.x3->p),
-                                                                   p);
+    k_tconv_rows<C, CG, LO, WHOLE><<<grid, kRThreads, smem, c->stream>>>(
+        xm[0], xm[1], reinterpret_cast<const uint16_t *>(w.x3->p), p);
     WOCR_LAUNCHED(c);
 }
 
-void launch_rows_any(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm) {
+void launch_rows_any(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm, bool whole) {
     if (w.x3_cout == 16) {
-        if (w.x3_cg == 16) launch_rows<16, 16>(c, w, p, smem, xm);
-        else if (w.x3_cg == 32) launch_rows<16, 32>(c, w, p, smem, xm);
-        else launch_rows<16, 64>(c, w, p, smem, xm);
+        if (w.x3_cg == 16) whole ? launch_rows<16, 16, true>(c, w, p, smem, xm) : launch_rows<16, 16, false>(c, w, p, smem, xm);
+        else if (w.x3_cg == 32) whole ? launch_rows<16, 32, true>(c, w, p, smem, xm) : launch_rows<16, 32, false>(c, w, p, smem, xm);
+        else launch_rows<16, 64, false>(c, w, p, smem, xm);
     } else {
-        if (w.x3_cg == 16) launch_rows<32, 16>(c, w, p, smem, xm);
-        else if (w.x3_cg == 32) launch_rows<32, 32>(c, w, p, smem, xm);
-        else launch_rows<32, 64>(c, w, p, smem, xm);
+        if (w.x3_cg == 16) whole ? launch_rows<32, 16, true>(c, w, p, smem, xm) : launch_rows<32, 16, false>(c, w, p, smem, xm);
+        else if (w.x3_cg == 32) whole ? launch_rows<32, 32, true>(c, w, p, smem, xm) : launch_rows<32, 32, false>(c, w, p, smem, xm);
+        else launch_rows<32, 64, false>(c, w, p, smem, xm);
     }
 }
 
 // The row kernel's launch parameters (geometry, stages); false when its stages do not fit.
-bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap *xm) {
+bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap *xm, bool &whole) {
     const int C = w.x3_cout, CG = w.x3_cg;
     p.trows = RX;
     p.tiles_x = (q.ow + RV - 1) / RV;
@@ -987,8 +998,17 @@ bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap 
     const cuuint64_t dims[4] = {(cuuint64_t)q.cin, (cuuint64_t)q.w, (cuuint64_t)q.h, (cuuint64_t)q.n};
     const cuuint64_t strides[3] = {(cuuint64_t)q.x_pix * 2, (cuuint64_t)q.w * q.x_pix * 2, (cuuint64_t)q.x_n * 2};
     const cuuint32_t box[4] = {(cuuint32_t)CG, (cuuint32_t)RP, (cuuint32_t)(RX + 2), 1};
-    encode(&xm[0], 4, const_cast<uint16_t *>(q.x), dims, strides, box, CG);
-    encode(&xm[1], 4, const_cast<uint16_t *>(q.x + q.x_pix / 2), dims, strides, box, CG);
+    whole = CG <= 32 && q.cin == CG && q.x_pix == 2 * CG;
+    if (whole) {
+        // whole pixels: [n][h][w][2 CG] (the hi and the lo parts), rows of 4 CG bytes
+        const cuuint64_t dw[4] = {(cuuint64_t)q.x_pix, (cuuint64_t)q.w, (cuuint64_t)q.h, (cuuint64_t)q.n};
+        const cuuint32_t bw[4] = {(cuuint32_t)(2 * CG), (cuuint32_t)RP, (cuuint32_t)(RX + 2), 1};
+        encode(&xm[0], 4, const_cast<uint16_t *>(q.x), dw, strides, bw, 2 * CG);
+        xm[1] = xm[0];
+    } else {
+        encode(&xm[0], 4, const_cast<uint16_t *>(q.x), dims, strides, box, CG);
+        encode(&xm[1], 4, const_cast<uint16_t *>(q.x + q.x_pix / 2), dims, strides, box, CG);
+    }
     const int b_region = (3 * (CG / 8) * 6 * C * 16 + 1023) / 1024 * 1024;
     const int SA = std::min(8, (kSmemBudget - b_region) / (int)p.a_stage);
     if (SA < 3) return false;
@@ -1120,9 +1140,10 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
         TcP pr = p;
         int smem = 0;
         CUtensorMap xm[2];
-        if (plan_rows(w, q, pr, smem, xm)) {
+        bool whole = false;
+        if (plan_rows(w, q, pr, smem, xm, whole)) {
             Prof pf(c, "tconv", flops, bytes);
-            launch_rows_any(c, w, pr, smem, xm);
+            launch_rows_any(c, w, pr, smem, xm, whole);
             c->flops += flops;
             return;
         }

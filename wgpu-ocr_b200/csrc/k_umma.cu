@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 const int n0 = (int)(t % ntn) * BN;
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 12)) {
+                    if (!mbar_wait_spin(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 12)) {
                         ok = false;
                         break;
                     }
@@ -319,14 +319,14 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
                 const int ab = lt % NACC;
                 const uint32_t dcol = tmem + ab * TCOLS;
-                ok = mbar_wait(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 16);
+                ok = mbar_wait_spin(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 16);
                 if (!ok) break;
                 tc_fence_after();
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % STAGES;
                     const uint32_t par = (it / STAGES) & 1;
-                    ok = mbar_wait(&afull[s], par, p.status, abort_flag, 13) &&
-                         mbar_wait(&bfull[s], par, p.status, abort_flag, 14);
+                    ok = mbar_wait_spin(&afull[s], par, p.status, abort_flag, 13) &&
+                         mbar_wait_spin(&bfull[s], par, p.status, abort_flag, 14);
                     if (!ok) break;
                     tc_fence_after();
                     uint8_t *base = smem + s * Lay::stage_bytes;

@@ -95,6 +95,36 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *s
     return true;
 }
 
+// Non-blocking test of a phase (never suspends the thread).
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// mbar_wait for the single threads that issue MMAs or TMA copies: a spin on test_wait, so the
+// thread reacts to the phase at once instead of after a suspended thread's wake-up; bounded alike.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
+                                               int code) {
+    if (mbar_test(bar, parity)) return true;
+    long long t0 = clock64();
+    while (!mbar_test(bar, parity)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitBudget) {
+            *abort_flag = 1;
+            atomicCAS(status, 0, code);
+            return false;
+        }
+    }
+    return true;
+}
+
 // One lane polls, the warp follows: a warp-uniform outcome for warp-wide code after the wait.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
                                           int code) {
