@@ -55,6 +55,7 @@ struct TcP {
     int two_acc;                // the tile's MMAs alternate between two accumulators
     int hw_w, halo_px;          // halo row length and pixel count
     uint32_t plane, a_stage;    // bytes of one 8-channel halo plane, of one A stage
+    uint32_t b_stage;           // bytes of one B ring stage (every tap of a chunk)
     int SA, SB, lag, b_res;     // A stages, B ring stages, cp.async stages in flight, B resident
     uint32_t b_off, bar_off;    // shared-memory offsets of the B region and the barriers
     const float *bias;
@@ -355,22 +356,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 bool ok = true;
                 for (int t = blockIdx.x; t < p.ntiles && ok; t += gridDim.x) {
                     const Tile tl = decode(p, t);
-                    for (int ch = 0; ch < p.nchunk && ok; ch++)
-                        for (int tap = 0; tap < p.taps; tap++, issued++) {
-                            if (!mbar_wait_spin(&emptyB[s], ph ^ 1, p.status, abort_flag, 22)) {
-                                ok = false;
-                                break;
-                            }
-                            uint8_t *dst = bsm + (uint32_t)s * 2 * B_BYTES;
-                            mbar_expect_tx(&fullB[s], 2 * B_BYTES);
-                            const int kx0 = tap * p.cin_pad + ch * CG;
-                            tma_load_2d(dst, &wb_hi, &fullB[s], kx0, tl.nt * BN);
-                            tma_load_2d(dst + B_BYTES, &wb_lo, &fullB[s], kx0, tl.nt * BN);
-                            if (++s == SB) {
-                                s = 0;
-                                ph ^= 1;
-                            }
+                    for (int ch = 0; ch < p.nchunk && ok; ch++, issued++) {
+                        // one stage: every tap of the chunk, hi and lo
+                        if (!mbar_wait_spin(&emptyB[s], ph ^ 1, p.status, abort_flag, 22)) {
+                            ok = false;
+                            break;
                         }
+                        uint8_t *dst = bsm + (uint32_t)s * p.b_stage;
+                        mbar_expect_tx(&fullB[s], (uint32_t)p.taps * 2 * B_BYTES);
+                        for (int tap = 0; tap < p.taps; tap++) {
+                            const int kx0 = tap * p.cin_pad + ch * CG;
+                            tma_load_2d(dst + (uint32_t)tap * 2 * B_BYTES, &wb_hi, &fullB[s], kx0, tl.nt * BN);
+                            tma_load_2d(dst + (uint32_t)tap * 2 * B_BYTES + B_BYTES, &wb_lo, &fullB[s], kx0, tl.nt * BN);
+                        }
+                        if (++s == SB) {
+                            s = 0;
+                            ph ^= 1;
+                        }
+                    }
                 }
                 // drain: the last SB issued loads land before the CTA may exit (bounded)
                 for (int j = (issued > SB ? issued - SB : 0); j < issued; j++) {
@@ -448,29 +451,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 } else {
-                    // B through the ring: a commit after every tap, which alternates the accumulator
-                    int par = 0;
-                    uint32_t fresh = 3;  // accumulators not yet written in this tile
+                    // B through the ring, a stage per chunk with all its taps: one wait and one
+                    // commit per chunk; chunks alternate between the two accumulators
                     for (int ch = 0; ch < p.nchunk && ok; ch++) {
-                        ok = mbar_wait_spin(&fullA[sa], pha, p.status, abort_flag, 23);
+                        ok = mbar_wait_spin(&fullA[sa], pha, p.status, abort_flag, 23) &&
+                             mbar_wait_spin(&fullB[sb], phb, p.status, abort_flag, 24);
                         if (!ok) break;
                         tc_fence_after();
                         const uint64_t da0 = smem_desc_plain(smem_u32(smem + (uint32_t)sa * p.a_stage), p.plane, sbo);
-                        for (int tap = 0; tap < taps; tap++) {
-                            ok = mbar_wait_spin(&fullB[sb], phb, p.status, abort_flag, 24);
-                            if (!ok) break;
-                            tc_fence_after();
-                            const uint64_t db = smem_desc_sw(bsm32 + (uint32_t)sb * 2 * B_BYTES, RB);
-                            const uint32_t d = dtile + par * ACCW;
-                            const uint32_t acc0 = (fresh >> par) & 1 ? 0u : 1u;
-                            fresh &= ~(1u << par);
+                        uint64_t db = smem_desc_sw(bsm32 + (uint32_t)sb * p.b_stage, RB);
+                        const uint32_t d = dtile + (ch & 1) * ACCW;
+                        const uint32_t acc0 = ch >= 2 ? 1u : 0u;
+#pragma unroll
+                        for (int tap = 0; tap < (TAPS ? TAPS : 64); tap++) {
+                            if (!TAPS && tap >= taps) break;
 #pragma unroll
                             for (int b = 0; b < MB; b++) {
                                 const uint64_t da = da0 + (uint32_t)((tap / kw) * hw_w + tap % kw) + b * blk16;
                                 const uint32_t db_d = d + b * 2 * ACCW;
-                                uint32_t acc = acc0;
 #pragma unroll
                                 for (int kk = 0; kk < CG / 16; kk++) {
+                                    const uint32_t acc = tap == 0 && kk == 0 ? acc0 : 1u;
                                     if (STACK) {
                                         umma(db_d, da + ahi_off[kk], db + 2 * kk, idesc2, acc);
                                         umma(db_d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
@@ -479,17 +480,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                                         umma(db_d, da + ahi_off[kk], db + b16 + 2 * kk, idesc, 1u);
                                         umma(db_d, da + alo_off[kk], db + 2 * kk, idesc, 1u);
                                     }
-                                    acc = 1u;
                                 }
                             }
-                            umma_commit(&emptyB[sb]);
-                            par ^= 1;
-                            if (++sb == SB) {
-                                sb = 0;
-                                phb ^= 1;
-                            }
+                            db += 2 * b16;
                         }
-                        if (!ok) break;
+                        umma_commit(&emptyB[sb]);
+                        if (++sb == SB) {
+                            sb = 0;
+                            phb ^= 1;
+                        }
                         umma_commit(&emptyA[sa]);
                         if (++sa == SA) {
                             sa = 0;
@@ -1031,9 +1030,12 @@ TconvW make_tconv_weights(Ctx *c, const std::vector<float> &wnk, int N, int taps
     w.cin = cin;
     // the widest chunk that fits in cin (a last partial chunk reads zeros past cin)
     if (cin < 16) fail(WOCR_ERR_UNSUPPORTED, "tap convolution with fewer than 16 input channels");
-    w.cg = cin >= 32 ? 32 : 16;
-    w.cin_pad = (cin + w.cg - 1) / w.cg * w.cg;
     w.bn = tconv_bn(N);
+    // B through the ring (over 96 KB) with several taps: 16-channel chunks, so a ring stage (every
+    // tap of a chunk) stays near 36 KB (N tile 64) or 72 KB (128)
+    const int64_t b_all16 = (int64_t)((N + w.bn - 1) / w.bn) * taps * ((cin + 15) / 16 * 16) * w.bn * 4;
+    w.cg = cin >= 32 && !(taps > 1 && b_all16 > 96 * 1024) ? 32 : 16;
+    w.cin_pad = (cin + w.cg - 1) / w.cg * w.cg;
     const int Npad = (N + w.bn - 1) / w.bn * w.bn;  // every TMA box lies inside the tensor
     const int64_t K = (int64_t)taps * w.cin_pad;
     std::vector<__nv_bfloat16> hi((size_t)Npad * K, __float2bfloat16_rn(0.f)), lo = hi;
@@ -1183,14 +1185,15 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
         p.bar_off = p.b_off + (uint32_t)b_region;
     } else {
         p.b_res = 0;
-        SB = std::min(8, std::max(2, (kSmemBudget / 2) / (2 * b_half)));
-        SA = std::min(8, (kSmemBudget - SB * 2 * b_half) / (int)p.a_stage);
+        p.b_stage = (uint32_t)(w.taps * 2 * b_half);
+        SB = std::min(8, std::max(2, (kSmemBudget / 2) / (int)p.b_stage));
+        SA = std::min(8, (kSmemBudget - SB * (int)p.b_stage) / (int)p.a_stage);
         p.b_off = (uint32_t)SA * p.a_stage;
-        p.bar_off = p.b_off + (uint32_t)((SB * 2 * b_half + 1023) / 1024 * 1024);
+        p.bar_off = p.b_off + (uint32_t)((SB * p.b_stage + 1023) / 1024 * 1024);
     }
     if (SA < 2) fail(WOCR_ERR_UNSUPPORTED, "tap convolution halo does not fit twice");
     // a second accumulator is written when a tile has a commit before its last MMA
-    p.two_acc = p.b_res ? (p.nchunk > 1) : (w.taps * p.nchunk > 1);
+    p.two_acc = p.nchunk > 1;
     p.SA = SA;
     p.SB = SB;
     p.lag = std::min(kLagMax, SA - 2);
