@@ -607,9 +607,12 @@ void mask_up(Ctx *c, const float *m, int stride, int64_t plane, int n, int vw, i
     Prof pf(c, "mask_up", 0, (double)n * ((double)vh * vw * 4 + (double)h * ((w + 31) / 32) * 4));
     int words = (w + 31) / 32;
     int warps = (words + 31) / 32;
-    dim3 grid((warps * 32 + kThreads - 1) / kThreads, h, n);
-    k_mask_up<<<grid, kThreads, 0, c->stream>>>(m, stride, plane, vw, vh, w, h, words, (float)vw / (float)w,
-                                                (float)vh / (float)h, thr, bits);
+    // one block per page row: exactly the row's warps (3 for a 2550-pixel page), so no idle warps
+    // hold block slots
+    const int per_block = std::min(warps, 32);
+    dim3 grid((warps + per_block - 1) / per_block, h, n);
+    k_mask_up<<<grid, per_block * 32, 0, c->stream>>>(m, stride, plane, vw, vh, w, h, words, (float)vw / (float)w,
+                                                  (float)vh / (float)h, thr, bits);
     WOCR_LAUNCHED(c);
 }
 
