@@ -56,15 +56,20 @@ struct wocr_detector {
     Stats last;
     DetGraph graphs[4];
     uint64_t uses = 0;
-    BufP up_buf[2], mask_buf;  // wocr_detect_pages: upload slots and the mask, kept between calls
-    // page uploads of wocr_detect_pages on their own stream, overlapped with detection:
-    // ready (buffers allocated), up[slot] (chunk uploaded), done[slot] (chunk detected)
-    cudaStream_t copy = nullptr;
-    cudaEvent_t ready = nullptr, up[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr};
+    // wocr_detect_pages: two upload slots and two mask slots, kept between calls (stable
+    // addresses, so each slot's detection pass is one cached graph)
+    BufP up_buf[2], mask_buf[2];
+    // page uploads on their own stream and mask read-backs on another, both overlapped with
+    // detection: ready (buffers allocated), up[slot] (chunk uploaded), done[slot] (chunk
+    // detected), back[slot] (chunk mask read back)
+    cudaStream_t copy = nullptr, copy_back = nullptr;
+    cudaEvent_t ready = nullptr, up[2] = {nullptr, nullptr}, done[2] = {nullptr, nullptr},
+                back[2] = {nullptr, nullptr}, fin = nullptr;
     ~wocr_detector() {
         for (auto &g : graphs) g.reset();
         if (copy) cudaStreamDestroy(copy);
-        for (cudaEvent_t e : {ready, up[0], up[1], done[0], done[1]})
+        if (copy_back) cudaStreamDestroy(copy_back);
+        for (cudaEvent_t e : {ready, up[0], up[1], done[0], done[1], back[0], back[1], fin})
             if (e) cudaEventDestroy(e);
     }
 };
@@ -522,13 +527,14 @@ int32_t wocr_detect_pages_device(wocr_detector *det, const uint8_t *d_rgb, int32
 }
 
 // Pages per chunk of wocr_detect_pages: the upload of one chunk overlaps the detection of the
-// previous one.  WOCR_DETECT_CHUNK overrides (0 = one chunk).
+// previous one and the read-back of the mask before, so the PCIe upload of the pages is what is
+// left exposed, plus one chunk's detection.  WOCR_DETECT_CHUNK overrides (0 = one chunk).
 static int detect_chunk(int n) {
     if (const char *e = std::getenv("WOCR_DETECT_CHUNK")) {
         int v = std::atoi(e);
         return v <= 0 ? n : std::min(v, n);
     }
-    return std::max(1, (n + 5) / 6);  // six chunks (two pages each for a batch of 12)
+    return std::max(1, (n + 11) / 12);  // one page per chunk up to 12 pages
 }
 
 int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int32_t w, int32_t h, float threshold,
@@ -542,36 +548,51 @@ int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int
         const int chunk = detect_chunk(n), nchunks = (n + chunk - 1) / chunk;
         if (!det->copy) {
             WOCR_CUDA(cudaStreamCreateWithFlags(&det->copy, cudaStreamNonBlocking));
-            for (cudaEvent_t *e : {&det->ready, &det->up[0], &det->up[1], &det->done[0], &det->done[1]})
+            WOCR_CUDA(cudaStreamCreateWithFlags(&det->copy_back, cudaStreamNonBlocking));
+            for (cudaEvent_t *e : {&det->ready, &det->up[0], &det->up[1], &det->done[0], &det->done[1], &det->back[0],
+                                   &det->back[1], &det->fin})
                 WOCR_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
         }
-        // upload slots and the mask persist between calls (stable addresses for the graph cache)
-        for (int b = 0; b < std::min(nchunks, 2); b++)
+        for (int b = 0; b < std::min(nchunks, 2); b++) {
             if (!det->up_buf[b] || det->up_buf[b]->bytes < (size_t)chunk * page_bytes)
                 det->up_buf[b] = alloc(c, (size_t)chunk * page_bytes);
-        if (!det->mask_buf || det->mask_buf->bytes < (size_t)n * page_words * 4)
-            det->mask_buf = alloc(c, (size_t)n * page_words * 4);
-        BufP src[2] = {det->up_buf[0], det->up_buf[1]}, dst = det->mask_buf;
-        // nothing of the upload stream may still run when the buffers go back to the pool
+            if (!det->mask_buf[b] || det->mask_buf[b]->bytes < (size_t)chunk * page_words * 4)
+                det->mask_buf[b] = alloc(c, (size_t)chunk * page_words * 4);
+        }
+        BufP src[2] = {det->up_buf[0], det->up_buf[1]}, dst[2] = {det->mask_buf[0], det->mask_buf[1]};
+        // nothing of the copy streams may still run when the buffers go back to the pool
         struct Drain {
-            cudaStream_t s;
-            ~Drain() { cudaStreamSynchronize(s); }
-        } drain{det->copy};
+            cudaStream_t s[2];
+            ~Drain() {
+                cudaStreamSynchronize(s[0]);
+                cudaStreamSynchronize(s[1]);
+            }
+        } drain{{det->copy, det->copy_back}};
         WOCR_CUDA(cudaEventRecord(det->ready, c->stream));
         WOCR_CUDA(cudaStreamWaitEvent(det->copy, det->ready, 0));
+        WOCR_CUDA(cudaStreamWaitEvent(det->copy_back, det->ready, 0));
         for (int i = 0; i < nchunks; i++) {
             const int slot = i & 1, k0 = i * chunk, kn = std::min(chunk, n - k0);
-            // the slot's buffer is free once the detection of chunk i - 2 has read it
-            if (i >= 2) WOCR_CUDA(cudaStreamWaitEvent(det->copy, det->done[slot], 0));
+            // the slot's upload buffer is free once the detection of chunk i - 2 has read it,
+            // its mask buffer once that chunk's mask is back on the host
+            if (i >= 2) {
+                WOCR_CUDA(cudaStreamWaitEvent(det->copy, det->done[slot], 0));
+                WOCR_CUDA(cudaStreamWaitEvent(c->stream, det->back[slot], 0));
+            }
             WOCR_CUDA(cudaMemcpyAsync(src[slot]->p, rgb + (size_t)k0 * page_bytes, (size_t)kn * page_bytes,
                                       cudaMemcpyHostToDevice, det->copy));
             WOCR_CUDA(cudaEventRecord(det->up[slot], det->copy));
             WOCR_CUDA(cudaStreamWaitEvent(c->stream, det->up[slot], 0));
-            detect_pages_run(det, (const uint8_t *)src[slot]->p, kn, w, h, threshold,
-                             (uint32_t *)dst->p + (size_t)k0 * page_words);
+            detect_pages_run(det, (const uint8_t *)src[slot]->p, kn, w, h, threshold, (uint32_t *)dst[slot]->p);
             WOCR_CUDA(cudaEventRecord(det->done[slot], c->stream));
+            WOCR_CUDA(cudaStreamWaitEvent(det->copy_back, det->done[slot], 0));
+            WOCR_CUDA(cudaMemcpyAsync(mask_out + (size_t)k0 * page_words, dst[slot]->p, (size_t)kn * page_words * 4,
+                                      cudaMemcpyDeviceToHost, det->copy_back));
+            WOCR_CUDA(cudaEventRecord(det->back[slot], det->copy_back));
         }
-        d2h(c, mask_out, dst->p, (size_t)n * page_words * 4);
+        // the context stream ends after the last read-back, so the bounded wait covers it
+        WOCR_CUDA(cudaEventRecord(det->fin, det->copy_back));
+        WOCR_CUDA(cudaStreamWaitEvent(c->stream, det->fin, 0));
         sync_bounded(c, 0);
     });
 }
