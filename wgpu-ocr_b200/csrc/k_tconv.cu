@@ -70,6 +70,7 @@ struct TcP {
     void *pool_y;               // fused 2 x 2 MaxPool output (null: none), oh / 2 x ow / 2
     int pool_split, pool_vec;
     int64_t pool_n, pool_pix;
+    uint32_t stg_off;           // per-warp 2 KB store staging (transposed stores), 0: none
     int *status;
 };
 
@@ -161,6 +162,49 @@ __device__ __forceinline__ void store16(const TcP &p, int64_t off, const float (
     }
 #pragma unroll
     for (int j = 0; j < 16; j++) store1(p, off + j, v[j]);
+}
+
+// store16 for a whole warp, transposed through the warp's 2 KB staging area so that each store
+// instruction covers 8 pixels x 4 pieces instead of 32 pixels x 1 piece: a lane's 16 channels
+// are 4 pieces of 16 bytes (hi 0-7, hi 8-15, lo 0-7, lo 8-15; or 4 float4), written to the
+// staging area (piece index XORed with bits 1-2 of the lane: conflict-free), then lane l stores
+// piece l % 4 of pixel 8 k + l / 4 for k = 0..3.  `off` and `valid` are each lane's own pixel.
+// Needs p.out_vec; every lane of the warp takes part.
+__device__ __forceinline__ void store16_t(const TcP &p, int64_t off, bool valid, const float (&v)[16], uint4 *stg,
+                                         int lane) {
+    uint4 q[4];
+    if (p.split_out) {
+        uint4 hi[2], lo[2];
+        split16(v, hi, lo);
+        q[0] = hi[0];
+        q[1] = hi[1];
+        q[2] = lo[0];
+        q[3] = lo[1];
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            q[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]), __float_as_uint(v[4 * i + 2]),
+                              __float_as_uint(v[4 * i + 3]));
+    }
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int i = 0; i < 4; i++) stg[lane * 4 + (i ^ sw)] = q[i];
+    __syncwarp();
+    const int pc = lane & 3;
+    // piece pc of a pixel: element offset from the pixel's channel 0 (bf16 or fp32 elements)
+    const int64_t poff = p.split_out ? (int64_t)(pc & 1) * 8 + (pc >> 1) * (p.y_pix / 2) : (int64_t)pc * 4;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int P = 8 * k + (lane >> 2);
+        const int64_t o = __shfl_sync(0xffffffffu, off, P);
+        const bool vv = __shfl_sync(0xffffffffu, (int)valid, P) != 0;
+        const uint4 val = stg[P * 4 + (pc ^ ((P >> 1) & 3))];
+        if (vv) {
+            if (p.split_out) *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(p.y) + o + poff) = val;
+            else *reinterpret_cast<uint4 *>(reinterpret_cast<float *>(p.y) + o + poff) = val;
+        }
+    }
+    __syncwarp();
 }
 
 // TAPS: 9 (3 x 3 kernel), 1 (1 x 1) or 0 (any kernel, taps counted at run time).
@@ -832,6 +876,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
         // ---------------- epilogue group g: tiles lt = g (mod 3), lane quadrant warp % 4 ----------------
         const int q = warp & 3, g = (warp - 4) >> 2;
         const int r = 2 * q + (lane >> 4), j = lane & 15;
+        uint4 *stg = reinterpret_cast<uint4 *>(smem + p.stg_off) + (warp - 4) * 128;
         int lt = 0;
         for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, lt++) {
             if (lt % kRGroups != g) continue;
@@ -870,9 +915,13 @@ __global__ void __launch_bounds__(kRThreads, 1)
                 }
                 act16(v, p.act);
                 const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
+                if (p.stg_off && col + 16 <= p.N) {
+                    store16_t(p, off, valid, v, stg, lane);
+                    if (!p.pool_y) continue;
+                }
                 if (p.pool_y) {
                     // N % 16 == 0 (checked on the host): every chunk is whole
-                    if (valid) store16(p, off, v);
+                    if (!p.stg_off && valid) store16(p, off, v);
                     const bool wv = j < RV && (oy | 1) < p.oh && (ox | 1) < p.ow;
                     pool_rows(p, v, lane,
                               (int64_t)tl.nb * p.pool_n + ((int64_t)(oy >> 1) * (p.ow >> 1) + (ox >> 1)) * p.pool_pix + col,
@@ -1009,15 +1058,18 @@ bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap 
         encode(&xm[1], 4, const_cast<uint16_t *>(q.x + q.x_pix / 2), dims, strides, box, CG);
     }
     const int b_region = (3 * (CG / 8) * 6 * C * 16 + 1023) / 1024 * 1024;
-    const int SA = std::min(8, (kSmemBudget - b_region) / (int)p.a_stage);
-    if (SA < 3) return false;
+    // transposed-store staging: 2 KB per epilogue warp when the stores are 16-byte aligned
+    const int stg = p.out_vec ? kRGroups * 4 * 2048 : 0;
+    const int SA = std::min(8, (kSmemBudget - b_region - stg) / (int)p.a_stage);
+    if (SA < 2) return false;
     p.SA = SA;
     p.SB = 0;
     p.lag = std::min(kLagMax, SA - 2);
     p.b_off = (uint32_t)SA * p.a_stage;
     p.bar_off = p.b_off + (uint32_t)b_region;
     p.bias_off = p.bar_off + 1024;
-    smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + 1024;
+    p.stg_off = stg ? p.bias_off + (uint32_t)((p.bias_n * 4 + 15) / 16 * 16) : 0;
+    smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + stg + 1024;
     return smem <= 227 * 1024;
 }
 
