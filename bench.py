@@ -11,7 +11,8 @@ one process per GPU (torchrun), timed on the device with CUDA events, max over r
   value  - pages/s with the pages already in HBM (B pages = 303 MB > L2 per step)
   e2e    - pages/s through the public API (`wocr_detect_pages`) from pinned host memory, the
            host->device copy of the pages and the device->host copy of the masks inside the
-           timed region
+           timed region.  A tall page goes up as the source rows the grey/resize reads (1600
+           of 3300, strided copies); h2d_bytes_per_step is what the library reports it copied
   roofline - the kernel with the largest share of device time, from a CUDA-event profile of the
            same workload: algorithmic FLOPs (or bytes) per launch / its mean launch time
   cpu_baseline - the CPU oracle (a C restatement of the reference's arithmetic, OpenMP) on a
@@ -319,8 +320,10 @@ def run_b200(args):
     e1.synchronize()
     wall = time.perf_counter() - t0
     ems = max_over_ranks(max(e0.elapsed_time(e1), 1e3 * wall))
-    e2e = {"value": world * B * args.steps / (ems / 1e3), "unit": "pages/s", "h2d_bytes_per_step": int(nbytes),
-           "d2h_bytes_per_step": int(mbytes)}
+    # the bytes that crossed PCIe in one call (tall pages go up compacted to the rows they use)
+    h2d_step, d2h_step = det.last_transfer_bytes()
+    e2e = {"value": world * B * args.steps / (ems / 1e3), "unit": "pages/s", "h2d_bytes_per_step": int(h2d_step),
+           "d2h_bytes_per_step": int(d2h_step), "host_page_bytes_per_step": int(nbytes)}
     wocr.lib().wocr_host_free(hp)
     wocr.lib().wocr_host_free(hm)
 

@@ -219,6 +219,11 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
  * and the launch count. */
 int32_t wocr_last_run_stats(void *handle, int32_t kind, double *flops, int64_t *launches);
 
+/* Bytes copied host -> device and device -> host by the last call on the handle (same kinds).
+ * wocr_detect_pages reports what crossed PCIe for its pages and masks: tall pages go up
+ * compacted to the source rows the grey/resize reads.  No reference counterpart (measurement). */
+int32_t wocr_last_transfer_bytes(void *handle, int32_t kind, int64_t *h2d, int64_t *d2h);
+
 #ifdef __cplusplus
 }
 #endif

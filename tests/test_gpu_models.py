@@ -36,6 +36,25 @@ def test_detect_page(detector, det_model, w, h):
     assert bad == 0, f"{bad} mask pixels differ outside the threshold band ({band} in it)"
 
 
+@pytest.mark.parametrize("w,h", [(1275, 1650), (640, 1999)])
+def test_detect_pages_compacted_upload(detector, det_model, w, h):
+    """Tall pages go up compacted to the rows the grey/resize reads (1650 rows: period 16 output
+    rows / 33 page rows); a height with no short period (1999) goes up whole.  Masks match the
+    oracle and the single-page path, and the reported upload bytes say which path ran."""
+    pages = np.stack([synth.page(40 + k, w, h) for k in range(2)])
+    many = detector.detect_pages(pages, 0.5)
+    h2d, d2h = detector.last_transfer_bytes()
+    assert d2h == many.nbytes
+    if h == 1650:
+        assert h2d == 2 * 800 * 2 * w * 3  # two pages, 1600 rows each
+    else:
+        assert h2d == pages.nbytes
+    for k in range(2):
+        rbits, prob, _ = ref.detect_page(det_model, pages[k], 0.5)
+        bad, band = mask_parity(many[k], rbits, prob, 0.5, w)
+        assert bad == 0, f"page {k}: {bad} mask pixels differ outside the threshold band ({band} in it)"
+
+
 def test_detect_pages_batched_equals_single(detector):
     pages = np.stack([synth.page(20 + k, 640, 480) for k in range(3)])
     many = detector.detect_pages(pages, 0.5)

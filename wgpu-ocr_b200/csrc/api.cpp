@@ -26,6 +26,7 @@ static void ctx_release(wocr_ctx *ctx);
 struct Stats {
     double flops = 0;
     int64_t launches = 0;
+    int64_t h2d = 0, d2h = 0;  // bytes copied between host and device
 };
 
 // One detection pass (detect_pages_dev) captured as a CUDA graph for a given page count, size,
@@ -34,6 +35,7 @@ struct Stats {
 struct DetGraph {
     int n = 0, w = 0, h = 0;
     float thr = 0;
+    const int2 *rows = nullptr;  // compacted pages: the row table (null: whole pages)
     const uint8_t *rgb = nullptr;
     uint32_t *mask = nullptr;
     cudaGraph_t graph = nullptr;
@@ -50,6 +52,24 @@ struct DetGraph {
     }
 };
 
+// The source rows the detector's grey/resize reads (src/gpu.rs:533-561): output row oy of the
+// 800 x 600 model input interpolates rows y1 = floor(iy) and y2 = min(y1 + 1, ph - 1) of the page,
+// iy = clamp(sy (oy + 0.5) - 0.5, 0, ph - 1), sy = ph / 800.  For a tall page (h > 1600) that is
+// under half of it, so wocr_detect_pages uploads only those rows: page row pairs (y1, y1 + 1)
+// whose positions repeat with a period of k output rows and P page rows go up as k strided
+// copies per page (cudaMemcpy2DAsync), the rest (the last rows, where y2 is clamped) one row at a
+// time, into rows 2 oy and 2 oy + 1 of a compacted page (k_grey_rows).  Pages with no period up
+// to 64 output rows, or not taller than 1600, upload whole.
+struct RowPlan {
+    int w = 0, h = 0;
+    bool ok = false;
+    int k = 0, P = 0, regular = 0;     // period; output rows [0, regular) are (y1, y1 + 1) pairs
+    std::vector<int> y1, y2;
+    std::vector<int> first, count;     // per phase j < k: first page row, number of periods
+    BufP table;                        // rows[oy] for k_grey_rows
+    size_t bytes = 0;                  // compacted page bytes
+};
+
 struct wocr_detector {
     wocr_ctx *ctx;
     std::unique_ptr<Executor> graph;
@@ -59,6 +79,7 @@ struct wocr_detector {
     // wocr_detect_pages: two upload slots and two mask slots, kept between calls (stable
     // addresses, so each slot's detection pass is one cached graph)
     BufP up_buf[2], mask_buf[2];
+    RowPlan plan;                      // of the last page size seen
     // page uploads on their own stream and mask read-backs on another, both overlapped with
     // detection: ready (buffers allocated), up[slot] (chunk uploaded), done[slot] (chunk
     // detected), back[slot] (chunk mask read back)
@@ -199,7 +220,10 @@ struct RunScope {
     Stats *out;
     double f0;
     int64_t l0;
-    RunScope(Ctx *ctx, Stats *s) : c(ctx), out(s), f0(ctx->flops), l0(ctx->launches) { WOCR_CUDA(cudaSetDevice(ctx->device)); }
+    RunScope(Ctx *ctx, Stats *s) : c(ctx), out(s), f0(ctx->flops), l0(ctx->launches) {
+        WOCR_CUDA(cudaSetDevice(ctx->device));
+        out->h2d = out->d2h = 0;
+    }
     ~RunScope() {
         out->flops = c->flops - f0;
         out->launches = c->launches - l0;
@@ -454,13 +478,14 @@ void wocr_detector_destroy(wocr_detector *det) {
 }
 
 static void detect_pages_dev(wocr_detector *det, const uint8_t *d_rgb, int n, int w, int h, float thr,
-                             uint32_t *d_mask) {
+                             uint32_t *d_mask, const int2 *rows = nullptr) {
     Ctx *c = &det->ctx->c;
     if (n <= 0 || w <= 0 || h <= 0) fail(WOCR_ERR_INVALID, "empty page");
     const int mh = 800, mw = 600;  // the model size (src/gpu.rs:1394)
     int ph = std::max(h, mh), pw = std::max(w, mw);
     DT in = new_nhwc(c, n, 1, mh, mw);
-    k::grey_resize(c, d_rgb, (int64_t)w * h * 3, n, w, h, mh, mw, in.p);
+    if (rows) k::grey_resize_rows(c, d_rgb, rows, n, w, mh, mw, in.p);
+    else k::grey_resize(c, d_rgb, (int64_t)w * h * 3, n, w, h, mh, mw, in.p);
     DT m = det->graph->run(in);
     if (m.rank() != 4 || m.shape[0] != n || m.shape[1] != 1)
         fail(WOCR_ERR_SHAPE, "detection output " + shape_str(m.shape));
@@ -473,15 +498,17 @@ static void detect_pages_dev(wocr_detector *det, const uint8_t *d_rgb, int n, in
 // detect_pages_dev through the detector's graph cache (direct when profiling, or with
 // WOCR_NO_GRAPH set).
 static void detect_pages_run(wocr_detector *det, const uint8_t *d_rgb, int n, int w, int h, float thr,
-                             uint32_t *d_mask) {
+                             uint32_t *d_mask, const int2 *rows = nullptr) {
     Ctx *c = &det->ctx->c;
     if (c->prof || std::getenv("WOCR_NO_GRAPH")) {
-        detect_pages_dev(det, d_rgb, n, w, h, thr, d_mask);
+        detect_pages_dev(det, d_rgb, n, w, h, thr, d_mask, rows);
         return;
     }
     DetGraph *g = nullptr;
     for (auto &e : det->graphs)
-        if (e.exec && e.n == n && e.w == w && e.h == h && e.thr == thr && e.rgb == d_rgb && e.mask == d_mask) g = &e;
+        if (e.exec && e.n == n && e.w == w && e.h == h && e.thr == thr && e.rgb == d_rgb && e.mask == d_mask &&
+            e.rows == rows)
+            g = &e;
     if (!g) {
         g = &det->graphs[0];
         for (auto &e : det->graphs)
@@ -491,7 +518,7 @@ static void detect_pages_run(wocr_detector *det, const uint8_t *d_rgb, int n, in
         const int64_t l0 = c->launches;
         WOCR_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
         try {
-            detect_pages_dev(det, d_rgb, n, w, h, thr, d_mask);
+            detect_pages_dev(det, d_rgb, n, w, h, thr, d_mask, rows);
         } catch (...) {
             cudaGraph_t dead = nullptr;
             cudaStreamEndCapture(c->stream, &dead);
@@ -506,6 +533,7 @@ static void detect_pages_run(wocr_detector *det, const uint8_t *d_rgb, int n, in
         g->thr = thr;
         g->rgb = d_rgb;
         g->mask = d_mask;
+        g->rows = rows;
         g->flops = c->flops - f0;
         g->launches = c->launches - l0;
         c->flops = f0;
@@ -526,15 +554,73 @@ int32_t wocr_detect_pages_device(wocr_detector *det, const uint8_t *d_rgb, int32
     });
 }
 
+// The row plan of a page size (RowPlan), built on its first use.
+static const RowPlan &row_plan(wocr_detector *det, int w, int h) {
+    RowPlan &pl = det->plan;
+    if (pl.w == w && pl.h == h) return pl;
+    pl = RowPlan();
+    pl.w = w;
+    pl.h = h;
+    const int mh = 800;  // the model height (src/gpu.rs:1394)
+    const int ph = std::max(h, mh);
+    const float sy = (float)ph / (float)mh;
+    pl.y1.resize(mh);
+    pl.y2.resize(mh);
+    std::vector<int2> table(mh);
+    for (int oy = 0; oy < mh; oy++) {
+        volatile float t = sy * ((float)oy + 0.5f);  // rounded before the subtraction, as K13 states it
+        const float iy = std::fmin(std::fmax(t - 0.5f, 0.f), (float)ph - 1.f);
+        const int y1 = (int)iy, y2 = std::min(y1 + 1, ph - 1);
+        const float wy = iy - (float)y1;
+        pl.y1[oy] = y1;
+        pl.y2[oy] = y2;
+        int wb;
+        std::memcpy(&wb, &wy, 4);
+        table[oy] = make_int2(wb, (y1 >= h ? 1 : 0) | (y2 >= h ? 2 : 0));
+    }
+    pl.bytes = (size_t)2 * mh * w * 3;
+    if (h <= 2 * mh) return pl;  // the compacted page would not be smaller
+    int R = 0;  // the regular prefix: (y1, y1 + 1) pairs inside the page
+    while (R < mh && pl.y1[R] + 1 < h && pl.y2[R] == pl.y1[R] + 1) R++;
+    for (int k = 1; k <= 64 && k < R; k++) {
+        const int P = pl.y1[k] - pl.y1[0];
+        bool good = P >= 2;
+        for (int oy = 0; good && oy + k < R; oy++) good = pl.y1[oy + k] - pl.y1[oy] == P;
+        if (good) {
+            pl.k = k;
+            pl.P = P;
+            break;
+        }
+    }
+    if (!pl.k) return pl;
+    pl.regular = R;
+    pl.first.assign(pl.k, 0);
+    pl.count.assign(pl.k, 0);
+    for (int j = 0; j < pl.k && j < R; j++) {
+        pl.first[j] = pl.y1[j];
+        pl.count[j] = (R - 1 - j) / pl.k + 1;
+    }
+    Ctx *c = &det->ctx->c;
+    pl.table = alloc(c, mh * sizeof(int2));
+    WOCR_CUDA(cudaMemcpyAsync(pl.table->p, table.data(), mh * sizeof(int2), cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    pl.ok = true;
+    return pl;
+}
+
 // Pages per chunk of wocr_detect_pages: the upload of one chunk overlaps the detection of the
-// previous one and the read-back of the mask before, so the PCIe upload of the pages is what is
-// left exposed, plus one chunk's detection.  WOCR_DETECT_CHUNK overrides (0 = one chunk).
-static int detect_chunk(int n) {
+// previous one and the read-back of the mask before, so what is left exposed is the PCIe upload
+// or the detection, whichever is longer, plus one chunk of the other.  Whole pages (the upload
+// the longer part): one page per chunk up to 12.  Compacted pages (the two about even): six
+// chunks, two pages each for 12, since a pass over one page fills the SMs poorly in the deep
+// layers (measured on 12-page steps: 2850 pages/s against 2420).  WOCR_DETECT_CHUNK overrides
+// (0 = one chunk).
+static int detect_chunk(int n, bool compact) {
     if (const char *e = std::getenv("WOCR_DETECT_CHUNK")) {
         int v = std::atoi(e);
         return v <= 0 ? n : std::min(v, n);
     }
-    return std::max(1, (n + 11) / 12);  // one page per chunk up to 12 pages
+    return compact ? std::max(1, (n + 5) / 6) : std::max(1, (n + 11) / 12);
 }
 
 int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int32_t w, int32_t h, float threshold,
@@ -545,7 +631,11 @@ int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int
         Ctx *c = &det->ctx->c;
         RunScope rs(c, &det->last);
         const size_t page_bytes = (size_t)w * h * 3, page_words = (size_t)h * ((w + 31) / 32);
-        const int chunk = detect_chunk(n), nchunks = (n + chunk - 1) / chunk;
+        // tall pages go up compacted: only the rows the grey/resize reads (RowPlan)
+        const RowPlan &pl = row_plan(det, w, h);
+        const bool compact = pl.ok && !std::getenv("WOCR_WHOLE_PAGES");
+        const int chunk = detect_chunk(n, compact), nchunks = (n + chunk - 1) / chunk;
+        const size_t up_page = compact ? pl.bytes : page_bytes, rb = (size_t)w * 3;
         if (!det->copy) {
             WOCR_CUDA(cudaStreamCreateWithFlags(&det->copy, cudaStreamNonBlocking));
             WOCR_CUDA(cudaStreamCreateWithFlags(&det->copy_back, cudaStreamNonBlocking));
@@ -554,8 +644,8 @@ int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int
                 WOCR_CUDA(cudaEventCreateWithFlags(e, cudaEventDisableTiming));
         }
         for (int b = 0; b < std::min(nchunks, 2); b++) {
-            if (!det->up_buf[b] || det->up_buf[b]->bytes < (size_t)chunk * page_bytes)
-                det->up_buf[b] = alloc(c, (size_t)chunk * page_bytes);
+            if (!det->up_buf[b] || det->up_buf[b]->bytes < (size_t)chunk * up_page)
+                det->up_buf[b] = alloc(c, (size_t)chunk * up_page);
             if (!det->mask_buf[b] || det->mask_buf[b]->bytes < (size_t)chunk * page_words * 4)
                 det->mask_buf[b] = alloc(c, (size_t)chunk * page_words * 4);
         }
@@ -579,15 +669,41 @@ int32_t wocr_detect_pages(wocr_detector *det, const uint8_t *rgb, int32_t n, int
                 WOCR_CUDA(cudaStreamWaitEvent(det->copy, det->done[slot], 0));
                 WOCR_CUDA(cudaStreamWaitEvent(c->stream, det->back[slot], 0));
             }
-            WOCR_CUDA(cudaMemcpyAsync(src[slot]->p, rgb + (size_t)k0 * page_bytes, (size_t)kn * page_bytes,
-                                      cudaMemcpyHostToDevice, det->copy));
+            if (compact) {
+                for (int pg = 0; pg < kn; pg++) {
+                    const uint8_t *page = rgb + (size_t)(k0 + pg) * page_bytes;
+                    uint8_t *cp = (uint8_t *)src[slot]->p + (size_t)pg * pl.bytes;
+                    // the row pairs of phase j: output rows j, j + k, ... -> compacted rows 2 oy, 2 oy + 1
+                    for (int j = 0; j < pl.k; j++)
+                        if (pl.count[j]) {
+                            WOCR_CUDA(cudaMemcpy2DAsync(cp + 2 * (size_t)j * rb, 2 * (size_t)pl.k * rb,
+                                                        page + (size_t)pl.first[j] * rb, (size_t)pl.P * rb, 2 * rb,
+                                                        pl.count[j], cudaMemcpyHostToDevice, det->copy));
+                            det->last.h2d += (int64_t)(2 * rb * pl.count[j]);
+                        }
+                    for (int oy = pl.regular; oy < 800; oy++)
+                        for (int r = 0; r < 2; r++) {
+                            const int yy = r ? pl.y2[oy] : pl.y1[oy];
+                            if (yy >= h) continue;  // padding: not read
+                            WOCR_CUDA(cudaMemcpyAsync(cp + (2 * (size_t)oy + r) * rb, page + (size_t)yy * rb, rb,
+                                                      cudaMemcpyHostToDevice, det->copy));
+                            det->last.h2d += (int64_t)rb;
+                        }
+                }
+            } else {
+                WOCR_CUDA(cudaMemcpyAsync(src[slot]->p, rgb + (size_t)k0 * page_bytes, (size_t)kn * page_bytes,
+                                          cudaMemcpyHostToDevice, det->copy));
+                det->last.h2d += (int64_t)(kn * page_bytes);
+            }
             WOCR_CUDA(cudaEventRecord(det->up[slot], det->copy));
             WOCR_CUDA(cudaStreamWaitEvent(c->stream, det->up[slot], 0));
-            detect_pages_run(det, (const uint8_t *)src[slot]->p, kn, w, h, threshold, (uint32_t *)dst[slot]->p);
+            detect_pages_run(det, (const uint8_t *)src[slot]->p, kn, w, h, threshold, (uint32_t *)dst[slot]->p,
+                             compact ? (const int2 *)pl.table->p : nullptr);
             WOCR_CUDA(cudaEventRecord(det->done[slot], c->stream));
             WOCR_CUDA(cudaStreamWaitEvent(det->copy_back, det->done[slot], 0));
             WOCR_CUDA(cudaMemcpyAsync(mask_out + (size_t)k0 * page_words, dst[slot]->p, (size_t)kn * page_words * 4,
                                       cudaMemcpyDeviceToHost, det->copy_back));
+            det->last.d2h += (int64_t)(kn * page_words * 4);
             WOCR_CUDA(cudaEventRecord(det->back[slot], det->copy_back));
         }
         // the context stream ends after the last read-back, so the bounded wait covers it
@@ -1311,6 +1427,19 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
             d2h(c, prob, r->out->p, (size_t)m * 4);
         }
         sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_last_transfer_bytes(void *handle, int32_t kind, int64_t *h2d, int64_t *d2h) {
+    return guard([&] {
+        if (!handle) fail(WOCR_ERR_INVALID, "null handle");
+        Stats *s = nullptr;
+        if (kind == 1) s = &((wocr_detector *)handle)->last;
+        else if (kind == 2) s = &((wocr_recognizer *)handle)->last;
+        else if (kind == 3) s = &((wocr_ndgraph *)handle)->last;
+        else fail(WOCR_ERR_INVALID, "kind must be 1 (detector), 2 (recogniser) or 3 (N-D graph)");
+        if (h2d) *h2d = s->h2d;
+        if (d2h) *d2h = s->d2h;
     });
 }
 

@@ -73,6 +73,37 @@ __global__ void k_grey_resize(const uint8_t *__restrict__ rgb, int64_t page_byte
     }
 }
 
+// k_grey_resize on a compacted page: only the two source rows each output row interpolates,
+// rows 2 oy (top) and 2 oy + 1 (bottom) of `cmp`, uploaded by the host.  rows[oy] = {wy (float
+// bits), flags}: the vertical weight, and bit 0 / bit 1 when the top / bottom row lies below the
+// page (the padding value).  The column arithmetic is k_grey_resize's.
+__global__ void k_grey_rows(const uint8_t *__restrict__ cmp, int64_t page_bytes, const int2 *__restrict__ rows, int w,
+                            int pw, int oh, int ow, float sx, float *__restrict__ y) {
+    int page = blockIdx.y;
+    const uint8_t *src = cmp + page * page_bytes;
+    float *dst = y + (int64_t)page * oh * ow;
+    const int64_t rb = (int64_t)w * 3;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)oh * ow;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int ox = (int)(i % ow), oy = (int)(i / ow);
+        const int2 rt = rows[oy];
+        float wy = __int_as_float(rt.x);
+        float ix = fminf(fmaxf(sx * ((float)ox + 0.5f) - 0.5f, 0.f), (float)pw - 1.f);
+        int x1 = (int)ix;
+        int x2 = min(x1 + 1, pw - 1);
+        float wx = ix - (float)x1;
+        auto grey = [&](int x, int r) -> float {
+            if (x >= w || (rt.y >> r) & 1) return -0.5f;
+            const uint8_t *p = src + (2 * oy + r) * rb + (int64_t)x * 3;
+            return -0.5f + (float)p[0] * (0.299f / 255.0f) + (float)p[1] * (0.587f / 255.0f) +
+                   (float)p[2] * (0.114f / 255.0f);
+        };
+        float top = mixf(grey(x1, 0), grey(x2, 0), wx);
+        float bot = mixf(grey(x1, 1), grey(x2, 1), wx);
+        dst[i] = mixf(top, bot, wy);
+    }
+}
+
 // One warp builds 32 consecutive words of a page row: lane b thresholds pixel 32*wx + b, a
 // ballot forms the word, lane j keeps word j and the warp stores its 32 words at once.
 __global__ void k_mask_up(const float *__restrict__ m, int stride, int64_t plane, int vw, int vh, int w, int h,
@@ -599,6 +630,15 @@ void grey_resize(Ctx *c, const uint8_t *rgb, int64_t page_bytes, int n, int w, i
     float sx = (float)pw / (float)ow, sy = (float)ph / (float)oh;
     dim3 grid(grid_for(c, (int64_t)oh * ow), n);
     k_grey_resize<<<grid, kThreads, 0, c->stream>>>(rgb, page_bytes, w, h, ph, pw, oh, ow, sx, sy, y);
+    WOCR_LAUNCHED(c);
+}
+
+void grey_resize_rows(Ctx *c, const uint8_t *cmp, const int2 *rows, int n, int w, int oh, int ow, float *y) {
+    const int64_t page_bytes = 2LL * oh * w * 3;
+    Prof pf(c, "grey_resize", 0, (double)n * ((double)page_bytes + (double)oh * ow * 4));
+    const int pw = w > ow ? w : ow;
+    dim3 grid(grid_for(c, (int64_t)oh * ow), n);
+    k_grey_rows<<<grid, kThreads, 0, c->stream>>>(cmp, page_bytes, rows, w, pw, oh, ow, (float)pw / (float)ow, y);
     WOCR_LAUNCHED(c);
 }
 

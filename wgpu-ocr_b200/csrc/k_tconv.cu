@@ -555,6 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // MB = 2: half h takes MMA block h (image rows 16 h .. 16 h + 15 of the tile), all columns
         const int blk = MB == 2 ? half : 0;
         const int r = row / TP + TR * blk, pc = row % TP;
+        uint4 *stg = reinterpret_cast<uint4 *>(smem + p.stg_off) + (warp - kEpi0) * 128;
         int lt = 0;
         for (int t = blockIdx.x; t < p.ntiles; t += gridDim.x, lt++) {
             if (TSPLIT && (lt & 1) != half) continue;
@@ -583,7 +584,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[col + jj];
                     act16(v, p.act);
-                    if (valid) store16(p, (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col, v);
+                    const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
+                    if (p.stg_off) store16_t(p, off, valid, v, stg, lane);
+                    else if (valid) store16(p, off, v);
 #pragma unroll
                     for (int jj = 0; jj < 16; jj++) {
                         float a = fmaxf(v[jj], __shfl_down_sync(0xffffffffu, v[jj], 1));
@@ -593,6 +596,25 @@ __global__ void __launch_bounds__(kThreads, 1)
                         store_pool(p, (int64_t)tl.nb * p.pool_n + ((int64_t)(oy >> 1) * (p.ow >> 1) + (ox >> 1)) * p.pool_pix +
                                           col,
                                    v);
+                    continue;
+                }
+                if (p.stg_off && col + 16 <= p.N && (!p.scatter || p.scat_cout % 16 == 0)) {
+                    // whole 16-channel chunk: every lane takes part in the transposed store
+                    int64_t off;
+                    int b0 = col;
+                    if (p.scatter) {
+                        // a 16-column chunk lies in one tap: 16 channels of pixel (s oy + ky, s ox + kx)
+                        const int sc = p.scatter, tap = col / p.scat_cout;
+                        b0 = col - tap * p.scat_cout;
+                        off = (int64_t)tl.nb * p.y_n +
+                              ((int64_t)(oy * sc + tap / sc) * p.ow_out + ox * sc + tap % sc) * p.y_pix + b0;
+                    } else {
+                        off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[b0 + jj];
+                    act16(v, p.act);
+                    store16_t(p, off, valid, v, stg, lane);
                     continue;
                 }
                 if (!valid || col >= p.N) continue;
@@ -1224,7 +1246,10 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.plane = (uint32_t)p.halo_px * 16;
     p.a_stage = (2 * (w.cg / 8) * p.plane + 1023) / 1024 * 1024;
 
-    // shared memory: A stages, then B (resident or a ring of tap chunks), then the barriers
+    // shared memory: A stages, then B (resident or a ring of tap chunks), then the barriers, the
+    // bias and the transposed-store staging (2 KB per epilogue warp, when stores are 16-byte aligned)
+    const int stg = p.out_vec ? kEpiWarps * 2048 : 0;
+    const int budget = kSmemBudget - stg;
     const int b_half = w.bn * w.cg * 2;
     const int b_all = p.ntn * w.taps * p.nchunk * 2 * b_half;
     int SA, SB;
@@ -1232,14 +1257,14 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
         p.b_res = 1;
         SB = 1;
         const int b_region = (b_all + 1023) / 1024 * 1024;
-        SA = std::min(8, (kSmemBudget - b_region) / (int)p.a_stage);
+        SA = std::min(8, (budget - b_region) / (int)p.a_stage);
         p.b_off = (uint32_t)SA * p.a_stage;
         p.bar_off = p.b_off + (uint32_t)b_region;
     } else {
         p.b_res = 0;
         p.b_stage = (uint32_t)(w.taps * 2 * b_half);
-        SB = std::min(8, std::max(2, (kSmemBudget / 2) / (int)p.b_stage));
-        SA = std::min(8, (kSmemBudget - SB * (int)p.b_stage) / (int)p.a_stage);
+        SB = std::min(8, std::max(2, (budget / 2) / (int)p.b_stage));
+        SA = std::min(8, (budget - SB * (int)p.b_stage) / (int)p.a_stage);
         p.b_off = (uint32_t)SA * p.a_stage;
         p.bar_off = p.b_off + (uint32_t)((SB * p.b_stage + 1023) / 1024 * 1024);
     }
@@ -1250,7 +1275,8 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     p.SB = SB;
     p.lag = std::min(kLagMax, SA - 2);
     p.bias_off = p.bar_off + 1024;
-    const int smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + 1024;  // + alignment slack
+    p.stg_off = stg ? p.bias_off + (uint32_t)((p.bias_n * 4 + 15) / 16 * 16) : 0;
+    const int smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + stg + 1024;  // + alignment slack
     if (smem > 227 * 1024) fail(WOCR_ERR_UNSUPPORTED, "tap convolution bias too large");
 
     Prof pf(c, q.scatter ? "tconv_convt" : "tconv", flops, bytes);

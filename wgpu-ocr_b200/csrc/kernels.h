@@ -133,6 +133,9 @@ void bmm(Ctx *c, const float *a, const float *bm, float *y, int64_t batch, int m
 // ocrs detector input (K13, src/gpu.rs:530-561): packed RGB pages -> grey, pad, half-pixel
 // bilinear to oh x ow.  n pages at rgb + i * page_bytes; output [n][oh][ow].
 void grey_resize(Ctx *c, const uint8_t *rgb, int64_t page_bytes, int n, int w, int h, int oh, int ow, float *y);
+// The same on compacted pages: per page 2 oh rows of w * 3 bytes (the top and bottom source rows
+// of each output row), rows[oy] = {vertical weight (float bits), bit 0/1: top/bottom is padding}.
+void grey_resize_rows(Ctx *c, const uint8_t *cmp, const int2 *rows, int n, int w, int oh, int ow, float *y);
 
 // ocrs detector output (K14, src/gpu.rs:563-593): valid vh x vw part of the map (row stride
 // `stride`, plane `plane` per page) -> page size, `> thr`, 32 pixels a word.

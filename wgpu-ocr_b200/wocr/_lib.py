@@ -96,6 +96,7 @@ _SIGS = [
     ("wocr_ppdet_page", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_void_p, c_i64, P(c_i32), P(c_i32),
                                 P(c_f32)]),
     ("wocr_last_run_stats", c_i32, [c_void_p, c_i32, P(c_f64), P(c_i64)]),
+    ("wocr_last_transfer_bytes", c_i32, [c_void_p, c_i32, P(c_i64), P(c_i64)]),
 ]
 
 EXPORTS = [s[0] for s in _SIGS]

@@ -90,6 +90,12 @@ class _Handle:
         L.check(L.lib().wocr_last_run_stats(self.h, self.kind, ctypes.byref(f), ctypes.byref(n)))
         return f.value, n.value
 
+    def last_transfer_bytes(self):
+        """(bytes host -> device, bytes device -> host) copied by the last call of this handle."""
+        a, b = ctypes.c_int64(), ctypes.c_int64()
+        L.check(L.lib().wocr_last_transfer_bytes(self.h, self.kind, ctypes.byref(a), ctypes.byref(b)))
+        return a.value, b.value
+
 
 class Detector(_Handle):
     """`Detector` (src/gpu.rs:1380-1431): the ocrs detection model lowered by Graph::build."""
