@@ -219,6 +219,19 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
  * and the launch count. */
 int32_t wocr_last_run_stats(void *handle, int32_t kind, double *flops, int64_t *launches);
 
+/* PP-OCR recognition lines cut from a device-resident RGB page (`d_rgb`, w x h u8) and batched
+ * on the device: `ppocr::line_input` (src/ppocr.rs:39-62) for each box rects[4 k .. 4 k + 3] =
+ * [left, top, right, bottom] (clamped to the page; resized to height 48 keeping the aspect ratio
+ * with the `image` crate's Triangle filter; (v / 255 - 0.5) / 0.5, planar), batched as
+ * `pp_batches` (src/bin/ocr-bench.rs:312-345) does: sorted by width, `per_batch` lines a batch,
+ * each [n, 3, 48, width], width = the widest line rounded up to 8, zero-padded.  The batches are
+ * written one after another to `d_out` (device, `cap` floats).  order[i]: the box of batch slot i;
+ * batch_n / batch_w: lines and width of each batch; *n_batches, *total (floats) always set; with
+ * d_out NULL only the layout is returned.  Output arrays may be NULL.  Waits for the device. */
+int32_t wocr_pp_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h, const float *rects, int32_t n,
+                      int32_t per_batch, float *d_out, int64_t cap, int32_t *order, int32_t *batch_n,
+                      int32_t *batch_w, int32_t *n_batches, int64_t *total);
+
 /* Bytes copied host -> device and device -> host by the last call on the handle (same kinds).
  * wocr_detect_pages reports what crossed PCIe for its pages and masks: tall pages go up
  * compacted to the source rows the grey/resize reads.  No reference counterpart (measurement). */

@@ -474,3 +474,89 @@ void oracle_unary(const float *x, long n, int op, float alpha, float beta, float
         y[i] = r;
     }
 }
+
+/*
+ * PP-OCR recognition line (src/ppocr.rs:39-62).  The box [left, top, right, bottom] of an RGB
+ * page is clamped to the page (v.max(0).min(size) as u32) and cut out as the reference cuts it:
+ * crop row y is the cw * 3 bytes at ((top + y) * w + left) * 3, or zeros when that range leaves
+ * the page buffer.  It is resized to height 48 keeping its aspect ratio,
+ * out_w = clamp(ceil(48 cw / ch), 8, 3200), with the Triangle filter of the `image` crate's
+ * imageops::resize (image =0.25.10, an un-vendored dependency; restated from its published
+ * separable-resampling algorithm):
+ *   - per axis: ratio = in / out, s = max(ratio, 1), support = s, c = (o + 0.5) ratio;
+ *   - taps i in [clamp(floor(c - s), 0, in - 1), clamp(ceil(c + s), left + 1, in));
+ *   - weight tri((i - (c - 0.5)) / s) / (sum of the weights), tri(x) = max(0, 1 - |x|);
+ *   - a vertical pass into an f32 image, then a horizontal pass clamped to [0, 255] and rounded
+ *     to u8 (half away from zero).
+ * Then (v / 255 - 0.5) / 0.5, planar [3][48][out_w].  Returns out_w; with out == NULL it only
+ * returns it.
+ */
+static float tri_kernel(float x) {
+    x = fabsf(x);
+    return x < 1.f ? 1.f - x : 0.f;
+}
+
+/* Taps of output coordinate o of one axis: first input index in *left, count returned, the
+ * normalised weights in ws (at most `cap`). */
+static int resample_taps(int in, int out, int o, int *left, float *ws, int cap) {
+    float ratio = (float)in / (float)out;
+    float sratio = ratio < 1.f ? 1.f : ratio;
+    float support = 1.0f * sratio;
+    float center = ((float)o + 0.5f) * ratio;
+    long l = (long)floorf(center - support);
+    l = l < 0 ? 0 : (l > in - 1 ? in - 1 : l);
+    long r = (long)ceilf(center + support);
+    r = r < l + 1 ? l + 1 : (r > in ? in : r);
+    center = center - 0.5f;
+    float sum = 0.f;
+    int n = 0;
+    for (long i = l; i < r && n < cap; i++, n++) {
+        ws[n] = tri_kernel(((float)i - center) / sratio);
+        sum = sum + ws[n];
+    }
+    for (int k = 0; k < n; k++) ws[k] = ws[k] / sum;
+    *left = (int)l;
+    return n;
+}
+
+static unsigned clamp_box(float v, int hi) {
+    if (!(v > 0.f)) v = 0.f; /* Rust f32::max ignores NaN */
+    if (v > (float)hi) v = (float)hi;
+    return (unsigned)v;
+}
+
+int oracle_pp_line(const uint8_t *rgb, int w, int h, const float *rect, float *out) {
+    unsigned l = clamp_box(rect[0], w), t = clamp_box(rect[1], h), r = clamp_box(rect[2], w), b = clamp_box(rect[3], h);
+    int cw = r > l ? (int)(r - l) : 1, ch = b > t ? (int)(b - t) : 1;
+    float fw = ceilf(48.f * (float)cw / (float)ch);
+    int ow = fw < 8.f ? 8 : (fw > 3200.f ? 3200 : (int)fw);
+    if (!out) return ow;
+    const long total = (long)w * h * 3;
+    int cap = 2 * (cw > ch ? cw : ch) + 8;
+    float *wx = (float *)malloc(sizeof(float) * cap), *wy = (float *)malloc(sizeof(float) * cap);
+    for (int y = 0; y < 48; y++) {
+        int ly, ny = resample_taps(ch, 48, y, &ly, wy, cap);
+        for (int x = 0; x < ow; x++) {
+            int lx, nx = resample_taps(cw, ow, x, &lx, wx, cap);
+            for (int c = 0; c < 3; c++) {
+                float acc = 0.f;
+                for (int j = 0; j < nx; j++) {
+                    float v = 0.f;
+                    for (int i = 0; i < ny; i++) {
+                        long row = ((long)(t + ly + i) * w + l) * 3;
+                        float px = 0.f;
+                        if (row + (long)cw * 3 <= total) px = (float)rgb[row + (long)(lx + j) * 3 + c];
+                        v = v + px * wy[i];
+                    }
+                    acc = acc + v * wx[j];
+                }
+                acc = acc < 0.f ? 0.f : (acc > 255.f ? 255.f : acc);
+                float q = roundf(acc);
+                out[((long)c * 48 + y) * ow + x] = (q / 255.f - 0.5f) / 0.5f;
+            }
+        }
+    }
+    free(wx);
+    free(wy);
+    return ow;
+}

@@ -67,12 +67,13 @@ def lib():
             "oracle_threads": [],
             "oracle_erf": [_F],
             "oracle_act": [_F, _I],
+            "oracle_pp_line": [_u8, _I, _I, _f, _f],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = ctypes.c_float if name in ("oracle_erf", "oracle_act") else (
-                ctypes.c_int if name == "oracle_threads" else None)
+                ctypes.c_int if name in ("oracle_threads", "oracle_pp_line") else None)
         _lib = L
     return _lib
 
@@ -132,6 +133,37 @@ def pool(x, kh, kw, sh, sw, pads=(0, 0, 0, 0), avg=False):
     y = np.empty((n, c, oh, ow), np.float32)
     lib().oracle_pool(_p(x), n * c, h, w, oh, ow, kh, kw, sh, sw, pt, pl, int(avg), _p(y))
     return y
+
+
+def pp_line(rgb: np.ndarray, rect) -> np.ndarray:
+    """One PP-OCR recognition line, [3, 48, out_w] in [-1, 1] (src/ppocr.rs:39-62; the Triangle
+    resize of image =0.25.10 restated in oracle.c)."""
+    rgb = np.ascontiguousarray(rgb, np.uint8)
+    h, w = rgb.shape[:2]
+    r = np.ascontiguousarray(rect, np.float32)
+    ow = lib().oracle_pp_line(_p(rgb, _u8), w, h, _p(r), None)
+    out = np.empty((3, 48, ow), np.float32)
+    lib().oracle_pp_line(_p(rgb, _u8), w, h, _p(r), _p(out))
+    return out
+
+
+def pp_batches(rgb: np.ndarray, rects, per: int = 16):
+    """PP-OCR line batches as src/bin/ocr-bench.rs:312-345 forms them (PPGROUP = 0): lines sorted
+    by width (stable), cut into batches of `per`, each [n, 3, 48, width] with width the widest
+    line rounded up to a multiple of 8, zero-padded on the right.  Returns (batches as
+    (data, n, width), order: the line index of each batch slot)."""
+    lines = [pp_line(rgb, r) for r in rects]
+    idx = sorted(range(len(lines)), key=lambda i: lines[i].shape[2])
+    batches, order = [], []
+    for k in range(0, len(idx), per):
+        part = idx[k:k + per]
+        width = -(-max(lines[i].shape[2] for i in part) // 8) * 8
+        data = np.zeros((len(part), 3, 48, width), np.float32)
+        for j, i in enumerate(part):
+            data[j, :, :, :lines[i].shape[2]] = lines[i]
+        batches.append((data, len(part), width))
+        order.extend(part)
+    return batches, order
 
 
 def grey_resize(rgb: np.ndarray, oh: int = 800, ow: int = 600) -> np.ndarray:

@@ -7,6 +7,7 @@ import pytest
 
 import wocr
 from oracle import ref
+from wocr import synth
 from wocr.synth import _Builder
 
 from _helpers import argmax_parity
@@ -290,3 +291,42 @@ def test_handles_outlive_their_context():
     x = rnd(1, 8, 9, 11)
     close(nd.run(x), ref.run_onnx(m, x))
     nd.close()
+
+
+def _pp_boxes(w, h, rng):
+    """Line boxes of a page: ordinary lines (down- and upsampled heights), boxes on the page's
+    edges and corners, a box reaching past the last row, degenerate (empty, reversed, NaN) boxes
+    and fractional coordinates."""
+    boxes = [[rng.uniform(0, w - 800), y, 0, 0] for y in rng.uniform(0, h - 120, 20)]
+    for b in boxes:
+        b[2] = b[0] + rng.uniform(30, 800)
+        b[3] = b[1] + rng.uniform(12, 110)
+    boxes += [[0, 0, 37, 21], [w - 13, h - 9, w + 40, h + 40], [w, 100, w, 140], [500, h - 3, 900, h + 50],
+              [300, 400, 200, 380], [float("nan"), 10, 60, 40], [10.7, 20.2, 1500.9, 20.9], [0, 0, w, 60],
+              [100, 200, 110, 1900]]
+    return np.array(boxes, np.float32)
+
+
+def test_pp_lines_bit_exact(gpu):
+    """Recognition line batches cut on the device (ppocr.rs line_input + ocr-bench.rs pp_batches):
+    the layout (order, batch sizes and widths) and every value equal the oracle's; 19 lines per
+    batch leaves a partial last batch."""
+    import torch
+
+    w, h = 2550, 3300
+    page = synth.page(7, w, h)
+    rects = _pp_boxes(w, h, np.random.default_rng(3))
+    order, batches, total = gpu.pp_lines(0, w, h, rects, per_batch=19)
+    rb, rorder = ref.pp_batches(page, rects, per=19)
+    assert order == rorder
+    assert batches == [(n, wd) for _, n, wd in rb]
+    d_page = torch.from_numpy(page).cuda()
+    d_out = torch.full((total,), float("nan"), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    gpu.pp_lines(d_page.data_ptr(), w, h, rects, per_batch=19, d_out=d_out.data_ptr(), cap=total)
+    got = d_out.cpu().numpy()
+    want = np.concatenate([b.ravel() for b, _, _ in rb])
+    assert got.shape == want.shape
+    np.testing.assert_array_equal(got, want)
+    with pytest.raises(wocr.WocrError):
+        gpu.pp_lines(d_page.data_ptr(), w, h, rects, per_batch=19, d_out=d_out.data_ptr(), cap=total - 1)

@@ -194,3 +194,53 @@ def test_synth_determinism():
     assert all((x == y).all() for x, y in zip(la, lb))
     ma, mb = synth.ocrs_det_model(), synth.ocrs_det_model()
     assert all((ma.weights[k] == mb.weights[k]).all() for k in ma.weights)
+
+
+def _tri_resize_np(crop, ow, oh):
+    """The image crate's two-pass Triangle resize, restated independently with numpy float32:
+    a vertical pass into an f32 image, then a horizontal pass clamped and rounded to u8."""
+    def taps(n_in, n_out, o):
+        ratio = np.float32(n_in) / np.float32(n_out)
+        s = max(ratio, np.float32(1.0))
+        c = (np.float32(o) + np.float32(0.5)) * ratio
+        left = int(min(max(np.floor(c - s), 0), n_in - 1))
+        right = int(min(max(np.ceil(c + s), left + 1), n_in))
+        c = c - np.float32(0.5)
+        ws = [np.float32(max(np.float32(0), np.float32(1) - abs((np.float32(i) - c) / s))) for i in range(left, right)]
+        tot = np.float32(0)
+        for wv in ws:
+            tot = np.float32(tot + wv)
+        return left, [np.float32(wv / tot) for wv in ws]
+
+    ch, cw, _ = crop.shape
+    tmp = np.zeros((oh, cw, 3), np.float32)
+    for y in range(oh):
+        left, ws = taps(ch, oh, y)
+        acc = np.zeros((cw, 3), np.float32)
+        for i, wv in enumerate(ws):
+            acc = (acc + crop[left + i].astype(np.float32) * wv).astype(np.float32)
+        tmp[y] = acc
+    out = np.zeros((oh, ow, 3), np.uint8)
+    for x in range(ow):
+        left, ws = taps(cw, ow, x)
+        acc = np.zeros((oh, 3), np.float32)
+        for j, wv in enumerate(ws):
+            acc = (acc + tmp[:, left + j] * wv).astype(np.float32)
+        out[:, x] = np.floor(np.clip(acc, 0, 255) + np.float32(0.5)).astype(np.uint8)
+    return out
+
+
+@pytest.mark.parametrize("rect", [[5, 7, 125, 40], [0, 0, 33, 90], [40, 60, 44, 63], [10, 3, 300, 4]])
+def test_pp_line_oracle_matches_two_pass_restatement(rect):
+    """oracle_pp_line (one output pixel at a time, vertical sums per horizontal tap) equals the
+    two-pass resize with an intermediate image, and the line's width and normalisation."""
+    rng = np.random.default_rng(5)
+    page = rng.integers(0, 256, (120, 320, 3), dtype=np.uint8)
+    got = ref.pp_line(page, rect)
+    l, t, r, b = (int(min(max(v, 0), lim)) for v, lim in zip(rect, (320, 120, 320, 120)))
+    cw, ch = max(r - l, 1), max(b - t, 1)
+    ow = int(min(max(np.ceil(np.float32(48) * np.float32(cw) / np.float32(ch)), 8), 3200))
+    assert got.shape == (3, 48, ow)
+    px = _tri_resize_np(page[t:t + ch, l:l + cw], ow, 48)
+    want = ((px.astype(np.float32) / np.float32(255) - np.float32(0.5)) / np.float32(0.5)).transpose(2, 0, 1)
+    np.testing.assert_array_equal(got, want)

@@ -1430,6 +1430,69 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
     });
 }
 
+int32_t wocr_pp_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h, const float *rects, int32_t n,
+                      int32_t per_batch, float *d_out, int64_t cap, int32_t *order, int32_t *batch_n,
+                      int32_t *batch_w, int32_t *n_batches, int64_t *total) {
+    return guard([&] {
+        if (!ctx || (n > 0 && !rects)) fail(WOCR_ERR_INVALID, "null argument");
+        if (n < 0 || w <= 0 || h <= 0 || per_batch <= 0) fail(WOCR_ERR_INVALID, "bad page size, line count or batch");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        // each box as ppocr::line_input clamps and sizes it
+        auto clampb = [](float v, int hi) -> int {
+            if (!(v > 0.f)) v = 0.f;  // f32::max ignores NaN
+            if (v > (float)hi) v = (float)hi;
+            return (int)(unsigned)v;
+        };
+        std::vector<k::PpLine> ln((size_t)n);
+        for (int i = 0; i < n; i++) {
+            const float *r = rects + 4 * (size_t)i;
+            const int l = clampb(r[0], w), t = clampb(r[1], h), rr = clampb(r[2], w), b = clampb(r[3], h);
+            k::PpLine &L = ln[i];
+            L.l = l;
+            L.t = t;
+            L.cw = std::max(rr - l, 1);
+            L.ch = std::max(b - t, 1);
+            volatile float q = 48.f * (float)L.cw;  // rounded before the division, as the oracle
+            const float fw = std::ceil(q / (float)L.ch);
+            L.ow = fw < 8.f ? 8 : (fw > 3200.f ? 3200 : (int)fw);
+        }
+        // sorted by width (stable), cut into batches of per_batch, widths rounded up to 8
+        std::vector<int> idx((size_t)n);
+        for (int i = 0; i < n; i++) idx[i] = i;
+        std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return ln[a].ow < ln[b].ow; });
+        std::vector<k::PpLine> plan((size_t)n);
+        int64_t off = 0;
+        int nb = 0, max_width = 0;
+        for (int k0 = 0; k0 < n; k0 += per_batch, nb++) {
+            const int kn = std::min(per_batch, n - k0);
+            int width = 0;
+            for (int j = 0; j < kn; j++) width = std::max(width, ln[idx[k0 + j]].ow);
+            width = (width + 7) / 8 * 8;
+            max_width = std::max(max_width, width);
+            for (int j = 0; j < kn; j++) {
+                plan[k0 + j] = ln[idx[k0 + j]];
+                plan[k0 + j].width = width;
+                plan[k0 + j].off = off + (int64_t)j * 3 * 48 * width;
+                if (order) order[k0 + j] = idx[k0 + j];
+            }
+            if (batch_n) batch_n[nb] = kn;
+            if (batch_w) batch_w[nb] = width;
+            off += (int64_t)kn * 3 * 48 * width;
+        }
+        if (n_batches) *n_batches = nb;
+        if (total) *total = off;
+        if (!d_out || n == 0) return;
+        if (!d_rgb) fail(WOCR_ERR_INVALID, "null page");
+        if (cap < off) fail(WOCR_ERR_CAPACITY, "line batches need " + std::to_string(off) + " floats");
+        BufP dl = alloc(c, plan.size() * sizeof(k::PpLine));
+        WOCR_CUDA(cudaMemcpyAsync(dl->p, plan.data(), plan.size() * sizeof(k::PpLine), cudaMemcpyHostToDevice,
+                                  c->stream));
+        k::pp_lines(c, d_rgb, w, h, (const k::PpLine *)dl->p, n, max_width, d_out);
+        sync_bounded(c, 0);  // the plan's host copy is read until the upload completes
+    });
+}
+
 int32_t wocr_last_transfer_bytes(void *handle, int32_t kind, int64_t *h2d, int64_t *d2h) {
     return guard([&] {
         if (!handle) fail(WOCR_ERR_INVALID, "null handle");

@@ -133,6 +133,15 @@ void bmm(Ctx *c, const float *a, const float *bm, float *y, int64_t batch, int m
 // ocrs detector input (K13, src/gpu.rs:530-561): packed RGB pages -> grey, pad, half-pixel
 // bilinear to oh x ow.  n pages at rgb + i * page_bytes; output [n][oh][ow].
 void grey_resize(Ctx *c, const uint8_t *rgb, int64_t page_bytes, int n, int w, int h, int oh, int ow, float *y);
+
+// One PP-OCR recognition line of a batch (k_lines.cu): the clamped box (left, top, cw x ch), its
+// resized width ow, the batch width (>= ow, zero padding past ow) and the float offset of its
+// [3][48][width] block in the output.
+struct PpLine {
+    int l, t, cw, ch, ow, width;
+    int64_t off;
+};
+void pp_lines(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_width, float *out);
 // The same on compacted pages: per page 2 oh rows of w * 3 bytes (the top and bottom source rows
 // of each output row), rows[oy] = {vertical weight (float bits), bit 0/1: top/bottom is padding}.
 void grey_resize_rows(Ctx *c, const uint8_t *cmp, const int2 *rows, int n, int w, int oh, int ow, float *y);

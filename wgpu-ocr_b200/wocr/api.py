@@ -51,6 +51,21 @@ class Gpu:
     def launches(self) -> int:
         return int(L.lib().wocr_ctx_launches(self.h))
 
+    def pp_lines(self, d_rgb: int, w: int, h: int, rects, per_batch: int = 16, d_out: int = 0, cap: int = 0):
+        """PP-OCR recognition line batches cut from a device page (`wocr_pp_lines`): returns
+        (order, [(n, width)] per batch, total floats).  With d_out (a device float buffer of `cap`
+        floats) the batches are written there, one after another, [n, 3, 48, width] each."""
+        r = np.ascontiguousarray(rects, np.float32).reshape(-1, 4)
+        n = r.shape[0]
+        order = np.zeros(max(n, 1), np.int32)
+        bn = np.zeros(max(n, 1), np.int32)
+        bw = np.zeros(max(n, 1), np.int32)
+        nb, tot = ctypes.c_int32(), ctypes.c_int64()
+        L.check(L.lib().wocr_pp_lines(self.h, ctypes.c_void_p(d_rgb), int(w), int(h), L.ptr(r), n, int(per_batch),
+                                      ctypes.c_void_p(d_out or None), int(cap), L.ptr(order), L.ptr(bn), L.ptr(bw),
+                                      ctypes.byref(nb), ctypes.byref(tot)))
+        return order[:n].tolist(), [(int(bn[i]), int(bw[i])) for i in range(nb.value)], tot.value
+
     def profile(self, on: bool):
         """Start (clearing earlier records) or stop per-kernel CUDA-event timing."""
         L.check(L.lib().wocr_ctx_profile(self.h, int(bool(on))))
