@@ -1488,7 +1488,9 @@ int32_t wocr_pp_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h,
         BufP dl = alloc(c, plan.size() * sizeof(k::PpLine));
         WOCR_CUDA(cudaMemcpyAsync(dl->p, plan.data(), plan.size() * sizeof(k::PpLine), cudaMemcpyHostToDevice,
                                   c->stream));
-        k::pp_lines(c, d_rgb, w, h, (const k::PpLine *)dl->p, n, max_width, d_out);
+        double bytes = 4.0 * (double)off;
+        for (const k::PpLine &L : plan) bytes += 3.0 * L.cw * L.ch;
+        k::pp_lines(c, d_rgb, w, h, (const k::PpLine *)dl->p, n, max_width, d_out, bytes);
         sync_bounded(c, 0);  // the plan's host copy is read until the upload completes
     });
 }

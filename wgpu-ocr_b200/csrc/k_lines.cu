@@ -52,50 +52,76 @@ __device__ __forceinline__ float weight(const Taps &t, int k) {
     return __fdiv_rn(tri(__fdiv_rn(__fsub_rn((float)(t.left + k), t.center), t.sratio)), t.sum);
 }
 
-__global__ void k_pp_lines(const uint8_t *__restrict__ rgb, int w, int h, const PpLine *__restrict__ lines,
-                           float *__restrict__ out) {
-    const PpLine L = lines[blockIdx.z];
-    const int y = blockIdx.y, x = blockIdx.x * blockDim.x + threadIdx.x;
+constexpr int kRowTaps = 16;  // vertical taps per row kept in shared memory (more: computed per use)
+constexpr int kMaxXTaps = 8;  // horizontal taps kept in registers (more: computed per use)
+
+// A block: 128 output columns of one line, all 48 rows.  The rows' vertical taps are computed
+// once per block (thread y: row y, its sum in order, then its weights), each thread's horizontal
+// taps once per thread.
+__global__ void __launch_bounds__(128) k_pp_lines(const uint8_t *__restrict__ rgb, int w, int h,
+                                                  const PpLine *__restrict__ lines, float *__restrict__ out) {
+    __shared__ Taps ty_s[48];
+    __shared__ float wy_s[48][kRowTaps];
+    const PpLine L = lines[blockIdx.y];
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    if (blockIdx.x * blockDim.x >= L.width) return;  // the whole block is past this line's batch width
+    if (threadIdx.x < 48) {
+        const Taps t = taps(L.ch, 48, threadIdx.x);
+        ty_s[threadIdx.x] = t;
+        for (int k = 0; k < t.n && k < kRowTaps; k++) wy_s[threadIdx.x][k] = weight(t, k);
+    }
+    __syncthreads();
     if (x >= L.width) return;
     float *o = out + L.off;
     const int64_t plane = (int64_t)48 * L.width;
     if (x >= L.ow) {
-        for (int c = 0; c < 3; c++) o[c * plane + (int64_t)y * L.width + x] = 0.f;
+        for (int y = 0; y < 48; y++)
+            for (int c = 0; c < 3; c++) o[c * plane + (int64_t)y * L.width + x] = 0.f;
         return;
     }
     const int64_t total = (int64_t)w * h * 3;
-    const Taps ty = taps(L.ch, 48, y), tx = taps(L.cw, L.ow, x);
-    float acc[3] = {0.f, 0.f, 0.f};
-    for (int j = 0; j < tx.n; j++) {
-        const float wx = weight(tx, j);
-        float v[3] = {0.f, 0.f, 0.f};
-        for (int i = 0; i < ty.n; i++) {
-            const float wy = weight(ty, i);
-            // crop row: cw * 3 bytes at ((top + row) * w + left) * 3, zeros when they leave the page
-            const int64_t row = ((int64_t)(L.t + ty.left + i) * w + L.l) * 3;
-            const bool in = row + (int64_t)L.cw * 3 <= total;
-            const uint8_t *p = rgb + row + (int64_t)(tx.left + j) * 3;
+    const Taps tx = taps(L.cw, L.ow, x);
+    float wxr[kMaxXTaps];
 #pragma unroll
-            for (int c = 0; c < 3; c++) v[c] = __fadd_rn(v[c], __fmul_rn(in ? (float)p[c] : 0.f, wy));
+    for (int k = 0; k < kMaxXTaps; k++) wxr[k] = k < tx.n ? weight(tx, k) : 0.f;
+    for (int y = 0; y < 48; y++) {
+        const Taps ty = ty_s[y];
+        float acc[3] = {0.f, 0.f, 0.f};
+        for (int j = 0; j < tx.n; j++) {
+            float wx = 0.f;
+#pragma unroll
+            for (int k = 0; k < kMaxXTaps; k++)
+                if (k == j) wx = wxr[k];
+            if (j >= kMaxXTaps) wx = weight(tx, j);
+            float v[3] = {0.f, 0.f, 0.f};
+            for (int i = 0; i < ty.n; i++) {
+                const float wy = i < kRowTaps ? wy_s[y][i] : weight(ty, i);
+                // crop row: cw * 3 bytes at ((top + row) * w + left) * 3, zeros when they leave the page
+                const int64_t row = ((int64_t)(L.t + ty.left + i) * w + L.l) * 3;
+                const bool in = row + (int64_t)L.cw * 3 <= total;
+                const uint8_t *p = rgb + row + (int64_t)(tx.left + j) * 3;
+#pragma unroll
+                for (int c = 0; c < 3; c++) v[c] = __fadd_rn(v[c], __fmul_rn(in ? (float)p[c] : 0.f, wy));
+            }
+#pragma unroll
+            for (int c = 0; c < 3; c++) acc[c] = __fadd_rn(acc[c], __fmul_rn(v[c], wx));
         }
 #pragma unroll
-        for (int c = 0; c < 3; c++) acc[c] = __fadd_rn(acc[c], __fmul_rn(v[c], wx));
-    }
-#pragma unroll
-    for (int c = 0; c < 3; c++) {
-        const float a = acc[c] < 0.f ? 0.f : (acc[c] > 255.f ? 255.f : acc[c]);
-        const float q = roundf(a);
-        o[c * plane + (int64_t)y * L.width + x] = __fdiv_rn(__fsub_rn(__fdiv_rn(q, 255.f), 0.5f), 0.5f);
+        for (int c = 0; c < 3; c++) {
+            const float a = acc[c] < 0.f ? 0.f : (acc[c] > 255.f ? 255.f : acc[c]);
+            const float q = roundf(a);
+            o[c * plane + (int64_t)y * L.width + x] = __fdiv_rn(__fsub_rn(__fdiv_rn(q, 255.f), 0.5f), 0.5f);
+        }
     }
 }
 
 }  // namespace
 
-void pp_lines(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_width, float *out) {
+void pp_lines(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_width, float *out,
+              double bytes) {
     if (n <= 0) return;
-    double bytes = 0;
     Prof pf(c, "pp_lines", 0, bytes);
-    dim3 grid((unsigned)((max_width + 127) / 128), 48, (unsigned)n);
+    dim3 grid((unsigned)((max_width + 127) / 128), (unsigned)n);
     k_pp_lines<<<grid, 128, 0, c->stream>>>(rgb, w, h, lines, out);
     WOCR_LAUNCHED(c);
 }

@@ -141,7 +141,9 @@ struct PpLine {
     int l, t, cw, ch, ow, width;
     int64_t off;
 };
-void pp_lines(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_width, float *out);
+// bytes: the algorithmic bytes (the boxes' page bytes read, the batches written), for the profile
+void pp_lines(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_width, float *out,
+              double bytes);
 // The same on compacted pages: per page 2 oh rows of w * 3 bytes (the top and bottom source rows
 // of each output row), rows[oy] = {vertical weight (float bits), bit 0/1: top/bottom is padding}.
 void grey_resize_rows(Ctx *c, const uint8_t *cmp, const int2 *rows, int n, int w, int oh, int ow, float *y);

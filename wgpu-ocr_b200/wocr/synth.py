@@ -424,24 +424,49 @@ def pp_batches(lines: List[np.ndarray], per: int = 16):
     return batches, order
 
 
-def page(seed: int = 1, w: int = 2550, h: int = 3300, bands: int = 36, line_h: int = 40,
-         ink: int = 20) -> np.ndarray:
-    """A US Letter page at 300 dpi as RGB u8 [h, w, 3]: white, with `bands` text lines of
-    dark rectangles (width 10..60 px, gaps 4..16 px, a wider word gap now and then)."""
+def _page_layout(seed: int, w: int, h: int, bands: int, line_h: int):
+    """The ink rectangles of page(seed, ...), band by band: [(y0, y1, [(x0, x1), ...]), ...]."""
     rng = np.random.default_rng(seed + 2000)
-    img = np.full((h, w, 3), 255, np.uint8)
     margin_y, margin_x = h * 150 // 3300, w * 150 // 2550
     pitch = (h - 2 * margin_y) / bands
+    out = []
     for i in range(bands):
         y0 = int(margin_y + i * pitch)
         y1 = min(h, y0 + line_h)
         x = margin_x + int(rng.integers(0, 40))
         end = w - margin_x - int(rng.integers(0, 400))
+        rects = []
         while x < end:
             rw = int(rng.integers(10, 61))
-            img[y0:y1, x:min(end, x + rw)] = ink
+            rects.append((x, min(end, x + rw)))
             x += rw + int(rng.integers(4, 17)) + (int(rng.integers(20, 40)) if rng.random() < 0.15 else 0)
+        out.append((y0, y1, rects))
+    return out
+
+
+def page(seed: int = 1, w: int = 2550, h: int = 3300, bands: int = 36, line_h: int = 40,
+         ink: int = 20) -> np.ndarray:
+    """A US Letter page at 300 dpi as RGB u8 [h, w, 3]: white, with `bands` text lines of
+    dark rectangles (width 10..60 px, gaps 4..16 px, a wider word gap now and then)."""
+    img = np.full((h, w, 3), 255, np.uint8)
+    for y0, y1, rects in _page_layout(seed, w, h, bands, line_h):
+        for x0, x1 in rects:
+            img[y0:y1, x0:x1] = ink
     return img
+
+
+def page_line_boxes(seed: int = 1, w: int = 2550, h: int = 3300, bands: int = 36, line_h: int = 40,
+                    relv: float = 0.1) -> np.ndarray:
+    """The text lines of page(seed, ...) as recognition boxes [left, top, right, bottom] (f32):
+    each band's ink extent, grown by relv x its height above and below, as the reference pads DB
+    boxes (RELV 0.1, src/bin/ocr-bench.rs:538-556)."""
+    boxes = []
+    for y0, y1, rects in _page_layout(seed, w, h, bands, line_h):
+        if not rects:
+            continue
+        pad = relv * (y1 - y0)
+        boxes.append([rects[0][0], y0 - pad, rects[-1][1], y1 + pad])
+    return np.array(boxes, np.float32)
 
 
 def pages(seed: int = 1, n: int = 12, w: int = 2550, h: int = 3300) -> List[np.ndarray]:
