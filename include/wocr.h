@@ -85,6 +85,14 @@ typedef struct {
     const char *output;               /* first graph output (onnx.rs:120)                   */
 } wocr_model;
 
+/* ONNX model files (src/onnx.rs:57-123, Onnx::load): the protobuf wire format decoded into a
+ * wocr_model with the loader's semantics (float / int64 initializers, Constant nodes folded
+ * into them, graph input = first input that is not a float weight, output = first output).
+ * The model owns its memory until wocr_model_free.  wocr_model_parse reads a buffer. */
+int32_t wocr_model_load(const char *path, wocr_model **out);
+int32_t wocr_model_parse(const uint8_t *bytes, int64_t n, wocr_model **out);
+void wocr_model_free(wocr_model *m);
+
 /* ---- device context: `Gpu` (src/gpu.rs:825-1056) -------------------------------------- */
 typedef struct wocr_ctx wocr_ctx;
 

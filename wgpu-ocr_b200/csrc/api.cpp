@@ -197,24 +197,6 @@ struct wocr_ndgraph {
 
 namespace {
 
-template <typename F>
-int32_t guard(F &&f) {
-    try {
-        f();
-        set_last_error("");
-        return WOCR_OK;
-    } catch (const Error &e) {
-        set_last_error(e.what());
-        return e.code;
-    } catch (const std::bad_alloc &) {
-        set_last_error("host out of memory");
-        return WOCR_ERR_OOM;
-    } catch (const std::exception &e) {
-        set_last_error(e.what());
-        return WOCR_ERR_INVALID;
-    }
-}
-
 struct RunScope {
     Ctx *c;
     Stats *out;

@@ -26,6 +26,25 @@ struct Error : std::runtime_error {
 [[noreturn]] void fail(int32_t code, const std::string &msg);
 void set_last_error(const std::string &msg);
 
+// Runs an ABI entry point's body: a status code and the thread-local message from what it threw.
+template <typename F>
+int32_t guard(F &&f) {
+    try {
+        f();
+        set_last_error("");
+        return WOCR_OK;
+    } catch (const Error &e) {
+        set_last_error(e.what());
+        return e.code;
+    } catch (const std::bad_alloc &) {
+        set_last_error("host out of memory");
+        return WOCR_ERR_OOM;
+    } catch (const std::exception &e) {
+        set_last_error(e.what());
+        return WOCR_ERR_INVALID;
+    }
+}
+
 #define WOCR_CUDA(call)                                                                          \
     do {                                                                                         \
         cudaError_t e_ = (call);                                                                 \

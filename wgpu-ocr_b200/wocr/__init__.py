@@ -7,6 +7,7 @@ models and inputs of the benchmark configurations are in `wocr.synth`.
 from ._lib import EXPORTS, LIB_PATH, WocrError, lib
 from .api import Detector, Gpu, NdGraph, Recognizer, ocrs_decode, pp_decode
 from .model import Model, Node
+from .onnx import load_onnx, parse_onnx
 
 __all__ = ["Gpu", "Detector", "Recognizer", "NdGraph", "WocrError", "Model", "Node", "ocrs_decode", "pp_decode",
-           "lib", "LIB_PATH", "EXPORTS"]
+           "lib", "LIB_PATH", "EXPORTS", "load_onnx", "parse_onnx"]
