@@ -299,7 +299,7 @@ static DT maxpool_run(Ctx *ctx, DT x, int kh, int kw, bool split_out) {
 // A convolution whose input is a split tensor: the tap convolution (stride 1, dense) or the
 // pointwise kernel; false when neither applies (the caller converts the input to fp32).
 static bool conv_split(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale,
-                       const OutAlloc *out, DT &y, PoolReq *pool) {
+                       const OutAlloc *out, DT &y, PoolReq *pool, HeadReq *head) {
     if (res || scale || cw.kind != ConvW::DENSE || !x.nhwc()) return false;
     int64_t n = x.shape[0], cin = x.shape[1], h = x.shape[2], w = x.shape[3];
     if (cw.cin != cin)
@@ -326,8 +326,42 @@ static bool conv_split(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *
     }
     if (!cw.tw || cw.sh != 1 || cw.sw != 1 || !k::tconv_input_ok(xp, x.strides[0], x.pix())) return false;
     const int64_t oh = h + pt + pb - cw.kh + 1, ow = w + pl + pr - cw.kw + 1;
-    KOut o = kout(c, out, n, cw.cout, oh, ow, true);
     k::TconvP p;
+    if (head && !pool && head->cw->cin == cw.cout && head->cw->cout <= 4) {
+        // the head from the row kernel's epilogue; this convolution's output is never stored
+        p.x = xp;
+        p.x_n = x.strides[0];
+        p.x_pix = x.pix();
+        p.n = (int)n;
+        p.h = (int)h;
+        p.w = (int)w;
+        p.cin = (int)cin;
+        p.kh = cw.kh;
+        p.kw = cw.kw;
+        p.pt = pt;
+        p.pl = pl;
+        p.oh = (int)oh;
+        p.ow = (int)ow;
+        p.bias = cw.b.p;
+        p.act = act;
+        if (k::tconv_rows_eligible(*cw.tw, p)) {
+            head->out = new_nhwc(c, n, head->cw->cout, oh, ow);
+            p.head_w = head->cw->w.p;
+            p.head_b = head->cw->b.p;
+            p.head_ldw = head->cw->ldw;
+            p.head_n = head->cw->cout;
+            p.head_act = head->act;
+            p.head_y = head->out.p;
+            p.head_y_n = head->out.strides[0];
+            p.head_y_pix = head->out.pix();
+            k::tconv(c, *cw.tw, p);
+            head->done = true;
+            y = DT();
+            return true;
+        }
+        p = k::TconvP();
+    }
+    KOut o = kout(c, out, n, cw.cout, oh, ow, true);
     p.x = xp;
     p.x_n = x.strides[0];
     p.x_pix = x.pix();
@@ -361,11 +395,25 @@ static bool conv_split(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *
     return true;
 }
 
+static DT conv_run_body(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale,
+                        const OutAlloc *out, PoolReq *pool, HeadReq *head);
+
 DT conv_run(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale, const OutAlloc *out,
-            PoolReq *pool) {
+            PoolReq *pool, HeadReq *head) {
+    DT y = conv_run_body(c, xin, cw, act, res, scale, out, pool, head);
+    if (head && !head->done) {
+        // not from the epilogue: the head as its own convolution of the stored output
+        head->out = conv_run_body(c, y, *head->cw, head->act, nullptr, nullptr, nullptr, nullptr, nullptr);
+        head->done = true;
+    }
+    return y;
+}
+
+static DT conv_run_body(Ctx *c, const DT &xin, const ConvW &cw, int act, const DT *res, const DT *scale,
+                        const OutAlloc *out, PoolReq *pool, HeadReq *head) {
     if (xin.split) {
         DT y;
-        if (conv_split(c, xin, cw, act, res, scale, out, y, pool)) {
+        if (conv_split(c, xin, cw, act, res, scale, out, y, pool, head)) {
             if (pool && !pool->done) pool->out = maxpool_run(c, y, 2, 2, pool->split), pool->done = true;
             return y;
         }
@@ -804,6 +852,48 @@ void Executor::finalize() {
             mp.pool_fused_away = true;
         }
     }
+    // 1 x 1 heads (at most 4 outputs, fp32) computed in the epilogue of the 3 x 3 tap convolution
+    // they read, when nothing else reads its output
+    for (auto &st : steps) st.head_output.clear(), st.head_step = -1, st.head_fused_away = false;
+    if (allow_split) {
+        for (size_t hi = 0; hi < steps.size(); hi++) {
+            Step &hs = steps[hi];
+            const ConvW &h = hs.conv;
+            if (hs.kind != Step::G_CONV || h.kind != ConvW::DENSE || h.kh != 1 || h.kw != 1 || h.sh != 1 ||
+                h.sw != 1 || h.cout > 4 || h.same_upper || h.pads[0] || h.pads[1] || h.pads[2] || h.pads[3] ||
+                hs.split_out || concat_slot.count(hs.output))
+                continue;
+            auto readers = [&](const std::string &v) {
+                int r = 0;
+                for (const Step &o : steps)
+                    for (const std::string &in : o.inputs) r += in == v;
+                return r;
+            };
+            // through identity steps (a zero Pad) with one reader each
+            std::string src = hs.inputs[0];
+            std::vector<int> between;
+            auto pi = producer.find(src);
+            bool ok = pi != producer.end();
+            while (ok && steps[pi->second].kind == Step::G_IDENTITY) {
+                const Step &id = steps[pi->second];
+                ok = readers(id.output) == 1 && id.output != output && !concat_slot.count(id.output);
+                between.push_back(pi->second);
+                src = id.inputs[0];
+                pi = producer.find(src);
+                ok = ok && pi != producer.end();
+            }
+            if (!ok) continue;
+            Step &cs = steps[pi->second];
+            if (cs.kind != Step::G_CONV || !cs.conv.tw || !cs.conv.tw->x3 || cs.conv.kh != 3 || cs.conv.kw != 3 ||
+                !cs.pool_output.empty() || !cs.head_output.empty() || cs.conv.cout != h.cin || cs.output == output ||
+                concat_slot.count(cs.output) || readers(cs.output) != 1)
+                continue;
+            cs.head_output = hs.output;
+            cs.head_step = (int)hi;
+            hs.head_fused_away = true;
+            for (int b : between) steps[b].head_fused_away = true;
+        }
+    }
 }
 
 // The output of a step registered in concat_slot: a channel slice of the Concat buffer (made on
@@ -924,6 +1014,18 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
     case Step::G_CONV:
     case Step::G_DIRECT:
     case Step::G_DEPTHWISE:
+        if (s.head_fused_away) return;  // computed with the convolution it reads
+        if (!s.head_output.empty()) {
+            const Step &hs = steps[s.head_step];
+            HeadReq hr;
+            hr.cw = &hs.conv;
+            hr.act = hs.act;
+            conv_run(ctx, getx(vals, s.inputs[0]), s.conv, s.act, nullptr, nullptr, &alloc_out, nullptr, &hr);
+            Value hv;
+            hv.f = hr.out;
+            vals[s.head_output] = hv;
+            return;  // this step's own output has no other reader
+        }
         if (!s.pool_output.empty()) {
             PoolReq pr;
             pr.split = s.pool_split;
@@ -1010,6 +1112,7 @@ void Executor::exec_step(const Step &s, std::map<std::string, Value> &vals) {
         break;
     }
     case Step::G_IDENTITY:
+        if (s.head_fused_away) return;  // between a convolution and the head fused into it
         out = get(vals, s.inputs[0]);
         break;
     case Step::N_LINEAR:

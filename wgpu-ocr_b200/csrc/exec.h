@@ -90,6 +90,12 @@ struct Step {
     // split when pool_split); the MaxPool step itself is then skipped (pool_fused_away)
     std::string pool_output;
     bool pool_split = false, pool_fused_away = false;
+    // a 1 x 1 head convolution (head_step, output head_output) computed by this convolution's
+    // epilogue: this step's own output is then never stored, and the head step is skipped
+    // (head_fused_away)
+    std::string head_output;
+    int head_step = -1;
+    bool head_fused_away = false;
 };
 
 class Executor {
@@ -149,8 +155,16 @@ struct PoolReq {
     bool done = false;
     DT out;
 };
+// A 1 x 1 convolution with at most 4 outputs (cw, act) that reads only the convolution being run:
+// computed by that convolution's epilogue when the row kernel runs it (done), else after it.
+struct HeadReq {
+    const ConvW *cw = nullptr;
+    int act = 0;
+    bool done = false;
+    DT out;
+};
 DT conv_run(Ctx *c, const DT &x, const ConvW &cw, int act, const DT *res, const DT *scale,
-            const OutAlloc *out = nullptr, PoolReq *pool = nullptr);
+            const OutAlloc *out = nullptr, PoolReq *pool = nullptr, HeadReq *head = nullptr);
 DT linear_run(Ctx *c, const DT &x, const DevW &w, const DevW &b, int K, int N, int ldw, int act,
               const k::UmmaW *uw = nullptr);
 // [K][N] row-major fp32 weights -> the tensor-core operand of y = x W.

@@ -71,6 +71,12 @@ struct TcP {
     int pool_split, pool_vec;
     int64_t pool_n, pool_pix;
     uint32_t stg_off;           // per-warp 2 KB store staging (transposed stores), 0: none
+    // fused 1 x 1 head (row kernel): weights [N][4] at head_off in shared memory, bias after them
+    const float *head_w, *head_b;
+    int head_ldw, head_n, head_act;
+    float *head_y;
+    int64_t head_y_n, head_y_pix;
+    uint32_t head_off;
     int *status;
 };
 
@@ -787,8 +793,15 @@ __global__ void __launch_bounds__(kRThreads, 1)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     float *bias_s = reinterpret_cast<float *>(smem + p.bias_off);
+    float *head_s = reinterpret_cast<float *>(smem + p.head_off);  // [C][4] weights, then 4 biases
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < p.bias_n; i += blockDim.x) bias_s[i] = p.bias[i];
+    if (p.head_y)
+        for (int i = threadIdx.x; i < C * 4 + 4; i += blockDim.x) {
+            const int c = i >> 2, co = i & 3;
+            head_s[i] = c < C ? (c < p.N && co < p.head_n ? p.head_w[(int64_t)c * p.head_ldw + co] : 0.f)
+                              : (co < p.head_n ? p.head_b[co] : 0.f);
+        }
     {
         // the stacked weights, resident for the whole kernel: generic stores, made visible to
         // the tensor cores by each writer's proxy fence before the barrier
@@ -910,6 +923,9 @@ __global__ void __launch_bounds__(kRThreads, 1)
             const Tile tl = decode_rows(p, t);
             const int oy = tl.oy0 + r, ox = tl.ox0 + j;
             const bool valid = j < RV && oy < p.oh && ox < p.ow;
+            float hacc[4];
+#pragma unroll
+            for (int co = 0; co < 4; co++) hacc[co] = head_s[C * 4 + co];
 #pragma unroll 1
             for (int c0 = 0; c0 < C; c0 += 16) {
                 const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + c0;
@@ -936,6 +952,15 @@ __global__ void __launch_bounds__(kRThreads, 1)
                     v[jj + 1] = o.y;
                 }
                 act16(v, p.act);
+                if (p.head_y) {
+                    // the 1 x 1 head, channels in order as k_pointwise sums them; no output stored
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++)
+                        if (c0 + jj < p.N)  // past N: padding columns, not channels
+#pragma unroll
+                            for (int co = 0; co < 4; co++) hacc[co] += v[jj] * head_s[(c0 + jj) * 4 + co];
+                    continue;
+                }
                 const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
                 if (p.stg_off && col + 16 <= p.N) {
                     store16_t(p, off, valid, v, stg, lane);
@@ -958,6 +983,12 @@ __global__ void __launch_bounds__(kRThreads, 1)
                     for (int jj = 0; jj < 16; jj++)
                         if (col + jj < p.N) store1(p, off + jj, v[jj]);
                 }
+            }
+            if (p.head_y && valid) {
+                float *hy = p.head_y + (int64_t)tl.nb * p.head_y_n + ((int64_t)oy * p.ow + ox) * p.head_y_pix;
+#pragma unroll
+                for (int co = 0; co < 4; co++)
+                    if (co < p.head_n) hy[co] = act_f(hacc[co], p.head_act);
             }
             tc_fence_before();
             __syncwarp();
@@ -1047,9 +1078,36 @@ void launch_rows_any(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUte
     }
 }
 
-// The row kernel's launch parameters (geometry, stages); false when its stages do not fit.
-bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap *xm, bool &whole) {
+// The row kernel's shared memory: A stages, B, barriers, bias, head, store staging (p.out_vec and
+// p.bias_n set); false when it does not fit.
+bool plan_rows_smem(const TconvW &w, TcP &p, int &smem) {
     const int C = w.x3_cout, CG = w.x3_cg;
+    p.hw_w = RP;
+    p.halo_px = (RX + 2) * RP;
+    p.plane = 0;
+    p.a_stage = (uint32_t)(2 * p.halo_px * CG * 2);  // hi part, lo part: multiples of 1024 bytes
+    const int b_region = (3 * (CG / 8) * 6 * C * 16 + 1023) / 1024 * 1024;
+    // transposed-store staging: 2 KB per epilogue warp when the stores are 16-byte aligned
+    const int stg = p.out_vec ? kRGroups * 4 * 2048 : 0;
+    const int SA = std::min(8, (kSmemBudget - b_region - stg) / (int)p.a_stage);
+    if (SA < 2) return false;
+    p.SA = SA;
+    p.SB = 0;
+    p.lag = std::min(kLagMax, SA - 2);
+    p.b_off = (uint32_t)SA * p.a_stage;
+    p.bar_off = p.b_off + (uint32_t)b_region;
+    p.bias_off = p.bar_off + 1024;
+    p.head_off = p.bias_off + (uint32_t)((p.bias_n * 4 + 15) / 16 * 16);
+    const int head_bytes = (C * 4 + 4) * 4;
+    p.stg_off = stg ? p.head_off + (uint32_t)head_bytes : 0;
+    smem = (int)p.head_off + head_bytes + stg + 1024;
+    return smem <= 227 * 1024;
+}
+
+// The row kernel's launch parameters (geometry, tensor maps of the halo, shared memory); false
+// when it does not fit.
+bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap *xm, bool &whole) {
+    const int CG = w.x3_cg;
     p.trows = RX;
     p.tiles_x = (q.ow + RV - 1) / RV;
     p.tiles_y = (q.oh + RX - 1) / RX;
@@ -1060,10 +1118,7 @@ bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap 
     p.div_ntn = FastDiv(1);
     p.div_tx = FastDiv((uint32_t)p.tiles_x);
     p.div_ty = FastDiv((uint32_t)p.tiles_y);
-    p.hw_w = RP;
-    p.halo_px = (RX + 2) * RP;
-    p.plane = 0;
-    p.a_stage = (uint32_t)(2 * p.halo_px * CG * 2);  // hi part, lo part: multiples of 1024 bytes
+    if (!plan_rows_smem(w, p, smem)) return false;
     // the halo boxes: [n][h][w][channels < cin] of the hi and of the lo parts, zeros outside
     const cuuint64_t dims[4] = {(cuuint64_t)q.cin, (cuuint64_t)q.w, (cuuint64_t)q.h, (cuuint64_t)q.n};
     const cuuint64_t strides[3] = {(cuuint64_t)q.x_pix * 2, (cuuint64_t)q.w * q.x_pix * 2, (cuuint64_t)q.x_n * 2};
@@ -1079,20 +1134,7 @@ bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap 
         encode(&xm[0], 4, const_cast<uint16_t *>(q.x), dims, strides, box, CG);
         encode(&xm[1], 4, const_cast<uint16_t *>(q.x + q.x_pix / 2), dims, strides, box, CG);
     }
-    const int b_region = (3 * (CG / 8) * 6 * C * 16 + 1023) / 1024 * 1024;
-    // transposed-store staging: 2 KB per epilogue warp when the stores are 16-byte aligned
-    const int stg = p.out_vec ? kRGroups * 4 * 2048 : 0;
-    const int SA = std::min(8, (kSmemBudget - b_region - stg) / (int)p.a_stage);
-    if (SA < 2) return false;
-    p.SA = SA;
-    p.SB = 0;
-    p.lag = std::min(kLagMax, SA - 2);
-    p.b_off = (uint32_t)SA * p.a_stage;
-    p.bar_off = p.b_off + (uint32_t)b_region;
-    p.bias_off = p.bar_off + 1024;
-    p.stg_off = stg ? p.bias_off + (uint32_t)((p.bias_n * 4 + 15) / 16 * 16) : 0;
-    smem = (int)p.bias_off + (p.bias_n * 4 + 15) / 16 * 16 + stg + 1024;
-    return smem <= 227 * 1024;
+    return true;
 }
 
 }  // namespace
@@ -1162,6 +1204,17 @@ bool tconv_input_ok(const uint16_t *x, int64_t x_n, int64_t x_pix) {
     return (reinterpret_cast<uintptr_t>(x) & 15) == 0 && x_pix % 16 == 0 && x_n % 8 == 0;
 }
 
+bool tconv_rows_eligible(const TconvW &w, const TconvP &q) {
+    if (!w.x3 || q.kh != 3 || q.kw != 3 || q.scatter || std::getenv("WOCR_NO_ROWS")) return false;
+    if ((int64_t)q.n * ((q.ow + RV - 1) / RV) * ((q.oh + RX - 1) / RX) >= (int64_t)INT32_MAX) return false;
+    TcP p{};
+    const bool al = (reinterpret_cast<uintptr_t>(q.y) & 15) == 0;
+    p.out_vec = q.split_out ? (al && q.y_pix % 16 == 0 && q.y_n % 8 == 0) : (al && q.y_pix % 4 == 0 && q.y_n % 4 == 0);
+    p.bias_n = w.N;
+    int smem = 0;
+    return plan_rows_smem(w, p, smem);
+}
+
 void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     const int64_t M = (int64_t)q.n * q.oh * q.ow;
     if (M == 0 || w.N == 0) return;
@@ -1209,8 +1262,21 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
                                   : (pal && q.pool_pix % 4 == 0 && q.pool_n % 4 == 0);
     }
     p.status = c->status;
+    if (q.head_y) {
+        if (q.head_n < 1 || q.head_n > 4 || q.pool_y || q.scatter)
+            fail(WOCR_ERR_UNSUPPORTED, "fused head: 1 to 4 outputs, no pool, no scatter");
+        p.head_w = q.head_w;
+        p.head_b = q.head_b;
+        p.head_ldw = q.head_ldw;
+        p.head_n = q.head_n;
+        p.head_act = q.head_act;
+        p.head_y = q.head_y;
+        p.head_y_n = q.head_y_n;
+        p.head_y_pix = q.head_y_pix;
+    }
     const double flops = 2.0 * (double)M * w.N * w.taps * w.cin;
     const double bytes = 4.0 * ((double)q.n * q.h * q.w * q.cin + (double)M * w.N) + 4.0 * (double)w.N * w.taps * w.cin;
+    if (q.head_y && !tconv_rows_eligible(w, q)) fail(WOCR_ERR_UNSUPPORTED, "fused head without the row kernel");
     // the narrow 3 x 3 layers: kernel columns stacked along N (k_tconv_rows)
     if (w.x3 && q.kh == 3 && q.kw == 3 && !q.scatter && !std::getenv("WOCR_NO_ROWS")) {
         TcP pr = p;

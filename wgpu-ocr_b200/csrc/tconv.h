@@ -44,7 +44,17 @@ struct TconvP {
     void *pool_y = nullptr;
     int pool_split = 0;
     int64_t pool_n = 0, pool_pix = 0;
+    // fused 1 x 1 head (null head_y: none): the output is not stored; instead
+    // head_y[n][oh][ow][head_n] (fp32, strides in floats) = act(head_b + sum_c out_c head_w[c][co]),
+    // head_w [cin][head_ldw], head_n <= 4.  Only the row kernel has it (tconv_rows_eligible).
+    const float *head_w = nullptr, *head_b = nullptr;
+    int head_ldw = 0, head_n = 0, head_act = 0;
+    float *head_y = nullptr;
+    int64_t head_y_n = 0, head_y_pix = 0;
 };
+
+// Whether tconv runs this launch on the row kernel (the only one with the fused head).
+bool tconv_rows_eligible(const TconvW &w, const TconvP &p);
 
 // The input view meets the TMA rules (16-byte aligned base, lo part and strides).
 bool tconv_input_ok(const uint16_t *x, int64_t x_n, int64_t x_pix);
