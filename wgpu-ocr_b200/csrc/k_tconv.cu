@@ -170,47 +170,11 @@ __device__ __forceinline__ void store16(const TcP &p, int64_t off, const float (
     for (int j = 0; j < 16; j++) store1(p, off + j, v[j]);
 }
 
-// store16 for a whole warp, transposed through the warp's 2 KB staging area so that each store
-// instruction covers 8 pixels x 4 pieces instead of 32 pixels x 1 piece: a lane's 16 channels
-// are 4 pieces of 16 bytes (hi 0-7, hi 8-15, lo 0-7, lo 8-15; or 4 float4), written to the
-// staging area (piece index XORed with bits 1-2 of the lane: conflict-free), then lane l stores
-// piece l % 4 of pixel 8 k + l / 4 for k = 0..3.  `off` and `valid` are each lane's own pixel.
+// store16 for a whole warp (warp_store16 in tc.h: transposed through the warp's staging area).
 // Needs p.out_vec; every lane of the warp takes part.
 __device__ __forceinline__ void store16_t(const TcP &p, int64_t off, bool valid, const float (&v)[16], uint4 *stg,
                                          int lane) {
-    uint4 q[4];
-    if (p.split_out) {
-        uint4 hi[2], lo[2];
-        split16(v, hi, lo);
-        q[0] = hi[0];
-        q[1] = hi[1];
-        q[2] = lo[0];
-        q[3] = lo[1];
-    } else {
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-            q[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]), __float_as_uint(v[4 * i + 2]),
-                              __float_as_uint(v[4 * i + 3]));
-    }
-    const int sw = (lane >> 1) & 3;
-#pragma unroll
-    for (int i = 0; i < 4; i++) stg[lane * 4 + (i ^ sw)] = q[i];
-    __syncwarp();
-    const int pc = lane & 3;
-    // piece pc of a pixel: element offset from the pixel's channel 0 (bf16 or fp32 elements)
-    const int64_t poff = p.split_out ? (int64_t)(pc & 1) * 8 + (pc >> 1) * (p.y_pix / 2) : (int64_t)pc * 4;
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-        const int P = 8 * k + (lane >> 2);
-        const int64_t o = __shfl_sync(0xffffffffu, off, P);
-        const bool vv = __shfl_sync(0xffffffffu, (int)valid, P) != 0;
-        const uint4 val = stg[P * 4 + (pc ^ ((P >> 1) & 3))];
-        if (vv) {
-            if (p.split_out) *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(p.y) + o + poff) = val;
-            else *reinterpret_cast<uint4 *>(reinterpret_cast<float *>(p.y) + o + poff) = val;
-        }
-    }
-    __syncwarp();
+    warp_store16(p.y, p.split_out != 0, p.y_pix, off, valid, v, stg, lane);
 }
 
 // TAPS: 9 (3 x 3 kernel), 1 (1 x 1) or 0 (any kernel, taps counted at run time).

@@ -285,6 +285,52 @@ __device__ __forceinline__ void split8(const float (&v)[8], uint4 &hi, uint4 &lo
     lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// 16 channels a lane stored for a whole warp, transposed through the warp's 2 KB staging area
+// (`stg`, 128 uint4) so that each store instruction covers 8 pixels x 4 pieces instead of 32
+// pixels x 1 piece (fewer lines per instruction).  A lane's channels are 4 pieces of 16 bytes:
+// split (y bf16 elements): hi 0-7, hi 8-15 at off, lo 0-7, lo 8-15 at off + y_pix / 2; fp32: 4
+// float4 at off.  They are written to the staging area (piece index XORed with bits 1-2 of the
+// lane: conflict-free), then lane l stores piece l % 4 of pixel 8 k + l / 4 for k = 0..3.  `off`
+// and `valid` are each lane's own pixel; the destination is 16-byte aligned.  Every lane of the
+// warp takes part.
+__device__ __forceinline__ void warp_store16(void *y, bool split, int64_t y_pix, int64_t off, bool valid,
+                                             const float (&v)[16], uint4 *stg, int lane) {
+    uint4 q[4];
+    if (split) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) t[j] = v[j];
+        split8(t, q[0], q[2]);
+#pragma unroll
+        for (int j = 0; j < 8; j++) t[j] = v[8 + j];
+        split8(t, q[1], q[3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            q[i] = make_uint4(__float_as_uint(v[4 * i]), __float_as_uint(v[4 * i + 1]), __float_as_uint(v[4 * i + 2]),
+                              __float_as_uint(v[4 * i + 3]));
+    }
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int i = 0; i < 4; i++) stg[lane * 4 + (i ^ sw)] = q[i];
+    __syncwarp();
+    const int pc = lane & 3;
+    // piece pc of a pixel: element offset from its channel 0 (bf16 or fp32 elements)
+    const int64_t poff = split ? (int64_t)(pc & 1) * 8 + (pc >> 1) * (y_pix / 2) : (int64_t)pc * 4;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int P = 8 * k + (lane >> 2);
+        const int64_t o = __shfl_sync(0xffffffffu, off, P);
+        const bool vv = __shfl_sync(0xffffffffu, (int)valid, P) != 0;
+        const uint4 val = stg[P * 4 + (pc ^ ((P >> 1) & 3))];
+        if (vv) {
+            if (split) *reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(y) + o + poff) = val;
+            else *reinterpret_cast<uint4 *>(reinterpret_cast<float *>(y) + o + poff) = val;
+        }
+    }
+    __syncwarp();
+}
+
 // K-major operand tile with rows of `row_bytes` (32, 64 or 128) in the matching TMA swizzle:
 // 8-row atoms of 8 * row_bytes bytes (the stride byte offset), layout codes 6 / 4 / 2.
 __device__ __forceinline__ uint64_t smem_desc_sw(uint32_t addr, int row_bytes) {
