@@ -141,6 +141,64 @@ __global__ void k_mask_up(const float *__restrict__ m, int stride, int64_t plane
     if (lane < nw) out[(int64_t)oy * words + wx0 + lane] = mine;
 }
 
+// k_mask_up for pages up to kMaskCols (3072) wide, a block per kMaskBlockRows page rows of a page.
+// Shared memory holds each page column's (x1, fx) (once per block) and the horizontally
+// interpolated top and bottom map rows of the current output row (recomputed only when the
+// output row reads another pair of map rows, about every h / vh rows); per pixel that leaves two
+// shared loads, one blend, a compare and a ballot.  Same arithmetic, in the same order, as
+// k_mask_up.
+constexpr int kMaskCols = 3072, kMaskBlockRows = 16;  // 43 KB of static shared memory
+
+__global__ void __launch_bounds__(256) k_mask_up_rows(const float *__restrict__ m, int stride, int64_t plane, int vw,
+                                                      int vh, int w, int h, int words, float sx, float sy, float thr,
+                                                      uint32_t *__restrict__ bits) {
+    __shared__ uint16_t xs1[kMaskCols];  // the map is narrower than 65536 columns (checked on the host)
+    __shared__ float xfx[kMaskCols], top[kMaskCols], bot[kMaskCols];
+    const int page = blockIdx.z;
+    const float *mp = m + page * plane;
+    uint32_t *out = bits + (int64_t)page * words * h;
+    const int oy0 = blockIdx.x * kMaskBlockRows, oy1 = min(oy0 + kMaskBlockRows, h);
+    for (int ox = threadIdx.x; ox < w; ox += blockDim.x) {
+        const float ix = fminf(fmaxf(sx * ((float)ox + 0.5f) - 0.5f, 0.f), (float)vw - 1.f);
+        const int x1 = (int)ix;
+        xs1[ox] = (uint16_t)x1;
+        xfx[ox] = ix - (float)x1;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    int cy = -1;
+    for (int oy = oy0; oy < oy1; oy++) {
+        const float iy = fminf(fmaxf(sy * ((float)oy + 0.5f) - 0.5f, 0.f), (float)vh - 1.f);
+        const int y1 = (int)iy;
+        const float fy = iy - (float)y1;
+        if (y1 != cy) {
+            __syncthreads();  // the column table is written; the previous rows' readers are done
+            cy = y1;
+            const int y2 = min(y1 + 1, vh - 1);
+            const float *r1 = mp + (int64_t)y1 * stride, *r2 = mp + (int64_t)y2 * stride;
+            for (int ox = threadIdx.x; ox < w; ox += blockDim.x) {
+                const int x1 = xs1[ox], x2 = min(x1 + 1, vw - 1);
+                const float fx = xfx[ox];
+                top[ox] = mixf(r1[x1], r1[x2], fx);
+                bot[ox] = mixf(r2[x1], r2[x2], fx);
+            }
+            __syncthreads();
+        }
+        // warp k takes words k, k + nwarps, ...: lane b thresholds pixel 32 word + b
+        for (int wd0 = warp * 32; wd0 < words; wd0 += nwarps * 32) {
+            uint32_t mine = 0;
+            const int nw = min(32, words - wd0);
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const int ox = (wd0 + j) * 32 + lane;
+                const bool on = j < nw && ox < w && mixf(top[ox < w ? ox : 0], bot[ox < w ? ox : 0], fy) > thr;
+                const uint32_t word = __ballot_sync(0xffffffffu, on);
+                mine = lane == j ? word : mine;
+            }
+            if (lane < nw) out[(int64_t)oy * words + wd0 + lane] = mine;
+        }
+    }
+}
+
 __global__ void k_det_prep(const uint8_t *__restrict__ rgb, int w, int h, int ow, int oh, float sx, float sy,
                            int nchw, float *__restrict__ y) {
     const float mean[3] = {0.485f, 0.456f, 0.406f};
@@ -649,6 +707,13 @@ void mask_up(Ctx *c, const float *m, int stride, int64_t plane, int n, int vw, i
     int warps = (words + 31) / 32;
     // one block per page row: exactly the row's warps (3 for a 2550-pixel page), so no idle warps
     // hold block slots
+    if (w <= kMaskCols && vw < 65536) {
+        dim3 grid((unsigned)((h + kMaskBlockRows - 1) / kMaskBlockRows), 1, n);
+        k_mask_up_rows<<<grid, 256, 0, c->stream>>>(m, stride, plane, vw, vh, w, h, words, (float)vw / (float)w,
+                                                    (float)vh / (float)h, thr, bits);
+        WOCR_LAUNCHED(c);
+        return;
+    }
     const int per_block = std::min(warps, 32);
     dim3 grid((warps + per_block - 1) / per_block, h, n);
     k_mask_up<<<grid, per_block * 32, 0, c->stream>>>(m, stride, plane, vw, vh, w, h, words, (float)vw / (float)w,
