@@ -165,6 +165,8 @@ void attach_tconv(Ctx *c, ConvTW &t, const HostW &w) {
                     nk[(size_t)((ky * s + kx) * t.cout + co) * t.cin + ci] =
                         w.data[(((size_t)ci * t.cout + co) * t.kh + ky) * t.kw + kx];
     t.tw = std::make_shared<k::TconvW>(k::make_tconv_weights(c, nk, N, 1, t.cin));
+    // the narrow 2 x 2 ones also on the row kernel (taps stacked along N)
+    if (s == 2 && t.cout <= 32 && t.cin <= 64) k::add_convt_rows(c, *t.tw, nk, t.cout, t.cin);
 }
 
 // =========================================================================================

@@ -77,6 +77,7 @@ struct TcP {
     float *head_y;
     int64_t head_y_n, head_y_pix;
     uint32_t head_off;
+    int tile_w;                 // row kernel: output columns a tile advances (RV, or RP for the ConvTranspose)
     int *status;
 };
 
@@ -674,7 +675,7 @@ __device__ __forceinline__ Tile decode_rows(const TcP &p, int t) {
     Tile r;
     const uint32_t q1 = p.div_tx.div((uint32_t)t), q2 = p.div_ty.div(q1);
     r.nt = 0;
-    r.ox0 = (t - (int)(q1 * p.div_tx.d)) * RV;
+    r.ox0 = (t - (int)(q1 * p.div_tx.d)) * p.tile_w;
     r.oy0 = (int)(q1 - q2 * p.div_ty.d) * RX;
     r.nb = (int)q2;
     return r;
@@ -735,16 +736,22 @@ __device__ __forceinline__ void pool_rows(const TcP &p, const float (&v)[16], in
     }
 }
 
-template <int C, int CG, bool LO, bool WHOLE>
+// CT: the ConvTranspose with kernel == stride 2 instead, a 1 x 1 GEMM whose four taps (ky, kx)
+// are stacked along N the way the kernel columns are (B rows v 4 C + (2 ky + kx) C + c): no halo
+// (tiles of 8 rows x 16 pixels, all output), one MMA pair (or triple) per 16-channel step, and an
+// epilogue that writes each tap's channels to output pixel (2 y + ky, 2 x + kx).
+template <int C, int CG, bool LO, bool WHOLE, bool CT>
 __global__ void __launch_bounds__(kRThreads, 1)
     k_tconv_rows(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo,
                  const uint16_t *__restrict__ wx, TcP p) {
     constexpr int NPL = CG / 8;                 // 8-channel planes per split part
-    constexpr int NB = 6 * C;                   // B rows
-    constexpr int TCOLS = LO ? 6 * C : 3 * C;   // accumulator columns of a tile
+    constexpr int T = CT ? 4 : 3;               // kernel columns (or taps) stacked along N
+    constexpr int DY = CT ? 1 : 3;              // kernel rows (MMA blocks shifted by a halo row)
+    constexpr int NB = 2 * T * C;               // B rows
+    constexpr int TCOLS = LO ? 2 * T * C : T * C;  // accumulator columns of a tile
     constexpr int NACC = 512 / TCOLS < 8 ? 512 / TCOLS : 8;
     constexpr uint32_t kCols = NACC * TCOLS <= 128 ? 128 : (NACC * TCOLS <= 256 ? 256 : 512);
-    constexpr uint32_t B_BYTES = 3u * NPL * NB * 16;
+    constexpr uint32_t B_BYTES = (uint32_t)DY * NPL * NB * 16;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int SA = p.SA;
@@ -828,7 +835,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
     } else if (warp == kRMmaW) {
         // ---------------- MMA issue ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc_w = instr_desc(NB), idesc_3 = instr_desc(3 * C);
+            constexpr uint32_t idesc_w = instr_desc(NB), idesc_3 = instr_desc(T * C);
             constexpr int ROWB = WHOLE ? 4 * CG : 2 * CG;  // bytes of a halo pixel row
             // the lo part: CG elements along the row, or half a stage further
             const uint32_t lo16 = WHOLE ? CG / 8 : p.a_stage >> 5;
@@ -844,7 +851,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
                 const uint64_t da0 = smem_desc_sw(smem_u32(smem + (uint32_t)sa * p.a_stage), ROWB);
                 const uint32_t d = tmem + ab * TCOLS;
 #pragma unroll
-                for (int dy = 0; dy < 3; dy++)
+                for (int dy = 0; dy < DY; dy++)
 #pragma unroll
                     for (int kk = 0; kk < CG / 16; kk++) {
                         // kernel row dy: RP pixel rows further; 16 channels: 32 bytes
@@ -856,7 +863,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
                             umma(d, da + lo16, db, idesc_3, 1u);               // lo . hi
                         } else {
                             umma(d, da, db, idesc_3, acc);                     // hi . hi
-                            umma(d, da, db + 3 * C, idesc_3, 1u);              // hi . lo
+                            umma(d, da, db + T * C, idesc_3, 1u);              // hi . lo
                             umma(d, da + lo16, db, idesc_3, 1u);               // lo . hi
                         }
                     }
@@ -885,6 +892,37 @@ __global__ void __launch_bounds__(kRThreads, 1)
             // the tile's MMAs are complete: its halo stage may be refilled
             if (q == 0 && lane == 0) mbar_arrive(&emptyA[lt % SA]);
             const Tile tl = decode_rows(p, t);
+            if constexpr (CT) {
+                // ConvTranspose: tap tp = 2 ky + kx of input pixel (iy, ix) is output (2 iy + ky, 2 ix + kx)
+                const int iy = tl.oy0 + r, ix = tl.ox0 + j;
+                const bool in_ok = iy < p.oh && ix < p.ow;
+#pragma unroll 1
+                for (int tp = 0; tp < 4; tp++)
+#pragma unroll 1
+                    for (int c0 = 0; c0 < C; c0 += 16) {
+                        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + tp * C + c0;
+                        float v[16];
+                        if (LO) tmem_ld16_sum2(tb, tb + T * C, v);  // hi + lo columns
+                        else tmem_ld16(tb, v);
+                        if (c0 >= p.scat_cout) continue;  // padding columns
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[c0 + jj];
+                        act16(v, p.act);
+                        const int yy = 2 * iy + (tp >> 1), xx = 2 * ix + (tp & 1);
+                        const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + c0;
+                        if (p.stg_off && c0 + 16 <= p.scat_cout) {
+                            store16_t(p, off, in_ok, v, stg, lane);
+                        } else if (in_ok) {
+#pragma unroll
+                            for (int jj = 0; jj < 16; jj++)
+                                if (c0 + jj < p.scat_cout) store1(p, off + jj, v[jj]);
+                        }
+                    }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[ab]);
+                continue;
+            }
             const int oy = tl.oy0 + r, ox = tl.ox0 + j;
             const bool valid = j < RV && oy < p.oh && ox < p.ow;
             float hacc[4];
@@ -1015,42 +1053,53 @@ void launch_taps(Ctx *c, const TconvW &w, const TcP &p, int smem, int kh, int kw
 
 int tconv_bn(int N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128; }
 
-template <int C, int CG, bool WHOLE>
+template <int C, int CG, bool WHOLE, bool CT>
 void launch_rows(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm) {
-    constexpr bool LO = C == 16;  // 2 MMAs over 6 C columns; C = 32: 3 MMAs over 3 C columns
+    constexpr bool LO = C == 16;  // 2 MMAs over 2 T C columns; C = 32: 3 MMAs over T C columns
     static bool set[64] = {false};
     if (!set[c->device]) {
-        WOCR_CUDA(cudaFuncSetAttribute(k_tconv_rows<C, CG, LO, WHOLE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       227 * 1024));
+        WOCR_CUDA(cudaFuncSetAttribute(k_tconv_rows<C, CG, LO, WHOLE, CT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         set[c->device] = true;
     }
     unsigned grid = (unsigned)std::min<int64_t>(p.ntiles, c->sm_count);
-    k_tconv_rows<C, CG, LO, WHOLE><<<grid, kRThreads, smem, c->stream>>>(
+    k_tconv_rows<C, CG, LO, WHOLE, CT><<<grid, kRThreads, smem, c->stream>>>(
         xm[0], xm[1], reinterpret_cast<const uint16_t *>(w.x3->p), p);
     WOCR_LAUNCHED(c);
 }
 
-void launch_rows_any(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm, bool whole) {
+template <bool CT>
+void launch_rows_ct(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm, bool whole) {
     if (w.x3_cout == 16) {
-        if (w.x3_cg == 16) whole ? launch_rows<16, 16, true>(c, w, p, smem, xm) : launch_rows<16, 16, false>(c, w, p, smem, xm);
-        else if (w.x3_cg == 32) whole ? launch_rows<16, 32, true>(c, w, p, smem, xm) : launch_rows<16, 32, false>(c, w, p, smem, xm);
-        else launch_rows<16, 64, false>(c, w, p, smem, xm);
+        if (w.x3_cg == 16)
+            whole ? launch_rows<16, 16, true, CT>(c, w, p, smem, xm) : launch_rows<16, 16, false, CT>(c, w, p, smem, xm);
+        else if (w.x3_cg == 32)
+            whole ? launch_rows<16, 32, true, CT>(c, w, p, smem, xm) : launch_rows<16, 32, false, CT>(c, w, p, smem, xm);
+        else launch_rows<16, 64, false, CT>(c, w, p, smem, xm);
     } else {
-        if (w.x3_cg == 16) whole ? launch_rows<32, 16, true>(c, w, p, smem, xm) : launch_rows<32, 16, false>(c, w, p, smem, xm);
-        else if (w.x3_cg == 32) whole ? launch_rows<32, 32, true>(c, w, p, smem, xm) : launch_rows<32, 32, false>(c, w, p, smem, xm);
-        else launch_rows<32, 64, false>(c, w, p, smem, xm);
+        if (w.x3_cg == 16)
+            whole ? launch_rows<32, 16, true, CT>(c, w, p, smem, xm) : launch_rows<32, 16, false, CT>(c, w, p, smem, xm);
+        else if (w.x3_cg == 32)
+            whole ? launch_rows<32, 32, true, CT>(c, w, p, smem, xm) : launch_rows<32, 32, false, CT>(c, w, p, smem, xm);
+        else launch_rows<32, 64, false, CT>(c, w, p, smem, xm);
     }
+}
+
+void launch_rows_any(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm, bool whole) {
+    if (w.x3_ct) launch_rows_ct<true>(c, w, p, smem, xm, whole);
+    else launch_rows_ct<false>(c, w, p, smem, xm, whole);
 }
 
 // The row kernel's shared memory: A stages, B, barriers, bias, head, store staging (p.out_vec and
 // p.bias_n set); false when it does not fit.
 bool plan_rows_smem(const TconvW &w, TcP &p, int &smem) {
     const int C = w.x3_cout, CG = w.x3_cg;
+    const int T = w.x3_ct ? 4 : 3, DY = w.x3_ct ? 1 : 3, HR = w.x3_ct ? RX : RX + 2;
     p.hw_w = RP;
-    p.halo_px = (RX + 2) * RP;
+    p.halo_px = HR * RP;
     p.plane = 0;
     p.a_stage = (uint32_t)(2 * p.halo_px * CG * 2);  // hi part, lo part: multiples of 1024 bytes
-    const int b_region = (3 * (CG / 8) * 6 * C * 16 + 1023) / 1024 * 1024;
+    const int b_region = (DY * (CG / 8) * 2 * T * C * 16 + 1023) / 1024 * 1024;
     // transposed-store staging: 2 KB per epilogue warp when the stores are 16-byte aligned
     const int stg = p.out_vec ? kRGroups * 4 * 2048 : 0;
     const int SA = std::min(8, (kSmemBudget - b_region - stg) / (int)p.a_stage);
@@ -1071,9 +1120,10 @@ bool plan_rows_smem(const TconvW &w, TcP &p, int &smem) {
 // The row kernel's launch parameters (geometry, tensor maps of the halo, shared memory); false
 // when it does not fit.
 bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap *xm, bool &whole) {
-    const int CG = w.x3_cg;
+    const int CG = w.x3_cg, HR = w.x3_ct ? RX : RX + 2;
     p.trows = RX;
-    p.tiles_x = (q.ow + RV - 1) / RV;
+    p.tile_w = w.x3_ct ? RP : RV;  // a ConvTranspose tile has no halo: all 16 positions are output
+    p.tiles_x = (q.ow + p.tile_w - 1) / p.tile_w;
     p.tiles_y = (q.oh + RX - 1) / RX;
     p.ntn = 1;
     const int64_t ntiles = (int64_t)q.n * p.tiles_x * p.tiles_y;
@@ -1086,12 +1136,12 @@ bool plan_rows(const TconvW &w, const TconvP &q, TcP &p, int &smem, CUtensorMap 
     // the halo boxes: [n][h][w][channels < cin] of the hi and of the lo parts, zeros outside
     const cuuint64_t dims[4] = {(cuuint64_t)q.cin, (cuuint64_t)q.w, (cuuint64_t)q.h, (cuuint64_t)q.n};
     const cuuint64_t strides[3] = {(cuuint64_t)q.x_pix * 2, (cuuint64_t)q.w * q.x_pix * 2, (cuuint64_t)q.x_n * 2};
-    const cuuint32_t box[4] = {(cuuint32_t)CG, (cuuint32_t)RP, (cuuint32_t)(RX + 2), 1};
+    const cuuint32_t box[4] = {(cuuint32_t)CG, (cuuint32_t)RP, (cuuint32_t)HR, 1};
     whole = CG <= 32 && q.cin == CG && q.x_pix == 2 * CG;
     if (whole) {
         // whole pixels: [n][h][w][2 CG] (the hi and the lo parts), rows of 4 CG bytes
         const cuuint64_t dw[4] = {(cuuint64_t)q.x_pix, (cuuint64_t)q.w, (cuuint64_t)q.h, (cuuint64_t)q.n};
-        const cuuint32_t bw[4] = {(cuuint32_t)(2 * CG), (cuuint32_t)RP, (cuuint32_t)(RX + 2), 1};
+        const cuuint32_t bw[4] = {(cuuint32_t)(2 * CG), (cuuint32_t)RP, (cuuint32_t)HR, 1};
         encode(&xm[0], 4, const_cast<uint16_t *>(q.x), dw, strides, bw, 2 * CG);
         xm[1] = xm[0];
     } else {
@@ -1163,13 +1213,43 @@ TconvW make_tconv_weights(Ctx *c, const std::vector<float> &wnk, int N, int taps
     return w;
 }
 
+void add_convt_rows(Ctx *c, TconvW &w, const std::vector<float> &nk, int cout, int cin) {
+    if (cout > 32 || cin > 64 || w.taps != 1 || w.N != 4 * cout) return;
+    // [8-channel plane][v 4 C + tap C + n][8], zeros past cout and cin, copied verbatim into
+    // shared memory by the row kernel
+    const int C = cout <= 16 ? 16 : 32, CG = cin <= 16 ? 16 : (cin <= 32 ? 32 : 64), NPL = CG / 8, NB = 8 * C;
+    std::vector<__nv_bfloat16> b((size_t)NPL * NB * 8, __float2bfloat16_rn(0.f));
+    for (int tap = 0; tap < 4; tap++)
+        for (int n = 0; n < cout; n++)
+            for (int ci = 0; ci < cin; ci++) {
+                const float v = nk[(size_t)(tap * cout + n) * cin + ci];
+                const __nv_bfloat16 h = __float2bfloat16_rn(v);
+                const size_t o = ((size_t)(ci / 8) * NB + tap * C + n) * 8 + ci % 8;
+                b[o] = h;
+                b[o + (size_t)4 * C * 8] = __float2bfloat16_rn(v - __bfloat162float(h));
+            }
+    w.x3 = alloc(c, b.size() * 2);
+    WOCR_CUDA(cudaMemcpyAsync(w.x3->p, b.data(), b.size() * 2, cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    w.x3_cout = C;
+    w.x3_cg = CG;
+    w.x3_ct = 1;
+}
+
 bool tconv_input_ok(const uint16_t *x, int64_t x_n, int64_t x_pix) {
     // 16-byte copies: base, lo part and pixel / image strides 16-byte aligned
     return (reinterpret_cast<uintptr_t>(x) & 15) == 0 && x_pix % 16 == 0 && x_n % 8 == 0;
 }
 
+// the row kernel's operand fits this launch: a 3 x 3 convolution, or the 2 x 2 / s2 ConvTranspose
+static bool rows_kind_ok(const TconvW &w, const TconvP &q) {
+    if (!w.x3 || std::getenv("WOCR_NO_ROWS")) return false;
+    return w.x3_ct ? q.scatter == 2 && q.kh == 1 && q.kw == 1 && q.scat_cout == w.N / 4
+                   : q.kh == 3 && q.kw == 3 && !q.scatter;
+}
+
 bool tconv_rows_eligible(const TconvW &w, const TconvP &q) {
-    if (!w.x3 || q.kh != 3 || q.kw != 3 || q.scatter || std::getenv("WOCR_NO_ROWS")) return false;
+    if (!rows_kind_ok(w, q)) return false;
     if ((int64_t)q.n * ((q.ow + RV - 1) / RV) * ((q.oh + RX - 1) / RX) >= (int64_t)INT32_MAX) return false;
     TcP p{};
     const bool al = (reinterpret_cast<uintptr_t>(q.y) & 15) == 0;
@@ -1241,14 +1321,14 @@ void tconv(Ctx *c, const TconvW &w, const TconvP &q) {
     const double flops = 2.0 * (double)M * w.N * w.taps * w.cin;
     const double bytes = 4.0 * ((double)q.n * q.h * q.w * q.cin + (double)M * w.N) + 4.0 * (double)w.N * w.taps * w.cin;
     if (q.head_y && !tconv_rows_eligible(w, q)) fail(WOCR_ERR_UNSUPPORTED, "fused head without the row kernel");
-    // the narrow 3 x 3 layers: kernel columns stacked along N (k_tconv_rows)
-    if (w.x3 && q.kh == 3 && q.kw == 3 && !q.scatter && !std::getenv("WOCR_NO_ROWS")) {
+    // the narrow 3 x 3 layers and 2 x 2 ConvTransposes: taps stacked along N (k_tconv_rows)
+    if (rows_kind_ok(w, q)) {
         TcP pr = p;
         int smem = 0;
         CUtensorMap xm[2];
         bool whole = false;
         if (plan_rows(w, q, pr, smem, xm, whole)) {
-            Prof pf(c, "tconv", flops, bytes);
+            Prof pf(c, q.scatter ? "tconv_convt" : "tconv", flops, bytes);
             launch_rows_any(c, w, pr, smem, xm, whole);
             c->flops += flops;
             return;

@@ -20,7 +20,14 @@ struct TconvW {
     // v 3 x3_cout + kx x3_cout + n holding the hi (v = 0) or lo (v = 1) part of w[n][dy][kx]
     BufP x3;
     int x3_cout = 0, x3_cg = 0;
+    // x3_ct: the operand is that of a 2 x 2 / stride 2 ConvTranspose instead (taps 2 ky + kx
+    // stacked along N the same way: row v 4 x3_cout + tap x3_cout + n, one plane set)
+    int x3_ct = 0;
 };
+
+// The row kernel's operand of a 2 x 2 / stride 2 ConvTranspose (cout <= 32, cin <= 64) added to
+// its tap-convolution weights; nk: [tap * cout + co][cin] (tap = 2 ky + kx).
+void add_convt_rows(Ctx *c, TconvW &w, const std::vector<float> &nk, int cout, int cin);
 
 // wnk: [N][taps][cin] fp32 (taps in (ky, kx) order).
 TconvW make_tconv_weights(Ctx *c, const std::vector<float> &wnk, int N, int taps, int cin);
