@@ -222,6 +222,17 @@ int32_t wocr_det_input(wocr_ctx *ctx, const uint8_t *rgb, int32_t w, int32_t h, 
 int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side,
                         float *prob, int64_t prob_cap, int32_t *ow, int32_t *oh, float *to_page);
 
+/* DB post-processing on the device (src/ppdet.rs:63-92), on the probability map of the last
+ * wocr_ppdet_page call of the handle (which may then pass prob = NULL):
+ *   wocr_ppdet_mask:   the map thresholded (p > thresh, as `boxes` builds its mask) into
+ *                      [oh][ceil(ow / 32)] words, bit b of word j = pixel 32 j + b;
+ *   wocr_ppdet_scores: `score` of each box rects[6 k .. 6 k + 5] = center x, center y, up axis x,
+ *                      up axis y, width, height (map coordinates): the mean probability of the
+ *                      pixels inside it, summed in the reference's order (bit-exact f32).
+ * The contour search between the two stays on the host, as in the reference. */
+int32_t wocr_ppdet_mask(wocr_ndgraph *g, float thresh, uint32_t *mask, int64_t cap, int32_t *ow, int32_t *oh);
+int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float *scores);
+
 /* Algorithmic work of the last run of a graph handle (detector, recogniser or N-D graph):
  * floating-point operations of its convolutions and matrix products (2 per multiply-add)
  * and the launch count. */

@@ -560,3 +560,45 @@ int oracle_pp_line(const uint8_t *rgb, int w, int h, const float *rect, float *o
     free(wy);
     return ow;
 }
+
+/*
+ * DB box score (src/ppdet.rs:63-83): the mean of the probabilities (map `prob`, w x h) of the
+ * pixels inside the rotated box rect = [cx, cy, up_x, up_y, width, height]:
+ * |dx up_x + dy up_y| <= height / 2 and |dx (-up_y) + dy up_x| <= width / 2, dx = x - cx,
+ * dy = y - cy, summed in f32 row by row.  The scan covers the box's bounding rectangle widened by
+ * a pixel and clamped to the map (the inside test alone decides which pixels count).  0 when no
+ * pixel is inside.
+ */
+/* Rust's `f32 as usize`: saturating, NaN to 0 */
+static long db_idx(float v) { return v > 0.f ? (v < 4e9f ? (long)v : 4000000000L) : 0; }
+
+float oracle_db_score(const float *prob, int w, int h, const float *r) {
+    float cx = r[0], cy = r[1], ux = r[2], uy = r[3], hw = r[4] / 2.0f, hh = r[5] / 2.0f;
+    float lo_x = INFINITY, hi_x = -INFINITY, lo_y = INFINITY, hi_y = -INFINITY;
+    for (int sa = -1; sa <= 1; sa += 2)
+        for (int sb = -1; sb <= 1; sb += 2) {
+            float px = cx + sa * hh * ux + sb * hw * -uy;
+            float py = cy + sa * hh * uy + sb * hw * ux;
+            lo_x = px < lo_x ? px : lo_x;
+            hi_x = px > hi_x ? px : hi_x;
+            lo_y = py < lo_y ? py : lo_y;
+            hi_y = py > hi_y ? py : hi_y;
+        }
+    float fx0 = floorf(lo_x) - 1.f, fy0 = floorf(lo_y) - 1.f, fx1 = ceilf(hi_x) + 1.f, fy1 = ceilf(hi_y) + 1.f;
+    long x0 = db_idx(fx0), y0 = db_idx(fy0), x1 = db_idx(fx1), y1 = db_idx(fy1);
+    if (x1 > w - 1) x1 = w - 1;
+    if (y1 > h - 1) y1 = h - 1;
+    float sum = 0.f;
+    long n = 0;
+    for (long y = y0; y <= y1; y++)
+        for (long x = x0; x <= x1; x++) {
+            float dx = (float)x - cx, dy = (float)y - cy;
+            float along = dx * ux + dy * uy;
+            float across = dx * -uy + dy * ux;
+            if (fabsf(along) <= hh && fabsf(across) <= hw) {
+                sum = sum + prob[y * w + x];
+                n++;
+            }
+        }
+    return n == 0 ? 0.f : sum / (float)n;
+}

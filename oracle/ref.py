@@ -68,11 +68,12 @@ def lib():
             "oracle_erf": [_F],
             "oracle_act": [_F, _I],
             "oracle_pp_line": [_u8, _I, _I, _f, _f],
+            "oracle_db_score": [_f, _I, _I, _f],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_float if name in ("oracle_erf", "oracle_act") else (
+            fn.restype = ctypes.c_float if name in ("oracle_erf", "oracle_act", "oracle_db_score") else (
                 ctypes.c_int if name in ("oracle_threads", "oracle_pp_line") else None)
         _lib = L
     return _lib
@@ -133,6 +134,18 @@ def pool(x, kh, kw, sh, sw, pads=(0, 0, 0, 0), avg=False):
     y = np.empty((n, c, oh, ow), np.float32)
     lib().oracle_pool(_p(x), n * c, h, w, oh, ow, kh, kw, sh, sw, pt, pl, int(avg), _p(y))
     return y
+
+
+def db_scores(prob: np.ndarray, rects) -> np.ndarray:
+    """`score` of src/ppdet.rs:63-83 for each box [cx, cy, up_x, up_y, width, height] of a
+    probability map [h, w]."""
+    prob = np.ascontiguousarray(prob, np.float32)
+    h, w = prob.shape
+    out = []
+    for r in np.asarray(rects, np.float32).reshape(-1, 6):
+        rr = np.ascontiguousarray(r)
+        out.append(lib().oracle_db_score(_p(prob), w, h, _p(rr)))
+    return np.array(out, np.float32)
 
 
 def pp_line(rgb: np.ndarray, rect) -> np.ndarray:

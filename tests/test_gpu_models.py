@@ -164,6 +164,45 @@ def test_pp_detection(gpu):
     assert np.abs(prob - want).max() < 1e-4
 
 
+def _db_rects(rng, w, h, n):
+    """Rotated boxes [cx, cy, up_x, up_y, width, height] over a w x h map: random ones, boxes on
+    and past every edge, an empty one, a tiny one, a NaN one and one larger than the map."""
+    ang = rng.uniform(-0.5, 0.5, n).astype(np.float32)
+    r = np.stack([rng.uniform(0, w, n), rng.uniform(0, h, n), np.sin(ang), -np.cos(ang),
+                  rng.uniform(2, 200, n), rng.uniform(2, 40, n)], 1).astype(np.float32)
+    edge = [[0, 0, 0, -1, 30, 12], [w - 1, h - 1, 0, -1, 40, 9], [w + 30, h / 2, 0, -1, 20, 20],
+            [w / 2, -5, 0.6, -0.8, 50, 15], [w / 2, h / 2, 0, -1, 0, 0], [7.3, 9.6, 0.7071, -0.7071, 1, 1],
+            [float("nan"), 4, 0, -1, 5, 5], [w / 2, h / 2, 0, -1, 1e7, 1e7]]
+    return np.concatenate([r, np.float32(edge)])
+
+
+def test_pp_db_mask_and_scores(gpu):
+    """DB post-processing on the device-resident map (src/ppdet.rs:63-92): the threshold bit mask
+    equals `prob > thresh` and every box score equals the CPU restatement to the bit, after the
+    first call and after a graph replay with another page."""
+    m = synth.pp_det_model()
+    rng = np.random.default_rng(11)
+    g = wocr.NdGraph(gpu, m)
+    try:
+        for seed in (3, 4):
+            page = synth.page(seed, 1275, 1650)
+            prob, _ = g.ppdet_page(page, 1275, 1650, 960)
+            h, w = prob.shape
+            for thr in (0.2, float(np.median(prob))):
+                bits = g.db_mask(thr)
+                assert bits.shape == (h, (w + 31) // 32)
+                on = np.zeros((h, bits.shape[1] * 32), bool)
+                on[:, :w] = prob > np.float32(thr)
+                want = np.packbits(on.reshape(h, -1, 32), axis=2, bitorder="little").view("<u4")[..., 0]
+                np.testing.assert_array_equal(bits, want)
+            rects = _db_rects(rng, w, h, 300)
+            got = g.db_scores(rects)
+            np.testing.assert_array_equal(got, ref.db_scores(prob, rects))
+            assert len(g.db_scores(np.zeros((0, 6), np.float32))) == 0
+    finally:
+        g.close()
+
+
 def test_ndgraph_replay(gpu, pp_model, monkeypatch):
     """NdGraph calls of a known shape replay a captured CUDA graph (run, arg-max and the PP
     detection page): the results equal direct runs, and new input values are seen."""

@@ -244,3 +244,35 @@ def test_pp_line_oracle_matches_two_pass_restatement(rect):
     px = _tri_resize_np(page[t:t + ch, l:l + cw], ow, 48)
     want = ((px.astype(np.float32) / np.float32(255) - np.float32(0.5)) / np.float32(0.5)).transpose(2, 0, 1)
     np.testing.assert_array_equal(got, want)
+
+
+def _db_score_loops(prob, r):
+    """`score` (src/ppdet.rs:63-83) over every pixel of the map, in f32 scalars: the inside test
+    alone selects, so the scan rectangle of the oracle must cover every pixel that passes."""
+    f = np.float32
+    cx, cy, ux, uy, hw, hh = f(r[0]), f(r[1]), f(r[2]), f(r[3]), f(r[4]) / f(2), f(r[5]) / f(2)
+    s, n = f(0), 0
+    for y in range(prob.shape[0]):
+        dy = f(y) - cy
+        for x in range(prob.shape[1]):
+            dx = f(x) - cx
+            if abs(dx * ux + dy * uy) <= hh and abs(dx * -uy + dy * ux) <= hw:
+                s = f(s + prob[y, x])
+                n += 1
+    return f(0) if n == 0 else f(s / f(n))
+
+
+def test_db_score_oracle_matches_full_scan():
+    """oracle_db_score (a scan of the box's bounding rectangle) equals the sum over the whole map,
+    for rotated, axis-aligned, clamped, off-map, empty and NaN boxes."""
+    rng = np.random.default_rng(3)
+    prob = rng.random((37, 53), dtype=np.float32)
+    a = np.float32(0.3)
+    rects = [[20.5, 14.0, 0, -1, 30, 6], [26.0, 18.0, np.sin(a), -np.cos(a), 25, 9], [1.0, 2.0, 0, -1, 9, 9],
+             [52.0, 36.0, -0.6, -0.8, 12, 7], [80.0, 60.0, 0, -1, 10, 10], [10.0, 10.0, 0, -1, 0, 0],
+             [10.3, 10.6, 0.70710678, -0.70710678, 1.0, 1.0], [float("nan"), 3.0, 0, -1, 4, 4],
+             [26.0, 18.0, 0, -1, 1e9, 1e9]]
+    got = ref.db_scores(prob, rects)
+    want = np.array([_db_score_loops(prob, r) for r in rects], np.float32)
+    np.testing.assert_array_equal(got, want)
+    assert got[4] == 0 and got[7] == 0

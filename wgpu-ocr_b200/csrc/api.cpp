@@ -190,6 +190,10 @@ struct wocr_ndgraph {
     Stats last;
     NdReplay replays[8];
     uint64_t uses = 0;
+    // the probability map of the last wocr_ppdet_page ([map_h][map_w] fp32) for the DB steps
+    BufP map_buf;
+    const float *map = nullptr;
+    int map_w = 0, map_h = 0;
     ~wocr_ndgraph() {
         for (auto &r : replays) r.reset();
     }
@@ -1368,6 +1372,10 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
             k::det_prep(c, (const uint8_t *)src->p, w, h, ow, oh, 0, x.p);
             DT y = to_rowmajor(c, g->graph->run(x));
             if (r) r->out_shape = y.shape;
+            g->map_buf = y.buf;
+            g->map = y.p;
+            g->map_w = (int)y.shape.back();
+            g->map_h = (int)(y.numel() / std::max<int64_t>(y.shape.back(), 1));
             if (prob) {
                 if (prob_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "probability buffer too small");
                 d2h(c, prob, y.p, (size_t)y.numel() * 4);
@@ -1404,10 +1412,79 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
             c->launches = l0;
         }
         nd_replay_launch(g, r, reinterpret_cast<const float *>(rgb));
+        g->map_buf = r->out;
+        g->map = (const float *)r->out->p;
+        g->map_w = (int)r->out_shape.back();
+        g->map_h = (int)(m / std::max<int64_t>(r->out_shape.back(), 1));
         if (prob) {
             if (prob_cap < m) fail(WOCR_ERR_CAPACITY, "probability buffer too small");
             d2h(c, prob, r->out->p, (size_t)m * 4);
         }
+        sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_ppdet_mask(wocr_ndgraph *g, float thresh, uint32_t *mask, int64_t cap, int32_t *ow, int32_t *oh) {
+    return guard([&] {
+        if (!g) fail(WOCR_ERR_INVALID, "null argument");
+        if (!g->map) fail(WOCR_ERR_INVALID, "no probability map: call wocr_ppdet_page first");
+        const int w = g->map_w, h = g->map_h, words = (w + 31) / 32;
+        if (ow) *ow = w;
+        if (oh) *oh = h;
+        if (!mask && cap == 0) return;  // size query
+        if (!mask) fail(WOCR_ERR_INVALID, "null argument");
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        if (cap < (int64_t)words * h) fail(WOCR_ERR_CAPACITY, "mask buffer too small");
+        BufP bits = alloc(c, (size_t)words * h * 4);
+        k::db_mask(c, g->map, w, h, thresh, (uint32_t *)bits->p);
+        d2h(c, mask, bits->p, (size_t)words * h * 4);
+        g->last.d2h += (int64_t)words * h * 4;
+        sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float *scores) {
+    return guard([&] {
+        if (!g || (n > 0 && (!rects || !scores)) || n < 0) fail(WOCR_ERR_INVALID, "bad argument");
+        if (!g->map) fail(WOCR_ERR_INVALID, "no probability map: call wocr_ppdet_page first");
+        if (n == 0) return;
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        const int w = g->map_w, h = g->map_h;
+        // the scan rectangle: the box's bounding rectangle (its four corners), floor / ceil,
+        // clamped to the map as score() clamps it
+        std::vector<k::DbBox> bx((size_t)n);
+        for (int i = 0; i < n; i++) {
+            const float *r = rects + 6 * (size_t)i;
+            k::DbBox &b = bx[i];
+            b.cx = r[0];
+            b.cy = r[1];
+            b.ux = r[2];
+            b.uy = r[3];
+            b.hw = r[4] / 2.0f;
+            b.hh = r[5] / 2.0f;
+            float lo_x = INFINITY, hi_x = -INFINITY, lo_y = INFINITY, hi_y = -INFINITY;
+            for (int sa = -1; sa <= 1; sa += 2)
+                for (int sb = -1; sb <= 1; sb += 2) {
+                    const float px = b.cx + sa * b.hh * b.ux + sb * b.hw * -b.uy;
+                    const float py = b.cy + sa * b.hh * b.uy + sb * b.hw * b.ux;
+                    lo_x = std::min(lo_x, px), hi_x = std::max(hi_x, px);
+                    lo_y = std::min(lo_y, py), hi_y = std::max(hi_y, py);
+                }
+            // one pixel wider on every side than floor / ceil of the corners: the pixels that pass
+            // the inside test lie in the box's bounding rectangle whatever the corner rounding
+            // `as usize`: saturating, NaN to 0
+            auto to_idx = [](float v) -> int64_t { return v > 0.f ? (v < 4e9f ? (int64_t)v : (int64_t)4e9) : 0; };
+            b.x0 = (int)std::min<int64_t>(to_idx(std::floor(lo_x) - 1.f), w);
+            b.y0 = (int)std::min<int64_t>(to_idx(std::floor(lo_y) - 1.f), h);
+            b.x1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_x) + 1.f), std::max(w - 1, 0));
+            b.y1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_y) + 1.f), std::max(h - 1, 0));
+        }
+        BufP db = alloc(c, bx.size() * sizeof(k::DbBox)), ds = alloc(c, (size_t)n * 4);
+        WOCR_CUDA(cudaMemcpyAsync(db->p, bx.data(), bx.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice, c->stream));
+        k::db_scores(c, g->map, w, h, (const k::DbBox *)db->p, n, (float *)ds->p);
+        d2h(c, scores, ds->p, (size_t)n * 4);
         sync_bounded(c, 0);
     });
 }

@@ -1,0 +1,74 @@
+// DB post-processing on the device (src/ppdet.rs:63-92): the detector's probability map
+// thresholded into a bit mask for the host's contour search, and the mean probability inside
+// each box the host found (`score`), so that only the bits and one float per box cross PCIe
+// instead of the probability map.
+#include "kernels.h"
+
+namespace wocr {
+namespace k {
+
+namespace {
+
+// One warp makes 32 consecutive words of a row: lane b thresholds pixel 32 word + b, a ballot
+// forms the word, lane j keeps word j (bit b of word j = pixel 32 j + b).
+__global__ void k_db_mask(const float *__restrict__ prob, int w, int h, int words, float thr,
+                          uint32_t *__restrict__ bits) {
+    const int y = blockIdx.y, lane = threadIdx.x & 31;
+    const int wd0 = (blockIdx.x * blockDim.x + threadIdx.x) / 32 * 32;
+    if (wd0 >= words) return;
+    const float *row = prob + (int64_t)y * w;
+    uint32_t mine = 0;
+    const int nw = min(32, words - wd0);
+    for (int j = 0; j < nw; j++) {
+        const int x = (wd0 + j) * 32 + lane;
+        const uint32_t word = __ballot_sync(0xffffffffu, x < w && row[x] > thr);
+        if (lane == j) mine = word;
+    }
+    if (lane < nw) bits[(int64_t)y * words + wd0 + lane] = mine;
+}
+
+// `score` of src/ppdet.rs:63-83, one thread per box with the reference's order of additions (a
+// sequential f32 sum over the rows, then the columns, of the pixels inside the box), so the
+// result is the reference's to the bit.  The scan covers the box's bounding rectangle clamped to
+// the map; the inside test alone decides which pixels count.
+__global__ void k_db_scores(const float *__restrict__ prob, int w, int h, const DbBox *__restrict__ boxes, int n,
+                            float *__restrict__ scores) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= n) return;
+    const DbBox b = boxes[k];
+    float sum = 0.f;
+    int64_t cnt = 0;
+    for (int y = b.y0; y <= b.y1; y++) {
+        const float dy = __fsub_rn((float)y, b.cy);
+        for (int x = b.x0; x <= b.x1; x++) {
+            const float dx = __fsub_rn((float)x, b.cx);
+            const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
+            const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
+            if (fabsf(along) <= b.hh && fabsf(across) <= b.hw) {
+                sum = __fadd_rn(sum, prob[(int64_t)y * w + x]);
+                cnt++;
+            }
+        }
+    }
+    scores[k] = cnt == 0 ? 0.f : __fdiv_rn(sum, (float)cnt);
+}
+
+}  // namespace
+
+void db_mask(Ctx *c, const float *prob, int w, int h, float thr, uint32_t *bits) {
+    const int words = (w + 31) / 32;
+    Prof pf(c, "db_mask", 0, (double)w * h * 4 + (double)words * h * 4);
+    dim3 grid((unsigned)((((words + 31) / 32) * 32 + 127) / 128), (unsigned)h);
+    k_db_mask<<<grid, 128, 0, c->stream>>>(prob, w, h, words, thr, bits);
+    WOCR_LAUNCHED(c);
+}
+
+void db_scores(Ctx *c, const float *prob, int w, int h, const DbBox *boxes, int n, float *scores) {
+    if (n <= 0) return;
+    Prof pf(c, "db_scores", 0, 0);
+    k_db_scores<<<(n + 63) / 64, 64, 0, c->stream>>>(prob, w, h, boxes, n, scores);
+    WOCR_LAUNCHED(c);
+}
+
+}  // namespace k
+}  // namespace wocr

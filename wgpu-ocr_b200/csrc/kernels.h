@@ -134,6 +134,15 @@ void bmm(Ctx *c, const float *a, const float *bm, float *y, int64_t batch, int m
 // bilinear to oh x ow.  n pages at rgb + i * page_bytes; output [n][oh][ow].
 void grey_resize(Ctx *c, const uint8_t *rgb, int64_t page_bytes, int n, int w, int h, int oh, int ow, float *y);
 
+// DB post-processing (k_db.cu): a box for `score` (src/ppdet.rs:63-83): its center, up axis,
+// half width and half height, and the map rectangle to scan ([x0, x1] x [y0, y1], inclusive).
+struct DbBox {
+    float cx, cy, ux, uy, hw, hh;
+    int x0, y0, x1, y1;
+};
+void db_mask(Ctx *c, const float *prob, int w, int h, float thr, uint32_t *bits);
+void db_scores(Ctx *c, const float *prob, int w, int h, const DbBox *boxes, int n, float *scores);
+
 // One PP-OCR recognition line of a batch (k_lines.cu): the clamped box (left, top, cw x ch), its
 // resized width ow, the batch width (>= ow, zero padding past ow) and the float offset of its
 // [3][48][width] block in the output.

@@ -286,6 +286,23 @@ class NdGraph(_Handle):
                                         ctypes.byref(ow), ctypes.byref(oh), tp))
         return prob, (tp[0], tp[1])
 
+    def db_mask(self, thresh: float) -> np.ndarray:
+        """The last `ppdet_page` map thresholded on the device (`p > thresh`, src/ppdet.rs:89):
+        uint32 [oh, ceil(ow / 32)], bit b of word j = pixel 32 j + b."""
+        ow, oh = ctypes.c_int32(), ctypes.c_int32()
+        L.check(L.lib().wocr_ppdet_mask(self.h, thresh, None, 0, ctypes.byref(ow), ctypes.byref(oh)))
+        bits = np.empty((oh.value, (ow.value + 31) // 32), np.uint32)
+        L.check(L.lib().wocr_ppdet_mask(self.h, thresh, L.ptr(bits), bits.size, ctypes.byref(ow), ctypes.byref(oh)))
+        return bits
+
+    def db_scores(self, rects) -> np.ndarray:
+        """`score` (src/ppdet.rs:63-83) of each box [cx, cy, up_x, up_y, width, height] on the last
+        `ppdet_page` map, computed on the device: float32 [n]."""
+        r = np.ascontiguousarray(np.asarray(rects, np.float32).reshape(-1, 6))
+        out = np.empty(len(r), np.float32)
+        L.check(L.lib().wocr_ppdet_scores(self.h, L.ptr(r), len(r), L.ptr(out)))
+        return out
+
     @staticmethod
     def det_input(gpu: Gpu, rgb: np.ndarray, w: int, h: int, max_side: int):
         """NdGraph::det_input (src/nd.rs:1353-1369): ([1, 3, oh, ow] f32, to_page factors)."""
