@@ -47,9 +47,10 @@ def parse():
     p.add_argument("--pages", type=int, default=12, help="pages per GPU per step")
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
-    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "pplines"],
+    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines"],
                    help="det1 (default, the driver's line): config 1 detection; rec0 / pp3 / ppdet4: configs "
-                        "0, 3 and 4 through their public calls (secondary measurements)")
+                        "0, 3 and 4 through their public calls; ppdb4: config 4 with the DB mask and box "
+                        "scores on the device; pplines: PP line extraction (secondary measurements)")
     return p.parse_args()
 
 
@@ -430,6 +431,29 @@ def run_workload(args):
         def cpu():
             ref.pp_batches(pages_np[0], boxes[0])
             return len(boxes[0]), f"{len(boxes[0])} lines (one page)"
+    elif args.workload == "ppdb4":
+        model = synth.pp_det_model()
+        page = synth.page(3, W_PAGE, H_PAGE)
+        handle = wocr.NdGraph(gpu, model)
+        _, tp = handle.ppdet_page(page, W_PAGE, H_PAGE, 960, read_map=False)
+        rects = synth.page_db_candidates(3, W_PAGE, H_PAGE, tp)
+        units, unit, workload = 1, "pages/s", (f"config 4 detection + DB scoring: PP-OCRv6-style DB detector on a "
+                                               f"2550x3300 page resized to 3x960x736, seed 3, the map kept on the "
+                                               f"device, its p > 0.2 bit mask read back and {len(rects)} candidate "
+                                               "boxes (the page's ink rectangles and lines) scored on the device")
+        h2d, d2h = page.nbytes + len(rects) * 40, 960 * (736 // 32) * 4 + len(rects) * 4
+
+        def step():
+            handle.ppdet_page(page, W_PAGE, H_PAGE, 960, read_map=False)
+            handle.db_mask(0.2)
+            handle.db_scores(rects)
+
+        def cpu():
+            x, _ = ref.det_input(page, 960)
+            prob = ref.run_onnx(model, x)[0, 0]
+            np.packbits(prob > np.float32(0.2), axis=1, bitorder="little")
+            ref.db_scores(prob, rects)
+            return 1, "1 page"
     else:
         model = synth.pp_det_model()
         page = synth.page(3, W_PAGE, H_PAGE)

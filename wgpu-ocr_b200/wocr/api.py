@@ -274,16 +274,19 @@ class NdGraph(_Handle):
             shape = tuple(oshape[i] for i in range(orank.value))
             return best[:r], mx[:r], lse[:r], shape
 
-    def ppdet_page(self, rgb: np.ndarray, w: int, h: int, max_side: int):
-        """det_input + run on one page (src/bin/ocr-bench.rs:186-200): (prob [oh, ow], to_page)."""
+    def ppdet_page(self, rgb: np.ndarray, w: int, h: int, max_side: int, read_map: bool = True):
+        """det_input + run on one page (src/bin/ocr-bench.rs:186-200): (prob [oh, ow], to_page).
+        With read_map=False the map stays on the device (for db_mask / db_scores) and prob is None."""
         rgb = np.ascontiguousarray(rgb, np.uint8)
         ow, oh = ctypes.c_int32(), ctypes.c_int32()
         tp = (ctypes.c_float * 2)()
-        L.check(L.lib().wocr_det_input(self.gpu.h, L.ptr(rgb), w, h, max_side, None, 0, ctypes.byref(ow),
-                                       ctypes.byref(oh), tp))
-        prob = np.empty((oh.value, ow.value), np.float32)
-        L.check(L.lib().wocr_ppdet_page(self.h, L.ptr(rgb), w, h, max_side, L.ptr(prob), prob.size,
-                                        ctypes.byref(ow), ctypes.byref(oh), tp))
+        prob = None
+        if read_map:
+            L.check(L.lib().wocr_det_input(self.gpu.h, L.ptr(rgb), w, h, max_side, None, 0, ctypes.byref(ow),
+                                           ctypes.byref(oh), tp))
+            prob = np.empty((oh.value, ow.value), np.float32)
+        L.check(L.lib().wocr_ppdet_page(self.h, L.ptr(rgb), w, h, max_side, L.ptr(prob) if read_map else None,
+                                        prob.size if read_map else 0, ctypes.byref(ow), ctypes.byref(oh), tp))
         return prob, (tp[0], tp[1])
 
     def db_mask(self, thresh: float) -> np.ndarray:

@@ -455,6 +455,19 @@ def page(seed: int = 1, w: int = 2550, h: int = 3300, bands: int = 36, line_h: i
     return img
 
 
+def page_db_candidates(seed: int, w: int, h: int, to_page, bands: int = 36, line_h: int = 40) -> np.ndarray:
+    """DB box candidates of page(seed, ...) in detector-map coordinates, as `score` takes them
+    ([cx, cy, up_x, up_y, width, height], src/ppdet.rs:63): every ink rectangle (a word piece)
+    and every text line, axis-aligned, divided by the map-to-page factors `to_page`."""
+    sx, sy = float(to_page[0]), float(to_page[1])
+    out = []
+    for y0, y1, rects in _page_layout(seed, w, h, bands, line_h):
+        boxes = list(rects) + ([(rects[0][0], rects[-1][1])] if rects else [])
+        for x0, x1 in boxes:
+            out.append([(x0 + x1) / 2 / sx, (y0 + y1) / 2 / sy, 0.0, -1.0, (x1 - x0) / sx, (y1 - y0) / sy])
+    return np.array(out, np.float32).reshape(-1, 6)
+
+
 def page_line_boxes(seed: int = 1, w: int = 2550, h: int = 3300, bands: int = 36, line_h: int = 40,
                     relv: float = 0.1) -> np.ndarray:
     """The text lines of page(seed, ...) as recognition boxes [left, top, right, bottom] (f32):
