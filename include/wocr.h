@@ -233,6 +233,20 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
 int32_t wocr_ppdet_mask(wocr_ndgraph *g, float thresh, uint32_t *mask, int64_t cap, int32_t *ow, int32_t *oh);
 int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float *scores);
 
+/* Word rectangles of binary page masks: `word_rects` (src/bin/ocr-bench.rs:38-60), i.e. the
+ * external contours (find_contours, External), each simplified (Douglas-Peucker, epsilon 2), its
+ * minimum-area rectangle resized to width + 2 (expand + expand_x) x height + 2 expand and kept
+ * when its area >= min_area (the reference: expand 3, expand_x 0, min_area 100).  `mask`: n
+ * pages of h rows x ceil(w / 32) words (bit b of word j = pixel 32 j + b, the layout of
+ * wocr_detect_pages), in host memory, or in device memory when mask_on_device != 0.  counts[n]
+ * gets each page's rectangle count; rects gets [cx, cy, up_x, up_y, width, height] per
+ * rectangle, page after page, each page's in the raster order of its contours' start pixels.
+ * rects = NULL with cap = 0 only counts; a cap below the total fails with WOCR_ERR_CAPACITY
+ * after filling counts. */
+int32_t wocr_word_rects(wocr_ctx *ctx, const uint32_t *mask, int32_t n, int32_t w, int32_t h,
+                        int32_t mask_on_device, float expand, float expand_x, float min_area, float *rects,
+                        int64_t cap, int32_t *counts);
+
 /* Algorithmic work of the last run of a graph handle (detector, recogniser or N-D graph):
  * floating-point operations of its convolutions and matrix products (2 per multiply-add)
  * and the launch count. */

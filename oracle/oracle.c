@@ -602,3 +602,334 @@ float oracle_db_score(const float *prob, int w, int h, const float *r) {
         }
     return n == 0 ? 0.f : sum / (float)n;
 }
+
+/*
+ * Word rectangles of a binary detection mask: `word_rects` of src/bin/ocr-bench.rs:38-60 (ocrs'
+ * find_connected_component_rects with expand 3, min area 100).  Its steps are rten-imageproc
+ * =0.26.0 functions, an un-vendored crates.io dependency, restated here from the published
+ * algorithms they name:
+ *   find_contours(mask, External): Suzuki & Abe 1985, "Topological structural analysis of
+ *     digitized binary images by border following", Algorithm 1 (8-connected foreground, the
+ *     image framed by 0-pixels), keeping the outer borders whose parent is the frame;
+ *   simplify_polygon(points, 2): Douglas-Peucker on the closed polyline (first point repeated at
+ *     the end, dropped again afterwards); point-to-segment distance;
+ *   min_area_rect: the convex hull (Andrew's monotone chain, collinear points dropped), then
+ *     the exhaustive search over hull edges (each edge's direction and its normal, extents of
+ *     the hull's projections, first strict minimum of the area);
+ *   RotatedRect::resize(width + 2 (expand + expand_x), height + 2 expand), kept if area >=
+ *     min_area.
+ * A rectangle is [cx, cy, up_x, up_y, width, height] (the height is measured along up).
+ */
+typedef struct {
+    int *x, *y;
+    int n, cap;
+} wr_pts;
+
+static void wr_push(wr_pts *p, int x, int y) {
+    if (p->n == p->cap) {
+        p->cap = p->cap ? 2 * p->cap : 256;
+        p->x = (int *)realloc(p->x, sizeof(int) * p->cap);
+        p->y = (int *)realloc(p->y, sizeof(int) * p->cap);
+    }
+    p->x[p->n] = x;
+    p->y[p->n] = y;
+    p->n++;
+}
+
+/* 8-neighbourhood in clockwise order on the screen (y down), starting at the left neighbour */
+static const int WR_DX[8] = {-1, -1, 0, 1, 1, 1, 0, -1};
+static const int WR_DY[8] = {0, -1, -1, -1, 0, 1, 1, 1};
+
+static int wr_dir(int dx, int dy) {
+    for (int d = 0; d < 8; d++)
+        if (WR_DX[d] == dx && WR_DY[d] == dy) return d;
+    return -1;
+}
+
+/* Steps (3.1)-(3.5) of Algorithm 1: follow the border through (x, y) of the padded label image
+ * f (row length W), entered from the 0-pixel in direction d2, labelling with nbd.  The border's
+ * points (each (i3, j3) in turn) go to out in padded coordinates. */
+static void wr_follow(int *f, int W, int x, int y, int d2, int nbd, wr_pts *out) {
+    int d1 = -1;
+    for (int k = 0; k < 8; k++) {
+        int d = (d2 + k) & 7;
+        if (f[(y + WR_DY[d]) * W + x + WR_DX[d]] != 0) {
+            d1 = d;
+            break;
+        }
+    }
+    if (d1 < 0) {
+        f[y * W + x] = -nbd;
+        wr_push(out, x, y);
+        return;
+    }
+    int x1 = x + WR_DX[d1], y1 = y + WR_DY[d1];
+    int x2 = x1, y2 = y1, x3 = x, y3 = y;
+    for (;;) {
+        wr_push(out, x3, y3);
+        int e = wr_dir(x2 - x3, y2 - y3), x4 = x3, y4 = y3, right_zero = 0;
+        for (int k = 1; k <= 8; k++) {
+            int d = (e - k) & 7, xx = x3 + WR_DX[d], yy = y3 + WR_DY[d];
+            if (f[yy * W + xx] != 0) {
+                x4 = xx;
+                y4 = yy;
+                break;
+            }
+            if (d == 4) right_zero = 1;
+        }
+        if (right_zero)
+            f[y3 * W + x3] = -nbd;
+        else if (f[y3 * W + x3] == 1)
+            f[y3 * W + x3] = nbd;
+        if (x4 == x && y4 == y && x3 == x1 && y3 == y1) break;
+        x2 = x3;
+        y2 = y3;
+        x3 = x4;
+        y3 = y4;
+    }
+}
+
+/* point-to-segment distance (the comp.graphics.algorithms FAQ 1.02 method) */
+static float wr_seg_dist(float px, float py, float ax, float ay, float bx, float by) {
+    float abx = bx - ax, aby = by - ay, acx = px - ax, acy = py - ay;
+    float l2 = abx * abx + aby * aby;
+    if (l2 == 0.f) return sqrtf(acx * acx + acy * acy);
+    float r = (acx * abx + acy * aby) / l2;
+    if (r <= 0.f) return sqrtf(acx * acx + acy * acy);
+    if (r >= 1.f) {
+        float bcx = px - bx, bcy = py - by;
+        return sqrtf(bcx * bcx + bcy * bcy);
+    }
+    float s = (abx * acy - aby * acx) / l2;
+    return fabsf(s * sqrtf(l2));
+}
+
+/* Douglas-Peucker over points[lo..hi] (inclusive ends kept), recursion by an explicit stack */
+static void wr_dp(const float *px, const float *py, int n, float eps, unsigned char *keep) {
+    int *st = (int *)malloc(sizeof(int) * 2 * (size_t)(n + 1));
+    int sp = 0;
+    keep[0] = keep[n - 1] = 1;
+    st[sp++] = 0;
+    st[sp++] = n - 1;
+    while (sp) {
+        int hi = st[--sp], lo = st[--sp];
+        float best = -1.f;
+        int bi = -1;
+        for (int i = lo + 1; i < hi; i++) {
+            float d = wr_seg_dist(px[i], py[i], px[lo], py[lo], px[hi], py[hi]);
+            if (d > best) {
+                best = d;
+                bi = i;
+            }
+        }
+        if (bi >= 0 && best > eps) {
+            keep[bi] = 1;
+            st[sp++] = lo;
+            st[sp++] = bi;
+            st[sp++] = bi;
+            st[sp++] = hi;
+        }
+    }
+    free(st);
+}
+
+static int wr_cmp(const void *a, const void *b) {
+    const int *p = (const int *)a, *q = (const int *)b;
+    if (p[0] != q[0]) return p[0] < q[0] ? -1 : 1;
+    return p[1] < q[1] ? -1 : p[1] > q[1];
+}
+
+static int64_t wr_cross(const int *o, const int *a, const int *b) {
+    return (int64_t)(a[0] - o[0]) * (b[1] - o[1]) - (int64_t)(a[1] - o[1]) * (b[0] - o[0]);
+}
+
+/* The minimum-area rectangle of integer points xy[n][2] (sorted in place).  Returns 0 when the
+ * points are fewer than two distinct ones. */
+static int wr_min_rect(int *xy, int n, float *rect) {
+    qsort(xy, (size_t)n, sizeof(int) * 2, wr_cmp);
+    int m = 0;
+    for (int i = 0; i < n; i++)
+        if (m == 0 || xy[2 * i] != xy[2 * (m - 1)] || xy[2 * i + 1] != xy[2 * (m - 1) + 1]) {
+            xy[2 * m] = xy[2 * i];
+            xy[2 * m + 1] = xy[2 * i + 1];
+            m++;
+        }
+    if (m < 2) return 0;
+    int *hull = (int *)malloc(sizeof(int) * 2 * (size_t)(2 * m + 1));
+    int k = 0;
+    for (int i = 0; i < m; i++) {
+        while (k >= 2 && wr_cross(hull + 2 * (k - 2), hull + 2 * (k - 1), xy + 2 * i) <= 0) k--;
+        hull[2 * k] = xy[2 * i];
+        hull[2 * k + 1] = xy[2 * i + 1];
+        k++;
+    }
+    for (int i = m - 2, lo = k + 1; i >= 0; i--) {
+        while (k >= lo && wr_cross(hull + 2 * (k - 2), hull + 2 * (k - 1), xy + 2 * i) <= 0) k--;
+        hull[2 * k] = xy[2 * i];
+        hull[2 * k + 1] = xy[2 * i + 1];
+        k++;
+    }
+    int h = k - 1; /* the last point repeats the first */
+    float best = INFINITY;
+    for (int i = 0; i < h; i++) {
+        const int *a = hull + 2 * i, *b = hull + 2 * ((i + 1) % h);
+        float dx = (float)(b[0] - a[0]), dy = (float)(b[1] - a[1]);
+        float len = sqrtf(dx * dx + dy * dy);
+        float ux = dx / len, uy = dy / len;
+        float s0 = INFINITY, s1 = -INFINITY, t0 = INFINITY, t1 = -INFINITY;
+        for (int j = 0; j < h; j++) {
+            float rx = (float)(hull[2 * j] - a[0]), ry = (float)(hull[2 * j + 1] - a[1]);
+            float s = rx * ux + ry * uy, t = rx * -uy + ry * ux;
+            s0 = s < s0 ? s : s0;
+            s1 = s > s1 ? s : s1;
+            t0 = t < t0 ? t : t0;
+            t1 = t > t1 ? t : t1;
+        }
+        float area = (s1 - s0) * (t1 - t0);
+        if (area < best) {
+            best = area;
+            float sc = (s0 + s1) * 0.5f, tc = (t0 + t1) * 0.5f;
+            rect[0] = (float)a[0] + ux * sc + -uy * tc;
+            rect[1] = (float)a[1] + uy * sc + ux * tc;
+            rect[2] = -uy;
+            rect[3] = ux;
+            rect[4] = s1 - s0;
+            rect[5] = t1 - t0;
+        }
+    }
+    free(hull);
+    return 1;
+}
+
+/* The rectangle of one contour (unpadded integer points), before resize: 0 when none. */
+static int wr_contour_rect(const wr_pts *c, float *rect) {
+    int n = c->n + 1; /* closed: the first point again at the end */
+    float *px = (float *)malloc(sizeof(float) * (size_t)n), *py = (float *)malloc(sizeof(float) * (size_t)n);
+    unsigned char *keep = (unsigned char *)calloc((size_t)n, 1);
+    for (int i = 0; i < n; i++) {
+        px[i] = (float)c->x[i % c->n];
+        py[i] = (float)c->y[i % c->n];
+    }
+    wr_dp(px, py, n, 2.0f, keep);
+    int *xy = (int *)malloc(sizeof(int) * 2 * (size_t)n), m = 0;
+    for (int i = 0; i < n - 1; i++)
+        if (keep[i]) {
+            xy[2 * m] = c->x[i];
+            xy[2 * m + 1] = c->y[i];
+            m++;
+        }
+    int ok = wr_min_rect(xy, m, rect);
+    free(px);
+    free(py);
+    free(keep);
+    free(xy);
+    return ok;
+}
+
+/* The external contours of mask (w x h bits, ceil(w / 32) words per row, bit b of word j =
+ * pixel 32 j + b) in the order the raster scan meets them, as unpadded pixel coordinates, into
+ * *out_c; returns their number. */
+static int wr_contours(const uint32_t *mask, int w, int h, wr_pts **out_c) {
+    const int W = w + 2, H = h + 2, words = (w + 31) / 32;
+    int *f = (int *)calloc((size_t)W * H, sizeof(int));
+    for (int y = 0; y < h; y++)
+        for (int x = 0; x < w; x++) f[(y + 1) * W + x + 1] = (mask[(size_t)y * words + x / 32] >> (x % 32)) & 1u;
+    int cap = 1024, nb = 1, nc = 0;
+    int *type = (int *)malloc(sizeof(int) * cap), *parent = (int *)malloc(sizeof(int) * cap);
+    wr_pts *cs = NULL;
+    int ccap = 0;
+    type[1] = 0; /* the frame: a hole border */
+    parent[1] = 0;
+    for (int y = 1; y < H - 1; y++) {
+        int lnbd = 1;
+        for (int x = 1; x < W - 1; x++) {
+            int v = f[y * W + x];
+            if (v == 0) continue;
+            int outer = v == 1 && f[y * W + x - 1] == 0;
+            int hole = !outer && v >= 1 && f[y * W + x + 1] == 0;
+            if (outer || hole) {
+                if (hole && v > 1) lnbd = v;
+                nb++;
+                if (nb >= cap) {
+                    cap *= 2;
+                    type = (int *)realloc(type, sizeof(int) * cap);
+                    parent = (int *)realloc(parent, sizeof(int) * cap);
+                }
+                type[nb] = outer;
+                if (outer)
+                    parent[nb] = type[lnbd] ? parent[lnbd] : lnbd;
+                else
+                    parent[nb] = type[lnbd] ? lnbd : parent[lnbd];
+                wr_pts pts = {0};
+                wr_follow(f, W, x, y, outer ? 0 : 4, nb, &pts);
+                if (outer && parent[nb] == 1) {
+                    if (nc == ccap) {
+                        ccap = ccap ? 2 * ccap : 64;
+                        cs = (wr_pts *)realloc(cs, sizeof(wr_pts) * ccap);
+                    }
+                    for (int i = 0; i < pts.n; i++) {
+                        pts.x[i] -= 1;
+                        pts.y[i] -= 1;
+                    }
+                    cs[nc++] = pts;
+                } else {
+                    free(pts.x);
+                    free(pts.y);
+                }
+            }
+            v = f[y * W + x];
+            if (v != 1) lnbd = v < 0 ? -v : v;
+        }
+    }
+    free(f);
+    free(type);
+    free(parent);
+    *out_c = cs;
+    return nc;
+}
+
+/* The external contours, flattened: returns the number of contours; lens / xs / ys are filled
+ * up to their capacities (cap_c contours, cap_p points); *n_points = the total length. */
+int oracle_contours(const uint32_t *mask, int w, int h, int *lens, int cap_c, int *xs, int *ys, int64_t cap_p,
+                    int64_t *n_points) {
+    wr_pts *cs = NULL;
+    int nc = wr_contours(mask, w, h, &cs);
+    int64_t np = 0;
+    for (int i = 0; i < nc; i++) {
+        if (i < cap_c) lens[i] = cs[i].n;
+        for (int j = 0; j < cs[i].n; j++, np++)
+            if (np < cap_p) {
+                xs[np] = cs[i].x[j];
+                ys[np] = cs[i].y[j];
+            }
+        free(cs[i].x);
+        free(cs[i].y);
+    }
+    free(cs);
+    *n_points = np;
+    return nc;
+}
+
+/* word_rects (src/bin/ocr-bench.rs:38-60): rectangles [cx, cy, up_x, up_y, width, height] of the
+ * external contours, expanded and filtered by area; returns their number (rects filled up to
+ * cap). */
+int oracle_word_rects(const uint32_t *mask, int w, int h, float expand, float expand_x, float min_area, float *rects,
+                      int cap) {
+    wr_pts *cs = NULL;
+    int nc = wr_contours(mask, w, h, &cs), n = 0;
+    for (int i = 0; i < nc; i++) {
+        float r[6] = {0};
+        if (wr_contour_rect(&cs[i], r)) {
+            r[4] = r[4] + 2.f * (expand + expand_x);
+            r[5] = r[5] + 2.f * expand;
+            if (r[4] * r[5] >= min_area) {
+                if (n < cap) memcpy(rects + 6 * (size_t)n, r, sizeof r);
+                n++;
+            }
+        }
+        free(cs[i].x);
+        free(cs[i].y);
+    }
+    free(cs);
+    return n;
+}

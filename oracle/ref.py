@@ -69,12 +69,15 @@ def lib():
             "oracle_act": [_F, _I],
             "oracle_pp_line": [_u8, _I, _I, _f, _f],
             "oracle_db_score": [_f, _I, _I, _f],
+            "oracle_contours": [_u32, _I, _I, _i32, _I, _i32, _i32, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)],
+            "oracle_word_rects": [_u32, _I, _I, _F, _F, _F, _f, _I],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = ctypes.c_float if name in ("oracle_erf", "oracle_act", "oracle_db_score") else (
-                ctypes.c_int if name in ("oracle_threads", "oracle_pp_line") else None)
+                ctypes.c_int if name in ("oracle_threads", "oracle_pp_line", "oracle_contours", "oracle_word_rects")
+                else None)
         _lib = L
     return _lib
 
@@ -134,6 +137,35 @@ def pool(x, kh, kw, sh, sw, pads=(0, 0, 0, 0), avg=False):
     y = np.empty((n, c, oh, ow), np.float32)
     lib().oracle_pool(_p(x), n * c, h, w, oh, ow, kh, kw, sh, sw, pt, pl, int(avg), _p(y))
     return y
+
+
+def contours(bits: np.ndarray, w: int, h: int):
+    """find_contours(mask, External) of a bit mask (uint32 [h, ceil(w / 32)]): a list of int32
+    [n, 2] (x, y) point arrays in raster order of their start pixels."""
+    bits = np.ascontiguousarray(bits, np.uint32)
+    np_ = ctypes.c_int64()
+    nc = lib().oracle_contours(_p(bits, _u32), w, h, None, 0, None, None, 0, ctypes.byref(np_))
+    lens = np.zeros(max(nc, 1), np.int32)
+    xs = np.zeros(max(np_.value, 1), np.int32)
+    ys = np.zeros(max(np_.value, 1), np.int32)
+    lib().oracle_contours(_p(bits, _u32), w, h, _p(lens, _i32), nc, _p(xs, _i32), _p(ys, _i32), np_.value,
+                          ctypes.byref(np_))
+    out, o = [], 0
+    for n in lens[:nc]:
+        out.append(np.stack([xs[o:o + n], ys[o:o + n]], 1))
+        o += n
+    return out
+
+
+def word_rects(bits: np.ndarray, w: int, h: int, expand: float = 3.0, expand_x: float = 0.0,
+               min_area: float = 100.0) -> np.ndarray:
+    """word_rects (src/bin/ocr-bench.rs:38-60) of a bit mask: float32 [n, 6] rectangles
+    [cx, cy, up_x, up_y, width, height] in contour order."""
+    bits = np.ascontiguousarray(bits, np.uint32)
+    n = lib().oracle_word_rects(_p(bits, _u32), w, h, expand, expand_x, min_area, None, 0)
+    out = np.zeros((max(n, 1), 6), np.float32)
+    lib().oracle_word_rects(_p(bits, _u32), w, h, expand, expand_x, min_area, _p(out), n)
+    return out[:n]
 
 
 def db_scores(prob: np.ndarray, rects) -> np.ndarray:

@@ -45,3 +45,41 @@ def softmax(x):
     m = x.max(axis=-1, keepdims=True)
     e = np.exp(x - m)
     return e / e.sum(axis=-1, keepdims=True)
+
+
+def pack_bits(m: np.ndarray) -> np.ndarray:
+    """A bool mask [h, w] as the library's bit mask: uint32 [h, ceil(w / 32)], bit b of word j =
+    pixel 32 j + b."""
+    h, w = m.shape
+    words = (w + 31) // 32
+    pad = np.zeros((h, words * 32), bool)
+    pad[:, :w] = m
+    return np.packbits(pad.reshape(h, words, 32), axis=2, bitorder="little").view("<u4")[..., 0].copy()
+
+
+def word_masks():
+    """Masks for the word-rectangle tests: nested shapes (a ring with a blob and a pixel in its
+    hole), shapes on every edge, a diagonal chain, a lone pixel, a thin bar; noise; random
+    blobs; an empty and a full mask (widths not multiples of 32)."""
+    rng = np.random.default_rng(7)
+    out = []
+    m = np.zeros((40, 70), bool)
+    m[3:20, 4:30] = True
+    m[7:15, 9:25] = False           # a ring ...
+    m[9:12, 12:15] = True           # ... with a blob in its hole (not external)
+    m[10, 20] = True                # ... and a single pixel in it
+    m[0:3, 60:70] = True            # touching the top and right edges
+    m[30, 0] = m[31, 1] = m[32, 2] = True   # a diagonal chain (one 8-connected component)
+    m[35:40, 40:50] = True          # touching the bottom
+    m[25, 50] = True                # a lone pixel
+    m[22:24, 33:57] = True          # a thin bar
+    out.append(m)
+    out.append(rng.random((33, 45)) < 0.45)                        # noise: many nested shapes
+    blob = np.zeros((60, 97), bool)
+    for _ in range(25):
+        y, x, hh, ww = rng.integers(0, 55), rng.integers(0, 90), rng.integers(2, 8), rng.integers(3, 25)
+        blob[y:y + hh, x:x + ww] = True
+    out.append(blob)
+    out.append(np.zeros((5, 7), bool))
+    out.append(np.ones((6, 33), bool))
+    return out

@@ -1,0 +1,62 @@
+"""Word rectangles of detection masks on the device (`wocr_word_rects`, src/bin/ocr-bench.rs:
+38-60) against the C restatement (`oracle_word_rects`): bit-identical rectangles, in the same
+order, for nested shapes, edge shapes, noise, random blobs, empty and full masks, several pages
+in one call, masks already on the device, and a config 1 detection mask."""
+import numpy as np
+import pytest
+
+import wocr
+from oracle import ref
+from wocr import synth
+
+from _helpers import pack_bits, word_masks
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("k", range(5))
+@pytest.mark.parametrize("params", [(3.0, 0.0, 100.0), (0.0, 0.0, 0.0), (3.0, 2.0, 50.0)])
+def test_word_rects_bit_exact(gpu, k, params):
+    m = word_masks()[k]
+    h, w = m.shape
+    got = gpu.word_rects(pack_bits(m), w, h, *params)[0]
+    want = ref.word_rects(pack_bits(m), w, h, *params)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_word_rects_pages_and_device_masks(gpu):
+    """Pages in one call equal pages one by one; a device mask equals the host mask."""
+    import torch
+
+    rng = np.random.default_rng(2)
+    h, w = 70, 131
+    pages = []
+    for i in range(4):
+        m = np.zeros((h, w), bool)
+        for _ in range(12 * i):
+            y, x = rng.integers(0, h - 6), rng.integers(0, w - 20)
+            m[y:y + rng.integers(2, 7), x:x + rng.integers(3, 20)] = True
+        pages.append(pack_bits(m))
+    bits = np.stack(pages)
+    got = gpu.word_rects(bits, w, h)
+    assert len(got) == 4 and len(got[0]) == 0
+    d = torch.from_numpy(bits.view(np.int32)).cuda()
+    dev = gpu.word_rects(None, w, h, d_mask=d.data_ptr(), n=4)
+    for g, dv, b in zip(got, dev, pages):
+        want = ref.word_rects(b, w, h)
+        np.testing.assert_array_equal(g, want)
+        np.testing.assert_array_equal(dv, want)
+
+
+def test_word_rects_detection_mask(gpu):
+    """A config 1 page through the detector, then its mask's word rectangles."""
+    det = wocr.Detector(gpu, synth.ocrs_det_model())
+    try:
+        page = synth.page(5, 2550, 3300)
+        bits = det.detect_page(page, 2550, 3300, 0.5)
+    finally:
+        det.close()
+    got = gpu.word_rects(bits, 2550, 3300)[0]
+    want = ref.word_rects(bits, 2550, 3300)
+    assert len(want) > 0
+    np.testing.assert_array_equal(got, want)

@@ -10,6 +10,8 @@ import torch.nn.functional as F
 from oracle import ref
 from wocr import synth
 
+from _helpers import pack_bits, word_masks
+
 RNG = np.random.default_rng(1234)
 
 
@@ -276,3 +278,63 @@ def test_db_score_oracle_matches_full_scan():
     want = np.array([_db_score_loops(prob, r) for r in rects], np.float32)
     np.testing.assert_array_equal(got, want)
     assert got[4] == 0 and got[7] == 0
+
+
+@pytest.mark.parametrize("k", range(5))
+def test_contour_oracle_vs_labelling(k):
+    """oracle_contours (Suzuki-Abe border following, External) against scipy's labelling: one
+    contour per 8-connected component whose surrounding 4-connected background reaches the
+    frame, starting at its first pixel in raster order, made of 8-adjacent steps (closed), and
+    visiting exactly the component's pixels that touch (4-neighbour) that background."""
+    from scipy import ndimage
+
+    m = word_masks()[k]
+    h, w = m.shape
+    cs = ref.contours(pack_bits(m), w, h)
+    fg, nf = ndimage.label(m, structure=np.ones((3, 3)))
+    pad = np.pad(~m, 1, constant_values=True)
+    bg, _ = ndimage.label(pad, structure=[[0, 1, 0], [1, 1, 1], [0, 1, 0]])
+    frame = bg[0, 0]
+    want = []
+    for lab in range(1, nf + 1):
+        ys, xs = np.nonzero(fg == lab)
+        i = np.lexsort((xs, ys))[0]
+        y0, x0 = ys[i], xs[i]
+        if bg[y0 + 1, x0] == frame:                       # the pixel left of the start (padded coords)
+            want.append((y0, x0, lab))
+    want.sort()
+    assert len(cs) == len(want)
+    for c, (y0, x0, lab) in zip(cs, want):
+        assert tuple(c[0]) == (x0, y0)
+        if len(c) > 1:
+            steps = np.abs(np.diff(np.vstack([c, c[:1]]), axis=0))
+            assert (steps.max(1) == 1).all()
+        comp = fg == lab
+        outer = np.zeros_like(comp)
+        for dy, dx in ((0, 1), (0, -1), (1, 0), (-1, 0)):
+            outer |= np.roll(np.roll(bg == frame, dy, 0), dx, 1)[1:-1, 1:-1]
+        border = comp & outer
+        got = np.zeros_like(comp)
+        got[c[:, 1], c[:, 0]] = True
+        assert (got == border).all()
+
+
+def test_word_rects_oracle_properties():
+    """Each rectangle of oracle_word_rects holds its contour's simplified points (so the
+    expanded rectangle holds the whole word up to the simplification's 2 px), has a unit up axis,
+    and its area passes the filter; a 1 x 1 blob collapses (one point) and is dropped."""
+    m = word_masks()[2]
+    h, w = m.shape
+    r = ref.word_rects(pack_bits(m), w, h)
+    assert len(r) > 5
+    assert np.allclose(np.hypot(r[:, 2], r[:, 3]), 1, atol=1e-6)
+    assert (r[:, 4] * r[:, 5] >= 100).all()
+    ys, xs = np.nonzero(m)
+    for cx, cy, ux, uy, rw, rh in r:
+        along = (xs - cx) * ux + (ys - cy) * uy
+        across = (xs - cx) * -uy + (ys - cy) * ux
+        inside = (np.abs(along) <= rh / 2 + 1e-3) & (np.abs(across) <= rw / 2 + 1e-3)
+        assert inside.sum() >= 3
+    one = np.zeros((8, 8), bool)
+    one[3, 3] = True
+    assert len(ref.word_rects(pack_bits(one), 8, 8, min_area=0)) == 0

@@ -1489,6 +1489,43 @@ int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float 
     });
 }
 
+int32_t wocr_word_rects(wocr_ctx *ctx, const uint32_t *mask, int32_t n, int32_t w, int32_t h,
+                        int32_t mask_on_device, float expand, float expand_x, float min_area, float *rects,
+                        int64_t cap, int32_t *counts) {
+    return guard([&] {
+        if (!ctx || !mask || !counts || (cap > 0 && !rects)) fail(WOCR_ERR_INVALID, "null argument");
+        if (n < 0 || w <= 0 || h <= 0 || cap < 0) fail(WOCR_ERR_INVALID, "bad page count or size");
+        if (w > 32767 || h > 32767) fail(WOCR_ERR_INVALID, "pages wider or taller than 32767 pixels");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        const int64_t words = (w + 31) / 32, page_words = words * h;
+        // page groups small enough for 32-bit run and point counts
+        const int group = (int)std::max<int64_t>(1, ((int64_t)1 << 28) / ((int64_t)w * h));
+        int64_t total = 0;
+        std::vector<float> host;
+        for (int p0 = 0; p0 < n; p0 += group) {
+            const int pn = std::min(group, n - p0);
+            const uint32_t *dm = mask + p0 * page_words;
+            BufP up;
+            if (!mask_on_device) {
+                up = alloc(c, (size_t)(pn * page_words * 4));
+                WOCR_CUDA(cudaMemcpyAsync(up->p, dm, (size_t)(pn * page_words * 4), cudaMemcpyHostToDevice, c->stream));
+                dm = (const uint32_t *)up->p;
+            }
+            k::WordRects wr = k::word_rects(c, dm, pn, w, h, expand, expand_x, min_area);
+            d2h(c, counts + p0, wr.page_count->p, (size_t)pn * 4);
+            const size_t o = host.size();
+            host.resize(o + (size_t)wr.n * 6);
+            d2h(c, host.data() + o, wr.rects->p, (size_t)wr.n * 24);
+            sync_bounded(c, 0);
+            total += wr.n;
+        }
+        if (!rects && cap == 0) return;
+        if (cap < total) fail(WOCR_ERR_CAPACITY, "rects holds " + std::to_string(cap) + " of " + std::to_string(total));
+        if (total) std::memcpy(rects, host.data(), (size_t)total * 24);
+    });
+}
+
 int32_t wocr_pp_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h, const float *rects, int32_t n,
                       int32_t per_batch, float *d_out, int64_t cap, int32_t *order, int32_t *batch_n,
                       int32_t *batch_w, int32_t *n_batches, int64_t *total) {

@@ -27,30 +27,55 @@ __global__ void k_db_mask(const float *__restrict__ prob, int w, int h, int word
     if (lane < nw) bits[(int64_t)y * words + wd0 + lane] = mine;
 }
 
-// `score` of src/ppdet.rs:63-83, one thread per box with the reference's order of additions (a
-// sequential f32 sum over the rows, then the columns, of the pixels inside the box), so the
-// result is the reference's to the bit.  The scan covers the box's bounding rectangle clamped to
-// the map; the inside test alone decides which pixels count.
-__global__ void k_db_scores(const float *__restrict__ prob, int w, int h, const DbBox *__restrict__ boxes, int n,
-                            float *__restrict__ scores) {
-    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+// `score` of src/ppdet.rs:63-83 with the reference's order of additions (a sequential f32 sum
+// over the rows, then the columns, of the pixels inside the box), so the result is the
+// reference's to the bit.  A warp per box: the lanes test and load 32 pixels of a row at a time
+// and stage them in shared memory, lane 0 adds the inside ones in column order (32 independent
+// loads, then a chain of predicated adds).  The scan covers the box's bounding rectangle clamped
+// to the map; the inside test alone decides which pixels count.
+constexpr int kDbWarps = 8;
+
+__global__ void __launch_bounds__(kDbWarps * 32) k_db_scores(const float *__restrict__ prob, int w, int h,
+                                                             const DbBox *__restrict__ boxes, int n,
+                                                             float *__restrict__ scores) {
+    __shared__ float stage[kDbWarps][32];
+    const int wi = threadIdx.x / 32, lane = threadIdx.x & 31;
+    const int k = blockIdx.x * kDbWarps + wi;
     if (k >= n) return;
     const DbBox b = boxes[k];
     float sum = 0.f;
     int64_t cnt = 0;
     for (int y = b.y0; y <= b.y1; y++) {
         const float dy = __fsub_rn((float)y, b.cy);
-        for (int x = b.x0; x <= b.x1; x++) {
-            const float dx = __fsub_rn((float)x, b.cx);
-            const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
-            const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
-            if (fabsf(along) <= b.hh && fabsf(across) <= b.hw) {
-                sum = __fadd_rn(sum, prob[(int64_t)y * w + x]);
-                cnt++;
+        const float *row = prob + (int64_t)y * w;
+        for (int xs = b.x0; xs <= b.x1; xs += 32) {
+            const int x = xs + lane;
+            bool in = false;
+            float v = 0.f;
+            if (x <= b.x1) {
+                const float dx = __fsub_rn((float)x, b.cx);
+                const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
+                const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
+                in = fabsf(along) <= b.hh && fabsf(across) <= b.hw;
+                if (in) v = row[x];
             }
+            const uint32_t m = __ballot_sync(0xffffffffu, in);
+            if (m == 0) continue;
+            stage[wi][lane] = v;
+            __syncwarp();
+            if (lane == 0) {
+                float t[32];
+#pragma unroll
+                for (int j = 0; j < 32; j++) t[j] = stage[wi][j];
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    if ((m >> j) & 1u) sum = __fadd_rn(sum, t[j]);
+                cnt += __popc(m);
+            }
+            __syncwarp();
         }
     }
-    scores[k] = cnt == 0 ? 0.f : __fdiv_rn(sum, (float)cnt);
+    if (lane == 0) scores[k] = cnt == 0 ? 0.f : __fdiv_rn(sum, (float)cnt);
 }
 
 }  // namespace
@@ -66,7 +91,7 @@ void db_mask(Ctx *c, const float *prob, int w, int h, float thr, uint32_t *bits)
 void db_scores(Ctx *c, const float *prob, int w, int h, const DbBox *boxes, int n, float *scores) {
     if (n <= 0) return;
     Prof pf(c, "db_scores", 0, 0);
-    k_db_scores<<<(n + 63) / 64, 64, 0, c->stream>>>(prob, w, h, boxes, n, scores);
+    k_db_scores<<<(n + kDbWarps - 1) / kDbWarps, kDbWarps * 32, 0, c->stream>>>(prob, w, h, boxes, n, scores);
     WOCR_LAUNCHED(c);
 }
 

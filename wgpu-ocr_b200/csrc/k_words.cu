@@ -1,0 +1,592 @@
+// Word rectangles of detection masks on the device: `word_rects` (src/bin/ocr-bench.rs:38-60),
+// i.e. rten-imageproc's find_contours(mask, External), simplify_polygon(2), min_area_rect, then
+// resize by the expand distances and an area filter, for a batch of page masks that never
+// leave HBM.
+//
+// The raster scan of Suzuki & Abe's border following is sequential; the same contours come
+// from a parallel labelling instead:
+//   1. every row of the bit mask is cut into runs of equal pixels (a warp per row);
+//   2. a union-find over the runs joins 8-connected foreground runs and 4-connected background
+//      runs of adjacent rows, and every background run on the page's edge with the page's frame
+//      node.  Union by smaller index makes a component's root its first run in raster order, so
+//      the root run starts at the pixel where the raster scan would meet the component;
+//   3. a foreground component is external (its outer border's parent is the frame) exactly when
+//      the background left of that pixel belongs to the frame's component (or the pixel is in
+//      column 0);
+//   4. one thread per external component follows its outer border from that pixel with
+//      Algorithm 1's steps (3.1)-(3.5) (count, then write), then runs Douglas-Peucker, the
+//      convex hull and the minimum-area rectangle on its own points.
+// Every floating-point step uses the round-to-nearest intrinsics in the order of the C
+// restatement, so the rectangles are bit-identical to it.
+#include "kernels.h"
+
+namespace wocr {
+namespace k {
+
+namespace {
+
+// (dx + 1) and (dy + 1) of the 8 neighbours, 2 bits each, clockwise on the screen (y down) from
+// the left neighbour: left, up-left, up, up-right, right, down-right, down, down-left.
+constexpr uint32_t kNbX = 6800, kNbY = 43265;
+__device__ __forceinline__ int nb_dx(int d) { return (int)((kNbX >> (2 * d)) & 3u) - 1; }
+__device__ __forceinline__ int nb_dy(int d) { return (int)((kNbY >> (2 * d)) & 3u) - 1; }
+
+__device__ __forceinline__ bool on_px(const uint32_t *m, int words, int w, int h, int x, int y) {
+    return (unsigned)x < (unsigned)w && (unsigned)y < (unsigned)h && ((__ldg(m + (int64_t)y * words + (x >> 5)) >> (x & 31)) & 1u);
+}
+
+// transitions between pixel x - 1 and x for the 32 pixels of word j (bit b = x = 32 j + b),
+// none at x = 0 or at x >= w
+__device__ __forceinline__ uint32_t row_edges(const uint32_t *row, int j, int w) {
+    const uint32_t cur = row[j], prev = j ? row[j - 1] : 0u;
+    uint32_t d = cur ^ ((cur << 1) | (prev >> 31));
+    if (j == 0) d &= ~1u;
+    const int valid = w - 32 * j;
+    if (valid < 32) d &= (1u << valid) - 1u;
+    return d;
+}
+
+// ---- scans ---------------------------------------------------------------------------------
+
+constexpr int kScanT = 1024, kScanItems = 4, kScanBlock = kScanT * kScanItems;
+
+// exclusive scan of each 4096-item block (in place allowed); the block's total to sums[block]
+__global__ void __launch_bounds__(kScanT) k_scan_blocks(const int *in, int n, int *out, int *sums) {
+    __shared__ int ws[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t base = (int64_t)blockIdx.x * kScanBlock + threadIdx.x * kScanItems;
+    int v[kScanItems], s = 0;
+#pragma unroll
+    for (int i = 0; i < kScanItems; i++) {
+        v[i] = base + i < n ? in[base + i] : 0;
+        s += v[i];
+    }
+    int x = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) ws[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int t = ws[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        ws[lane] = t;
+    }
+    __syncthreads();
+    int pre = x - s + (warp ? ws[warp - 1] : 0);
+#pragma unroll
+    for (int i = 0; i < kScanItems; i++) {
+        if (base + i < n) out[base + i] = pre;
+        pre += v[i];
+    }
+    if (threadIdx.x == kScanT - 1) sums[blockIdx.x] = pre;
+}
+
+__global__ void __launch_bounds__(kScanT) k_scan_add(int *out, int n, const int *sums) {
+    const int64_t base = (int64_t)blockIdx.x * kScanBlock + threadIdx.x * kScanItems;
+    const int add = sums[blockIdx.x];
+#pragma unroll
+    for (int i = 0; i < kScanItems; i++)
+        if (base + i < n) out[base + i] += add;
+}
+
+// ---- runs ----------------------------------------------------------------------------------
+
+constexpr int kRowWarps = 8;
+
+// runs per row = transitions + 1 (a warp per row)
+__global__ void __launch_bounds__(kRowWarps * 32) k_run_count(const uint32_t *__restrict__ mask, int words, int w,
+                                                              int rows, int *__restrict__ cnt) {
+    const int row = blockIdx.x * kRowWarps + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const uint32_t *m = mask + (int64_t)row * words;
+    int t = 0;
+    for (int j = lane; j < words; j += 32) t += __popc(row_edges(m, j, w));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) cnt[row] = t + 1;
+}
+
+// run starts (x), colours and rows; run 0 of a row starts at x = 0
+__global__ void __launch_bounds__(kRowWarps * 32) k_run_write(const uint32_t *__restrict__ mask, int words, int w,
+                                                              int rows, const int *__restrict__ off,
+                                                              int *__restrict__ run_x, uint8_t *__restrict__ run_c,
+                                                              int *__restrict__ run_row) {
+    const int row = blockIdx.x * kRowWarps + threadIdx.x / 32, lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const uint32_t *m = mask + (int64_t)row * words;
+    const int o = off[row];
+    if (lane == 0) {
+        run_x[o] = 0;
+        run_c[o] = (uint8_t)(m[0] & 1u);
+        run_row[o] = row;
+    }
+    int done = 1;
+    for (int j0 = 0; j0 < words; j0 += 32) {
+        const int j = j0 + lane;
+        const uint32_t d = j < words ? row_edges(m, j, w) : 0u;
+        const uint32_t cur = j < words ? m[j] : 0u;
+        const int c = __popc(d);
+        int x = c;
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, s);
+            if (lane >= s) x += y;
+        }
+        int k = o + done + x - c;
+        for (uint32_t b = d; b; b &= b - 1, k++) {
+            const int bit = __ffs(b) - 1;
+            run_x[k] = 32 * j + bit;
+            run_c[k] = (uint8_t)((cur >> bit) & 1u);
+            run_row[k] = row;
+        }
+        done += __shfl_sync(0xffffffffu, x, 31);
+    }
+}
+
+// ---- union-find over runs (node p < pages: page p's frame; node pages + r: run r) ------------
+
+__device__ __forceinline__ int uf_find(int *P, int x) {
+    for (;;) {
+        const int p = __ldcg(P + x);
+        if (p == x) return x;
+        const int g = __ldcg(P + p);
+        if (g != p) __stcg(P + x, g);
+        x = p;
+    }
+}
+
+__device__ __forceinline__ void uf_unite(int *P, int a, int b) {
+    a = uf_find(P, a);
+    b = uf_find(P, b);
+    while (a != b) {
+        if (a > b) {
+            const int t = a;
+            a = b;
+            b = t;
+        }
+        const int old = atomicCAS(P + b, b, a);
+        if (old == b) return;
+        b = uf_find(P, old);
+        a = uf_find(P, a);
+    }
+}
+
+__global__ void k_uf_init(int *P, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) P[i] = i;
+}
+
+__device__ __forceinline__ int run_end(const int *run_x, int r, int row_end, int w) {
+    return r + 1 < row_end ? run_x[r + 1] - 1 : w - 1;
+}
+
+__global__ void k_uf_union(const int *__restrict__ run_x, const uint8_t *__restrict__ run_c,
+                           const int *__restrict__ run_row, const int *__restrict__ off, const int *__restrict__ cnt,
+                           int R, int w, int h, int pages, int *P) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    const int row = run_row[r], y = row % h, page = row / h;
+    const int a = run_x[r], c = run_c[r], b = run_end(run_x, r, off[row] + cnt[row], w);
+    const int node = pages + r;
+    if (!c && (y == 0 || y == h - 1 || a == 0 || b == w - 1)) uf_unite(P, node, page);
+    if (y == 0) return;
+    const int q0 = off[row - 1], q1 = q0 + cnt[row - 1];
+    const int lo = c ? max(a - 1, 0) : a, hi = c ? min(b + 1, w - 1) : b;
+    int l = q0, u = q1 - 1;  // the last run of the row above starting at or before lo
+    while (l < u) {
+        const int mid = (l + u + 1) >> 1;
+        if (run_x[mid] <= lo)
+            l = mid;
+        else
+            u = mid - 1;
+    }
+    for (int q = l; q < q1 && run_x[q] <= hi; q++)
+        if (run_c[q] == c) uf_unite(P, node, pages + q);
+}
+
+__global__ void k_uf_flatten(int *P, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) P[i] = uf_find(P, i);
+}
+
+// 1 for the root run of an external foreground component
+__device__ __forceinline__ int is_ext_root(const int *run_x, const uint8_t *run_c, const int *run_row, const int *P,
+                                           int r, int h, int pages) {
+    if (!run_c[r] || P[pages + r] != pages + r) return 0;
+    return run_x[r] == 0 || P[pages + r - 1] == run_row[r] / h;
+}
+
+__global__ void k_ext_flag(const int *__restrict__ run_x, const uint8_t *__restrict__ run_c,
+                           const int *__restrict__ run_row, const int *__restrict__ P, int R, int h, int pages,
+                           int *__restrict__ flag) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < R) flag[r] = is_ext_root(run_x, run_c, run_row, P, r, h, pages);
+}
+
+__global__ void k_ext_list(const int *__restrict__ run_x, const uint8_t *__restrict__ run_c,
+                           const int *__restrict__ run_row, const int *__restrict__ P, int R, int h, int pages,
+                           const int *__restrict__ pos, int *__restrict__ comp_run) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < R && is_ext_root(run_x, run_c, run_row, P, r, h, pages)) comp_run[pos[r]] = r;
+}
+
+// ---- border following ------------------------------------------------------------------------
+
+// Algorithm 1 (3.1)-(3.5) from the outer-border start (x, y) entered from its left neighbour:
+// the number of border points; with WRITE, the points go to out.  A border is at most 4 points
+// a pixel; past that the status word is set and the trace stops.
+template <bool WRITE>
+__device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, short2 *out, int *status) {
+    int d1 = -1;
+    for (int d = 0; d < 8; d++)
+        if (on_px(m, words, w, h, x + nb_dx(d), y + nb_dy(d))) {
+            d1 = d;
+            break;
+        }
+    if (d1 < 0) {
+        if (WRITE) out[0] = make_short2((short)x, (short)y);
+        return 1;
+    }
+    const int x1 = x + nb_dx(d1), y1 = y + nb_dy(d1);
+    int x3 = x, y3 = y, e = d1, n = 0;
+    const int64_t cap = 4 * (int64_t)w * h + 8;
+    for (;;) {
+        if (WRITE) out[n] = make_short2((short)x3, (short)y3);
+        n++;
+        int x4 = x3, y4 = y3, d4 = e;
+        for (int k = 1; k <= 8; k++) {
+            const int d = (e - k) & 7, xx = x3 + nb_dx(d), yy = y3 + nb_dy(d);
+            if (on_px(m, words, w, h, xx, yy)) {
+                x4 = xx;
+                y4 = yy;
+                d4 = d;
+                break;
+            }
+        }
+        if (x4 == x && y4 == y && x3 == x1 && y3 == y1) break;
+        if (n >= cap) {
+            atomicExch(status, 40);
+            break;
+        }
+        e = (d4 + 4) & 7;  // from the new (i3, j3) back to the old one
+        x3 = x4;
+        y3 = y4;
+    }
+    return n;
+}
+
+__global__ void k_trace_len(const uint32_t *__restrict__ mask, int words, int w, int h,
+                            const int *__restrict__ run_x, const int *__restrict__ run_row,
+                            const int *__restrict__ comp_run, int C, int *__restrict__ len, int *status) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= C) return;
+    const int r = comp_run[k], row = run_row[r];
+    const uint32_t *m = mask + (int64_t)(row / h) * h * words;
+    len[k] = follow<false>(m, words, w, h, run_x[r], row % h, nullptr, status);
+}
+
+// ---- per-component geometry ------------------------------------------------------------------
+
+__device__ __forceinline__ float sq_len(float x, float y) { return __fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y)); }
+
+// point-to-segment distance (comp.graphics.algorithms FAQ 1.02)
+__device__ float seg_dist(float px, float py, float ax, float ay, float bx, float by) {
+    const float abx = __fsub_rn(bx, ax), aby = __fsub_rn(by, ay), acx = __fsub_rn(px, ax), acy = __fsub_rn(py, ay);
+    const float l2 = sq_len(abx, aby);
+    if (l2 == 0.f) return __fsqrt_rn(sq_len(acx, acy));
+    const float r = __fdiv_rn(__fadd_rn(__fmul_rn(acx, abx), __fmul_rn(acy, aby)), l2);
+    if (r <= 0.f) return __fsqrt_rn(sq_len(acx, acy));
+    if (r >= 1.f) return __fsqrt_rn(sq_len(__fsub_rn(px, bx), __fsub_rn(py, by)));
+    const float s = __fdiv_rn(__fsub_rn(__fmul_rn(abx, acy), __fmul_rn(aby, acx)), l2);
+    return fabsf(__fmul_rn(s, __fsqrt_rn(l2)));
+}
+
+__device__ __forceinline__ int key_x(uint32_t k) { return (int)(k >> 16); }
+__device__ __forceinline__ int key_y(uint32_t k) { return (int)(k & 0xffffu); }
+
+__device__ __forceinline__ int64_t cross3(uint32_t o, uint32_t a, uint32_t b) {
+    return (int64_t)(key_x(a) - key_x(o)) * (key_y(b) - key_y(o)) -
+           (int64_t)(key_y(a) - key_y(o)) * (key_x(b) - key_x(o));
+}
+
+__device__ void heap_sort(uint32_t *a, int n) {
+    auto sift = [&](int i, int end) {
+        for (;;) {
+            int c = 2 * i + 1;
+            if (c >= end) return;
+            if (c + 1 < end && a[c + 1] > a[c]) c++;
+            if (a[c] <= a[i]) return;
+            const uint32_t t = a[c];
+            a[c] = a[i];
+            a[i] = t;
+            i = c;
+        }
+    };
+    for (int i = n / 2 - 1; i >= 0; i--) sift(i, n);
+    for (int end = n - 1; end > 0; end--) {
+        const uint32_t t = a[0];
+        a[0] = a[end];
+        a[end] = t;
+        sift(0, end);
+    }
+}
+
+struct WordP {
+    const uint32_t *mask;
+    int words, w, h;
+    const int *run_x, *run_row, *comp_run, *pt_off;
+    int C;
+    short2 *pts;      // per component: its border, then the first point again
+    uint8_t *keep;    // Douglas-Peucker marks, same slots
+    int2 *stack;      // Douglas-Peucker segments, same slots
+    uint32_t *keys;   // kept points as (x << 16) | y, same slots
+    uint32_t *hull;   // 2 (n + 1) + 1 slots per component
+    float *rect;      // 6 per component
+    int *valid;
+    float expand, expand_x, min_area;
+    int *status;
+};
+
+__global__ void k_word_rect(WordP p) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= p.C) return;
+    const int r = p.comp_run[k], row = p.run_row[r];
+    const int64_t base = (int64_t)p.pt_off[k] + k;
+    short2 *pts = p.pts + base;
+    const uint32_t *m = p.mask + (int64_t)(row / p.h) * p.h * p.words;
+    const int nb = follow<true>(m, p.words, p.w, p.h, p.run_x[r], row % p.h, pts, p.status);
+    const int n = nb + 1;
+    pts[nb] = pts[0];
+    // Douglas-Peucker, epsilon 2, on the closed polyline
+    uint8_t *keep = p.keep + base;
+    for (int i = 0; i < n; i++) keep[i] = 0;
+    keep[0] = keep[n - 1] = 1;
+    int2 *st = p.stack + base;
+    int sp = 0;
+    st[sp++] = make_int2(0, n - 1);
+    while (sp) {
+        const int2 s = st[--sp];
+        const float ax = pts[s.x].x, ay = pts[s.x].y, bx = pts[s.y].x, by = pts[s.y].y;
+        float best = -1.f;
+        int bi = -1;
+        for (int i = s.x + 1; i < s.y; i++) {
+            const float d = seg_dist((float)pts[i].x, (float)pts[i].y, ax, ay, bx, by);
+            if (d > best) {
+                best = d;
+                bi = i;
+            }
+        }
+        if (bi >= 0 && best > 2.0f) {
+            keep[bi] = 1;
+            st[sp++] = make_int2(bi, s.y);  // popped after the left half, as the C stack does
+            st[sp++] = make_int2(s.x, bi);
+        }
+    }
+    uint32_t *keys = p.keys + base;
+    int mk = 0;
+    for (int i = 0; i < n - 1; i++)
+        if (keep[i]) keys[mk++] = ((uint32_t)pts[i].x << 16) | (uint32_t)pts[i].y;
+    heap_sort(keys, mk);
+    int u = 0;
+    for (int i = 0; i < mk; i++)
+        if (u == 0 || keys[i] != keys[u - 1]) keys[u++] = keys[i];
+    float *out = p.rect + 6 * (int64_t)k;
+    if (u < 2) {
+        p.valid[k] = 0;
+        return;
+    }
+    // Andrew's monotone chain
+    uint32_t *hl = p.hull + 2 * base + k;
+    int hn = 0;
+    for (int i = 0; i < u; i++) {
+        while (hn >= 2 && cross3(hl[hn - 2], hl[hn - 1], keys[i]) <= 0) hn--;
+        hl[hn++] = keys[i];
+    }
+    for (int i = u - 2, lo = hn + 1; i >= 0; i--) {
+        while (hn >= lo && cross3(hl[hn - 2], hl[hn - 1], keys[i]) <= 0) hn--;
+        hl[hn++] = keys[i];
+    }
+    const int hc = hn - 1;
+    // exhaustive search over the hull's edges
+    float best = __int_as_float(0x7f800000);
+    float rc[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int i = 0; i < hc; i++) {
+        const uint32_t a = hl[i], b = hl[(i + 1) % hc];
+        const float dx = (float)(key_x(b) - key_x(a)), dy = (float)(key_y(b) - key_y(a));
+        const float len = __fsqrt_rn(sq_len(dx, dy));
+        const float ux = __fdiv_rn(dx, len), uy = __fdiv_rn(dy, len);
+        float s0 = __int_as_float(0x7f800000), s1 = -s0, t0 = s0, t1 = -s0;
+        for (int j = 0; j < hc; j++) {
+            const float rx = (float)(key_x(hl[j]) - key_x(a)), ry = (float)(key_y(hl[j]) - key_y(a));
+            const float s = __fadd_rn(__fmul_rn(rx, ux), __fmul_rn(ry, uy));
+            const float t = __fadd_rn(__fmul_rn(rx, -uy), __fmul_rn(ry, ux));
+            s0 = s < s0 ? s : s0;
+            s1 = s > s1 ? s : s1;
+            t0 = t < t0 ? t : t0;
+            t1 = t > t1 ? t : t1;
+        }
+        const float area = __fmul_rn(__fsub_rn(s1, s0), __fsub_rn(t1, t0));
+        if (area < best) {
+            best = area;
+            const float sc = __fmul_rn(__fadd_rn(s0, s1), 0.5f), tc = __fmul_rn(__fadd_rn(t0, t1), 0.5f);
+            rc[0] = __fadd_rn(__fadd_rn((float)key_x(a), __fmul_rn(ux, sc)), __fmul_rn(-uy, tc));
+            rc[1] = __fadd_rn(__fadd_rn((float)key_y(a), __fmul_rn(uy, sc)), __fmul_rn(ux, tc));
+            rc[2] = -uy;
+            rc[3] = ux;
+            rc[4] = __fsub_rn(s1, s0);
+            rc[5] = __fsub_rn(t1, t0);
+        }
+    }
+    rc[4] = __fadd_rn(rc[4], __fmul_rn(2.f, __fadd_rn(p.expand, p.expand_x)));
+    rc[5] = __fadd_rn(rc[5], __fmul_rn(2.f, p.expand));
+#pragma unroll
+    for (int i = 0; i < 6; i++) out[i] = rc[i];
+    p.valid[k] = __fmul_rn(rc[4], rc[5]) >= p.min_area;
+}
+
+__global__ void k_word_pack(const float *__restrict__ rect, const int *__restrict__ valid, const int *__restrict__ pos,
+                            const int *__restrict__ comp_run, const int *__restrict__ run_row, int h, int C,
+                            float *__restrict__ out, int *__restrict__ page_cnt) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= C || !valid[k]) return;
+#pragma unroll
+    for (int i = 0; i < 6; i++) out[6 * (int64_t)pos[k] + i] = rect[6 * (int64_t)k + i];
+    atomicAdd(page_cnt + run_row[comp_run[k]] / h, 1);
+}
+
+inline unsigned blocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+}  // namespace
+
+void scan_i32(Ctx *c, const int *in, int n, int *out, int *total) {
+    if (n <= 0) {
+        WOCR_CUDA(cudaMemsetAsync(total, 0, sizeof(int), c->stream));
+        return;
+    }
+    const int nb = (n + kScanBlock - 1) / kScanBlock;
+    if (nb == 1) {
+        k_scan_blocks<<<1, kScanT, 0, c->stream>>>(in, n, out, total);
+        WOCR_LAUNCHED(c);
+        return;
+    }
+    BufP sums = alloc(c, (size_t)nb * sizeof(int));
+    int *s = (int *)sums->p;
+    k_scan_blocks<<<nb, kScanT, 0, c->stream>>>(in, n, out, s);
+    WOCR_LAUNCHED(c);
+    scan_i32(c, s, nb, s, total);
+    k_scan_add<<<nb, kScanT, 0, c->stream>>>(out, n, s);
+    WOCR_LAUNCHED(c);
+}
+
+namespace {
+int read_int(Ctx *c, const int *d) {
+    int v = 0;
+    WOCR_CUDA(cudaMemcpyAsync(&v, d, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    return v;
+}
+}  // namespace
+
+WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, float expand, float expand_x,
+                     float min_area) {
+    WordRects res;
+    res.page_count = alloc(c, (size_t)pages * sizeof(int));
+    WOCR_CUDA(cudaMemsetAsync(res.page_count->p, 0, (size_t)pages * sizeof(int), c->stream));
+    const int words = (w + 31) / 32, rows = pages * h;
+    BufP cnt = alloc(c, (size_t)rows * 4), off = alloc(c, (size_t)rows * 4), tot = alloc(c, 4);
+    int *d_cnt = (int *)cnt->p, *d_off = (int *)off->p, *d_tot = (int *)tot->p;
+    {
+        Prof pf(c, "word_runs", 0, (double)rows * words * 4);
+        k_run_count<<<blocks(rows, kRowWarps), kRowWarps * 32, 0, c->stream>>>(mask, words, w, rows, d_cnt);
+        WOCR_LAUNCHED(c);
+    }
+    scan_i32(c, d_cnt, rows, d_off, d_tot);
+    const int R = read_int(c, d_tot);
+    BufP rx = alloc(c, (size_t)R * 4), rc = alloc(c, (size_t)R), rr = alloc(c, (size_t)R * 4);
+    BufP par = alloc(c, (size_t)(R + pages) * 4), flag = alloc(c, (size_t)R * 4), pos = alloc(c, (size_t)R * 4);
+    int *run_x = (int *)rx->p, *run_row = (int *)rr->p, *P = (int *)par->p;
+    uint8_t *run_c = (uint8_t *)rc->p;
+    {
+        Prof pf(c, "word_runs", 0, (double)rows * words * 4 + (double)R * 9);
+        k_run_write<<<blocks(rows, kRowWarps), kRowWarps * 32, 0, c->stream>>>(mask, words, w, rows, d_off, run_x,
+                                                                                 run_c, run_row);
+        WOCR_LAUNCHED(c);
+    }
+    {
+        Prof pf(c, "word_label", 0, (double)R * 30);
+        k_uf_init<<<blocks(R + pages, 256), 256, 0, c->stream>>>(P, R + pages);
+        WOCR_LAUNCHED(c);
+        k_uf_union<<<blocks(R, 256), 256, 0, c->stream>>>(run_x, run_c, run_row, d_off, d_cnt, R, w, h, pages, P);
+        WOCR_LAUNCHED(c);
+        k_uf_flatten<<<blocks(R + pages, 256), 256, 0, c->stream>>>(P, R + pages);
+        WOCR_LAUNCHED(c);
+        k_ext_flag<<<blocks(R, 256), 256, 0, c->stream>>>(run_x, run_c, run_row, P, R, h, pages, (int *)flag->p);
+        WOCR_LAUNCHED(c);
+    }
+    scan_i32(c, (const int *)flag->p, R, (int *)pos->p, d_tot);
+    const int C = read_int(c, d_tot);
+    res.n = 0;
+    if (C == 0) {
+        res.rects = alloc(c, 4);
+        return res;
+    }
+    BufP crun = alloc(c, (size_t)C * 4), len = alloc(c, (size_t)C * 4), ptoff = alloc(c, (size_t)C * 4);
+    k_ext_list<<<blocks(R, 256), 256, 0, c->stream>>>(run_x, run_c, run_row, P, R, h, pages, (const int *)pos->p,
+                                                      (int *)crun->p);
+    WOCR_LAUNCHED(c);
+    {
+        Prof pf(c, "word_trace", 0, 0);
+        k_trace_len<<<blocks(C, 64), 64, 0, c->stream>>>(mask, words, w, h, run_x, run_row, (const int *)crun->p, C,
+                                                         (int *)len->p, c->status);
+        WOCR_LAUNCHED(c);
+    }
+    scan_i32(c, (const int *)len->p, C, (int *)ptoff->p, d_tot);
+    const int64_t slots = (int64_t)read_int(c, d_tot) + C;
+    BufP pts = alloc(c, (size_t)slots * 4), keep = alloc(c, (size_t)slots), stack = alloc(c, (size_t)slots * 8);
+    BufP keys = alloc(c, (size_t)slots * 4), hull = alloc(c, (size_t)(2 * slots + C) * 4);
+    BufP rect = alloc(c, (size_t)C * 24), valid = alloc(c, (size_t)C * 4), vpos = alloc(c, (size_t)C * 4);
+    WordP p;
+    p.mask = mask;
+    p.words = words;
+    p.w = w;
+    p.h = h;
+    p.run_x = run_x;
+    p.run_row = run_row;
+    p.comp_run = (const int *)crun->p;
+    p.pt_off = (const int *)ptoff->p;
+    p.C = C;
+    p.pts = (short2 *)pts->p;
+    p.keep = (uint8_t *)keep->p;
+    p.stack = (int2 *)stack->p;
+    p.keys = (uint32_t *)keys->p;
+    p.hull = (uint32_t *)hull->p;
+    p.rect = (float *)rect->p;
+    p.valid = (int *)valid->p;
+    p.expand = expand;
+    p.expand_x = expand_x;
+    p.min_area = min_area;
+    p.status = c->status;
+    {
+        Prof pf(c, "word_rect", 0, 0);
+        k_word_rect<<<blocks(C, 64), 64, 0, c->stream>>>(p);
+        WOCR_LAUNCHED(c);
+    }
+    scan_i32(c, (const int *)valid->p, C, (int *)vpos->p, d_tot);
+    res.n = read_int(c, d_tot);
+    res.rects = alloc(c, (size_t)std::max(res.n, 1) * 24);
+    k_word_pack<<<blocks(C, 256), 256, 0, c->stream>>>((const float *)rect->p, (const int *)valid->p,
+                                                       (const int *)vpos->p, (const int *)crun->p, run_row, h, C,
+                                                       (float *)res.rects->p, (int *)res.page_count->p);
+    WOCR_LAUNCHED(c);
+    return res;
+}
+
+}  // namespace k
+}  // namespace wocr

@@ -143,6 +143,19 @@ struct DbBox {
 void db_mask(Ctx *c, const float *prob, int w, int h, float thr, uint32_t *bits);
 void db_scores(Ctx *c, const float *prob, int w, int h, const DbBox *boxes, int n, float *scores);
 
+// Word rectangles of bit masks (k_words.cu, `word_rects` of src/bin/ocr-bench.rs:38-60): `pages`
+// masks of h rows x ceil(w / 32) words at mask; rects [n][6] = [cx, cy, up_x, up_y, width,
+// height] page after page in raster order of the contours, page_count[pages] per page.
+// Synchronises the stream to size its buffers.
+struct WordRects {
+    BufP rects, page_count;
+    int n = 0;
+};
+WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, float expand, float expand_x,
+                     float min_area);
+// exclusive prefix sum of n ints (out may be in); the total to *total (device)
+void scan_i32(Ctx *c, const int *in, int n, int *out, int *total);
+
 // One PP-OCR recognition line of a batch (k_lines.cu): the clamped box (left, top, cw x ch), its
 // resized width ow, the batch width (>= ow, zero padding past ow) and the float offset of its
 // [3][48][width] block in the output.

@@ -66,6 +66,27 @@ class Gpu:
                                       ctypes.byref(nb), ctypes.byref(tot)))
         return order[:n].tolist(), [(int(bn[i]), int(bw[i])) for i in range(nb.value)], tot.value
 
+    def word_rects(self, mask, w: int, h: int, expand: float = 3.0, expand_x: float = 0.0,
+                   min_area: float = 100.0, d_mask: int = 0, n: int = 0):
+        """word_rects (src/bin/ocr-bench.rs:38-60) of bit masks on the device (`wocr_word_rects`):
+        `mask` uint32 [n, h, ceil(w / 32)] (or [h, words] for one page) in host memory, or
+        d_mask, a device pointer to n such pages.  Returns a list per page of float32 [k, 6]
+        rectangles [cx, cy, up_x, up_y, width, height]."""
+        if d_mask:
+            src, npg = ctypes.c_void_p(d_mask), int(n)
+        else:
+            m = np.ascontiguousarray(mask, np.uint32)
+            npg = 1 if m.ndim == 2 else m.shape[0]
+            src = L.ptr(m)
+        counts = np.zeros(max(npg, 1), np.int32)
+        L.check(L.lib().wocr_word_rects(self.h, src, npg, int(w), int(h), int(bool(d_mask)), expand, expand_x,
+                                        min_area, None, 0, L.ptr(counts)))
+        out = np.zeros((max(int(counts[:npg].sum()), 1), 6), np.float32)
+        L.check(L.lib().wocr_word_rects(self.h, src, npg, int(w), int(h), int(bool(d_mask)), expand, expand_x,
+                                        min_area, L.ptr(out), out.shape[0], L.ptr(counts)))
+        ends = np.cumsum(counts[:npg])
+        return [out[e - k:e] for e, k in zip(ends, counts[:npg])]
+
     def profile(self, on: bool):
         """Start (clearing earlier records) or stop per-kernel CUDA-event timing."""
         L.check(L.lib().wocr_ctx_profile(self.h, int(bool(on))))
