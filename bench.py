@@ -47,10 +47,11 @@ def parse():
     p.add_argument("--pages", type=int, default=12, help="pages per GPU per step")
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
-    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines"],
+    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines", "words1"],
                    help="det1 (default, the driver's line): config 1 detection; rec0 / pp3 / ppdet4: configs "
                         "0, 3 and 4 through their public calls; ppdb4: config 4 with the DB mask and box "
-                        "scores on the device; pplines: PP line extraction (secondary measurements)")
+                        "scores on the device; pplines: PP line extraction; words1: word rectangles of config 1 "
+                        "detection masks (secondary measurements)")
     return p.parse_args()
 
 
@@ -431,6 +432,27 @@ def run_workload(args):
         def cpu():
             ref.pp_batches(pages_np[0], boxes[0])
             return len(boxes[0]), f"{len(boxes[0])} lines (one page)"
+    elif args.workload == "words1":
+        handle = None
+        npg = 12
+        masks = synth.pack_mask(np.stack([synth.page_word_mask(2000 + k, W_PAGE, H_PAGE) for k in range(npg)]))
+        d_masks = torch.from_numpy(masks.view(np.int32)).to(dev)
+        torch.cuda.synchronize()
+        nrects = sum(len(r) for r in gpu.word_rects(None, W_PAGE, H_PAGE, d_mask=d_masks.data_ptr(), n=npg))
+        units, unit, workload = npg, "pages/s", (f"config 1 word rectangles: word_rects (external contours, "
+                                                 f"Douglas-Peucker 2 px, minimum-area rectangles, expand 3, min "
+                                                 f"area 100) of {npg} device-resident 2550x3300 text masks of "
+                                                 f"synthetic pages (seeds 2000..2011: each page's ink rectangles "
+                                                 f"grown 8 x 3 px into word blobs, as a trained detector marks "
+                                                 f"words), {nrects} rectangles read back")
+        h2d, d2h = 0, nrects * 24 + npg * 4
+
+        def step():
+            gpu.word_rects(None, W_PAGE, H_PAGE, d_mask=d_masks.data_ptr(), n=npg)
+
+        def cpu():
+            ref.word_rects(masks[0], W_PAGE, H_PAGE)
+            return 1, "1 page"
     elif args.workload == "ppdb4":
         model = synth.pp_det_model()
         page = synth.page(3, W_PAGE, H_PAGE)

@@ -48,13 +48,10 @@ def softmax(x):
 
 
 def pack_bits(m: np.ndarray) -> np.ndarray:
-    """A bool mask [h, w] as the library's bit mask: uint32 [h, ceil(w / 32)], bit b of word j =
-    pixel 32 j + b."""
-    h, w = m.shape
-    words = (w + 31) // 32
-    pad = np.zeros((h, words * 32), bool)
-    pad[:, :w] = m
-    return np.packbits(pad.reshape(h, words, 32), axis=2, bitorder="little").view("<u4")[..., 0].copy()
+    """A bool mask [h, w] as the library's bit mask (uint32 [h, ceil(w / 32)])."""
+    from wocr import synth
+
+    return synth.pack_mask(m)
 
 
 def word_masks():

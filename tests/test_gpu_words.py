@@ -48,6 +48,25 @@ def test_word_rects_pages_and_device_masks(gpu):
         np.testing.assert_array_equal(dv, want)
 
 
+def _comb_disk(r=1100, size=2500, seed=4):
+    """A disk with a ragged rim (radius jittered by +-8 px every 0.1 degrees): thousands of
+    Douglas-Peucker points outside the octagon of extremes, past the shared-memory sort."""
+    rng = np.random.default_rng(seed)
+    jit = rng.integers(-8, 9, 3600)
+    yy, xx = np.mgrid[:size, :size]
+    ang = (np.degrees(np.arctan2(yy - size / 2, xx - size / 2)) % 360 / 0.1).astype(int) % 3600
+    return np.hypot(yy - size / 2, xx - size / 2) <= r + jit[ang]
+
+
+def test_word_rects_large_components(gpu):
+    """One large component with a ragged rim (the global-memory sort), and a page of word blobs
+    (the benchmark's masks)."""
+    for m in (_comb_disk(), synth.page_word_mask(2003)):
+        h, w = m.shape
+        bits = pack_bits(m)
+        np.testing.assert_array_equal(gpu.word_rects(bits, w, h)[0], ref.word_rects(bits, w, h))
+
+
 def test_word_rects_detection_mask(gpu):
     """A config 1 page through the detector, then its mask's word rectangles."""
     det = wocr.Detector(gpu, synth.ocrs_det_model())

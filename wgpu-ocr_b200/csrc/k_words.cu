@@ -14,8 +14,8 @@
 //      the background left of that pixel belongs to the frame's component (or the pixel is in
 //      column 0);
 //   4. one thread per external component follows its outer border from that pixel with
-//      Algorithm 1's steps (3.1)-(3.5) (count, then write), then runs Douglas-Peucker, the
-//      convex hull and the minimum-area rectangle on its own points.
+//      Algorithm 1's steps (3.1)-(3.5) (count, then write); a block per component then runs
+//      Douglas-Peucker, the convex hull and the minimum-area rectangle on its points.
 // Every floating-point step uses the round-to-nearest intrinsics in the order of the C
 // restatement, so the rectangles are bit-identical to it.
 #include "kernels.h"
@@ -343,81 +343,235 @@ struct WordP {
     int words, w, h;
     const int *run_x, *run_row, *comp_run, *pt_off;
     int C;
-    short2 *pts;      // per component: its border, then the first point again
-    uint8_t *keep;    // Douglas-Peucker marks, same slots
-    int2 *stack;      // Douglas-Peucker segments, same slots
-    uint32_t *keys;   // kept points as (x << 16) | y, same slots
-    uint32_t *hull;   // 2 (n + 1) + 1 slots per component
-    float *rect;      // 6 per component
+    // per component, n + 1 slots each (n border points; slot base = pt_off[k] + k)
+    short2 *pts;       // its border, then the first point again
+    uint8_t *keep;     // Douglas-Peucker marks
+    int2 *seg_a, *seg_b;  // segments of the current and the next level
+    int *pref;         // exclusive prefix of the current level's interior sizes
+    unsigned long long *best;  // per segment: (distance bits << 32) | ~index, the level's argmax
+    uint32_t *keys;    // kept points as (x << 16) | y
+    uint32_t *hull;    // 2 (n + 1) + 1 slots per component (base 2 base + k)
+    float *rect;       // 6 per component
     int *valid;
     float expand, expand_x, min_area;
     int *status;
 };
 
-__global__ void k_word_rect(WordP p) {
-    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+constexpr int kWT = 128, kSortCap = 2048;
+
+// exclusive prefix of size(i) for i < n into out; returns the total (all threads)
+template <typename F>
+__device__ int block_scan(int n, int *out, F size, int *warp_tot) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int carry = 0;
+    for (int c0 = 0; c0 < n; c0 += kWT) {
+        const int i = c0 + threadIdx.x;
+        const int v = i < n ? size(i) : 0;
+        int x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_tot[warp] = x;
+        __syncthreads();
+        int before = carry;
+        for (int q = 0; q < warp; q++) before += warp_tot[q];
+        int all = carry;
+        for (int q = 0; q < kWT / 32; q++) all += warp_tot[q];
+        if (i < n) out[i] = before + x - v;
+        __syncthreads();
+        carry = all;
+    }
+    return carry;
+}
+
+__device__ __forceinline__ unsigned long long dp_key(float d, int i) {
+    return ((unsigned long long)__float_as_uint(d) << 32) | (0xffffffffu - (uint32_t)i);
+}
+
+// a point strictly inside the octagon of extreme points cannot be a hull vertex
+__device__ __forceinline__ bool in_octagon(const uint32_t *oct, int noct, uint32_t q) {
+    if (noct < 3) return false;
+    for (int i = 0; i < 8; i++) {
+        const uint32_t a = oct[i], b = oct[(i + 1) & 7];
+        if (a == b) continue;
+        if (cross3(a, b, q) <= 0) return false;
+    }
+    return true;
+}
+
+// One block per external component: border following (one thread), Douglas-Peucker by levels
+// (every point of every open segment at once, argmax per segment by a 64-bit atomicMax: the
+// largest distance, then the smallest index, as the sequential search finds it), the hull of
+// the kept points (octagon filter, sort, monotone chain) and the minimum-area rectangle (an
+// argmin over the hull's edges, first edge on ties).
+__global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
+    __shared__ int s_n, s_nseg, s_next, s_tot, s_m, s_ns, s_hc, s_noct;
+    __shared__ int warp_tot[kWT / 32];
+    __shared__ uint32_t s_oct[8];
+    __shared__ unsigned long long s_ext[8], s_best;
+    __shared__ uint32_t s_sort[kSortCap];
+    const int k = blockIdx.x, tid = threadIdx.x;
     if (k >= p.C) return;
     const int r = p.comp_run[k], row = p.run_row[r];
     const int64_t base = (int64_t)p.pt_off[k] + k;
     short2 *pts = p.pts + base;
-    const uint32_t *m = p.mask + (int64_t)(row / p.h) * p.h * p.words;
-    const int nb = follow<true>(m, p.words, p.w, p.h, p.run_x[r], row % p.h, pts, p.status);
-    const int n = nb + 1;
-    pts[nb] = pts[0];
-    // Douglas-Peucker, epsilon 2, on the closed polyline
+    if (tid == 0) {
+        const uint32_t *m = p.mask + (int64_t)(row / p.h) * p.h * p.words;
+        const int nb = follow<true>(m, p.words, p.w, p.h, p.run_x[r], row % p.h, pts, p.status);
+        pts[nb] = pts[0];
+        s_n = nb + 1;
+        s_nseg = 0;
+        if (nb + 1 > 2) {
+            p.seg_a[base] = make_int2(0, nb);
+            s_nseg = 1;
+        }
+    }
+    __syncthreads();
+    const int n = s_n;
     uint8_t *keep = p.keep + base;
-    for (int i = 0; i < n; i++) keep[i] = 0;
-    keep[0] = keep[n - 1] = 1;
-    int2 *st = p.stack + base;
-    int sp = 0;
-    st[sp++] = make_int2(0, n - 1);
-    while (sp) {
-        const int2 s = st[--sp];
-        const float ax = pts[s.x].x, ay = pts[s.x].y, bx = pts[s.y].x, by = pts[s.y].y;
-        float best = -1.f;
-        int bi = -1;
-        for (int i = s.x + 1; i < s.y; i++) {
-            const float d = seg_dist((float)pts[i].x, (float)pts[i].y, ax, ay, bx, by);
-            if (d > best) {
-                best = d;
-                bi = i;
+    for (int i = tid; i < n; i += kWT) keep[i] = (i == 0 || i == n - 1);
+    int2 *sa = p.seg_a + base, *sb = p.seg_b + base;
+    int *pref = p.pref + base;
+    unsigned long long *best = p.best + base;
+    __syncthreads();
+    // Douglas-Peucker, epsilon 2, on the closed polyline
+    while (s_nseg > 0) {
+        const int nseg = s_nseg;
+        for (int q = tid; q < nseg; q += kWT) best[q] = 0ull;
+        const int tot = block_scan(nseg, pref, [&](int q) { return sa[q].y - sa[q].x - 1; }, warp_tot);
+        for (int g = tid; g < tot; g += kWT) {
+            int lo = 0, hi = nseg - 1;  // the last segment whose prefix is <= g
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (pref[mid] <= g)
+                    lo = mid;
+                else
+                    hi = mid - 1;
+            }
+            const int2 sg = sa[lo];
+            const int i = sg.x + 1 + (g - pref[lo]);
+            const float d = seg_dist((float)pts[i].x, (float)pts[i].y, (float)pts[sg.x].x, (float)pts[sg.x].y,
+                                     (float)pts[sg.y].x, (float)pts[sg.y].y);
+            atomicMax(best + lo, dp_key(d, i));
+        }
+        if (tid == 0) s_next = 0;
+        __syncthreads();
+        for (int q = tid; q < nseg; q += kWT) {
+            const unsigned long long b = best[q];
+            const float d = __uint_as_float((uint32_t)(b >> 32));
+            const int i = (int)(0xffffffffu - (uint32_t)b);
+            const int2 sg = sa[q];
+            if (d > 2.0f) {
+                keep[i] = 1;
+                if (i - sg.x > 1) sb[atomicAdd(&s_next, 1)] = make_int2(sg.x, i);
+                if (sg.y - i > 1) sb[atomicAdd(&s_next, 1)] = make_int2(i, sg.y);
             }
         }
-        if (bi >= 0 && best > 2.0f) {
-            keep[bi] = 1;
-            st[sp++] = make_int2(bi, s.y);  // popped after the left half, as the C stack does
-            st[sp++] = make_int2(s.x, bi);
-        }
+        __syncthreads();
+        if (tid == 0) s_nseg = s_next;
+        int2 *t = sa;
+        sa = sb;
+        sb = t;
+        __syncthreads();
     }
+    // the kept points (the closing copy excluded), and their extremes
     uint32_t *keys = p.keys + base;
-    int mk = 0;
-    for (int i = 0; i < n - 1; i++)
-        if (keep[i]) keys[mk++] = ((uint32_t)pts[i].x << 16) | (uint32_t)pts[i].y;
-    heap_sort(keys, mk);
-    int u = 0;
-    for (int i = 0; i < mk; i++)
-        if (u == 0 || keys[i] != keys[u - 1]) keys[u++] = keys[i];
-    float *out = p.rect + 6 * (int64_t)k;
-    if (u < 2) {
-        p.valid[k] = 0;
+    if (tid == 0) s_m = 0;
+    if (tid < 8) s_ext[tid] = (tid & 1) ? 0ull : ~0ull;
+    __syncthreads();
+    for (int i = tid; i < n - 1; i += kWT)
+        if (keep[i]) {
+            const uint32_t kk = ((uint32_t)pts[i].x << 16) | (uint32_t)pts[i].y;
+            keys[atomicAdd(&s_m, 1)] = kk;
+            const int x = pts[i].x, y = pts[i].y;
+            // (value, key) pairs: even slots take the minimum, odd ones the maximum
+            const int v[4] = {x, y, x + y, x - y + 65536};
+            for (int e = 0; e < 4; e++) {
+                const unsigned long long pk = ((unsigned long long)(uint32_t)v[e] << 32) | kk;
+                atomicMin(&s_ext[2 * e], pk);
+                atomicMax(&s_ext[2 * e + 1], pk);
+            }
+        }
+    __syncthreads();
+    const int m = s_m;
+    if (tid == 0) {
+        // octagon in order: min x, min x+y, min y, max x-y, max x, max x+y, max y, min x-y
+        const int ord[8] = {0, 4, 2, 7, 1, 5, 3, 6};
+        int distinct = 0;
+        for (int i = 0; i < 8; i++) {
+            s_oct[i] = (uint32_t)s_ext[ord[i]];
+            bool seen = false;
+            for (int j = 0; j < i; j++) seen |= s_oct[j] == s_oct[i];
+            distinct += !seen;
+        }
+        s_noct = m > 0 ? distinct : 0;
+        s_ns = 0;
+    }
+    __syncthreads();
+    // survivors of the octagon filter (into the free segment slots), sorted in shared memory
+    // when they fit
+    uint32_t *surv = (uint32_t *)sb;
+    for (int i = tid; i < m; i += kWT)
+        if (!in_octagon(s_oct, s_noct, keys[i])) surv[atomicAdd(&s_ns, 1)] = keys[i];
+    __syncthreads();
+    const bool small = s_ns <= kSortCap;
+    uint32_t *sv = small ? s_sort : surv;
+    if (small) {
+        const int ns = s_ns;
+        for (int i = tid; i < ns; i += kWT) s_sort[i] = surv[i];
+        int np2 = 1;
+        while (np2 < ns) np2 <<= 1;
+        for (int i = ns + tid; i < np2; i += kWT) s_sort[i] = 0xffffffffu;
+        __syncthreads();
+        for (int len = 2; len <= np2; len <<= 1)
+            for (int j = len >> 1; j > 0; j >>= 1) {
+                for (int i = tid; i < np2; i += kWT) {
+                    const int l = i ^ j;
+                    if (l > i) {
+                        const uint32_t a = s_sort[i], b = s_sort[l];
+                        const bool up = (i & len) == 0;
+                        if ((a > b) == up) {
+                            s_sort[i] = b;
+                            s_sort[l] = a;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+    } else if (tid == 0) {
+        heap_sort(surv, s_ns);
+    }
+    __syncthreads();
+    uint32_t *hl = p.hull + 2 * base + k;
+    if (tid == 0) {
+        const int ns = s_ns;
+        int u = 0;
+        for (int i = 0; i < ns; i++)
+            if (u == 0 || sv[i] != sv[u - 1]) sv[u++] = sv[i];
+        int hn = 0;
+        if (u >= 2) {
+            for (int i = 0; i < u; i++) {
+                while (hn >= 2 && cross3(hl[hn - 2], hl[hn - 1], sv[i]) <= 0) hn--;
+                hl[hn++] = sv[i];
+            }
+            for (int i = u - 2, lo = hn + 1; i >= 0; i--) {
+                while (hn >= lo && cross3(hl[hn - 2], hl[hn - 1], sv[i]) <= 0) hn--;
+                hl[hn++] = sv[i];
+            }
+        }
+        s_hc = u >= 2 ? hn - 1 : 0;
+        s_best = ~0ull;
+    }
+    __syncthreads();
+    const int hc = s_hc;
+    if (hc == 0) {
+        if (tid == 0) p.valid[k] = 0;
         return;
     }
-    // Andrew's monotone chain
-    uint32_t *hl = p.hull + 2 * base + k;
-    int hn = 0;
-    for (int i = 0; i < u; i++) {
-        while (hn >= 2 && cross3(hl[hn - 2], hl[hn - 1], keys[i]) <= 0) hn--;
-        hl[hn++] = keys[i];
-    }
-    for (int i = u - 2, lo = hn + 1; i >= 0; i--) {
-        while (hn >= lo && cross3(hl[hn - 2], hl[hn - 1], keys[i]) <= 0) hn--;
-        hl[hn++] = keys[i];
-    }
-    const int hc = hn - 1;
-    // exhaustive search over the hull's edges
-    float best = __int_as_float(0x7f800000);
-    float rc[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int i = 0; i < hc; i++) {
+    // the edge of least area (first on ties)
+    auto edge = [&](int i, float *rc) -> float {
         const uint32_t a = hl[i], b = hl[(i + 1) % hc];
         const float dx = (float)(key_x(b) - key_x(a)), dy = (float)(key_y(b) - key_y(a));
         const float len = __fsqrt_rn(sq_len(dx, dy));
@@ -432,9 +586,7 @@ __global__ void k_word_rect(WordP p) {
             t0 = t < t0 ? t : t0;
             t1 = t > t1 ? t : t1;
         }
-        const float area = __fmul_rn(__fsub_rn(s1, s0), __fsub_rn(t1, t0));
-        if (area < best) {
-            best = area;
+        if (rc) {
             const float sc = __fmul_rn(__fadd_rn(s0, s1), 0.5f), tc = __fmul_rn(__fadd_rn(t0, t1), 0.5f);
             rc[0] = __fadd_rn(__fadd_rn((float)key_x(a), __fmul_rn(ux, sc)), __fmul_rn(-uy, tc));
             rc[1] = __fadd_rn(__fadd_rn((float)key_y(a), __fmul_rn(uy, sc)), __fmul_rn(ux, tc));
@@ -443,12 +595,21 @@ __global__ void k_word_rect(WordP p) {
             rc[4] = __fsub_rn(s1, s0);
             rc[5] = __fsub_rn(t1, t0);
         }
-    }
-    rc[4] = __fadd_rn(rc[4], __fmul_rn(2.f, __fadd_rn(p.expand, p.expand_x)));
-    rc[5] = __fadd_rn(rc[5], __fmul_rn(2.f, p.expand));
+        return __fmul_rn(__fsub_rn(s1, s0), __fsub_rn(t1, t0));
+    };
+    for (int i = tid; i < hc; i += kWT)
+        atomicMin(&s_best, ((unsigned long long)__float_as_uint(edge(i, nullptr)) << 32) | (uint32_t)i);
+    __syncthreads();
+    if (tid == 0) {
+        float rc[6];
+        edge((int)(uint32_t)s_best, rc);
+        rc[4] = __fadd_rn(rc[4], __fmul_rn(2.f, __fadd_rn(p.expand, p.expand_x)));
+        rc[5] = __fadd_rn(rc[5], __fmul_rn(2.f, p.expand));
+        float *out = p.rect + 6 * (int64_t)k;
 #pragma unroll
-    for (int i = 0; i < 6; i++) out[i] = rc[i];
-    p.valid[k] = __fmul_rn(rc[4], rc[5]) >= p.min_area;
+        for (int i = 0; i < 6; i++) out[i] = rc[i];
+        p.valid[k] = __fmul_rn(rc[4], rc[5]) >= p.min_area;
+    }
 }
 
 __global__ void k_word_pack(const float *__restrict__ rect, const int *__restrict__ valid, const int *__restrict__ pos,
@@ -549,7 +710,8 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     }
     scan_i32(c, (const int *)len->p, C, (int *)ptoff->p, d_tot);
     const int64_t slots = (int64_t)read_int(c, d_tot) + C;
-    BufP pts = alloc(c, (size_t)slots * 4), keep = alloc(c, (size_t)slots), stack = alloc(c, (size_t)slots * 8);
+    BufP pts = alloc(c, (size_t)slots * 4), keep = alloc(c, (size_t)slots), sega = alloc(c, (size_t)slots * 8);
+    BufP segb = alloc(c, (size_t)slots * 8), pref = alloc(c, (size_t)slots * 4), best = alloc(c, (size_t)slots * 8);
     BufP keys = alloc(c, (size_t)slots * 4), hull = alloc(c, (size_t)(2 * slots + C) * 4);
     BufP rect = alloc(c, (size_t)C * 24), valid = alloc(c, (size_t)C * 4), vpos = alloc(c, (size_t)C * 4);
     WordP p;
@@ -564,7 +726,10 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     p.C = C;
     p.pts = (short2 *)pts->p;
     p.keep = (uint8_t *)keep->p;
-    p.stack = (int2 *)stack->p;
+    p.seg_a = (int2 *)sega->p;
+    p.seg_b = (int2 *)segb->p;
+    p.pref = (int *)pref->p;
+    p.best = (unsigned long long *)best->p;
     p.keys = (uint32_t *)keys->p;
     p.hull = (uint32_t *)hull->p;
     p.rect = (float *)rect->p;
@@ -575,7 +740,7 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     p.status = c->status;
     {
         Prof pf(c, "word_rect", 0, 0);
-        k_word_rect<<<blocks(C, 64), 64, 0, c->stream>>>(p);
+        k_word_rect<<<C, kWT, 0, c->stream>>>(p);
         WOCR_LAUNCHED(c);
     }
     scan_i32(c, (const int *)valid->p, C, (int *)vpos->p, d_tot);

@@ -79,11 +79,15 @@ class Gpu:
             npg = 1 if m.ndim == 2 else m.shape[0]
             src = L.ptr(m)
         counts = np.zeros(max(npg, 1), np.int32)
-        L.check(L.lib().wocr_word_rects(self.h, src, npg, int(w), int(h), int(bool(d_mask)), expand, expand_x,
-                                        min_area, None, 0, L.ptr(counts)))
-        out = np.zeros((max(int(counts[:npg].sum()), 1), 6), np.float32)
-        L.check(L.lib().wocr_word_rects(self.h, src, npg, int(w), int(h), int(bool(d_mask)), expand, expand_x,
-                                        min_area, L.ptr(out), out.shape[0], L.ptr(counts)))
+        out = np.zeros((4096 * max(npg, 1), 6), np.float32)
+        for _ in range(2):  # again only when the first guess of the capacity was short (status 8)
+            st = L.lib().wocr_word_rects(self.h, src, npg, int(w), int(h), int(bool(d_mask)), expand, expand_x,
+                                         min_area, L.ptr(out), out.shape[0], L.ptr(counts))
+            if st == 8 and counts[:npg].sum() > out.shape[0]:
+                out = np.zeros((int(counts[:npg].sum()), 6), np.float32)
+                continue
+            L.check(st)
+            break
         ends = np.cumsum(counts[:npg])
         return [out[e - k:e] for e, k in zip(ends, counts[:npg])]
 

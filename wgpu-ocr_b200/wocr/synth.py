@@ -444,6 +444,30 @@ def _page_layout(seed: int, w: int, h: int, bands: int, line_h: int):
     return out
 
 
+def page_word_mask(seed: int = 1, w: int = 2550, h: int = 3300, bands: int = 36, line_h: int = 40,
+                   grow_x: int = 8, grow_y: int = 3) -> np.ndarray:
+    """The text mask a trained detector gives for page(seed, ...): bool [h, w], each ink
+    rectangle grown by grow_x / grow_y (so the glyph gaps of a word close and the word gaps stay
+    open), its top and bottom edges jittered by up to 2 px so the word outlines are ragged."""
+    rng = np.random.default_rng(seed + 4000)
+    m = np.zeros((h, w), bool)
+    for y0, y1, rects in _page_layout(seed, w, h, bands, line_h):
+        for x0, x1 in rects:
+            t, b = y0 - grow_y + int(rng.integers(-2, 3)), y1 + grow_y + int(rng.integers(-2, 3))
+            m[max(t, 0):min(b, h), max(x0 - grow_x, 0):min(x1 + grow_x, w)] = True
+    return m
+
+
+def pack_mask(m: np.ndarray) -> np.ndarray:
+    """A bool mask [..., h, w] as the library's bit mask: uint32 [..., h, ceil(w / 32)], bit b of
+    word j = pixel 32 j + b."""
+    w = m.shape[-1]
+    words = (w + 31) // 32
+    pad = np.zeros(m.shape[:-1] + (words * 32,), bool)
+    pad[..., :w] = m
+    return np.packbits(pad.reshape(m.shape[:-1] + (words, 32)), axis=-1, bitorder="little").view("<u4")[..., 0].copy()
+
+
 def page(seed: int = 1, w: int = 2550, h: int = 3300, bands: int = 36, line_h: int = 40,
          ink: int = 20) -> np.ndarray:
     """A US Letter page at 300 dpi as RGB u8 [h, w, 3]: white, with `bands` text lines of
