@@ -25,7 +25,8 @@ def test_word_rects_bit_exact(gpu, k, params):
 
 
 def test_word_rects_pages_and_device_masks(gpu):
-    """Pages in one call equal pages one by one; a device mask equals the host mask."""
+    """Pages in one call equal pages one by one; a device mask equals the host mask; bits past
+    the page's width are ignored."""
     import torch
 
     rng = np.random.default_rng(2)
@@ -38,6 +39,7 @@ def test_word_rects_pages_and_device_masks(gpu):
             m[y:y + rng.integers(2, 7), x:x + rng.integers(3, 20)] = True
         pages.append(pack_bits(m))
     bits = np.stack(pages)
+    bits[..., -1] |= np.uint32(0xffffffff << (w % 32) & 0xffffffff)  # set bits past the width are ignored
     got = gpu.word_rects(bits, w, h)
     assert len(got) == 4 and len(got[0]) == 0
     d = torch.from_numpy(bits.view(np.int32)).cuda()

@@ -31,10 +31,6 @@ constexpr uint32_t kNbX = 6800, kNbY = 43265;
 __device__ __forceinline__ int nb_dx(int d) { return (int)((kNbX >> (2 * d)) & 3u) - 1; }
 __device__ __forceinline__ int nb_dy(int d) { return (int)((kNbY >> (2 * d)) & 3u) - 1; }
 
-__device__ __forceinline__ bool on_px(const uint32_t *m, int words, int w, int h, int x, int y) {
-    return (unsigned)x < (unsigned)w && (unsigned)y < (unsigned)h && ((__ldg(m + (int64_t)y * words + (x >> 5)) >> (x & 31)) & 1u);
-}
-
 // transitions between pixel x - 1 and x for the 32 pixels of word j (bit b = x = 32 j + b),
 // none at x = 0 or at x >= w
 __device__ __forceinline__ uint32_t row_edges(const uint32_t *row, int j, int w) {
@@ -239,54 +235,88 @@ __global__ void k_ext_list(const int *__restrict__ run_x, const uint8_t *__restr
 
 // ---- border following ------------------------------------------------------------------------
 
+// Columns wx0 .. wx0 + 31 of row y as bits (pixels off the page read 0).
+__device__ __forceinline__ uint32_t row_win(const uint32_t *m, int words, int w, int h, int y, int wx0) {
+    if ((unsigned)y >= (unsigned)h) return 0u;
+    const uint32_t *row = m + (int64_t)y * words;
+    const int j = wx0 >> 5;  // floor, also for wx0 < 0
+    const uint32_t lo = (unsigned)j < (unsigned)words ? __ldg(row + j) : 0u;
+    const uint32_t hi = (unsigned)(j + 1) < (unsigned)words ? __ldg(row + j + 1) : 0u;
+    uint32_t v = __funnelshift_r(lo, hi, wx0 & 31);
+    const int valid = w - wx0;
+    if (valid < 32) v &= valid <= 0 ? 0u : (1u << valid) - 1u;
+    return v;
+}
+
 // Algorithm 1 (3.1)-(3.5) from the outer-border start (x, y) entered from its left neighbour:
-// the number of border points; with WRITE, the points go to out.  A border is at most 4 points
-// a pixel; past that the status word is set and the trace stops.
+// the number of border points; with WRITE, the points go to out.  The rows y - 1 .. y + 1 of the
+// current point, columns wx0 .. wx0 + 31, stay in registers: a step down or up loads one row, a
+// step that leaves the columns reloads the three.  (3.1) takes the first set neighbour clockwise
+// from the left one, (3.3) the first counterclockwise from the one after the previous point: a
+// rotate of the 8 neighbour bits (bit d = neighbour d) and a leading-zero count.  A border is at
+// most 4 points a pixel; past that the status word is set and the trace stops.
 template <bool WRITE>
 __device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, short2 *out, int *status) {
-    int d1 = -1;
-    for (int d = 0; d < 8; d++)
-        if (on_px(m, words, w, h, x + nb_dx(d), y + nb_dy(d))) {
-            d1 = d;
-            break;
-        }
-    if (d1 < 0) {
+    int wx0 = x - 16;
+    uint32_t up = row_win(m, words, w, h, y - 1, wx0), mid = row_win(m, words, w, h, y, wx0),
+             dn = row_win(m, words, w, h, y + 1, wx0);
+    auto nbits = [&](int xx) -> uint32_t {
+        const int b = xx - 1 - wx0;
+        const uint32_t u = up >> b & 7u, c = mid >> b & 7u, d = dn >> b & 7u;
+        return (c & 1u) | (u & 1u) << 1 | (u >> 1 & 1u) << 2 | (u >> 2 & 1u) << 3 | (c >> 2 & 1u) << 4 |
+               (d >> 2 & 1u) << 5 | (d >> 1 & 1u) << 6 | (d & 1u) << 7;
+    };
+    uint32_t nb = nbits(x);
+    if (nb == 0) {
         if (WRITE) out[0] = make_short2((short)x, (short)y);
         return 1;
     }
+    const int d1 = __ffs(nb) - 1;
     const int x1 = x + nb_dx(d1), y1 = y + nb_dy(d1);
     int x3 = x, y3 = y, e = d1, n = 0;
     const int64_t cap = 4 * (int64_t)w * h + 8;
     for (;;) {
         if (WRITE) out[n] = make_short2((short)x3, (short)y3);
         n++;
-        int x4 = x3, y4 = y3, d4 = e;
-        for (int k = 1; k <= 8; k++) {
-            const int d = (e - k) & 7, xx = x3 + nb_dx(d), yy = y3 + nb_dy(d);
-            if (on_px(m, words, w, h, xx, yy)) {
-                x4 = xx;
-                y4 = yy;
-                d4 = d;
-                break;
-            }
-        }
-        if (x4 == x && y4 == y && x3 == x1 && y3 == y1) break;
-        if (n >= cap) {
+        // counterclockwise from e - 1: bit t -> 7, t - 1 -> 6, ...; the first set is the highest
+        const int t = (e - 1) & 7;
+        const uint32_t rot = ((nb << (7 - t)) | (nb >> (t + 1))) & 0xffu;
+        if (rot == 0u || n >= cap) {  // the previous point is always set: a broken mask read
             atomicExch(status, 40);
             break;
         }
+        const int d4 = (t - (7 - (31 - __clz(rot)))) & 7;
+        const int x4 = x3 + nb_dx(d4), y4 = y3 + nb_dy(d4);
+        if (x4 == x && y4 == y && x3 == x1 && y3 == y1) break;
         e = (d4 + 4) & 7;  // from the new (i3, j3) back to the old one
+        if (x4 - 1 < wx0 || x4 + 1 > wx0 + 31) {
+            wx0 = x4 - 16;
+            up = row_win(m, words, w, h, y4 - 1, wx0);
+            mid = row_win(m, words, w, h, y4, wx0);
+            dn = row_win(m, words, w, h, y4 + 1, wx0);
+        } else if (y4 > y3) {
+            up = mid;
+            mid = dn;
+            dn = row_win(m, words, w, h, y4 + 1, wx0);
+        } else if (y4 < y3) {
+            dn = mid;
+            mid = up;
+            up = row_win(m, words, w, h, y4 - 1, wx0);
+        }
         x3 = x4;
         y3 = y4;
+        nb = nbits(x3);
     }
     return n;
 }
 
-__global__ void k_trace_len(const uint32_t *__restrict__ mask, int words, int w, int h,
-                            const int *__restrict__ run_x, const int *__restrict__ run_row,
-                            const int *__restrict__ comp_run, int C, int *__restrict__ len, int *status) {
-    const int k = blockIdx.x * blockDim.x + threadIdx.x;
-    if (k >= C) return;
+// A warp per component, lane 0 tracing: lanes of one warp would wait on each other's loads.
+__global__ void __launch_bounds__(32) k_trace_len(const uint32_t *__restrict__ mask, int words, int w, int h,
+                                                  const int *__restrict__ run_x, const int *__restrict__ run_row,
+                                                  const int *__restrict__ comp_run, int C, int *__restrict__ len,
+                                                  int *status) {
+    const int k = blockIdx.x;
+    if (k >= C || threadIdx.x != 0) return;
     const int r = comp_run[k], row = run_row[r];
     const uint32_t *m = mask + (int64_t)(row / h) * h * words;
     len[k] = follow<false>(m, words, w, h, run_x[r], row % h, nullptr, status);
@@ -704,7 +734,7 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     WOCR_LAUNCHED(c);
     {
         Prof pf(c, "word_trace", 0, 0);
-        k_trace_len<<<blocks(C, 64), 64, 0, c->stream>>>(mask, words, w, h, run_x, run_row, (const int *)crun->p, C,
+        k_trace_len<<<C, 32, 0, c->stream>>>(mask, words, w, h, run_x, run_row, (const int *)crun->p, C,
                                                          (int *)len->p, c->status);
         WOCR_LAUNCHED(c);
     }
