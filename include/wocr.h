@@ -233,6 +233,24 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
 int32_t wocr_ppdet_mask(wocr_ndgraph *g, float thresh, uint32_t *mask, int64_t cap, int32_t *ow, int32_t *oh);
 int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float *scores);
 
+/* `ppdet::boxes` (src/ppdet.rs:87-132) with the map on the device: the p > thresh mask, its
+ * external contours simplified (Douglas-Peucker, epsilon 2) and their minimum-area rectangles
+ * (all on the device, as wocr_word_rects), kept when min(width, height) >= min_size and the
+ * device `score` >= box_thresh, unclipped by w h unclip_ratio / (2 (w + h)) on every side,
+ * dropped when their smaller side is below min_size + 2, scaled to the page (centre by to_page,
+ * sides by the factors' mean) and put in reading order (top edge; boxes whose tops are within
+ * 10 px ordered by their left edge).  boxes[6 k ..] = center x, center y, up x, up y, width,
+ * height; *n = the count (boxes = NULL with cap = 0 only counts; a smaller cap fails with
+ * WOCR_ERR_CAPACITY).  ppdet::Db::default(): thresh 0.2, box_thresh 0.45, unclip_ratio 1.4,
+ * min_size 3.
+ *   wocr_ppdet_boxes: on the map of the handle's last wocr_ppdet_page, with its to_page;
+ *   wocr_db_boxes:    on a map [h][w] in host memory, or device memory when prob_on_device. */
+int32_t wocr_ppdet_boxes(wocr_ndgraph *g, float thresh, float box_thresh, float unclip_ratio, float min_size,
+                         float *boxes, int32_t cap, int32_t *n);
+int32_t wocr_db_boxes(wocr_ctx *ctx, const float *prob, int32_t w, int32_t h, int32_t prob_on_device,
+                      const float *to_page, float thresh, float box_thresh, float unclip_ratio, float min_size,
+                      float *boxes, int32_t cap, int32_t *n);
+
 /* Word rectangles of binary page masks: `word_rects` (src/bin/ocr-bench.rs:38-60), i.e. the
  * external contours (find_contours, External), each simplified (Douglas-Peucker, epsilon 2), its
  * minimum-area rectangle resized to width + 2 (expand + expand_x) x height + 2 expand and kept

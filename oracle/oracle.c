@@ -933,3 +933,88 @@ int oracle_word_rects(const uint32_t *mask, int w, int h, float expand, float ex
     free(cs);
     return n;
 }
+
+/* A box's bounding rectangle (its four corners: center +- up * height / 2 +- across * width / 2)
+ * for the reading-order sort of src/ppdet.rs:117-130. */
+static void db_bounds(const float *r, float *left, float *top) {
+    float hw = r[4] / 2.0f, hh = r[5] / 2.0f, lx = INFINITY, ty = INFINITY;
+    for (int sa = -1; sa <= 1; sa += 2)
+        for (int sb = -1; sb <= 1; sb += 2) {
+            float px = r[0] + sa * hh * r[2] + sb * hw * -r[3];
+            float py = r[1] + sa * hh * r[3] + sb * hw * r[2];
+            lx = px < lx ? px : lx;
+            ty = py < ty ? py : ty;
+        }
+    *left = lx;
+    *top = ty;
+}
+
+/*
+ * `ppdet::boxes` (src/ppdet.rs:87-132): DB text boxes of a probability map (w x h) in page
+ * coordinates, in reading order.  The mask is p > thresh; each external contour, simplified
+ * (epsilon 2), gives its minimum-area rectangle (the word_rects restatement above, no expand);
+ * it is kept when min(width, height) >= min_size and its `score` >= box_thresh, then unclipped
+ * by d = w h unclip_ratio / max(2 (w + h), 1e-6) on every side, dropped when min side <
+ * min_size + 2, and scaled to the page (center by to_page, sides by their mean).  Sorted by the
+ * top of the bounding rectangle (stable), then boxes whose tops are within 10 px move left of
+ * their predecessors by an insertion pass.  Returns the number of boxes (filled up to cap).
+ */
+int oracle_db_boxes(const float *prob, int w, int h, const float *to_page, float thresh, float box_thresh,
+                    float unclip_ratio, float min_size, float *out, int cap) {
+    const int words = (w + 31) / 32;
+    uint32_t *bits = (uint32_t *)calloc((size_t)words * h, 4);
+    for (int y = 0; y < h; y++)
+        for (int x = 0; x < w; x++)
+            if (prob[(size_t)y * w + x] > thresh) bits[(size_t)y * words + x / 32] |= 1u << (x % 32);
+    int nr = oracle_word_rects(bits, w, h, 0.f, 0.f, -INFINITY, NULL, 0);
+    float *rs = (float *)malloc(sizeof(float) * 6 * (size_t)(nr > 0 ? nr : 1));
+    oracle_word_rects(bits, w, h, 0.f, 0.f, -INFINITY, rs, nr);
+    free(bits);
+    float *keep = (float *)malloc(sizeof(float) * 6 * (size_t)(nr > 0 ? nr : 1));
+    int n = 0;
+    const float s = (to_page[0] + to_page[1]) / 2.0f;
+    for (int i = 0; i < nr; i++) {
+        const float *r = rs + 6 * (size_t)i;
+        float rw = r[4], rh = r[5];
+        if ((rw < rh ? rw : rh) < min_size || oracle_db_score(prob, w, h, r) < box_thresh) continue;
+        float per = 2.0f * (rw + rh);
+        float d = rw * rh * unclip_ratio / (per > 1e-6f ? per : 1e-6f);
+        float nw = rw + 2.0f * d, nh = rh + 2.0f * d;
+        if ((nw < nh ? nw : nh) < min_size + 2.0f) continue;
+        float *o = keep + 6 * (size_t)n++;
+        o[0] = r[0] * to_page[0];
+        o[1] = r[1] * to_page[1];
+        o[2] = r[2];
+        o[3] = r[3];
+        o[4] = nw * s;
+        o[5] = nh * s;
+    }
+    free(rs);
+    /* stable sort by top (insertion sort keeps equal keys in order) */
+    float *tops = (float *)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    float *lefts = (float *)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+    for (int i = 0; i < n; i++) db_bounds(keep + 6 * (size_t)i, &lefts[i], &tops[i]);
+    for (int i = 1; i < n; i++)
+        for (int j = i; j > 0 && tops[j] < tops[j - 1]; j--) {
+            float t[6];
+            memcpy(t, keep + 6 * (size_t)j, sizeof t);
+            memcpy(keep + 6 * (size_t)j, keep + 6 * (size_t)(j - 1), sizeof t);
+            memcpy(keep + 6 * (size_t)(j - 1), t, sizeof t);
+            float u = tops[j]; tops[j] = tops[j - 1]; tops[j - 1] = u;
+            u = lefts[j]; lefts[j] = lefts[j - 1]; lefts[j - 1] = u;
+        }
+    for (int i = 0; i < n; i++)
+        for (int j = i; j > 0 && fabsf(tops[j] - tops[j - 1]) < 10.0f && lefts[j] < lefts[j - 1]; j--) {
+            float t[6];
+            memcpy(t, keep + 6 * (size_t)j, sizeof t);
+            memcpy(keep + 6 * (size_t)j, keep + 6 * (size_t)(j - 1), sizeof t);
+            memcpy(keep + 6 * (size_t)(j - 1), t, sizeof t);
+            float u = tops[j]; tops[j] = tops[j - 1]; tops[j - 1] = u;
+            u = lefts[j]; lefts[j] = lefts[j - 1]; lefts[j - 1] = u;
+        }
+    if (out) memcpy(out, keep, sizeof(float) * 6 * (size_t)(n < cap ? n : cap));
+    free(keep);
+    free(tops);
+    free(lefts);
+    return n;
+}

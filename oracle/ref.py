@@ -71,12 +71,14 @@ def lib():
             "oracle_db_score": [_f, _I, _I, _f],
             "oracle_contours": [_u32, _I, _I, _i32, _I, _i32, _i32, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)],
             "oracle_word_rects": [_u32, _I, _I, _F, _F, _F, _f, _I],
+            "oracle_db_boxes": [_f, _I, _I, _f, _F, _F, _F, _F, _f, _I],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = ctypes.c_float if name in ("oracle_erf", "oracle_act", "oracle_db_score") else (
-                ctypes.c_int if name in ("oracle_threads", "oracle_pp_line", "oracle_contours", "oracle_word_rects")
+                ctypes.c_int if name in ("oracle_threads", "oracle_pp_line", "oracle_contours", "oracle_word_rects",
+                                 "oracle_db_boxes")
                 else None)
         _lib = L
     return _lib
@@ -165,6 +167,20 @@ def word_rects(bits: np.ndarray, w: int, h: int, expand: float = 3.0, expand_x: 
     n = lib().oracle_word_rects(_p(bits, _u32), w, h, expand, expand_x, min_area, None, 0)
     out = np.zeros((max(n, 1), 6), np.float32)
     lib().oracle_word_rects(_p(bits, _u32), w, h, expand, expand_x, min_area, _p(out), n)
+    return out[:n]
+
+
+def db_boxes(prob: np.ndarray, to_page, thresh: float = 0.2, box_thresh: float = 0.45, unclip_ratio: float = 1.4,
+             min_size: float = 3.0) -> np.ndarray:
+    """ppdet::boxes (src/ppdet.rs:87-132) of a probability map [h, w]: float32 [n, 6] boxes
+    [cx, cy, up_x, up_y, width, height] in page coordinates, in reading order (defaults:
+    ppdet::Db::default())."""
+    prob = np.ascontiguousarray(prob, np.float32)
+    h, w = prob.shape
+    tp = np.ascontiguousarray(to_page, np.float32)
+    n = lib().oracle_db_boxes(_p(prob), w, h, _p(tp), thresh, box_thresh, unclip_ratio, min_size, None, 0)
+    out = np.zeros((max(n, 1), 6), np.float32)
+    lib().oracle_db_boxes(_p(prob), w, h, _p(tp), thresh, box_thresh, unclip_ratio, min_size, _p(out), n)
     return out[:n]
 
 

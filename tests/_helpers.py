@@ -80,3 +80,36 @@ def word_masks():
     out.append(np.zeros((5, 7), bool))
     out.append(np.ones((6, 33), bool))
     return out
+
+
+def db_map(seed: int = 0, w: int = 736, h: int = 960) -> np.ndarray:
+    """A DB probability map [h, w] like a trained detector's on a text page: low background,
+    bands of word blobs at several confidences (some below box_thresh), rotated blobs, tiny
+    blobs (below min_size), softened by a 3 x 3 box blur."""
+    rng = np.random.default_rng(seed)
+    p = rng.random((h, w), dtype=np.float32) * np.float32(0.15)
+    for band in range((h - 40) // 30):
+        y0, bh = 20 + band * 30, int(rng.integers(6, 15))
+        x = int(rng.integers(5, 60))
+        while x < w - 40:
+            bw = int(rng.integers(12, 120))
+            v = np.float32(rng.choice([0.92, 0.8, 0.5, 0.4, 0.33]))
+            blk = p[y0:y0 + bh, x:x + bw]
+            np.maximum(blk, v - rng.random(blk.shape, dtype=np.float32) * np.float32(0.1), out=blk)
+            x += bw + int(rng.integers(4, 30))
+    yy, xx = np.mgrid[:h, :w].astype(np.float32)
+    for _ in range(8):
+        cx, cy, a = rng.uniform(60, w - 60), rng.uniform(60, h - 60), rng.uniform(-0.6, 0.6)
+        hw, hh = rng.uniform(10, 50), rng.uniform(3, 10)
+        along = (xx - cx) * np.cos(a) + (yy - cy) * np.sin(a)
+        across = -(xx - cx) * np.sin(a) + (yy - cy) * np.cos(a)
+        p[(np.abs(along) <= hw) & (np.abs(across) <= hh)] = np.float32(0.85)
+    for _ in range(20):
+        y, x = int(rng.integers(0, h - 2)), int(rng.integers(0, w - 2))
+        p[y:y + 2, x:x + 2] = np.float32(0.9)
+    q = np.pad(p, 1, mode="edge")
+    acc = np.zeros_like(p)
+    for dy in range(3):
+        for dx in range(3):
+            acc += q[dy:dy + h, dx:dx + w]
+    return (acc / np.float32(9)).astype(np.float32)

@@ -81,3 +81,32 @@ def test_word_rects_detection_mask(gpu):
     want = ref.word_rects(bits, 2550, 3300)
     assert len(want) > 0
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("seed,thresh", [(1, 0.3), (2, 0.2), (3, 0.5)])
+def test_db_boxes_bit_exact(gpu, seed, thresh):
+    """ppdet::boxes on the device (`wocr_db_boxes`, host and device maps) equals the C
+    restatement: the same boxes, bit for bit, in the same reading order."""
+    import torch
+
+    from _helpers import db_map
+
+    prob = db_map(seed)
+    tp = (3.4647, 3.4375)
+    want = ref.db_boxes(prob, tp, thresh)
+    assert len(want) > 10
+    np.testing.assert_array_equal(gpu.db_boxes(prob, tp, thresh), want)
+    d = torch.from_numpy(prob).cuda()
+    np.testing.assert_array_equal(gpu.db_boxes(None, tp, thresh, d_prob=d.data_ptr(), w=prob.shape[1],
+                                               h=prob.shape[0]), want)
+
+
+def test_ppdet_boxes_on_detector_map(gpu):
+    """The DB boxes of a config 4 page's map, straight from the detector's resident map."""
+    g = wocr.NdGraph(gpu, synth.pp_det_model())
+    try:
+        prob, tp = g.ppdet_page(synth.page(3, 1275, 1650), 1275, 1650, 960)
+        got = g.db_boxes(0.3)
+    finally:
+        g.close()
+    np.testing.assert_array_equal(got, ref.db_boxes(prob, tp, 0.3))

@@ -338,3 +338,47 @@ def test_word_rects_oracle_properties():
     one = np.zeros((8, 8), bool)
     one[3, 3] = True
     assert len(ref.word_rects(pack_bits(one), 8, 8, min_area=0)) == 0
+
+
+def test_db_boxes_oracle_steps():
+    """oracle_db_boxes against its steps restated in numpy on the oracle's own pieces
+    (word_rects without expand, db_score): the size and score filters, unclip, page scaling and
+    the reading order of src/ppdet.rs:87-132."""
+    from _helpers import db_map
+
+    prob = db_map(1)
+    h, w = prob.shape
+    tp = np.float32([3.4647, 3.4375])
+    got = ref.db_boxes(prob, tp, 0.3)
+    f = np.float32
+    rects = ref.word_rects(pack_bits(prob > f(0.3)), w, h, 0.0, 0.0, -np.inf)
+    keep = []
+    for r in rects:
+        if min(r[4], r[5]) < f(3) or ref.db_scores(prob, r[None])[0] < f(0.45):
+            continue
+        d = f(r[4] * r[5] * f(1.4)) / max(f(2) * f(r[4] + r[5]), f(1e-6))
+        nw, nh = f(r[4] + f(2) * d), f(r[5] + f(2) * d)
+        if min(nw, nh) < f(5):
+            continue
+        s = f(f(tp[0] + tp[1]) / f(2))
+        keep.append([r[0] * tp[0], r[1] * tp[1], r[2], r[3], nw * s, nh * s])
+    keep = np.float32(keep)
+    assert 30 < len(keep) < len(rects)
+
+    def bounds(r):
+        hw, hh = r[4] / f(2), r[5] / f(2)
+        xs = [r[0] + f(sa) * hh * r[2] + f(sb) * hw * -r[3] for sa in (-1, 1) for sb in (-1, 1)]
+        ys = [r[1] + f(sa) * hh * r[3] + f(sb) * hw * r[2] for sa in (-1, 1) for sb in (-1, 1)]
+        return min(xs), min(ys)
+
+    order = sorted(range(len(keep)), key=lambda i: bounds(keep[i])[1])
+    for i in range(len(order)):
+        j = i
+        while j > 0:
+            (la, ta), (lb, tb) = bounds(keep[order[j - 1]]), bounds(keep[order[j]])
+            if abs(tb - ta) < 10 and lb < la:
+                order[j - 1], order[j] = order[j], order[j - 1]
+                j -= 1
+            else:
+                break
+    np.testing.assert_array_equal(got, keep[order])

@@ -194,6 +194,7 @@ struct wocr_ndgraph {
     BufP map_buf;
     const float *map = nullptr;
     int map_w = 0, map_h = 0;
+    float map_to_page[2] = {1.f, 1.f};
     ~wocr_ndgraph() {
         for (auto &r : replays) r.reset();
     }
@@ -1358,6 +1359,8 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
         det_input_sizes(w, h, max_side, &ow, &oh);
         if (ow_out) *ow_out = ow;
         if (oh_out) *oh_out = oh;
+        g->map_to_page[0] = (float)w / (float)ow;
+        g->map_to_page[1] = (float)h / (float)oh;
         if (to_page) {
             to_page[0] = (float)w / (float)ow;
             to_page[1] = (float)h / (float)oh;
@@ -1444,6 +1447,129 @@ int32_t wocr_ppdet_mask(wocr_ndgraph *g, float thresh, uint32_t *mask, int64_t c
     });
 }
 
+namespace {
+
+// `score` (src/ppdet.rs:63-83) of rects [n][6] on the device map prob (w x h), into host scores.
+void db_score_boxes(Ctx *c, const float *prob, int w, int h, const float *rects, int n, float *scores) {
+    if (n == 0) return;
+    // the scan rectangle: the box's bounding rectangle (its four corners), floor / ceil,
+    // clamped to the map as score() clamps it
+    std::vector<k::DbBox> bx((size_t)n);
+    for (int i = 0; i < n; i++) {
+        const float *r = rects + 6 * (size_t)i;
+        k::DbBox &b = bx[i];
+        b.cx = r[0];
+        b.cy = r[1];
+        b.ux = r[2];
+        b.uy = r[3];
+        b.hw = r[4] / 2.0f;
+        b.hh = r[5] / 2.0f;
+        float lo_x = INFINITY, hi_x = -INFINITY, lo_y = INFINITY, hi_y = -INFINITY;
+        for (int sa = -1; sa <= 1; sa += 2)
+            for (int sb = -1; sb <= 1; sb += 2) {
+                const float px = b.cx + sa * b.hh * b.ux + sb * b.hw * -b.uy;
+                const float py = b.cy + sa * b.hh * b.uy + sb * b.hw * b.ux;
+                lo_x = std::min(lo_x, px), hi_x = std::max(hi_x, px);
+                lo_y = std::min(lo_y, py), hi_y = std::max(hi_y, py);
+            }
+        // one pixel wider on every side than floor / ceil of the corners: the pixels that pass
+        // the inside test lie in the box's bounding rectangle whatever the corner rounding
+        // `as usize`: saturating, NaN to 0
+        auto to_idx = [](float v) -> int64_t { return v > 0.f ? (v < 4e9f ? (int64_t)v : (int64_t)4e9) : 0; };
+        b.x0 = (int)std::min<int64_t>(to_idx(std::floor(lo_x) - 1.f), w);
+        b.y0 = (int)std::min<int64_t>(to_idx(std::floor(lo_y) - 1.f), h);
+        b.x1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_x) + 1.f), std::max(w - 1, 0));
+        b.y1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_y) + 1.f), std::max(h - 1, 0));
+    }
+    BufP db = alloc(c, bx.size() * sizeof(k::DbBox)), ds = alloc(c, (size_t)n * 4);
+    WOCR_CUDA(cudaMemcpyAsync(db->p, bx.data(), bx.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice, c->stream));
+    k::db_scores(c, prob, w, h, (const k::DbBox *)db->p, n, (float *)ds->p);
+    d2h(c, scores, ds->p, (size_t)n * 4);
+    sync_bounded(c, 0);
+}
+
+// A box's left and top (the minimum of its four corners) for the reading-order sort.
+void db_bounds(const float *r, float *left, float *top) {
+    const float hw = r[4] / 2.0f, hh = r[5] / 2.0f;
+    float lx = INFINITY, ty = INFINITY;
+    for (int sa = -1; sa <= 1; sa += 2)
+        for (int sb = -1; sb <= 1; sb += 2) {
+            const float px = r[0] + sa * hh * r[2] + sb * hw * -r[3];
+            const float py = r[1] + sa * hh * r[3] + sb * hw * r[2];
+            lx = px < lx ? px : lx;
+            ty = py < ty ? py : ty;
+        }
+    *left = lx;
+    *top = ty;
+}
+
+// `ppdet::boxes` (src/ppdet.rs:87-132) on a device map: the p > thresh mask, its external
+// contours' minimum-area rectangles (simplified, epsilon 2) and their scores on the device; the
+// size checks, unclip, page scaling and reading order on the host, as the reference orders them.
+std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float *to_page, float thresh,
+                            float box_thresh, float unclip_ratio, float min_size) {
+    const int words = (w + 31) / 32;
+    BufP bits = alloc(c, (size_t)words * h * 4);
+    k::db_mask(c, prob, w, h, thresh, (uint32_t *)bits->p);
+    k::WordRects wr = k::word_rects(c, (const uint32_t *)bits->p, 1, w, h, 0.f, 0.f, -INFINITY);
+    std::vector<float> rs((size_t)wr.n * 6);
+    d2h(c, rs.data(), wr.rects->p, rs.size() * 4);
+    sync_bounded(c, 0);
+    std::vector<float> cand;
+    for (int i = 0; i < wr.n; i++) {
+        const float *r = rs.data() + 6 * (size_t)i;
+        if (std::min(r[4], r[5]) >= min_size) cand.insert(cand.end(), r, r + 6);
+    }
+    const int nc = (int)(cand.size() / 6);
+    std::vector<float> sc((size_t)nc);
+    db_score_boxes(c, prob, w, h, cand.data(), nc, sc.data());
+    std::vector<float> out;
+    const float s = (to_page[0] + to_page[1]) / 2.0f;
+    for (int i = 0; i < nc; i++) {
+        const float *r = cand.data() + 6 * (size_t)i;
+        if (sc[i] < box_thresh) continue;
+        const float rw = r[4], rh = r[5];
+        const float per = 2.0f * (rw + rh);
+        const float d = rw * rh * unclip_ratio / (per > 1e-6f ? per : 1e-6f);
+        const float nw = rw + 2.0f * d, nh = rh + 2.0f * d;
+        if (std::min(nw, nh) < min_size + 2.0f) continue;
+        const float o[6] = {r[0] * to_page[0], r[1] * to_page[1], r[2], r[3], nw * s, nh * s};
+        out.insert(out.end(), o, o + 6);
+    }
+    // stable by the top of the bounding rectangle, then boxes whose tops are within 10 px of
+    // their predecessor's by the left edge (one insertion pass)
+    const int n = (int)(out.size() / 6);
+    std::vector<int> idx((size_t)n);
+    std::vector<float> top((size_t)n), left((size_t)n);
+    for (int i = 0; i < n; i++) {
+        idx[i] = i;
+        db_bounds(out.data() + 6 * (size_t)i, &left[i], &top[i]);
+    }
+    std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return top[a] < top[b]; });
+    for (int i = 0; i < n; i++)
+        for (int j = i; j > 0; j--) {
+            const int a = idx[j - 1], b = idx[j];
+            if (std::fabs(top[b] - top[a]) < 10.0f && left[b] < left[a])
+                std::swap(idx[j - 1], idx[j]);
+            else
+                break;
+        }
+    std::vector<float> sorted(out.size());
+    for (int i = 0; i < n; i++)
+        std::memcpy(sorted.data() + 6 * (size_t)i, out.data() + 6 * (size_t)idx[i], 24);
+    return sorted;
+}
+
+void put_boxes(const std::vector<float> &b, float *boxes, int32_t cap, int32_t *n) {
+    const int nb = (int)(b.size() / 6);
+    *n = nb;
+    if (!boxes && cap == 0) return;
+    if (cap < nb) fail(WOCR_ERR_CAPACITY, "boxes holds " + std::to_string(cap) + " of " + std::to_string(nb));
+    if (nb) std::memcpy(boxes, b.data(), b.size() * 4);
+}
+
+}  // namespace
+
 int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float *scores) {
     return guard([&] {
         if (!g || (n > 0 && (!rects || !scores)) || n < 0) fail(WOCR_ERR_INVALID, "bad argument");
@@ -1451,41 +1577,38 @@ int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float 
         if (n == 0) return;
         Ctx *c = &g->ctx->c;
         RunScope rs(c, &g->last);
-        const int w = g->map_w, h = g->map_h;
-        // the scan rectangle: the box's bounding rectangle (its four corners), floor / ceil,
-        // clamped to the map as score() clamps it
-        std::vector<k::DbBox> bx((size_t)n);
-        for (int i = 0; i < n; i++) {
-            const float *r = rects + 6 * (size_t)i;
-            k::DbBox &b = bx[i];
-            b.cx = r[0];
-            b.cy = r[1];
-            b.ux = r[2];
-            b.uy = r[3];
-            b.hw = r[4] / 2.0f;
-            b.hh = r[5] / 2.0f;
-            float lo_x = INFINITY, hi_x = -INFINITY, lo_y = INFINITY, hi_y = -INFINITY;
-            for (int sa = -1; sa <= 1; sa += 2)
-                for (int sb = -1; sb <= 1; sb += 2) {
-                    const float px = b.cx + sa * b.hh * b.ux + sb * b.hw * -b.uy;
-                    const float py = b.cy + sa * b.hh * b.uy + sb * b.hw * b.ux;
-                    lo_x = std::min(lo_x, px), hi_x = std::max(hi_x, px);
-                    lo_y = std::min(lo_y, py), hi_y = std::max(hi_y, py);
-                }
-            // one pixel wider on every side than floor / ceil of the corners: the pixels that pass
-            // the inside test lie in the box's bounding rectangle whatever the corner rounding
-            // `as usize`: saturating, NaN to 0
-            auto to_idx = [](float v) -> int64_t { return v > 0.f ? (v < 4e9f ? (int64_t)v : (int64_t)4e9) : 0; };
-            b.x0 = (int)std::min<int64_t>(to_idx(std::floor(lo_x) - 1.f), w);
-            b.y0 = (int)std::min<int64_t>(to_idx(std::floor(lo_y) - 1.f), h);
-            b.x1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_x) + 1.f), std::max(w - 1, 0));
-            b.y1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_y) + 1.f), std::max(h - 1, 0));
+        db_score_boxes(c, g->map, g->map_w, g->map_h, rects, n, scores);
+    });
+}
+
+int32_t wocr_ppdet_boxes(wocr_ndgraph *g, float thresh, float box_thresh, float unclip_ratio, float min_size,
+                         float *boxes, int32_t cap, int32_t *n) {
+    return guard([&] {
+        if (!g || !n || cap < 0 || (cap > 0 && !boxes)) fail(WOCR_ERR_INVALID, "bad argument");
+        if (!g->map) fail(WOCR_ERR_INVALID, "no probability map: call wocr_ppdet_page first");
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        put_boxes(db_boxes(c, g->map, g->map_w, g->map_h, g->map_to_page, thresh, box_thresh, unclip_ratio, min_size),
+                  boxes, cap, n);
+    });
+}
+
+int32_t wocr_db_boxes(wocr_ctx *ctx, const float *prob, int32_t w, int32_t h, int32_t prob_on_device,
+                      const float *to_page, float thresh, float box_thresh, float unclip_ratio, float min_size,
+                      float *boxes, int32_t cap, int32_t *n) {
+    return guard([&] {
+        if (!ctx || !prob || !to_page || !n || cap < 0 || (cap > 0 && !boxes)) fail(WOCR_ERR_INVALID, "bad argument");
+        if (w <= 0 || h <= 0 || w > 32767 || h > 32767) fail(WOCR_ERR_INVALID, "bad map size");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        const float *dp = prob;
+        BufP up;
+        if (!prob_on_device) {
+            up = alloc(c, (size_t)w * h * 4);
+            WOCR_CUDA(cudaMemcpyAsync(up->p, prob, (size_t)w * h * 4, cudaMemcpyHostToDevice, c->stream));
+            dp = (const float *)up->p;
         }
-        BufP db = alloc(c, bx.size() * sizeof(k::DbBox)), ds = alloc(c, (size_t)n * 4);
-        WOCR_CUDA(cudaMemcpyAsync(db->p, bx.data(), bx.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice, c->stream));
-        k::db_scores(c, g->map, w, h, (const k::DbBox *)db->p, n, (float *)ds->p);
-        d2h(c, scores, ds->p, (size_t)n * 4);
-        sync_bounded(c, 0);
+        put_boxes(db_boxes(c, dp, w, h, to_page, thresh, box_thresh, unclip_ratio, min_size), boxes, cap, n);
     });
 }
 

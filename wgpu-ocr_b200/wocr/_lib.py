@@ -99,6 +99,9 @@ _SIGS = [
     ("wocr_last_transfer_bytes", c_i32, [c_void_p, c_i32, P(c_i64), P(c_i64)]),
     ("wocr_word_rects", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_i32, c_f32, c_f32, c_f32, c_void_p, c_i64,
                                 c_void_p]),
+    ("wocr_ppdet_boxes", c_i32, [c_void_p, c_f32, c_f32, c_f32, c_f32, c_void_p, c_i32, P(c_i32)]),
+    ("wocr_db_boxes", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_void_p, c_f32, c_f32, c_f32, c_f32, c_void_p,
+                              c_i32, P(c_i32)]),
     ("wocr_ppdet_mask", c_i32, [c_void_p, c_f32, c_void_p, c_i64, P(c_i32), P(c_i32)]),
     ("wocr_ppdet_scores", c_i32, [c_void_p, c_void_p, c_i32, c_void_p]),
     ("wocr_model_load", c_i32, [c_char_p, P(P(CModel))]),

@@ -91,6 +91,29 @@ class Gpu:
         ends = np.cumsum(counts[:npg])
         return [out[e - k:e] for e, k in zip(ends, counts[:npg])]
 
+    def db_boxes(self, prob, to_page, thresh: float = 0.2, box_thresh: float = 0.45, unclip_ratio: float = 1.4,
+                 min_size: float = 3.0, d_prob: int = 0, w: int = 0, h: int = 0) -> np.ndarray:
+        """ppdet::boxes (src/ppdet.rs:87-132) of a probability map (`wocr_db_boxes`): `prob`
+        float32 [h, w] in host memory, or d_prob, a device pointer to a w x h map."""
+        if d_prob:
+            src, dev = ctypes.c_void_p(d_prob), 1
+        else:
+            prob = np.ascontiguousarray(prob, np.float32)
+            h, w = prob.shape
+            src, dev = L.ptr(prob), 0
+        tp = np.ascontiguousarray(to_page, np.float32)
+        n = ctypes.c_int32()
+        out = np.zeros((1024, 6), np.float32)
+        for _ in range(2):  # again only when the first guess of the capacity was short (status 8)
+            st = L.lib().wocr_db_boxes(self.h, src, int(w), int(h), dev, L.ptr(tp), thresh, box_thresh, unclip_ratio,
+                                       min_size, L.ptr(out), out.shape[0], ctypes.byref(n))
+            if st == 8 and n.value > out.shape[0]:
+                out = np.zeros((n.value, 6), np.float32)
+                continue
+            L.check(st)
+            break
+        return out[:n.value].copy()
+
     def profile(self, on: bool):
         """Start (clearing earlier records) or stop per-kernel CUDA-event timing."""
         L.check(L.lib().wocr_ctx_profile(self.h, int(bool(on))))
@@ -322,6 +345,22 @@ class NdGraph(_Handle):
         bits = np.empty((oh.value, (ow.value + 31) // 32), np.uint32)
         L.check(L.lib().wocr_ppdet_mask(self.h, thresh, L.ptr(bits), bits.size, ctypes.byref(ow), ctypes.byref(oh)))
         return bits
+
+    def db_boxes(self, thresh: float = 0.2, box_thresh: float = 0.45, unclip_ratio: float = 1.4,
+                 min_size: float = 3.0) -> np.ndarray:
+        """ppdet::boxes (src/ppdet.rs:87-132) of the last `ppdet_page` map, on the device: float32
+        [n, 6] boxes [cx, cy, up_x, up_y, width, height] in page coordinates, reading order."""
+        n = ctypes.c_int32()
+        out = np.zeros((1024, 6), np.float32)
+        for _ in range(2):  # again only when the first guess of the capacity was short (status 8)
+            st = L.lib().wocr_ppdet_boxes(self.h, thresh, box_thresh, unclip_ratio, min_size, L.ptr(out),
+                                          out.shape[0], ctypes.byref(n))
+            if st == 8 and n.value > out.shape[0]:
+                out = np.zeros((n.value, 6), np.float32)
+                continue
+            L.check(st)
+            break
+        return out[:n.value].copy()
 
     def db_scores(self, rects) -> np.ndarray:
         """`score` (src/ppdet.rs:63-83) of each box [cx, cy, up_x, up_y, width, height] on the last
