@@ -47,11 +47,11 @@ def parse():
     p.add_argument("--pages", type=int, default=12, help="pages per GPU per step")
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
-    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines", "words1"],
+    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pp4", "pplines", "words1"],
                    help="det1 (default, the driver's line): config 1 detection; rec0 / pp3 / ppdet4: configs "
                         "0, 3 and 4 through their public calls; ppdb4: config 4 with the DB mask and box "
-                        "scores on the device; pplines: PP line extraction; words1: word rectangles of config 1 "
-                        "detection masks (secondary measurements)")
+                        "scores on the device; pp4: the full PP-OCRv6 page pipeline; pplines: PP line extraction; "
+                        "words1: word rectangles of config 1 detection masks (secondary measurements)")
     return p.parse_args()
 
 
@@ -453,6 +453,33 @@ def run_workload(args):
         def cpu():
             ref.word_rects(masks[0], W_PAGE, H_PAGE)
             return 1, "1 page"
+    elif args.workload == "pp4":
+        det_m, rec_m = synth.pp_det_model(), synth.pp_rec_model()
+        handle = wocr.PPPipeline(gpu, det_m, rec_m)
+        npg = 12
+        pages = [synth.page(3000 + k, W_PAGE, H_PAGE) for k in range(npg)]
+        nlines = sum(len(handle.page(pg, W_PAGE, H_PAGE)[0]) for pg in pages)
+        units, unit, workload = npg, "pages/s", (f"config 4 full page: PP-OCRv6-style DB detection of {npg} "
+                                                 f"2550x3300 pages (seeds 3000..3011; 3x960x736), DB boxes at 0.3 "
+                                                 f"on the device, lines grown 0.1 x height, cut and batched 16 by "
+                                                 f"width on the device, PP recognition arg-max per batch; "
+                                                 f"{nlines} lines (random-init det weights mark most of the page, "
+                                                 f"so a page gives few large boxes)")
+        h2d, d2h = npg * W_PAGE * H_PAGE * 3, 0
+
+        def step():
+            for pg in pages:
+                handle.page(pg, W_PAGE, H_PAGE)
+
+        def cpu():
+            x, tp = ref.det_input(pages[0], 960)
+            prob = ref.run_onnx(det_m, x)[0, 0]
+            boxes = ref.db_boxes(prob, tp, 0.3)
+            batches, _ = ref.pp_batches(pages[0], ref.pp_line_rects(boxes, 0.1))
+            for data, _, _ in batches:
+                lg = ref.run_onnx(rec_m, data, stop_before_softmax=True)
+                ref.argmax(lg.reshape(-1, lg.shape[-1]))
+            return 1, f"1 page ({len(boxes)} lines)"
     elif args.workload == "ppdb4":
         model = synth.pp_det_model()
         page = synth.page(3, W_PAGE, H_PAGE)

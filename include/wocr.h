@@ -177,6 +177,8 @@ int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const 
                        int32_t *lens, uint32_t *best, int32_t *tmax_out);
 
 /* ---- N-D graph executor: `NdGraph` (src/nd.rs:428-1394) -------------------------------- */
+/* The inputs of wocr_ndgraph_run, wocr_ndgraph_run_argmax and wocr_ppdet_page (x, rgb) may be
+ * in host or in device memory: they are copied by unified addressing. */
 typedef struct wocr_ndgraph wocr_ndgraph;
 
 /* NdGraph::new (src/nd.rs:505-817), with the same load-time fusions. */
@@ -250,6 +252,25 @@ int32_t wocr_ppdet_boxes(wocr_ndgraph *g, float thresh, float box_thresh, float 
 int32_t wocr_db_boxes(wocr_ctx *ctx, const float *prob, int32_t w, int32_t h, int32_t prob_on_device,
                       const float *to_page, float thresh, float box_thresh, float unclip_ratio, float min_size,
                       float *boxes, int32_t cap, int32_t *n);
+
+/* ---- The PP-OCRv6 page pipeline (src/bin/ocr-bench.rs:133-310, 458-585 with PPDET / PPOCR) --
+ * One page through detection, DB boxes, line images and recognition, with the page uploaded
+ * once and every intermediate (map, bit mask, line batches) kept on the device:
+ *   det:   wocr_ppdet_page (max_side), then wocr_ppdet_boxes with db = {thresh, box_thresh,
+ *          unclip_ratio, min_size};
+ *   lines: each box its own line, grown by relv x its height above and below (the height along
+ *          whichever axis is nearer vertical), cut at its bounding rectangle by wocr_pp_lines,
+ *          sorted by width into batches of per_batch;
+ *   rec:   the recognition graph's arg-max per step of each batch (wocr_ndgraph_run_argmax).
+ * Outputs, line by line in reading order: boxes[6 i ..] (before the relv growth), steps[i]
+ * (its batch's time steps) and its arg-max classes, concatenated in `best` (cap entries).
+ * *n_lines counts the lines; a call with best = NULL and cap = 0 stops after the boxes. */
+typedef struct wocr_pp wocr_pp;
+int32_t wocr_pp_create(wocr_ctx *ctx, const wocr_model *det, const wocr_model *rec, wocr_pp **out);
+void wocr_pp_destroy(wocr_pp *p);
+int32_t wocr_pp_page(wocr_pp *p, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, const float *db,
+                     float relv, int32_t per_batch, float *boxes, int32_t box_cap, int32_t *n_lines,
+                     uint32_t *best, int64_t cap, int32_t *steps);
 
 /* Word rectangles of binary page masks: `word_rects` (src/bin/ocr-bench.rs:38-60), i.e. the
  * external contours (find_contours, External), each simplified (Douglas-Peucker, epsilon 2), its

@@ -208,6 +208,24 @@ def pp_line(rgb: np.ndarray, rect) -> np.ndarray:
     return out
 
 
+def pp_line_rects(boxes, relv: float = 0.1) -> np.ndarray:
+    """The line rectangles [left, top, right, bottom] of DB boxes as the page pipeline cuts them
+    (src/bin/ocr-bench.rs:534-558 and 312-321: each box its own line, grown by relv x its height
+    across the text, then its bounding rectangle), in f32."""
+    f = np.float32
+    out = []
+    for cx, cy, ux, uy, bw, bh in np.asarray(boxes, np.float32).reshape(-1, 6):
+        upright = abs(uy) >= abs(ux)
+        across = f(relv) * (bh if upright else bw)
+        rw = bw if upright else f(bw + f(2) * across)
+        rh = f(bh + f(2) * across) if upright else bh
+        hw, hh = rw / f(2), rh / f(2)
+        xs = [cx + f(sa) * hh * ux + f(sb) * hw * -uy for sa in (-1, 1) for sb in (-1, 1)]
+        ys = [cy + f(sa) * hh * uy + f(sb) * hw * ux for sa in (-1, 1) for sb in (-1, 1)]
+        out.append([min(xs), min(ys), max(xs), max(ys)])
+    return np.array(out, np.float32).reshape(-1, 4)
+
+
 def pp_batches(rgb: np.ndarray, rects, per: int = 16):
     """PP-OCR line batches as src/bin/ocr-bench.rs:312-345 forms them (PPGROUP = 0): lines sorted
     by width (stable), cut into batches of `per`, each [n, 3, 48, width] with width the widest

@@ -110,3 +110,35 @@ def test_ppdet_boxes_on_detector_map(gpu):
     finally:
         g.close()
     np.testing.assert_array_equal(got, ref.db_boxes(prob, tp, 0.3))
+
+
+def test_pp_page_pipeline(gpu):
+    """The PP-OCRv6 page pipeline (`wocr_pp_page`) against its stages: its boxes are the DB boxes
+    of the detector's map (bit-exact), and each line's arg-max classes equal the oracle's
+    recognition of the same line images (up to near-ties at the oracle's precision)."""
+    from _helpers import argmax_parity
+
+    det, rec = synth.pp_det_model(), synth.pp_rec_model()
+    w, h = 1275, 1650
+    page = synth.page(6, w, h)
+    with wocr.PPPipeline(gpu, det, rec) as pp:
+        boxes, bests = pp.page(page, w, h)
+    g = wocr.NdGraph(gpu, det)
+    try:
+        prob, tp = g.ppdet_page(page, w, h, 960)
+    finally:
+        g.close()
+    np.testing.assert_array_equal(boxes, ref.db_boxes(prob, tp, 0.3))
+    assert len(bests) == len(boxes) > 0
+    rects = ref.pp_line_rects(boxes, 0.1)
+    batches, order = ref.pp_batches(page, rects)
+    k = 0
+    for data, n, width in batches:
+        logits = ref.run_onnx(rec, data, stop_before_softmax=True)
+        T = logits.shape[1]
+        for j in range(n):
+            line = order[k + j]
+            assert len(bests[line]) == T
+            bad, _ = argmax_parity(bests[line], logits[j])
+            assert bad == 0
+        k += n

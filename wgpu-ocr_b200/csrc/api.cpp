@@ -1219,7 +1219,7 @@ static void nd_capture(wocr_ndgraph *g, NdReplay *r) {
 
 static void nd_replay_launch(wocr_ndgraph *g, NdReplay *r, const float *x) {
     Ctx *c = &g->ctx->c;
-    WOCR_CUDA(cudaMemcpyAsync(r->in->p, x, r->in->bytes, cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaMemcpyAsync(r->in->p, x, r->in->bytes, cudaMemcpyDefault, c->stream));
     WOCR_CUDA(cudaGraphLaunch(r->exec, c->stream));
     c->flops += r->flops;
     c->launches += r->launches;
@@ -1370,7 +1370,7 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
         NdReplay *r = nd_replay(g, {h, w, 3, max_side}, 2, &first);
         if (!r || first) {
             BufP src = alloc(c, (size_t)w * h * 3);
-            WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, (size_t)w * h * 3, cudaMemcpyHostToDevice, c->stream));
+            WOCR_CUDA(cudaMemcpyAsync(src->p, rgb, (size_t)w * h * 3, cudaMemcpyDefault, c->stream));
             DT x = new_nhwc(c, 1, 3, oh, ow);
             k::det_prep(c, (const uint8_t *)src->p, w, h, ow, oh, 0, x.p);
             DT y = to_rowmajor(c, g->graph->run(x));
@@ -1741,3 +1741,121 @@ int32_t wocr_last_run_stats(void *handle, int32_t kind, double *flops, int64_t *
 }
 
 }  // extern "C"
+
+// ---- the PP-OCRv6 page pipeline --------------------------------------------------------------
+
+struct wocr_pp {
+    wocr_ctx *ctx = nullptr;
+    wocr_ndgraph *det = nullptr, *rec = nullptr;
+    ~wocr_pp() {
+        if (det) wocr_ndgraph_destroy(det);
+        if (rec) wocr_ndgraph_destroy(rec);
+    }
+};
+
+namespace {
+// a failing inner entry point: its status and message, rethrown
+void check_st(int32_t st) {
+    if (st != WOCR_OK) fail(st, wocr_last_error());
+}
+}  // namespace
+
+int32_t wocr_pp_create(wocr_ctx *ctx, const wocr_model *det, const wocr_model *rec, wocr_pp **out) {
+    return guard([&] {
+        if (!ctx || !det || !rec || !out) fail(WOCR_ERR_INVALID, "null argument");
+        auto p = std::make_unique<wocr_pp>();
+        p->ctx = ctx;
+        check_st(wocr_ndgraph_create(ctx, det, 0, &p->det));
+        check_st(wocr_ndgraph_create(ctx, rec, 1, &p->rec));
+        *out = p.release();
+    });
+}
+
+void wocr_pp_destroy(wocr_pp *p) { delete p; }
+
+int32_t wocr_pp_page(wocr_pp *p, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, const float *db,
+                     float relv, int32_t per_batch, float *boxes, int32_t box_cap, int32_t *n_lines, uint32_t *best,
+                     int64_t cap, int32_t *steps) {
+    return guard([&] {
+        if (!p || !rgb || !db || !n_lines || box_cap < 0 || cap < 0) fail(WOCR_ERR_INVALID, "bad argument");
+        if (w <= 0 || h <= 0 || max_side <= 0 || per_batch <= 0) fail(WOCR_ERR_INVALID, "bad page size or batch");
+        Ctx *c = &p->ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        // the page crosses PCIe once; detection and the line cuts read it on the device
+        BufP page = alloc(c, (size_t)w * h * 3);
+        WOCR_CUDA(cudaMemcpyAsync(page->p, rgb, (size_t)w * h * 3, cudaMemcpyDefault, c->stream));
+        const uint8_t *dpage = (const uint8_t *)page->p;
+        int32_t ow = 0, oh = 0;
+        float tp[2];
+        check_st(wocr_ppdet_page(p->det, dpage, w, h, max_side, nullptr, 0, &ow, &oh, tp));
+        const std::vector<float> bx = db_boxes(c, p->det->map, p->det->map_w, p->det->map_h, p->det->map_to_page,
+                                               db[0], db[1], db[2], db[3]);
+        const int n = (int)(bx.size() / 6);
+        *n_lines = n;
+        if (boxes) {
+            if (box_cap < n) fail(WOCR_ERR_CAPACITY, "boxes holds " + std::to_string(box_cap) + " of " + std::to_string(n));
+            if (n) std::memcpy(boxes, bx.data(), bx.size() * 4);
+        }
+        if (!best && cap == 0) return;
+        if (!best || !steps) fail(WOCR_ERR_INVALID, "null outputs");
+        if (n == 0) return;
+        // lines: each box grown by relv x its height across the text (src/bin/ocr-bench.rs:534-558:
+        // a line of one box, whose median height is its own), cut at its bounding rectangle
+        std::vector<float> lr((size_t)n * 4);
+        for (int i = 0; i < n; i++) {
+            const float *r = bx.data() + 6 * (size_t)i;
+            const bool upright = std::fabs(r[3]) >= std::fabs(r[2]);
+            const float across = relv * (upright ? r[5] : r[4]);
+            const float rw = upright ? r[4] : r[4] + 2.f * across, rh = upright ? r[5] + 2.f * across : r[5];
+            const float hw = rw / 2.0f, hh = rh / 2.0f;
+            float lx = INFINITY, ty = INFINITY, rx = -INFINITY, by = -INFINITY;
+            for (int sa = -1; sa <= 1; sa += 2)
+                for (int sb = -1; sb <= 1; sb += 2) {
+                    const float px = r[0] + sa * hh * r[2] + sb * hw * -r[3];
+                    const float py = r[1] + sa * hh * r[3] + sb * hw * r[2];
+                    lx = std::min(lx, px), rx = std::max(rx, px);
+                    ty = std::min(ty, py), by = std::max(by, py);
+                }
+            float *o = lr.data() + 4 * (size_t)i;
+            o[0] = lx;
+            o[1] = ty;
+            o[2] = rx;
+            o[3] = by;
+        }
+        std::vector<int32_t> order((size_t)n), bn((size_t)n), bw((size_t)n);
+        int32_t nb = 0;
+        int64_t total = 0;
+        check_st(wocr_pp_lines(p->ctx, dpage, w, h, lr.data(), n, per_batch, nullptr, 0, order.data(), bn.data(),
+                               bw.data(), &nb, &total));
+        BufP lines = alloc(c, (size_t)std::max<int64_t>(total, 1) * 4);
+        check_st(wocr_pp_lines(p->ctx, dpage, w, h, lr.data(), n, per_batch, (float *)lines->p, total, order.data(),
+                               bn.data(), bw.data(), &nb, &total));
+        // recognition, a batch at a time, arg-max in the CTC head's epilogue
+        std::vector<std::vector<uint32_t>> per_line((size_t)n);
+        int64_t off = 0;
+        int k = 0;
+        for (int b = 0; b < nb; b++) {
+            const int64_t shape[4] = {bn[b], 3, 48, bw[b]};
+            const int64_t bcap = (int64_t)bn[b] * bw[b];
+            std::vector<uint32_t> bb((size_t)bcap);
+            int64_t rows = 0, oshape[kMaxRank];
+            int32_t orank = 0;
+            check_st(wocr_ndgraph_run_argmax(p->rec, (const float *)lines->p + off, shape, 4, bb.data(), nullptr, nullptr,
+                                             bcap, &rows, oshape, &orank));
+            const int64_t T = rows / std::max(bn[b], 1);
+            for (int j = 0; j < bn[b]; j++)
+                per_line[order[k + j]].assign(bb.begin() + j * T, bb.begin() + (j + 1) * T);
+            off += (int64_t)bn[b] * 3 * 48 * bw[b];
+            k += bn[b];
+        }
+        int64_t need = 0;
+        for (const auto &v : per_line) need += (int64_t)v.size();
+        if (cap < need) fail(WOCR_ERR_CAPACITY, "best holds " + std::to_string(cap) + " of " + std::to_string(need));
+        int64_t o = 0;
+        for (int i = 0; i < n; i++) {
+            steps[i] = (int32_t)per_line[i].size();
+            std::copy(per_line[i].begin(), per_line[i].end(), best + o);
+            o += (int64_t)per_line[i].size();
+        }
+    });
+}

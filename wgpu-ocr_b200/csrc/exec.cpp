@@ -204,7 +204,7 @@ DT to_rowmajor(Ctx *c, const DT &x) {
 DT from_host(Ctx *c, const float *x, const std::vector<int64_t> &shape) {
     DT t = new_rowmajor(c, shape);
     if (t.numel() > 0)
-        WOCR_CUDA(cudaMemcpyAsync(t.p, x, (size_t)t.numel() * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+        WOCR_CUDA(cudaMemcpyAsync(t.p, x, (size_t)t.numel() * sizeof(float), cudaMemcpyDefault, c->stream));
     return t;
 }
 

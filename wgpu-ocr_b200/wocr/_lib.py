@@ -99,6 +99,10 @@ _SIGS = [
     ("wocr_last_transfer_bytes", c_i32, [c_void_p, c_i32, P(c_i64), P(c_i64)]),
     ("wocr_word_rects", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_i32, c_f32, c_f32, c_f32, c_void_p, c_i64,
                                 c_void_p]),
+    ("wocr_pp_create", c_i32, [c_void_p, P(CModel), P(CModel), P(c_void_p)]),
+    ("wocr_pp_destroy", None, [c_void_p]),
+    ("wocr_pp_page", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_void_p, c_f32, c_i32, c_void_p, c_i32,
+                             P(c_i32), c_void_p, c_i64, c_void_p]),
     ("wocr_ppdet_boxes", c_i32, [c_void_p, c_f32, c_f32, c_f32, c_f32, c_void_p, c_i32, P(c_i32)]),
     ("wocr_db_boxes", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_void_p, c_f32, c_f32, c_f32, c_f32, c_void_p,
                               c_i32, P(c_i32)]),

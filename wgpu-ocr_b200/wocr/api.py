@@ -408,6 +408,64 @@ def ocrs_decode(best_col: Sequence[int], steps: int, width: int, alphabet: str) 
     return "".join(s)
 
 
+class PPPipeline:
+    """The PP-OCRv6 page pipeline of the reference's bench (`wocr_pp_*`; src/bin/ocr-bench.rs:
+    133-310, 458-585 with PPDET and PPOCR): detection, DB boxes, line images and recognition of
+    a page, with the page uploaded once and the map, mask and line batches kept on the device."""
+
+    def __init__(self, gpu: Gpu, det_model: Model, rec_model: Model):
+        self.gpu = gpu
+        dh, rh = L.CModelHolder(det_model), L.CModelHolder(rec_model)
+        h = ctypes.c_void_p()
+        L.check(L.lib().wocr_pp_create(gpu.h, dh.ref(), rh.ref(), ctypes.byref(h)))
+        self.h = h
+
+    def page(self, rgb, w: int, h: int, max_side: int = 960, db=(0.3, 0.45, 1.4, 3.0), relv: float = 0.1,
+             per_batch: int = 16, d_rgb: int = 0):
+        """(boxes float32 [n, 6] in reading order, [arg-max classes per step] per line) of an RGB
+        page (host array, or d_rgb, a device pointer).  db = (thresh, box_thresh, unclip_ratio,
+        min_size); config 4 uses thresh 0.3."""
+        src = ctypes.c_void_p(d_rgb) if d_rgb else L.ptr(np.ascontiguousarray(rgb, np.uint8))
+        keep = None if d_rgb else rgb
+        dbp = np.float32(db)
+        n = ctypes.c_int32()
+        boxes = np.zeros((256, 6), np.float32)
+        cap = 1 << 16
+        for _ in range(8):  # again only when a capacity guess was short (status 8)
+            best = np.empty(cap, np.uint32)
+            steps = np.zeros(boxes.shape[0], np.int32)
+            st = L.lib().wocr_pp_page(self.h, src, int(w), int(h), int(max_side), L.ptr(dbp), relv, int(per_batch),
+                                      L.ptr(boxes), boxes.shape[0], ctypes.byref(n), L.ptr(best), cap, L.ptr(steps))
+            if st == 8 and n.value > boxes.shape[0]:
+                boxes = np.zeros((n.value, 6), np.float32)
+                continue
+            if st == 8:
+                cap *= 4
+                continue
+            break
+        L.check(st)
+        del keep
+        k = n.value
+        ends = np.cumsum(steps[:k])
+        return boxes[:k].copy(), [best[e - s:e].copy() for e, s in zip(ends, steps[:k])]
+
+    def texts(self, rgb, w: int, h: int, chars: List[str], **kw) -> List[str]:
+        """The page's text lines in reading order (`Dictionary::decode` of each line)."""
+        _, bests = self.page(rgb, w, h, **kw)
+        return [pp_decode(b, chars) for b in bests]
+
+    def close(self):
+        if self.h:
+            L.lib().wocr_pp_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
 def pp_decode(best: Sequence[int], chars: List[str]) -> str:
     """`Dictionary::decode` (src/ppocr.rs:23-33): repeats merged, blanks dropped."""
     out, prev = [], 0
