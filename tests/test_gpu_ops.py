@@ -295,15 +295,17 @@ def test_handles_outlive_their_context():
 
 def _pp_boxes(w, h, rng):
     """Line boxes of a page: ordinary lines (down- and upsampled heights), boxes on the page's
-    edges and corners, a box reaching past the last row, degenerate (empty, reversed, NaN) boxes
-    and fractional coordinates."""
+    edges and corners, a box reaching past the last row, degenerate (empty, reversed, NaN) boxes,
+    fractional coordinates, and tall crops for the two-pass kernels (383 and 384 rows, the whole
+    page)."""
     boxes = [[rng.uniform(0, w - 800), y, 0, 0] for y in rng.uniform(0, h - 120, 20)]
     for b in boxes:
         b[2] = b[0] + rng.uniform(30, 800)
         b[3] = b[1] + rng.uniform(12, 110)
     boxes += [[0, 0, 37, 21], [w - 13, h - 9, w + 40, h + 40], [w, 100, w, 140], [500, h - 3, 900, h + 50],
               [300, 400, 200, 380], [float("nan"), 10, 60, 40], [10.7, 20.2, 1500.9, 20.9], [0, 0, w, 60],
-              [100, 200, 110, 1900]]
+              [100, 200, 110, 1900], [40, 500, 900, 883], [40, 500, 900, 884], [0, 0, w, h],
+              [50, 100, 2400, 3000]]
     return np.array(boxes, np.float32)
 
 

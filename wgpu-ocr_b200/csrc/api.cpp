@@ -1682,13 +1682,12 @@ int32_t wocr_pp_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h,
         std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return ln[a].ow < ln[b].ow; });
         std::vector<k::PpLine> plan((size_t)n);
         int64_t off = 0;
-        int nb = 0, max_width = 0;
+        int nb = 0;
         for (int k0 = 0; k0 < n; k0 += per_batch, nb++) {
             const int kn = std::min(per_batch, n - k0);
             int width = 0;
             for (int j = 0; j < kn; j++) width = std::max(width, ln[idx[k0 + j]].ow);
             width = (width + 7) / 8 * 8;
-            max_width = std::max(max_width, width);
             for (int j = 0; j < kn; j++) {
                 plan[k0 + j] = ln[idx[k0 + j]];
                 plan[k0 + j].width = width;
@@ -1704,12 +1703,42 @@ int32_t wocr_pp_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h,
         if (!d_out || n == 0) return;
         if (!d_rgb) fail(WOCR_ERR_INVALID, "null page");
         if (cap < off) fail(WOCR_ERR_CAPACITY, "line batches need " + std::to_string(off) + " floats");
-        BufP dl = alloc(c, plan.size() * sizeof(k::PpLine));
-        WOCR_CUDA(cudaMemcpyAsync(dl->p, plan.data(), plan.size() * sizeof(k::PpLine), cudaMemcpyHostToDevice,
-                                  c->stream));
-        double bytes = 4.0 * (double)off;
-        for (const k::PpLine &L : plan) bytes += 3.0 * L.cw * L.ch;
-        k::pp_lines(c, d_rgb, w, h, (const k::PpLine *)dl->p, n, max_width, d_out, bytes);
+        // tall crops (a vertical downscale of 8 or more) go through the two-pass kernels
+        std::vector<k::PpLine> normal, tall;
+        std::vector<int64_t> toff;
+        int64_t tmp_total = 0;
+        int max_w_n = 0, max_w_t = 0, max_cw = 0;
+        double bytes_n = 0, bytes_t = 0;
+        for (const k::PpLine &L : plan) {
+            const double b = 3.0 * L.cw * L.ch + 4.0 * 3 * 48 * L.width;
+            if (L.ch >= k::kPpTallRows) {
+                tall.push_back(L);
+                toff.push_back(tmp_total);
+                tmp_total += (int64_t)48 * L.cw * 3;
+                max_w_t = std::max(max_w_t, L.width);
+                max_cw = std::max(max_cw, L.cw);
+                bytes_t += b;
+            } else {
+                normal.push_back(L);
+                max_w_n = std::max(max_w_n, L.width);
+                bytes_n += b;
+            }
+        }
+        if (!normal.empty()) {
+            BufP dl = alloc(c, normal.size() * sizeof(k::PpLine));
+            WOCR_CUDA(cudaMemcpyAsync(dl->p, normal.data(), normal.size() * sizeof(k::PpLine), cudaMemcpyHostToDevice,
+                                      c->stream));
+            k::pp_lines(c, d_rgb, w, h, (const k::PpLine *)dl->p, (int)normal.size(), max_w_n, d_out, bytes_n);
+        }
+        if (!tall.empty()) {
+            BufP dl = alloc(c, tall.size() * sizeof(k::PpLine)), dt = alloc(c, toff.size() * 8);
+            BufP tmp = alloc(c, (size_t)tmp_total * 4);
+            WOCR_CUDA(cudaMemcpyAsync(dl->p, tall.data(), tall.size() * sizeof(k::PpLine), cudaMemcpyHostToDevice,
+                                      c->stream));
+            WOCR_CUDA(cudaMemcpyAsync(dt->p, toff.data(), toff.size() * 8, cudaMemcpyHostToDevice, c->stream));
+            k::pp_lines_tall(c, d_rgb, w, h, (const k::PpLine *)dl->p, (int)tall.size(), max_cw, max_w_t,
+                             (const int64_t *)dt->p, (float *)tmp->p, d_out, bytes_t);
+        }
         sync_bounded(c, 0);  // the plan's host copy is read until the upload completes
     });
 }

@@ -166,6 +166,12 @@ struct PpLine {
 // bytes: the algorithmic bytes (the boxes' page bytes read, the batches written), for the profile
 void pp_lines(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_width, float *out,
               double bytes);
+// The same for tall crops (ch >= kPpTallRows: a vertical downscale of 8 or more) in two passes
+// through tmp: line i's intermediate at tmp + tmp_off[i], 48 * cw * 3 floats; max_cw and
+// max_width over the lines.
+constexpr int kPpTallRows = 8 * 48;
+void pp_lines_tall(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_cw, int max_width,
+                   const int64_t *tmp_off, float *tmp, float *out, double bytes);
 // The same on compacted pages: per page 2 oh rows of w * 3 bytes (the top and bottom source rows
 // of each output row), rows[oy] = {vertical weight (float bits), bit 0/1: top/bottom is padding}.
 void grey_resize_rows(Ctx *c, const uint8_t *cmp, const int2 *rows, int n, int w, int oh, int ow, float *y);
