@@ -29,16 +29,17 @@ __global__ void k_db_mask(const float *__restrict__ prob, int w, int h, int word
 
 // `score` of src/ppdet.rs:63-83 with the reference's order of additions (a sequential f32 sum
 // over the rows, then the columns, of the pixels inside the box), so the result is the
-// reference's to the bit.  A warp per box: the lanes test and load 32 pixels of a row at a time
-// and stage them in shared memory, lane 0 adds the inside ones in column order (32 independent
-// loads, then a chain of predicated adds).  The scan covers the box's bounding rectangle clamped
-// to the map; the inside test alone decides which pixels count.
-constexpr int kDbWarps = 8;
+// reference's to the bit.  A warp per box: the lanes test and load 8 x 32 pixels of a row at a
+// time (8 loads in flight per lane) and stage them in shared memory, lane 0 adds the inside ones
+// in column order (independent shared loads, then a chain of predicated adds).  The scan covers
+// the box's bounding rectangle clamped to the map; the inside test alone decides which pixels
+// count.
+constexpr int kDbWarps = 8, kDbChunks = 8;
 
 __global__ void __launch_bounds__(kDbWarps * 32) k_db_scores(const float *__restrict__ prob, int w, int h,
                                                              const DbBox *__restrict__ boxes, int n,
                                                              float *__restrict__ scores) {
-    __shared__ float stage[kDbWarps][32];
+    __shared__ float stage[kDbWarps][kDbChunks * 32];
     const int wi = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int k = blockIdx.x * kDbWarps + wi;
     if (k >= n) return;
@@ -48,29 +49,42 @@ __global__ void __launch_bounds__(kDbWarps * 32) k_db_scores(const float *__rest
     for (int y = b.y0; y <= b.y1; y++) {
         const float dy = __fsub_rn((float)y, b.cy);
         const float *row = prob + (int64_t)y * w;
-        for (int xs = b.x0; xs <= b.x1; xs += 32) {
-            const int x = xs + lane;
-            bool in = false;
-            float v = 0.f;
-            if (x <= b.x1) {
-                const float dx = __fsub_rn((float)x, b.cx);
-                const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
-                const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
-                in = fabsf(along) <= b.hh && fabsf(across) <= b.hw;
-                if (in) v = row[x];
+        for (int xs = b.x0; xs <= b.x1; xs += kDbChunks * 32) {
+            uint32_t m[kDbChunks];
+            float v[kDbChunks];
+            bool any = false;
+#pragma unroll
+            for (int q = 0; q < kDbChunks; q++) {
+                const int x = xs + q * 32 + lane;
+                bool in = false;
+                v[q] = 0.f;
+                if (x <= b.x1) {
+                    const float dx = __fsub_rn((float)x, b.cx);
+                    const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
+                    const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
+                    in = fabsf(along) <= b.hh && fabsf(across) <= b.hw;
+                    if (in) v[q] = row[x];
+                }
+                m[q] = __ballot_sync(0xffffffffu, in);
+                any |= m[q] != 0u;
             }
-            const uint32_t m = __ballot_sync(0xffffffffu, in);
-            if (m == 0) continue;
-            stage[wi][lane] = v;
+            if (!any) continue;
+#pragma unroll
+            for (int q = 0; q < kDbChunks; q++) stage[wi][q * 32 + lane] = v[q];
             __syncwarp();
             if (lane == 0) {
-                float t[32];
 #pragma unroll
-                for (int j = 0; j < 32; j++) t[j] = stage[wi][j];
+                for (int q = 0; q < kDbChunks; q++) {
+                    const uint32_t mq = m[q];
+                    if (mq == 0u) continue;
+                    float t[32];
 #pragma unroll
-                for (int j = 0; j < 32; j++)
-                    if ((m >> j) & 1u) sum = __fadd_rn(sum, t[j]);
-                cnt += __popc(m);
+                    for (int j = 0; j < 32; j++) t[j] = stage[wi][q * 32 + j];
+#pragma unroll
+                    for (int j = 0; j < 32; j++)
+                        if ((mq >> j) & 1u) sum = __fadd_rn(sum, t[j]);
+                    cnt += __popc(mq);
+                }
             }
             __syncwarp();
         }
