@@ -371,7 +371,7 @@ __device__ void heap_sort(uint32_t *a, int n) {
 struct WordP {
     const uint32_t *mask;
     int words, w, h;
-    const int *run_x, *run_row, *comp_run, *pt_off;
+    const int *run_x, *run_row, *comp_run, *pt_off, *len;
     int C;
     // per component, n + 1 slots each (n border points; slot base = pt_off[k] + k)
     short2 *pts;       // its border, then the first point again
@@ -387,14 +387,15 @@ struct WordP {
     int *status;
 };
 
-constexpr int kWT = 128, kSortCap = 2048;
+// Block sizes of k_word_rect: components of more than kBigLen border points get kWTBig threads.
+constexpr int kWT = 128, kWTBig = 1024, kBigLen = 8192, kSortCap = 2048;
 
 // exclusive prefix of size(i) for i < n into out; returns the total (all threads)
-template <typename F>
+template <int T, typename F>
 __device__ int block_scan(int n, int *out, F size, int *warp_tot) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int carry = 0;
-    for (int c0 = 0; c0 < n; c0 += kWT) {
+    for (int c0 = 0; c0 < n; c0 += T) {
         const int i = c0 + threadIdx.x;
         const int v = i < n ? size(i) : 0;
         int x = v;
@@ -408,7 +409,7 @@ __device__ int block_scan(int n, int *out, F size, int *warp_tot) {
         int before = carry;
         for (int q = 0; q < warp; q++) before += warp_tot[q];
         int all = carry;
-        for (int q = 0; q < kWT / 32; q++) all += warp_tot[q];
+        for (int q = 0; q < T / 32; q++) all += warp_tot[q];
         if (i < n) out[i] = before + x - v;
         __syncthreads();
         carry = all;
@@ -436,14 +437,15 @@ __device__ __forceinline__ bool in_octagon(const uint32_t *oct, int noct, uint32
 // largest distance, then the smallest index, as the sequential search finds it), the hull of
 // the kept points (octagon filter, sort, monotone chain) and the minimum-area rectangle (an
 // argmin over the hull's edges, first edge on ties).
-__global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
+template <int T>
+__global__ void __launch_bounds__(T) k_word_rect(WordP p) {
     __shared__ int s_n, s_nseg, s_next, s_tot, s_m, s_ns, s_hc, s_noct;
-    __shared__ int warp_tot[kWT / 32];
+    __shared__ int warp_tot[T / 32];
     __shared__ uint32_t s_oct[8];
     __shared__ unsigned long long s_ext[8], s_best;
     __shared__ uint32_t s_sort[kSortCap];
     const int k = blockIdx.x, tid = threadIdx.x;
-    if (k >= p.C) return;
+    if (k >= p.C || (p.len[k] > kBigLen) != (T == kWTBig)) return;  // the other instance's component
     const int r = p.comp_run[k], row = p.run_row[r];
     const int64_t base = (int64_t)p.pt_off[k] + k;
     short2 *pts = p.pts + base;
@@ -461,7 +463,7 @@ __global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
     __syncthreads();
     const int n = s_n;
     uint8_t *keep = p.keep + base;
-    for (int i = tid; i < n; i += kWT) keep[i] = (i == 0 || i == n - 1);
+    for (int i = tid; i < n; i += T) keep[i] = (i == 0 || i == n - 1);
     int2 *sa = p.seg_a + base, *sb = p.seg_b + base;
     int *pref = p.pref + base;
     unsigned long long *best = p.best + base;
@@ -469,9 +471,9 @@ __global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
     // Douglas-Peucker, epsilon 2, on the closed polyline
     while (s_nseg > 0) {
         const int nseg = s_nseg;
-        for (int q = tid; q < nseg; q += kWT) best[q] = 0ull;
-        const int tot = block_scan(nseg, pref, [&](int q) { return sa[q].y - sa[q].x - 1; }, warp_tot);
-        for (int g = tid; g < tot; g += kWT) {
+        for (int q = tid; q < nseg; q += T) best[q] = 0ull;
+        const int tot = block_scan<T>(nseg, pref, [&](int q) { return sa[q].y - sa[q].x - 1; }, warp_tot);
+        for (int g = tid; g < tot; g += T) {
             int lo = 0, hi = nseg - 1;  // the last segment whose prefix is <= g
             while (lo < hi) {
                 const int mid = (lo + hi + 1) >> 1;
@@ -488,7 +490,7 @@ __global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
         }
         if (tid == 0) s_next = 0;
         __syncthreads();
-        for (int q = tid; q < nseg; q += kWT) {
+        for (int q = tid; q < nseg; q += T) {
             const unsigned long long b = best[q];
             const float d = __uint_as_float((uint32_t)(b >> 32));
             const int i = (int)(0xffffffffu - (uint32_t)b);
@@ -511,7 +513,7 @@ __global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
     if (tid == 0) s_m = 0;
     if (tid < 8) s_ext[tid] = (tid & 1) ? 0ull : ~0ull;
     __syncthreads();
-    for (int i = tid; i < n - 1; i += kWT)
+    for (int i = tid; i < n - 1; i += T)
         if (keep[i]) {
             const uint32_t kk = ((uint32_t)pts[i].x << 16) | (uint32_t)pts[i].y;
             keys[atomicAdd(&s_m, 1)] = kk;
@@ -543,21 +545,21 @@ __global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
     // survivors of the octagon filter (into the free segment slots), sorted in shared memory
     // when they fit
     uint32_t *surv = (uint32_t *)sb;
-    for (int i = tid; i < m; i += kWT)
+    for (int i = tid; i < m; i += T)
         if (!in_octagon(s_oct, s_noct, keys[i])) surv[atomicAdd(&s_ns, 1)] = keys[i];
     __syncthreads();
     const bool small = s_ns <= kSortCap;
     uint32_t *sv = small ? s_sort : surv;
     if (small) {
         const int ns = s_ns;
-        for (int i = tid; i < ns; i += kWT) s_sort[i] = surv[i];
+        for (int i = tid; i < ns; i += T) s_sort[i] = surv[i];
         int np2 = 1;
         while (np2 < ns) np2 <<= 1;
-        for (int i = ns + tid; i < np2; i += kWT) s_sort[i] = 0xffffffffu;
+        for (int i = ns + tid; i < np2; i += T) s_sort[i] = 0xffffffffu;
         __syncthreads();
         for (int len = 2; len <= np2; len <<= 1)
             for (int j = len >> 1; j > 0; j >>= 1) {
-                for (int i = tid; i < np2; i += kWT) {
+                for (int i = tid; i < np2; i += T) {
                     const int l = i ^ j;
                     if (l > i) {
                         const uint32_t a = s_sort[i], b = s_sort[l];
@@ -627,7 +629,7 @@ __global__ void __launch_bounds__(kWT) k_word_rect(WordP p) {
         }
         return __fmul_rn(__fsub_rn(s1, s0), __fsub_rn(t1, t0));
     };
-    for (int i = tid; i < hc; i += kWT)
+    for (int i = tid; i < hc; i += T)
         atomicMin(&s_best, ((unsigned long long)__float_as_uint(edge(i, nullptr)) << 32) | (uint32_t)i);
     __syncthreads();
     if (tid == 0) {
@@ -753,6 +755,7 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     p.run_row = run_row;
     p.comp_run = (const int *)crun->p;
     p.pt_off = (const int *)ptoff->p;
+    p.len = (const int *)len->p;
     p.C = C;
     p.pts = (short2 *)pts->p;
     p.keep = (uint8_t *)keep->p;
@@ -770,7 +773,9 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     p.status = c->status;
     {
         Prof pf(c, "word_rect", 0, 0);
-        k_word_rect<<<C, kWT, 0, c->stream>>>(p);
+        k_word_rect<kWT><<<C, kWT, 0, c->stream>>>(p);
+        WOCR_LAUNCHED(c);
+        k_word_rect<kWTBig><<<C, kWTBig, 0, c->stream>>>(p);
         WOCR_LAUNCHED(c);
     }
     scan_i32(c, (const int *)valid->p, C, (int *)vpos->p, d_tot);
