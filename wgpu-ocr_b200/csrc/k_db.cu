@@ -29,65 +29,86 @@ __global__ void k_db_mask(const float *__restrict__ prob, int w, int h, int word
 
 // `score` of src/ppdet.rs:63-83 with the reference's order of additions (a sequential f32 sum
 // over the rows, then the columns, of the pixels inside the box), so the result is the
-// reference's to the bit.  A warp per box: the lanes test and load 8 x 32 pixels of a row at a
-// time (8 loads in flight per lane) and stage them in shared memory, lane 0 adds the inside ones
-// in column order (independent shared loads, then a chain of predicated adds).  The scan covers
-// the box's bounding rectangle clamped to the map; the inside test alone decides which pixels
-// count.
-constexpr int kDbWarps = 8, kDbChunks = 8;
+// reference's to the bit.  A warp per box walks the box's bounding rectangle in rounds of 8 x 32
+// pixels (row by row, left to right): the lanes test and load a round (8 loads in flight per
+// lane) and stage it in shared memory, lane 0 adds the inside values in column order.  The next
+// round's loads are issued before lane 0's chain of adds, so they arrive while it runs.  The
+// inside test alone decides which pixels count.
+constexpr int kDbWarps = 8, kDbChunks = 8, kDbRound = kDbChunks * 32;
+
+struct DbRound {
+    float v[kDbChunks];
+    uint32_t m[kDbChunks];
+};
+
+// round r of box b: row y0 + r / per_row, columns from x0 + (r % per_row) * kDbRound
+__device__ __forceinline__ void db_load(const float *prob, int w, const DbBox &b, int per_row, int r, int lane,
+                                        DbRound &o) {
+    const int y = b.y0 + r / per_row, xs = b.x0 + (r % per_row) * kDbRound;
+    const float dy = __fsub_rn((float)y, b.cy);
+    const float *row = prob + (int64_t)y * w;
+#pragma unroll
+    for (int q = 0; q < kDbChunks; q++) {
+        const int x = xs + q * 32 + lane;
+        bool in = false;
+        o.v[q] = 0.f;
+        if (x <= b.x1) {
+            const float dx = __fsub_rn((float)x, b.cx);
+            const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
+            const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
+            in = fabsf(along) <= b.hh && fabsf(across) <= b.hw;
+            if (in) o.v[q] = row[x];
+        }
+        o.m[q] = __ballot_sync(0xffffffffu, in);
+    }
+}
 
 __global__ void __launch_bounds__(kDbWarps * 32) k_db_scores(const float *__restrict__ prob, int w, int h,
                                                              const DbBox *__restrict__ boxes, int n,
                                                              float *__restrict__ scores) {
-    __shared__ float stage[kDbWarps][kDbChunks * 32];
+    __shared__ float stage[kDbWarps][kDbRound];
     const int wi = threadIdx.x / 32, lane = threadIdx.x & 31;
     const int k = blockIdx.x * kDbWarps + wi;
     if (k >= n) return;
     const DbBox b = boxes[k];
     float sum = 0.f;
     int64_t cnt = 0;
-    for (int y = b.y0; y <= b.y1; y++) {
-        const float dy = __fsub_rn((float)y, b.cy);
-        const float *row = prob + (int64_t)y * w;
-        for (int xs = b.x0; xs <= b.x1; xs += kDbChunks * 32) {
-            uint32_t m[kDbChunks];
-            float v[kDbChunks];
-            bool any = false;
+    const int per_row = b.x1 >= b.x0 ? (b.x1 - b.x0) / kDbRound + 1 : 0;
+    const int rounds = b.y1 >= b.y0 ? per_row * (b.y1 - b.y0 + 1) : 0;
+    DbRound cur;
+    if (rounds > 0) db_load(prob, w, b, per_row, 0, lane, cur);
+    for (int r = 0; r < rounds; r++) {
+        bool any = false;
+#pragma unroll
+        for (int q = 0; q < kDbChunks; q++) any |= cur.m[q] != 0u;
+        if (any) {
+#pragma unroll
+            for (int q = 0; q < kDbChunks; q++) stage[wi][q * 32 + lane] = cur.v[q];
+        }
+        const DbRound now = cur;
+        if (r + 1 < rounds) db_load(prob, w, b, per_row, r + 1, lane, cur);  // in flight during the adds
+        if (!any) continue;
+        __syncwarp();
+        if (lane == 0) {
 #pragma unroll
             for (int q = 0; q < kDbChunks; q++) {
-                const int x = xs + q * 32 + lane;
-                bool in = false;
-                v[q] = 0.f;
-                if (x <= b.x1) {
-                    const float dx = __fsub_rn((float)x, b.cx);
-                    const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
-                    const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
-                    in = fabsf(along) <= b.hh && fabsf(across) <= b.hw;
-                    if (in) v[q] = row[x];
-                }
-                m[q] = __ballot_sync(0xffffffffu, in);
-                any |= m[q] != 0u;
-            }
-            if (!any) continue;
+                const uint32_t mq = now.m[q];
+                if (mq == 0u) continue;
+                float t[32];
 #pragma unroll
-            for (int q = 0; q < kDbChunks; q++) stage[wi][q * 32 + lane] = v[q];
-            __syncwarp();
-            if (lane == 0) {
+                for (int j = 0; j < 32; j++) t[j] = stage[wi][q * 32 + j];
+                if (mq == 0xffffffffu) {  // all 32 inside: a plain chain of adds
 #pragma unroll
-                for (int q = 0; q < kDbChunks; q++) {
-                    const uint32_t mq = m[q];
-                    if (mq == 0u) continue;
-                    float t[32];
-#pragma unroll
-                    for (int j = 0; j < 32; j++) t[j] = stage[wi][q * 32 + j];
+                    for (int j = 0; j < 32; j++) sum = __fadd_rn(sum, t[j]);
+                } else {
 #pragma unroll
                     for (int j = 0; j < 32; j++)
                         if ((mq >> j) & 1u) sum = __fadd_rn(sum, t[j]);
-                    cnt += __popc(mq);
                 }
+                cnt += __popc(mq);
             }
-            __syncwarp();
         }
+        __syncwarp();
     }
     if (lane == 0) scores[k] = cnt == 0 ? 0.f : __fdiv_rn(sum, (float)cnt);
 }

@@ -388,7 +388,9 @@ struct WordP {
 };
 
 // Block sizes of k_word_rect: components of more than kBigLen border points get kWTBig threads.
-constexpr int kWT = 128, kWTBig = 1024, kBigLen = 8192, kSortCap = 2048;
+// A Douglas-Peucker level of at most kFewSegs open segments runs each segment with the whole
+// block (a shuffle and shared-memory argmax) instead of the flat scan over all of them.
+constexpr int kWT = 128, kWTBig = 1024, kBigLen = 4096, kSortCap = 2048, kFewSegs = 4;
 
 // exclusive prefix of size(i) for i < n into out; returns the total (all threads)
 template <int T, typename F>
@@ -444,7 +446,9 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
     __shared__ uint32_t s_oct[8];
     __shared__ unsigned long long s_ext[8], s_best;
     __shared__ uint32_t s_sort[kSortCap];
-    const int k = blockIdx.x, tid = threadIdx.x;
+    __shared__ int2 s_few[2][kFewSegs];                   // a level's segments when few (by parity)
+    __shared__ unsigned long long s_wbest[kFewSegs][T / 32];
+    const int k = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (k >= p.C || (p.len[k] > kBigLen) != (T == kWTBig)) return;  // the other instance's component
     const int r = p.comp_run[k], row = p.run_row[r];
     const int64_t base = (int64_t)p.pt_off[k] + k;
@@ -457,6 +461,7 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
         s_nseg = 0;
         if (nb + 1 > 2) {
             p.seg_a[base] = make_int2(0, nb);
+            s_few[0][0] = make_int2(0, nb);
             s_nseg = 1;
         }
     }
@@ -469,8 +474,85 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
     unsigned long long *best = p.best + base;
     __syncthreads();
     // Douglas-Peucker, epsilon 2, on the closed polyline
+    int par = 0;
     while (s_nseg > 0) {
         const int nseg = s_nseg;
+        if (nseg <= kFewSegs) {
+            // few open segments (deep, narrow levels): one pass of the block over all of them,
+            // each thread keeping a maximum per segment, then a warp and a block reduction
+            int2 sg[kFewSegs];
+            int pre[kFewSegs + 1];
+            pre[0] = 0;
+#pragma unroll
+            for (int u = 0; u < kFewSegs; u++) {
+                sg[u] = u < nseg ? s_few[par][u] : make_int2(0, 1);
+                pre[u + 1] = pre[u] + (u < nseg ? sg[u].y - sg[u].x - 1 : 0);
+            }
+            unsigned long long bk[kFewSegs];
+#pragma unroll
+            for (int u = 0; u < kFewSegs; u++) bk[u] = 0ull;
+            for (int g = tid; g < pre[kFewSegs]; g += T) {
+#pragma unroll
+                for (int u = 0; u < kFewSegs; u++)
+                    if (g >= pre[u] && g < pre[u + 1]) {
+                        const int i = sg[u].x + 1 + (g - pre[u]);
+                        const unsigned long long key =
+                            dp_key(seg_dist((float)pts[i].x, (float)pts[i].y, (float)pts[sg[u].x].x, (float)pts[sg[u].x].y,
+                                            (float)pts[sg[u].y].x, (float)pts[sg[u].y].y),
+                                   i);
+                        bk[u] = key > bk[u] ? key : bk[u];
+                    }
+            }
+#pragma unroll
+            for (int u = 0; u < kFewSegs; u++) {
+#pragma unroll
+                for (int o = 16; o; o >>= 1) {
+                    const unsigned long long ot = __shfl_xor_sync(0xffffffffu, bk[u], o);
+                    bk[u] = ot > bk[u] ? ot : bk[u];
+                }
+                if (lane == 0) s_wbest[u][warp] = bk[u];
+            }
+            __syncthreads();
+            if (warp == 0) {
+#pragma unroll
+                for (int u = 0; u < kFewSegs; u++) {
+                    unsigned long long v = lane < T / 32 ? s_wbest[u][lane] : 0ull;
+#pragma unroll
+                    for (int o = 16; o; o >>= 1) {
+                        const unsigned long long ot = __shfl_xor_sync(0xffffffffu, v, o);
+                        v = ot > v ? ot : v;
+                    }
+                    bk[u] = v;
+                }
+                if (tid == 0) {
+                    int nx = 0;
+#pragma unroll
+                    for (int u = 0; u < kFewSegs; u++) {
+                        if (u >= nseg) break;
+                        const float d = __uint_as_float((uint32_t)(bk[u] >> 32));
+                        const int i = (int)(0xffffffffu - (uint32_t)bk[u]);
+                        if (d > 2.0f) {
+                            keep[i] = 1;
+                            if (i - sg[u].x > 1) {
+                                if (nx < kFewSegs) s_few[par ^ 1][nx] = make_int2(sg[u].x, i);
+                                sb[nx++] = make_int2(sg[u].x, i);
+                            }
+                            if (sg[u].y - i > 1) {
+                                if (nx < kFewSegs) s_few[par ^ 1][nx] = make_int2(i, sg[u].y);
+                                sb[nx++] = make_int2(i, sg[u].y);
+                            }
+                        }
+                    }
+                    s_nseg = nx;
+                }
+            }
+            int2 *t = sa;
+            sa = sb;
+            sb = t;
+            par ^= 1;
+            __syncthreads();
+            continue;
+        }
         for (int q = tid; q < nseg; q += T) best[q] = 0ull;
         const int tot = block_scan<T>(nseg, pref, [&](int q) { return sa[q].y - sa[q].x - 1; }, warp_tot);
         for (int g = tid; g < tot; g += T) {
@@ -497,8 +579,16 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
             const int2 sg = sa[q];
             if (d > 2.0f) {
                 keep[i] = 1;
-                if (i - sg.x > 1) sb[atomicAdd(&s_next, 1)] = make_int2(sg.x, i);
-                if (sg.y - i > 1) sb[atomicAdd(&s_next, 1)] = make_int2(i, sg.y);
+                if (i - sg.x > 1) {
+                    const int j = atomicAdd(&s_next, 1);
+                    sb[j] = make_int2(sg.x, i);
+                    if (j < kFewSegs) s_few[par ^ 1][j] = make_int2(sg.x, i);
+                }
+                if (sg.y - i > 1) {
+                    const int j = atomicAdd(&s_next, 1);
+                    sb[j] = make_int2(i, sg.y);
+                    if (j < kFewSegs) s_few[par ^ 1][j] = make_int2(i, sg.y);
+                }
             }
         }
         __syncthreads();
@@ -506,6 +596,7 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
         int2 *t = sa;
         sa = sb;
         sb = t;
+        par ^= 1;
         __syncthreads();
     }
     // the kept points (the closing copy excluded), and their extremes
