@@ -142,3 +142,21 @@ def test_pp_page_pipeline(gpu):
             bad, _ = argmax_parity(bests[line], logits[j])
             assert bad == 0
         k += n
+
+
+def test_db_boxes_at_the_score_threshold(gpu):
+    """box_thresh equal to boxes' exact scores (and one ulp either side): the order-free bound
+    cannot settle those boxes, so the ordered score decides, and the boxes still equal the
+    oracle's."""
+    from _helpers import db_map
+
+    prob = db_map(4)
+    h, w = prob.shape
+    tp = (3.4647, 3.4375)
+    rects = ref.word_rects(pack_bits(prob > np.float32(0.3)), w, h, 0.0, 0.0, -np.inf)
+    rects = rects[np.minimum(rects[:, 4], rects[:, 5]) >= 3]
+    scores = ref.db_scores(prob, rects)
+    for s in scores[:: max(1, len(scores) // 6)]:
+        for t in (np.nextafter(s, np.float32(-1)), s, np.nextafter(s, np.float32(2))):
+            want = ref.db_boxes(prob, tp, 0.3, float(t))
+            np.testing.assert_array_equal(gpu.db_boxes(prob, tp, 0.3, float(t)), want)

@@ -1449,11 +1449,9 @@ int32_t wocr_ppdet_mask(wocr_ndgraph *g, float thresh, uint32_t *mask, int64_t c
 
 namespace {
 
-// `score` (src/ppdet.rs:63-83) of rects [n][6] on the device map prob (w x h), into host scores.
-void db_score_boxes(Ctx *c, const float *prob, int w, int h, const float *rects, int n, float *scores) {
-    if (n == 0) return;
-    // the scan rectangle: the box's bounding rectangle (its four corners), floor / ceil,
-    // clamped to the map as score() clamps it
+// The score boxes of rects [n][6] on a w x h map: the scan rectangle is the box's bounding
+// rectangle (its four corners), floor / ceil, clamped to the map as score() clamps it.
+std::vector<k::DbBox> db_make_boxes(const float *rects, int n, int w, int h) {
     std::vector<k::DbBox> bx((size_t)n);
     for (int i = 0; i < n; i++) {
         const float *r = rects + 6 * (size_t)i;
@@ -1481,6 +1479,13 @@ void db_score_boxes(Ctx *c, const float *prob, int w, int h, const float *rects,
         b.x1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_x) + 1.f), std::max(w - 1, 0));
         b.y1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_y) + 1.f), std::max(h - 1, 0));
     }
+    return bx;
+}
+
+// `score` (src/ppdet.rs:63-83) of rects [n][6] on the device map prob (w x h), into host scores.
+void db_score_boxes(Ctx *c, const float *prob, int w, int h, const float *rects, int n, float *scores) {
+    if (n == 0) return;
+    const std::vector<k::DbBox> bx = db_make_boxes(rects, n, w, h);
     BufP db = alloc(c, bx.size() * sizeof(k::DbBox)), ds = alloc(c, (size_t)n * 4);
     WOCR_CUDA(cudaMemcpyAsync(db->p, bx.data(), bx.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice, c->stream));
     k::db_scores(c, prob, w, h, (const k::DbBox *)db->p, n, (float *)ds->p);
@@ -1521,13 +1526,62 @@ std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float
         if (std::min(r[4], r[5]) >= min_size) cand.insert(cand.end(), r, r + 6);
     }
     const int nc = (int)(cand.size() / 6);
-    std::vector<float> sc((size_t)nc);
-    db_score_boxes(c, prob, w, h, cand.data(), nc, sc.data());
+    // `score < box_thresh` per candidate.  The ordered f32 sum S of a box's n inside values lies
+    // within gamma(n - 1) * sum |v| of their exact sum (gamma(k) = k u / (1 - k u), u = 2^-24),
+    // and the division by n adds a rounding; an order-free pass (sum in double) settles every box
+    // whose mean is clear of box_thresh by that margin, and only the rest get the ordered score.
+    std::vector<char> below((size_t)nc, 0);
+    if (nc > 0) {
+        const std::vector<k::DbBox> bx = db_make_boxes(cand.data(), nc, w, h);
+        BufP db = alloc(c, bx.size() * sizeof(k::DbBox)), dsum = alloc(c, (size_t)nc * 16),
+             dcnt = alloc(c, (size_t)nc * 8);
+        WOCR_CUDA(cudaMemcpyAsync(db->p, bx.data(), bx.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice, c->stream));
+        k::db_bounds(c, prob, w, (const k::DbBox *)db->p, nc, (double *)dsum->p, (long long *)dcnt->p);
+        std::vector<double> sums((size_t)nc * 2);
+        std::vector<long long> cnts((size_t)nc);
+        d2h(c, sums.data(), dsum->p, sums.size() * 8);
+        d2h(c, cnts.data(), dcnt->p, cnts.size() * 8);
+        sync_bounded(c, 0);
+        std::vector<float> amb;
+        std::vector<int> amb_idx;
+        const double u = std::ldexp(1.0, -24);
+        for (int i = 0; i < nc; i++) {
+            const long long n = cnts[i];
+            if (n == 0) {  // no pixel inside: the score is 0
+                below[i] = 0.f < box_thresh;
+                continue;
+            }
+            const double S = sums[2 * (size_t)i], A = sums[2 * (size_t)i + 1], ku = (double)(n - 1) * u;
+            bool settled = std::isfinite(S) && std::isfinite(A) && ku < 0.25;
+            if (settled) {
+                // f32 ordering error, plus the double pass's own (far below it), doubled for safety
+                const double err = 2.0 * (ku / (1.0 - ku) + (double)n * std::ldexp(1.0, -52)) * A;
+                double lo = (S - err) / (double)n, hi = (S + err) / (double)n;
+                lo -= std::fabs(lo) * 4.0 * u;  // the f32 division (and n's conversion past 2^24)
+                hi += std::fabs(hi) * 4.0 * u;
+                if (hi < (double)box_thresh)
+                    below[i] = 1;
+                else if (lo >= (double)box_thresh)
+                    below[i] = 0;
+                else
+                    settled = false;
+            }
+            if (!settled) {
+                amb.insert(amb.end(), cand.data() + 6 * (size_t)i, cand.data() + 6 * (size_t)i + 6);
+                amb_idx.push_back(i);
+            }
+        }
+        if (!amb_idx.empty()) {
+            std::vector<float> sc(amb_idx.size());
+            db_score_boxes(c, prob, w, h, amb.data(), (int)amb_idx.size(), sc.data());
+            for (size_t j = 0; j < amb_idx.size(); j++) below[amb_idx[j]] = sc[j] < box_thresh;
+        }
+    }
     std::vector<float> out;
     const float s = (to_page[0] + to_page[1]) / 2.0f;
     for (int i = 0; i < nc; i++) {
         const float *r = cand.data() + 6 * (size_t)i;
-        if (sc[i] < box_thresh) continue;
+        if (below[i]) continue;
         const float rw = r[4], rh = r[5];
         const float per = 2.0f * (rw + rh);
         const float d = rw * rh * unclip_ratio / (per > 1e-6f ? per : 1e-6f);

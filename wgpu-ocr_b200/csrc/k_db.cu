@@ -113,7 +113,68 @@ __global__ void __launch_bounds__(kDbWarps * 32) k_db_scores(const float *__rest
     if (lane == 0) scores[k] = cnt == 0 ? 0.f : __fdiv_rn(sum, (float)cnt);
 }
 
+// Per box, the inside pixels' count, their sum in double and the sum of their magnitudes, in
+// any order (a block per box over its bounding rectangle, the same inside test as above): enough
+// to bound the ordered f32 score without forming it.
+constexpr int kDbBoundT = 256;
+
+__global__ void __launch_bounds__(kDbBoundT) k_db_bounds(const float *__restrict__ prob, int w,
+                                                         const DbBox *__restrict__ boxes, double *__restrict__ sums,
+                                                         long long *__restrict__ counts) {
+    __shared__ double s_s[kDbBoundT / 32], s_a[kDbBoundT / 32];
+    __shared__ long long s_c[kDbBoundT / 32];
+    const DbBox b = boxes[blockIdx.x];
+    const int bw = b.x1 - b.x0 + 1, bh = b.y1 - b.y0 + 1;
+    double sum = 0.0, mag = 0.0;
+    long long cnt = 0;
+    if (bw > 0 && bh > 0) {
+        const int64_t total = (int64_t)bw * bh;
+        for (int64_t g = threadIdx.x; g < total; g += kDbBoundT) {
+            const int y = b.y0 + (int)(g / bw), x = b.x0 + (int)(g % bw);
+            const float dy = __fsub_rn((float)y, b.cy), dx = __fsub_rn((float)x, b.cx);
+            const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
+            const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
+            if (fabsf(along) <= b.hh && fabsf(across) <= b.hw) {
+                const double v = (double)prob[(int64_t)y * w + x];
+                sum += v;
+                mag += fabs(v);
+                cnt++;
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        mag += __shfl_xor_sync(0xffffffffu, mag, o);
+        cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    }
+    const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+    if (lane == 0) {
+        s_s[wi] = sum;
+        s_a[wi] = mag;
+        s_c[wi] = cnt;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < kDbBoundT / 32; i++) {
+            sum += s_s[i];
+            mag += s_a[i];
+            cnt += s_c[i];
+        }
+        sums[2 * blockIdx.x] = sum;
+        sums[2 * blockIdx.x + 1] = mag;
+        counts[blockIdx.x] = cnt;
+    }
+}
+
 }  // namespace
+
+void db_bounds(Ctx *c, const float *prob, int w, const DbBox *boxes, int n, double *sums, long long *counts) {
+    if (n <= 0) return;
+    Prof pf(c, "db_bounds", 0, 0);
+    k_db_bounds<<<n, kDbBoundT, 0, c->stream>>>(prob, w, boxes, sums, counts);
+    WOCR_LAUNCHED(c);
+}
 
 void db_mask(Ctx *c, const float *prob, int w, int h, float thr, uint32_t *bits) {
     const int words = (w + 31) / 32;
