@@ -128,17 +128,20 @@ __global__ void __launch_bounds__(kDbBoundT) k_db_bounds(const float *__restrict
     double sum = 0.0, mag = 0.0;
     long long cnt = 0;
     if (bw > 0 && bh > 0) {
-        const int64_t total = (int64_t)bw * bh;
-        for (int64_t g = threadIdx.x; g < total; g += kDbBoundT) {
-            const int y = b.y0 + (int)(g / bw), x = b.x0 + (int)(g % bw);
-            const float dy = __fsub_rn((float)y, b.cy), dx = __fsub_rn((float)x, b.cx);
-            const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
-            const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
-            if (fabsf(along) <= b.hh && fabsf(across) <= b.hw) {
-                const double v = (double)prob[(int64_t)y * w + x];
-                sum += v;
-                mag += fabs(v);
-                cnt++;
+        // a warp per row, lanes along it (coalesced)
+        for (int y = b.y0 + (int)(threadIdx.x >> 5); y <= b.y1; y += kDbBoundT / 32) {
+            const float dy = __fsub_rn((float)y, b.cy);
+            const float *row = prob + (int64_t)y * w;
+            for (int x = b.x0 + (int)(threadIdx.x & 31); x <= b.x1; x += 32) {
+                const float dx = __fsub_rn((float)x, b.cx);
+                const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));
+                const float across = __fadd_rn(__fmul_rn(dx, -b.uy), __fmul_rn(dy, b.ux));
+                if (fabsf(along) <= b.hh && fabsf(across) <= b.hw) {
+                    const double v = (double)row[x];
+                    sum += v;
+                    mag += fabs(v);
+                    cnt++;
+                }
             }
         }
     }
