@@ -255,8 +255,8 @@ __device__ __forceinline__ uint32_t row_win(const uint32_t *m, int words, int w,
 // from the left one, (3.3) the first counterclockwise from the one after the previous point: a
 // rotate of the 8 neighbour bits (bit d = neighbour d) and a leading-zero count.  A border is at
 // most 4 points a pixel; past that the status word is set and the trace stops.
-template <bool WRITE>
-__device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, short2 *out, int *status) {
+// Points are written to out while their index is below wcap (0: count only).
+__device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, short2 *out, int wcap, int *status) {
     int wx0 = x - 16;
     uint32_t up = row_win(m, words, w, h, y - 1, wx0), mid = row_win(m, words, w, h, y, wx0),
              dn = row_win(m, words, w, h, y + 1, wx0);
@@ -268,7 +268,7 @@ __device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, 
     };
     uint32_t nb = nbits(x);
     if (nb == 0) {
-        if (WRITE) out[0] = make_short2((short)x, (short)y);
+        if (wcap > 0) out[0] = make_short2((short)x, (short)y);
         return 1;
     }
     const int d1 = __ffs(nb) - 1;
@@ -276,7 +276,7 @@ __device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, 
     int x3 = x, y3 = y, e = d1, n = 0;
     const int64_t cap = 4 * (int64_t)w * h + 8;
     for (;;) {
-        if (WRITE) out[n] = make_short2((short)x3, (short)y3);
+        if (n < wcap) out[n] = make_short2((short)x3, (short)y3);
         n++;
         // counterclockwise from e - 1: bit t -> 7, t - 1 -> 6, ...; the first set is the highest
         const int t = (e - 1) & 7;
@@ -310,16 +310,18 @@ __device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, 
     return n;
 }
 
-// A warp per component, lane 0 tracing: lanes of one warp would wait on each other's loads.
+// A warp per component, lane 0 tracing: lanes of one warp would wait on each other's loads.  The
+// first cache_cap points go to the component's cache slot, so borders no longer than that are
+// not followed a second time.
 __global__ void __launch_bounds__(32) k_trace_len(const uint32_t *__restrict__ mask, int words, int w, int h,
                                                   const int *__restrict__ run_x, const int *__restrict__ run_row,
                                                   const int *__restrict__ comp_run, int C, int *__restrict__ len,
-                                                  int *status) {
+                                                  short2 *__restrict__ cache, int cache_cap, int *status) {
     const int k = blockIdx.x;
     if (k >= C || threadIdx.x != 0) return;
     const int r = comp_run[k], row = run_row[r];
     const uint32_t *m = mask + (int64_t)(row / h) * h * words;
-    len[k] = follow<false>(m, words, w, h, run_x[r], row % h, nullptr, status);
+    len[k] = follow(m, words, w, h, run_x[r], row % h, cache + (int64_t)k * cache_cap, cache_cap, status);
 }
 
 // ---- per-component geometry ------------------------------------------------------------------
@@ -372,6 +374,8 @@ struct WordP {
     const uint32_t *mask;
     int words, w, h;
     const int *run_x, *run_row, *comp_run, *pt_off, *len;
+    const short2 *cache;  // the length pass's first cache_cap points of each border
+    int cache_cap;
     int C;
     // per component, n + 1 slots each (n border points; slot base = pt_off[k] + k)
     short2 *pts;       // its border, then the first point again
@@ -453,10 +457,20 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
     const int r = p.comp_run[k], row = p.run_row[r];
     const int64_t base = (int64_t)p.pt_off[k] + k;
     short2 *pts = p.pts + base;
+    const int L = p.len[k];
+    if (L <= p.cache_cap) {  // the border is in the cache: copy it
+        const short2 *src = p.cache + (int64_t)k * p.cache_cap;
+        for (int i = tid; i < L; i += T) pts[i] = src[i];
+    }
     if (tid == 0) {
-        const uint32_t *m = p.mask + (int64_t)(row / p.h) * p.h * p.words;
-        const int nb = follow<true>(m, p.words, p.w, p.h, p.run_x[r], row % p.h, pts, p.status);
-        pts[nb] = pts[0];
+        int nb = L;
+        if (L <= p.cache_cap) {
+            pts[nb] = p.cache[(int64_t)k * p.cache_cap];
+        } else {
+            const uint32_t *m = p.mask + (int64_t)(row / p.h) * p.h * p.words;
+            nb = follow(m, p.words, p.w, p.h, p.run_x[r], row % p.h, pts, 0x7fffffff, p.status);
+            pts[nb] = pts[0];
+        }
         s_n = nb + 1;
         s_nseg = 0;
         if (nb + 1 > 2) {
@@ -822,13 +836,16 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
         return res;
     }
     BufP crun = alloc(c, (size_t)C * 4), len = alloc(c, (size_t)C * 4), ptoff = alloc(c, (size_t)C * 4);
+    // border cache of the length pass: 256 MiB shared by the components, 64 .. 16384 points each
+    const int cache_cap = (int)std::min<int64_t>(16384, std::max<int64_t>(64, ((int64_t)64 << 20) / C));
+    BufP cache = alloc(c, (size_t)C * cache_cap * 4);
     k_ext_list<<<blocks(R, 256), 256, 0, c->stream>>>(run_x, run_c, run_row, P, R, h, pages, (const int *)pos->p,
                                                       (int *)crun->p);
     WOCR_LAUNCHED(c);
     {
         Prof pf(c, "word_trace", 0, 0);
         k_trace_len<<<C, 32, 0, c->stream>>>(mask, words, w, h, run_x, run_row, (const int *)crun->p, C,
-                                                         (int *)len->p, c->status);
+                                             (int *)len->p, (short2 *)cache->p, cache_cap, c->status);
         WOCR_LAUNCHED(c);
     }
     scan_i32(c, (const int *)len->p, C, (int *)ptoff->p, d_tot);
@@ -847,6 +864,8 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     p.comp_run = (const int *)crun->p;
     p.pt_off = (const int *)ptoff->p;
     p.len = (const int *)len->p;
+    p.cache = (const short2 *)cache->p;
+    p.cache_cap = cache_cap;
     p.C = C;
     p.pts = (short2 *)pts->p;
     p.keep = (uint8_t *)keep->p;
