@@ -324,6 +324,17 @@ __global__ void __launch_bounds__(32) k_trace_len(const uint32_t *__restrict__ m
     len[k] = follow(m, words, w, h, run_x[r], row % h, cache + (int64_t)k * cache_cap, cache_cap, status);
 }
 
+// Block sizes of k_word_rect: components of more than kBigLen border points get kWTBig threads.
+// A Douglas-Peucker level of at most kFewSegs open segments runs each segment with the whole
+// block (a shuffle and shared-memory argmax) instead of the flat scan over all of them.
+constexpr int kWT = 128, kWTBig = 1024, kBigLen = 4096, kSortCap = 2048, kFewSegs = 4;
+
+// the components whose border is longer than kBigLen, for the wide instance of k_word_rect
+__global__ void k_big_list(const int *__restrict__ len, int C, int *__restrict__ big, int *__restrict__ nbig) {
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k < C && len[k] > kBigLen) big[atomicAdd(nbig, 1)] = k;
+}
+
 // ---- per-component geometry ------------------------------------------------------------------
 
 __device__ __forceinline__ float sq_len(float x, float y) { return __fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y)); }
@@ -376,6 +387,7 @@ struct WordP {
     const int *run_x, *run_row, *comp_run, *pt_off, *len;
     const short2 *cache;  // the length pass's first cache_cap points of each border
     int cache_cap;
+    const int *big;       // for the kWTBig instance: the components of more than kBigLen points
     int C;
     // per component, n + 1 slots each (n border points; slot base = pt_off[k] + k)
     short2 *pts;       // its border, then the first point again
@@ -391,10 +403,6 @@ struct WordP {
     int *status;
 };
 
-// Block sizes of k_word_rect: components of more than kBigLen border points get kWTBig threads.
-// A Douglas-Peucker level of at most kFewSegs open segments runs each segment with the whole
-// block (a shuffle and shared-memory argmax) instead of the flat scan over all of them.
-constexpr int kWT = 128, kWTBig = 1024, kBigLen = 4096, kSortCap = 2048, kFewSegs = 4;
 
 // exclusive prefix of size(i) for i < n into out; returns the total (all threads)
 template <int T, typename F>
@@ -452,7 +460,8 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
     __shared__ uint32_t s_sort[kSortCap];
     __shared__ int2 s_few[2][kFewSegs];                   // a level's segments when few (by parity)
     __shared__ unsigned long long s_wbest[kFewSegs][T / 32];
-    const int k = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int k = T == kWTBig ? p.big[blockIdx.x] : (int)blockIdx.x, tid = threadIdx.x, lane = tid & 31,
+              warp = tid >> 5;
     if (k >= p.C || (p.len[k] > kBigLen) != (T == kWTBig)) return;  // the other instance's component
     const int r = p.comp_run[k], row = p.run_row[r];
     const int64_t base = (int64_t)p.pt_off[k] + k;
@@ -848,8 +857,14 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
                                              (int *)len->p, (short2 *)cache->p, cache_cap, c->status);
         WOCR_LAUNCHED(c);
     }
+    BufP big = alloc(c, (size_t)C * 4), nbig = alloc(c, 4);
+    WOCR_CUDA(cudaMemsetAsync(nbig->p, 0, 4, c->stream));
+    k_big_list<<<blocks(C, 256), 256, 0, c->stream>>>((const int *)len->p, C, (int *)big->p, (int *)nbig->p);
+    WOCR_LAUNCHED(c);
     scan_i32(c, (const int *)len->p, C, (int *)ptoff->p, d_tot);
-    const int64_t slots = (int64_t)read_int(c, d_tot) + C;
+    int n_big = 0;
+    WOCR_CUDA(cudaMemcpyAsync(&n_big, nbig->p, 4, cudaMemcpyDeviceToHost, c->stream));
+    const int64_t slots = (int64_t)read_int(c, d_tot) + C;  // (its sync also brings n_big)
     BufP pts = alloc(c, (size_t)slots * 4), keep = alloc(c, (size_t)slots), sega = alloc(c, (size_t)slots * 8);
     BufP segb = alloc(c, (size_t)slots * 8), pref = alloc(c, (size_t)slots * 4), best = alloc(c, (size_t)slots * 8);
     BufP keys = alloc(c, (size_t)slots * 4), hull = alloc(c, (size_t)(2 * slots + C) * 4);
@@ -866,6 +881,7 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     p.len = (const int *)len->p;
     p.cache = (const short2 *)cache->p;
     p.cache_cap = cache_cap;
+    p.big = (const int *)big->p;
     p.C = C;
     p.pts = (short2 *)pts->p;
     p.keep = (uint8_t *)keep->p;
@@ -885,8 +901,10 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
         Prof pf(c, "word_rect", 0, 0);
         k_word_rect<kWT><<<C, kWT, 0, c->stream>>>(p);
         WOCR_LAUNCHED(c);
-        k_word_rect<kWTBig><<<C, kWTBig, 0, c->stream>>>(p);
-        WOCR_LAUNCHED(c);
+        if (n_big > 0) {
+            k_word_rect<kWTBig><<<n_big, kWTBig, 0, c->stream>>>(p);
+            WOCR_LAUNCHED(c);
+        }
     }
     scan_i32(c, (const int *)valid->p, C, (int *)vpos->p, d_tot);
     res.n = read_int(c, d_tot);
