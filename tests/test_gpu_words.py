@@ -112,15 +112,13 @@ def test_ppdet_boxes_on_detector_map(gpu):
     np.testing.assert_array_equal(got, ref.db_boxes(prob, tp, 0.3))
 
 
-def test_pp_page_pipeline(gpu):
-    """The PP-OCRv6 page pipeline (`wocr_pp_page`) against its stages: its boxes are the DB boxes
-    of the detector's map (bit-exact), and each line's arg-max classes equal the oracle's
-    recognition of the same line images (up to near-ties at the oracle's precision)."""
+def _check_pipeline(gpu, det, page, w, h, min_lines, min_batches):
+    """wocr_pp_page against its stages: its boxes are the DB boxes of the detector's map
+    (bit-exact), and each line's arg-max classes equal the oracle's recognition of the same line
+    images (up to near-ties at the oracle's precision), line by line in reading order."""
     from _helpers import argmax_parity
 
-    det, rec = synth.pp_det_model(), synth.pp_rec_model()
-    w, h = 1275, 1650
-    page = synth.page(6, w, h)
+    rec = synth.pp_rec_model()
     with wocr.PPPipeline(gpu, det, rec) as pp:
         boxes, bests = pp.page(page, w, h)
     g = wocr.NdGraph(gpu, det)
@@ -129,9 +127,9 @@ def test_pp_page_pipeline(gpu):
     finally:
         g.close()
     np.testing.assert_array_equal(boxes, ref.db_boxes(prob, tp, 0.3))
-    assert len(bests) == len(boxes) > 0
-    rects = ref.pp_line_rects(boxes, 0.1)
-    batches, order = ref.pp_batches(page, rects)
+    assert len(bests) == len(boxes) >= min_lines
+    batches, order = ref.pp_batches(page, ref.pp_line_rects(boxes, 0.1))
+    assert len(batches) >= min_batches
     k = 0
     for data, n, width in batches:
         logits = ref.run_onnx(rec, data, stop_before_softmax=True)
@@ -140,8 +138,19 @@ def test_pp_page_pipeline(gpu):
             line = order[k + j]
             assert len(bests[line]) == T
             bad, _ = argmax_parity(bests[line], logits[j])
-            assert bad == 0
+            assert bad == 0, f"line {line}: {bad} steps differ"
         k += n
+
+
+def test_pp_page_pipeline(gpu):
+    """The PP-OCRv6 page pipeline with the random-init DB detector (one page-sized box)."""
+    _check_pipeline(gpu, synth.pp_det_model(), synth.page(6, 1275, 1650), 1275, 1650, 1, 1)
+
+
+def test_pp_page_pipeline_many_lines(gpu):
+    """The pipeline with a detector that marks word blobs: over a hundred boxes in reading order,
+    recognised in width-sorted batches whose results must come back to the right lines."""
+    _check_pipeline(gpu, synth.pp_ink_det_model(), synth.page(6, 1275, 1650, bands=10), 1275, 1650, 100, 5)
 
 
 def test_db_boxes_at_the_score_threshold(gpu):

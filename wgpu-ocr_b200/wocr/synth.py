@@ -303,6 +303,20 @@ def pp_rec_model(seed: int = 2, classes: int = PP_CLASSES) -> Model:
 # ---------------------------------------------------------------------------------------
 # config 4: PP-OCRv6-style DB detector
 # ---------------------------------------------------------------------------------------
+def pp_ink_det_model(gain: float = 1.2, bias: float = -2.0) -> Model:
+    """A hand-set stand-in for a trained DB detector, for tests of the page pipeline (not a
+    benchmark model): darkness (a 1 x 1 conv summing the normalised channels, negated), a 3 x 9
+    box average that joins the glyphs of a word, and a sigmoid.  On page(...) it marks word blobs,
+    so a page yields hundreds of DB boxes instead of the one page-sized box of the random-init
+    detector."""
+    b = _Builder(0)
+    ins = ["x", b.w("W", -np.ones((1, 3, 1, 1))), b.w("B", np.zeros(1))]
+    d = b.op("Conv", ins, {"kernel_shape": [1, 1], "pads": [0, 0, 0, 0], "strides": [1, 1], "dilations": [1, 1]})
+    ins = [d, b.w("W", np.full((1, 1, 3, 9), gain / 27.0)), b.w("B", np.full(1, bias))]
+    a = b.op("Conv", ins, {"kernel_shape": [3, 9], "pads": [1, 4, 1, 4], "strides": [1, 1], "dilations": [1, 1]})
+    return b.model("x", b.op("Sigmoid", [a]))
+
+
 def pp_det_model(seed: int = 3) -> Model:
     b = _Builder(seed)
     x = "x"                                                              # [1, 3, H, W]
