@@ -47,10 +47,11 @@ def parse():
     p.add_argument("--pages", type=int, default=12, help="pages per GPU per step")
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
-    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pp4", "pplines", "words1"],
+    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pp4", "pp4ink", "pplines", "words1"],
                    help="det1 (default, the driver's line): config 1 detection; rec0 / pp3 / ppdet4: configs "
                         "0, 3 and 4 through their public calls; ppdb4: config 4 with the DB mask and box "
-                        "scores on the device; pp4: the full PP-OCRv6 page pipeline; pplines: PP line extraction; "
+                        "scores on the device; pp4: the full PP-OCRv6 page pipeline (pp4ink: with a hand-set ink "
+                        "detector, hundreds of lines a page); pplines: PP line extraction; "
                         "words1: word rectangles of config 1 detection masks (secondary measurements)")
     return p.parse_args()
 
@@ -453,18 +454,21 @@ def run_workload(args):
         def cpu():
             ref.word_rects(masks[0], W_PAGE, H_PAGE)
             return 1, "1 page"
-    elif args.workload == "pp4":
-        det_m, rec_m = synth.pp_det_model(), synth.pp_rec_model()
+    elif args.workload in ("pp4", "pp4ink"):
+        ink = args.workload == "pp4ink"
+        det_m, rec_m = (synth.pp_ink_det_model() if ink else synth.pp_det_model()), synth.pp_rec_model()
         handle = wocr.PPPipeline(gpu, det_m, rec_m)
         npg = 12
         pages = [synth.page(3000 + k, W_PAGE, H_PAGE) for k in range(npg)]
         nlines = sum(len(handle.page(pg, W_PAGE, H_PAGE)[0]) for pg in pages)
-        units, unit, workload = npg, "pages/s", (f"config 4 full page: PP-OCRv6-style DB detection of {npg} "
-                                                 f"2550x3300 pages (seeds 3000..3011; 3x960x736), DB boxes at 0.3 "
-                                                 f"on the device, lines grown 0.1 x height, cut and batched 16 by "
-                                                 f"width on the device, PP recognition arg-max per batch; "
-                                                 f"{nlines} lines (random-init det weights mark most of the page, "
-                                                 f"so a page gives few large boxes)")
+        detector = ("a hand-set ink detector (darkness, 3x9 box average, sigmoid) standing in for trained DB "
+                    "weights, which marks word blobs" if ink else
+                    "the PP-OCRv6-style DB detector (random-init weights mark most of the page, so a page gives "
+                    "few large boxes)")
+        units, unit, workload = npg, "pages/s", (f"config 4 full page: {detector}; {npg} 2550x3300 pages (seeds "
+                                                 f"3000..3011; 3x960x736), DB boxes at 0.3 on the device, lines "
+                                                 f"grown 0.1 x height, cut and batched 16 by width on the device, "
+                                                 f"PP recognition arg-max per batch; {nlines} lines")
         h2d, d2h = npg * W_PAGE * H_PAGE * 3, 0
 
         def step():
