@@ -355,10 +355,11 @@ def run_b200(args):
 
 
 def run_workload(args):
-    """Configs 0, 3 and 4 through the public calls a user makes (host inputs, as the reference's
-    Recognizer::recognize, NdGraph::run + argmax and the PP detection page take them).  `value`:
-    units over the context stream's busy time (CUDA events; the H2D copies the call makes are
-    inside); `e2e`: the same over wall-clock time of the calls."""
+    """Configs 0, 3 and 4 and the next rows through the public calls a user makes (host inputs in
+    pinned memory, as the reference's Recognizer::recognize, NdGraph::run + argmax and the PP
+    detection page take them; device pages for the line and word kernels).  `value`: units over
+    the context stream's busy time (CUDA events; the H2D copies the call makes are inside);
+    `e2e`: the same over wall-clock time of the calls."""
     import numpy as np
     import torch
 
@@ -372,9 +373,24 @@ def run_workload(args):
     gpu = wocr.Gpu(lines=8, device=local)
     stream = torch.cuda.ExternalStream(gpu.stream, device=dev)
     ref.set_threads(os.cpu_count() or 1)
+    held = []
+
+    def pinned(a):
+        """A copy of `a` in page-locked host memory (`wocr_host_alloc`): the timed calls' inputs
+        come from pinned memory, as the driver's end-to-end contract asks."""
+        import ctypes
+        p = ctypes.c_void_p()
+        wocr._lib.check(wocr.lib().wocr_host_alloc(max(a.nbytes, 1), ctypes.byref(p)))
+        held.append(p)
+        out = np.frombuffer((ctypes.c_char * max(a.nbytes, 1)).from_address(p.value), dtype=a.dtype,
+                            count=a.size).reshape(a.shape)
+        out[...] = a
+        return out
+
     if args.workload == "rec0":
         model = synth.ocrs_rec_model()
         batches, _, _ = synth.ocrs_batches(synth.ocrs_lines(0, n=64))
+        batches = [(pinned(np.ascontiguousarray(d, np.float32)), n, w) for d, n, w in batches]
         handle = wocr.Recognizer(gpu, model)
         units, unit, workload = 64, "lines/s", ("config 0: ocrs recognition, 64 lines 1x64xW (W ~ U{64..1024}), "
                                                 "conv trunk + 2-layer biGRU(256) + Linear 512->97, seed 0")
@@ -393,6 +409,7 @@ def run_workload(args):
     elif args.workload == "pp3":
         model = synth.pp_rec_model()
         batches, _ = synth.pp_batches(synth.pp_lines(2, n=256))
+        batches = [(pinned(np.ascontiguousarray(d, np.float32)), n, w) for d, n, w in batches]
         handle = wocr.NdGraph(gpu, model, stop_before_softmax=True)
         units, unit, workload = 256, "lines/s", ("config 3: PP-OCRv6-style recognition, 256 lines 3x48xW "
                                                  "(W ~ U{96..1280}), trunk + 2 SVTR blocks + CTC head 120->18709, "
@@ -459,7 +476,7 @@ def run_workload(args):
         det_m, rec_m = (synth.pp_ink_det_model() if ink else synth.pp_det_model()), synth.pp_rec_model()
         handle = wocr.PPPipeline(gpu, det_m, rec_m)
         npg = 12
-        pages = [synth.page(3000 + k, W_PAGE, H_PAGE) for k in range(npg)]
+        pages = [pinned(synth.page(3000 + k, W_PAGE, H_PAGE)) for k in range(npg)]
         nlines = sum(len(handle.page(pg, W_PAGE, H_PAGE)[0]) for pg in pages)
         detector = ("a hand-set ink detector (darkness, 3x9 box average, sigmoid) standing in for trained DB "
                     "weights, which marks word blobs" if ink else
@@ -486,7 +503,7 @@ def run_workload(args):
             return 1, f"1 page ({len(boxes)} lines)"
     elif args.workload == "ppdb4":
         model = synth.pp_det_model()
-        page = synth.page(3, W_PAGE, H_PAGE)
+        page = pinned(synth.page(3, W_PAGE, H_PAGE))
         handle = wocr.NdGraph(gpu, model)
         _, tp = handle.ppdet_page(page, W_PAGE, H_PAGE, 960, read_map=False)
         rects = synth.page_db_candidates(3, W_PAGE, H_PAGE, tp)
@@ -509,7 +526,7 @@ def run_workload(args):
             return 1, "1 page"
     else:
         model = synth.pp_det_model()
-        page = synth.page(3, W_PAGE, H_PAGE)
+        page = pinned(synth.page(3, W_PAGE, H_PAGE))
         handle = wocr.NdGraph(gpu, model)
         units, unit, workload = 1, "pages/s", ("config 4 detection: PP-OCRv6-style DB detector on a 2550x3300 "
                                                "page resized to 3x960x736, seed 3, probability map read back")
@@ -563,6 +580,8 @@ def run_workload(args):
         print(json.dumps(line), flush=True)
     if handle is not None:
         handle.close()
+    for p in held:
+        wocr.lib().wocr_host_free(p)
     return 0
 
 
