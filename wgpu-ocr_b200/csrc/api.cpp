@@ -188,7 +188,9 @@ struct wocr_ndgraph {
     wocr_ctx *ctx;
     std::unique_ptr<Executor> graph;
     Stats last;
-    NdReplay replays[8];
+    // captured runs per input shape: config 3 recognises 16 width buckets a step, so the cache
+    // holds more than that (an LRU of fewer entries would miss on every call of such a cycle)
+    NdReplay replays[32];
     uint64_t uses = 0;
     // the probability map of the last wocr_ppdet_page ([map_h][map_w] fp32) for the DB steps
     BufP map_buf;
