@@ -171,11 +171,14 @@ __device__ __forceinline__ void load8_tab(const UmmaP &p, const ARow &r, uint32_
     }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CHAINS>
 __global__ void __launch_bounds__(kAllThreads, 1)
     k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo, UmmaP p) {
     using Lay = Layout<BN, STAGES>;
-    constexpr int NACC = Acc<BN>::n;
+    // CHAINS: accumulation chains per tile (0: Acc<BN>'s choice); one chain sums in the order of
+    // the 128- and 256-column tiles, so a narrowed launch gives their results to the bit
+    constexpr int NCH = CHAINS ? CHAINS : Acc<BN>::chains, TCOLS = BN * NCH;
+    constexpr int NACC = 512 / TCOLS < 8 ? 512 / TCOLS : 8;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *afull = reinterpret_cast<uint64_t *>(smem + Lay::bar_off);
@@ -192,7 +195,6 @@ __global__ void __launch_bounds__(kAllThreads, 1)
     const int ntn = (p.N + BN - 1) / BN;
     const int64_t ntiles = ((p.M + BM - 1) / BM) * ntn;
     // two accumulators of BN fp32 columns each
-    constexpr int NCH = Acc<BN>::chains, TCOLS = Acc<BN>::cols;
     constexpr uint32_t kCols = NACC * TCOLS <= 32 ? 32 : (NACC * TCOLS <= 64 ? 64 : (NACC * TCOLS <= 128 ? 128 : (NACC * TCOLS <= 256 ? 256 : 512)));
 
     if (threadIdx.x == 0) {
@@ -501,17 +503,18 @@ void make_map(CUtensorMap *map, void *base, int N, int Kpad, int bn) {
     if (r != CUDA_SUCCESS) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
 }
 
-template <int BN, int STAGES>
-void launch(Ctx *c, const UmmaW &w, const UmmaP &p) {
+template <int BN, int STAGES, int CHAINS = 0>
+void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const UmmaP &p) {
     using Lay = Layout<BN, STAGES>;
     static bool set[64] = {false};
     if (!set[c->device]) {
-        WOCR_CUDA(cudaFuncSetAttribute(k_umma<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lay::total));
+        WOCR_CUDA(cudaFuncSetAttribute(k_umma<BN, STAGES, CHAINS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Lay::total));
         set[c->device] = true;
     }
     int64_t tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     unsigned grid = (unsigned)std::min<int64_t>(tiles, c->sm_count);
-    k_umma<BN, STAGES><<<grid, kAllThreads, Lay::total, c->stream>>>(w.map_hi, w.map_lo, p);
+    k_umma<BN, STAGES, CHAINS><<<grid, kAllThreads, Lay::total, c->stream>>>(map_hi, map_lo, p);
     WOCR_LAUNCHED(c);
 }
 
@@ -549,6 +552,11 @@ UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int
     WOCR_CUDA(cudaStreamSynchronize(c->stream));
     make_map(&w.map_hi, w.hi->p, Npad, w.Kpad, w.bn);
     make_map(&w.map_lo, w.lo->p, Npad, w.Kpad, w.bn);
+    if (w.bn > 64) {
+        make_map(&w.map_hi64, w.hi->p, Npad, w.Kpad, 64);
+        make_map(&w.map_lo64, w.lo->p, Npad, w.Kpad, 64);
+        w.has64 = true;
+    }
     return w;
 }
 
@@ -572,12 +580,20 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
     double bytes = 4.0 * ((double)p.M * w.K / (p.mode == 1 ? (double)p.kh * p.kw : 1.0) + (double)p.M * w.N) +
                    4.0 * (double)w.N * w.Kpad;
     Prof pf(c, p.scatter ? "umma_convt" : (p.mode == 1 ? "umma_conv" : "umma_linear"), flops, bytes);
+    // few row tiles (short inputs): 64-column tiles put more SMs on the launch; the arg-max
+    // partials keep one slot per weight tile, and the scatter epilogue keeps its tile width
+    const int64_t mt = (p.M + BM - 1) / BM, tiles = mt * ((w.N + w.bn - 1) / w.bn);
+    if (w.has64 && !p.part_max && !p.scatter && 2 * tiles <= c->sm_count) {
+        launch<64, 4, 1>(c, w.map_hi64, w.map_lo64, p);
+        c->flops += flops;
+        return;
+    }
     switch (w.bn) {
-    case 16: launch<16, 6>(c, w, p); break;
-    case 32: launch<32, 5>(c, w, p); break;
-    case 64: launch<64, 4>(c, w, p); break;
-    case 128: launch<128, 3>(c, w, p); break;
-    default: launch<256, 2>(c, w, p); break;
+    case 16: launch<16, 6>(c, w.map_hi, w.map_lo, p); break;
+    case 32: launch<32, 5>(c, w.map_hi, w.map_lo, p); break;
+    case 64: launch<64, 4>(c, w.map_hi, w.map_lo, p); break;
+    case 128: launch<128, 3>(c, w.map_hi, w.map_lo, p); break;
+    default: launch<256, 2>(c, w.map_hi, w.map_lo, p); break;
     }
     c->flops += flops;
 }
