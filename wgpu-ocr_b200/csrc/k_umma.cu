@@ -557,6 +557,11 @@ UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int
         make_map(&w.map_lo64, w.lo->p, Npad, w.Kpad, 64);
         w.has64 = true;
     }
+    if (w.bn > 32) {
+        make_map(&w.map_hi32, w.hi->p, Npad, w.Kpad, 32);
+        make_map(&w.map_lo32, w.lo->p, Npad, w.Kpad, 32);
+        w.has32 = true;
+    }
     return w;
 }
 
@@ -580,13 +585,26 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
     double bytes = 4.0 * ((double)p.M * w.K / (p.mode == 1 ? (double)p.kh * p.kw : 1.0) + (double)p.M * w.N) +
                    4.0 * (double)w.N * w.Kpad;
     Prof pf(c, p.scatter ? "umma_convt" : (p.mode == 1 ? "umma_conv" : "umma_linear"), flops, bytes);
-    // few row tiles (short inputs): 64-column tiles put more SMs on the launch; the arg-max
-    // partials keep one slot per weight tile, and the scatter epilogue keeps its tile width
-    const int64_t mt = (p.M + BM - 1) / BM, tiles = mt * ((w.N + w.bn - 1) / w.bn);
-    if (w.has64 && !p.part_max && !p.scatter && 2 * tiles <= c->sm_count) {
-        launch<64, 4, 1>(c, w.map_hi64, w.map_lo64, p);
-        c->flops += flops;
-        return;
+    // few row tiles (short inputs): 64- or 32-column tiles put more SMs on the launch, with the
+    // accumulation chains of the weights' own tile width (so the same sums); the arg-max partials
+    // keep one slot per weight tile, and the scatter epilogue keeps its tile width
+    const int64_t mt = (p.M + BM - 1) / BM;
+    auto fills_half = [&](int bn) { return 2 * mt * ((w.N + bn - 1) / bn) > c->sm_count; };
+    if (!p.part_max && !p.scatter && !fills_half(w.bn)) {
+        const bool wide = w.bn > 64;  // one chain (128 / 256 columns), else two (64)
+        if (w.has32 && !fills_half(64)) {
+            if (wide)
+                launch<32, 5, 1>(c, w.map_hi32, w.map_lo32, p);
+            else
+                launch<32, 5, 2>(c, w.map_hi32, w.map_lo32, p);
+            c->flops += flops;
+            return;
+        }
+        if (w.has64) {
+            launch<64, 4, 1>(c, w.map_hi64, w.map_lo64, p);
+            c->flops += flops;
+            return;
+        }
     }
     switch (w.bn) {
     case 16: launch<16, 6>(c, w.map_hi, w.map_lo, p); break;

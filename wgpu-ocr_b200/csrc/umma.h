@@ -14,10 +14,10 @@ namespace k {
 struct UmmaW {
     BufP hi, lo;
     CUtensorMap map_hi, map_lo;
-    // the same weights in 64-row boxes (bn > 64): a launch with few row tiles takes narrower N
-    // tiles, so more SMs share it
-    CUtensorMap map_hi64, map_lo64;
-    bool has64 = false;
+    // the same weights in 64- and 32-row boxes (when bn is wider): a launch with few row tiles
+    // takes narrower N tiles, so more SMs share it
+    CUtensorMap map_hi64, map_lo64, map_hi32, map_lo32;
+    bool has64 = false, has32 = false;
     int N = 0, K = 0, Kpad = 0, bn = 0;
 };
 
