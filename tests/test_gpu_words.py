@@ -169,3 +169,56 @@ def test_db_boxes_at_the_score_threshold(gpu):
         for t in (np.nextafter(s, np.float32(-1)), s, np.nextafter(s, np.float32(2))):
             want = ref.db_boxes(prob, tp, 0.3, float(t))
             np.testing.assert_array_equal(gpu.db_boxes(prob, tp, 0.3, float(t)), want)
+
+
+def test_post_processing_argument_errors(gpu):
+    """The C entry points of the post-processing reject what they cannot do with a status and a
+    message, as the reference returns Err: a short output buffer (counts still filled, so the
+    caller can size it), pages past 32,767 pixels, a map that is neither given nor computed,
+    missing outputs."""
+    import ctypes
+
+    lib = wocr.lib()
+    m = word_masks()[2]
+    h, w = m.shape
+    bits = pack_bits(m)
+    want = ref.word_rects(bits, w, h)
+    counts = np.zeros(1, np.int32)
+    out = np.zeros((1, 6), np.float32)
+    st = lib.wocr_word_rects(gpu.h, bits.ctypes.data, 1, w, h, 0, 3.0, 0.0, 100.0, out.ctypes.data, 1,
+                             counts.ctypes.data)
+    assert st == 8 and counts[0] == len(want) > 1 and b"rects holds 1" in lib.wocr_last_error()
+    st = lib.wocr_word_rects(gpu.h, bits.ctypes.data, 1, 40000, h, 0, 3.0, 0.0, 100.0, None, 0, counts.ctypes.data)
+    assert st == 1 and b"32767" in lib.wocr_last_error()
+    st = lib.wocr_word_rects(gpu.h, bits.ctypes.data, 1, w, h, 0, 3.0, 0.0, 100.0, None, 0, None)
+    assert st == 1
+
+    prob = np.random.default_rng(0).random((40, 30), dtype=np.float32)
+    tp = np.float32([1, 1])
+    n = ctypes.c_int32()
+    st = lib.wocr_db_boxes(gpu.h, prob.ctypes.data, 30, 40, 0, tp.ctypes.data, 0.2, 0.45, 1.4, 3.0, None, 0,
+                           ctypes.byref(n))
+    assert st == 0
+    if n.value > 0:
+        st = lib.wocr_db_boxes(gpu.h, prob.ctypes.data, 30, 40, 0, tp.ctypes.data, 0.2, 0.45, 1.4, 3.0,
+                               out.ctypes.data, 0, ctypes.byref(n))
+        assert st == 8
+    st = lib.wocr_db_boxes(gpu.h, prob.ctypes.data, 0, 40, 0, tp.ctypes.data, 0.2, 0.45, 1.4, 3.0, None, 0,
+                           ctypes.byref(n))
+    assert st == 1 and b"map size" in lib.wocr_last_error()
+
+    g = wocr.NdGraph(gpu, synth.pp_det_model())
+    try:
+        st = lib.wocr_ppdet_boxes(g.h, 0.2, 0.45, 1.4, 3.0, None, 0, ctypes.byref(n))
+        assert st == 1 and b"wocr_ppdet_page first" in lib.wocr_last_error()
+    finally:
+        g.close()
+    with wocr.PPPipeline(gpu, synth.pp_det_model(), synth.pp_rec_model()) as pp:
+        db = np.float32([0.3, 0.45, 1.4, 3.0])
+        page = synth.page(1, 200, 300)
+        st = lib.wocr_pp_page(pp.h, page.ctypes.data, 200, 300, 960, db.ctypes.data, 0.1, 0, None, 0,
+                              ctypes.byref(n), None, 0, None)
+        assert st == 1 and b"batch" in lib.wocr_last_error()
+        st = lib.wocr_pp_page(pp.h, page.ctypes.data, 200, 300, 960, db.ctypes.data, 0.1, 16, None, 0,
+                              ctypes.byref(n), None, 0, None)
+        assert st == 0 and n.value >= 0                       # boxes only: best = NULL, cap = 0
