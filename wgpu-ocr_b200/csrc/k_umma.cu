@@ -394,20 +394,33 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 }
                 if (m >= p.M || n0 + c0 >= p.N) continue;
                 if (p.part_max) {
-                    // online arg-max and sum of exponentials (ties keep the lowest column)
+                    // online arg-max and sum of exponentials, a 16-column chunk at a time and
+                    // without branches (the epilogue has one warp per scheduler, so nothing
+                    // else hides a serial chain): the chunk's maximum by a select scan (strict >:
+                    // ties keep the lowest column), then 16 independent exponentials against the
+                    // new running maximum and one rescale of the running sum
+                    float o[16];
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int col = n0 + c0 + j;
-                        if (col >= p.N) break;
-                        const float o = v[j] + (p.bias ? p.bias[col] : 0.f);
-                        if (o > amx) {
-                            asum = asum * __expf(amx - o) + 1.f;
-                            amx = o;
-                            aidx = (uint32_t)col;
-                        } else {
-                            asum += __expf(o - amx);
-                        }
+                        o[j] = col < p.N ? v[j] + (p.bias ? p.bias[col] : 0.f) : -INFINITY;
                     }
+                    float cm = o[0];
+                    uint32_t ci = (uint32_t)(n0 + c0);
+#pragma unroll
+                    for (int j = 1; j < 16; j++) {
+                        const bool gt = o[j] > cm;
+                        cm = gt ? o[j] : cm;
+                        ci = gt ? (uint32_t)(n0 + c0 + j) : ci;
+                    }
+                    const bool up = cm > amx;
+                    const float nm = up ? cm : amx;
+                    aidx = up ? ci : aidx;
+                    float cs = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) cs += n0 + c0 + j < p.N ? __expf(o[j] - nm) : 0.f;
+                    asum = (amx == -INFINITY ? 0.f : asum * __expf(amx - nm)) + cs;
+                    amx = nm;
                     continue;
                 }
                 if (p.scatter && p.scat_cout % 16 == 0) {
