@@ -582,6 +582,41 @@ __global__ void k_softmax(const float *__restrict__ x, float *__restrict__ y, in
     for (int64_t j = threadIdx.x; j < len; j += blockDim.x) y[row * len + j] = expf(xr[j] - m) / s;
 }
 
+// Rows of at most 1024 values (attention scores): a warp per row, the row in registers, the
+// maximum and the sum by shuffles (one block per row spends its time in block barriers).
+constexpr int kSmRowWarps = 8;
+
+__global__ void __launch_bounds__(kSmRowWarps * 32) k_softmax_warp(const float *__restrict__ x, float *__restrict__ y,
+                                                                   int64_t rows, int len) {
+    const int64_t row = (int64_t)blockIdx.x * kSmRowWarps + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float *xr = x + row * len;
+    float v[32];
+    float m = -3.4e38f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        const int j = lane + 32 * i;
+        v[i] = j < len ? xr[j] : -3.4e38f;
+        m = fmaxf(m, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+        if (lane + 32 * i < len) {
+            v[i] = expf(v[i] - m);
+            s += v[i];
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    float *yr = y + row * len;
+#pragma unroll
+    for (int i = 0; i < 32; i++)
+        if (lane + 32 * i < len) yr[lane + 32 * i] = v[i] / s;
+}
+
 // One block per row: best index (tie rule per `tie_last`), row max and log-sum-exp.
 __global__ void k_argmax(const float *__restrict__ x, int64_t rows, int64_t len, int64_t ld, uint32_t *__restrict__ best,
                          float *__restrict__ row_max, float *__restrict__ row_lse, int tie_last) {
@@ -862,7 +897,12 @@ void layer_norm(Ctx *c, const float *x, float *y, int64_t rows, int len, const f
 void softmax(Ctx *c, const float *x, float *y, int64_t rows, int64_t len) {
     Prof pf(c, "softmax", 0, 8.0 * rows * len);
     if (rows == 0) return;
-    k_softmax<<<(unsigned)rows, kThreads, 0, c->stream>>>(x, y, rows, len);
+    if (len <= 1024) {
+        k_softmax_warp<<<(unsigned)((rows + kSmRowWarps - 1) / kSmRowWarps), kSmRowWarps * 32, 0, c->stream>>>(
+            x, y, rows, (int)len);
+    } else {
+        k_softmax<<<(unsigned)rows, kThreads, 0, c->stream>>>(x, y, rows, len);
+    }
     WOCR_LAUNCHED(c);
 }
 
