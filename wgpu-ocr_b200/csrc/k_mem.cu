@@ -450,7 +450,32 @@ __global__ void k_resize_nearest(const float *__restrict__ x, int64_t x_n, int64
 }
 
 // ---------------------------------------------------------------------------------------
+// The element's coordinates from its linear index with 32-bit divisions (tensors below 2^31
+// elements: 64-bit division is many times slower), its offsets in x, b and y from them.
+__device__ __forceinline__ void strided_offsets32(uint32_t i, const Strided &s, int64_t &xi, int64_t &bi,
+                                                  int64_t &yi) {
+    uint32_t rem = i;
+    xi = bi = yi = 0;
+#pragma unroll
+    for (int d = kMaxRank - 1; d >= 0; d--) {
+        if (d >= s.rank) continue;
+        const uint32_t dim = (uint32_t)s.dims[d], cdx = rem % dim;
+        rem /= dim;
+        xi += (int64_t)cdx * s.xs[d];
+        bi += (int64_t)cdx * s.bs[d];
+        yi += (int64_t)cdx * s.ys[d];
+    }
+}
+
 __global__ void k_copy(const float *__restrict__ x, float *__restrict__ y, Strided s, int64_t total) {
+    if (total < (int64_t)INT32_MAX) {
+        for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < (uint32_t)total; i += gridDim.x * blockDim.x) {
+            int64_t xi, bi, yi;
+            strided_offsets32(i, s, xi, bi, yi);
+            y[yi] = x[xi];
+        }
+        return;
+    }
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t rem = i, xi = 0, yi = 0;
 #pragma unroll
@@ -465,8 +490,26 @@ __global__ void k_copy(const float *__restrict__ x, float *__restrict__ y, Strid
     }
 }
 
+__device__ __forceinline__ float binop(int op, float xv, float z) {
+    switch (op) {
+    case 0: return xv + z;
+    case 1: return xv - z;
+    case 2: return xv * z;
+    case 3: return xv / z;
+    default: return z == 2.0f ? xv * xv : (z == 0.5f ? sqrtf(xv) : powf(xv, z));
+    }
+}
+
 __global__ void k_binary(int op, const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ y,
                          Strided s, int64_t total) {
+    if (total < (int64_t)INT32_MAX) {
+        for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < (uint32_t)total; i += gridDim.x * blockDim.x) {
+            int64_t ai, bi, yi;
+            strided_offsets32(i, s, ai, bi, yi);
+            y[yi] = binop(op, a[ai], b[bi]);
+        }
+        return;
+    }
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         int64_t rem = i, ai = 0, bi = 0, yi = 0;
 #pragma unroll
@@ -478,15 +521,7 @@ __global__ void k_binary(int op, const float *__restrict__ a, const float *__res
             bi += cdx * s.bs[d];
             yi += cdx * s.ys[d];
         }
-        float xv = a[ai], z = b[bi], v;
-        switch (op) {
-        case 0: v = xv + z; break;
-        case 1: v = xv - z; break;
-        case 2: v = xv * z; break;
-        case 3: v = xv / z; break;
-        default: v = z == 2.0f ? xv * xv : (z == 0.5f ? sqrtf(xv) : powf(xv, z)); break;
-        }
-        y[yi] = v;
+        y[yi] = binop(op, a[ai], b[bi]);
     }
 }
 
