@@ -5,9 +5,9 @@ page pipeline `PPPipeline`, plus the host-side greedy CTC decoders.  Model descr
 models and inputs of the benchmark configurations are in `wocr.synth`.
 """
 from ._lib import EXPORTS, LIB_PATH, WocrError, lib
-from .api import Detector, Gpu, NdGraph, PPPipeline, Recognizer, ocrs_decode, pp_decode
+from .api import Detector, Gpu, NdGraph, PPPipeline, Recognizer, load_pp_dictionary, ocrs_decode, pp_decode
 from .model import Model, Node
 from .onnx import load_onnx, parse_onnx
 
-__all__ = ["Gpu", "Detector", "Recognizer", "NdGraph", "PPPipeline", "WocrError", "Model", "Node", "ocrs_decode", "pp_decode",
-           "lib", "LIB_PATH", "EXPORTS", "load_onnx", "parse_onnx"]
+__all__ = ["Gpu", "Detector", "Recognizer", "NdGraph", "PPPipeline", "WocrError", "Model", "Node", "ocrs_decode",
+           "pp_decode", "load_pp_dictionary", "lib", "LIB_PATH", "EXPORTS", "load_onnx", "parse_onnx"]

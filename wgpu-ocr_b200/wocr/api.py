@@ -466,6 +466,18 @@ class PPPipeline:
         self.close()
 
 
+def load_pp_dictionary(path: str) -> List[str]:
+    """`Dictionary::load` (src/ppocr.rs:10-16): class 0 the blank, then the file's lines in order
+    (split as Rust's `str::lines` splits: at "\n", a "\r" before it dropped, no empty line after
+    a final newline), then the space."""
+    with open(path, encoding="utf-8") as f:
+        text = f.read()
+    lines = text.split("\n")
+    if lines and lines[-1] == "":
+        lines.pop()
+    return [""] + [ln[:-1] if ln.endswith("\r") else ln for ln in lines] + [" "]
+
+
 def pp_decode(best: Sequence[int], chars: List[str]) -> str:
     """`Dictionary::decode` (src/ppocr.rs:23-33): repeats merged, blanks dropped."""
     out, prev = [], 0
