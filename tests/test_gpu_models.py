@@ -267,3 +267,30 @@ def test_recognize_replay(gpu, rec_model, monkeypatch):
         assert (x[0] == a[0]).all() and (x[3] == a[3]).all()
     assert (o[0] == od[0]).all() and (o[3] == od[3]).all()
     assert (nb[3] == a[3]).all() and (nb2[3] == a[3]).all()
+
+
+def test_recognizer_rejects_unsupported_models(gpu, rec_model):
+    """Recognizer::new's checks (src/gpu.rs:1452-1506): hidden size 256, linear_before_reset = 1,
+    bidirectional, exactly two GRU layers, an AveragePool after the trunk; anything else is an
+    error with a message, as the reference returns Err."""
+    import copy
+
+    grus = [i for i, n in enumerate(rec_model.nodes) if n.op == "GRU"]
+    assert len(grus) == 2
+    for attr, value in (("hidden_size", 128), ("linear_before_reset", 0), ("direction", "forward")):
+        m = copy.deepcopy(rec_model)
+        m.nodes[grus[0]].attrs[attr] = value
+        with pytest.raises(wocr.WocrError, match="unsupported GRU attributes"):
+            wocr.Recognizer(gpu, m)
+    m = copy.deepcopy(rec_model)
+    del m.nodes[grus[1]]
+    with pytest.raises(wocr.WocrError, match="1 GRU layers"):
+        wocr.Recognizer(gpu, m)
+    m = copy.deepcopy(rec_model)
+    for n in m.nodes:
+        if n.op == "AveragePool":
+            n.op = "MaxPool"
+    # the trunk is built up to the AveragePool; without one it runs into the GRU's ops, which
+    # the 4-D graph rejects like the reference's Graph::build
+    with pytest.raises(wocr.WocrError, match="no AveragePool|unsupported op"):
+        wocr.Recognizer(gpu, m)
