@@ -1538,7 +1538,9 @@ std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float
         BufP db = alloc(c, bx.size() * sizeof(k::DbBox)), dsum = alloc(c, (size_t)nc * 16),
              dcnt = alloc(c, (size_t)nc * 8);
         WOCR_CUDA(cudaMemcpyAsync(db->p, bx.data(), bx.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice, c->stream));
-        k::db_bounds(c, prob, w, (const k::DbBox *)db->p, nc, (double *)dsum->p, (long long *)dcnt->p);
+        int max_rows = 1;
+        for (const k::DbBox &b : bx) max_rows = std::max(max_rows, b.y1 - b.y0 + 1);
+        k::db_bounds(c, prob, w, (const k::DbBox *)db->p, nc, max_rows, (double *)dsum->p, (long long *)dcnt->p);
         std::vector<double> sums((size_t)nc * 2);
         std::vector<long long> cnts((size_t)nc);
         d2h(c, sums.data(), dsum->p, sums.size() * 8);

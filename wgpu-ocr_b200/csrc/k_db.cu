@@ -118,18 +118,21 @@ __global__ void __launch_bounds__(kDbWarps * 32) k_db_scores(const float *__rest
 // to bound the ordered f32 score without forming it.
 constexpr int kDbBoundT = 256;
 
+constexpr int kDbBoundRows = 8;  // box rows per block (blockIdx.y picks the slice)
+
 __global__ void __launch_bounds__(kDbBoundT) k_db_bounds(const float *__restrict__ prob, int w,
                                                          const DbBox *__restrict__ boxes, double *__restrict__ sums,
                                                          long long *__restrict__ counts) {
     __shared__ double s_s[kDbBoundT / 32], s_a[kDbBoundT / 32];
     __shared__ long long s_c[kDbBoundT / 32];
     const DbBox b = boxes[blockIdx.x];
-    const int bw = b.x1 - b.x0 + 1, bh = b.y1 - b.y0 + 1;
+    const int ya = b.y0 + (int)blockIdx.y * kDbBoundRows, yb = min(b.y1, ya + kDbBoundRows - 1);
+    if (ya > b.y1 || b.x1 < b.x0) return;  // past this box (the grid covers the tallest box)
     double sum = 0.0, mag = 0.0;
     long long cnt = 0;
-    if (bw > 0 && bh > 0) {
+    {
         // a warp per row, lanes along it (coalesced)
-        for (int y = b.y0 + (int)(threadIdx.x >> 5); y <= b.y1; y += kDbBoundT / 32) {
+        for (int y = ya + (int)(threadIdx.x >> 5); y <= yb; y += kDbBoundT / 32) {
             const float dy = __fsub_rn((float)y, b.cy);
             const float *row = prob + (int64_t)y * w;
             for (int x = b.x0 + (int)(threadIdx.x & 31); x <= b.x1; x += 32) {
@@ -164,18 +167,23 @@ __global__ void __launch_bounds__(kDbBoundT) k_db_bounds(const float *__restrict
             mag += s_a[i];
             cnt += s_c[i];
         }
-        sums[2 * blockIdx.x] = sum;
-        sums[2 * blockIdx.x + 1] = mag;
-        counts[blockIdx.x] = cnt;
+        // slices of one box add up in any order: the bound on the ordered sum allows for that
+        atomicAdd(&sums[2 * blockIdx.x], sum);
+        atomicAdd(&sums[2 * blockIdx.x + 1], mag);
+        atomicAdd(reinterpret_cast<unsigned long long *>(&counts[blockIdx.x]), (unsigned long long)cnt);
     }
 }
 
 }  // namespace
 
-void db_bounds(Ctx *c, const float *prob, int w, const DbBox *boxes, int n, double *sums, long long *counts) {
+void db_bounds(Ctx *c, const float *prob, int w, const DbBox *boxes, int n, int max_rows, double *sums,
+               long long *counts) {
     if (n <= 0) return;
     Prof pf(c, "db_bounds", 0, 0);
-    k_db_bounds<<<n, kDbBoundT, 0, c->stream>>>(prob, w, boxes, sums, counts);
+    WOCR_CUDA(cudaMemsetAsync(sums, 0, (size_t)n * 16, c->stream));
+    WOCR_CUDA(cudaMemsetAsync(counts, 0, (size_t)n * 8, c->stream));
+    const dim3 grid((unsigned)n, (unsigned)std::max(1, (max_rows + kDbBoundRows - 1) / kDbBoundRows));
+    k_db_bounds<<<grid, kDbBoundT, 0, c->stream>>>(prob, w, boxes, sums, counts);
     WOCR_LAUNCHED(c);
 }
 

@@ -144,7 +144,9 @@ void db_mask(Ctx *c, const float *prob, int w, int h, float thr, uint32_t *bits)
 void db_scores(Ctx *c, const float *prob, int w, int h, const DbBox *boxes, int n, float *scores);
 // Per box: sums[2 k] = the inside pixels' sum in double, sums[2 k + 1] = the sum of their
 // magnitudes, counts[k] = their number (order-free: a bound on `score`, not its value).
-void db_bounds(Ctx *c, const float *prob, int w, const DbBox *boxes, int n, double *sums, long long *counts);
+// max_rows: the tallest box's scan rows (y1 - y0 + 1); blocks take 8-row slices of a box.
+void db_bounds(Ctx *c, const float *prob, int w, const DbBox *boxes, int n, int max_rows, double *sums,
+               long long *counts);
 
 // Word rectangles of bit masks (k_words.cu, `word_rects` of src/bin/ocr-bench.rs:38-60): `pages`
 // masks of h rows x ceil(w / 32) words at mask; rects [n][6] = [cx, cy, up_x, up_y, width,
