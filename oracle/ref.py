@@ -383,8 +383,9 @@ def _axis(a, r):
     return a + r if a < 0 else a
 
 
-def run_onnx(model, x: np.ndarray, stop_before_softmax: bool = False, trace=None) -> np.ndarray:
-    """Run `model` (a `wocr.model.Model`) on `x` with plain ONNX semantics, node by node."""
+def run_onnx(model, x: np.ndarray, stop_before_softmax: bool = False, trace=None, values=None) -> np.ndarray:
+    """Run `model` (a `wocr.model.Model`) on `x` with plain ONNX semantics, node by node.
+    `values` (a dict) receives every computed value by name."""
     vals: Dict[str, object] = {model.input: _c32(x)}
     nodes = list(model.nodes)
     out_name = model.output
@@ -568,6 +569,8 @@ def run_onnx(model, x: np.ndarray, stop_before_softmax: bool = False, trace=None
         else:
             raise ValueError(f"unsupported op {op}")
         vals[nd.outputs[0]] = y
+        if values is not None:
+            values[nd.outputs[0]] = y
         if trace is not None:
             trace.append((nd.op, nd.outputs[0], getattr(y, "shape", None)))
     out = vals[out_name]

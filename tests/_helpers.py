@@ -2,15 +2,27 @@
 
 * Detection masks: bit-exact except pixels whose oracle page-level probability lies within
   MASK_BAND of the threshold.
-* Recognition: identical arg-max class at every time step, except steps where the class the
-  GPU chose is, in the oracle's own logits, within ARGMAX_TIE of the oracle's maximum (a tie
-  at the oracle's precision); per-step softmax probabilities within PROB_TOL absolute.
+* Recognition: identical arg-max class at every time step.  The whole-model tests on the
+  benchmark configurations (configs 0 and 3, every step of every line) require it outright.
+  Elsewhere a step may be excused as a near-tie when the class the GPU chose is, in the
+  oracle's own logits, within ARGMAX_TIE of the oracle's maximum, and at most max_ties(rows)
+  steps may be excused; per-step softmax probabilities within PROB_TOL absolute.
+
+ARGMAX_TIE is the error bound of the tensor-core products behind a logit.  Each operand is split
+into bf16 hi + lo parts and the products hi*hi + hi*lo + lo*hi are accumulated in fp32: an
+operand's split leaves at most 2^-17 of it, the dropped lo*lo term is at most 2^-16 of the
+product, so a product carries at most 2^-15 |a||b| and a logit at most 2^-15 * L1, where
+L1 = sum_k |x_k||w_k| over its dot product (not |logit|: with random-init weights L1 is many
+times the logit).  The CTC heads here have L1 <= 1.7 (config 3's head: 1.20 to 1.69, measured
+over all 23,248 steps), so 2^-15 * 1.7 = 5.2e-5.  Measured on a B200 over configs 0 and 3
+(31,657 steps): no step differs, the largest logit difference is 2.3e-5 (config 0) and the
+largest row-maximum difference 7.0e-6 (config 3), while the smallest top-2 gap is 1.9e-6.
 """
 import numpy as np
 
 MASK_BAND = 1e-3
 PROB_TOL = 1e-3
-ARGMAX_TIE = 1e-4
+ARGMAX_TIE = 5.2e-5
 
 
 def mask_parity(bits_gpu, bits_ref, prob_ref, thr, w):
@@ -29,9 +41,20 @@ def mask_parity(bits_gpu, bits_ref, prob_ref, thr, w):
     return int(bad.sum()), int(band.sum())
 
 
+# At most this fraction of the steps (and at least one step) may be excused as near-ties.
+MAX_TIE_FRACTION = 1e-3
+
+
+def max_ties(rows: int) -> int:
+    """The near-tie steps a parity check over `rows` steps may excuse."""
+    return max(1, int(rows * MAX_TIE_FRACTION))
+
+
 def argmax_parity(best_gpu, logits_ref):
     """best_gpu [rows], logits_ref [rows, classes]: number of rows whose GPU class is not the
-    oracle's maximum nor within ARGMAX_TIE of it, and the number of such near-tie rows."""
+    oracle's maximum nor within ARGMAX_TIE of it, and the number of such near-tie rows (rows
+    whose class differs from the oracle's arg-max but lies within the margin; callers assert
+    that they are at most max_ties(rows))."""
     rows = np.arange(len(best_gpu))
     top = logits_ref.max(axis=1)
     at = logits_ref[rows, best_gpu.astype(np.int64)]

@@ -10,7 +10,7 @@ from oracle import ref
 from wocr import synth
 from wocr.synth import _Builder
 
-from _helpers import argmax_parity
+from _helpers import argmax_parity, max_ties
 
 pytestmark = pytest.mark.gpu
 
@@ -134,8 +134,9 @@ def test_linear_argmax_fused(gpu, classes, monkeypatch):
     assert (best == ub).all() and (mx == umx).all()
     assert np.abs(lse - ulse).max() < 1e-4
     logits = ref.run_onnx(m, x).reshape(-1, classes)
-    bad, _ = argmax_parity(best, logits)
+    bad, ties = argmax_parity(best, logits)
     assert bad == 0
+    assert ties <= max_ties(len(best)), f"{ties} near-tie steps of {len(best)}"
     _, rmx, _, rlse = ref.argmax(logits)
     assert np.abs(mx - rmx).max() < 1e-4 and np.abs(lse - rlse).max() < 1e-4
 

@@ -116,7 +116,7 @@ def _check_pipeline(gpu, det, page, w, h, min_lines, min_batches):
     """wocr_pp_page against its stages: its boxes are the DB boxes of the detector's map
     (bit-exact), and each line's arg-max classes equal the oracle's recognition of the same line
     images (up to near-ties at the oracle's precision), line by line in reading order."""
-    from _helpers import argmax_parity
+    from _helpers import argmax_parity, max_ties
 
     rec = synth.pp_rec_model()
     with wocr.PPPipeline(gpu, det, rec) as pp:
@@ -130,16 +130,19 @@ def _check_pipeline(gpu, det, page, w, h, min_lines, min_batches):
     assert len(bests) == len(boxes) >= min_lines
     batches, order = ref.pp_batches(page, ref.pp_line_rects(boxes, 0.1))
     assert len(batches) >= min_batches
-    k = 0
+    k = steps = ties_all = 0
     for data, n, width in batches:
         logits = ref.run_onnx(rec, data, stop_before_softmax=True)
         T = logits.shape[1]
         for j in range(n):
             line = order[k + j]
             assert len(bests[line]) == T
-            bad, _ = argmax_parity(bests[line], logits[j])
+            bad, ties = argmax_parity(bests[line], logits[j])
             assert bad == 0, f"line {line}: {bad} steps differ"
+            steps += T
+            ties_all += ties
         k += n
+    assert ties_all <= max_ties(steps), f"{ties_all} near-tie steps of {steps}"
 
 
 def test_pp_page_pipeline(gpu):
@@ -151,6 +154,13 @@ def test_pp_page_pipeline_many_lines(gpu):
     """The pipeline with a detector that marks word blobs: over a hundred boxes in reading order,
     recognised in width-sorted batches whose results must come back to the right lines."""
     _check_pipeline(gpu, synth.pp_ink_det_model(), synth.page(6, 1275, 1650, bands=10), 1275, 1650, 100, 5)
+
+
+def test_pp_page_pipeline_full_size(gpu):
+    """Config 4's page size (2550 x 3300): the random-init DB detector (one page-sized box, a
+    two-pass cut of a tall crop) and the ink detector (hundreds of boxes, dozens of batches)."""
+    _check_pipeline(gpu, synth.pp_det_model(), synth.page(3000, 2550, 3300), 2550, 3300, 1, 1)
+    _check_pipeline(gpu, synth.pp_ink_det_model(), synth.page(3001, 2550, 3300), 2550, 3300, 500, 30)
 
 
 def test_db_boxes_at_the_score_threshold(gpu):

@@ -653,6 +653,10 @@ __global__ void __launch_bounds__(kSmRowWarps * 32) k_softmax_warp(const float *
 }
 
 // One block per row: best index (tie rule per `tie_last`), row max and log-sum-exp.
+// Lowest-index rule (K30, src/nd.rs:360-391): the search starts from (-3.4e38, index 0) and
+// takes a value only when it is larger, so a row of NaN or -inf values gives 0, as there.
+// Last-index rule: a row with no value above -3.4e38 gives its last index (Rust's max_by over
+// equal keys returns the last).
 __global__ void k_argmax(const float *__restrict__ x, int64_t rows, int64_t len, int64_t ld, uint32_t *__restrict__ best,
                          float *__restrict__ row_max, float *__restrict__ row_lse, int tie_last) {
     __shared__ float bv[32];
@@ -662,7 +666,7 @@ __global__ void k_argmax(const float *__restrict__ x, int64_t rows, int64_t len,
     if (row >= rows) return;
     const float *xr = x + row * ld;
     float m = -3.4e38f;
-    int64_t at = tie_last ? -1 : INT64_MAX;
+    int64_t at = tie_last ? -1 : 0;
     for (int64_t j = threadIdx.x; j < len; j += blockDim.x) {
         float v = xr[j];
         if (v > m || (v == m && (tie_last ? j > at : j < at))) { m = v; at = j; }
@@ -700,7 +704,7 @@ __global__ void k_argmax(const float *__restrict__ x, int64_t rows, int64_t len,
         }
     }
     if (threadIdx.x == 0) {
-        best[row] = (uint32_t)bi[0];
+        best[row] = (uint32_t)(bi[0] < 0 ? len - 1 : bi[0]);
         if (row_max) row_max[row] = m;
     }
 }
