@@ -1,23 +1,26 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 hot path: ocrs page detection (benchmark config 1), pages/s.
+"""Benchmark of the B200 hot path: full-page OCR, pages/s (BASELINE metric; config 4 by default).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--pages B] [--impl b200|reference]
+                    [--workload pp4|pp4ink|det1|...] [--lanes L] [--merge M]
 
-A step is one pass of the detection hot path (RGB page -> grey/pad/resize -> U-Net -> mask
-resize/threshold/bit-pack, `Detector::detect_page`, src/gpu.rs:1393-1422) over a batch of B
-synthetic 2550 x 3300 pages per GPU.  Pages shard across GPUs with no collective (weak scaling):
-one process per GPU (torchrun), timed on the device with CUDA events, max over ranks.
+Default workload (`pp4`): the PP-OCRv6 page pipeline of the reference's bench
+(src/bin/ocr-bench.rs:133-310, 458-585 with DET=ppocr REC=ppocr): per page detection
+(NdGraph::det_input + the DB detector, seed 3), DB boxes at 0.3 (`ppdet::boxes`), line images
+(`ppocr::line_input`, batched 16 by width) and recognition (the SVTR recogniser, seed 2, arg-max
+per step).  A step is B synthetic 2550 x 3300 pages per GPU through `wocr_pp_pages` (L lanes on
+the GPU, recognitions merged M pages at a time per lane).  Pages shard across GPUs with no
+collective (weak scaling): one process per GPU (torchrun), timed on the device, max over ranks.
 
   value  - pages/s with the pages already in HBM (B pages = 303 MB > L2 per step)
-  e2e    - pages/s through the public API (`wocr_detect_pages`) from pinned host memory, the
-           host->device copy of the pages and the device->host copy of the masks inside the
-           timed region.  A tall page goes up as the source rows the grey/resize reads (1600
-           of 3300, strided copies); h2d_bytes_per_step is what the library reports it copied
-  roofline - the kernel with the largest share of device time, from a CUDA-event profile of the
-           same workload: algorithmic FLOPs (or bytes) per launch / its mean launch time
-  cpu_baseline - the CPU oracle (a C restatement of the reference's arithmetic, OpenMP) on a
-           bounded sample of pages, on this host's cores
+  e2e    - pages/s through the same public call from pinned host pages: the pages' upload and
+           the read-back of every line's arg-max classes inside the timed region
+  roofline - the kernel with the largest share of device time in a CUDA-event profile of the
+           same workload (one lane): algorithmic bytes (or FLOPs) per launch / its mean time
+  cpu_baseline - the CPU oracle (a C/numpy restatement of the reference's arithmetic, OpenMP)
+           on a bounded sample of pages, on this host's cores
 
+`--workload det1` is config 1 (ocrs detection alone); the others are secondary measurements.
 `--impl reference` times the reference's CPU implementation stand-in (the oracle; the reference
 itself is Rust + wgpu and cannot run here) on the same workload, rank 0 only.
 """
@@ -47,12 +50,16 @@ def parse():
     p.add_argument("--pages", type=int, default=12, help="pages per GPU per step")
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
-    p.add_argument("--workload", default="det1", choices=["det1", "rec0", "pp3", "ppdet4", "ppdb4", "pp4", "pp4ink", "pplines", "words1"],
-                   help="det1 (default, the driver's line): config 1 detection; rec0 / pp3 / ppdet4: configs "
-                        "0, 3 and 4 through their public calls; ppdb4: config 4 with the DB mask and box "
-                        "scores on the device; pp4: the full PP-OCRv6 page pipeline (pp4ink: with a hand-set ink "
-                        "detector, hundreds of lines a page); pplines: PP line extraction; "
-                        "words1: word rectangles of config 1 detection masks (secondary measurements)")
+    p.add_argument("--workload", default="pp4",
+                   choices=["pp4", "pp4ink", "det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines", "words1"],
+                   help="pp4 (default, the driver's line): config 4, the full PP-OCRv6 page pipeline (pp4ink: "
+                        "with a hand-set ink detector, hundreds of lines a page); det1: config 1 detection; rec0 / "
+                        "pp3 / ppdet4: configs 0, 3 and 4 through their public calls; ppdb4: config 4 with the DB "
+                        "mask and box scores on the device; pplines: PP line extraction; words1: word rectangles "
+                        "of config 1 detection masks (secondary measurements)")
+    p.add_argument("--lanes", type=int, default=4, help="page-pipeline workers per GPU (pp4, pp4ink)")
+    p.add_argument("--merge", type=int, default=3, help="pages whose recognitions a lane runs together")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (pp4, pp4ink)")
     return p.parse_args()
 
 
@@ -195,10 +202,44 @@ def cpu_baseline(sample: int):
                       f"{dt:.2f} s"}
 
 
+PP_MAX_SIDE = 960
+PP_DB = (0.3, 0.45, 1.4, 3.0)
+
+
+def pp_workload(ink: bool):
+    """Config 4's models and its description (pp4ink: the ink detector in place of the DB's)."""
+    from wocr import synth
+    det_m = synth.pp_ink_det_model() if ink else synth.pp_det_model()
+    detector = ("a hand-set ink detector (darkness, 3x9 box average, sigmoid) standing in for trained DB weights, "
+                "which marks word blobs" if ink else
+                "the PP-OCRv6-style DB detector with random-init weights (seed 3), which mark most of each page, "
+                "so a page gives about one page-sized box")
+    desc = (f"config 4 full page: {detector}; 2550x3300 RGB u8 synthetic pages (36 text bands), det input "
+            f"3x960x736, DB boxes at 0.3 on the device, lines grown 0.1 x height, cut to height 48 and batched "
+            f"16 by width on the device, PP-OCRv6-style recognition (seed 2, 18,709 classes), arg-max per step")
+    return det_m, synth.pp_rec_model(), desc
+
+
+def oracle_pp_page(det_m, rec_m, page):
+    """One page of config 4 through the CPU oracle: detection, DB boxes, line images,
+    recognition arg-max.  Returns the number of lines."""
+    from oracle import ref
+    x, tp = ref.det_input(page, PP_MAX_SIDE)
+    prob = ref.run_onnx(det_m, x)[0, 0]
+    boxes = ref.db_boxes(prob, tp, *PP_DB)
+    batches, _ = ref.pp_batches(page, ref.pp_line_rects(boxes, 0.1))
+    for data, _, _ in batches:
+        lg = ref.run_onnx(rec_m, data, stop_before_softmax=True)
+        ref.argmax(lg.reshape(-1, lg.shape[-1]))
+    return len(boxes)
+
+
 def run_reference(args):
     world, rank, _ = dist()
     if rank != 0:
         return 0
+    if args.workload in ("pp4", "pp4ink"):
+        return run_reference_pages(args)
     from oracle import ref
     from wocr import synth
     m = synth.ocrs_det_model()
@@ -352,6 +393,186 @@ def run_b200(args):
         tdist.barrier(device_ids=[local])
         tdist.destroy_process_group()
     return 0
+
+
+def run_reference_pages(args):
+    """The reference arm on config 4: the CPU oracle, one page per step, all host threads."""
+    from oracle import ref
+    from wocr import synth
+    det_m, rec_m, desc = pp_workload(args.workload == "pp4ink")
+    pages = [synth.page(7000 + k, W_PAGE, H_PAGE) for k in range(max(args.steps, 1) + max(args.warmup, 1))]
+    ref.set_threads(os.cpu_count() or 1)
+    for k in range(args.warmup):
+        oracle_pp_page(det_m, rec_m, pages[k])
+    t0 = time.perf_counter()
+    nl = 0
+    for k in range(args.steps):
+        nl += oracle_pp_page(det_m, rec_m, pages[args.warmup + k])
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    line = {"impl": "reference", "metric": "pages/s", "value": v, "unit": "pages/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": desc, "step": "1 page per step (bounded CPU sample)", "parallelism": "host threads",
+                       "lines_per_page": nl / max(args.steps, 1)},
+            "cpu_baseline": {"value": v, "unit": "pages/s", "cores": ref.threads(), "kind": "port",
+                             "sample": "1 page per step through the CPU oracle (the reference is Rust + wgpu over "
+                                       "Vulkan and cannot run here)"},
+            "e2e": {"value": v, "unit": "pages/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_pages(args):
+    """Config 4 (default): the whole PP-OCRv6 page pipeline, B pages per GPU per step."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as tdist
+
+    import wocr
+    from wocr import shard, synth
+
+    world, rank, local = dist()
+    if world > 1:
+        from datetime import timedelta
+        tdist.init_process_group("nccl", timeout=timedelta(seconds=300))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, L, M = args.pages, max(1, args.lanes), max(1, args.merge)
+    det_m, rec_m, desc = pp_workload(args.workload == "pp4ink")
+    gpu = wocr.Gpu(lines=8, device=local)
+    pp = wocr.PPPipeline(gpu, det_m, rec_m)
+    host_np = [synth.page(3000 + g, W_PAGE, H_PAGE) for g in shard.weak_pages_of(rank, B)]
+    held = []
+
+    def pinned(a):
+        p = ctypes.c_void_p()
+        wocr._lib.check(wocr.lib().wocr_host_alloc(a.nbytes, ctypes.byref(p)))
+        held.append(p)
+        out = np.frombuffer((ctypes.c_char * a.nbytes).from_address(p.value), dtype=a.dtype,
+                            count=a.size).reshape(a.shape)
+        out[...] = a
+        return out
+
+    host = [pinned(a) for a in host_np]
+    d_pages = [torch.from_numpy(a).to(dev) for a in host_np]
+    d_ptrs = [t.data_ptr() for t in d_pages]
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        shard.barrier(local)
+        torch.cuda.synchronize(dev)
+
+    def step(src):
+        return pp.pages(src, W_PAGE, H_PAGE, max_side=PP_MAX_SIDE, db=PP_DB, merge=M, lanes=L)
+
+    # warm-up: every lane captures its graphs for every batch shape of these pages
+    for _ in range(max(args.warmup, 3)):
+        res = step(d_ptrs)
+    lines_per_page = sum(len(b) for b, _ in res) / B
+    steps_per_page = sum(sum(len(x) for x in ls) for _, ls in res) / B
+    barrier()
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+    except Exception:
+        bus = None
+    # the call is synchronous and spreads over L streams; events on a stream of their own bracket
+    # it, so the elapsed time covers every lane's work and the host steps between
+    ts = torch.cuda.Stream(device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(bus)
+    clocks.start()
+    l0 = pp.launches()
+    e0.record(ts)
+    for _ in range(args.steps):
+        step(d_ptrs)
+    e1.record(ts)
+    e1.synchronize()
+    clk = clocks.stop()
+    launches = pp.launches() - l0
+    barrier()
+    ms = shard.max_over_ranks(e0.elapsed_time(e1), dev)
+    value = world * B * args.steps / (ms / 1e3)
+
+    # end to end: pinned host pages in, every line's classes out
+    for _ in range(2):
+        step(host)
+    barrier()
+    e0.record(ts)
+    for _ in range(args.steps):
+        step(host)
+    e1.record(ts)
+    e1.synchronize()
+    h2d, d2h = pp.last_bytes
+    barrier()
+    ems = shard.max_over_ranks(e0.elapsed_time(e1), dev)
+    e2e = {"value": world * B * args.steps / (ems / 1e3), "unit": "pages/s", "h2d_bytes_per_step": int(h2d),
+           "d2h_bytes_per_step": int(d2h)}
+
+    # per-kernel profile of one more step on one lane (the profile records the caller's context)
+    gpu.profile(True)
+    pp.pages(d_ptrs, W_PAGE, H_PAGE, max_side=PP_MAX_SIDE, db=PP_DB, merge=M, lanes=1)
+    rep = gpu.profile_report()
+    gpu.profile(False)
+    total_ms = sum(r["ms"] for r in rep) or 1.0
+    top = max(rep, key=lambda r: r["ms"])
+    roof = roofline(top, total_ms, with_traffic=False)
+    roof["traffic"] = pp_traffic(top["kernel"])
+    kernels = {r["kernel"]: {"launches": r["launches"], "ms_per_step": r["ms"], "share": r["ms"] / total_ms}
+               for r in rep}
+
+    cpu = None
+    if rank == 0 and world == 1:
+        from oracle import ref
+        ref.set_threads(os.cpu_count() or 1)
+        oracle_pp_page(det_m, rec_m, host_np[0])  # warm-up
+        t0, k, nl = time.perf_counter(), 0, 0
+        while k < 2 or (time.perf_counter() - t0 < args.cpu_seconds and k < B):
+            nl += oracle_pp_page(det_m, rec_m, host_np[k % B])
+            k += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": k / dt, "unit": "pages/s", "cores": ref.threads(), "kind": "port",
+               "sample": f"{k} pages ({nl} lines) of this workload through the CPU oracle (detection, DB boxes, "
+                         f"line images, recognition arg-max), {dt:.1f} s"}
+    if rank == 0:
+        line = {"metric": "pages/s", "value": value, "unit": "pages/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": desc, "pages_per_gpu_per_step": B, "global_batch": B * world,
+                           "lanes_per_gpu": L, "merge": M, "lines_per_page": lines_per_page,
+                           "recognition_steps_per_page": steps_per_page,
+                           "parallelism": f"pages sharded over {world} GPU(s), no collective",
+                           "l2": f"inputs {B * W_PAGE * H_PAGE * 3 / 1e6:.0f} MB per GPU per step > 126 MB L2"},
+                "e2e": e2e, "gpu_launches": int(launches),
+                "roofline": roof, "cpu_baseline": cpu, "clocks": clk, "kernels": kernels}
+        print(json.dumps(line), flush=True)
+    pp.close()
+    gpu.close()
+    for p_ in held:
+        wocr.lib().wocr_host_free(p_)
+    if world > 1:
+        tdist.barrier(device_ids=[local])
+        tdist.destroy_process_group()
+    return 0
+
+
+def pp_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` in config 4's page pipeline from the committed ncu
+    summary, or None."""
+    path = os.path.join(ROOT, "profiles", "pp_page_config4.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic per launch (bytes):"):
+                for item in line.split(":", 1)[1].split():
+                    name, _, val = item.partition("=")
+                    if name == kernel:
+                        return float(val)
+    except OSError:
+        pass
+    return None
 
 
 def run_workload(args):
@@ -589,6 +810,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload in ("pp4", "pp4ink"):
+        return run_pages(args)
     if args.workload != "det1":
         return run_workload(args)
     return run_b200(args)

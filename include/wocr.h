@@ -199,6 +199,34 @@ int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *
                                 uint32_t *best, float *row_max, float *row_lse, int64_t cap,
                                 int64_t *rows_out, int64_t *out_shape, int32_t *out_rank);
 
+/* ---- record, then read in one wait --------------------------------------------------------
+ * The reference records NdGraph::run / NdGraph::argmax_record (src/nd.rs:1372-1380) into one
+ * command encoder and reads every recorded buffer with one Gpu::read_many (src/gpu.rs:1011-1037,
+ * used at src/bin/ocr-bench.rs:240-253).  A wocr_batch is that read list: each *_enqueue call
+ * queues its work on the context stream (nothing waits) and stages a copy of its results in
+ * page-locked memory owned by the batch; wocr_wait waits once for the context stream (bounded by
+ * timeout_ms, <= 0: no bound) and only then writes every recorded result to the caller's output
+ * buffers.  Output buffers must stay valid until wocr_wait returns; an input in page-locked or
+ * device memory must stay unchanged until then (pageable inputs are copied before the enqueue
+ * returns).  A wait that times out keeps the reads pending for a later wocr_wait.  A batch belongs
+ * to one context and is used by that context's thread. */
+typedef struct wocr_batch wocr_batch;
+int32_t wocr_batch_create(wocr_ctx *ctx, wocr_batch **out);
+void wocr_batch_destroy(wocr_batch *b);
+/* Number of enqueue calls recorded since the last wocr_wait. */
+int64_t wocr_batch_pending(wocr_batch *b);
+/* NdGraph::run recorded: arguments as wocr_ndgraph_run, out written at wocr_wait (the shape
+ * outputs at once). */
+int32_t wocr_ndgraph_run_enqueue(wocr_ndgraph *g, wocr_batch *b, const float *x, const int64_t *shape, int32_t rank,
+                                 float *out, int64_t out_cap, int64_t *out_shape, int32_t *out_rank);
+/* NdGraph::run + argmax_record: arguments as wocr_ndgraph_run_argmax, best / row_max / row_lse
+ * written at wocr_wait (rows_out and the shape at once). */
+int32_t wocr_ndgraph_argmax_enqueue(wocr_ndgraph *g, wocr_batch *b, const float *x, const int64_t *shape,
+                                    int32_t rank, uint32_t *best, float *row_max, float *row_lse, int64_t cap,
+                                    int64_t *rows_out, int64_t *out_shape, int32_t *out_rank);
+/* Gpu::read_many: wait for everything recorded in b and deliver it. */
+int32_t wocr_wait(wocr_batch *b, int32_t timeout_ms);
+
 /* No counterpart in the reference.  The arg-max of wocr_ndgraph_run_argmax for callers that
  * cannot let the library allocate device memory (a host program whose own allocator owns the
  * GPU, a process under a device-memory cap, a latency-critical path that avoids cudaMalloc's
@@ -209,8 +237,10 @@ int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *
  * (more rows: WOCR_ERR_CAPACITY); every GPU that loads the library holds that array until the
  * process exits.  Nothing is allocated: no cudaMalloc, cudaFree or allocating routine.  The
  * first call on a device looks up the array's device address (once per device), so make that
- * first call before any stream capture.  All calls share the array: calls that overlap on the
- * GPU (several contexts or threads at once) race on it. */
+ * first call before any stream capture.  With lazy module loading (CUDA's default) that first
+ * lookup may also load the library's device code, the array included: make one warm-up call (or
+ * set CUDA_MODULE_LOADING=EAGER) before a memory cap starts to matter.  All calls share the
+ * array: calls that overlap on the GPU (several contexts or threads at once) race on it. */
 int32_t wocr_argmax_rows_noalloc(wocr_ctx *ctx, const float *d_logits, int64_t rows, int64_t len, uint32_t *best,
                                  float *row_max, float *row_lse);
 
@@ -231,7 +261,7 @@ int32_t wocr_ppdet_page(wocr_ndgraph *g, const uint8_t *rgb, int32_t w, int32_t 
  *   wocr_ppdet_scores: `score` of each box rects[6 k .. 6 k + 5] = center x, center y, up axis x,
  *                      up axis y, width, height (map coordinates): the mean probability of the
  *                      pixels inside it, summed in the reference's order (bit-exact f32).
- * The contour search between the two stays on the host, as in the reference. */
+ * wocr_ppdet_boxes below runs the whole of `boxes`, contours included, on the device. */
 int32_t wocr_ppdet_mask(wocr_ndgraph *g, float thresh, uint32_t *mask, int64_t cap, int32_t *ow, int32_t *oh);
 int32_t wocr_ppdet_scores(wocr_ndgraph *g, const float *rects, int32_t n, float *scores);
 
@@ -268,9 +298,27 @@ int32_t wocr_db_boxes(wocr_ctx *ctx, const float *prob, int32_t w, int32_t h, in
 typedef struct wocr_pp wocr_pp;
 int32_t wocr_pp_create(wocr_ctx *ctx, const wocr_model *det, const wocr_model *rec, wocr_pp **out);
 void wocr_pp_destroy(wocr_pp *p);
+/* Kernels launched so far by all lanes of the pipeline (instrumentation). */
+int64_t wocr_pp_launches(wocr_pp *p);
 int32_t wocr_pp_page(wocr_pp *p, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, const float *db,
                      float relv, int32_t per_batch, float *boxes, int32_t box_cap, int32_t *n_lines,
                      uint32_t *best, int64_t cap, int32_t *steps);
+
+/* Many pages through the same pipeline, as the reference's page loop runs them
+ * (src/bin/ocr-bench.rs:458-585 with its GPU thread, 133-310): page k is pages[k] (host or
+ * device memory), w[k] x h[k].  The work is spread over `lanes` workers on the pipeline's GPU
+ * (each its own stream, graphs and host thread; lane j takes pages j, j + lanes, ...), so one
+ * page's detection and recognition overlap another's latency-bound steps.  Each lane holds the
+ * line batches of `merge` of its pages (MERGE, src/bin/ocr-bench.rs:162-229) and recognises them
+ * together with one wait (wocr_ndgraph_argmax_enqueue + wocr_wait).  Results are those of
+ * wocr_pp_page page by page, whatever lanes and merge are: n_lines[k] per page; boxes, steps and
+ * best concatenated over the pages in page order (lines in reading order within a page).
+ * bytes (nullable) gets {bytes copied host -> device, device -> host}.  A short box_cap or cap
+ * fails with WOCR_ERR_CAPACITY after filling n_lines. */
+int32_t wocr_pp_pages(wocr_pp *p, const uint8_t *const *pages, const int32_t *w, const int32_t *h, int32_t n,
+                      int32_t max_side, const float *db, float relv, int32_t per_batch, int32_t merge, int32_t lanes,
+                      float *boxes, int64_t box_cap, int32_t *n_lines, uint32_t *best, int64_t cap, int32_t *steps,
+                      int64_t *bytes);
 
 /* Word rectangles of binary page masks: `word_rects` (src/bin/ocr-bench.rs:38-60), i.e. the
  * external contours (find_contours, External), each simplified (Douglas-Peucker, epsilon 2), its

@@ -1099,23 +1099,33 @@ int32_t wocr_recognize(wocr_recognizer *rec, const float *const *batches, const 
 }
 
 // ---- N-D graph ----------------------------------------------------------------------------
+}  // extern "C"
+
+// An N-D graph handle on `ctx` from a parsed model (wocr_ndgraph_create, and the extra lanes of
+// the page pipeline, which rebuild their graphs from the models kept at create time).
+static wocr_ndgraph *ndgraph_from_model(wocr_ctx *ctx, const Model &m, bool stop_before_softmax) {
+    WOCR_CUDA(cudaSetDevice(ctx->c.device));
+    auto *g = new wocr_ndgraph();
+    g->ctx = ctx;
+    ctx->refs++;
+    try {
+        g->graph = build_ndgraph(&ctx->c, m, stop_before_softmax);
+        WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
+    } catch (...) {
+        delete g;
+        ctx_release(ctx);
+        throw;
+    }
+    return g;
+}
+
+extern "C" {
+
 int32_t wocr_ndgraph_create(wocr_ctx *ctx, const wocr_model *model, int32_t stop_before_softmax, wocr_ndgraph **out) {
     return guard([&] {
         if (!ctx || !out) fail(WOCR_ERR_INVALID, "null argument");
         WOCR_CUDA(cudaSetDevice(ctx->c.device));
-        Model m = model_from_c(model);
-        auto *g = new wocr_ndgraph();
-        g->ctx = ctx;
-        ctx->refs++;
-        try {
-            g->graph = build_ndgraph(&ctx->c, m, stop_before_softmax != 0);
-            WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
-        } catch (...) {
-            delete g;
-            ctx_release(ctx);
-            throw;
-        }
-        *out = g;
+        *out = ndgraph_from_model(ctx, model_from_c(model), stop_before_softmax != 0);
     });
 }
 
@@ -1233,35 +1243,176 @@ static void put_dims(const std::vector<int64_t> &s, int64_t *out_shape, int32_t 
         for (size_t d = 0; d < s.size(); d++) out_shape[d] = s[d];
 }
 
+}  // extern "C"
+
+// The bodies of NdGraph::run and NdGraph::run + argmax.  `read(dst, device src, bytes)` brings a
+// result to the host: at once for the synchronous entry points (then a wait), or staged into a
+// wocr_batch for the enqueue variants (NdGraph::argmax_record, src/nd.rs:1372-1380, read later by
+// wocr_wait as Gpu::read_many reads, src/gpu.rs:1011-1037).
+template <typename Read>
+static void nd_run_core(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank, float *out,
+                        int64_t out_cap, int64_t *out_shape, int32_t *out_rank, Read &&read) {
+    Ctx *c = &g->ctx->c;
+    if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
+    bool first = false;
+    NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 0, &first);
+    if (!r || first) {
+        DT y = g->graph->run(nd_input(c, x, shape, rank));
+        put_shape(y, out_shape, out_rank);
+        if (r) r->out_shape = y.shape;
+        if (out) {
+            if (out_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(y.shape));
+            y = to_rowmajor(c, y);
+            read(out, y.p, (size_t)y.numel() * 4);
+        }
+        return;
+    }
+    put_dims(r->out_shape, out_shape, out_rank);
+    int64_t m = 1;
+    for (auto d : r->out_shape) m *= d;
+    if (!out) return;
+    if (out_cap < m) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(r->out_shape));
+    nd_capture(g, r);
+    nd_replay_launch(g, r, x);
+    read(out, r->out->p, (size_t)m * 4);
+}
+
+template <typename Read>
+static void nd_argmax_core(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank, uint32_t *best,
+                           float *row_max, float *row_lse, int64_t cap, int64_t *rows_out, int64_t *out_shape,
+                           int32_t *out_rank, Read &&read) {
+    Ctx *c = &g->ctx->c;
+    if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
+    bool first = false;
+    NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 1, &first);
+    if (!r || first) {
+        Executor &ex = *g->graph;
+        DT in = nd_input(c, x, shape, rank);
+        // a final linear layer (the CTC head) takes the arg-max into its epilogue
+        const bool fused = ex.ends_in_linear() && !std::getenv("WOCR_UNFUSED_ARGMAX");
+        DT y = fused ? ex.run_to(in, (int)ex.steps.size() - 1) : to_rowmajor(c, ex.run(in));
+        std::vector<int64_t> oshape = y.shape;
+        if (fused && !oshape.empty()) oshape.back() = ex.steps.back().ln;
+        put_dims(oshape, out_shape, out_rank);
+        int64_t len = oshape.empty() ? 1 : oshape.back(), rows = 1;
+        for (auto d : oshape) rows *= d;
+        rows /= std::max<int64_t>(len, 1);
+        if (rows_out) *rows_out = rows;
+        if (r) {
+            r->out_shape = oshape;
+            r->rows = rows;
+            r->len = len;
+        }
+        if (cap < rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
+        BufP b = alloc(c, (size_t)rows * 4), mx = alloc(c, (size_t)rows * 4), ls = alloc(c, (size_t)rows * 4);
+        if (fused)
+            ex.linear_argmax(y, (uint32_t *)b->p, (float *)mx->p, (float *)ls->p);
+        else
+            k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr,
+                      0);
+        read(best, b->p, (size_t)rows * 4);
+        read(row_max, mx->p, (size_t)rows * 4);
+        read(row_lse, ls->p, (size_t)rows * 4);
+        return;
+    }
+    put_dims(r->out_shape, out_shape, out_rank);
+    if (rows_out) *rows_out = r->rows;
+    if (cap < r->rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
+    nd_capture(g, r);
+    nd_replay_launch(g, r, x);
+    read(best, r->best->p, (size_t)r->rows * 4);
+    read(row_max, r->mx->p, (size_t)r->rows * 4);
+    read(row_lse, r->lse->p, (size_t)r->rows * 4);
+}
+
+// ---- record, then read in one wait ------------------------------------------------------------
+// The reference records NdGraph::run and argmax_record into one command encoder and reads every
+// recorded buffer with one Gpu::read_many (src/bin/ocr-bench.rs:240-253).  A wocr_batch is that
+// encoder's read list: each enqueue queues its work on the context stream and a device-to-host
+// copy of its results into page-locked staging owned by the batch; wocr_wait waits once and
+// copies the staged results to the callers' buffers.
+struct wocr_batch {
+    wocr_ctx *ctx = nullptr;
+    struct Chunk {
+        uint8_t *p = nullptr;
+        size_t bytes = 0;
+    };
+    std::vector<Chunk> chunks;  // staging, kept for reuse across waits
+    size_t cur = 0, off = 0;
+    struct Out {
+        void *dst;
+        const uint8_t *src;
+        size_t bytes;
+    };
+    std::vector<Out> outs;
+    int64_t recorded = 0;
+    ~wocr_batch() {
+        for (auto &ch : chunks) cudaFreeHost(ch.p);
+    }
+};
+
+static uint8_t *batch_stage(wocr_batch *b, size_t bytes) {
+    bytes = (bytes + 255) / 256 * 256;
+    while (b->cur < b->chunks.size() && b->off + bytes > b->chunks[b->cur].bytes) {
+        b->cur++;
+        b->off = 0;
+    }
+    if (b->cur == b->chunks.size()) {
+        const size_t sz = std::max<size_t>(bytes, (size_t)4 << 20);
+        void *p = nullptr;
+        WOCR_CUDA(cudaHostAlloc(&p, sz, cudaHostAllocPortable));
+        b->chunks.push_back({(uint8_t *)p, sz});
+        b->off = 0;
+    }
+    uint8_t *p = b->chunks[b->cur].p + b->off;
+    b->off += bytes;
+    return p;
+}
+
+// A reader for the cores above that stages into `b`.
+struct BatchRead {
+    wocr_batch *b;
+    Ctx *c;
+    void operator()(void *dst, const void *src, size_t bytes) const {
+        if (!dst || !bytes) return;
+        uint8_t *s = batch_stage(b, bytes);
+        WOCR_CUDA(cudaMemcpyAsync(s, src, bytes, cudaMemcpyDeviceToHost, c->stream));
+        b->outs.push_back({dst, s, bytes});
+    }
+};
+
+// Waits for everything recorded in `b` (bounded) and hands the staged results to their buffers.
+static void batch_wait(wocr_batch *b, int timeout_ms) {
+    Ctx *c = &b->ctx->c;
+    WOCR_CUDA(cudaSetDevice(c->device));
+    try {
+        sync_bounded(c, timeout_ms);
+    } catch (const Error &e) {
+        // a wait that ran out while the stream still works keeps the reads pending (a later
+        // wocr_wait may finish them); any other failure drops them
+        if (!(e.code == WOCR_ERR_TIMEOUT && cudaStreamQuery(c->stream) == cudaErrorNotReady)) {
+            b->outs.clear();
+            b->cur = b->off = 0;
+            b->recorded = 0;
+        }
+        throw;
+    }
+    for (const auto &o : b->outs) std::memcpy(o.dst, o.src, o.bytes);
+    b->outs.clear();
+    b->cur = b->off = 0;
+    b->recorded = 0;
+}
+
+extern "C" {
+
 int32_t wocr_ndgraph_run(wocr_ndgraph *g, const float *x, const int64_t *shape, int32_t rank, float *out,
                          int64_t out_cap, int64_t *out_shape, int32_t *out_rank) {
     return guard([&] {
         if (!g) fail(WOCR_ERR_INVALID, "null graph");
         Ctx *c = &g->ctx->c;
         RunScope rs(c, &g->last);
-        if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
-        bool first = false;
-        NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 0, &first);
-        if (!r || first) {
-            DT y = g->graph->run(nd_input(c, x, shape, rank));
-            put_shape(y, out_shape, out_rank);
-            if (r) r->out_shape = y.shape;
-            if (out) {
-                if (out_cap < y.numel()) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(y.shape));
-                y = to_rowmajor(c, y);
-                d2h(c, out, y.p, (size_t)y.numel() * 4);
-            }
-            sync_bounded(c, 0);
-            return;
-        }
-        put_dims(r->out_shape, out_shape, out_rank);
-        int64_t m = 1;
-        for (auto d : r->out_shape) m *= d;
-        if (!out) return;
-        if (out_cap < m) fail(WOCR_ERR_CAPACITY, "output buffer too small for " + shape_str(r->out_shape));
-        nd_capture(g, r);
-        nd_replay_launch(g, r, x);
-        d2h(c, out, r->out->p, (size_t)m * 4);
+        nd_run_core(g, x, shape, rank, out, out_cap, out_shape, out_rank,
+                    [&](void *dst, const void *src, size_t bytes) { d2h(c, dst, src, bytes); });
         sync_bounded(c, 0);
     });
 }
@@ -1273,49 +1424,65 @@ int32_t wocr_ndgraph_run_argmax(wocr_ndgraph *g, const float *x, const int64_t *
         if (!g) fail(WOCR_ERR_INVALID, "null graph");
         Ctx *c = &g->ctx->c;
         RunScope rs(c, &g->last);
-        if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
-        bool first = false;
-        NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 1, &first);
-        if (!r || first) {
-            Executor &ex = *g->graph;
-            DT in = nd_input(c, x, shape, rank);
-            // a final linear layer (the CTC head) takes the arg-max into its epilogue
-            const bool fused = ex.ends_in_linear() && !std::getenv("WOCR_UNFUSED_ARGMAX");
-            DT y = fused ? ex.run_to(in, (int)ex.steps.size() - 1) : to_rowmajor(c, ex.run(in));
-            std::vector<int64_t> oshape = y.shape;
-            if (fused && !oshape.empty()) oshape.back() = ex.steps.back().ln;
-            put_dims(oshape, out_shape, out_rank);
-            int64_t len = oshape.empty() ? 1 : oshape.back(), rows = 1;
-            for (auto d : oshape) rows *= d;
-            rows /= std::max<int64_t>(len, 1);
-            if (rows_out) *rows_out = rows;
-            if (r) {
-                r->out_shape = oshape;
-                r->rows = rows;
-                r->len = len;
-            }
-            if (cap < rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
-            BufP b = alloc(c, (size_t)rows * 4), mx = alloc(c, (size_t)rows * 4), ls = alloc(c, (size_t)rows * 4);
-            if (fused)
-                ex.linear_argmax(y, (uint32_t *)b->p, (float *)mx->p, (float *)ls->p);
-            else
-                k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr,
-                          0);
-            if (best) d2h(c, best, b->p, (size_t)rows * 4);
-            if (row_max) d2h(c, row_max, mx->p, (size_t)rows * 4);
-            if (row_lse) d2h(c, row_lse, ls->p, (size_t)rows * 4);
-            sync_bounded(c, 0);
-            return;
-        }
-        put_dims(r->out_shape, out_shape, out_rank);
-        if (rows_out) *rows_out = r->rows;
-        if (cap < r->rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
-        nd_capture(g, r);
-        nd_replay_launch(g, r, x);
-        if (best) d2h(c, best, r->best->p, (size_t)r->rows * 4);
-        if (row_max) d2h(c, row_max, r->mx->p, (size_t)r->rows * 4);
-        if (row_lse) d2h(c, row_lse, r->lse->p, (size_t)r->rows * 4);
+        nd_argmax_core(g, x, shape, rank, best, row_max, row_lse, cap, rows_out, out_shape, out_rank,
+                       [&](void *dst, const void *src, size_t bytes) {
+                           if (dst) d2h(c, dst, src, bytes);
+                       });
         sync_bounded(c, 0);
+    });
+}
+
+int32_t wocr_batch_create(wocr_ctx *ctx, wocr_batch **out) {
+    return guard([&] {
+        if (!ctx || !out) fail(WOCR_ERR_INVALID, "null argument");
+        auto *b = new wocr_batch();
+        b->ctx = ctx;
+        ctx->refs++;
+        *out = b;
+    });
+}
+
+void wocr_batch_destroy(wocr_batch *b) {
+    if (!b) return;
+    wocr_ctx *ctx = b->ctx;
+    cudaSetDevice(ctx->c.device);
+    cudaStreamSynchronize(ctx->c.stream);  // no staged copy may still be writing
+    delete b;
+    ctx_release(ctx);
+}
+
+int64_t wocr_batch_pending(wocr_batch *b) { return b ? b->recorded : -1; }
+
+int32_t wocr_ndgraph_run_enqueue(wocr_ndgraph *g, wocr_batch *b, const float *x, const int64_t *shape, int32_t rank,
+                                 float *out, int64_t out_cap, int64_t *out_shape, int32_t *out_rank) {
+    return guard([&] {
+        if (!g || !b) fail(WOCR_ERR_INVALID, "null graph or batch");
+        if (b->ctx != g->ctx) fail(WOCR_ERR_INVALID, "the batch belongs to another context");
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        nd_run_core(g, x, shape, rank, out, out_cap, out_shape, out_rank, BatchRead{b, c});
+        b->recorded++;
+    });
+}
+
+int32_t wocr_ndgraph_argmax_enqueue(wocr_ndgraph *g, wocr_batch *b, const float *x, const int64_t *shape,
+                                    int32_t rank, uint32_t *best, float *row_max, float *row_lse, int64_t cap,
+                                    int64_t *rows_out, int64_t *out_shape, int32_t *out_rank) {
+    return guard([&] {
+        if (!g || !b) fail(WOCR_ERR_INVALID, "null graph or batch");
+        if (b->ctx != g->ctx) fail(WOCR_ERR_INVALID, "the batch belongs to another context");
+        Ctx *c = &g->ctx->c;
+        RunScope rs(c, &g->last);
+        nd_argmax_core(g, x, shape, rank, best, row_max, row_lse, cap, rows_out, out_shape, out_rank,
+                       BatchRead{b, c});
+        b->recorded++;
+    });
+}
+
+int32_t wocr_wait(wocr_batch *b, int32_t timeout_ms) {
+    return guard([&] {
+        if (!b) fail(WOCR_ERR_INVALID, "null batch");
+        batch_wait(b, timeout_ms);
     });
 }
 
@@ -1830,14 +1997,35 @@ int32_t wocr_last_run_stats(void *handle, int32_t kind, double *flops, int64_t *
 }  // extern "C"
 
 // ---- the PP-OCRv6 page pipeline --------------------------------------------------------------
-
-struct wocr_pp {
+//
+// The reference's bench runs a page in two halves on two threads (src/bin/ocr-bench.rs:133-310,
+// 458-585): its GPU thread detects page k + 1 while the CPU turns page k's map into boxes and
+// line images; recognition jobs wait until MERGE pages are held and then run every batch in one
+// encoder, read with one wait.  Here both halves run on the device, so the overlap is between
+// pages on the device: a pipeline owns `lanes` workers on one GPU, each a context (stream, pool,
+// graph caches) with its own detector and recogniser graphs and a host thread.  Lane j takes
+// pages j, j + lanes, ...; while one lane's page is in its latency-bound steps (the contour of a
+// large component, a small recognition batch), the others' kernels fill the SMs.  Each lane holds
+// the line batches of `merge` of its pages and recognises them together: every batch queued on
+// its stream with its arg-max read staged (wocr_ndgraph_argmax_enqueue), then one wait.
+struct PpLane {
     wocr_ctx *ctx = nullptr;
     wocr_ndgraph *det = nullptr, *rec = nullptr;
-    ~wocr_pp() {
+    wocr_batch *batch = nullptr;
+    BufP page;  // the device copy of a host page
+    size_t page_bytes = 0;
+    ~PpLane() {
+        if (batch) wocr_batch_destroy(batch);
         if (det) wocr_ndgraph_destroy(det);
         if (rec) wocr_ndgraph_destroy(rec);
+        if (ctx) wocr_ctx_destroy(ctx);  // the lane's own reference
     }
+};
+
+struct wocr_pp {
+    wocr_ctx *ctx = nullptr;  // lane 0's context (the caller's)
+    Model det_m, rec_m;       // kept to build further lanes
+    std::vector<std::unique_ptr<PpLane>> lanes;
 };
 
 namespace {
@@ -1845,20 +2033,206 @@ namespace {
 void check_st(int32_t st) {
     if (st != WOCR_OK) fail(st, wocr_last_error());
 }
+
+// One page between its two halves: boxes in reading order, the line batches on the device,
+// then the arg-max classes of each line.
+struct PpPage {
+    std::vector<float> boxes;  // [n][6]
+    std::vector<int32_t> order, bn, bw;
+    int32_t nb = 0;
+    BufP lines;                // the batches, one after another, [bn, 3, 48, bw] each
+    std::vector<std::vector<uint32_t>> best;  // per line
+    int64_t h2d = 0, d2h = 0;
+};
+
+struct PpArgs {
+    int max_side;
+    const float *db;
+    float relv;
+    int per_batch;
+    bool want_rec;
+};
+
+bool on_device(const void *p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice;
+}
+
+// The first half of a page: upload (host pages), detection, DB boxes, line cuts.
+void pp_front(PpLane &ln, const uint8_t *rgb, int w, int h, const PpArgs &a, PpPage &out) {
+    Ctx *c = &ln.ctx->c;
+    WOCR_CUDA(cudaSetDevice(c->device));
+    const size_t bytes = (size_t)w * h * 3;
+    const uint8_t *dpage = rgb;
+    if (!on_device(rgb)) {
+        // the page crosses PCIe once; detection and the line cuts read it on the device
+        if (ln.page_bytes < bytes) {
+            ln.page = alloc(c, bytes);
+            ln.page_bytes = bytes;
+        }
+        WOCR_CUDA(cudaMemcpyAsync(ln.page->p, rgb, bytes, cudaMemcpyHostToDevice, c->stream));
+        dpage = (const uint8_t *)ln.page->p;
+        out.h2d += (int64_t)bytes;
+    }
+    int32_t ow = 0, oh = 0;
+    float tp[2];
+    check_st(wocr_ppdet_page(ln.det, dpage, w, h, a.max_side, nullptr, 0, &ow, &oh, tp));
+    out.boxes = db_boxes(c, ln.det->map, ln.det->map_w, ln.det->map_h, ln.det->map_to_page, a.db[0], a.db[1], a.db[2],
+                         a.db[3]);
+    const int n = (int)(out.boxes.size() / 6);
+    if (!a.want_rec || n == 0) return;
+    // lines: each box grown by relv x its height across the text (src/bin/ocr-bench.rs:534-558:
+    // a line of one box, whose median height is its own), cut at its bounding rectangle
+    std::vector<float> lr((size_t)n * 4);
+    for (int i = 0; i < n; i++) {
+        const float *r = out.boxes.data() + 6 * (size_t)i;
+        const bool upright = std::fabs(r[3]) >= std::fabs(r[2]);
+        const float across = a.relv * (upright ? r[5] : r[4]);
+        const float rw = upright ? r[4] : r[4] + 2.f * across, rh = upright ? r[5] + 2.f * across : r[5];
+        const float hw = rw / 2.0f, hh = rh / 2.0f;
+        float lx = INFINITY, ty = INFINITY, rx = -INFINITY, by = -INFINITY;
+        for (int sa = -1; sa <= 1; sa += 2)
+            for (int sb = -1; sb <= 1; sb += 2) {
+                const float px = r[0] + sa * hh * r[2] + sb * hw * -r[3];
+                const float py = r[1] + sa * hh * r[3] + sb * hw * r[2];
+                lx = std::min(lx, px), rx = std::max(rx, px);
+                ty = std::min(ty, py), by = std::max(by, py);
+            }
+        float *o = lr.data() + 4 * (size_t)i;
+        o[0] = lx;
+        o[1] = ty;
+        o[2] = rx;
+        o[3] = by;
+    }
+    out.order.assign((size_t)n, 0);
+    out.bn.assign((size_t)n, 0);
+    out.bw.assign((size_t)n, 0);
+    int64_t total = 0;
+    check_st(wocr_pp_lines(ln.ctx, dpage, w, h, lr.data(), n, a.per_batch, nullptr, 0, out.order.data(), out.bn.data(),
+                           out.bw.data(), &out.nb, &total));
+    out.lines = alloc(c, (size_t)std::max<int64_t>(total, 1) * 4);
+    check_st(wocr_pp_lines(ln.ctx, dpage, w, h, lr.data(), n, a.per_batch, (float *)out.lines->p, total,
+                           out.order.data(), out.bn.data(), out.bw.data(), &out.nb, &total));
+}
+
+// The second half of the held pages: every batch's recognition and arg-max queued on the lane's
+// stream with its read staged, one wait, then the classes handed to their lines.
+void pp_recognize(PpLane &ln, const std::vector<PpPage *> &held) {
+    struct Job {
+        PpPage *pg;
+        int first;  // the batch's first slot in pg->order
+        int n;
+        std::vector<uint32_t> best;
+        int64_t rows = 0;
+    };
+    std::vector<Job> jobs;
+    for (PpPage *pg : held) {
+        pg->best.assign(pg->boxes.size() / 6, {});
+        int k = 0;
+        for (int b = 0; b < pg->nb; k += pg->bn[b], b++) jobs.push_back({pg, k, pg->bn[b], {}, 0});
+    }
+    if (jobs.empty()) return;
+    size_t j = 0;
+    for (PpPage *pg : held) {
+        int64_t off = 0;
+        for (int b = 0; b < pg->nb; b++, j++) {
+            Job &jb = jobs[j];
+            const int64_t shape[4] = {pg->bn[b], 3, 48, pg->bw[b]};
+            const int64_t bcap = (int64_t)pg->bn[b] * pg->bw[b];
+            jb.best.resize((size_t)bcap);
+            int64_t oshape[kMaxRank];
+            int32_t orank = 0;
+            check_st(wocr_ndgraph_argmax_enqueue(ln.rec, ln.batch, (const float *)pg->lines->p + off, shape, 4,
+                                                 jb.best.data(), nullptr, nullptr, bcap, &jb.rows, oshape, &orank));
+            off += (int64_t)pg->bn[b] * 3 * 48 * pg->bw[b];
+        }
+    }
+    check_st(wocr_wait(ln.batch, 0));
+    for (Job &jb : jobs) {
+        const int64_t T = jb.rows / std::max(jb.n, 1);
+        for (int q = 0; q < jb.n; q++)
+            jb.pg->best[jb.pg->order[jb.first + q]].assign(jb.best.begin() + q * T, jb.best.begin() + (q + 1) * T);
+        jb.pg->d2h += jb.rows * 4;
+    }
+}
+
+PpLane *pp_lane(wocr_pp *p, int i) {
+    while ((int)p->lanes.size() <= i) {
+        auto ln = std::make_unique<PpLane>();
+        if (p->lanes.empty()) {
+            ln->ctx = p->ctx;
+            p->ctx->refs++;
+        } else {
+            check_st(wocr_ctx_create(p->ctx->c.device, p->ctx->c.lines, &ln->ctx));
+        }
+        ln->det = ndgraph_from_model(ln->ctx, p->det_m, false);
+        ln->rec = ndgraph_from_model(ln->ctx, p->rec_m, true);
+        check_st(wocr_batch_create(ln->ctx, &ln->batch));
+        p->lanes.push_back(std::move(ln));
+    }
+    return p->lanes[i].get();
+}
+
+// Pages [0, n) over `lanes` lanes, recognitions merged `merge` pages at a time per lane.
+void pp_run(wocr_pp *p, const uint8_t *const *pages, const int32_t *w, const int32_t *h, int n, const PpArgs &a,
+            int merge, int lanes, std::vector<PpPage> &out) {
+    lanes = std::max(1, std::min(lanes, n));
+    merge = std::max(1, merge);
+    for (int i = 0; i < lanes; i++) pp_lane(p, i);
+    out.assign((size_t)n, PpPage{});
+    std::vector<std::exception_ptr> errs((size_t)lanes);
+    auto work = [&](int L) {
+        try {
+            PpLane &ln = *p->lanes[L];
+            WOCR_CUDA(cudaSetDevice(ln.ctx->c.device));
+            std::vector<PpPage *> held;
+            for (int k = L; k < n; k += lanes) {
+                pp_front(ln, pages[k], w[k], h[k], a, out[k]);
+                held.push_back(&out[k]);
+                if (a.want_rec && ((int)held.size() >= merge || k + lanes >= n)) {
+                    pp_recognize(ln, held);
+                    held.clear();
+                }
+            }
+        } catch (...) {
+            errs[L] = std::current_exception();
+        }
+    };
+    std::vector<std::thread> th;
+    for (int L = 1; L < lanes; L++) th.emplace_back(work, L);
+    work(0);
+    for (auto &t : th) t.join();
+    for (auto &e : errs)
+        if (e) std::rethrow_exception(e);
+}
 }  // namespace
+
+extern "C" {
 
 int32_t wocr_pp_create(wocr_ctx *ctx, const wocr_model *det, const wocr_model *rec, wocr_pp **out) {
     return guard([&] {
         if (!ctx || !det || !rec || !out) fail(WOCR_ERR_INVALID, "null argument");
         auto p = std::make_unique<wocr_pp>();
         p->ctx = ctx;
-        check_st(wocr_ndgraph_create(ctx, det, 0, &p->det));
-        check_st(wocr_ndgraph_create(ctx, rec, 1, &p->rec));
+        p->det_m = model_from_c(det);
+        p->rec_m = model_from_c(rec);
+        pp_lane(p.get(), 0);
         *out = p.release();
     });
 }
 
 void wocr_pp_destroy(wocr_pp *p) { delete p; }
+
+int64_t wocr_pp_launches(wocr_pp *p) {
+    if (!p) return -1;
+    int64_t n = 0;
+    for (const auto &ln : p->lanes) n += ln->ctx->c.launches;
+    return n;
+}
 
 int32_t wocr_pp_page(wocr_pp *p, const uint8_t *rgb, int32_t w, int32_t h, int32_t max_side, const float *db,
                      float relv, int32_t per_batch, float *boxes, int32_t box_cap, int32_t *n_lines, uint32_t *best,
@@ -1866,83 +2240,76 @@ int32_t wocr_pp_page(wocr_pp *p, const uint8_t *rgb, int32_t w, int32_t h, int32
     return guard([&] {
         if (!p || !rgb || !db || !n_lines || box_cap < 0 || cap < 0) fail(WOCR_ERR_INVALID, "bad argument");
         if (w <= 0 || h <= 0 || max_side <= 0 || per_batch <= 0) fail(WOCR_ERR_INVALID, "bad page size or batch");
-        Ctx *c = &p->ctx->c;
-        WOCR_CUDA(cudaSetDevice(c->device));
-        // the page crosses PCIe once; detection and the line cuts read it on the device
-        BufP page = alloc(c, (size_t)w * h * 3);
-        WOCR_CUDA(cudaMemcpyAsync(page->p, rgb, (size_t)w * h * 3, cudaMemcpyDefault, c->stream));
-        const uint8_t *dpage = (const uint8_t *)page->p;
-        int32_t ow = 0, oh = 0;
-        float tp[2];
-        check_st(wocr_ppdet_page(p->det, dpage, w, h, max_side, nullptr, 0, &ow, &oh, tp));
-        const std::vector<float> bx = db_boxes(c, p->det->map, p->det->map_w, p->det->map_h, p->det->map_to_page,
-                                               db[0], db[1], db[2], db[3]);
-        const int n = (int)(bx.size() / 6);
+        const bool want_rec = !(!best && cap == 0);
+        if (want_rec && (!best || !steps)) fail(WOCR_ERR_INVALID, "null outputs");
+        std::vector<PpPage> out;
+        const uint8_t *pages[1] = {rgb};
+        pp_run(p, pages, &w, &h, 1, PpArgs{max_side, db, relv, per_batch, want_rec}, 1, 1, out);
+        const PpPage &pg = out[0];
+        const int n = (int)(pg.boxes.size() / 6);
         *n_lines = n;
         if (boxes) {
             if (box_cap < n) fail(WOCR_ERR_CAPACITY, "boxes holds " + std::to_string(box_cap) + " of " + std::to_string(n));
-            if (n) std::memcpy(boxes, bx.data(), bx.size() * 4);
+            if (n) std::memcpy(boxes, pg.boxes.data(), pg.boxes.size() * 4);
         }
-        if (!best && cap == 0) return;
-        if (!best || !steps) fail(WOCR_ERR_INVALID, "null outputs");
-        if (n == 0) return;
-        // lines: each box grown by relv x its height across the text (src/bin/ocr-bench.rs:534-558:
-        // a line of one box, whose median height is its own), cut at its bounding rectangle
-        std::vector<float> lr((size_t)n * 4);
-        for (int i = 0; i < n; i++) {
-            const float *r = bx.data() + 6 * (size_t)i;
-            const bool upright = std::fabs(r[3]) >= std::fabs(r[2]);
-            const float across = relv * (upright ? r[5] : r[4]);
-            const float rw = upright ? r[4] : r[4] + 2.f * across, rh = upright ? r[5] + 2.f * across : r[5];
-            const float hw = rw / 2.0f, hh = rh / 2.0f;
-            float lx = INFINITY, ty = INFINITY, rx = -INFINITY, by = -INFINITY;
-            for (int sa = -1; sa <= 1; sa += 2)
-                for (int sb = -1; sb <= 1; sb += 2) {
-                    const float px = r[0] + sa * hh * r[2] + sb * hw * -r[3];
-                    const float py = r[1] + sa * hh * r[3] + sb * hw * r[2];
-                    lx = std::min(lx, px), rx = std::max(rx, px);
-                    ty = std::min(ty, py), by = std::max(by, py);
-                }
-            float *o = lr.data() + 4 * (size_t)i;
-            o[0] = lx;
-            o[1] = ty;
-            o[2] = rx;
-            o[3] = by;
-        }
-        std::vector<int32_t> order((size_t)n), bn((size_t)n), bw((size_t)n);
-        int32_t nb = 0;
-        int64_t total = 0;
-        check_st(wocr_pp_lines(p->ctx, dpage, w, h, lr.data(), n, per_batch, nullptr, 0, order.data(), bn.data(),
-                               bw.data(), &nb, &total));
-        BufP lines = alloc(c, (size_t)std::max<int64_t>(total, 1) * 4);
-        check_st(wocr_pp_lines(p->ctx, dpage, w, h, lr.data(), n, per_batch, (float *)lines->p, total, order.data(),
-                               bn.data(), bw.data(), &nb, &total));
-        // recognition, a batch at a time, arg-max in the CTC head's epilogue
-        std::vector<std::vector<uint32_t>> per_line((size_t)n);
-        int64_t off = 0;
-        int k = 0;
-        for (int b = 0; b < nb; b++) {
-            const int64_t shape[4] = {bn[b], 3, 48, bw[b]};
-            const int64_t bcap = (int64_t)bn[b] * bw[b];
-            std::vector<uint32_t> bb((size_t)bcap);
-            int64_t rows = 0, oshape[kMaxRank];
-            int32_t orank = 0;
-            check_st(wocr_ndgraph_run_argmax(p->rec, (const float *)lines->p + off, shape, 4, bb.data(), nullptr, nullptr,
-                                             bcap, &rows, oshape, &orank));
-            const int64_t T = rows / std::max(bn[b], 1);
-            for (int j = 0; j < bn[b]; j++)
-                per_line[order[k + j]].assign(bb.begin() + j * T, bb.begin() + (j + 1) * T);
-            off += (int64_t)bn[b] * 3 * 48 * bw[b];
-            k += bn[b];
-        }
+        if (!want_rec) return;
         int64_t need = 0;
-        for (const auto &v : per_line) need += (int64_t)v.size();
+        for (const auto &v : pg.best) need += (int64_t)v.size();
         if (cap < need) fail(WOCR_ERR_CAPACITY, "best holds " + std::to_string(cap) + " of " + std::to_string(need));
         int64_t o = 0;
         for (int i = 0; i < n; i++) {
-            steps[i] = (int32_t)per_line[i].size();
-            std::copy(per_line[i].begin(), per_line[i].end(), best + o);
-            o += (int64_t)per_line[i].size();
+            steps[i] = (int32_t)pg.best[i].size();
+            std::copy(pg.best[i].begin(), pg.best[i].end(), best + o);
+            o += (int64_t)pg.best[i].size();
         }
     });
 }
+
+int32_t wocr_pp_pages(wocr_pp *p, const uint8_t *const *pages, const int32_t *w, const int32_t *h, int32_t n,
+                      int32_t max_side, const float *db, float relv, int32_t per_batch, int32_t merge, int32_t lanes,
+                      float *boxes, int64_t box_cap, int32_t *n_lines, uint32_t *best, int64_t cap, int32_t *steps,
+                      int64_t *bytes) {
+    return guard([&] {
+        if (!p || !pages || !w || !h || !db || !n_lines || n < 0 || box_cap < 0 || cap < 0)
+            fail(WOCR_ERR_INVALID, "bad argument");
+        if (max_side <= 0 || per_batch <= 0 || merge <= 0 || lanes <= 0 || lanes > 64)
+            fail(WOCR_ERR_INVALID, "bad max_side, batch, merge or lane count");
+        for (int k = 0; k < n; k++)
+            if (!pages[k] || w[k] <= 0 || h[k] <= 0) fail(WOCR_ERR_INVALID, "bad page " + std::to_string(k));
+        const bool want_rec = !(!best && cap == 0);
+        if (want_rec && (!best || !steps)) fail(WOCR_ERR_INVALID, "null outputs");
+        std::vector<PpPage> out;
+        pp_run(p, pages, w, h, n, PpArgs{max_side, db, relv, per_batch, want_rec}, merge, lanes, out);
+        int64_t nl = 0, need = 0, h2d = 0, d2h = 0;
+        for (int k = 0; k < n; k++) {
+            n_lines[k] = (int32_t)(out[k].boxes.size() / 6);
+            nl += n_lines[k];
+            for (const auto &v : out[k].best) need += (int64_t)v.size();
+            h2d += out[k].h2d;
+            d2h += out[k].d2h;
+        }
+        if (bytes) {
+            bytes[0] = h2d;
+            bytes[1] = d2h;
+        }
+        if (boxes || box_cap) {
+            if (box_cap < nl) fail(WOCR_ERR_CAPACITY, "boxes holds " + std::to_string(box_cap) + " of " + std::to_string(nl));
+            int64_t o = 0;
+            for (int k = 0; k < n; k++) {
+                if (!out[k].boxes.empty()) std::memcpy(boxes + o, out[k].boxes.data(), out[k].boxes.size() * 4);
+                o += (int64_t)out[k].boxes.size();
+            }
+        }
+        if (!want_rec) return;
+        if (cap < need) fail(WOCR_ERR_CAPACITY, "best holds " + std::to_string(cap) + " of " + std::to_string(need));
+        int64_t o = 0, li = 0;
+        for (int k = 0; k < n; k++)
+            for (const auto &v : out[k].best) {
+                steps[li++] = (int32_t)v.size();
+                std::copy(v.begin(), v.end(), best + o);
+                o += (int64_t)v.size();
+            }
+    });
+}
+
+}  // extern "C"

@@ -26,12 +26,11 @@ static int round4(int v) { return (v + 3) / 4 * 4; }
 // Dense convolutions and matrix products run on the tcgen05 tensor-core kernel; WOCR_SIMT_GEMM=1
 // selects the CUDA-core fp32 kernel instead (a diagnosis switch for comparing the two).
 static bool use_umma() {
-    static int v = -1;
-    if (v < 0) {
+    static const bool v = [] {
         const char *e = std::getenv("WOCR_SIMT_GEMM");
-        v = (e && e[0] == '1') ? 0 : 1;
-    }
-    return v == 1;
+        return !(e && e[0] == '1');
+    }();
+    return v;
 }
 
 std::shared_ptr<k::UmmaW> linear_umma(Ctx *c, const float *w_kn, int K, int N) {

@@ -12,6 +12,7 @@
 //      and `barrier.cluster` (hardware co-scheduled CTAs: no global-memory spin waits) publishes
 //      it: arrive right after the stores, wait before the next step reads h.
 // Each line runs for its own length; the backward direction starts at len - 1 (src/gpu.rs:797-800).
+#include <atomic>
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
@@ -202,7 +203,7 @@ template <int L>
 void launch_gru(Ctx *c, const float *g, const float *r, const float *rb, const int *lens, int tmax, int ntot,
                 float *y) {
     size_t smem = gru_smem<L>();
-    static bool configured[64] = {false};
+    static std::atomic<bool> configured[64];
     if (!configured[c->device]) {
         WOCR_CUDA(cudaFuncSetAttribute(k_gru<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         configured[c->device] = true;
@@ -226,7 +227,7 @@ void launch_gru(Ctx *c, const float *g, const float *r, const float *rb, const i
 
 template <int L>
 int max_clusters(Ctx *c) {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];
     if (cached[c->device]) return cached[c->device];
     size_t smem = gru_smem<L>();
     WOCR_CUDA(cudaFuncSetAttribute(k_gru<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -23,6 +23,7 @@
 //   warp 13     tensor-memory allocation and MMA issue.
 // Every wait is bounded; on expiry the kernel records an error code, drains its own copies and
 // MMAs, frees its tensor memory and returns.
+#include <atomic>
 #include "kernels.h"
 #include "tc.h"
 #include "tconv.h"
@@ -1022,7 +1023,7 @@ void encode(CUtensorMap *map, int rank, void *base, const cuuint64_t *dims, cons
 
 template <int BN, int CG, int TAPS, int MB>
 void launch(Ctx *c, const TconvW &w, const TcP &p, int smem) {
-    static bool set[64] = {false};
+    static std::atomic<bool> set[64];
     if (!set[c->device]) {
         WOCR_CUDA(cudaFuncSetAttribute(k_tconv<BN, CG, TAPS, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        227 * 1024));
@@ -1056,7 +1057,7 @@ int tconv_bn(int N) { return N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128; }
 template <int C, int CG, bool WHOLE, bool CT>
 void launch_rows(Ctx *c, const TconvW &w, const TcP &p, int smem, const CUtensorMap *xm) {
     constexpr bool LO = C == 16;  // 2 MMAs over 2 T C columns; C = 32: 3 MMAs over T C columns
-    static bool set[64] = {false};
+    static std::atomic<bool> set[64];
     if (!set[c->device]) {
         WOCR_CUDA(cudaFuncSetAttribute(k_tconv_rows<C, CG, LO, WHOLE, CT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));

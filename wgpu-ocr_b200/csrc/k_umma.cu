@@ -23,6 +23,7 @@
 // Stages are handed over with mbarriers.  Every wait is bounded by a clock budget; on expiry
 // the kernel records an error code in `status`, drains its own TMA loads and MMAs, frees its
 // tensor memory and returns.
+#include <atomic>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -519,7 +520,7 @@ void make_map(CUtensorMap *map, void *base, int N, int Kpad, int bn) {
 template <int BN, int STAGES, int CHAINS = 0>
 void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const UmmaP &p) {
     using Lay = Layout<BN, STAGES>;
-    static bool set[64] = {false};
+    static std::atomic<bool> set[64];
     if (!set[c->device]) {
         WOCR_CUDA(cudaFuncSetAttribute(k_umma<BN, STAGES, CHAINS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        Lay::total));

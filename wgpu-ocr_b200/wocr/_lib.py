@@ -101,6 +101,7 @@ _SIGS = [
                                 c_void_p]),
     ("wocr_pp_create", c_i32, [c_void_p, P(CModel), P(CModel), P(c_void_p)]),
     ("wocr_pp_destroy", None, [c_void_p]),
+    ("wocr_pp_launches", c_i64, [c_void_p]),
     ("wocr_pp_page", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_void_p, c_f32, c_i32, c_void_p, c_i32,
                              P(c_i32), c_void_p, c_i64, c_void_p]),
     ("wocr_ppdet_boxes", c_i32, [c_void_p, c_f32, c_f32, c_f32, c_f32, c_void_p, c_i32, P(c_i32)]),
@@ -111,6 +112,16 @@ _SIGS = [
     ("wocr_model_load", c_i32, [c_char_p, P(P(CModel))]),
     ("wocr_model_parse", c_i32, [c_void_p, c_i64, P(P(CModel))]),
     ("wocr_model_free", None, [P(CModel)]),
+    ("wocr_batch_create", c_i32, [c_void_p, P(c_void_p)]),
+    ("wocr_batch_destroy", None, [c_void_p]),
+    ("wocr_batch_pending", c_i64, [c_void_p]),
+    ("wocr_ndgraph_run_enqueue", c_i32, [c_void_p, c_void_p, c_void_p, P(c_i64), c_i32, c_void_p, c_i64, P(c_i64),
+                                         P(c_i32)]),
+    ("wocr_ndgraph_argmax_enqueue", c_i32, [c_void_p, c_void_p, c_void_p, P(c_i64), c_i32, c_void_p, c_void_p,
+                                            c_void_p, c_i64, P(c_i64), P(c_i64), P(c_i32)]),
+    ("wocr_wait", c_i32, [c_void_p, c_i32]),
+    ("wocr_pp_pages", c_i32, [c_void_p, c_void_p, c_void_p, c_void_p, c_i32, c_i32, c_void_p, c_f32, c_i32, c_i32,
+                              c_i32, c_void_p, c_i64, c_void_p, c_void_p, c_i64, c_void_p, c_void_p]),
     ("wocr_pp_lines", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_void_p, c_i32, c_i32, c_void_p, c_i64, c_void_p,
                               c_void_p, c_void_p, P(c_i32), P(c_i64)]),
 ]

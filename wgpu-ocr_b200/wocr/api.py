@@ -269,6 +269,57 @@ class Recognizer(_Handle):
             pass
 
 
+class Batch:
+    """A record-then-read list (`wocr_batch`): the reference's command encoder plus
+    `Gpu::read_many` (src/gpu.rs:1011-1037).  `NdGraph.argmax_enqueue` / `run_enqueue` queue work
+    on the device without waiting; `wait()` waits once and fills every pending result."""
+
+    def __init__(self, gpu: Gpu):
+        self.gpu = gpu
+        h = ctypes.c_void_p()
+        L.check(L.lib().wocr_batch_create(gpu.h, ctypes.byref(h)))
+        self.h = h
+        self._keep = []      # inputs and outputs that must live until the wait
+        self._pending = []
+
+    @property
+    def pending(self) -> int:
+        return int(L.lib().wocr_batch_pending(self.h))
+
+    def wait(self, timeout_ms: int = 0):
+        """Wait (bounded when timeout_ms > 0) and deliver every recorded result."""
+        L.check(L.lib().wocr_wait(self.h, int(timeout_ms)))
+        for p in self._pending:
+            p.done = True
+        self._pending = []
+        self._keep = []
+
+    def close(self):
+        if getattr(self, "h", None):
+            L.lib().wocr_batch_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Pending:
+    """Results of one enqueued call, valid once its batch has waited (`done`)."""
+
+    def __init__(self, **kw):
+        self.done = False
+        self.__dict__.update(kw)
+
+
 class NdGraph(_Handle):
     """`NdGraph` (src/nd.rs:428-1394): the N-D executor with its load-time fusions."""
 
@@ -321,6 +372,34 @@ class NdGraph(_Handle):
             r = rows.value
             shape = tuple(oshape[i] for i in range(orank.value))
             return best[:r], mx[:r], lse[:r], shape
+
+    def argmax_enqueue(self, batch: "Batch", x: np.ndarray) -> "Pending":
+        """NdGraph::run + argmax_record (src/nd.rs:1372-1380): queued on the device, read by
+        `batch.wait()`.  Returns a `Pending` whose best / row_max / row_lse ([rows]) and shape
+        are filled by the wait."""
+        x = np.ascontiguousarray(x, np.float32)
+        shp = (ctypes.c_int64 * x.ndim)(*x.shape)
+        cap = max(int(np.prod(x.shape)), 1 << 16)
+        while True:
+            best = np.empty(cap, np.uint32)
+            mx = np.empty(cap, np.float32)
+            lse = np.empty(cap, np.float32)
+            rows = ctypes.c_int64()
+            oshape = (ctypes.c_int64 * 6)()
+            orank = ctypes.c_int32()
+            st = L.lib().wocr_ndgraph_argmax_enqueue(self.h, batch.h, L.ptr(x), shp, x.ndim, L.ptr(best), L.ptr(mx),
+                                                     L.ptr(lse), cap, ctypes.byref(rows), oshape, ctypes.byref(orank))
+            if st == 8 and rows.value > cap:
+                cap = rows.value
+                continue
+            L.check(st)
+            break
+        r = rows.value
+        pend = Pending(best=best[:r], row_max=mx[:r], row_lse=lse[:r],
+                       shape=tuple(oshape[i] for i in range(orank.value)))
+        batch._keep += [x, best, mx, lse]
+        batch._pending.append(pend)
+        return pend
 
     def ppdet_page(self, rgb: np.ndarray, w: int, h: int, max_side: int, read_map: bool = True):
         """det_input + run on one page (src/bin/ocr-bench.rs:186-200): (prob [oh, ow], to_page).
@@ -448,6 +527,67 @@ class PPPipeline:
         k = n.value
         ends = np.cumsum(steps[:k])
         return boxes[:k].copy(), [best[e - s:e].copy() for e, s in zip(ends, steps[:k])]
+
+    def pages(self, pages, w: int, h: int, max_side: int = 960, db=(0.3, 0.45, 1.4, 3.0), relv: float = 0.1,
+              per_batch: int = 16, merge: int = 1, lanes: int = 1, boxes_only: bool = False):
+        """Many pages of one size (`wocr_pp_pages`): host arrays [h, w, 3] u8 or device pointers
+        (ints).  `lanes` workers on this GPU take pages in turn; each recognises `merge` of its
+        pages with one wait.  Returns [(boxes float32 [n, 6], [classes per step] per line)] per
+        page, equal to `page()` page by page.  `self.last_bytes` = (H2D, D2H) bytes."""
+        n = len(pages)
+        ptrs = (ctypes.c_void_p * max(n, 1))()
+        keep = []
+        for k, pg in enumerate(pages):
+            if isinstance(pg, (int, np.integer)):
+                ptrs[k] = int(pg)
+            else:
+                a = np.ascontiguousarray(pg, np.uint8)
+                keep.append(a)
+                ptrs[k] = a.ctypes.data
+        ws = np.full(max(n, 1), w, np.int32)
+        hs = np.full(max(n, 1), h, np.int32)
+        dbp = np.float32(db)
+        nl = np.zeros(max(n, 1), np.int32)
+        byts = np.zeros(2, np.int64)
+        box_cap = getattr(self, "_box_cap", 1024 * max(n, 1))
+        cap = getattr(self, "_cap", 1 << 18)
+        for _ in range(8):  # again only when a capacity guess was short (status 8)
+            boxes = np.zeros((box_cap, 6), np.float32)
+            best = np.empty(0 if boxes_only else cap, np.uint32)
+            steps = np.zeros(box_cap, np.int32)
+            st = L.lib().wocr_pp_pages(self.h, ptrs, L.ptr(ws), L.ptr(hs), n, int(max_side), L.ptr(dbp), relv,
+                                       int(per_batch), int(merge), int(lanes), L.ptr(boxes), box_cap, L.ptr(nl),
+                                       None if boxes_only else L.ptr(best), 0 if boxes_only else cap,
+                                       None if boxes_only else L.ptr(steps), L.ptr(byts))
+            if st == 8 and int(nl[:n].sum()) > box_cap:
+                box_cap = int(nl[:n].sum()) * 2
+                continue
+            if st == 8:
+                cap *= 4
+                continue
+            break
+        L.check(st)
+        self._box_cap, self._cap = box_cap, cap
+        self.last_bytes = (int(byts[0]), int(byts[1]))
+        del keep
+        out, b0, l0, o = [], 0, 0, 0
+        for k in range(n):
+            m = int(nl[k])
+            bx = boxes[b0:b0 + m].copy()
+            lines = []
+            if not boxes_only:
+                for i in range(m):
+                    t = int(steps[l0 + i])
+                    lines.append(best[o:o + t].copy())
+                    o += t
+            out.append((bx, lines))
+            b0 += m
+            l0 += m
+        return out
+
+    def launches(self) -> int:
+        """Kernels launched so far by every lane of this pipeline."""
+        return int(L.lib().wocr_pp_launches(self.h))
 
     def texts(self, rgb, w: int, h: int, chars: List[str], **kw) -> List[str]:
         """The page's text lines in reading order (`Dictionary::decode` of each line)."""
