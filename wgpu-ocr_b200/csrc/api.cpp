@@ -233,9 +233,18 @@ void check_status(Ctx *c) {
     }
 }
 
+void wait_stream(Ctx *c) {
+    if (c->sync_ev) {
+        WOCR_CUDA(cudaEventRecord(c->sync_ev, c->stream));
+        WOCR_CUDA(cudaEventSynchronize(c->sync_ev));
+    } else {
+        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    }
+}
+
 void sync_bounded(Ctx *c, int timeout_ms) {
     if (timeout_ms <= 0) {
-        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        wait_stream(c);
         check_status(c);
         return;
     }
@@ -277,6 +286,7 @@ static void ctx_release(wocr_ctx *ctx) {
         cudaEventDestroy(r.b);
     }
     for (auto e : c.spare) cudaEventDestroy(e);
+    if (c.sync_ev) cudaEventDestroy(c.sync_ev);
     c.recs.clear();
     c.spare.clear();
     cudaStreamSynchronize(c.stream);
@@ -315,6 +325,8 @@ int32_t wocr_ctx_create(int32_t device, int32_t lines, wocr_ctx **out) {
         uint64_t thr = UINT64_MAX;
         WOCR_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr));
         h->c.pool = pool;
+        if (!std::getenv("WOCR_SPIN_SYNC"))
+            WOCR_CUDA(cudaEventCreateWithFlags(&h->c.sync_ev, cudaEventBlockingSync | cudaEventDisableTiming));
         // the device error word of bounded waits, allocated before any graph capture
         h->c.status_buf = alloc(&h->c, 16);
         h->c.status = (int *)h->c.status_buf->p;

@@ -88,6 +88,10 @@ struct Ctx {
     // device error word written by kernels whose bounded waits gave up (0 = fine)
     int *status = nullptr;
     std::shared_ptr<struct Buf> status_buf;
+    // unbounded waits block on this event (the host thread sleeps until the stream reaches it)
+    // instead of spinning: several contexts per GPU, each with its own host thread, share the
+    // host's cores with the other GPUs' processes
+    cudaEvent_t sync_ev = nullptr;
 };
 
 // Brackets one kernel launch with events when the context profiles; records its algorithmic
@@ -147,6 +151,8 @@ struct DT {
 
 // Waits for the context stream (bounded when timeout_ms > 0) and raises the device error word.
 void sync_bounded(Ctx *c, int timeout_ms);
+// Waits for the context stream (unbounded, on the context's blocking event when it has one).
+void wait_stream(Ctx *c);
 // The context behind a C-ABI handle.
 Ctx *ctx_of(wocr_ctx *h);
 

@@ -796,7 +796,7 @@ namespace {
 int read_int(Ctx *c, const int *d) {
     int v = 0;
     WOCR_CUDA(cudaMemcpyAsync(&v, d, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
-    WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    wait_stream(c);
     return v;
 }
 }  // namespace
