@@ -51,9 +51,11 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
     p.add_argument("--workload", default="pp4",
-                   choices=["pp4", "pp4ink", "det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines", "words1"],
+                   choices=["pp4", "pp4ink", "ocrs2", "ocrs2ink", "det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines",
+                            "words1"],
                    help="pp4 (default, the driver's line): config 4, the full PP-OCRv6 page pipeline (pp4ink: "
-                        "with a hand-set ink detector, hundreds of lines a page); det1: config 1 detection; rec0 / "
+                        "with a hand-set ink detector, hundreds of lines a page); ocrs2: config 2, the full ocrs page "
+                        "pipeline (ocrs2ink: with a hand-set ink detector, 36 lines a page); det1: config 1 detection; rec0 / "
                         "pp3 / ppdet4: configs 0, 3 and 4 through their public calls; ppdb4: config 4 with the DB "
                         "mask and box scores on the device; pplines: PP line extraction; words1: word rectangles "
                         "of config 1 detection masks (secondary measurements)")
@@ -234,11 +236,48 @@ def oracle_pp_page(det_m, rec_m, page):
     return len(boxes)
 
 
+def ocrs_workload(ink: bool):
+    """Config 2's models and its description (ocrs2ink: the ink detector in place of the U-Net)."""
+    from wocr import synth
+    det_m = synth.ocrs_ink_det_model() if ink else synth.ocrs_det_model()
+    detector = ("a hand-set ink detector (darkness, 3x5 box sum, sigmoid) standing in for trained ocrs weights, "
+                "which marks words" if ink else
+                "the ocrs-style detection U-Net with random-init weights (seed 1), whose mask is noise-like, so a "
+                "page gives about one page-sized word and line")
+    desc = (f"config 2 full ocrs page: {detector}; 2550x3300 RGB u8 synthetic pages (36 text bands), grey/resize "
+            f"to 800x600, mask at 0.5, word rectangles (expand 3, min area 100), text lines (ocrs line grouping "
+            f"restated), lines padded 0.15 / 0.1 x median height, 64-row line images batched by width, ocrs-style "
+            f"recognition (conv trunk + 2-layer biGRU(256) + Linear 512->97, seed 0), arg-max per step")
+    return det_m, synth.ocrs_rec_model(), desc
+
+
+def oracle_ocrs_page(det_m, rec_m, page):
+    """One page of config 2 through the CPU oracle: detection, word rectangles, lines, line
+    images, recognition.  Returns the number of lines."""
+    from oracle import ref
+    h, w = page.shape[:2]
+    bits, _, _ = ref.detect_page(det_m, page, THRESHOLD)
+    lines = ref.ocrs_page_lines(bits, w, h)
+    if lines:
+        batches, _, _ = ref.ocrs_line_batches(page, lines)
+        ref.recognize(rec_m, batches)
+    return len(lines)
+
+
+def page_workload(name: str):
+    """(models, description, oracle page function) of a full-page workload."""
+    if name in ("pp4", "pp4ink"):
+        det_m, rec_m, desc = pp_workload(name == "pp4ink")
+        return det_m, rec_m, desc, oracle_pp_page
+    det_m, rec_m, desc = ocrs_workload(name == "ocrs2ink")
+    return det_m, rec_m, desc, oracle_ocrs_page
+
+
 def run_reference(args):
     world, rank, _ = dist()
     if rank != 0:
         return 0
-    if args.workload in ("pp4", "pp4ink"):
+    if args.workload in ("pp4", "pp4ink", "ocrs2", "ocrs2ink"):
         return run_reference_pages(args)
     from oracle import ref
     from wocr import synth
@@ -399,15 +438,15 @@ def run_reference_pages(args):
     """The reference arm on config 4: the CPU oracle, one page per step, all host threads."""
     from oracle import ref
     from wocr import synth
-    det_m, rec_m, desc = pp_workload(args.workload == "pp4ink")
+    det_m, rec_m, desc, oracle_page = page_workload(args.workload)
     pages = [synth.page(7000 + k, W_PAGE, H_PAGE) for k in range(max(args.steps, 1) + max(args.warmup, 1))]
     ref.set_threads(os.cpu_count() or 1)
     for k in range(args.warmup):
-        oracle_pp_page(det_m, rec_m, pages[k])
+        oracle_page(det_m, rec_m, pages[k])
     t0 = time.perf_counter()
     nl = 0
     for k in range(args.steps):
-        nl += oracle_pp_page(det_m, rec_m, pages[args.warmup + k])
+        nl += oracle_page(det_m, rec_m, pages[args.warmup + k])
     dt = time.perf_counter() - t0
     v = args.steps / dt
     line = {"impl": "reference", "metric": "pages/s", "value": v, "unit": "pages/s", "n_gpus": args.gpus,
@@ -424,7 +463,7 @@ def run_reference_pages(args):
 
 
 def run_pages(args):
-    """Config 4 (default): the whole PP-OCRv6 page pipeline, B pages per GPU per step."""
+    """Configs 4 (default) and 2: a whole page pipeline, B pages per GPU per step."""
     import ctypes
 
     import numpy as np
@@ -441,9 +480,10 @@ def run_pages(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     B, L, M = args.pages, max(1, args.lanes), max(1, args.merge)
-    det_m, rec_m, desc = pp_workload(args.workload == "pp4ink")
+    det_m, rec_m, desc, oracle_page = page_workload(args.workload)
+    ocrs = args.workload.startswith("ocrs")
     gpu = wocr.Gpu(lines=8, device=local)
-    pp = wocr.PPPipeline(gpu, det_m, rec_m)
+    pp = (wocr.OcrsPipeline if ocrs else wocr.PPPipeline)(gpu, det_m, rec_m)
     host_np = [synth.page(3000 + g, W_PAGE, H_PAGE) for g in shard.weak_pages_of(rank, B)]
     held = []
 
@@ -465,14 +505,20 @@ def run_pages(args):
         shard.barrier(local)
         torch.cuda.synchronize(dev)
 
-    def step(src):
-        return pp.pages(src, W_PAGE, H_PAGE, max_side=PP_MAX_SIDE, db=PP_DB, merge=M, lanes=L)
+    def step(src, lanes=L):
+        if ocrs:
+            return pp.pages(src, W_PAGE, H_PAGE, threshold=THRESHOLD, merge=M, lanes=lanes)
+        return pp.pages(src, W_PAGE, H_PAGE, max_side=PP_MAX_SIDE, db=PP_DB, merge=M, lanes=lanes)
 
     # warm-up: every lane captures its graphs for every batch shape of these pages
     for _ in range(max(args.warmup, 3)):
         res = step(d_ptrs)
-    lines_per_page = sum(len(b) for b, _ in res) / B
-    steps_per_page = sum(sum(len(x) for x in ls) for _, ls in res) / B
+    if ocrs:
+        lines_per_page = sum(len(ls) for ls in res) / B
+        steps_per_page = sum(sum(len(b) for _, _, b in ls) for ls in res) / B
+    else:
+        lines_per_page = sum(len(b) for b, _ in res) / B
+        steps_per_page = sum(sum(len(x) for x in ls) for _, ls in res) / B
     barrier()
     bus = None
     try:
@@ -514,7 +560,7 @@ def run_pages(args):
 
     # per-kernel profile of one more step on one lane (the profile records the caller's context)
     gpu.profile(True)
-    pp.pages(d_ptrs, W_PAGE, H_PAGE, max_side=PP_MAX_SIDE, db=PP_DB, merge=M, lanes=1)
+    step(d_ptrs, lanes=1)
     rep = gpu.profile_report()
     gpu.profile(False)
     total_ms = sum(r["ms"] for r in rep) or 1.0
@@ -528,10 +574,10 @@ def run_pages(args):
     if rank == 0 and world == 1:
         from oracle import ref
         ref.set_threads(os.cpu_count() or 1)
-        oracle_pp_page(det_m, rec_m, host_np[0])  # warm-up
+        oracle_page(det_m, rec_m, host_np[0])  # warm-up
         t0, k, nl = time.perf_counter(), 0, 0
         while k < 2 or (time.perf_counter() - t0 < args.cpu_seconds and k < B):
-            nl += oracle_pp_page(det_m, rec_m, host_np[k % B])
+            nl += oracle_page(det_m, rec_m, host_np[k % B])
             k += 1
         dt = time.perf_counter() - t0
         cpu = {"value": k / dt, "unit": "pages/s", "cores": ref.threads(), "kind": "port",
@@ -692,36 +738,6 @@ def run_workload(args):
         def cpu():
             ref.word_rects(masks[0], W_PAGE, H_PAGE)
             return 1, "1 page"
-    elif args.workload in ("pp4", "pp4ink"):
-        ink = args.workload == "pp4ink"
-        det_m, rec_m = (synth.pp_ink_det_model() if ink else synth.pp_det_model()), synth.pp_rec_model()
-        handle = wocr.PPPipeline(gpu, det_m, rec_m)
-        npg = 12
-        pages = [pinned(synth.page(3000 + k, W_PAGE, H_PAGE)) for k in range(npg)]
-        nlines = sum(len(handle.page(pg, W_PAGE, H_PAGE)[0]) for pg in pages)
-        detector = ("a hand-set ink detector (darkness, 3x9 box average, sigmoid) standing in for trained DB "
-                    "weights, which marks word blobs" if ink else
-                    "the PP-OCRv6-style DB detector (random-init weights mark most of the page, so a page gives "
-                    "few large boxes)")
-        units, unit, workload = npg, "pages/s", (f"config 4 full page: {detector}; {npg} 2550x3300 pages (seeds "
-                                                 f"3000..3011; 3x960x736), DB boxes at 0.3 on the device, lines "
-                                                 f"grown 0.1 x height, cut and batched 16 by width on the device, "
-                                                 f"PP recognition arg-max per batch; {nlines} lines")
-        h2d, d2h = npg * W_PAGE * H_PAGE * 3, 0
-
-        def step():
-            for pg in pages:
-                handle.page(pg, W_PAGE, H_PAGE)
-
-        def cpu():
-            x, tp = ref.det_input(pages[0], 960)
-            prob = ref.run_onnx(det_m, x)[0, 0]
-            boxes = ref.db_boxes(prob, tp, 0.3)
-            batches, _ = ref.pp_batches(pages[0], ref.pp_line_rects(boxes, 0.1))
-            for data, _, _ in batches:
-                lg = ref.run_onnx(rec_m, data, stop_before_softmax=True)
-                ref.argmax(lg.reshape(-1, lg.shape[-1]))
-            return 1, f"1 page ({len(boxes)} lines)"
     elif args.workload == "ppdb4":
         model = synth.pp_det_model()
         page = pinned(synth.page(3, W_PAGE, H_PAGE))
@@ -810,7 +826,7 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload in ("pp4", "pp4ink"):
+    if args.workload in ("pp4", "pp4ink", "ocrs2", "ocrs2ink"):
         return run_pages(args)
     if args.workload != "det1":
         return run_workload(args)

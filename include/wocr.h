@@ -334,6 +334,52 @@ int32_t wocr_word_rects(wocr_ctx *ctx, const uint32_t *mask, int32_t n, int32_t 
                         int32_t mask_on_device, float expand, float expand_x, float min_area, float *rects,
                         int64_t cap, int32_t *counts);
 
+/* ---- The ocrs page pipeline (src/bin/ocr-bench.rs:458-585 without DET / REC) --------------
+ * Text lines from word rectangles: ocrs' find_text_lines (ocrs =0.13.1, called at
+ * src/bin/ocr-bench.rs:516; not vendored, restated from its documented behaviour: words ordered
+ * by their bounding left edge, each line grown to the right by the nearest word that starts no
+ * more than 5 px left of its last word's right edge and overlaps it vertically by 5 px or more;
+ * lines by the top of their first word).  words [n][6] = [cx, cy, up_x, up_y, width, height];
+ * order[n] gets the word indices line by line (left to right), line_len[*n_lines] the words of
+ * each line.  Host only, no device work. */
+int32_t wocr_text_lines(const float *words, int32_t n, int32_t *order, int32_t *line_len, int32_t *n_lines);
+/* The line padding of src/bin/ocr-bench.rs:534-558 on one line's words (in place): relv x the
+ * median word height across the text, relend x it at the line's two ends (ocrs: 0.15, 0.1). */
+int32_t wocr_pad_line(float *words, int32_t n, float relv, float relend);
+/* ocrs line images from a device-resident RGB page (ocrs' prepare_recognition_input, run on the
+ * host by the reference's line_batches, src/bin/ocr-bench.rs:365-408): per line (words
+ * concatenated line by line, line_len words each, already padded) its polygon (the words' top
+ * edges left to right, then their bottom edges right to left), the polygon's bounding rectangle
+ * on the page, pixels outside the polygon -0.5, the others grey, resized to 64 x W
+ * (W = clamp(64 width / height, 10, 800)), batched as line_batches batches them: by W rounded up to
+ * 50, 20 lines a batch, -0.5 past each line's width.  The batches [n][1][64][width] go one after
+ * another to d_out (device, cap floats); slots[i] = the line in batch slot i, widths[i] = its W;
+ * batch_n / batch_w per batch; *n_batches and *total (floats) always set, d_out = NULL returns
+ * only the layout.  Output arrays may be NULL.  Waits for the device. */
+int32_t wocr_ocrs_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h, const float *words,
+                        const int32_t *line_len, int32_t n_lines, float *d_out, int64_t cap, int32_t *slots,
+                        int32_t *widths, int32_t *batch_n, int32_t *batch_w, int32_t *n_batches, int64_t *total);
+
+/* The whole ocrs page: Detector::detect_page (threshold), word_rects (expand 3, min area 100),
+ * text lines, padding (relv, relend), line images, Recognizer::recognize of the lines of
+ * `merge` pages at a time in one pass (MERGE, src/bin/ocr-bench.rs:162-229), arg-max per step
+ * (Rust max_by: the last index on ties).  Pages [n] of w x h RGB u8 in host or device memory,
+ * spread over `lanes` workers of the pipeline's GPU (each its own stream, detector, recogniser
+ * and host thread; lane j takes pages j, j + lanes, ...).  Per page n_lines[k]; per line, pages
+ * in order and lines in reading order: line_words (its words), widths (its image width W, for
+ * the decode's t * 4 < W rule), steps (its time steps = its batch's trunk width) and its classes
+ * concatenated in best; words [Σ line_words][6] the padded words.  Output arrays other than
+ * n_lines may be NULL; a capacity below the need fails with WOCR_ERR_CAPACITY after n_lines is
+ * filled.  bytes (nullable) = {host -> device, device -> host} bytes of the pages and classes. */
+typedef struct wocr_ocrs wocr_ocrs;
+int32_t wocr_ocrs_create(wocr_ctx *ctx, const wocr_model *det, const wocr_model *rec, wocr_ocrs **out);
+void wocr_ocrs_destroy(wocr_ocrs *p);
+int64_t wocr_ocrs_launches(wocr_ocrs *p);
+int32_t wocr_ocrs_pages(wocr_ocrs *p, const uint8_t *const *pages, int32_t n, int32_t w, int32_t h, float threshold,
+                        float relv, float relend, int32_t merge, int32_t lanes, int32_t *n_lines, int32_t *line_words,
+                        int64_t lines_cap, float *words, int64_t words_cap, int32_t *widths, int32_t *steps,
+                        uint32_t *best, int64_t cap, int64_t *bytes);
+
 /* Algorithmic work of the last run of a graph handle (detector, recogniser or N-D graph):
  * floating-point operations of its convolutions and matrix products (2 per multiply-add)
  * and the launch count. */

@@ -1018,3 +1018,249 @@ int oracle_db_boxes(const float *prob, int w, int h, const float *to_page, float
     free(lefts);
     return n;
 }
+
+/*
+ * ---- the ocrs page pipeline: text lines, line padding, line images -----------------------
+ * The reference's ocrs path (src/bin/ocr-bench.rs:458-585 without DET / REC) turns the word
+ * rectangles of a page mask (word_rects above) into text lines with ocrs' find_text_lines
+ * (src/bin/ocr-bench.rs:516), pads them (src/bin/ocr-bench.rs:534-558, RELV 0.15, RELEND 0.1)
+ * and cuts one 64-row line image per line with ocrs' prepare_recognition_input
+ * (src/bin/ocr-bench.rs:365-408), batched by width.  ocrs =0.13.1 is an un-vendored crates.io
+ * dependency, so its two functions are restated from their documented behaviour; PARITY
+ * UNPINNED for them (no test of the reference pins either).  The rules, in full:
+ *
+ * Lines (group_into_lines): words sorted by the integer part of their bounding rectangle's left
+ * edge (stable).  A line starts at the first remaining word and grows to the right: among the
+ * remaining words whose bounding left edge is at least the last word's right edge minus 5 px and
+ * whose bounding rectangles overlap the last word's vertically by at least 5 px, the one with the
+ * smallest left edge (the first in sorted order on ties) joins, until none does.  Lines are put in
+ * reading order by the top of their first word's bounding rectangle (stable).  ocrs also splits
+ * lines at column separators found from empty page regions; the single-column synthetic pages
+ * have none, and that step is not restated.
+ *
+ * Line image: the line's polygon is, word by word left to right, the two corners of each word's
+ * top edge, then, right to left, the two corners of each bottom edge, each corner truncated to
+ * integers (Rust's `as i32`).  A word's top edge is the side its most upward axis points to: of
+ * up, -up, right = (-up.y, up.x) and -right (first on ties), the one with the smallest y
+ * component.  The crop is the polygon's bounding rectangle clamped to the page (at least 1 x 1).
+ * Each crop pixel whose centre is inside the polygon (even-odd rule) takes its grey value
+ * (-0.5 + (0.299 r + 0.587 g + 0.114 b) / 255, the ocrs input normalisation the detector's grey
+ * conversion also follows, src/gpu.rs:537-542); the others are BLACK (-0.5).  The crop is resized
+ * to 64 x W, W = (int) clamp(64 cw / ch, 10, 800), by half-pixel bilinear interpolation with the
+ * detector's resize arithmetic (src/gpu.rs:543-560).
+ *
+ * Batches (line_batches, src/bin/ocr-bench.rs:365-408): lines grouped by W rounded up to a
+ * multiple of 50 (ascending), 20 lines a batch in line order, padded with BLACK.
+ */
+
+static void rr_corner(const float *r, int sa, int sb, float *x, float *y) {
+    const float hw = r[4] / 2.0f, hh = r[5] / 2.0f;
+    *x = r[0] + (float)sa * hh * r[2] + (float)sb * hw * -r[3];
+    *y = r[1] + (float)sa * hh * r[3] + (float)sb * hw * r[2];
+}
+
+/* The bounding rectangle of a rotated rect [cx, cy, up_x, up_y, width, height]. */
+static void rr_bounds(const float *r, float *l, float *t, float *rt, float *b) {
+    *l = INFINITY, *t = INFINITY, *rt = -INFINITY, *b = -INFINITY;
+    for (int sa = -1; sa <= 1; sa += 2)
+        for (int sb = -1; sb <= 1; sb += 2) {
+            float x, y;
+            rr_corner(r, sa, sb, &x, &y);
+            *l = x < *l ? x : *l;
+            *rt = x > *rt ? x : *rt;
+            *t = y < *t ? y : *t;
+            *b = y > *b ? y : *b;
+        }
+}
+
+int oracle_text_lines(const float *words, int n, int *order, int *line_len) {
+    int *idx = (int *)malloc(sizeof(int) * (size_t)(n > 0 ? n : 1));
+    int *key = (int *)malloc(sizeof(int) * (size_t)(n > 0 ? n : 1));
+    float *bl = (float *)malloc(sizeof(float) * 4 * (size_t)(n > 0 ? n : 1));
+    char *used = (char *)calloc((size_t)(n > 0 ? n : 1), 1);
+    for (int i = 0; i < n; i++) {
+        float *q = bl + 4 * (size_t)i;
+        rr_bounds(words + 6 * (size_t)i, &q[0], &q[1], &q[2], &q[3]);
+        key[i] = (int)q[0];
+        idx[i] = i;
+    }
+    for (int i = 1; i < n; i++)  /* stable insertion sort by the truncated left edge */
+        for (int j = i; j > 0 && key[idx[j]] < key[idx[j - 1]]; j--) {
+            int u = idx[j];
+            idx[j] = idx[j - 1];
+            idx[j - 1] = u;
+        }
+    int nl = 0, o = 0;
+    int *first = (int *)malloc(sizeof(int) * (size_t)(n > 0 ? n : 1));
+    int *tmp = (int *)malloc(sizeof(int) * (size_t)(n > 0 ? n : 1));
+    for (int s = 0; s < n; s++) {
+        if (used[idx[s]]) continue;
+        int last = idx[s], start = o, len = 1;
+        used[last] = 1;
+        tmp[o++] = last;
+        for (;;) {
+            const float *lb = bl + 4 * (size_t)last;
+            int best = -1;
+            for (int q = 0; q < n; q++) {
+                const int c = idx[q];
+                if (used[c]) continue;
+                const float *cb = bl + 4 * (size_t)c;
+                const float ov = (lb[3] < cb[3] ? lb[3] : cb[3]) - (lb[1] > cb[1] ? lb[1] : cb[1]);
+                if (cb[0] >= lb[2] - 5.0f && ov >= 5.0f && (best < 0 || cb[0] < bl[4 * (size_t)best]))
+                    best = c;
+            }
+            if (best < 0) break;
+            used[best] = 1;
+            tmp[o++] = best;
+            last = best;
+            len++;
+        }
+        first[nl] = start;
+        line_len[nl] = len;
+        nl++;
+    }
+    /* reading order: stable by the top of the first word's bounding rectangle */
+    int *lo = (int *)malloc(sizeof(int) * (size_t)(nl > 0 ? nl : 1));
+    for (int i = 0; i < nl; i++) lo[i] = i;
+    for (int i = 1; i < nl; i++)
+        for (int j = i; j > 0 && bl[4 * (size_t)tmp[first[lo[j]]] + 1] < bl[4 * (size_t)tmp[first[lo[j - 1]]] + 1];
+             j--) {
+            int u = lo[j];
+            lo[j] = lo[j - 1];
+            lo[j - 1] = u;
+        }
+    int *lens = (int *)malloc(sizeof(int) * (size_t)(nl > 0 ? nl : 1));
+    memcpy(lens, line_len, sizeof(int) * (size_t)nl);
+    o = 0;
+    for (int i = 0; i < nl; i++) {
+        line_len[i] = lens[lo[i]];
+        for (int k = 0; k < lens[lo[i]]; k++) order[o++] = tmp[first[lo[i]] + k];
+    }
+    free(idx), free(key), free(bl), free(used), free(first), free(tmp), free(lo), free(lens);
+    return nl;
+}
+
+/* Line padding of src/bin/ocr-bench.rs:534-558 on words[nw] of one line, in place: every word
+ * relv x the line's median word height taller on both sides, the first and last relend x it
+ * longer at their ends (height and width swap for a word whose up axis is nearer horizontal). */
+void oracle_pad_line(float *words, int nw, float relv, float relend) {
+    if (nw <= 0) return;
+    float *hs = (float *)malloc(sizeof(float) * (size_t)nw);
+    for (int i = 0; i < nw; i++) {
+        const float *r = words + 6 * (size_t)i;
+        hs[i] = fabsf(r[3]) >= fabsf(r[2]) ? r[5] : r[4];
+    }
+    for (int i = 1; i < nw; i++)
+        for (int j = i; j > 0 && hs[j] < hs[j - 1]; j--) {
+            float u = hs[j];
+            hs[j] = hs[j - 1];
+            hs[j - 1] = u;
+        }
+    const float med = hs[nw / 2];
+    free(hs);
+    for (int i = 0; i < nw; i++) {
+        float *r = words + 6 * (size_t)i;
+        const float along = (i == 0 || i + 1 == nw) ? relend * med : 0.0f, across = relv * med;
+        if (fabsf(r[3]) >= fabsf(r[2])) {
+            r[4] = r[4] + 2.0f * along;
+            r[5] = r[5] + 2.0f * across;
+        } else {
+            r[4] = r[4] + 2.0f * across;
+            r[5] = r[5] + 2.0f * along;
+        }
+    }
+}
+
+/* The integer polygon of a line (4 nw vertices, x then y). */
+static void line_polygon(const float *words, int nw, int *px, int *py) {
+    for (int i = 0; i < nw; i++) {
+        const float *r = words + 6 * (size_t)i;
+        const float hw = r[4] / 2.0f, hh = r[5] / 2.0f;
+        /* candidates: up, -up, right = (-up.y, up.x), -right */
+        const float cand[4][3] = {{r[2], r[3], hh}, {-r[2], -r[3], hh}, {-r[3], r[2], hw}, {r[3], -r[2], hw}};
+        int k = 0;
+        for (int q = 1; q < 4; q++)
+            if (cand[q][1] < cand[k][1]) k = q;
+        const float ux = cand[k][0], uy = cand[k][1], eu = cand[k][2], er = (k < 2) ? hw : hh;
+        const float rx = -uy, ry = ux;
+        const float tx = r[0] + eu * ux, ty = r[1] + eu * uy, bx = r[0] - eu * ux, by = r[1] - eu * uy;
+        /* upper chain left to right: top-left, top-right */
+        px[2 * i] = (int)(tx - er * rx);
+        py[2 * i] = (int)(ty - er * ry);
+        px[2 * i + 1] = (int)(tx + er * rx);
+        py[2 * i + 1] = (int)(ty + er * ry);
+        /* lower chain right to left: bottom-right, bottom-left */
+        const int j = 4 * nw - 2 - 2 * i;
+        px[j] = (int)(bx + er * rx);
+        py[j] = (int)(by + er * ry);
+        px[j + 1] = (int)(bx - er * rx);
+        py[j + 1] = (int)(by - er * ry);
+    }
+}
+
+static int poly_inside(const int *px, const int *py, int nv, float cx, float cy) {
+    int in = 0;
+    for (int k = 0, j = nv - 1; k < nv; j = k++) {
+        const float yk = (float)py[k], yj = (float)py[j];
+        if ((yk > cy) != (yj > cy)) {
+            const float xc = (float)px[k] + (cy - yk) * (float)(px[j] - px[k]) / (yj - yk);
+            if (cx < xc) in = !in;
+        }
+    }
+    return in;
+}
+
+/* The 64-row image of one line (words[nw], padded); returns its width W and, with out, writes
+ * [64][W]; crop (nullable) gets [left, top, width, height]. */
+int oracle_ocrs_line(const uint8_t *rgb, int w, int h, const float *words, int nw, float *out, int *crop) {
+    if (nw <= 0) return 0;
+    int *px = (int *)malloc(sizeof(int) * 4 * (size_t)nw), *py = (int *)malloc(sizeof(int) * 4 * (size_t)nw);
+    line_polygon(words, nw, px, py);
+    int mnx = px[0], mxx = px[0], mny = py[0], mxy = py[0];
+    for (int k = 1; k < 4 * nw; k++) {
+        mnx = px[k] < mnx ? px[k] : mnx;
+        mxx = px[k] > mxx ? px[k] : mxx;
+        mny = py[k] < mny ? py[k] : mny;
+        mxy = py[k] > mxy ? py[k] : mxy;
+    }
+    const int l = mnx < 0 ? 0 : (mnx > w - 1 ? w - 1 : mnx), t = mny < 0 ? 0 : (mny > h - 1 ? h - 1 : mny);
+    const int r = mxx < l + 1 ? l + 1 : (mxx > w ? w : mxx), b = mxy < t + 1 ? t + 1 : (mxy > h ? h : mxy);
+    const int cw = r - l, ch = b - t;
+    float fw = 64.0f * (float)cw / (float)ch;
+    fw = fw < 10.0f ? 10.0f : (fw > 800.0f ? 800.0f : fw);
+    const int W = (int)fw;
+    if (crop) {
+        crop[0] = l;
+        crop[1] = t;
+        crop[2] = cw;
+        crop[3] = ch;
+    }
+    if (out) {
+        const float sx = (float)cw / (float)W, sy = (float)ch / 64.0f;
+        for (int oy = 0; oy < 64; oy++) {
+            float iy = sy * ((float)oy + 0.5f) - 0.5f;
+            iy = iy < 0.f ? 0.f : (iy > (float)ch - 1.f ? (float)ch - 1.f : iy);
+            const int y1 = (int)iy, y2 = y1 + 1 < ch ? y1 + 1 : ch - 1;
+            const float wy = iy - (float)y1;
+            for (int ox = 0; ox < W; ox++) {
+                float ix = sx * ((float)ox + 0.5f) - 0.5f;
+                ix = ix < 0.f ? 0.f : (ix > (float)cw - 1.f ? (float)cw - 1.f : ix);
+                const int x1 = (int)ix, x2 = x1 + 1 < cw ? x1 + 1 : cw - 1;
+                const float wx = ix - (float)x1;
+                float v[2][2];
+                for (int a = 0; a < 2; a++)
+                    for (int c = 0; c < 2; c++) {
+                        const int gx = l + (c ? x2 : x1), gy = t + (a ? y2 : y1);
+                        v[a][c] = poly_inside(px, py, 4 * nw, (float)gx + 0.5f, (float)gy + 0.5f)
+                                      ? grey_px(rgb, w, h, gx, gy)
+                                      : -0.5f;
+                    }
+                const float top = mixf(v[0][0], v[0][1], wx), bot = mixf(v[1][0], v[1][1], wx);
+                out[(size_t)oy * W + ox] = mixf(top, bot, wy);
+            }
+        }
+    }
+    free(px);
+    free(py);
+    return W;
+}

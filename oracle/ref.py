@@ -72,13 +72,16 @@ def lib():
             "oracle_contours": [_u32, _I, _I, _i32, _I, _i32, _i32, ctypes.c_int64, ctypes.POINTER(ctypes.c_int64)],
             "oracle_word_rects": [_u32, _I, _I, _F, _F, _F, _f, _I],
             "oracle_db_boxes": [_f, _I, _I, _f, _F, _F, _F, _F, _f, _I],
+            "oracle_text_lines": [_f, _I, _i32, _i32],
+            "oracle_pad_line": [_f, _I, _F, _F],
+            "oracle_ocrs_line": [_u8, _I, _I, _f, _I, _f, _i32],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = ctypes.c_float if name in ("oracle_erf", "oracle_act", "oracle_db_score") else (
                 ctypes.c_int if name in ("oracle_threads", "oracle_pp_line", "oracle_contours", "oracle_word_rects",
-                                 "oracle_db_boxes")
+                                 "oracle_db_boxes", "oracle_text_lines", "oracle_ocrs_line")
                 else None)
         _lib = L
     return _lib
@@ -243,6 +246,70 @@ def pp_batches(rgb: np.ndarray, rects, per: int = 16):
         batches.append((data, len(part), width))
         order.extend(part)
     return batches, order
+
+
+def text_lines(words) -> List[List[int]]:
+    """ocrs' find_text_lines as restated in oracle.c (parity unpinned): the word indices of each
+    line, lines in reading order, words left to right."""
+    r = np.ascontiguousarray(np.asarray(words, np.float32).reshape(-1, 6))
+    n = len(r)
+    order = np.zeros(max(n, 1), np.int32)
+    lens = np.zeros(max(n, 1), np.int32)
+    nl = lib().oracle_text_lines(_p(r), n, _p(order, _i32), _p(lens, _i32))
+    out, o = [], 0
+    for k in range(nl):
+        out.append(order[o:o + lens[k]].tolist())
+        o += int(lens[k])
+    return out
+
+
+def pad_line(words, relv: float = 0.15, relend: float = 0.1) -> np.ndarray:
+    """The words of one line padded as src/bin/ocr-bench.rs:534-558 pads them."""
+    r = np.array(np.asarray(words, np.float32).reshape(-1, 6), np.float32, copy=True)
+    lib().oracle_pad_line(_p(r), len(r), relv, relend)
+    return r
+
+
+def ocrs_line(rgb: np.ndarray, words):
+    """The 64-row ocrs line image [64, W] of one (padded) line, and its crop [l, t, w, h]."""
+    rgb = np.ascontiguousarray(rgb, np.uint8)
+    h, w = rgb.shape[:2]
+    r = np.ascontiguousarray(np.asarray(words, np.float32).reshape(-1, 6))
+    crop = np.zeros(4, np.int32)
+    W = lib().oracle_ocrs_line(_p(rgb, _u8), w, h, _p(r), len(r), None, _p(crop, _i32))
+    out = np.empty((64, W), np.float32)
+    lib().oracle_ocrs_line(_p(rgb, _u8), w, h, _p(r), len(r), _p(out), None)
+    return out, crop
+
+
+def ocrs_page_lines(bits: np.ndarray, w: int, h: int, relv: float = 0.15, relend: float = 0.1):
+    """The host half of the ocrs page pipeline on a page mask: word rectangles (expand 3, min
+    area 100), text lines, padding.  Returns the padded words of each line (float32 [k, 6])."""
+    words = word_rects(bits, w, h)
+    return [pad_line(words[idx], relv, relend) for idx in text_lines(words)]
+
+
+def ocrs_line_batches(rgb: np.ndarray, lines, bucket: int = 50, per: int = 20):
+    """line_batches (src/bin/ocr-bench.rs:365-408): each line's image, grouped by width rounded
+    up to `bucket` (ascending), `per` lines a batch in line order, padded with -0.5.  Returns
+    (batches as (data [n, 1, 64, width], n, width), order: line of each slot, widths: each slot's
+    image width)."""
+    imgs = [ocrs_line(rgb, l)[0] for l in lines]
+    groups = {}
+    for i, im in enumerate(imgs):
+        groups.setdefault(-(-im.shape[1] // bucket) * bucket, []).append(i)
+    batches, order, widths = [], [], []
+    for width in sorted(groups):
+        mem = groups[width]
+        for k in range(0, len(mem), per):
+            part = mem[k:k + per]
+            data = np.full((len(part), 1, 64, width), -0.5, np.float32)
+            for j, i in enumerate(part):
+                data[j, 0, :, :imgs[i].shape[1]] = imgs[i]
+                order.append(i)
+                widths.append(imgs[i].shape[1])
+            batches.append((data, len(part), width))
+    return batches, order, widths
 
 
 def grey_resize(rgb: np.ndarray, oh: int = 800, ow: int = 600) -> np.ndarray:

@@ -7,6 +7,7 @@
 #include <thread>
 
 #include "exec.h"
+#include "layout.h"
 
 using namespace wocr;
 
@@ -449,23 +450,33 @@ void wocr_host_free(void *p) {
 }
 
 // ---- detector ---------------------------------------------------------------------------
+}  // extern "C"
+
+// Detector::new from a parsed model (wocr_detector_create, and the lanes of the ocrs page
+// pipeline, which rebuild their detectors from the model kept at create time).
+static wocr_detector *detector_from_model(wocr_ctx *ctx, const Model &m) {
+    WOCR_CUDA(cudaSetDevice(ctx->c.device));
+    auto *d = new wocr_detector();
+    d->ctx = ctx;
+    ctx->refs++;
+    try {
+        d->graph = build_graph(&ctx->c, m, nullptr, nullptr);
+        WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
+    } catch (...) {
+        delete d;
+        ctx_release(ctx);
+        throw;
+    }
+    return d;
+}
+
+extern "C" {
+
 int32_t wocr_detector_create(wocr_ctx *ctx, const wocr_model *model, wocr_detector **out) {
     return guard([&] {
         if (!ctx || !out) fail(WOCR_ERR_INVALID, "null argument");
         WOCR_CUDA(cudaSetDevice(ctx->c.device));
-        Model m = model_from_c(model);
-        auto *d = new wocr_detector();
-        d->ctx = ctx;
-        ctx->refs++;
-        try {
-            d->graph = build_graph(&ctx->c, m, nullptr, nullptr);
-            WOCR_CUDA(cudaStreamSynchronize(ctx->c.stream));
-        } catch (...) {
-            delete d;
-            ctx_release(ctx);
-            throw;
-        }
-        *out = d;
+        *out = detector_from_model(ctx, model_from_c(model));
     });
 }
 
@@ -739,99 +750,108 @@ int32_t wocr_detect(wocr_detector *det, const float *input, int32_t h, int32_t w
 }
 
 // ---- recogniser -------------------------------------------------------------------------
+}  // extern "C"
+
+// Recognizer::new from a parsed model (wocr_recognizer_create and the ocrs pipeline's lanes).
+static wocr_recognizer *recognizer_from_model(wocr_ctx *ctx, const Model &m, int32_t lines) {
+    Ctx *c = &ctx->c;
+    WOCR_CUDA(cudaSetDevice(c->device));
+    auto *r = new wocr_recognizer();
+    r->ctx = ctx;
+    ctx->refs++;
+    r->lines = lines > 0 ? lines : c->lines;
+    try {
+        Node pool;
+        r->trunk = build_graph(c, m, "AveragePool", &pool);
+        if (pool.op.empty()) fail(WOCR_ERR_UNSUPPORTED, "no AveragePool in the recognition model");
+        auto kv = pool.ints("kernel_shape");
+        if (!kv) fail(WOCR_ERR_UNSUPPORTED, "AveragePool without kernel_shape");
+        auto sv = pool.ints("strides");
+        if (kv->size() != 2 || (*kv)[1] != 1 || !sv || *sv != *kv)
+            fail(WOCR_ERR_UNSUPPORTED, "unsupported AveragePool " + shape_str(*kv));
+        r->pool_kh = (int)(*kv)[0];
+        int nl = 0;
+        for (auto &n : m.nodes) {
+            if (n.op != "GRU") continue;
+            if (n.int_("hidden_size").value_or(0) != 256 || n.int_("linear_before_reset").value_or(0) != 1 ||
+                n.str("direction").value_or("") != "bidirectional")
+                fail(WOCR_ERR_UNSUPPORTED, "unsupported GRU attributes");
+            if (nl >= 2) {
+                nl++;
+                continue;
+            }
+            const HostW &W = m.weight(n.in(1)), &R = m.weight(n.in(2)), &B = m.weight(n.in(3));
+            if (W.dims.size() != 3 || W.dims[0] != 2 || W.dims[1] != 768 || R.data.size() != 2 * 768 * 256 ||
+                B.data.size() != 2 * 1536)
+                fail(WOCR_ERR_SHAPE, "GRU weights " + shape_str(W.dims));
+            int input = (int)W.dims[2];
+            // W [2][768][in] as rows of the projection -> [in][1536] (src/gpu.rs:1466-1472)
+            std::vector<float> wt((size_t)input * 1536);
+            for (int row = 0; row < 1536; row++)
+                for (int i = 0; i < input; i++) wt[(size_t)i * 1536 + row] = W.data[(size_t)row * input + i];
+            std::vector<float> wb, rb;
+            for (int dir = 0; dir < 2; dir++) {
+                wb.insert(wb.end(), B.data.begin() + dir * 1536, B.data.begin() + dir * 1536 + 768);
+                rb.insert(rb.end(), B.data.begin() + dir * 1536 + 768, B.data.begin() + dir * 1536 + 1536);
+            }
+            GruLayer &L = r->layers[nl];
+            L.input = input;
+            L.w_t = upload(c, wt);
+            L.uw = linear_umma(c, wt.data(), input, 1536);
+            L.wb = upload(c, wb);
+            L.r = upload(c, R.data);
+            L.rb = upload(c, rb);
+            nl++;
+        }
+        if (nl != 2) fail(WOCR_ERR_UNSUPPORTED, std::to_string(nl) + " GRU layers");
+        const Node *mm = nullptr;
+        for (auto &n : m.nodes)
+            if (n.op == "MatMul") {
+                mm = &n;
+                break;
+            }
+        if (!mm) fail(WOCR_ERR_UNSUPPORTED, "no MatMul");
+        const HostW &lin = m.weight(mm->in(1));  // [512][classes]
+        if (lin.dims.size() != 2 || lin.dims[0] != 512) fail(WOCR_ERR_SHAPE, "output layer " + shape_str(lin.dims));
+        const Node *add = nullptr;
+        for (auto &n : m.nodes)
+            if (n.op == "Add" && std::find(n.inputs.begin(), n.inputs.end(), mm->outputs[0]) != n.inputs.end()) {
+                add = &n;
+                break;
+            }
+        if (!add) fail(WOCR_ERR_UNSUPPORTED, "no bias Add");
+        const HostW *bias = nullptr;
+        for (auto &i : add->inputs)
+            if (m.weights.count(i)) {
+                bias = &m.weights.at(i);
+                break;
+            }
+        if (!bias) fail(WOCR_ERR_UNSUPPORTED, "no bias weight");
+        r->classes = (int)lin.dims[1];
+        r->ldw = (r->classes + 3) / 4 * 4;
+        std::vector<float> lw((size_t)512 * r->ldw, 0.f), lb(r->ldw, 0.f);
+        for (int i = 0; i < 512; i++)
+            for (int q = 0; q < r->classes; q++) lw[(size_t)i * r->ldw + q] = lin.data[(size_t)i * r->classes + q];
+        for (int q = 0; q < r->classes && q < (int)bias->data.size(); q++) lb[q] = bias->data[q];
+        r->lin_w = upload(c, lw);
+        r->lin_uw = linear_umma(c, lin.data.data(), 512, r->classes);
+        r->lin_b = upload(c, lb);
+        WOCR_CUDA(cudaStreamSynchronize(c->stream));
+    } catch (...) {
+        delete r;
+        ctx_release(ctx);
+        throw;
+    }
+    return r;
+}
+
+extern "C" {
+
 int32_t wocr_recognizer_create(wocr_ctx *ctx, const wocr_model *model, int32_t lines, wocr_recognizer **out) {
     return guard([&] {
         if (!ctx || !out) fail(WOCR_ERR_INVALID, "null argument");
-        Ctx *c = &ctx->c;
-        WOCR_CUDA(cudaSetDevice(c->device));
-        Model m = model_from_c(model);
-        auto *r = new wocr_recognizer();
-        r->ctx = ctx;
-        ctx->refs++;
-        r->lines = lines > 0 ? lines : c->lines;
-        try {
-            Node pool;
-            r->trunk = build_graph(c, m, "AveragePool", &pool);
-            if (pool.op.empty()) fail(WOCR_ERR_UNSUPPORTED, "no AveragePool in the recognition model");
-            auto kv = pool.ints("kernel_shape");
-            if (!kv) fail(WOCR_ERR_UNSUPPORTED, "AveragePool without kernel_shape");
-            auto sv = pool.ints("strides");
-            if (kv->size() != 2 || (*kv)[1] != 1 || !sv || *sv != *kv)
-                fail(WOCR_ERR_UNSUPPORTED, "unsupported AveragePool " + shape_str(*kv));
-            r->pool_kh = (int)(*kv)[0];
-            int nl = 0;
-            for (auto &n : m.nodes) {
-                if (n.op != "GRU") continue;
-                if (n.int_("hidden_size").value_or(0) != 256 || n.int_("linear_before_reset").value_or(0) != 1 ||
-                    n.str("direction").value_or("") != "bidirectional")
-                    fail(WOCR_ERR_UNSUPPORTED, "unsupported GRU attributes");
-                if (nl >= 2) {
-                    nl++;
-                    continue;
-                }
-                const HostW &W = m.weight(n.in(1)), &R = m.weight(n.in(2)), &B = m.weight(n.in(3));
-                if (W.dims.size() != 3 || W.dims[0] != 2 || W.dims[1] != 768 || R.data.size() != 2 * 768 * 256 ||
-                    B.data.size() != 2 * 1536)
-                    fail(WOCR_ERR_SHAPE, "GRU weights " + shape_str(W.dims));
-                int input = (int)W.dims[2];
-                // W [2][768][in] as rows of the projection -> [in][1536] (src/gpu.rs:1466-1472)
-                std::vector<float> wt((size_t)input * 1536);
-                for (int row = 0; row < 1536; row++)
-                    for (int i = 0; i < input; i++) wt[(size_t)i * 1536 + row] = W.data[(size_t)row * input + i];
-                std::vector<float> wb, rb;
-                for (int dir = 0; dir < 2; dir++) {
-                    wb.insert(wb.end(), B.data.begin() + dir * 1536, B.data.begin() + dir * 1536 + 768);
-                    rb.insert(rb.end(), B.data.begin() + dir * 1536 + 768, B.data.begin() + dir * 1536 + 1536);
-                }
-                GruLayer &L = r->layers[nl];
-                L.input = input;
-                L.w_t = upload(c, wt);
-                L.uw = linear_umma(c, wt.data(), input, 1536);
-                L.wb = upload(c, wb);
-                L.r = upload(c, R.data);
-                L.rb = upload(c, rb);
-                nl++;
-            }
-            if (nl != 2) fail(WOCR_ERR_UNSUPPORTED, std::to_string(nl) + " GRU layers");
-            const Node *mm = nullptr;
-            for (auto &n : m.nodes)
-                if (n.op == "MatMul") {
-                    mm = &n;
-                    break;
-                }
-            if (!mm) fail(WOCR_ERR_UNSUPPORTED, "no MatMul");
-            const HostW &lin = m.weight(mm->in(1));  // [512][classes]
-            if (lin.dims.size() != 2 || lin.dims[0] != 512) fail(WOCR_ERR_SHAPE, "output layer " + shape_str(lin.dims));
-            const Node *add = nullptr;
-            for (auto &n : m.nodes)
-                if (n.op == "Add" && std::find(n.inputs.begin(), n.inputs.end(), mm->outputs[0]) != n.inputs.end()) {
-                    add = &n;
-                    break;
-                }
-            if (!add) fail(WOCR_ERR_UNSUPPORTED, "no bias Add");
-            const HostW *bias = nullptr;
-            for (auto &i : add->inputs)
-                if (m.weights.count(i)) {
-                    bias = &m.weights.at(i);
-                    break;
-                }
-            if (!bias) fail(WOCR_ERR_UNSUPPORTED, "no bias weight");
-            r->classes = (int)lin.dims[1];
-            r->ldw = (r->classes + 3) / 4 * 4;
-            std::vector<float> lw((size_t)512 * r->ldw, 0.f), lb(r->ldw, 0.f);
-            for (int i = 0; i < 512; i++)
-                for (int q = 0; q < r->classes; q++) lw[(size_t)i * r->ldw + q] = lin.data[(size_t)i * r->classes + q];
-            for (int q = 0; q < r->classes && q < (int)bias->data.size(); q++) lb[q] = bias->data[q];
-            r->lin_w = upload(c, lw);
-            r->lin_uw = linear_umma(c, lin.data.data(), 512, r->classes);
-            r->lin_b = upload(c, lb);
-            WOCR_CUDA(cudaStreamSynchronize(c->stream));
-        } catch (...) {
-            delete r;
-            ctx_release(ctx);
-            throw;
-        }
-        *out = r;
+        WOCR_CUDA(cudaSetDevice(ctx->c.device));
+        *out = recognizer_from_model(ctx, model_from_c(model), lines);
     });
 }
 
@@ -2321,6 +2341,395 @@ int32_t wocr_pp_pages(wocr_pp *p, const uint8_t *const *pages, const int32_t *w,
                 std::copy(v.begin(), v.end(), best + o);
                 o += (int64_t)v.size();
             }
+    });
+}
+
+}  // extern "C"
+
+// ---- the ocrs page pipeline -----------------------------------------------------------------
+//
+// The reference's default page loop (src/bin/ocr-bench.rs:458-585, no DET / REC): the GPU thread
+// detects a page into its thresholded mask (Detector::detect_page); the CPU finds its words
+// (word_rects), lines (ocrs find_text_lines), pads them and cuts ocrs line images
+// (line_batches); the GPU thread recognises the batches of MERGE pages in one
+// Recognizer::recognize call; the CPU decodes.  Here the mask, the words and the line images stay
+// on the device (wocr_detect_pages' kernels, wocr_word_rects' kernels, k_ocrs_lines); only the
+// word rectangles come to the host for the line grouping (layout.cpp) and only the arg-max
+// classes for the decode.  As in the PP pipeline, a pipeline owns `lanes` workers on one GPU,
+// each its own context, detector, recogniser and host thread; a lane detects `merge` of its pages
+// in one batched pass and recognises all their lines in one recogniser pass.
+
+namespace {
+
+// Batches of one page's lines as line_batches forms them: grouped by image width rounded up to
+// 50 (ascending), 20 lines a batch in line order.  Fills slots (line index per slot), and the
+// batches' line counts and widths.
+void ocrs_batching(const std::vector<LineCut> &cuts, std::vector<int> &slots, std::vector<int> &bn,
+                   std::vector<int> &bw) {
+    std::map<int, std::vector<int>> groups;
+    for (int i = 0; i < (int)cuts.size(); i++)
+        groups[(cuts[i].W + kLineBucket - 1) / kLineBucket * kLineBucket].push_back(i);
+    for (auto &g : groups)
+        for (size_t k = 0; k < g.second.size(); k += kLinesPerBatch) {
+            const size_t e = std::min(g.second.size(), k + kLinesPerBatch);
+            bn.push_back((int)(e - k));
+            bw.push_back(g.first);
+            slots.insert(slots.end(), g.second.begin() + k, g.second.begin() + e);
+        }
+}
+
+// One page's lines: grouping and padding on the host; its crops and polygons.
+struct OcrsPageLines {
+    std::vector<float> words;     // padded, line by line
+    std::vector<int> line_len;
+    std::vector<LineCut> cuts;
+    std::vector<int> vxy;         // polygons, x y pairs
+    std::vector<int> v0;          // each line's first vertex
+};
+
+void ocrs_page_lines(const float *rects, int n, int pw, int ph, float relv, float relend, OcrsPageLines &out) {
+    std::vector<int> order;
+    text_lines(rects, n, order, out.line_len);
+    out.words.resize(order.size() * 6);
+    for (size_t i = 0; i < order.size(); i++) std::memcpy(out.words.data() + 6 * i, rects + 6 * (size_t)order[i], 24);
+    size_t w0 = 0;
+    for (int len : out.line_len) {
+        float *lw = out.words.data() + 6 * w0;
+        if (4 * len > kMaxLineVerts)
+            fail(WOCR_ERR_UNSUPPORTED, "a text line of " + std::to_string(len) + " words (at most " +
+                                           std::to_string(kMaxLineVerts / 4) + ")");
+        pad_line(lw, len, relv, relend);
+        out.v0.push_back((int)(out.vxy.size() / 2));
+        out.cuts.push_back(line_cut(lw, len, pw, ph, out.vxy));
+        w0 += (size_t)len;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t wocr_text_lines(const float *words, int32_t n, int32_t *order, int32_t *line_len, int32_t *n_lines) {
+    return guard([&] {
+        if (n < 0 || (n > 0 && (!words || !order || !line_len)) || !n_lines) fail(WOCR_ERR_INVALID, "bad argument");
+        std::vector<int> o, l;
+        text_lines(words, n, o, l);
+        std::copy(o.begin(), o.end(), order);
+        std::copy(l.begin(), l.end(), line_len);
+        *n_lines = (int32_t)l.size();
+    });
+}
+
+int32_t wocr_pad_line(float *words, int32_t n, float relv, float relend) {
+    return guard([&] {
+        if (n < 0 || (n > 0 && !words)) fail(WOCR_ERR_INVALID, "bad argument");
+        pad_line(words, n, relv, relend);
+    });
+}
+
+int32_t wocr_ocrs_lines(wocr_ctx *ctx, const uint8_t *d_rgb, int32_t w, int32_t h, const float *words,
+                        const int32_t *line_len, int32_t n_lines, float *d_out, int64_t cap, int32_t *slots,
+                        int32_t *widths, int32_t *batch_n, int32_t *batch_w, int32_t *n_batches, int64_t *total) {
+    return guard([&] {
+        if (!ctx || n_lines < 0 || (n_lines > 0 && (!words || !line_len)) || w <= 0 || h <= 0)
+            fail(WOCR_ERR_INVALID, "bad argument");
+        Ctx *c = &ctx->c;
+        WOCR_CUDA(cudaSetDevice(c->device));
+        std::vector<LineCut> cuts;
+        std::vector<int> vxy, v0;
+        size_t w0 = 0;
+        for (int i = 0; i < n_lines; i++) {
+            if (line_len[i] <= 0 || 4 * line_len[i] > kMaxLineVerts)
+                fail(WOCR_ERR_INVALID, "line " + std::to_string(i) + " has " + std::to_string(line_len[i]) + " words");
+            v0.push_back((int)(vxy.size() / 2));
+            cuts.push_back(line_cut(words + 6 * w0, line_len[i], w, h, vxy));
+            w0 += (size_t)line_len[i];
+        }
+        std::vector<int> sl, bn, bw;
+        ocrs_batching(cuts, sl, bn, bw);
+        int64_t off = 0;
+        std::vector<k::OcrsLine> plan;
+        size_t q = 0;
+        for (size_t b = 0; b < bn.size(); b++) {
+            for (int j = 0; j < bn[b]; j++, q++) {
+                const int i = sl[q];
+                const LineCut &lc = cuts[i];
+                plan.push_back({d_rgb, w, h, lc.l, lc.t, lc.cw, lc.ch, lc.W, bw[b], v0[i],
+                                4 * line_len[i], off + (int64_t)j * 64 * bw[b]});
+                if (slots) slots[q] = i;
+                if (widths) widths[q] = lc.W;
+            }
+            if (batch_n) batch_n[b] = bn[b];
+            if (batch_w) batch_w[b] = bw[b];
+            off += (int64_t)bn[b] * 64 * bw[b];
+        }
+        if (n_batches) *n_batches = (int32_t)bn.size();
+        if (total) *total = off;
+        if (!d_out || n_lines == 0) return;
+        if (!d_rgb) fail(WOCR_ERR_INVALID, "null page");
+        if (cap < off) fail(WOCR_ERR_CAPACITY, "line batches need " + std::to_string(off) + " floats");
+        double bytes = 0;
+        for (const auto &L : plan) bytes += 3.0 * L.cw * L.ch + 4.0 * 64 * L.bw;
+        BufP dl = alloc(c, plan.size() * sizeof(k::OcrsLine)), dv = alloc(c, std::max<size_t>(vxy.size(), 2) * 4);
+        WOCR_CUDA(cudaMemcpyAsync(dl->p, plan.data(), plan.size() * sizeof(k::OcrsLine), cudaMemcpyHostToDevice,
+                                  c->stream));
+        WOCR_CUDA(cudaMemcpyAsync(dv->p, vxy.data(), vxy.size() * 4, cudaMemcpyHostToDevice, c->stream));
+        k::ocrs_lines(c, (const k::OcrsLine *)dl->p, (int)plan.size(), (const int2 *)dv->p, d_out, bytes);
+        sync_bounded(c, 0);  // the plan's host copies are read until the uploads complete
+    });
+}
+
+}  // extern "C"
+
+struct OcrsLane {
+    wocr_ctx *ctx = nullptr;
+    wocr_detector *det = nullptr;
+    wocr_recognizer *rec = nullptr;
+    BufP pages, masks;  // a chunk of pages back to back, their masks
+    size_t pages_bytes = 0, masks_bytes = 0;
+    ~OcrsLane() {
+        if (det) wocr_detector_destroy(det);
+        if (rec) wocr_recognizer_destroy(rec);
+        if (ctx) wocr_ctx_destroy(ctx);
+    }
+};
+
+struct wocr_ocrs {
+    wocr_ctx *ctx = nullptr;
+    Model det_m, rec_m;
+    std::vector<std::unique_ptr<OcrsLane>> lanes;
+};
+
+namespace {
+
+// One page's results: the padded words of its lines, each line's image width and arg-max classes.
+struct OcrsPage {
+    OcrsPageLines lines;
+    std::vector<int> widths;                 // per line
+    std::vector<std::vector<uint32_t>> best;  // per line, its steps t < len
+    int64_t h2d = 0, d2h = 0;
+};
+
+struct OcrsArgs {
+    int w, h;
+    float thr, relv, relend;
+};
+
+OcrsLane *ocrs_lane(wocr_ocrs *p, int i) {
+    while ((int)p->lanes.size() <= i) {
+        auto ln = std::make_unique<OcrsLane>();
+        if (p->lanes.empty()) {
+            ln->ctx = p->ctx;
+            p->ctx->refs++;
+        } else {
+            check_st(wocr_ctx_create(p->ctx->c.device, p->ctx->c.lines, &ln->ctx));
+        }
+        ln->det = detector_from_model(ln->ctx, p->det_m);
+        ln->rec = recognizer_from_model(ln->ctx, p->rec_m, ln->ctx->c.lines);
+        p->lanes.push_back(std::move(ln));
+    }
+    return p->lanes[i].get();
+}
+
+// A chunk of pages on one lane: batched detection, word rectangles, lines (host), line images,
+// one recognition pass, classes back.
+void ocrs_chunk(OcrsLane &ln, const uint8_t *const *pages, const std::vector<int> &ks, const OcrsArgs &a,
+                std::vector<OcrsPage> &out) {
+    Ctx *c = &ln.ctx->c;
+    WOCR_CUDA(cudaSetDevice(c->device));
+    const int n = (int)ks.size(), words = (a.w + 31) / 32;
+    const size_t page_bytes = (size_t)a.w * a.h * 3, mask_bytes = (size_t)words * a.h * 4;
+    if (ln.pages_bytes < page_bytes * n) {
+        ln.pages = alloc(c, page_bytes * n);
+        ln.pages_bytes = page_bytes * n;
+    }
+    if (ln.masks_bytes < mask_bytes * n) {
+        ln.masks = alloc(c, mask_bytes * n);
+        ln.masks_bytes = mask_bytes * n;
+    }
+    uint8_t *dp = (uint8_t *)ln.pages->p;
+    for (int q = 0; q < n; q++) {
+        const uint8_t *src = pages[ks[q]];
+        const bool dev = on_device(src);
+        WOCR_CUDA(cudaMemcpyAsync(dp + page_bytes * q, src, page_bytes,
+                                  dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, c->stream));
+        if (!dev) out[ks[q]].h2d += (int64_t)page_bytes;
+    }
+    uint32_t *dm = (uint32_t *)ln.masks->p;
+    detect_pages_run(ln.det, dp, n, a.w, a.h, a.thr, dm);
+    // words: ocrs' word rectangles (expand 3, min area 100, src/bin/ocr-bench.rs:38-60)
+    k::WordRects wr = k::word_rects(c, dm, n, a.w, a.h, 3.0f, 0.0f, 100.0f);
+    std::vector<int32_t> counts((size_t)n);
+    std::vector<float> rects((size_t)wr.n * 6);
+    d2h(c, counts.data(), wr.page_count->p, (size_t)n * 4);
+    d2h(c, rects.data(), wr.rects->p, rects.size() * 4);
+    sync_bounded(c, 0);
+    // lines, padding and crops on the host; every page's batches after the previous page's
+    std::vector<k::OcrsLine> plan;
+    std::vector<int> vxy;
+    struct Batch {
+        int page, n, w;
+        int64_t off;
+    };
+    std::vector<Batch> batches;
+    std::vector<std::pair<int, int>> slot_line;  // (page, line) of each batch slot, in order
+    int64_t off = 0;
+    size_t r0 = 0;
+    for (int q = 0; q < n; q++) {
+        OcrsPage &pg = out[ks[q]];
+        ocrs_page_lines(rects.data() + 6 * r0, counts[q], a.w, a.h, a.relv, a.relend, pg.lines);
+        r0 += (size_t)counts[q];
+        std::vector<int> sl, bn, bw;
+        ocrs_batching(pg.lines.cuts, sl, bn, bw);
+        pg.widths.assign(pg.lines.cuts.size(), 0);
+        size_t s = 0;
+        const int vbase = (int)(vxy.size() / 2);
+        vxy.insert(vxy.end(), pg.lines.vxy.begin(), pg.lines.vxy.end());
+        for (size_t b = 0; b < bn.size(); b++) {
+            batches.push_back({ks[q], bn[b], bw[b], off});
+            for (int j = 0; j < bn[b]; j++, s++) {
+                const int i = sl[s];
+                const LineCut &lc = pg.lines.cuts[i];
+                plan.push_back({dp + page_bytes * q, a.w, a.h, lc.l, lc.t, lc.cw, lc.ch, lc.W, bw[b],
+                                vbase + pg.lines.v0[i], 4 * pg.lines.line_len[i], off + (int64_t)j * 64 * bw[b]});
+                pg.widths[i] = lc.W;
+                slot_line.push_back({ks[q], i});
+            }
+            off += (int64_t)bn[b] * 64 * bw[b];
+        }
+    }
+    if (plan.empty()) return;
+    BufP lines = alloc(c, (size_t)off * 4);
+    BufP dl = alloc(c, plan.size() * sizeof(k::OcrsLine)), dv = alloc(c, std::max<size_t>(vxy.size(), 2) * 4);
+    WOCR_CUDA(cudaMemcpyAsync(dl->p, plan.data(), plan.size() * sizeof(k::OcrsLine), cudaMemcpyHostToDevice, c->stream));
+    WOCR_CUDA(cudaMemcpyAsync(dv->p, vxy.data(), vxy.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    double bytes = 0;
+    for (const auto &L : plan) bytes += 3.0 * L.cw * L.ch + 4.0 * 64 * L.bw;
+    k::ocrs_lines(c, (const k::OcrsLine *)dl->p, (int)plan.size(), (const int2 *)dv->p, (float *)lines->p, bytes);
+    // every batch of the chunk in one recogniser pass (the reference's merged recognize)
+    std::vector<DT> xs;
+    for (const Batch &b : batches) {
+        DT x;
+        x.buf = lines;
+        x.p = (float *)lines->p + b.off;
+        x.shape = {b.n, 1, 64, b.w};
+        x.strides = rowmajor_strides(x.shape);
+        xs.push_back(x);
+    }
+    RecResult rr = recognize_dev(ln.rec, xs, nullptr, true, nullptr);
+    std::vector<uint32_t> best((size_t)rr.tmax * rr.ntot);
+    d2h(c, best.data(), rr.best->p, best.size() * 4);
+    sync_bounded(c, 0);
+    for (int line = 0; line < rr.ntot; line++) {
+        OcrsPage &pg = out[slot_line[line].first];
+        if (pg.best.empty()) pg.best.assign(pg.lines.cuts.size(), {});
+        std::vector<uint32_t> &dst = pg.best[slot_line[line].second];
+        const int len = rr.lens[line];
+        dst.resize((size_t)len);
+        for (int t = 0; t < len; t++) dst[t] = best[(size_t)t * rr.ntot + line];
+        pg.d2h += (int64_t)len * 4;
+    }
+}
+
+void ocrs_run(wocr_ocrs *p, const uint8_t *const *pages, int n, const OcrsArgs &a, int merge, int lanes,
+              std::vector<OcrsPage> &out) {
+    lanes = std::max(1, std::min(lanes, n));
+    merge = std::max(1, merge);
+    for (int i = 0; i < lanes; i++) ocrs_lane(p, i);
+    out.assign((size_t)n, OcrsPage{});
+    std::vector<std::exception_ptr> errs((size_t)lanes);
+    auto work = [&](int L) {
+        try {
+            std::vector<int> ks;
+            for (int k = L; k < n; k += lanes) {
+                ks.push_back(k);
+                if ((int)ks.size() >= merge || k + lanes >= n) {
+                    ocrs_chunk(*p->lanes[L], pages, ks, a, out);
+                    ks.clear();
+                }
+            }
+        } catch (...) {
+            errs[L] = std::current_exception();
+        }
+    };
+    std::vector<std::thread> th;
+    for (int L = 1; L < lanes; L++) th.emplace_back(work, L);
+    work(0);
+    for (auto &t : th) t.join();
+    for (auto &e : errs)
+        if (e) std::rethrow_exception(e);
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t wocr_ocrs_create(wocr_ctx *ctx, const wocr_model *det, const wocr_model *rec, wocr_ocrs **out) {
+    return guard([&] {
+        if (!ctx || !det || !rec || !out) fail(WOCR_ERR_INVALID, "null argument");
+        auto p = std::make_unique<wocr_ocrs>();
+        p->ctx = ctx;
+        p->det_m = model_from_c(det);
+        p->rec_m = model_from_c(rec);
+        ocrs_lane(p.get(), 0);
+        *out = p.release();
+    });
+}
+
+void wocr_ocrs_destroy(wocr_ocrs *p) { delete p; }
+
+int64_t wocr_ocrs_launches(wocr_ocrs *p) {
+    if (!p) return -1;
+    int64_t n = 0;
+    for (const auto &ln : p->lanes) n += ln->ctx->c.launches;
+    return n;
+}
+
+int32_t wocr_ocrs_pages(wocr_ocrs *p, const uint8_t *const *pages, int32_t n, int32_t w, int32_t h, float threshold,
+                        float relv, float relend, int32_t merge, int32_t lanes, int32_t *n_lines, int32_t *line_words,
+                        int64_t lines_cap, float *words, int64_t words_cap, int32_t *widths, int32_t *steps,
+                        uint32_t *best, int64_t cap, int64_t *bytes) {
+    return guard([&] {
+        if (!p || !pages || !n_lines || n < 0 || lines_cap < 0 || words_cap < 0 || cap < 0)
+            fail(WOCR_ERR_INVALID, "bad argument");
+        if (w <= 0 || h <= 0 || merge <= 0 || lanes <= 0 || lanes > 64)
+            fail(WOCR_ERR_INVALID, "bad page size, merge or lane count");
+        for (int k = 0; k < n; k++)
+            if (!pages[k]) fail(WOCR_ERR_INVALID, "null page " + std::to_string(k));
+        std::vector<OcrsPage> out;
+        ocrs_run(p, pages, n, OcrsArgs{w, h, threshold, relv, relend}, merge, lanes, out);
+        int64_t nl = 0, nw = 0, need = 0, h2d = 0, d2h_ = 0;
+        for (int k = 0; k < n; k++) {
+            n_lines[k] = (int32_t)out[k].lines.line_len.size();
+            nl += n_lines[k];
+            nw += (int64_t)out[k].lines.words.size() / 6;
+            for (const auto &v : out[k].best) need += (int64_t)v.size();
+            h2d += out[k].h2d;
+            d2h_ += out[k].d2h;
+        }
+        if (bytes) {
+            bytes[0] = h2d;
+            bytes[1] = d2h_;
+        }
+        if (lines_cap < nl || words_cap < nw || cap < need)
+            fail(WOCR_ERR_CAPACITY, "outputs hold " + std::to_string(lines_cap) + " lines, " + std::to_string(words_cap) +
+                                        " words, " + std::to_string(cap) + " classes; the pages need " +
+                                        std::to_string(nl) + ", " + std::to_string(nw) + ", " + std::to_string(need));
+        int64_t li = 0, wi = 0, o = 0;
+        for (int k = 0; k < n; k++) {
+            const OcrsPage &pg = out[k];
+            for (size_t i = 0; i < pg.lines.line_len.size(); i++, li++) {
+                if (line_words) line_words[li] = pg.lines.line_len[i];
+                if (widths) widths[li] = pg.widths[i];
+                const size_t t = i < pg.best.size() ? pg.best[i].size() : 0;
+                if (steps) steps[li] = (int32_t)t;
+                if (best && t) std::copy(pg.best[i].begin(), pg.best[i].end(), best + o);
+                o += (int64_t)t;
+            }
+            if (words && !pg.lines.words.empty())
+                std::memcpy(words + 6 * wi, pg.lines.words.data(), pg.lines.words.size() * 4);
+            wi += (int64_t)pg.lines.words.size() / 6;
+        }
     });
 }
 

@@ -177,6 +177,21 @@ void pp_lines(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int
 constexpr int kPpTallRows = 8 * 48;
 void pp_lines_tall(Ctx *c, const uint8_t *rgb, int w, int h, const PpLine *lines, int n, int max_cw, int max_width,
                    const int64_t *tmp_off, float *tmp, float *out, double bytes);
+// One ocrs recognition line (k_ocrs.cu): its page (device RGB, pw x ph), the crop (left, top,
+// cw x ch) of its polygon (nv vertices from v0 in the vertex array, x, y pairs), its image width
+// W, the batch width bw (>= W, BLACK past W) and the float offset of its [64][bw] block.
+struct OcrsLine {
+    const uint8_t *page;
+    int pw, ph;
+    int l, t, cw, ch;
+    int W, bw;
+    int v0, nv;
+    int64_t off;
+};
+// The 64-row line images of n lines: polygon mask, grey, half-pixel bilinear resize to 64 x W.
+// bytes: the algorithmic bytes (crops read, images written), for the profile.
+void ocrs_lines(Ctx *c, const OcrsLine *lines, int n, const int2 *verts, float *out, double bytes);
+
 // The same on compacted pages: per page 2 oh rows of w * 3 bytes (the top and bottom source rows
 // of each output row), rows[oy] = {vertical weight (float bits), bit 0/1: top/bottom is padding}.
 void grey_resize_rows(Ctx *c, const uint8_t *cmp, const int2 *rows, int n, int w, int oh, int ow, float *y);

@@ -122,6 +122,15 @@ _SIGS = [
     ("wocr_wait", c_i32, [c_void_p, c_i32]),
     ("wocr_pp_pages", c_i32, [c_void_p, c_void_p, c_void_p, c_void_p, c_i32, c_i32, c_void_p, c_f32, c_i32, c_i32,
                               c_i32, c_void_p, c_i64, c_void_p, c_void_p, c_i64, c_void_p, c_void_p]),
+    ("wocr_text_lines", c_i32, [c_void_p, c_i32, c_void_p, c_void_p, P(c_i32)]),
+    ("wocr_pad_line", c_i32, [c_void_p, c_i32, c_f32, c_f32]),
+    ("wocr_ocrs_lines", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_void_p, c_void_p, c_i32, c_void_p, c_i64,
+                                c_void_p, c_void_p, c_void_p, c_void_p, P(c_i32), P(c_i64)]),
+    ("wocr_ocrs_create", c_i32, [c_void_p, P(CModel), P(CModel), P(c_void_p)]),
+    ("wocr_ocrs_destroy", None, [c_void_p]),
+    ("wocr_ocrs_launches", c_i64, [c_void_p]),
+    ("wocr_ocrs_pages", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_i32, c_f32, c_f32, c_f32, c_i32, c_i32, c_void_p,
+                                c_void_p, c_i64, c_void_p, c_i64, c_void_p, c_void_p, c_void_p, c_i64, c_void_p]),
     ("wocr_pp_lines", c_i32, [c_void_p, c_void_p, c_i32, c_i32, c_void_p, c_i32, c_i32, c_void_p, c_i64, c_void_p,
                               c_void_p, c_void_p, P(c_i32), P(c_i64)]),
 ]

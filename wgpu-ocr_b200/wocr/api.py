@@ -66,6 +66,26 @@ class Gpu:
                                       ctypes.byref(nb), ctypes.byref(tot)))
         return order[:n].tolist(), [(int(bn[i]), int(bw[i])) for i in range(nb.value)], tot.value
 
+    def ocrs_lines(self, d_rgb: int, w: int, h: int, lines, d_out: int = 0, cap: int = 0):
+        """ocrs line images cut from a device page (`wocr_ocrs_lines`): `lines` = the padded words
+        of each line (float32 [k, 6] each).  Returns (slots: the line of each batch slot, widths:
+        each slot's image width, [(n, width)] per batch, total floats); with d_out (a device float
+        buffer of `cap` floats) the batches [n, 1, 64, width] are written there one after another."""
+        ws = [np.asarray(l, np.float32).reshape(-1, 6) for l in lines]
+        words = np.ascontiguousarray(np.concatenate(ws) if ws else np.zeros((0, 6), np.float32))
+        lens = np.array([len(x) for x in ws] or [0], np.int32)
+        n = len(ws)
+        slots = np.zeros(max(n, 1), np.int32)
+        widths = np.zeros(max(n, 1), np.int32)
+        bn = np.zeros(max(n, 1), np.int32)
+        bw = np.zeros(max(n, 1), np.int32)
+        nb, tot = ctypes.c_int32(), ctypes.c_int64()
+        L.check(L.lib().wocr_ocrs_lines(self.h, ctypes.c_void_p(d_rgb or None), int(w), int(h), L.ptr(words),
+                                        L.ptr(lens), n, ctypes.c_void_p(d_out or None), int(cap), L.ptr(slots),
+                                        L.ptr(widths), L.ptr(bn), L.ptr(bw), ctypes.byref(nb), ctypes.byref(tot)))
+        return (slots[:n].tolist(), widths[:n].tolist(), [(int(bn[i]), int(bw[i])) for i in range(nb.value)],
+                tot.value)
+
     def word_rects(self, mask, w: int, h: int, expand: float = 3.0, expand_x: float = 0.0,
                    min_area: float = 100.0, d_mask: int = 0, n: int = 0):
         """word_rects (src/bin/ocr-bench.rs:38-60) of bit masks on the device (`wocr_word_rects`):
@@ -597,6 +617,110 @@ class PPPipeline:
     def close(self):
         if self.h:
             L.lib().wocr_pp_destroy(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+def text_lines(words) -> List[List[int]]:
+    """ocrs' find_text_lines as the library restates it (`wocr_text_lines`, host code): the word
+    indices of each line (left to right), lines in reading order."""
+    r = np.ascontiguousarray(np.asarray(words, np.float32).reshape(-1, 6))
+    n = len(r)
+    order = np.zeros(max(n, 1), np.int32)
+    lens = np.zeros(max(n, 1), np.int32)
+    nl = ctypes.c_int32()
+    L.check(L.lib().wocr_text_lines(L.ptr(r), n, L.ptr(order), L.ptr(lens), ctypes.byref(nl)))
+    out, o = [], 0
+    for k in range(nl.value):
+        out.append(order[o:o + lens[k]].tolist())
+        o += int(lens[k])
+    return out
+
+
+def pad_line(words, relv: float = 0.15, relend: float = 0.1) -> np.ndarray:
+    """One line's words padded as src/bin/ocr-bench.rs:534-558 pads them (`wocr_pad_line`)."""
+    r = np.array(np.asarray(words, np.float32).reshape(-1, 6), np.float32, copy=True)
+    L.check(L.lib().wocr_pad_line(L.ptr(r), len(r), relv, relend))
+    return r
+
+
+class OcrsPipeline:
+    """The ocrs page pipeline of the reference's bench (`wocr_ocrs_*`; src/bin/ocr-bench.rs:
+    458-585 without DET / REC): detection, word rectangles, text lines, padding, line images and
+    recognition, with the pages, masks and line images kept on the device."""
+
+    def __init__(self, gpu: Gpu, det_model: Model, rec_model: Model):
+        self.gpu = gpu
+        dh, rh = L.CModelHolder(det_model), L.CModelHolder(rec_model)
+        h = ctypes.c_void_p()
+        L.check(L.lib().wocr_ocrs_create(gpu.h, dh.ref(), rh.ref(), ctypes.byref(h)))
+        self.h = h
+
+    def pages(self, pages, w: int, h: int, threshold: float = 0.5, relv: float = 0.15, relend: float = 0.1,
+              merge: int = 1, lanes: int = 1):
+        """Pages of one size (host arrays [h, w, 3] u8 or device pointers).  Returns per page a
+        list of lines in reading order, each (padded words float32 [k, 6], image width W, arg-max
+        classes of its steps).  `self.last_bytes` = (H2D, D2H) bytes."""
+        n = len(pages)
+        ptrs = (ctypes.c_void_p * max(n, 1))()
+        keep = []
+        for k, pg in enumerate(pages):
+            if isinstance(pg, (int, np.integer)):
+                ptrs[k] = int(pg)
+            else:
+                a = np.ascontiguousarray(pg, np.uint8)
+                keep.append(a)
+                ptrs[k] = a.ctypes.data
+        nl = np.zeros(max(n, 1), np.int32)
+        byts = np.zeros(2, np.int64)
+        lcap = getattr(self, "_lcap", 256 * max(n, 1))
+        wcap = getattr(self, "_wcap", 2048 * max(n, 1))
+        cap = getattr(self, "_cap", 1 << 18)
+        for _ in range(8):  # again only when a capacity guess was short (status 8)
+            lw = np.zeros(lcap, np.int32)
+            widths = np.zeros(lcap, np.int32)
+            steps = np.zeros(lcap, np.int32)
+            words = np.zeros((wcap, 6), np.float32)
+            best = np.empty(cap, np.uint32)
+            st = L.lib().wocr_ocrs_pages(self.h, ptrs, n, int(w), int(h), float(threshold), relv, relend, int(merge),
+                                         int(lanes), L.ptr(nl), L.ptr(lw), lcap, L.ptr(words), wcap, L.ptr(widths),
+                                         L.ptr(steps), L.ptr(best), cap, L.ptr(byts))
+            if st == 8:
+                lcap, wcap, cap = lcap * 4, wcap * 4, cap * 4
+                continue
+            break
+        L.check(st)
+        self._lcap, self._wcap, self._cap = lcap, wcap, cap
+        self.last_bytes = (int(byts[0]), int(byts[1]))
+        del keep
+        out, li, wi, o = [], 0, 0, 0
+        for k in range(n):
+            lines = []
+            for _ in range(int(nl[k])):
+                kw, t = int(lw[li]), int(steps[li])
+                lines.append((words[wi:wi + kw].copy(), int(widths[li]), best[o:o + t].copy()))
+                wi += kw
+                o += t
+                li += 1
+            out.append(lines)
+        return out
+
+    def launches(self) -> int:
+        """Kernels launched so far by every lane of this pipeline."""
+        return int(L.lib().wocr_ocrs_launches(self.h))
+
+    def texts(self, pages, w: int, h: int, alphabet: str, **kw) -> List[List[str]]:
+        """Each page's text lines (greedy CTC of src/bin/ocr-bench.rs:62-74)."""
+        return [[ocrs_decode(b, len(b), W, alphabet) for _, W, b in lines] for lines in self.pages(pages, w, h, **kw)]
+
+    def close(self):
+        if self.h:
+            L.lib().wocr_ocrs_destroy(self.h)
             self.h = None
 
     def __enter__(self):

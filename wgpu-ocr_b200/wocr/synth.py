@@ -237,6 +237,23 @@ def ocrs_det_model(seed: int = 1) -> Model:
     return b.model("image", out)
 
 
+def ocrs_ink_det_model(gain: float = 10.0, bias: float = -1.0) -> Model:
+    """A hand-set stand-in for the trained ocrs detector, for the page pipeline's tests and its
+    secondary measurement (not the config's random-init model): darkness (a 1 x 1 conv, 0.5 - x,
+    so white and the convolution's zero padding are both 0), a 5 x 5 conv whose middle three rows
+    sum it (the outer rows zero), and a sigmoid.  On page(...), resized to 800 x 600, a glyph gap
+    (1-4 px there) stays above the 0.5 threshold and a word gap (6 px or more) falls below it, so
+    the mask marks words and a page has its 36 text lines."""
+    b = _Builder(0)
+    ins = ["image", b.w("W", -np.ones((1, 1, 1, 1))), b.w("B", np.full(1, 0.5))]
+    d = b.op("Conv", ins, {"kernel_shape": [1, 1], "pads": [0, 0, 0, 0], "strides": [1, 1], "dilations": [1, 1]})
+    wt = np.zeros((1, 1, 5, 5))
+    wt[0, 0, 1:4, :] = gain / 15.0
+    ins = [d, b.w("W", wt), b.w("B", np.full(1, bias))]
+    c = b.op("Conv", ins, {"kernel_shape": [5, 5], "pads": [2, 2, 2, 2], "strides": [1, 1], "dilations": [1, 1]})
+    return b.model("image", b.op("Sigmoid", [c]))
+
+
 # ---------------------------------------------------------------------------------------
 # config 3: PP-OCRv6-style recognition (trunk + SVTR neck + CTC head)
 # ---------------------------------------------------------------------------------------
