@@ -2,8 +2,8 @@
 
 * Detection masks: bit-exact except pixels whose oracle page-level probability lies within
   MASK_BAND of the threshold.
-* Recognition: identical arg-max class at every time step.  The whole-model tests on the
-  benchmark configurations (configs 0 and 3, every step of every line) require it outright.
+* Recognition: identical arg-max class at every time step.  The whole-model test of config 3
+  (every step of every line of its 16 batches) requires it outright.
   Elsewhere a step may be excused as a near-tie when the class the GPU chose is, in the
   oracle's own logits, within ARGMAX_TIE of the oracle's maximum, and at most max_ties(rows)
   steps may be excused; per-step softmax probabilities within PROB_TOL absolute.
@@ -17,6 +17,8 @@ times the logit).  The CTC heads here have L1 <= 1.7 (config 3's head: 1.20 to 1
 over all 23,248 steps), so 2^-15 * 1.7 = 5.2e-5.  Measured on a B200 over configs 0 and 3
 (31,657 steps): no step differs, the largest logit difference is 2.3e-5 (config 0) and the
 largest row-maximum difference 7.0e-6 (config 3), while the smallest top-2 gap is 1.9e-6.
+With the GRU's recurrent weights in fp16 (as the reference's GPU path keeps them) one step of
+config 0's 8,409 is a near-tie: the fp16 and fp32 oracles themselves disagree on it.
 """
 import numpy as np
 
@@ -62,6 +64,19 @@ def argmax_parity(best_gpu, logits_ref):
     tie_ok = (~exact) & (top - at <= ARGMAX_TIE)
     bad = (~exact) & ~tie_ok
     return int(bad.sum()), int(tie_ok.sum())
+
+
+def gru_r16(model):
+    """The model with its GRU recurrent weights rounded to fp16: the arithmetic of the reference's
+    GPU path, which converts R to f16 on devices with shader-f16 (src/gpu.rs:1478-1487) and
+    accumulates in f32, as the library does.  The fp32 model is the rten CPU reference."""
+    import copy
+
+    m = copy.deepcopy(model)
+    for n in m.nodes:
+        if n.op == "GRU":
+            m.weights[n.inputs[2]] = np.asarray(m.weights[n.inputs[2]], np.float32).astype(np.float16).astype(np.float32)
+    return m
 
 
 def softmax(x):

@@ -1,19 +1,27 @@
 // GRU recurrence (ONNX, linear_before_reset = 1, hidden 256, gate order z, r, h) for all lines
 // and both directions in one launch per layer -- the reference's K16/K17 (src/gpu.rs:680-819).
 //
-// B200 design: one thread-block cluster of 8 CTAs per (direction, group of L lines).  CTA c of
-// the cluster owns hidden units 32c .. 32c + 32 and keeps their three gate rows of R (3 x 32 x 256
-// fp32 = 96 KB, padded to 128 KB) in shared memory for the whole sequence.  Every step:
-//   1. each CTA computes its rows' dot products with h for its L lines (thread = unit x k-slice,
-//      R read as one float4 of the unit's z/r/h weights, h broadcast as float4),
-//   2. the 8 k-slices (one warp each) are summed, the gate nonlinearity gives the new h for its
-//      32 units (the step's input gates were loaded during the previous step),
-//   3. the new h is stored into every CTA's next-step buffer through distributed shared memory
-//      and `barrier.cluster` (hardware co-scheduled CTAs: no global-memory spin waits) publishes
-//      it: arrive right after the stores, wait before the next step reads h.
+// The recurrent weights are fp16, as the reference's GPU path keeps them (src/gpu.rs:1478-1487:
+// R converted to f16 when the device has shader-f16), with fp32 accumulation.
+//
+// B200 design: one thread-block cluster of 4 CTAs per (direction, group of L = 8 or 16 lines).
+// CTA c of the cluster owns hidden units 64c .. 64c + 64, i.e. 192 rows of R (64 units x 3 gates),
+// and holds them for the whole sequence in registers, as the A fragments of m16n8k16 tensor-core
+// products: warp w < 12 owns the 16 rows (gate w / 4, units 16 (w % 4) ..) over all 256 k, 16
+// fragments of 4 registers.  Every step:
+//   1. each of the 12 warps multiplies its rows with h, the B operand read from shared memory as
+//      fp16 hi and lo parts (h = hi + lo to about 2^-22, so the products are those of fp16 R with
+//      the fp32 h: two products per k tile, accumulated in fp32), and leaves its 16 x L
+//      pre-activations in shared memory;
+//   2. one thread per (pair of units, line) applies the gates (the step's input-gate values were
+//      fetched during the previous step), keeps its fp32 h in registers and stores the new h's
+//      hi / lo parts into every CTA of the cluster through distributed shared memory;
+//   3. `barrier.cluster` (hardware co-scheduled CTAs, no global-memory spin waits) publishes h:
+//      arrive right after the stores, wait before the next step reads it.
 // Each line runs for its own length; the backward direction starts at len - 1 (src/gpu.rs:797-800).
 #include <atomic>
 #include <cooperative_groups.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "kernels.h"
@@ -26,33 +34,26 @@ namespace k {
 namespace {
 
 constexpr int kHid = 256;
-constexpr int kCluster = 8;
-constexpr int kUnits = kHid / kCluster;  // 32 hidden units per CTA
-constexpr int kSlices = 8;               // k split over 8 warps
-constexpr int kThreadsG = kSlices * 32;
-constexpr int kSliceLen = kHid / kSlices;
+constexpr int kCluster = 4;
+constexpr int kUnits = kHid / kCluster;  // 64 hidden units per CTA
+constexpr int kKT = kHid / 16;           // k tiles of the m16n8k16 products
+constexpr int kMatWarps = 12;            // 3 gates x 4 tiles of 16 units
+constexpr int kThreadsG = 512;
+constexpr int kHS = kHid + 8;            // halves per line row of h (pads the banks apart)
 
 __device__ __forceinline__ float sigm(float v) { return 1.0f / (1.0f + expf(-v)); }
 
-// h of L lines at one k (L consecutive floats, 4 L-byte aligned) as vector loads
-template <int L>
-__device__ __forceinline__ void load_h(const float *p, float (&h)[L]) {
-    if (L % 4 == 0) {
-#pragma unroll
-        for (int i = 0; i < L / 4; i++) {
-            const float4 v = reinterpret_cast<const float4 *>(p)[i];
-            h[4 * i] = v.x;
-            h[4 * i + 1] = v.y;
-            h[4 * i + 2] = v.z;
-            h[4 * i + 3] = v.w;
-        }
-    } else if (L == 2) {
-        const float2 v = *reinterpret_cast<const float2 *>(p);
-        h[0] = v.x;
-        h[L - 1] = v.y;
-    } else {
-        h[0] = p[0];
-    }
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void cluster_arrive() {
@@ -60,121 +61,151 @@ __device__ __forceinline__ void cluster_arrive() {
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// shared memory: h [2 buffers][hi, lo][L lines][kHS halves], pre-activations [3][L][64] floats
 template <int L>
-__global__ void __launch_bounds__(kThreadsG) k_gru(const float *__restrict__ g, const float *__restrict__ r,
-                                            const float *__restrict__ rb, const int *__restrict__ lens, int tmax,
-                                            int ntot, float *__restrict__ y) {
-    extern __shared__ __align__(16) float smem[];
-    float4 *Rs = reinterpret_cast<float4 *>(smem);              // [256 k][32 u] (z, r, h, 0)
-    float *hbuf = smem + kHid * kUnits * 4;                       // [2][256 k][L]
-    float *red = hbuf + 2 * kHid * L;                             // [8 slices][3][L][32 u]
+constexpr size_t gru_smem() {
+    return sizeof(__half) * 2 * 2 * L * kHS + sizeof(float) * 3 * L * kUnits;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kThreadsG, 1) k_gru(const float *__restrict__ g, const float *__restrict__ r,
+                                                      const float *__restrict__ rb, const int *__restrict__ lens,
+                                                      int tmax, int ntot, float *__restrict__ y) {
+    constexpr int L = 8 * NT;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __half *hs = reinterpret_cast<__half *>(smem_raw);                                     // [2][2][L][kHS]
+    float *pre = reinterpret_cast<float *>(smem_raw + sizeof(__half) * 2 * 2 * L * kHS);  // [3][L][64]
 
     cg::cluster_group cluster = cg::this_cluster();
     const int crank = (int)cluster.block_rank();
     const int dir = blockIdx.y;
-    const int group = blockIdx.x / kCluster;
-    const int line0 = group * L;
+    const int line0 = (blockIdx.x / kCluster) * L;
     const int u0 = crank * kUnits;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int grp = lane >> 2, tig = lane & 3;
 
-    // R rows of this CTA's units, k-major
-    const float *Rd = r + (size_t)dir * 3 * kHid * kHid;
-    for (int i = tid; i < kHid * kUnits; i += blockDim.x) {
-        int u = i % kUnits, kk = i / kUnits;
-        float4 v;
-        v.x = Rd[(size_t)(0 * kHid + u0 + u) * kHid + kk];
-        v.y = Rd[(size_t)(1 * kHid + u0 + u) * kHid + kk];
-        v.z = Rd[(size_t)(2 * kHid + u0 + u) * kHid + kk];
-        v.w = 0.f;
-        Rs[kk * kUnits + u] = v;
+    // the A fragments of this warp's 16 rows, fp16, for the whole sequence
+    uint32_t a[kKT][4];
+    const int gate = warp / 4, ut = warp % 4;
+    if (warp < kMatWarps) {
+        const float *Rd = r + (size_t)dir * 3 * kHid * kHid;
+        const float *r0 = Rd + (size_t)(gate * kHid + u0 + ut * 16 + grp) * kHid;
+        const float *r8 = r0 + (size_t)8 * kHid;
+#pragma unroll
+        for (int kt = 0; kt < kKT; kt++) {
+            const int k0 = kt * 16 + 2 * tig;
+            a[kt][0] = pack2(r0[k0], r0[k0 + 1]);
+            a[kt][1] = pack2(r8[k0], r8[k0 + 1]);
+            a[kt][2] = pack2(r0[k0 + 8], r0[k0 + 9]);
+            a[kt][3] = pack2(r8[k0 + 8], r8[k0 + 9]);
+        }
     }
-    for (int i = tid; i < 2 * kHid * L; i += blockDim.x) hbuf[i] = 0.f;
+    for (int i = tid; i < 2 * 2 * L * kHS / 2; i += kThreadsG) reinterpret_cast<uint32_t *>(hs)[i] = 0u;
 
     int steps = 0;
 #pragma unroll
     for (int l = 0; l < L; l++) {
-        int len = line0 + l < ntot ? lens[line0 + l] : 0;
+        const int len = line0 + l < ntot ? lens[line0 + l] : 0;
         steps = max(steps, min(len, tmax));
     }
-    // phase-2 role of this thread: unit u2, line l2
-    const int u2 = tid % kUnits, l2 = tid / kUnits;
-    const int j = u0 + u2;
-    const int line = line0 + l2;
-    const bool owner = l2 < L && line < ntot;
+    // gate role: a pair of units (2 up, 2 up + 1 of this CTA) of one line
+    const int up = tid % 32, gl = tid / 32;
+    const bool gater = gl < L;
+    const int line = line0 + gl;
+    const bool owner = gater && line < ntot;
     const int mylen = owner ? min(lens[line], tmax) : 0;
-    float bz = 0.f, br = 0.f, bh = 0.f;
-    if (owner) {
-        bz = rb[dir * 768 + j];
-        br = rb[dir * 768 + 256 + j];
-        bh = rb[dir * 768 + 512 + j];
-    }
-    // phase-1 role: unit u1, k-slice sl
-    const int u1 = tid % kUnits, sl = tid / kUnits;
-    // the input-gate values of this thread's (unit, line) for the next step, loaded a step ahead
+    const int j0 = u0 + 2 * up;  // the pair's first unit in the layer
+    float bz[2] = {0.f, 0.f}, br[2] = {0.f, 0.f}, bh[2] = {0.f, 0.f};
+    float hold[2] = {0.f, 0.f};
+    float gz[2] = {0.f, 0.f}, gr[2] = {0.f, 0.f}, gh[2] = {0.f, 0.f};
     auto gate_ptr = [&](int s) {
         const int t = dir == 0 ? s : mylen - 1 - s;
         return g + ((size_t)t * ntot + line) * 1536 + dir * 768;
     };
-    float gz = 0.f, gr = 0.f, gh = 0.f;
-    if (owner && mylen > 0) {
-        const float *gb = gate_ptr(0);
-        gz = gb[j];
-        gr = gb[256 + j];
-        gh = gb[512 + j];
+    if (owner) {
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+            bz[q] = rb[dir * 768 + j0 + q];
+            br[q] = rb[dir * 768 + 256 + j0 + q];
+            bh[q] = rb[dir * 768 + 512 + j0 + q];
+        }
+        if (mylen > 0) {
+            const float *gb = gate_ptr(0);
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                gz[q] = gb[j0 + q];
+                gr[q] = gb[256 + j0 + q];
+                gh[q] = gb[512 + j0 + q];
+            }
+        }
     }
     cluster.sync();
 
     for (int s = 0; s < steps; s++) {
-        const float *hc = hbuf + (s & 1) * kHid * L;
-        float *hn_buf = hbuf + ((s + 1) & 1) * kHid * L;
-        float az[L], ar[L], ah[L];
+        const __half *hc = hs + (size_t)(s & 1) * 2 * L * kHS;
+        __half *hn_buf = hs + (size_t)((s + 1) & 1) * 2 * L * kHS;
+        if (warp < kMatWarps) {
+            float acc[2][NT][4];
 #pragma unroll
-        for (int l = 0; l < L; l++) az[l] = ar[l] = ah[l] = 0.f;
-#pragma unroll 4
-        for (int kk = 0; kk < kSliceLen; kk++) {
-            int k = sl * kSliceLen + kk;
-            float4 w = Rs[k * kUnits + u1];
-            float hv[L];
-            load_h<L>(hc + k * L, hv);
+            for (int c = 0; c < 2; c++)
 #pragma unroll
-            for (int l = 0; l < L; l++) {
-                az[l] += w.x * hv[l];
-                ar[l] += w.y * hv[l];
-                ah[l] += w.z * hv[l];
+                for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                    for (int q = 0; q < 4; q++) acc[c][nt][q] = 0.f;
+#pragma unroll
+            for (int kt = 0; kt < kKT; kt++) {
+#pragma unroll
+                for (int nt = 0; nt < NT; nt++) {
+                    const __half *hi = hc + (size_t)(nt * 8 + grp) * kHS + kt * 16 + 2 * tig;
+                    const __half *lo = hi + (size_t)L * kHS;
+                    const uint32_t h0 = *reinterpret_cast<const uint32_t *>(hi);
+                    const uint32_t h1 = *reinterpret_cast<const uint32_t *>(hi + 8);
+                    const uint32_t l0 = *reinterpret_cast<const uint32_t *>(lo);
+                    const uint32_t l1 = *reinterpret_cast<const uint32_t *>(lo + 8);
+                    mma16816(acc[kt & 1][nt], a[kt], h0, h1);
+                    mma16816(acc[kt & 1][nt], a[kt], l0, l1);
+                }
             }
-        }
-        float *rd = red + (size_t)sl * 3 * L * kUnits + u1;
+            // rows = units (grp, grp + 8), columns = lines (2 tig, 2 tig + 1)
+            float *pg = pre + (size_t)gate * L * kUnits;
 #pragma unroll
-        for (int l = 0; l < L; l++) {
-            rd[l * kUnits] = az[l];
-            rd[(L + l) * kUnits] = ar[l];
-            rd[(2 * L + l) * kUnits] = ah[l];
+            for (int nt = 0; nt < NT; nt++) {
+                const int ln = nt * 8 + 2 * tig, u = ut * 16 + grp;
+                pg[(size_t)ln * kUnits + u] = acc[0][nt][0] + acc[1][nt][0];
+                pg[(size_t)(ln + 1) * kUnits + u] = acc[0][nt][1] + acc[1][nt][1];
+                pg[(size_t)ln * kUnits + u + 8] = acc[0][nt][2] + acc[1][nt][2];
+                pg[(size_t)(ln + 1) * kUnits + u + 8] = acc[0][nt][3] + acc[1][nt][3];
+            }
         }
         __syncthreads();
-        float hn = 0.f;
         bool wrote = false;
-        if (l2 < L) {
-            float hold = hc[j * L + l2];
-            hn = hold;
+        float hn[2] = {hold[0], hold[1]};
+        if (gater) {
             if (owner && s < mylen) {
-                float pz = 0.f, pr = 0.f, ph = 0.f;
 #pragma unroll
-                for (int q = 0; q < kSlices; q++) {
-                    const float *rq = red + (size_t)q * 3 * L * kUnits + u2;
-                    pz += rq[l2 * kUnits];
-                    pr += rq[(L + l2) * kUnits];
-                    ph += rq[(2 * L + l2) * kUnits];
+                for (int q = 0; q < 2; q++) {
+                    const int u = 2 * up + q;
+                    const float pz = pre[(size_t)(0 * L + gl) * kUnits + u];
+                    const float pr = pre[(size_t)(1 * L + gl) * kUnits + u];
+                    const float ph = pre[(size_t)(2 * L + gl) * kUnits + u];
+                    const float z = sigm(gz[q] + pz + bz[q]);
+                    const float rr = sigm(gr[q] + pr + br[q]);
+                    const float cc = tanhf(gh[q] + rr * (ph + bh[q]));
+                    hn[q] = (1.0f - z) * cc + z * hold[q];
                 }
-                float z = sigm(gz + pz + bz);
-                float rr = sigm(gr + pr + br);
-                float c = tanhf(gh + rr * (ph + bh));
-                hn = (1.0f - z) * c + z * hold;
                 wrote = true;
             }
+            hold[0] = hn[0];
+            hold[1] = hn[1];
+            const __half hi0 = __float2half_rn(hn[0]), hi1 = __float2half_rn(hn[1]);
+            const __half2 hi2 = __halves2half2(hi0, hi1);
+            const __half2 lo2 = __floats2half2_rn(hn[0] - __half2float(hi0), hn[1] - __half2float(hi1));
+            const uint32_t hv = *reinterpret_cast<const uint32_t *>(&hi2), lv = *reinterpret_cast<const uint32_t *>(&lo2);
+            __half *dst_hi = hn_buf + (size_t)gl * kHS + j0, *dst_lo = dst_hi + (size_t)L * kHS;
 #pragma unroll
             for (int q = 0; q < kCluster; q++) {
-                float *dst = cluster.map_shared_rank(hn_buf + j * L + l2, q);
-                *dst = hn;
+                *reinterpret_cast<uint32_t *>(cluster.map_shared_rank(dst_hi, q)) = hv;
+                *reinterpret_cast<uint32_t *>(cluster.map_shared_rank(dst_lo, q)) = lv;
             }
         }
         // publish h (release), then store y and fetch the next step's gates while the other
@@ -182,68 +213,68 @@ __global__ void __launch_bounds__(kThreadsG) k_gru(const float *__restrict__ g, 
         cluster_arrive();
         if (wrote) {
             const int t = dir == 0 ? s : mylen - 1 - s;
-            y[((size_t)t * ntot + line) * 512 + dir * 256 + j] = hn;
+            float *yo = y + ((size_t)t * ntot + line) * 512 + dir * 256 + j0;
+            *reinterpret_cast<float2 *>(yo) = make_float2(hn[0], hn[1]);
             if (s + 1 < mylen) {
                 const float *gb = gate_ptr(s + 1);
-                gz = gb[j];
-                gr = gb[256 + j];
-                gh = gb[512 + j];
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    gz[q] = gb[j0 + q];
+                    gr[q] = gb[256 + j0 + q];
+                    gh[q] = gb[512 + j0 + q];
+                }
             }
         }
         cluster_wait();
     }
 }
 
-template <int L>
-size_t gru_smem() {
-    return sizeof(float) * ((size_t)kHid * kUnits * 4 + 2 * kHid * L + (size_t)kSlices * kUnits * 3 * L);
-}
-
-template <int L>
-void launch_gru(Ctx *c, const float *g, const float *r, const float *rb, const int *lens, int tmax, int ntot,
-                float *y) {
-    size_t smem = gru_smem<L>();
-    static std::atomic<bool> configured[64];
-    if (!configured[c->device]) {
-        WOCR_CUDA(cudaFuncSetAttribute(k_gru<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        configured[c->device] = true;
-    }
-    int groups = (ntot + L - 1) / L;
+template <int NT>
+cudaLaunchConfig_t gru_config(Ctx *c, int clusters, cudaLaunchAttribute *attr) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(groups * kCluster, 2, 1);
+    cfg.gridDim = dim3(clusters * kCluster, 2, 1);
     cfg.blockDim = dim3(kThreadsG, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = gru_smem<8 * NT>();
     cfg.stream = c->stream;
-    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kCluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    WOCR_CUDA(cudaLaunchKernelEx(&cfg, k_gru<L>, g, r, rb, lens, tmax, ntot, y));
+    return cfg;
+}
+
+template <int NT>
+void configure(Ctx *c) {
+    static std::atomic<bool> configured[64];
+    if (!configured[c->device]) {
+        WOCR_CUDA(cudaFuncSetAttribute(k_gru<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)gru_smem<8 * NT>()));
+        configured[c->device] = true;
+    }
+}
+
+template <int NT>
+void launch_gru(Ctx *c, const float *g, const float *r, const float *rb, const int *lens, int tmax, int ntot,
+                float *y) {
+    configure<NT>(c);
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = gru_config<NT>(c, (ntot + 8 * NT - 1) / (8 * NT), attr);
+    WOCR_CUDA(cudaLaunchKernelEx(&cfg, k_gru<NT>, g, r, rb, lens, tmax, ntot, y));
     WOCR_LAUNCHED(c);
 }
 
-template <int L>
+// clusters of the NT instance resident at once (both directions count)
+template <int NT>
 int max_clusters(Ctx *c) {
     static std::atomic<int> cached[64];
     if (cached[c->device]) return cached[c->device];
-    size_t smem = gru_smem<L>();
-    WOCR_CUDA(cudaFuncSetAttribute(k_gru<L>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kCluster * 64, 2, 1);
-    cfg.blockDim = dim3(kThreadsG, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    configure<NT>(c);
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kCluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cudaLaunchConfig_t cfg = gru_config<NT>(c, 32, attr);
     int n = 0;
-    WOCR_CUDA(cudaOccupancyMaxActiveClusters(&n, k_gru<L>, &cfg));
+    WOCR_CUDA(cudaOccupancyMaxActiveClusters(&n, k_gru<NT>, &cfg));
     cached[c->device] = n > 0 ? n : 1;
     return cached[c->device];
 }
@@ -255,12 +286,11 @@ void gru_layer(Ctx *c, const float *g, const float *r, const float *rb, const in
     if (ntot == 0 || tmax == 0) return;
     Prof pf(c, "gru", 2.0 * 2.0 * ntot * (double)tmax * 768.0 * 256.0,
             4.0 * (double)tmax * ntot * (1536.0 + 512.0) + 4.0 * 2 * 768 * 256);
-    // The fewest lines per cluster that still fit all clusters of both directions at once.
-    auto fits = [&](int L, int maxc) { return 2 * ((ntot + L - 1) / L) <= maxc; };
-    if (fits(1, max_clusters<1>(c))) launch_gru<1>(c, g, r, rb, lens, tmax, ntot, y);
-    else if (fits(2, max_clusters<2>(c))) launch_gru<2>(c, g, r, rb, lens, tmax, ntot, y);
-    else if (fits(4, max_clusters<4>(c))) launch_gru<4>(c, g, r, rb, lens, tmax, ntot, y);
-    else launch_gru<8>(c, g, r, rb, lens, tmax, ntot, y);
+    // 8 lines a cluster while both directions' clusters are all resident at once, else 16
+    if (2 * ((ntot + 7) / 8) <= max_clusters<1>(c))
+        launch_gru<1>(c, g, r, rb, lens, tmax, ntot, y);
+    else
+        launch_gru<2>(c, g, r, rb, lens, tmax, ntot, y);
     c->flops += 2.0 * 2.0 * ntot * (double)tmax * 768.0 * 256.0;
 }
 

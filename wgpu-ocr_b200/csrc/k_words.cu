@@ -898,7 +898,9 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     p.min_area = min_area;
     p.status = c->status;
     {
-        Prof pf(c, "word_rect", 0, 0);
+        // algorithmic bytes: every border point read from the cache and written once, its keep
+        // flag, and the rectangles (the kernel is bound by the sequential Douglas-Peucker levels)
+        Prof pf(c, "word_rect", 0, 9.0 * (double)slots + 24.0 * C);
         k_word_rect<kWT><<<C, kWT, 0, c->stream>>>(p);
         WOCR_LAUNCHED(c);
         if (n_big > 0) {
