@@ -59,7 +59,7 @@ def parse():
                         "pp3 / ppdet4: configs 0, 3 and 4 through their public calls; ppdb4: config 4 with the DB "
                         "mask and box scores on the device; pplines: PP line extraction; words1: word rectangles "
                         "of config 1 detection masks (secondary measurements)")
-    p.add_argument("--lanes", type=int, default=8, help="page-pipeline workers per GPU (pp4, pp4ink)")
+    p.add_argument("--lanes", type=int, default=4, help="page-pipeline workers per GPU (pp4, pp4ink)")
     p.add_argument("--merge", type=int, default=3, help="pages whose recognitions a lane runs together")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (pp4, pp4ink)")
     return p.parse_args()

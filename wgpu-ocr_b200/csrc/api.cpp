@@ -189,9 +189,10 @@ struct wocr_ndgraph {
     wocr_ctx *ctx;
     std::unique_ptr<Executor> graph;
     Stats last;
-    // captured runs per input shape: config 3 recognises 16 width buckets a step, so the cache
-    // holds more than that (an LRU of fewer entries would miss on every call of such a cycle)
-    NdReplay replays[32];
+    // captured runs per input shape: config 3 recognises 16 width buckets a step and a page of
+    // the page pipeline up to ~50 line batches of different widths, so the cache holds far more
+    // than that (an LRU of fewer entries than a cycle's shapes misses on every call of it)
+    NdReplay replays[256];
     uint64_t uses = 0;
     // the probability map of the last wocr_ppdet_page ([map_h][map_w] fp32) for the DB steps
     BufP map_buf;
@@ -1679,6 +1680,7 @@ std::vector<k::DbBox> db_make_boxes(const float *rects, int n, int w, int h) {
         b.y0 = (int)std::min<int64_t>(to_idx(std::floor(lo_y) - 1.f), h);
         b.x1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_x) + 1.f), std::max(w - 1, 0));
         b.y1 = (int)std::min<int64_t>(to_idx(std::ceil(hi_y) + 1.f), std::max(h - 1, 0));
+        b.map = 0;
     }
     return bx;
 }
@@ -1709,22 +1711,38 @@ void db_bounds(const float *r, float *left, float *top) {
     *top = ty;
 }
 
-// `ppdet::boxes` (src/ppdet.rs:87-132) on a device map: the p > thresh mask, its external
-// contours' minimum-area rectangles (simplified, epsilon 2) and their scores on the device; the
-// size checks, unclip, page scaling and reading order on the host, as the reference orders them.
-std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float *to_page, float thresh,
-                            float box_thresh, float unclip_ratio, float min_size) {
+// `ppdet::boxes` (src/ppdet.rs:87-132) on n device maps of one size, stacked [n][h][w]: the
+// p > thresh masks, their external contours' minimum-area rectangles (simplified, epsilon 2) and
+// the box scores on the device, every page in the same launches; the size checks, unclip, page
+// scaling and reading order on the host, page by page, as the reference orders them.
+std::vector<std::vector<float>> db_boxes_pages(Ctx *c, const float *maps, int npages, int w, int h,
+                                               const float *to_page, float thresh, float box_thresh,
+                                               float unclip_ratio, float min_size) {
     const int words = (w + 31) / 32;
-    BufP bits = alloc(c, (size_t)words * h * 4);
-    k::db_mask(c, prob, w, h, thresh, (uint32_t *)bits->p);
-    k::WordRects wr = k::word_rects(c, (const uint32_t *)bits->p, 1, w, h, 0.f, 0.f, -INFINITY);
+    const int64_t plane = (int64_t)w * h;
+    BufP bits = alloc(c, (size_t)words * h * npages * 4);
+    // the stacked maps threshold as one tall map: rows are independent
+    k::db_mask(c, maps, w, h * npages, thresh, (uint32_t *)bits->p);
+    k::WordRects wr = k::word_rects(c, (const uint32_t *)bits->p, npages, w, h, 0.f, 0.f, -INFINITY);
     std::vector<float> rs((size_t)wr.n * 6);
+    std::vector<int32_t> counts((size_t)npages);
     d2h(c, rs.data(), wr.rects->p, rs.size() * 4);
+    d2h(c, counts.data(), wr.page_count->p, counts.size() * 4);
     sync_bounded(c, 0);
     std::vector<float> cand;
-    for (int i = 0; i < wr.n; i++) {
-        const float *r = rs.data() + 6 * (size_t)i;
-        if (std::min(r[4], r[5]) >= min_size) cand.insert(cand.end(), r, r + 6);
+    std::vector<int> cand_page;
+    {
+        size_t r0 = 0;
+        for (int q = 0; q < npages; q++) {
+            for (int i = 0; i < counts[q]; i++) {
+                const float *r = rs.data() + 6 * (r0 + (size_t)i);
+                if (std::min(r[4], r[5]) >= min_size) {
+                    cand.insert(cand.end(), r, r + 6);
+                    cand_page.push_back(q);
+                }
+            }
+            r0 += (size_t)counts[q];
+        }
     }
     const int nc = (int)(cand.size() / 6);
     // `score < box_thresh` per candidate.  The ordered f32 sum S of a box's n inside values lies
@@ -1733,19 +1751,20 @@ std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float
     // whose mean is clear of box_thresh by that margin, and only the rest get the ordered score.
     std::vector<char> below((size_t)nc, 0);
     if (nc > 0) {
-        const std::vector<k::DbBox> bx = db_make_boxes(cand.data(), nc, w, h);
+        std::vector<k::DbBox> bx = db_make_boxes(cand.data(), nc, w, h);
+        for (int i = 0; i < nc; i++) bx[i].map = plane * cand_page[i];
         BufP db = alloc(c, bx.size() * sizeof(k::DbBox)), dsum = alloc(c, (size_t)nc * 16),
              dcnt = alloc(c, (size_t)nc * 8);
         WOCR_CUDA(cudaMemcpyAsync(db->p, bx.data(), bx.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice, c->stream));
         int max_rows = 1;
         for (const k::DbBox &b : bx) max_rows = std::max(max_rows, b.y1 - b.y0 + 1);
-        k::db_bounds(c, prob, w, (const k::DbBox *)db->p, nc, max_rows, (double *)dsum->p, (long long *)dcnt->p);
+        k::db_bounds(c, maps, w, (const k::DbBox *)db->p, nc, max_rows, (double *)dsum->p, (long long *)dcnt->p);
         std::vector<double> sums((size_t)nc * 2);
         std::vector<long long> cnts((size_t)nc);
         d2h(c, sums.data(), dsum->p, sums.size() * 8);
         d2h(c, cnts.data(), dcnt->p, cnts.size() * 8);
         sync_bounded(c, 0);
-        std::vector<float> amb;
+        std::vector<k::DbBox> amb;
         std::vector<int> amb_idx;
         const double u = std::ldexp(1.0, -24);
         for (int i = 0; i < nc; i++) {
@@ -1770,17 +1789,24 @@ std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float
                     settled = false;
             }
             if (!settled) {
-                amb.insert(amb.end(), cand.data() + 6 * (size_t)i, cand.data() + 6 * (size_t)i + 6);
+                amb.push_back(bx[i]);
                 amb_idx.push_back(i);
             }
         }
         if (!amb_idx.empty()) {
-            std::vector<float> sc(amb_idx.size());
-            db_score_boxes(c, prob, w, h, amb.data(), (int)amb_idx.size(), sc.data());
+            const int na = (int)amb.size();
+            BufP da = alloc(c, amb.size() * sizeof(k::DbBox)), ds = alloc(c, (size_t)na * 4);
+            WOCR_CUDA(cudaMemcpyAsync(da->p, amb.data(), amb.size() * sizeof(k::DbBox), cudaMemcpyHostToDevice,
+                                      c->stream));
+            k::db_scores(c, maps, w, h, (const k::DbBox *)da->p, na, (float *)ds->p);
+            std::vector<float> sc((size_t)na);
+            d2h(c, sc.data(), ds->p, (size_t)na * 4);
+            sync_bounded(c, 0);
             for (size_t j = 0; j < amb_idx.size(); j++) below[amb_idx[j]] = sc[j] < box_thresh;
         }
     }
-    std::vector<float> out;
+    std::vector<std::vector<float>> pages((size_t)npages);
+    std::vector<std::vector<float>> outs((size_t)npages);
     const float s = (to_page[0] + to_page[1]) / 2.0f;
     for (int i = 0; i < nc; i++) {
         const float *r = cand.data() + 6 * (size_t)i;
@@ -1791,30 +1817,39 @@ std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float
         const float nw = rw + 2.0f * d, nh = rh + 2.0f * d;
         if (std::min(nw, nh) < min_size + 2.0f) continue;
         const float o[6] = {r[0] * to_page[0], r[1] * to_page[1], r[2], r[3], nw * s, nh * s};
-        out.insert(out.end(), o, o + 6);
+        outs[cand_page[i]].insert(outs[cand_page[i]].end(), o, o + 6);
     }
-    // stable by the top of the bounding rectangle, then boxes whose tops are within 10 px of
-    // their predecessor's by the left edge (one insertion pass)
-    const int n = (int)(out.size() / 6);
-    std::vector<int> idx((size_t)n);
-    std::vector<float> top((size_t)n), left((size_t)n);
-    for (int i = 0; i < n; i++) {
-        idx[i] = i;
-        db_bounds(out.data() + 6 * (size_t)i, &left[i], &top[i]);
-    }
-    std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return top[a] < top[b]; });
-    for (int i = 0; i < n; i++)
-        for (int j = i; j > 0; j--) {
-            const int a = idx[j - 1], b = idx[j];
-            if (std::fabs(top[b] - top[a]) < 10.0f && left[b] < left[a])
-                std::swap(idx[j - 1], idx[j]);
-            else
-                break;
+    for (int q = 0; q < npages; q++) {
+        const std::vector<float> &out = outs[q];
+        // stable by the top of the bounding rectangle, then boxes whose tops are within 10 px of
+        // their predecessor's by the left edge (one insertion pass)
+        const int n = (int)(out.size() / 6);
+        std::vector<int> idx((size_t)n);
+        std::vector<float> top((size_t)n), left((size_t)n);
+        for (int i = 0; i < n; i++) {
+            idx[i] = i;
+            db_bounds(out.data() + 6 * (size_t)i, &left[i], &top[i]);
         }
-    std::vector<float> sorted(out.size());
-    for (int i = 0; i < n; i++)
-        std::memcpy(sorted.data() + 6 * (size_t)i, out.data() + 6 * (size_t)idx[i], 24);
-    return sorted;
+        std::stable_sort(idx.begin(), idx.end(), [&](int a, int b) { return top[a] < top[b]; });
+        for (int i = 0; i < n; i++)
+            for (int j = i; j > 0; j--) {
+                const int a = idx[j - 1], b = idx[j];
+                if (std::fabs(top[b] - top[a]) < 10.0f && left[b] < left[a])
+                    std::swap(idx[j - 1], idx[j]);
+                else
+                    break;
+            }
+        std::vector<float> &sorted = pages[q];
+        sorted.resize(out.size());
+        for (int i = 0; i < n; i++)
+            std::memcpy(sorted.data() + 6 * (size_t)i, out.data() + 6 * (size_t)idx[i], 24);
+    }
+    return pages;
+}
+
+std::vector<float> db_boxes(Ctx *c, const float *prob, int w, int h, const float *to_page, float thresh,
+                            float box_thresh, float unclip_ratio, float min_size) {
+    return db_boxes_pages(c, prob, 1, w, h, to_page, thresh, box_thresh, unclip_ratio, min_size)[0];
 }
 
 void put_boxes(const std::vector<float> &b, float *boxes, int32_t cap, int32_t *n) {
@@ -2044,8 +2079,9 @@ struct PpLane {
     wocr_ctx *ctx = nullptr;
     wocr_ndgraph *det = nullptr, *rec = nullptr;
     wocr_batch *batch = nullptr;
-    BufP page;  // the device copy of a host page
+    BufP page;  // a chunk of pages back to back on the device (the detection batch's input)
     size_t page_bytes = 0;
+    BufP maps_tmp;  // the maps of a batch that ran without a captured graph
     ~PpLane() {
         if (batch) wocr_batch_destroy(batch);
         if (det) wocr_ndgraph_destroy(det);
@@ -2094,36 +2130,16 @@ bool on_device(const void *p) {
     return a.type == cudaMemoryTypeDevice;
 }
 
-// The first half of a page: upload (host pages), detection, DB boxes, line cuts.
-void pp_front(PpLane &ln, const uint8_t *rgb, int w, int h, const PpArgs &a, PpPage &out) {
-    Ctx *c = &ln.ctx->c;
-    WOCR_CUDA(cudaSetDevice(c->device));
-    const size_t bytes = (size_t)w * h * 3;
-    const uint8_t *dpage = rgb;
-    if (!on_device(rgb)) {
-        // the page crosses PCIe once; detection and the line cuts read it on the device
-        if (ln.page_bytes < bytes) {
-            ln.page = alloc(c, bytes);
-            ln.page_bytes = bytes;
-        }
-        WOCR_CUDA(cudaMemcpyAsync(ln.page->p, rgb, bytes, cudaMemcpyHostToDevice, c->stream));
-        dpage = (const uint8_t *)ln.page->p;
-        out.h2d += (int64_t)bytes;
-    }
-    int32_t ow = 0, oh = 0;
-    float tp[2];
-    check_st(wocr_ppdet_page(ln.det, dpage, w, h, a.max_side, nullptr, 0, &ow, &oh, tp));
-    out.boxes = db_boxes(c, ln.det->map, ln.det->map_w, ln.det->map_h, ln.det->map_to_page, a.db[0], a.db[1], a.db[2],
-                         a.db[3]);
-    const int n = (int)(out.boxes.size() / 6);
-    if (!a.want_rec || n == 0) return;
-    // lines: each box grown by relv x its height across the text (src/bin/ocr-bench.rs:534-558:
-    // a line of one box, whose median height is its own), cut at its bounding rectangle
+// The line rectangles of a page's boxes: each box grown by relv x its height across the text
+// (src/bin/ocr-bench.rs:534-558: a line of one box, whose median height is its own), then its
+// bounding rectangle [left, top, right, bottom].
+std::vector<float> pp_line_rects(const std::vector<float> &boxes, float relv) {
+    const int n = (int)(boxes.size() / 6);
     std::vector<float> lr((size_t)n * 4);
     for (int i = 0; i < n; i++) {
-        const float *r = out.boxes.data() + 6 * (size_t)i;
+        const float *r = boxes.data() + 6 * (size_t)i;
         const bool upright = std::fabs(r[3]) >= std::fabs(r[2]);
-        const float across = a.relv * (upright ? r[5] : r[4]);
+        const float across = relv * (upright ? r[5] : r[4]);
         const float rw = upright ? r[4] : r[4] + 2.f * across, rh = upright ? r[5] + 2.f * across : r[5];
         const float hw = rw / 2.0f, hh = rh / 2.0f;
         float lx = INFINITY, ty = INFINITY, rx = -INFINITY, by = -INFINITY;
@@ -2140,55 +2156,191 @@ void pp_front(PpLane &ln, const uint8_t *rgb, int w, int h, const PpArgs &a, PpP
         o[2] = rx;
         o[3] = by;
     }
-    out.order.assign((size_t)n, 0);
-    out.bn.assign((size_t)n, 0);
-    out.bw.assign((size_t)n, 0);
-    int64_t total = 0;
-    check_st(wocr_pp_lines(ln.ctx, dpage, w, h, lr.data(), n, a.per_batch, nullptr, 0, out.order.data(), out.bn.data(),
-                           out.bw.data(), &out.nb, &total));
-    out.lines = alloc(c, (size_t)std::max<int64_t>(total, 1) * 4);
-    check_st(wocr_pp_lines(ln.ctx, dpage, w, h, lr.data(), n, a.per_batch, (float *)out.lines->p, total,
-                           out.order.data(), out.bn.data(), out.bw.data(), &out.nb, &total));
+    return lr;
+}
+
+// NdGraph::det_input + the DB detector on n device pages of one size, back to back at d_pages,
+// in one batch [n, 3, oh, ow] (each image's results are those of a batch of one: every kernel
+// computes an image's outputs from that image alone, in the same order).  Replayed from a CUDA
+// graph per (n, size, input buffer) after the first call.  Returns the maps [n][mh][mw].
+const float *ppdet_batch(PpLane &ln, const uint8_t *d_pages, int n, int w, int h, int max_side, int *mw, int *mh) {
+    wocr_ndgraph *g = ln.det;
+    Ctx *c = &g->ctx->c;
+    RunScope rs(c, &g->last);
+    int ow, oh;
+    det_input_sizes(w, h, max_side, &ow, &oh);
+    const size_t page_bytes = (size_t)w * h * 3;
+    auto pass = [&]() {
+        DT x = new_nhwc(c, n, 3, oh, ow);
+        for (int q = 0; q < n; q++)
+            k::det_prep(c, d_pages + page_bytes * q, w, h, ow, oh, 0, x.p + (int64_t)q * oh * ow * 3);
+        return to_rowmajor(c, g->graph->run(x));
+    };
+    auto dims = [&](const std::vector<int64_t> &shape) {
+        int64_t m = 1;
+        for (auto d : shape) m *= d;
+        *mw = (int)shape.back();
+        *mh = (int)(m / std::max<int64_t>((int64_t)n * shape.back(), 1));
+        return m;
+    };
+    bool first = false;
+    NdReplay *r = nd_replay(g, {n, h, w, max_side, (int64_t)(intptr_t)d_pages}, 3, &first);
+    if (!r || first) {
+        DT y = pass();
+        if (r) r->out_shape = y.shape;
+        dims(y.shape);
+        ln.maps_tmp = y.buf;
+        return y.p;
+    }
+    const int64_t m = dims(r->out_shape);
+    if (!r->exec) {
+        r->out = alloc(c, (size_t)std::max<int64_t>(m, 1) * 4);
+        const double f0 = c->flops;
+        const int64_t l0 = c->launches;
+        WOCR_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+        try {
+            DT y = pass();
+            if (y.shape != r->out_shape) fail(WOCR_ERR_SHAPE, "NdGraph output shape changed between runs");
+            WOCR_CUDA(cudaMemcpyAsync(r->out->p, y.p, (size_t)m * 4, cudaMemcpyDeviceToDevice, c->stream));
+        } catch (...) {
+            cudaGraph_t dead = nullptr;
+            cudaStreamEndCapture(c->stream, &dead);
+            if (dead) cudaGraphDestroy(dead);
+            r->reset();
+            throw;
+        }
+        WOCR_CUDA(cudaStreamEndCapture(c->stream, &r->graph));
+        WOCR_CUDA(cudaGraphInstantiate(&r->exec, r->graph, 0));
+        r->flops = c->flops - f0;
+        r->launches = c->launches - l0;
+        c->flops = f0;
+        c->launches = l0;
+    }
+    WOCR_CUDA(cudaGraphLaunch(r->exec, c->stream));
+    c->flops += r->flops;
+    c->launches += r->launches;
+    return (const float *)r->out->p;
+}
+
+// The first half of a chunk of pages of one size: the pages gathered on the device (uploads
+// for host pages), their detection in one batch, the DB boxes of all their maps in the same
+// launches, each page's line cuts.
+void pp_front_chunk(PpLane &ln, const uint8_t *const *pages, const std::vector<int> &ks, int w, int h,
+                    const PpArgs &a, std::vector<PpPage> &out) {
+    Ctx *c = &ln.ctx->c;
+    WOCR_CUDA(cudaSetDevice(c->device));
+    const int n = (int)ks.size();
+    const size_t bytes = (size_t)w * h * 3;
+    if (ln.page_bytes < bytes * n) {
+        ln.page = alloc(c, bytes * n);
+        ln.page_bytes = bytes * n;
+    }
+    uint8_t *dp = (uint8_t *)ln.page->p;
+    for (int q = 0; q < n; q++) {
+        const uint8_t *src = pages[ks[q]];
+        const bool dev = on_device(src);
+        WOCR_CUDA(cudaMemcpyAsync(dp + bytes * q, src, bytes, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                  c->stream));
+        if (!dev) out[ks[q]].h2d += (int64_t)bytes;
+    }
+    int mw = 0, mh = 0, ow = 0, oh = 0;
+    const float *maps = ppdet_batch(ln, dp, n, w, h, a.max_side, &mw, &mh);
+    det_input_sizes(w, h, a.max_side, &ow, &oh);
+    const float tp[2] = {(float)w / (float)ow, (float)h / (float)oh};
+    std::vector<std::vector<float>> bx = db_boxes_pages(c, maps, n, mw, mh, tp, a.db[0], a.db[1], a.db[2], a.db[3]);
+    for (int q = 0; q < n; q++) {
+        PpPage &pg = out[ks[q]];
+        pg.boxes = std::move(bx[q]);
+        const int nb = (int)(pg.boxes.size() / 6);
+        if (!a.want_rec || nb == 0) continue;
+        const std::vector<float> lr = pp_line_rects(pg.boxes, a.relv);
+        const uint8_t *dpage = dp + bytes * q;
+        pg.order.assign((size_t)nb, 0);
+        pg.bn.assign((size_t)nb, 0);
+        pg.bw.assign((size_t)nb, 0);
+        int64_t total = 0;
+        check_st(wocr_pp_lines(ln.ctx, dpage, w, h, lr.data(), nb, a.per_batch, nullptr, 0, pg.order.data(),
+                               pg.bn.data(), pg.bw.data(), &pg.nb, &total));
+        pg.lines = alloc(c, (size_t)std::max<int64_t>(total, 1) * 4);
+        check_st(wocr_pp_lines(ln.ctx, dpage, w, h, lr.data(), nb, a.per_batch, (float *)pg.lines->p, total,
+                               pg.order.data(), pg.bn.data(), pg.bw.data(), &pg.nb, &total));
+    }
 }
 
 // The second half of the held pages: every batch's recognition and arg-max queued on the lane's
 // stream with its read staged, one wait, then the classes handed to their lines.
 void pp_recognize(PpLane &ln, const std::vector<PpPage *> &held) {
-    struct Job {
+    // The held pages' batches, grouped by width: batches of one width (of one page or several)
+    // run as one batch of all their lines.  A line's recognition depends only on its own image
+    // and its batch's width (the padding it is decoded over), not on the other lines of its
+    // batch, so the classes are those of the reference's 16-line batches (src/bin/ocr-bench.rs:
+    // 322-333), with fewer, larger launches.
+    struct Part {
         PpPage *pg;
-        int first;  // the batch's first slot in pg->order
+        int first;   // the batch's first slot in pg->order
         int n;
+        int64_t off;  // its float offset in pg->lines
+    };
+    std::map<int, std::vector<Part>> groups;
+    for (PpPage *pg : held) {
+        pg->best.assign(pg->boxes.size() / 6, {});
+        int k = 0;
+        int64_t off = 0;
+        for (int b = 0; b < pg->nb; b++) {
+            groups[pg->bw[b]].push_back({pg, k, pg->bn[b], off});
+            k += pg->bn[b];
+            off += (int64_t)pg->bn[b] * 3 * 48 * pg->bw[b];
+        }
+    }
+    if (groups.empty()) return;
+    Ctx *c = &ln.ctx->c;
+    struct Job {
+        const std::vector<Part> *parts;
+        int n = 0;
         std::vector<uint32_t> best;
         int64_t rows = 0;
     };
     std::vector<Job> jobs;
-    for (PpPage *pg : held) {
-        pg->best.assign(pg->boxes.size() / 6, {});
-        int k = 0;
-        for (int b = 0; b < pg->nb; k += pg->bn[b], b++) jobs.push_back({pg, k, pg->bn[b], {}, 0});
-    }
-    if (jobs.empty()) return;
-    size_t j = 0;
-    for (PpPage *pg : held) {
-        int64_t off = 0;
-        for (int b = 0; b < pg->nb; b++, j++) {
-            Job &jb = jobs[j];
-            const int64_t shape[4] = {pg->bn[b], 3, 48, pg->bw[b]};
-            const int64_t bcap = (int64_t)pg->bn[b] * pg->bw[b];
-            jb.best.resize((size_t)bcap);
-            int64_t oshape[kMaxRank];
-            int32_t orank = 0;
-            check_st(wocr_ndgraph_argmax_enqueue(ln.rec, ln.batch, (const float *)pg->lines->p + off, shape, 4,
-                                                 jb.best.data(), nullptr, nullptr, bcap, &jb.rows, oshape, &orank));
-            off += (int64_t)pg->bn[b] * 3 * 48 * pg->bw[b];
+    std::vector<BufP> merged;  // kept until the wait: the enqueued runs read them
+    for (const auto &g : groups) {
+        const int W = g.first;
+        Job jb;
+        jb.parts = &g.second;
+        for (const Part &p : g.second) jb.n += p.n;
+        const int64_t line_floats = (int64_t)3 * 48 * W;
+        const float *x = nullptr;
+        if (g.second.size() == 1) {
+            x = (const float *)g.second[0].pg->lines->p + g.second[0].off;
+        } else {
+            BufP m = alloc(c, (size_t)(jb.n * line_floats) * 4);
+            int64_t o = 0;
+            for (const Part &p : g.second) {
+                WOCR_CUDA(cudaMemcpyAsync((float *)m->p + o, (const float *)p.pg->lines->p + p.off,
+                                          (size_t)(p.n * line_floats) * 4, cudaMemcpyDeviceToDevice, c->stream));
+                o += p.n * line_floats;
+            }
+            x = (const float *)m->p;
+            merged.push_back(m);
         }
+        const int64_t shape[4] = {jb.n, 3, 48, W};
+        const int64_t bcap = (int64_t)jb.n * W;
+        jb.best.resize((size_t)bcap);
+        jobs.push_back(std::move(jb));
+        Job &jr = jobs.back();
+        int64_t oshape[kMaxRank];
+        int32_t orank = 0;
+        check_st(wocr_ndgraph_argmax_enqueue(ln.rec, ln.batch, x, shape, 4, jr.best.data(), nullptr, nullptr, bcap,
+                                             &jr.rows, oshape, &orank));
     }
     check_st(wocr_wait(ln.batch, 0));
     for (Job &jb : jobs) {
         const int64_t T = jb.rows / std::max(jb.n, 1);
-        for (int q = 0; q < jb.n; q++)
-            jb.pg->best[jb.pg->order[jb.first + q]].assign(jb.best.begin() + q * T, jb.best.begin() + (q + 1) * T);
-        jb.pg->d2h += jb.rows * 4;
+        int64_t line = 0;
+        for (const Part &p : *jb.parts) {
+            for (int q = 0; q < p.n; q++, line++)
+                p.pg->best[p.pg->order[p.first + q]].assign(jb.best.begin() + line * T, jb.best.begin() + (line + 1) * T);
+            p.pg->d2h += (int64_t)p.n * T * 4;
+        }
     }
 }
 
@@ -2221,14 +2373,21 @@ void pp_run(wocr_pp *p, const uint8_t *const *pages, const int32_t *w, const int
         try {
             PpLane &ln = *p->lanes[L];
             WOCR_CUDA(cudaSetDevice(ln.ctx->c.device));
-            std::vector<PpPage *> held;
+            // chunks: up to `merge` of this lane's pages in a row of one size, detected in one batch
+            // and recognised with one wait
+            std::vector<int> ks;
             for (int k = L; k < n; k += lanes) {
-                pp_front(ln, pages[k], w[k], h[k], a, out[k]);
-                held.push_back(&out[k]);
-                if (a.want_rec && ((int)held.size() >= merge || k + lanes >= n)) {
+                ks.push_back(k);
+                const int nx = k + lanes;
+                const bool last = nx >= n || (int)ks.size() >= merge || w[nx] != w[k] || h[nx] != h[k];
+                if (!last) continue;
+                pp_front_chunk(ln, pages, ks, w[k], h[k], a, out);
+                if (a.want_rec) {
+                    std::vector<PpPage *> held;
+                    for (int q : ks) held.push_back(&out[q]);
                     pp_recognize(ln, held);
-                    held.clear();
                 }
+                ks.clear();
             }
         } catch (...) {
             errs[L] = std::current_exception();

@@ -46,7 +46,7 @@ __device__ __forceinline__ void db_load(const float *prob, int w, const DbBox &b
                                         DbRound &o) {
     const int y = b.y0 + r / per_row, xs = b.x0 + (r % per_row) * kDbRound;
     const float dy = __fsub_rn((float)y, b.cy);
-    const float *row = prob + (int64_t)y * w;
+    const float *row = prob + b.map + (int64_t)y * w;
 #pragma unroll
     for (int q = 0; q < kDbChunks; q++) {
         const int x = xs + q * 32 + lane;
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kDbBoundT) k_db_bounds(const float *__restrict
         // a warp per row, lanes along it (coalesced)
         for (int y = ya + (int)(threadIdx.x >> 5); y <= yb; y += kDbBoundT / 32) {
             const float dy = __fsub_rn((float)y, b.cy);
-            const float *row = prob + (int64_t)y * w;
+            const float *row = prob + b.map + (int64_t)y * w;
             for (int x = b.x0 + (int)(threadIdx.x & 31); x <= b.x1; x += 32) {
                 const float dx = __fsub_rn((float)x, b.cx);
                 const float along = __fadd_rn(__fmul_rn(dx, b.ux), __fmul_rn(dy, b.uy));

@@ -139,6 +139,7 @@ void grey_resize(Ctx *c, const uint8_t *rgb, int64_t page_bytes, int n, int w, i
 struct DbBox {
     float cx, cy, ux, uy, hw, hh;
     int x0, y0, x1, y1;
+    int64_t map;  // element offset of the box's map from `prob` (maps of several pages stacked)
 };
 void db_mask(Ctx *c, const float *prob, int w, int h, float thr, uint32_t *bits);
 void db_scores(Ctx *c, const float *prob, int w, int h, const DbBox *boxes, int n, float *scores);
