@@ -512,6 +512,10 @@ static DT conv_run_body(Ctx *c, const DT &xin, const ConvW &cw, int act, const D
         s = to_rowmajor(c, *scale);
         p.insc = s.p;
     }
+    if (k::conv_narrow_ok(p) && !std::getenv("WOCR_NO_NARROW")) {
+        k::conv_narrow(c, p);
+        return done(c, o);
+    }
     if (cw.uw) {
         k::UmmaP u;
         u.mode = 1;

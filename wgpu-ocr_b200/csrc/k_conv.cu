@@ -547,6 +547,138 @@ void conv_gemm(Ctx *c, const ConvP &p) {
     c->flops += 2.0 * (double)M * p.cout * p.kh * p.kw * p.cin;
 }
 
+// Narrow convolutions: at most 64 output channels and at most kNarrowMacs multiply-adds per
+// output pixel.  Their arithmetic intensity is far below the tensor cores' ridge, so they are
+// bound by the activations' bytes, and a tensor-core tile (128 pixels x 64 + channels, an
+// implicit-GEMM A tile split into bf16 parts) would spend its time on tiles mostly of padding.
+// CUDA cores in fp32 instead: a thread per output pixel keeps its output channels in registers;
+// the weights [K][CO] sit in shared memory and every read of them is a warp-wide broadcast.  The
+// K order (ky, kx, ci) and the epilogue (bias, activation, then the residual) are those of
+// k_conv_gemm.
+template <int CO, bool VEC, bool VEC4>
+__global__ void __launch_bounds__(256) k_conv_narrow(ConvP p) {
+    extern __shared__ float ws[];  // [K][CO]
+    const int K = p.kh * p.kw * p.cin;
+    for (int i = threadIdx.x; i < K * CO; i += blockDim.x) {
+        const int k = i / CO, co = i - k * CO;
+        ws[i] = co < p.cout ? p.wt[(int64_t)k * p.ldw + co] : 0.f;
+    }
+    __syncthreads();
+    const int64_t M = (int64_t)p.n * p.oh * p.ow;
+    for (int64_t m = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; m < M; m += (int64_t)gridDim.x * blockDim.x) {
+        const int ox = (int)(m % p.ow);
+        const int64_t t = m / p.ow;
+        const int oy = (int)(t % p.oh), nb = (int)(t / p.oh);
+        float acc[CO];
+#pragma unroll
+        for (int co = 0; co < CO; co++) acc[co] = 0.f;
+        const float *xb = p.x + (int64_t)nb * p.x_n;
+        const float *scb = p.insc ? p.insc + (int64_t)nb * p.cin : nullptr;
+        for (int ky = 0; ky < p.kh; ky++) {
+            const int iy = oy * p.sh - p.pt + ky;
+            if (iy < 0 || iy >= p.h) continue;
+            for (int kx = 0; kx < p.kw; kx++) {
+                const int ix = ox * p.sw - p.pl + kx;
+                if (ix < 0 || ix >= p.w) continue;
+                const float *xp = xb + ((int64_t)iy * p.w + ix) * p.x_pix;
+                const float *wk = ws + (ky * p.kw + kx) * p.cin * CO;
+                if (VEC) {
+                    for (int ci = 0; ci < p.cin; ci += 4) {
+                        float4 v4 = *reinterpret_cast<const float4 *>(xp + ci);
+                        float v[4] = {v4.x, v4.y, v4.z, v4.w};
+                        if (scb) {
+#pragma unroll
+                            for (int e = 0; e < 4; e++) v[e] *= scb[ci + e];
+                        }
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const float4 *w4 = reinterpret_cast<const float4 *>(wk + (ci + e) * CO);
+#pragma unroll
+                            for (int q = 0; q < CO / 4; q++) {
+                                const float4 w = w4[q];
+                                acc[4 * q] += v[e] * w.x;
+                                acc[4 * q + 1] += v[e] * w.y;
+                                acc[4 * q + 2] += v[e] * w.z;
+                                acc[4 * q + 3] += v[e] * w.w;
+                            }
+                        }
+                    }
+                } else {
+                    for (int ci = 0; ci < p.cin; ci++) {
+                        float v = xp[ci];
+                        if (scb) v *= scb[ci];
+                        const float4 *w4 = reinterpret_cast<const float4 *>(wk + ci * CO);
+#pragma unroll
+                        for (int q = 0; q < CO / 4; q++) {
+                            const float4 w = w4[q];
+                            acc[4 * q] += v * w.x;
+                            acc[4 * q + 1] += v * w.y;
+                            acc[4 * q + 2] += v * w.z;
+                            acc[4 * q + 3] += v * w.w;
+                        }
+                    }
+                }
+            }
+        }
+        const int64_t pix = (int64_t)oy * p.ow + ox;
+        float *yp = p.y + (int64_t)nb * p.y_n + pix * p.y_pix;
+        const float *rp = p.res ? p.res + (int64_t)nb * p.res_n + pix * p.res_pix : nullptr;
+#pragma unroll
+        for (int co = 0; co < CO; co++) {
+            float v = act_f(acc[co] + (p.bias && co < p.cout ? p.bias[co] : 0.f), p.act);
+            if (rp && co < p.cout) v += rp[co];
+            acc[co] = v;
+        }
+        if (VEC4) {  // whole output pixels of 16-byte aligned float4s
+#pragma unroll
+            for (int q = 0; q < CO / 4; q++)
+                if (4 * q < p.cout)
+                    *reinterpret_cast<float4 *>(yp + 4 * q) =
+                        make_float4(acc[4 * q], acc[4 * q + 1], acc[4 * q + 2], acc[4 * q + 3]);
+        } else {
+#pragma unroll
+            for (int co = 0; co < CO; co++)
+                if (co < p.cout) yp[co] = acc[co];
+        }
+    }
+}
+
+template <int CO>
+void launch_narrow(Ctx *c, const ConvP &p, bool vec) {
+    const int K = p.kh * p.kw * p.cin;
+    const size_t smem = (size_t)K * CO * 4;
+    const int64_t M = (int64_t)p.n * p.oh * p.ow;
+    // a few blocks per SM, each over many pixels: the weights are staged once per block
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((M + 255) / 256, (int64_t)c->sm_count * 4));
+    const bool vec4 = p.cout % 4 == 0 && p.y_pix % 4 == 0 && p.y_n % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(p.y) & 15) == 0;
+    if (vec && vec4) k_conv_narrow<CO, true, true><<<grid, 256, smem, c->stream>>>(p);
+    else if (vec) k_conv_narrow<CO, true, false><<<grid, 256, smem, c->stream>>>(p);
+    else if (vec4) k_conv_narrow<CO, false, true><<<grid, 256, smem, c->stream>>>(p);
+    else k_conv_narrow<CO, false, false><<<grid, 256, smem, c->stream>>>(p);
+    WOCR_LAUNCHED(c);
+}
+
+bool conv_narrow_ok(const ConvP &p) {
+    const int K = p.kh * p.kw * p.cin;
+    const int co = p.cout <= 16 ? 16 : (p.cout <= 32 ? 32 : 64);  // the instance launch_narrow picks
+    return p.scatter == 0 && p.cout > 0 && p.cout <= 64 && (int64_t)K * p.cout <= kNarrowMacs &&
+           (int64_t)K * co * 4 <= 48 * 1024;
+}
+
+void conv_narrow(Ctx *c, const ConvP &p) {
+    const int64_t M = (int64_t)p.n * p.oh * p.ow;
+    if (M == 0) return;
+    Prof pf(c, "conv_narrow", 2.0 * (double)M * p.cout * p.kh * p.kw * p.cin,
+            4.0 * ((double)p.n * p.h * p.w * p.cin + (double)M * p.cout * (p.res ? 2 : 1)));
+    const bool vec = (p.cin % 4 == 0) && (p.x_pix % 4 == 0) && (p.x_n % 4 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0);
+    if (p.cout <= 16) launch_narrow<16>(c, p, vec);
+    else if (p.cout <= 32) launch_narrow<32>(c, p, vec);
+    else launch_narrow<64>(c, p, vec);
+    c->flops += 2.0 * (double)M * p.cout * p.kh * p.kw * p.cin;
+}
+
 void pointwise(Ctx *c, const void *x, int64_t x_n, int64_t x_pix, int64_t hw, int n, int cin, const float *wt, int ldw,
                const float *bias, int cout, int act, float *y, int64_t y_n, int64_t y_pix, int split_in) {
     const int64_t total = (int64_t)n * hw;

@@ -35,6 +35,11 @@ struct ConvP {
     int scat_cout = 0;
 };
 void conv_gemm(Ctx *c, const ConvP &p);
+// Narrow convolutions on CUDA cores (k_conv.cu): at most 64 output channels and kNarrowMacs
+// multiply-adds per output pixel; conv_narrow_ok says whether p qualifies.
+constexpr int kNarrowMacs = 4096;
+bool conv_narrow_ok(const ConvP &p);
+void conv_narrow(Ctx *c, const ConvP &p);
 
 // Cin = 1, stride 1 convolution with its activation and an optional fused MaxPool (ph, pw)
 // (K6, src/gpu.rs:385-422).  wt [kh][kw][cout]; output NHWC with pixel stride y_pix.
