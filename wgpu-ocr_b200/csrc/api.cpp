@@ -236,12 +236,20 @@ void check_status(Ctx *c) {
 }
 
 void wait_stream(Ctx *c) {
-    if (c->sync_ev) {
-        WOCR_CUDA(cudaEventRecord(c->sync_ev, c->stream));
-        WOCR_CUDA(cudaEventSynchronize(c->sync_ev));
-    } else {
+    if (!c->sync_ev) {
         WOCR_CUDA(cudaStreamSynchronize(c->stream));
+        return;
     }
+    // a short wait polls (a blocking wait's wake-up costs tens of microseconds), a long one
+    // sleeps on the event
+    WOCR_CUDA(cudaEventRecord(c->sync_ev, c->stream));
+    const auto t0 = std::chrono::steady_clock::now();
+    while (std::chrono::steady_clock::now() - t0 < std::chrono::microseconds(100)) {
+        const cudaError_t e = cudaEventQuery(c->sync_ev);
+        if (e == cudaSuccess) return;
+        if (e != cudaErrorNotReady) WOCR_CUDA(e);
+    }
+    WOCR_CUDA(cudaEventSynchronize(c->sync_ev));
 }
 
 void sync_bounded(Ctx *c, int timeout_ms) {

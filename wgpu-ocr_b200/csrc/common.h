@@ -88,9 +88,9 @@ struct Ctx {
     // device error word written by kernels whose bounded waits gave up (0 = fine)
     int *status = nullptr;
     std::shared_ptr<struct Buf> status_buf;
-    // unbounded waits block on this event (the host thread sleeps until the stream reaches it)
-    // instead of spinning: several contexts per GPU, each with its own host thread, share the
-    // host's cores with the other GPUs' processes
+    // unbounded waits poll this event briefly, then block on it (the host thread sleeps until
+    // the stream reaches it) instead of spinning: several contexts per GPU, each with its own
+    // host thread, share the host's cores with the other GPUs' processes
     cudaEvent_t sync_ev = nullptr;
 };
 
