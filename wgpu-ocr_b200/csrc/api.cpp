@@ -2087,10 +2087,22 @@ struct PpLane {
     wocr_ctx *ctx = nullptr;
     wocr_ndgraph *det = nullptr, *rec = nullptr;
     wocr_batch *batch = nullptr;
-    BufP page;  // a chunk of pages back to back on the device (the detection batch's input)
-    size_t page_bytes = 0;
+    // two chunk buffers (pages back to back: the detection batch's input): the next chunk's pages
+    // go up on the copy stream while the current chunk computes.  up[b]: chunk in b uploaded;
+    // freed[b]: the compute stream is done with b (and b's allocation is ordered before reuse)
+    BufP page[2];
+    size_t page_bytes[2] = {0, 0};
+    cudaStream_t copy = nullptr;
+    cudaEvent_t up[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr};
     BufP maps_tmp;  // the maps of a batch that ran without a captured graph
     ~PpLane() {
+        if (ctx) cudaStreamSynchronize(ctx->c.stream);
+        if (copy) {
+            cudaStreamSynchronize(copy);
+            cudaStreamDestroy(copy);
+        }
+        for (cudaEvent_t e : {up[0], up[1], freed[0], freed[1]})
+            if (e) cudaEventDestroy(e);
         if (batch) wocr_batch_destroy(batch);
         if (det) wocr_ndgraph_destroy(det);
         if (rec) wocr_ndgraph_destroy(rec);
@@ -2233,24 +2245,38 @@ const float *ppdet_batch(PpLane &ln, const uint8_t *d_pages, int n, int w, int h
 // The first half of a chunk of pages of one size: the pages gathered on the device (uploads
 // for host pages), their detection in one batch, the DB boxes of all their maps in the same
 // launches, each page's line cuts.
-void pp_front_chunk(PpLane &ln, const uint8_t *const *pages, const std::vector<int> &ks, int w, int h,
-                    const PpArgs &a, std::vector<PpPage> &out) {
+// The pages of a chunk into chunk buffer b on the lane's copy stream (after the compute stream is
+// done with b); up[b] marks their arrival.
+void pp_upload_chunk(PpLane &ln, int b, const uint8_t *const *pages, const std::vector<int> &ks, int w, int h,
+                     std::vector<PpPage> &out) {
     Ctx *c = &ln.ctx->c;
-    WOCR_CUDA(cudaSetDevice(c->device));
     const int n = (int)ks.size();
     const size_t bytes = (size_t)w * h * 3;
-    if (ln.page_bytes < bytes * n) {
-        ln.page = alloc(c, bytes * n);
-        ln.page_bytes = bytes * n;
+    if (ln.page_bytes[b] < bytes * n) {
+        ln.page[b] = alloc(c, bytes * n);
+        ln.page_bytes[b] = bytes * n;
     }
-    uint8_t *dp = (uint8_t *)ln.page->p;
+    WOCR_CUDA(cudaEventRecord(ln.freed[b], c->stream));
+    WOCR_CUDA(cudaStreamWaitEvent(ln.copy, ln.freed[b], 0));
+    uint8_t *dp = (uint8_t *)ln.page[b]->p;
     for (int q = 0; q < n; q++) {
         const uint8_t *src = pages[ks[q]];
         const bool dev = on_device(src);
         WOCR_CUDA(cudaMemcpyAsync(dp + bytes * q, src, bytes, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
-                                  c->stream));
+                                  ln.copy));
         if (!dev) out[ks[q]].h2d += (int64_t)bytes;
     }
+    WOCR_CUDA(cudaEventRecord(ln.up[b], ln.copy));
+}
+
+void pp_front_chunk(PpLane &ln, int buf, const std::vector<int> &ks, int w, int h, const PpArgs &a,
+                    std::vector<PpPage> &out) {
+    Ctx *c = &ln.ctx->c;
+    WOCR_CUDA(cudaSetDevice(c->device));
+    const int n = (int)ks.size();
+    const size_t bytes = (size_t)w * h * 3;
+    WOCR_CUDA(cudaStreamWaitEvent(c->stream, ln.up[buf], 0));
+    const uint8_t *dp = (const uint8_t *)ln.page[buf]->p;
     int mw = 0, mh = 0, ow = 0, oh = 0;
     const float *maps = ppdet_batch(ln, dp, n, w, h, a.max_side, &mw, &mh);
     det_input_sizes(w, h, a.max_side, &ow, &oh);
@@ -2364,6 +2390,12 @@ PpLane *pp_lane(wocr_pp *p, int i) {
         ln->det = ndgraph_from_model(ln->ctx, p->det_m, false);
         ln->rec = ndgraph_from_model(ln->ctx, p->rec_m, true);
         check_st(wocr_batch_create(ln->ctx, &ln->batch));
+        WOCR_CUDA(cudaSetDevice(ln->ctx->c.device));
+        WOCR_CUDA(cudaStreamCreateWithFlags(&ln->copy, cudaStreamNonBlocking));
+        for (int b = 0; b < 2; b++) {
+            WOCR_CUDA(cudaEventCreateWithFlags(&ln->up[b], cudaEventDisableTiming));
+            WOCR_CUDA(cudaEventCreateWithFlags(&ln->freed[b], cudaEventDisableTiming));
+        }
         p->lanes.push_back(std::move(ln));
     }
     return p->lanes[i].get();
@@ -2382,20 +2414,28 @@ void pp_run(wocr_pp *p, const uint8_t *const *pages, const int32_t *w, const int
             PpLane &ln = *p->lanes[L];
             WOCR_CUDA(cudaSetDevice(ln.ctx->c.device));
             // chunks: up to `merge` of this lane's pages in a row of one size, detected in one batch
-            // and recognised with one wait
-            std::vector<int> ks;
+            // and recognised with one wait; chunk j + 1 uploads while chunk j computes
+            std::vector<std::vector<int>> chunks(1);
             for (int k = L; k < n; k += lanes) {
-                ks.push_back(k);
+                chunks.back().push_back(k);
                 const int nx = k + lanes;
-                const bool last = nx >= n || (int)ks.size() >= merge || w[nx] != w[k] || h[nx] != h[k];
-                if (!last) continue;
-                pp_front_chunk(ln, pages, ks, w[k], h[k], a, out);
+                const bool last = nx >= n || (int)chunks.back().size() >= merge || w[nx] != w[k] || h[nx] != h[k];
+                if (last && nx < n) chunks.emplace_back();
+            }
+            if (chunks.back().empty()) chunks.pop_back();
+            if (!chunks.empty()) pp_upload_chunk(ln, 0, pages, chunks[0], w[chunks[0][0]], h[chunks[0][0]], out);
+            for (size_t j = 0; j < chunks.size(); j++) {
+                const std::vector<int> &ks = chunks[j];
+                if (j + 1 < chunks.size()) {
+                    const std::vector<int> &nk = chunks[j + 1];
+                    pp_upload_chunk(ln, (int)((j + 1) & 1), pages, nk, w[nk[0]], h[nk[0]], out);
+                }
+                pp_front_chunk(ln, (int)(j & 1), ks, w[ks[0]], h[ks[0]], a, out);
                 if (a.want_rec) {
                     std::vector<PpPage *> held;
                     for (int q : ks) held.push_back(&out[q]);
                     pp_recognize(ln, held);
                 }
-                ks.clear();
             }
         } catch (...) {
             errs[L] = std::current_exception();

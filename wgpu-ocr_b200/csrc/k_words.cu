@@ -183,9 +183,85 @@ __device__ __forceinline__ int run_end(const int *run_x, int r, int row_end, int
     return r + 1 < row_end ? run_x[r + 1] - 1 : w - 1;
 }
 
-__global__ void k_uf_union(const int *__restrict__ run_x, const uint8_t *__restrict__ run_c,
+// Band-local union-find: block b takes the runs of rows [b kBandRows, (b + 1) kBandRows).  Their
+// unions with runs of the band's own rows happen in shared memory (local indices, smaller root
+// wins), then every run's global parent is its band-local root.  Unions that leave the band (a
+// band's first row with the row above, background runs touching the page frame) are left to
+// k_uf_cross, after every band has written its parents.  Linking always points a root to a
+// smaller index, so whatever the order of the unions, a component's final root is its smallest
+// node.  A band with more than kBandRuns runs writes P[r] = r and leaves all of its unions to
+// k_uf_cross.
+constexpr int kBandRows = 16, kBandRuns = 8192;
+
+__device__ __forceinline__ int band_find(int *L, int x) {
+    for (;;) {
+        const int p = L[x];
+        if (p == x) return x;
+        const int g = L[p];
+        if (g != p) L[x] = g;
+        x = p;
+    }
+}
+
+__device__ __forceinline__ void band_unite(int *L, int a, int b) {
+    a = band_find(L, a);
+    b = band_find(L, b);
+    while (a != b) {
+        if (a > b) {
+            const int t = a;
+            a = b;
+            b = t;
+        }
+        const int old = atomicCAS(L + b, b, a);
+        if (old == b) return;
+        b = band_find(L, old);
+        a = band_find(L, a);
+    }
+}
+
+__global__ void __launch_bounds__(512) k_uf_band(const int *__restrict__ run_x, const uint8_t *__restrict__ run_c,
+                                                 const int *__restrict__ off, const int *__restrict__ cnt, int rows,
+                                                 int w, int h, int pages, int *__restrict__ P, int *__restrict__ big) {
+    __shared__ int L[kBandRuns];
+    const int row0 = blockIdx.x * kBandRows, row1 = min(rows, row0 + kBandRows);
+    const int r0 = off[row0], r1 = off[row1 - 1] + cnt[row1 - 1], nr = r1 - r0;
+    if (nr > kBandRuns) {  // too many runs for shared memory: k_uf_union unites these rows
+        for (int i = threadIdx.x; i < nr; i += blockDim.x) P[pages + r0 + i] = pages + r0 + i;
+        if (threadIdx.x == 0) big[blockIdx.x] = 1;
+        return;
+    }
+    if (threadIdx.x == 0) big[blockIdx.x] = 0;
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) L[i] = i;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) {
+        const int r = r0 + i;
+        // this run's row: the last band row whose first run is at or before r
+        int row = row0;
+        while (row + 1 < row1 && off[row + 1] <= r) row++;
+        if (row == row0 || row % h == 0) continue;  // the row above is another band's (or page's)
+        const int a = run_x[r], c = run_c[r], b = run_end(run_x, r, off[row] + cnt[row], w);
+        const int q0 = off[row - 1], q1 = q0 + cnt[row - 1];
+        const int lo = c ? max(a - 1, 0) : a, hi = c ? min(b + 1, w - 1) : b;
+        int l = q0, u = q1 - 1;  // the last run of the row above starting at or before lo
+        while (l < u) {
+            const int mid = (l + u + 1) >> 1;
+            if (run_x[mid] <= lo)
+                l = mid;
+            else
+                u = mid - 1;
+        }
+        for (int q = l; q < q1 && run_x[q] <= hi; q++)
+            if (run_c[q] == c) band_unite(L, i, q - r0);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr; i += blockDim.x) P[pages + r0 + i] = pages + r0 + band_find(L, i);
+}
+
+// The unions k_uf_band left: a band's first row with the row above, background runs on the page's
+// edge with the frame node, and every union of an oversized band's runs.
+__global__ void k_uf_cross(const int *__restrict__ run_x, const uint8_t *__restrict__ run_c,
                            const int *__restrict__ run_row, const int *__restrict__ off, const int *__restrict__ cnt,
-                           int R, int w, int h, int pages, int *P) {
+                           int R, int w, int h, int pages, const int *__restrict__ big, int *P) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= R) return;
     const int row = run_row[r], y = row % h, page = row / h;
@@ -193,9 +269,10 @@ __global__ void k_uf_union(const int *__restrict__ run_x, const uint8_t *__restr
     const int node = pages + r;
     if (!c && (y == 0 || y == h - 1 || a == 0 || b == w - 1)) uf_unite(P, node, page);
     if (y == 0) return;
+    if (row % kBandRows != 0 && !big[row / kBandRows]) return;  // united inside its band
     const int q0 = off[row - 1], q1 = q0 + cnt[row - 1];
     const int lo = c ? max(a - 1, 0) : a, hi = c ? min(b + 1, w - 1) : b;
-    int l = q0, u = q1 - 1;  // the last run of the row above starting at or before lo
+    int l = q0, u = q1 - 1;
     while (l < u) {
         const int mid = (l + u + 1) >> 1;
         if (run_x[mid] <= lo)
@@ -828,9 +905,14 @@ WordRects word_rects(Ctx *c, const uint32_t *mask, int pages, int w, int h, floa
     }
     {
         Prof pf(c, "word_label", 0, (double)R * 30);
-        k_uf_init<<<blocks(R + pages, 256), 256, 0, c->stream>>>(P, R + pages);
+        const int bands = (rows + kBandRows - 1) / kBandRows;
+        BufP bigb = alloc(c, (size_t)bands * 4);
+        k_uf_init<<<blocks(pages, 256), 256, 0, c->stream>>>(P, pages);  // the frame nodes
         WOCR_LAUNCHED(c);
-        k_uf_union<<<blocks(R, 256), 256, 0, c->stream>>>(run_x, run_c, run_row, d_off, d_cnt, R, w, h, pages, P);
+        k_uf_band<<<bands, 512, 0, c->stream>>>(run_x, run_c, d_off, d_cnt, rows, w, h, pages, P, (int *)bigb->p);
+        WOCR_LAUNCHED(c);
+        k_uf_cross<<<blocks(R, 256), 256, 0, c->stream>>>(run_x, run_c, run_row, d_off, d_cnt, R, w, h, pages,
+                                                          (const int *)bigb->p, P);
         WOCR_LAUNCHED(c);
         k_uf_flatten<<<blocks(R + pages, 256), 256, 0, c->stream>>>(P, R + pages);
         WOCR_LAUNCHED(c);
