@@ -57,7 +57,9 @@ struct Layout {
     static constexpr int stage_bytes = 2 * Smem::a_bytes + 2 * b_bytes;
     static constexpr int bar_off = STAGES * stage_bytes;
     static constexpr int tab_off = bar_off + 1024;   // barriers and tmem slot first
-    static constexpr int total = tab_off + 4 * kTapTable + 1024;  // + tap table + alignment slack
+    // per epilogue warp, two tiles' bias columns (each warp stages its own: no cross-warp barrier)
+    static constexpr int ebias_off = tab_off + 4 * kTapTable;
+    static constexpr int total = ebias_off + 4 * 2 * BN * 4 + 1024;  // + alignment slack
 };
 
 // The fp32 source of one row of A (an output pixel of a convolution, or a row of x).
@@ -362,13 +364,23 @@ __global__ void __launch_bounds__(kAllThreads, 1)
         // ---------------- epilogue: warps 16-19, TMEM lanes 32 * (warp % 4) ----------------
         const int q = warp & 3;
         const int row = q * 32 + lane;
+        float *ebias = reinterpret_cast<float *>(smem + Lay::ebias_off) + q * 2 * BN;
         int lt = 0;
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
             const int ab = lt % NACC;
-            if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 15)) break;
-            tc_fence_after();
             const int64_t m = (t / ntn) * BM + row;
             const int n0 = (int)(t % ntn) * BN;
+            // the tile's bias columns (scatter tiles: per output channel) into this warp's slot while
+            // the MMAs run, so no chunk below waits on a global load
+            float *eb = ebias + (lt & 1) * BN;
+            for (int j = lane; j < BN; j += 32) {
+                const int col = n0 + j;
+                const int bc = p.scatter ? col % p.scat_cout : col;
+                eb[j] = p.bias && col < p.N ? p.bias[bc] : 0.f;
+            }
+            __syncwarp();
+            if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 15)) break;
+            tc_fence_after();
             int ox = 0, oy = 0, nb = 0;
             int64_t pix = 0;
             if (p.mode == 1 && m < p.M) {
@@ -381,17 +393,43 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             }
             float amx = -INFINITY, asum = 0.f;  // arg-max partials of this row over the tile
             uint32_t aidx = 0;
+            const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS;
+            // one chain: the next chunk's load is in flight while this one is processed (not for
+            // 32-column tiles, two chunks, where the registers it holds spill); more chains: a
+            // chunk's chains two loads per wait, summed in chain order
+            constexpr bool kAhead = NCH == 1 && BN >= 64;
+            uint32_t nx[16];
+            if (kAhead) tmem_ld16_async(trow, nx);
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 16) {
                 float v[16];
-                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS + c0;
-                tmem_ld16(tbase, v);
-#pragma unroll 1
-                for (int ch = 1; ch < NCH; ch++) {
-                    float w[16];
-                    tmem_ld16(tbase + ch * BN, w);
+                const uint32_t tbase = trow + c0;
+                if (kAhead) {
+                    tmem_wait16(nx);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] += w[j];
+                    for (int j = 0; j < 16; j++) v[j] = __uint_as_float(nx[j]);
+                    if (c0 + 16 < BN) tmem_ld16_async(tbase + 16, nx);
+                } else if (NCH == 1) {
+                    tmem_ld16(tbase, v);
+                } else {
+                    uint32_t a[16], b[16];
+                    tmem_ld16_async(tbase, a);
+                    tmem_ld16_async(tbase + BN, b);
+                    tmem_wait16x2(a, b);
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = __uint_as_float(a[j]) + __uint_as_float(b[j]);
+#pragma unroll 1
+                    for (int ch = 2; ch < NCH; ch += 2) {
+                        tmem_ld16_async(tbase + ch * BN, a);
+                        if (ch + 1 < NCH) tmem_ld16_async(tbase + (ch + 1) * BN, b);
+                        tmem_wait16x2(a, b);
+#pragma unroll
+                        for (int j = 0; j < 16; j++) v[j] += __uint_as_float(a[j]);
+                        if (ch + 1 < NCH) {
+#pragma unroll
+                            for (int j = 0; j < 16; j++) v[j] += __uint_as_float(b[j]);
+                        }
+                    }
                 }
                 if (m >= p.M || n0 + c0 >= p.N) continue;
                 if (p.part_max) {
@@ -404,7 +442,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int col = n0 + c0 + j;
-                        o[j] = col < p.N ? v[j] + (p.bias ? p.bias[col] : 0.f) : -INFINITY;
+                        o[j] = col < p.N ? v[j] + eb[c0 + j] : -INFINITY;
                     }
                     float cm = o[0];
                     uint32_t ci = (uint32_t)(n0 + c0);
@@ -432,7 +470,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     const int yy = oy * s + tap / s, xx = ox * s + tap % s;
                     float *dst = p.y + (int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co0;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] = act_f(v[j] + (p.bias ? p.bias[co0 + j] : 0.f), p.act);
+                    for (int j = 0; j < 16; j++) v[j] = act_f(v[j] + eb[c0 + j], p.act);
                     if (p.out_vec) {
                         float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
@@ -452,7 +490,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                         if (col >= p.N) break;
                         const int co = col % p.scat_cout, tap = col / p.scat_cout;
                         const int yy = oy * s + tap / s, xx = ox * s + tap % s;
-                        float o = act_f(v[j] + (p.bias ? p.bias[co] : 0.f), p.act);
+                        float o = act_f(v[j] + eb[c0 + j], p.act);
                         p.y[(int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co] = o;
                     }
                     continue;
@@ -465,10 +503,9 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 } else {
                     dst = p.y + m * p.ldy + n0 + c0;
                 }
-                const float *bsrc = p.bias ? p.bias + n0 + c0 : nullptr;
 #pragma unroll
                 for (int j = 0; j < 16; j++) {
-                    float o = act_f(v[j] + (bsrc && n0 + c0 + j < p.N ? bsrc[j] : 0.f), p.act);
+                    float o = act_f(v[j] + eb[c0 + j], p.act);
                     if (rsrc && n0 + c0 + j < p.N) o += rsrc[j];
                     v[j] = o;
                 }
