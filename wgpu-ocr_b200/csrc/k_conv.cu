@@ -6,30 +6,13 @@
 
 #include <type_traits>
 
+#include "act.h"
 #include "kernels.h"
 
 namespace wocr {
 namespace k {
 
 namespace {
-
-__device__ __forceinline__ float erf_as(float v) {
-    float s = (v > 0.f) - (v < 0.f);
-    float a = fabsf(v);
-    float t = 1.0f / (1.0f + 0.3275911f * a);
-    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-    return s * (1.0f - poly * expf(-a * a));
-}
-
-__device__ __forceinline__ float act_f(float v, int act) {
-    switch (act) {
-    case 1: return fmaxf(v, 0.f);
-    case 2: return 1.0f / (1.0f + expf(-v));
-    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
-    case 4: return v / (1.0f + expf(-v));
-    default: return v;
-    }
-}
 
 constexpr int BM = 128, BN = 64, BK = 16;
 
@@ -229,8 +212,9 @@ __global__ void k_conv_direct(const float *__restrict__ x, int64_t x_n, int64_t 
                         for (int c = 0; c < COUT; c++) acc[c] += v * wr[c];
                     }
                 }
+                act_n(acc, act);
 #pragma unroll
-                for (int c = 0; c < COUT; c++) best[c] = fmaxf(best[c], act_f(acc[c], act));
+                for (int c = 0; c < COUT; c++) best[c] = fmaxf(best[c], acc[c]);
             }
         const int64_t off = nb * y_n + ((int64_t)oy * ow + ox) * y_pix;
         if (SPLIT) {
@@ -302,8 +286,7 @@ __global__ void __launch_bounds__(256) k_conv3_cin1(const float *__restrict__ x,
                     acc[4 * c4 + 3] += v * q.w;
                 }
             }
-#pragma unroll
-        for (int c = 0; c < COUT; c++) acc[c] = act_f(acc[c], act);
+        act_n(acc, act);
         int oy = cy0 + ty, ox = cx0 + tx;
         bool store = oy < ch && ox < cw;
         if (POOL == 2) {
@@ -517,9 +500,10 @@ __global__ void k_pointwise(const void *__restrict__ xv, int64_t x_n, int64_t x_
             }
         }
         float *yp = y + nb * y_n + pix * y_pix;
+        act_n(acc, act);
 #pragma unroll
         for (int co = 0; co < COUT; co++)
-            if (co < cout) yp[co] = act_f(acc[co], act);
+            if (co < cout) yp[co] = acc[co];
     }
 }
 
@@ -624,10 +608,12 @@ __global__ void __launch_bounds__(256) k_conv_narrow(ConvP p) {
         float *yp = p.y + (int64_t)nb * p.y_n + pix * p.y_pix;
         const float *rp = p.res ? p.res + (int64_t)nb * p.res_n + pix * p.res_pix : nullptr;
 #pragma unroll
-        for (int co = 0; co < CO; co++) {
-            float v = act_f(acc[co] + (p.bias && co < p.cout ? p.bias[co] : 0.f), p.act);
-            if (rp && co < p.cout) v += rp[co];
-            acc[co] = v;
+        for (int co = 0; co < CO; co++) acc[co] += p.bias && co < p.cout ? p.bias[co] : 0.f;
+        act_n(acc, p.act);
+        if (rp) {
+#pragma unroll
+            for (int co = 0; co < CO; co++)
+                if (co < p.cout) acc[co] += rp[co];
         }
         if (VEC4) {  // whole output pixels of 16-byte aligned float4s
 #pragma unroll

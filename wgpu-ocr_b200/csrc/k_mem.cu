@@ -8,6 +8,7 @@
 #include <cfloat>
 #include <cmath>
 
+#include "act.h"
 #include "kernels.h"
 
 namespace wocr {
@@ -23,25 +24,6 @@ inline int grid_for(Ctx *c, int64_t work, int per_block = kThreads) {
     if (g > cap) g = cap;
     if (g < 1) g = 1;
     return (int)g;
-}
-
-// Abramowitz & Stegun 7.1.26, the erf of the reference's epilogue (src/gpu.rs:19-27).
-__device__ __forceinline__ float erf_as(float v) {
-    float s = (v > 0.f) - (v < 0.f);
-    float a = fabsf(v);
-    float t = 1.0f / (1.0f + 0.3275911f * a);
-    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-    return s * (1.0f - poly * expf(-a * a));
-}
-
-__device__ __forceinline__ float act_f(float v, int act) {
-    switch (act) {
-    case 1: return fmaxf(v, 0.f);
-    case 2: return 1.0f / (1.0f + expf(-v));
-    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
-    case 4: return v / (1.0f + expf(-v));
-    default: return v;
-    }
 }
 
 // WGSL mix(a, b, t) = a * (1 - t) + b * t.

@@ -97,17 +97,6 @@ __device__ __forceinline__ Tile decode(const TcP &p, int t) {
     return r;
 }
 
-// activation of 16 values (uniform branch on the code)
-__device__ __forceinline__ void act16(float (&v)[16], int act) {
-    if (act == 0) return;
-    if (act == 1) {
-#pragma unroll
-        for (int j = 0; j < 16; j++) v[j] = fmaxf(v[j], 0.f);
-        return;
-    }
-#pragma unroll
-    for (int j = 0; j < 16; j++) v[j] = act_f(v[j], act);
-}
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(src_bytes)
@@ -555,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // lane stores the maximum
 #pragma unroll
                     for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[col + jj];
-                    act16(v, p.act);
+                    act_n(v, p.act);
                     const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)oy * p.ow_out + ox) * p.y_pix + col;
                     if (p.stg_off) store16_t(p, off, valid, v, stg, lane);
                     else if (valid) store16(p, off, v);
@@ -585,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
 #pragma unroll
                     for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[b0 + jj];
-                    act16(v, p.act);
+                    act_n(v, p.act);
                     store16_t(p, off, valid, v, stg, lane);
                     continue;
                 }
@@ -598,16 +587,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const int yy = oy * sc + tap / sc, xx = ox * sc + tap % sc;
 #pragma unroll
                         for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[co0 + jj];
-                        act16(v, p.act);
+                        act_n(v, p.act);
                         store16(p, (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + co0, v);
                     } else {
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj++) {
+                            const int cc = col + jj < p.N ? col + jj : p.N - 1;
+                            v[jj] += bias_s[cc - cc / p.scat_cout * p.scat_cout];
+                        }
+                        act_n(v, p.act);
 #pragma unroll
                         for (int jj = 0; jj < 16; jj++) {
                             if (col + jj >= p.N) continue;
                             const int cc = col + jj, tap = cc / p.scat_cout, co = cc - tap * p.scat_cout;
                             const int yy = oy * sc + tap / sc, xx = ox * sc + tap % sc;
-                            store1(p, (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + co,
-                                   act_f(v[jj] + bias_s[co], p.act));
+                            store1(p, (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + co, v[jj]);
                         }
                     }
                     continue;
@@ -616,12 +610,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (col + 16 <= p.N) {
 #pragma unroll
                     for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[col + jj];
-                    act16(v, p.act);
+                    act_n(v, p.act);
                     store16(p, off, v);
                 } else {
 #pragma unroll
+                    for (int jj = 0; jj < 16; jj++) v[jj] += col + jj < p.N ? bias_s[col + jj] : 0.f;
+                    act_n(v, p.act);
+#pragma unroll
                     for (int jj = 0; jj < 16; jj++)
-                        if (col + jj < p.N) store1(p, off + jj, act_f(v[jj] + bias_s[col + jj], p.act));
+                        if (col + jj < p.N) store1(p, off + jj, v[jj]);
                 }
             }
             tc_fence_before();
@@ -908,7 +905,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
                         if (c0 >= p.scat_cout) continue;  // padding columns
 #pragma unroll
                         for (int jj = 0; jj < 16; jj++) v[jj] += bias_s[c0 + jj];
-                        act16(v, p.act);
+                        act_n(v, p.act);
                         const int yy = 2 * iy + (tp >> 1), xx = 2 * ix + (tp & 1);
                         const int64_t off = (int64_t)tl.nb * p.y_n + ((int64_t)yy * p.ow_out + xx) * p.y_pix + c0;
                         if (p.stg_off && c0 + 16 <= p.scat_cout) {
@@ -954,7 +951,7 @@ __global__ void __launch_bounds__(kRThreads, 1)
                     v[jj] = o.x;
                     v[jj + 1] = o.y;
                 }
-                act16(v, p.act);
+                act_n(v, p.act);
                 if (p.head_y) {
                     // the 1 x 1 head, channels in order as k_pointwise sums them; no output stored
 #pragma unroll

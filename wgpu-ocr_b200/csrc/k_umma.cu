@@ -470,7 +470,8 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     const int yy = oy * s + tap / s, xx = ox * s + tap % s;
                     float *dst = p.y + (int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co0;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] = act_f(v[j] + eb[c0 + j], p.act);
+                    for (int j = 0; j < 16; j++) v[j] += eb[c0 + j];
+                    act_n(v, p.act);
                     if (p.out_vec) {
                         float4 *d4 = reinterpret_cast<float4 *>(dst);
 #pragma unroll
@@ -485,13 +486,15 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 if (p.scatter) {
                     const int s = p.scatter;
 #pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] += eb[c0 + j];
+                    act_n(v, p.act);
+#pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int col = n0 + c0 + j;
                         if (col >= p.N) break;
                         const int co = col % p.scat_cout, tap = col / p.scat_cout;
                         const int yy = oy * s + tap / s, xx = ox * s + tap % s;
-                        float o = act_f(v[j] + eb[c0 + j], p.act);
-                        p.y[(int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co] = o;
+                        p.y[(int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co] = v[j];
                     }
                     continue;
                 }
@@ -504,10 +507,12 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     dst = p.y + m * p.ldy + n0 + c0;
                 }
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    float o = act_f(v[j] + eb[c0 + j], p.act);
-                    if (rsrc && n0 + c0 + j < p.N) o += rsrc[j];
-                    v[j] = o;
+                for (int j = 0; j < 16; j++) v[j] += eb[c0 + j];
+                act_n(v, p.act);
+                if (rsrc) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (n0 + c0 + j < p.N) v[j] += rsrc[j];
                 }
                 const bool full = n0 + c0 + 16 <= p.N && p.out_vec;
                 if (full) {

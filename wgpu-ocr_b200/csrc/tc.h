@@ -1,6 +1,6 @@
 // Device helpers shared by the tcgen05 kernels (k_umma.cu, k_tconv.cu): mbarriers with bounded
-// waits, TMA loads, shared-memory matrix descriptors, tcgen05.mma / commit / ld, the epilogue
-// activations and the bf16 hi/lo split.  All inline PTX for sm_100a.
+// waits, TMA loads, shared-memory matrix descriptors, tcgen05.mma / commit / ld, the bf16 hi/lo
+// split (the epilogue activations are in act.h).  All inline PTX for sm_100a.
 #pragma once
 
 #include <cuda.h>
@@ -9,6 +9,8 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+
+#include "act.h"
 
 namespace wocr {
 namespace k {
@@ -282,24 +284,6 @@ __device__ __forceinline__ void tmem_ld16_sum4(uint32_t a0, uint32_t a1, uint32_
     tmem_ld16_sum2(a2, a3, w);
 #pragma unroll
     for (int i = 0; i < 16; i++) v[i] = u[i] + w[i];
-}
-
-__device__ __forceinline__ float erf_as(float v) {
-    float s = (v > 0.f) - (v < 0.f);
-    float a = fabsf(v);
-    float t = 1.0f / (1.0f + 0.3275911f * a);
-    float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t + 0.254829592f) * t;
-    return s * (1.0f - poly * expf(-a * a));
-}
-
-__device__ __forceinline__ float act_f(float v, int act) {
-    switch (act) {
-    case 1: return fmaxf(v, 0.f);
-    case 2: return 1.0f / (1.0f + expf(-v));
-    case 3: return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
-    case 4: return v / (1.0f + expf(-v));
-    default: return v;
-    }
 }
 
 // Split 8 fp32 values into bf16 hi and lo parts, packed 2 per word.
