@@ -28,6 +28,7 @@ from __future__ import annotations
 
 import argparse
 import json
+from concurrent.futures import ThreadPoolExecutor
 import os
 import sys
 import threading
@@ -59,7 +60,9 @@ def parse():
                         "pp3 / ppdet4: configs 0, 3 and 4 through their public calls; ppdb4: config 4 with the DB "
                         "mask and box scores on the device; pplines: PP line extraction; words1: word rectangles "
                         "of config 1 detection masks (secondary measurements)")
-    p.add_argument("--lanes", type=int, default=4, help="page-pipeline workers per GPU (pp4, pp4ink)")
+    p.add_argument("--lanes", type=int, default=4,
+                   help="workers per GPU: page-pipeline lanes (pp4, pp4ink, ocrs2, ocrs2ink); contexts with a "
+                        "host thread each over the width batches (pp3)")
     p.add_argument("--merge", type=int, default=3, help="pages whose recognitions a lane runs together")
     p.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample length (pp4, pp4ink)")
     return p.parse_args()
@@ -654,6 +657,14 @@ def run_workload(args):
         out[...] = a
         return out
 
+    serial_step = None  # the one-lane step the per-kernel profile runs (default: step)
+
+    def lane_launches():
+        return 0
+
+    def close_lanes():
+        pass
+
     if args.workload == "rec0":
         model = synth.ocrs_rec_model()
         batches, _, _ = synth.ocrs_batches(synth.ocrs_lines(0, n=64))
@@ -678,15 +689,48 @@ def run_workload(args):
         batches, _ = synth.pp_batches(synth.pp_lines(2, n=256))
         batches = [(pinned(np.ascontiguousarray(d, np.float32)), n, w) for d, n, w in batches]
         handle = wocr.NdGraph(gpu, model, stop_before_softmax=True)
+        # lanes: more contexts (each its own stream and graph), a host thread each; the width
+        # batches go to the least loaded lane, widest first (a batch's cost ~ lines x width)
+        L = max(1, args.lanes)
+        lane_gpus = [wocr.Gpu(lines=8, device=local) for _ in range(L - 1)]
+        lane_handles = [handle] + [wocr.NdGraph(g_, model, stop_before_softmax=True) for g_ in lane_gpus]
+        plan, load = [[] for _ in range(L)], [0] * L
+        for i in sorted(range(len(batches)), key=lambda i: -batches[i][1] * batches[i][2]):
+            k_ = load.index(min(load))
+            plan[k_].append(i)
+            load[k_] += batches[i][1] * batches[i][2]
+        pool = ThreadPoolExecutor(L) if L > 1 else None
         units, unit, workload = 256, "lines/s", ("config 3: PP-OCRv6-style recognition, 256 lines 3x48xW "
                                                  "(W ~ U{96..1280}), trunk + 2 SVTR blocks + CTC head 120->18709, "
-                                                 "seed 2, arg-max per step")
+                                                 f"seed 2, arg-max per step; {len(batches)} width batches over {L} "
+                                                 "lane(s) (a context and a host thread each)")
         h2d = sum(b[0].nbytes for b in batches)
         d2h = sum(b[1] * (b[2] // 8) * 12 for b in batches)
 
+        def run_lane(k_):
+            for i in plan[k_]:
+                lane_handles[k_].argmax(batches[i][0])
+
         def step():
+            if pool is None:
+                run_lane(0)
+            else:
+                list(pool.map(run_lane, range(L)))
+
+        def serial_step():
             for data, _, _ in batches:
                 handle.argmax(data)
+
+        def lane_launches():
+            return sum(g_.launches() for g_ in lane_gpus)
+
+        def close_lanes():
+            if pool is not None:
+                pool.shutdown()
+            for h_ in lane_handles[1:]:
+                h_.close()
+            for g_ in lane_gpus:
+                g_.close()
 
         def cpu():
             data, n, _ = batches[0]
@@ -781,18 +825,20 @@ def run_workload(args):
         step()
     gpu.submit_wait()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    l0 = gpu.launches()
+    l0 = gpu.launches() + lane_launches()
     e0.record(stream)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
+    # every lane's calls have returned (they wait for their results): the context stream's event
+    # closes the region
     e1.record(stream)
     e1.synchronize()
     wall = time.perf_counter() - t0
-    launches = gpu.launches() - l0
+    launches = gpu.launches() + lane_launches() - l0
     ms = e0.elapsed_time(e1)
     gpu.profile(True)
-    step()
+    (serial_step or step)()
     rep = gpu.profile_report()
     gpu.profile(False)
     total_ms = sum(r["ms"] for r in rep) or 1.0
@@ -815,6 +861,7 @@ def run_workload(args):
                 "kernels": {r["kernel"]: {"launches": r["launches"], "ms_per_step": r["ms"],
                                           "share": r["ms"] / total_ms} for r in rep}}
         print(json.dumps(line), flush=True)
+    close_lanes()
     if handle is not None:
         handle.close()
     for p in held:

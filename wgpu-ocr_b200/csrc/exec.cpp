@@ -948,7 +948,8 @@ DT Executor::run_to(const DT &x, int upto) {
 bool Executor::ends_in_linear() const {
     if (steps.empty()) return false;
     const Step &s = steps.back();
-    return s.kind == Step::N_LINEAR && s.act == 0 && s.luw && s.output == output;
+    // the fused arg-max epilogue exists for tiles of 64 columns or more (more than 32 classes)
+    return s.kind == Step::N_LINEAR && s.act == 0 && s.luw && s.luw->bn >= 64 && s.output == output;
 }
 
 // The final linear layer with the row arg-max in its epilogue: per N tile partials, then one
@@ -960,7 +961,7 @@ std::vector<int64_t> Executor::linear_argmax(const DT &xin, uint32_t *best, floa
                                  std::to_string(s.ln) + "]");
     DT x = to_rowmajor(ctx, xin);
     const int64_t M = x.numel() / s.lk;
-    const int ntn = k::umma_ntiles(*s.luw);
+    const int ntn = k::umma_part_slots(*s.luw);
     BufP pm = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4), ps = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4),
          pi = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4);
     k::UmmaP u;

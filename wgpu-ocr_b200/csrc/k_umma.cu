@@ -24,6 +24,7 @@
 // the kernel records an error code in `status`, drains its own TMA loads and MMAs, frees its
 // tensor memory and returns.
 #include <atomic>
+#include <cstdlib>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -44,6 +45,7 @@ namespace {
 
 constexpr int BK = 64;
 constexpr int kTapTable = 1024;  // 8-wide k chunks described in shared memory (K <= 8192)
+constexpr int kEpiWarps = 8;      // epilogue warps: two per TMEM lane quadrant
 using namespace tc;
 
 struct Smem {
@@ -57,9 +59,15 @@ struct Layout {
     static constexpr int stage_bytes = 2 * Smem::a_bytes + 2 * b_bytes;
     static constexpr int bar_off = STAGES * stage_bytes;
     static constexpr int tab_off = bar_off + 1024;   // barriers and tmem slot first
-    // per epilogue warp, two tiles' bias columns (each warp stages its own: no cross-warp barrier)
+    // per epilogue warp, two tiles' bias columns of its half (each warp stages its own: no
+    // cross-warp barrier)
+    static constexpr int ecols = (BN / 16 + 1) / 2 * 16;
     static constexpr int ebias_off = tab_off + 4 * kTapTable;
-    static constexpr int total = ebias_off + 4 * 2 * BN * 4 + 1024;  // + alignment slack
+    // per epilogue warp, a 32-row x 16-column output chunk for the TMA tensor store (64-byte
+    // swizzle; 1024-byte aligned like every region above)
+    static constexpr int ystage_off = ebias_off + kEpiWarps * 2 * ecols * 4;
+    static constexpr int total = ystage_off + kEpiWarps * 2048 + 1024;  // + alignment slack
+    static_assert(total <= 232448, "shared memory of one CTA");
 };
 
 // The fp32 source of one row of A (an output pixel of a convolution, or a row of x).
@@ -140,12 +148,13 @@ __device__ __forceinline__ void load8(const UmmaP &p, const ARow &r, int k0, flo
     }
 }
 
-// Warp roles of the persistent kernel (448 threads):
+// Warp roles of the persistent kernel (832 threads):
 constexpr int kProdWarps = 16;  // warps 0-15: A producers, four threads per tile row
-constexpr int kEpiWarp0 = 16;   // warps 16-19: epilogue (TMEM lane quadrant = warp % 4)
+constexpr int kEpiWarp0 = 16;   // warps 16-19: epilogue, a tile's first half of columns
 constexpr int kTmaWarp = 20;    // warp 20: B tiles by TMA
 constexpr int kMmaWarp = 21;    // warp 21: TMEM allocation, MMA issue
-constexpr int kAllThreads = 22 * 32;
+constexpr int kEpiWarp1 = 22;   // warps 22-25: epilogue, the second half (lane quadrant = warp % 4)
+constexpr int kAllThreads = 26 * 32;
 
 
 // The im2col source of one 8-wide k chunk of a convolution, precomputed per CTA: tap row (bits
@@ -176,7 +185,8 @@ __device__ __forceinline__ void load8_tab(const UmmaP &p, const ARow &r, uint32_
 
 template <int BN, int STAGES, int CHAINS>
 __global__ void __launch_bounds__(kAllThreads, 1)
-    k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo, UmmaP p) {
+    k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
+           const __grid_constant__ CUtensorMap tm_y, UmmaP p) {
     using Lay = Layout<BN, STAGES>;
     // CHAINS: accumulation chains per tile (0: Acc<BN>'s choice); one chain sums in the order of
     // the 128- and 256-column tiles, so a narrowed launch gives their results to the bit
@@ -188,7 +198,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
     uint64_t *bfull = afull + STAGES;
     uint64_t *empty = bfull + STAGES;
     uint64_t *tfull = empty + STAGES;   // [NACC] accumulator ready (tcgen05.commit)
-    uint64_t *tempty = tfull + NACC;    // [NACC] accumulator drained by the epilogue (4 warps)
+    uint64_t *tempty = tfull + NACC;    // [NACC] accumulator drained by the epilogue (8 warps)
     uint64_t *drain = tempty + NACC;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -208,7 +218,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
         }
         for (int a = 0; a < NACC; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4);
+            mbar_init(&tempty[a], kEpiWarps);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -361,20 +371,29 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             }
         }
     } else {
-        // ---------------- epilogue: warps 16-19, TMEM lanes 32 * (warp % 4) ----------------
-        const int q = warp & 3;
+        // ---------- epilogue: warps 16-19 and 22-25, TMEM lanes 32 * (warp % 4) ----------
+        // The two warps of a lane quadrant split each tile's 16-column chunks (the first
+        // ceil(NCK / 2) to warps 16-19), so two warps a scheduler hide each other's latencies.
+        constexpr int NCK = BN / 16, HCK = (NCK + 1) / 2;
+        const int q = warp & 3, h = warp >= kEpiWarp1 ? 1 : 0;
+        const int ck0 = h * HCK, nck = h ? NCK - HCK : HCK;  // this warp's chunks of a tile
         const int row = q * 32 + lane;
-        float *ebias = reinterpret_cast<float *>(smem + Lay::ebias_off) + q * 2 * BN;
+        float *ebias = reinterpret_cast<float *>(smem + Lay::ebias_off) + (q + 4 * h) * 2 * Lay::ecols;
+        float *ystage = reinterpret_cast<float *>(smem + Lay::ystage_off) + (q + 4 * h) * 512;
+        // row-major stores of whole 32-row chunks by the TMA engine (the host's map of y): the
+        // lanes only write the warp's staging chunk in shared memory, instead of 32 rows' 16-byte
+        // pieces through the load/store unit (which bounds the epilogue)
+        const bool tma_y = p.tma_y && !p.part_max && !p.scatter;
         int lt = 0;
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
             const int ab = lt % NACC;
-            const int64_t m = (t / ntn) * BM + row;
+            const int64_t m = (t / ntn) * BM + row, qrow0 = m - lane;  // qrow0: the quadrant's first row
             const int n0 = (int)(t % ntn) * BN;
             // the tile's bias columns (scatter tiles: per output channel) into this warp's slot while
             // the MMAs run, so no chunk below waits on a global load
-            float *eb = ebias + (lt & 1) * BN;
-            for (int j = lane; j < BN; j += 32) {
-                const int col = n0 + j;
+            float *eb = ebias + (lt & 1) * Lay::ecols;
+            for (int j = lane; j < nck * 16; j += 32) {
+                const int col = n0 + ck0 * 16 + j;
                 const int bc = p.scatter ? col % p.scat_cout : col;
                 eb[j] = p.bias && col < p.N ? p.bias[bc] : 0.f;
             }
@@ -391,24 +410,34 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 nb = tt / p.oh;
                 pix = (int64_t)oy * p.ow + ox;
             }
-            float amx = -INFINITY, asum = 0.f;  // arg-max partials of this row over the tile
+            // arg-max partials of this row over the warp's half of the tile: the maximum and its
+            // first column, then the exponentials' sum against that maximum in four partial sums
+            float amx = -INFINITY, as4[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t aidx = 0;
             const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS;
             // one chain: the next chunk's load is in flight while this one is processed (not for
             // 32-column tiles, two chunks, where the registers it holds spill); more chains: a
-            // chunk's chains two loads per wait, summed in chain order
-            constexpr bool kAhead = NCH == 1 && BN >= 64;
+            // chunk's chains two loads per wait, summed in chain order.  The arg-max epilogue
+            // reads the accumulator twice (pass chunk i is the warp's chunk i mod nck): no store
+            // is in flight to delay a tensor-memory load there, so the second pass costs little
+            // beside the serial chain of an online maximum it replaces.
+            constexpr bool kAhead = false;
+            const bool amax = BN >= 64 && p.part_max;  // arg-max partials (64-column tiles or wider)
+            const int nck_all = amax ? 2 * nck : nck;
+            const bool full_tile = n0 + BN <= p.N;
             uint32_t nx[16];
-            if (kAhead) tmem_ld16_async(trow, nx);
+            if (kAhead && nck_all > 0) tmem_ld16_async(trow + ck0 * 16, nx);
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 16) {
+            for (int ci = 0; ci < nck_all; ci++) {
                 float v[16];
+                const int c0 = (ck0 + ci % nck) * 16;
+                const float *ebc = eb + (c0 - ck0 * 16);  // the chunk's bias columns
                 const uint32_t tbase = trow + c0;
                 if (kAhead) {
                     tmem_wait16(nx);
 #pragma unroll
                     for (int j = 0; j < 16; j++) v[j] = __uint_as_float(nx[j]);
-                    if (c0 + 16 < BN) tmem_ld16_async(tbase + 16, nx);
+                    if (ci + 1 < nck_all) tmem_ld16_async(trow + (ck0 + (ci + 1) % nck) * 16, nx);
                 } else if (NCH == 1) {
                     tmem_ld16(tbase, v);
                 } else {
@@ -431,35 +460,49 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                         }
                     }
                 }
-                if (m >= p.M || n0 + c0 >= p.N) continue;
-                if (p.part_max) {
-                    // online arg-max and sum of exponentials, a 16-column chunk at a time and
-                    // without branches (the epilogue has one warp per scheduler, so nothing
-                    // else hides a serial chain): the chunk's maximum by a select scan (strict >:
-                    // ties keep the lowest column), then 16 independent exponentials against the
-                    // new running maximum and one rescale of the running sum
-                    float o[16];
+                // (a TMA chunk is the warp's: only a chunk past N or past M for every lane is skipped)
+                if (tma_y ? (n0 + c0 >= p.N || qrow0 >= p.M) : (m >= p.M || n0 + c0 >= p.N)) continue;
+                if (amax) {
+                    // the logits are v + bias, as the unfused GEMM stores them (columns past N:
+                    // -inf); the epilogue has one warp per scheduler, so the chunk's work is
+                    // short independent chains
+                    float *o = v;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const int col = n0 + c0 + j;
-                        o[j] = col < p.N ? v[j] + eb[c0 + j] : -INFINITY;
+                    for (int j = 0; j < 16; j++) o[j] = v[j] + ebc[j];
+                    if (!full_tile) {
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            if (n0 + c0 + j >= p.N) o[j] = -INFINITY;
                     }
-                    float cm = o[0];
-                    uint32_t ci = (uint32_t)(n0 + c0);
+                    if (ci < nck) {
+                        // pass 1: the chunk's maximum and first column by a 4-level select tree
+                        // (the right side wins only when strictly greater), then against the row's
+                        float m8[8];
+                        int i8[8];
 #pragma unroll
-                    for (int j = 1; j < 16; j++) {
-                        const bool gt = o[j] > cm;
-                        cm = gt ? o[j] : cm;
-                        ci = gt ? (uint32_t)(n0 + c0 + j) : ci;
+                        for (int t = 0; t < 8; t++) {
+                            const bool g = o[2 * t + 1] > o[2 * t];
+                            m8[t] = g ? o[2 * t + 1] : o[2 * t];
+                            i8[t] = 2 * t + (g ? 1 : 0);
+                        }
+#pragma unroll
+                        for (int w = 4; w >= 1; w >>= 1) {
+#pragma unroll
+                            for (int t = 0; t < w; t++) {
+                                const bool g = m8[2 * t + 1] > m8[2 * t];
+                                m8[t] = g ? m8[2 * t + 1] : m8[2 * t];
+                                i8[t] = g ? i8[2 * t + 1] : i8[2 * t];
+                            }
+                        }
+                        if (m8[0] > amx) {
+                            amx = m8[0];
+                            aidx = (uint32_t)(n0 + c0 + i8[0]);
+                        }
+                    } else {
+                        // pass 2: exponentials against the row's maximum (exp(-inf) = 0 past N)
+#pragma unroll
+                        for (int j = 0; j < 16; j++) as4[j & 3] += __expf(o[j] - amx);
                     }
-                    const bool up = cm > amx;
-                    const float nm = up ? cm : amx;
-                    aidx = up ? ci : aidx;
-                    float cs = 0.f;
-#pragma unroll
-                    for (int j = 0; j < 16; j++) cs += n0 + c0 + j < p.N ? __expf(o[j] - nm) : 0.f;
-                    asum = (amx == -INFINITY ? 0.f : asum * __expf(amx - nm)) + cs;
-                    amx = nm;
                     continue;
                 }
                 if (p.scatter && p.scat_cout % 16 == 0) {
@@ -470,7 +513,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     const int yy = oy * s + tap / s, xx = ox * s + tap % s;
                     float *dst = p.y + (int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co0;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] += eb[c0 + j];
+                    for (int j = 0; j < 16; j++) v[j] += ebc[j];
                     act_n(v, p.act);
                     if (p.out_vec) {
                         float4 *d4 = reinterpret_cast<float4 *>(dst);
@@ -486,7 +529,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 if (p.scatter) {
                     const int s = p.scatter;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] += eb[c0 + j];
+                    for (int j = 0; j < 16; j++) v[j] += ebc[j];
                     act_n(v, p.act);
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
@@ -502,17 +545,32 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 const float *rsrc = nullptr;
                 if (p.mode == 1) {
                     dst = p.y + (int64_t)nb * p.y_n + pix * p.y_pix + n0 + c0;
-                    if (p.res) rsrc = p.res + (int64_t)nb * p.res_n + pix * p.res_pix + n0 + c0;
+                    if (p.res && m < p.M) rsrc = p.res + (int64_t)nb * p.res_n + pix * p.res_pix + n0 + c0;
                 } else {
                     dst = p.y + m * p.ldy + n0 + c0;
                 }
 #pragma unroll
-                for (int j = 0; j < 16; j++) v[j] += eb[c0 + j];
+                for (int j = 0; j < 16; j++) v[j] += ebc[j];
                 act_n(v, p.act);
                 if (rsrc) {
 #pragma unroll
                     for (int j = 0; j < 16; j++)
                         if (n0 + c0 + j < p.N) v[j] += rsrc[j];
+                }
+                if (tma_y) {
+                    // the previous chunk's store has read the staging chunk; then row `lane`'s 16
+                    // values in the 64-byte swizzle (16-byte piece u at u ^ ((lane >> 1) & 3)), and
+                    // one store of the 32 x 16 box (the engine clips rows past M, columns past N)
+                    if (lane == 0) bulk_wait_read0();
+                    __syncwarp();
+#pragma unroll
+                    for (int u = 0; u < 4; u++)
+                        *reinterpret_cast<float4 *>(ystage + lane * 16 + 4 * (u ^ ((lane >> 1) & 3))) =
+                            make_float4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) tma_store_2d(&tm_y, ystage, n0 + c0, (int)qrow0);
+                    continue;
                 }
                 const bool full = n0 + c0 + 16 <= p.N && p.out_vec;
                 if (full) {
@@ -525,16 +583,17 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                         if (n0 + c0 + j < p.N) dst[j] = v[j];
                 }
             }
-            if (p.part_max && m < p.M) {
-                const int64_t o = m * p.part_ld + n0 / BN;
+            if (amax && m < p.M) {
+                const int64_t o = m * p.part_ld + 2 * (n0 / BN) + h;  // two slots a tile
                 p.part_max[o] = amx;
-                p.part_sum[o] = asum;
+                p.part_sum[o] = (as4[0] + as4[1]) + (as4[2] + as4[3]);
                 p.part_idx[o] = aidx;
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[ab]);  // one arrival per warp
         }
+        if (tma_y && lane == 0) bulk_wait_all();  // the warp's tensor stores are done
     }
     tc_fence_before();
     __syncthreads();
@@ -545,6 +604,20 @@ __global__ void __launch_bounds__(kAllThreads, 1)
 }
 
 // ---- host side ------------------------------------------------------------------------------
+
+// The output map of a TMA-store epilogue: fp32 [M][N] rows `stride` floats apart, 16 x 32 boxes
+// (16 columns of the quadrant's 32 rows) in the 64-byte swizzle.
+void make_ymap(CUtensorMap *map, float *y, int N, int64_t M, int64_t stride) {
+    auto fn = encode_fn();
+    if (!fn) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)stride * 4};
+    cuuint32_t box[2] = {16, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) fail(WOCR_ERR_CUDA, "cuTensorMapEncodeTiled (output) failed: " + std::to_string((int)r));
+}
 
 void make_map(CUtensorMap *map, void *base, int N, int Kpad, int bn) {
     auto fn = encode_fn();
@@ -560,7 +633,7 @@ void make_map(CUtensorMap *map, void *base, int N, int Kpad, int bn) {
 }
 
 template <int BN, int STAGES, int CHAINS = 0>
-void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const UmmaP &p) {
+void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const CUtensorMap &map_y, const UmmaP &p) {
     using Lay = Layout<BN, STAGES>;
     static std::atomic<bool> set[64];
     if (!set[c->device]) {
@@ -570,7 +643,7 @@ void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const 
     }
     int64_t tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
     unsigned grid = (unsigned)std::min<int64_t>(tiles, c->sm_count);
-    k_umma<BN, STAGES, CHAINS><<<grid, kAllThreads, Lay::total, c->stream>>>(map_hi, map_lo, p);
+    k_umma<BN, STAGES, CHAINS><<<grid, kAllThreads, Lay::total, c->stream>>>(map_hi, map_lo, map_y, p);
     WOCR_LAUNCHED(c);
 }
 
@@ -624,8 +697,8 @@ UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int
 void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
     if (p.M == 0 || w.N == 0) return;
     if (p.M >= (int64_t)INT32_MAX - BM) fail(WOCR_ERR_UNSUPPORTED, "GEMM with 2^31 rows or more");
-    if (p.part_max && (p.mode != 0 || p.part_ld != umma_ntiles(w)))
-        fail(WOCR_ERR_INVALID, "arg-max partials need a row-major GEMM and one slot per N tile");
+    if (p.part_max && (p.mode != 0 || p.part_ld != umma_part_slots(w) || w.bn < 64))
+        fail(WOCR_ERR_INVALID, "arg-max partials need a row-major GEMM of 64-column tiles and two slots per N tile");
     if (!c->status) {
         c->status_buf = alloc(c, 16);
         c->status = (int *)c->status_buf->p;
@@ -634,6 +707,14 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
     p.status = c->status;
     const bool al = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0;
     p.out_vec = p.mode == 1 ? (al && p.y_pix % 4 == 0 && p.y_n % 4 == 0) : (al && p.ldy % 4 == 0);
+    // TMA tensor stores of the output: rows of y at a fixed stride (a convolution's pixels
+    // consecutive over the batch), 16-byte aligned; the arg-max and scatter epilogues store
+    // otherwise
+    CUtensorMap my{};
+    const int64_t ystride = p.mode == 1 ? p.y_pix : p.ldy;
+    p.tma_y = !p.part_max && !p.scatter && p.out_vec &&
+              (p.mode == 0 || p.n == 1 || p.y_n == (int64_t)p.oh * p.ow * p.y_pix) && !std::getenv("WOCR_NO_TMA_STORE");
+    if (p.tma_y) make_ymap(&my, p.y, w.N, p.M, ystride);
     p.K = w.K;
     p.Kpad = w.Kpad;
     p.N = w.N;
@@ -650,24 +731,24 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
         const bool wide = w.bn > 64;  // one chain (128 / 256 columns), else two (64)
         if (w.has32 && !fills_half(64)) {
             if (wide)
-                launch<32, 5, 1>(c, w.map_hi32, w.map_lo32, p);
+                launch<32, 5, 1>(c, w.map_hi32, w.map_lo32, my, p);
             else
-                launch<32, 5, 2>(c, w.map_hi32, w.map_lo32, p);
+                launch<32, 5, 2>(c, w.map_hi32, w.map_lo32, my, p);
             c->flops += flops;
             return;
         }
         if (w.has64) {
-            launch<64, 4, 1>(c, w.map_hi64, w.map_lo64, p);
+            launch<64, 4, 1>(c, w.map_hi64, w.map_lo64, my, p);
             c->flops += flops;
             return;
         }
     }
     switch (w.bn) {
-    case 16: launch<16, 6>(c, w.map_hi, w.map_lo, p); break;
-    case 32: launch<32, 5>(c, w.map_hi, w.map_lo, p); break;
-    case 64: launch<64, 4>(c, w.map_hi, w.map_lo, p); break;
-    case 128: launch<128, 3>(c, w.map_hi, w.map_lo, p); break;
-    default: launch<256, 2>(c, w.map_hi, w.map_lo, p); break;
+    case 16: launch<16, 5>(c, w.map_hi, w.map_lo, my, p); break;
+    case 32: launch<32, 5>(c, w.map_hi, w.map_lo, my, p); break;
+    case 64: launch<64, 4>(c, w.map_hi, w.map_lo, my, p); break;
+    case 128: launch<128, 3>(c, w.map_hi, w.map_lo, my, p); break;
+    default: launch<256, 2>(c, w.map_hi, w.map_lo, my, p); break;
     }
     c->flops += flops;
 }

@@ -110,13 +110,15 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// mbar_wait for the single threads that issue MMAs or TMA copies: a spin on test_wait, so the
-// thread reacts to the phase at once instead of after a suspended thread's wake-up; bounded alike.
+// mbar_wait for the single threads that issue MMAs or TMA copies: a test first, then try_wait
+// without a time hint, which parks the thread in hardware until the phase completes (or a short
+// limit passes) instead of a test_wait spin whose instructions take issue slots from the
+// epilogue warps on the same scheduler; bounded alike.
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
                                                int code) {
     if (mbar_test(bar, parity)) return true;
     long long t0 = clock64();
-    while (!mbar_test(bar, parity)) {
+    while (!mbar_try(bar, parity)) {
         if (*abort_flag) return false;
         if (clock64() - t0 > kWaitBudget) {
             *abort_flag = 1;
@@ -155,6 +157,22 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
+
+// Tensor store of a shared-memory box to the map's (x, y) (its own bulk group) by one thread;
+// x * 4 bytes is a multiple of 16 and x, y >= 0 at every call site.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(smem_u32(src))
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// The thread's bulk stores have read their shared memory (the source may be rewritten).
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// The thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // K-major operand tile in the 128-byte swizzle: rows of 128 bytes, 8-row atoms of 1024 bytes.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {

@@ -37,6 +37,7 @@ struct UmmaP {
     float *y = nullptr;
     int64_t y_n = 0, y_pix = 0, ldy = 0;
     int out_vec = 0;              // 16-byte aligned output rows: float4 stores
+    int tma_y = 0;                // y rows (M x N, 16-byte aligned) written by TMA tensor stores
     const float *res = nullptr;
     int64_t res_n = 0, res_pix = 0;
     int scatter = 0, scat_cout = 0;
@@ -56,6 +57,8 @@ int umma_bn(int N);
 UmmaW make_umma_weights(Ctx *c, const std::vector<float> &wnk, int N, int K, int max_bn = 256);
 void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p);
 inline int umma_ntiles(const UmmaW &w) { return (w.N + w.bn - 1) / w.bn; }
+// arg-max partial slots per row of a fused arg-max launch: two per N tile (a slot per half tile)
+inline int umma_part_slots(const UmmaW &w) { return 2 * umma_ntiles(w); }
 
 }  // namespace k
 }  // namespace wocr
