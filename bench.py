@@ -705,11 +705,12 @@ def run_workload(args):
                                                  f"seed 2, arg-max per step; {len(batches)} width batches over {L} "
                                                  "lane(s) (a context and a host thread each)")
         h2d = sum(b[0].nbytes for b in batches)
-        d2h = sum(b[1] * (b[2] // 8) * 12 for b in batches)
+        d2h = sum(b[1] * (b[2] // 8) * 8 for b in batches)  # classes and maxima, 4 bytes each a step
 
+        # the classes per step, as the reference's NdGraph::argmax gives them (no log-sum-exp)
         def run_lane(k_):
             for i in plan[k_]:
-                lane_handles[k_].argmax(batches[i][0])
+                lane_handles[k_].argmax(batches[i][0], lse=False)
 
         def step():
             if pool is None:
@@ -719,7 +720,7 @@ def run_workload(args):
 
         def serial_step():
             for data, _, _ in batches:
-                handle.argmax(data)
+                handle.argmax(data, lse=False)
 
         def lane_launches():
             return sum(g_.launches() for g_ in lane_gpus)

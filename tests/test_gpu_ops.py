@@ -125,6 +125,12 @@ def test_linear_argmax_fused(gpu, classes, monkeypatch):
     g = wocr.NdGraph(gpu, m)
     try:
         best, mx, lse, shape = g.argmax(x)
+        # without the log-sum-exp (the epilogue skips the exponentials): the same classes and
+        # maxima, on the recorded first call and on the graph replay
+        for _ in range(2):
+            nb, nmx, nlse, nshape = g.argmax(x, lse=False)
+            assert nlse is None and nshape == shape
+            assert (nb == best).all() and (nmx == mx).all()
         monkeypatch.setenv("WOCR_UNFUSED_ARGMAX", "1")
         monkeypatch.setenv("WOCR_NO_GRAPH", "1")
         ub, umx, ulse, ushape = g.argmax(x)

@@ -163,7 +163,9 @@ struct wocr_recognizer {
 // records the output shape; the second captures.
 struct NdReplay {
     std::vector<int64_t> in_shape, out_shape;
-    int mode = -1;  // 0 wocr_ndgraph_run, 1 wocr_ndgraph_run_argmax
+    // 0 wocr_ndgraph_run, 1 wocr_ndgraph_run_argmax, 4 the same without the log-sum-exp (a
+    // caller that reads only the classes and maxima), 2 / 3 PP detection
+    int mode = -1;
     int64_t rows = 0, len = 0;
     BufP in, out, best, mx, lse;
     cudaGraph_t graph = nullptr;
@@ -1239,9 +1241,10 @@ static void nd_capture(wocr_ndgraph *g, NdReplay *r) {
         x.shape = r->in_shape;
         x.strides = rowmajor_strides(x.shape);
         Executor &ex = *g->graph;
-        if (r->mode == 1 && ex.ends_in_linear() && !std::getenv("WOCR_UNFUSED_ARGMAX")) {
+        float *lse = r->mode == 1 ? (float *)r->lse->p : nullptr;  // run (0) and no-lse (4): none
+        if (r->mode != 0 && ex.ends_in_linear() && !std::getenv("WOCR_UNFUSED_ARGMAX")) {
             DT xl = ex.run_to(x, (int)ex.steps.size() - 1);
-            if (ex.linear_argmax(xl, (uint32_t *)r->best->p, (float *)r->mx->p, (float *)r->lse->p) != r->out_shape)
+            if (ex.linear_argmax(xl, (uint32_t *)r->best->p, (float *)r->mx->p, lse) != r->out_shape)
                 fail(WOCR_ERR_SHAPE, "NdGraph output shape changed between runs");
         } else {
             DT y = to_rowmajor(c, ex.run(x));
@@ -1251,8 +1254,7 @@ static void nd_capture(wocr_ndgraph *g, NdReplay *r) {
                     WOCR_CUDA(cudaMemcpyAsync(r->out->p, y.p, (size_t)y.numel() * 4, cudaMemcpyDeviceToDevice,
                                               c->stream));
             } else {
-                k::argmax(c, y.p, r->rows, r->len, r->len, (uint32_t *)r->best->p, (float *)r->mx->p,
-                          (float *)r->lse->p, 0);
+                k::argmax(c, y.p, r->rows, r->len, r->len, (uint32_t *)r->best->p, (float *)r->mx->p, lse, 0);
             }
         }
     } catch (...) {
@@ -1325,7 +1327,8 @@ static void nd_argmax_core(wocr_ndgraph *g, const float *x, const int64_t *shape
     Ctx *c = &g->ctx->c;
     if (!x || !shape || rank <= 0 || rank > kMaxRank) fail(WOCR_ERR_INVALID, "bad input tensor");
     bool first = false;
-    NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), 1, &first);
+    // without a log-sum-exp to read, the fused arg-max skips the exponentials' sums
+    NdReplay *r = nd_replay(g, std::vector<int64_t>(shape, shape + rank), row_lse ? 1 : 4, &first);
     if (!r || first) {
         Executor &ex = *g->graph;
         DT in = nd_input(c, x, shape, rank);
@@ -1347,7 +1350,7 @@ static void nd_argmax_core(wocr_ndgraph *g, const float *x, const int64_t *shape
         if (cap < rows) fail(WOCR_ERR_CAPACITY, "argmax buffers too small");
         BufP b = alloc(c, (size_t)rows * 4), mx = alloc(c, (size_t)rows * 4), ls = alloc(c, (size_t)rows * 4);
         if (fused)
-            ex.linear_argmax(y, (uint32_t *)b->p, (float *)mx->p, (float *)ls->p);
+            ex.linear_argmax(y, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr);
         else
             k::argmax(c, y.p, rows, len, len, (uint32_t *)b->p, (float *)mx->p, row_lse ? (float *)ls->p : nullptr,
                       0);

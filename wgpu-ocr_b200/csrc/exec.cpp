@@ -962,7 +962,9 @@ std::vector<int64_t> Executor::linear_argmax(const DT &xin, uint32_t *best, floa
     DT x = to_rowmajor(ctx, xin);
     const int64_t M = x.numel() / s.lk;
     const int ntn = k::umma_part_slots(*s.luw);
-    BufP pm = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4), ps = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4),
+    // no log-sum-exp wanted: no exponentials' sums (the epilogue's second pass is skipped)
+    BufP pm = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4),
+         ps = row_lse ? alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4) : nullptr,
          pi = alloc(ctx, (size_t)std::max<int64_t>(M, 1) * ntn * 4);
     k::UmmaP u;
     u.mode = 0;
@@ -973,12 +975,12 @@ std::vector<int64_t> Executor::linear_argmax(const DT &xin, uint32_t *best, floa
     u.bias = s.lb.p;
     u.act = 0;
     u.part_max = (float *)pm->p;
-    u.part_sum = (float *)ps->p;
+    u.part_sum = ps ? (float *)ps->p : nullptr;
     u.part_idx = (uint32_t *)pi->p;
     u.part_ld = ntn;
     k::umma_gemm(ctx, *s.luw, u);
-    k::argmax_merge(ctx, (const float *)pm->p, (const float *)ps->p, (const uint32_t *)pi->p, M, ntn, best, row_max,
-                    row_lse);
+    k::argmax_merge(ctx, (const float *)pm->p, ps ? (const float *)ps->p : nullptr, (const uint32_t *)pi->p, M, ntn,
+                    best, row_max, row_lse);
     std::vector<int64_t> shape = x.shape;
     shape.back() = s.ln;
     return shape;

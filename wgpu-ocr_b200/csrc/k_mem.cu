@@ -382,7 +382,7 @@ __global__ void k_argmax_merge(const float *__restrict__ pmax, const float *__re
         for (int t = lane; t < ntiles; t += 32) {
             const float v = pm[t];
             if (v == m && t < first) first = t;
-            s += psum[r * ntiles + t] * __expf(v - m);
+            if (psum) s += psum[r * ntiles + t] * __expf(v - m);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -392,7 +392,7 @@ __global__ void k_argmax_merge(const float *__restrict__ pmax, const float *__re
         if (lane == 0) {
             best[r] = first < ntiles ? pidx[r * ntiles + first] : 0u;
             if (row_max) row_max[r] = m;
-            if (row_lse) row_lse[r] = m + logf(s);
+            if (row_lse && psum) row_lse[r] = m + logf(s);
         }
     }
 }

@@ -183,6 +183,26 @@ __device__ __forceinline__ void load8_tab(const UmmaP &p, const ARow &r, uint32_
     }
 }
 
+// v[j] += b[j] for a chunk's 16 bias columns staged 64-byte aligned: four 16-byte loads
+__device__ __forceinline__ void add_bias16(float (&v)[16], const float *b) {
+    const float4 *b4 = reinterpret_cast<const float4 *>(b);
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const float4 t = b4[u];
+        v[4 * u] += t.x;
+        v[4 * u + 1] += t.y;
+        v[4 * u + 2] += t.z;
+        v[4 * u + 3] += t.w;
+    }
+}
+
+// 2^x by the tensor unit's base-2 exponential (inputs <= 0 here, results in [0, 1])
+__device__ __forceinline__ float ex2_approx(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 template <int BN, int STAGES, int CHAINS>
 __global__ void __launch_bounds__(kAllThreads, 1)
     k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
@@ -415,30 +435,22 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             float amx = -INFINITY, as4[4] = {0.f, 0.f, 0.f, 0.f};
             uint32_t aidx = 0;
             const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + ab * TCOLS;
-            // one chain: the next chunk's load is in flight while this one is processed (not for
-            // 32-column tiles, two chunks, where the registers it holds spill); more chains: a
-            // chunk's chains two loads per wait, summed in chain order.  The arg-max epilogue
-            // reads the accumulator twice (pass chunk i is the warp's chunk i mod nck): no store
-            // is in flight to delay a tensor-memory load there, so the second pass costs little
-            // beside the serial chain of an online maximum it replaces.
-            constexpr bool kAhead = false;
+            // A chunk's accumulator: one load and wait (tensor-memory loads take tens of cycles
+            // once no store still reads the registers they overwrite, and the other epilogue
+            // warp of the scheduler runs meanwhile); several chains summed in chain order, the
+            // first two in one wait.  The arg-max epilogue reads the accumulator twice (pass
+            // chunk i is the warp's chunk i mod nck), a second pass cheaper than the serial chain
+            // of an online maximum it replaces.
             const bool amax = BN >= 64 && p.part_max;  // arg-max partials (64-column tiles or wider)
-            const int nck_all = amax ? 2 * nck : nck;
+            const int nck_all = amax && p.part_sum ? 2 * nck : nck;  // no sums wanted: pass 1 only
             const bool full_tile = n0 + BN <= p.N;
-            uint32_t nx[16];
-            if (kAhead && nck_all > 0) tmem_ld16_async(trow + ck0 * 16, nx);
 #pragma unroll 1
             for (int ci = 0; ci < nck_all; ci++) {
                 float v[16];
                 const int c0 = (ck0 + ci % nck) * 16;
                 const float *ebc = eb + (c0 - ck0 * 16);  // the chunk's bias columns
                 const uint32_t tbase = trow + c0;
-                if (kAhead) {
-                    tmem_wait16(nx);
-#pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] = __uint_as_float(nx[j]);
-                    if (ci + 1 < nck_all) tmem_ld16_async(trow + (ck0 + (ci + 1) % nck) * 16, nx);
-                } else if (NCH == 1) {
+                if (NCH == 1) {
                     tmem_ld16(tbase, v);
                 } else {
                     uint32_t a[16], b[16];
@@ -448,27 +460,21 @@ __global__ void __launch_bounds__(kAllThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; j++) v[j] = __uint_as_float(a[j]) + __uint_as_float(b[j]);
 #pragma unroll 1
-                    for (int ch = 2; ch < NCH; ch += 2) {
-                        tmem_ld16_async(tbase + ch * BN, a);
-                        if (ch + 1 < NCH) tmem_ld16_async(tbase + (ch + 1) * BN, b);
-                        tmem_wait16x2(a, b);
+                    for (int ch = 2; ch < NCH; ch++) {  // one chain a wait: fewer live registers
+                        tmem_ld16_async(tbase + ch * BN, b);
+                        tmem_wait16(b);
 #pragma unroll
-                        for (int j = 0; j < 16; j++) v[j] += __uint_as_float(a[j]);
-                        if (ch + 1 < NCH) {
-#pragma unroll
-                            for (int j = 0; j < 16; j++) v[j] += __uint_as_float(b[j]);
-                        }
+                        for (int j = 0; j < 16; j++) v[j] += __uint_as_float(b[j]);
                     }
                 }
                 // (a TMA chunk is the warp's: only a chunk past N or past M for every lane is skipped)
                 if (tma_y ? (n0 + c0 >= p.N || qrow0 >= p.M) : (m >= p.M || n0 + c0 >= p.N)) continue;
                 if (amax) {
                     // the logits are v + bias, as the unfused GEMM stores them (columns past N:
-                    // -inf); the epilogue has one warp per scheduler, so the chunk's work is
+                    // -inf); a scheduler has only two epilogue warps, so the chunk's work is
                     // short independent chains
                     float *o = v;
-#pragma unroll
-                    for (int j = 0; j < 16; j++) o[j] = v[j] + ebc[j];
+                    add_bias16(v, ebc);
                     if (!full_tile) {
 #pragma unroll
                         for (int j = 0; j < 16; j++)
@@ -499,9 +505,11 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                             aidx = (uint32_t)(n0 + c0 + i8[0]);
                         }
                     } else {
-                        // pass 2: exponentials against the row's maximum (exp(-inf) = 0 past N)
+                        // pass 2: exponentials against the row's maximum, e^(o - max) as
+                        // 2^(o log2(e) - max log2(e)) (exp(-inf) = 0 past N)
+                        const float nl = -amx * 1.4426950408889634f;
 #pragma unroll
-                        for (int j = 0; j < 16; j++) as4[j & 3] += __expf(o[j] - amx);
+                        for (int j = 0; j < 16; j++) as4[j & 3] += ex2_approx(fmaf(o[j], 1.4426950408889634f, nl));
                     }
                     continue;
                 }
@@ -512,8 +520,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     const int tap = col / p.scat_cout, co0 = col - tap * p.scat_cout;
                     const int yy = oy * s + tap / s, xx = ox * s + tap % s;
                     float *dst = p.y + (int64_t)nb * p.y_n + ((int64_t)yy * p.ow * s + xx) * p.y_pix + co0;
-#pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] += ebc[j];
+                    add_bias16(v, ebc);
                     act_n(v, p.act);
                     if (p.out_vec) {
                         float4 *d4 = reinterpret_cast<float4 *>(dst);
@@ -528,8 +535,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 }
                 if (p.scatter) {
                     const int s = p.scatter;
-#pragma unroll
-                    for (int j = 0; j < 16; j++) v[j] += ebc[j];
+                    add_bias16(v, ebc);
                     act_n(v, p.act);
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
@@ -549,8 +555,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 } else {
                     dst = p.y + m * p.ldy + n0 + c0;
                 }
-#pragma unroll
-                for (int j = 0; j < 16; j++) v[j] += ebc[j];
+                add_bias16(v, ebc);
                 act_n(v, p.act);
                 if (rsrc) {
 #pragma unroll
@@ -586,7 +591,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             if (amax && m < p.M) {
                 const int64_t o = m * p.part_ld + 2 * (n0 / BN) + h;  // two slots a tile
                 p.part_max[o] = amx;
-                p.part_sum[o] = (as4[0] + as4[1]) + (as4[2] + as4[3]);
+                if (p.part_sum) p.part_sum[o] = (as4[0] + as4[1]) + (as4[2] + as4[3]);
                 p.part_idx[o] = aidx;
             }
             tc_fence_before();

@@ -43,7 +43,8 @@ struct UmmaP {
     int scatter = 0, scat_cout = 0;
     // mode 0 only: instead of storing y, each N tile writes its per-row arg-max partials at
     // [row][tile] (part_ld tiles a row): the maximum, the lowest column reaching it and the sum
-    // of exp(value - maximum) over the tile's columns
+    // of exp(value - maximum) over the tile's columns (part_sum null: no sums, maxima and
+    // columns only)
     float *part_max = nullptr, *part_sum = nullptr;
     uint32_t *part_idx = nullptr;
     int part_ld = 0;

@@ -370,28 +370,31 @@ class NdGraph(_Handle):
             L.check(st)
             return out[: int(np.prod(shape))].reshape(shape)
 
-    def argmax(self, x: np.ndarray):
+    def argmax(self, x: np.ndarray, lse: bool = True):
         """run + arg-max over the last axis per row (ties -> lowest index, src/nd.rs:360-391).
-        Returns (best [rows], row_max [rows], row_lse [rows], output shape)."""
+        Returns (best [rows], row_max [rows], row_lse [rows], output shape); with lse=False the
+        log-sum-exp is not computed (as the reference's argmax, which gives the classes only)
+        and row_lse is None."""
         x = np.ascontiguousarray(x, np.float32)
         shp = (ctypes.c_int64 * x.ndim)(*x.shape)
         cap = max(int(np.prod(x.shape)), 1 << 16)
         while True:
             best = np.empty(cap, np.uint32)
             mx = np.empty(cap, np.float32)
-            lse = np.empty(cap, np.float32)
+            ls = np.empty(cap, np.float32) if lse else None
             rows = ctypes.c_int64()
             oshape = (ctypes.c_int64 * 6)()
             orank = ctypes.c_int32()
-            st = L.lib().wocr_ndgraph_run_argmax(self.h, L.ptr(x), shp, x.ndim, L.ptr(best), L.ptr(mx), L.ptr(lse),
-                                                 cap, ctypes.byref(rows), oshape, ctypes.byref(orank))
+            st = L.lib().wocr_ndgraph_run_argmax(self.h, L.ptr(x), shp, x.ndim, L.ptr(best), L.ptr(mx),
+                                                 L.ptr(ls) if lse else None, cap, ctypes.byref(rows), oshape,
+                                                 ctypes.byref(orank))
             if st == 8 and rows.value > cap:
                 cap = rows.value
                 continue
             L.check(st)
             r = rows.value
             shape = tuple(oshape[i] for i in range(orank.value))
-            return best[:r], mx[:r], lse[:r], shape
+            return best[:r], mx[:r], (ls[:r] if lse else None), shape
 
     def argmax_enqueue(self, batch: "Batch", x: np.ndarray) -> "Pending":
         """NdGraph::run + argmax_record (src/nd.rs:1372-1380): queued on the device, read by
