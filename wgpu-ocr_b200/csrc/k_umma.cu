@@ -203,6 +203,12 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return r;
 }
 
+// A tile index t (< 2^31) as (row tile, N tile): t / ntn by the launch's multiply-high divisor.
+__device__ __forceinline__ uint32_t tile_row(const UmmaP &p, int64_t t) {
+    const uint32_t x = (uint32_t)t;
+    return (__umulhi(x, p.ntn_m) + x) >> p.ntn_l;
+}
+
 template <int BN, int STAGES, int CHAINS>
 __global__ void __launch_bounds__(kAllThreads, 1)
     k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
@@ -277,7 +283,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             }
         };
         if (t < ntiles) {
-            ARow r = a_row(p, (t / ntn) * BM + row);
+            ARow r = a_row(p, (int64_t)tile_row(p, t) * BM + row);
             float cur[2][8], nxt[2][8];
             load_pair(r, 0, cur);
             while (true) {
@@ -290,7 +296,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 }
                 const bool more = t2 < ntiles;
                 if (more) {
-                    if (t2 != t) r = a_row(p, (t2 / ntn) * BM + row);
+                    if (t2 != t) r = a_row(p, (int64_t)tile_row(p, t2) * BM + row);
                     load_pair(r, kb2, nxt);
                 }
                 const int s = it % STAGES;
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             int it = 0;
             bool ok = true;
             for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int n0 = (int)(t % ntn) * BN;
+                const int n0 = (int)((uint32_t)t - tile_row(p, t) * (uint32_t)ntn) * BN;
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % STAGES;
                     if (!mbar_wait_spin(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 12)) {
@@ -407,8 +413,9 @@ __global__ void __launch_bounds__(kAllThreads, 1)
         int lt = 0;
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
             const int ab = lt % NACC;
-            const int64_t m = (t / ntn) * BM + row, qrow0 = m - lane;  // qrow0: the quadrant's first row
-            const int n0 = (int)(t % ntn) * BN;
+            const uint32_t trow_i = tile_row(p, t);
+            const int64_t m = (int64_t)trow_i * BM + row, qrow0 = m - lane;  // qrow0: the quadrant's first row
+            const int n0 = (int)((uint32_t)t - trow_i * (uint32_t)ntn) * BN;
             // the tile's bias columns (scatter tiles: per output channel) into this warp's slot while
             // the MMAs run, so no chunk below waits on a global load
             float *eb = ebias + (lt & 1) * Lay::ecols;
@@ -447,7 +454,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
 #pragma unroll 1
             for (int ci = 0; ci < nck_all; ci++) {
                 float v[16];
-                const int c0 = (ck0 + ci % nck) * 16;
+                const int c0 = (ck0 + (ci < nck ? ci : ci - nck)) * 16;  // ci < 2 nck
                 const float *ebc = eb + (c0 - ck0 * 16);  // the chunk's bias columns
                 const uint32_t tbase = trow + c0;
                 if (NCH == 1) {
@@ -647,8 +654,13 @@ void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const 
         set[c->device] = true;
     }
     int64_t tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+    if (tiles >= ((int64_t)1 << 31)) fail(WOCR_ERR_UNSUPPORTED, "GEMM with 2^31 tiles or more");
+    UmmaP q = p;
+    const FastDiv fd((uint32_t)((p.N + BN - 1) / BN));
+    q.ntn_m = fd.m;
+    q.ntn_l = fd.l;
     unsigned grid = (unsigned)std::min<int64_t>(tiles, c->sm_count);
-    k_umma<BN, STAGES, CHAINS><<<grid, kAllThreads, Lay::total, c->stream>>>(map_hi, map_lo, map_y, p);
+    k_umma<BN, STAGES, CHAINS><<<grid, kAllThreads, Lay::total, c->stream>>>(map_hi, map_lo, map_y, q);
     WOCR_LAUNCHED(c);
 }
 

@@ -416,16 +416,38 @@ __global__ void k_big_list(const int *__restrict__ len, int C, int *__restrict__
 
 __device__ __forceinline__ float sq_len(float x, float y) { return __fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y)); }
 
-// point-to-segment distance (comp.graphics.algorithms FAQ 1.02)
-__device__ float seg_dist(float px, float py, float ax, float ay, float bx, float by) {
-    const float abx = __fsub_rn(bx, ax), aby = __fsub_rn(by, ay), acx = __fsub_rn(px, ax), acy = __fsub_rn(py, ay);
-    const float l2 = sq_len(abx, aby);
-    if (l2 == 0.f) return __fsqrt_rn(sq_len(acx, acy));
-    const float r = __fdiv_rn(__fadd_rn(__fmul_rn(acx, abx), __fmul_rn(acy, aby)), l2);
-    if (r <= 0.f) return __fsqrt_rn(sq_len(acx, acy));
-    if (r >= 1.f) return __fsqrt_rn(sq_len(__fsub_rn(px, bx), __fsub_rn(py, by)));
-    const float s = __fdiv_rn(__fsub_rn(__fmul_rn(abx, acy), __fmul_rn(aby, acx)), l2);
-    return fabsf(__fmul_rn(s, __fsqrt_rn(l2)));
+// point-to-segment distance (comp.graphics.algorithms FAQ 1.02): r = dot / l2 picks the nearer
+// end or the perpendicular, s = cross / l2, distance |s| sqrt(l2).  The tests on r are made on
+// dot itself (SegC holds the segment's terms), which takes the same branch
+// with one division less: l2 > 0 and dot are integer-valued floats here (page coordinates), so
+// fl(dot / l2) <= 0 exactly when dot <= 0, and fl(dot / l2) >= 1 exactly when dot >= l2 (for
+// positive normal a < b, a / b <= 1 - 2^-24 (the float below 1) before rounding, so it never
+// rounds up to 1).  The distance is therefore the C restatement's to the bit.
+// (b = a + ab exactly: integer-valued coordinates below 2^24)
+struct SegC {
+    float ax, ay, abx, aby, l2, sl2;
+};
+
+__device__ __forceinline__ SegC seg_c(float ax, float ay, float bx, float by) {
+    SegC c;
+    c.ax = ax;
+    c.ay = ay;
+    c.abx = __fsub_rn(bx, ax);
+    c.aby = __fsub_rn(by, ay);
+    c.l2 = sq_len(c.abx, c.aby);
+    c.sl2 = __fsqrt_rn(c.l2);
+    return c;
+}
+
+__device__ __forceinline__ float seg_dist(const SegC &c, float px, float py) {
+    const float acx = __fsub_rn(px, c.ax), acy = __fsub_rn(py, c.ay);
+    if (c.l2 == 0.f) return __fsqrt_rn(sq_len(acx, acy));
+    const float dot = __fadd_rn(__fmul_rn(acx, c.abx), __fmul_rn(acy, c.aby));
+    if (dot <= 0.f) return __fsqrt_rn(sq_len(acx, acy));
+    if (dot >= c.l2)
+        return __fsqrt_rn(sq_len(__fsub_rn(px, __fadd_rn(c.ax, c.abx)), __fsub_rn(py, __fadd_rn(c.ay, c.aby))));
+    const float s = __fdiv_rn(__fsub_rn(__fmul_rn(c.abx, acy), __fmul_rn(c.aby, acx)), c.l2);
+    return fabsf(__fmul_rn(s, c.sl2));
 }
 
 __device__ __forceinline__ int key_x(uint32_t k) { return (int)(k >> 16); }
@@ -596,15 +618,16 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
                 for (int u = 0; u < kFewSegs; u++)
                     if (g >= pre[u] && g < pre[u + 1]) {
                         const int i = sg[u].x + 1 + (g - pre[u]);
-                        const unsigned long long key =
-                            dp_key(seg_dist((float)pts[i].x, (float)pts[i].y, (float)pts[sg[u].x].x, (float)pts[sg[u].x].y,
-                                            (float)pts[sg[u].y].x, (float)pts[sg[u].y].y),
-                                   i);
+                        const SegC c = seg_c((float)pts[sg[u].x].x, (float)pts[sg[u].x].y, (float)pts[sg[u].y].x,
+                                             (float)pts[sg[u].y].y);
+                        const unsigned long long key = dp_key(seg_dist(c, (float)pts[i].x, (float)pts[i].y), i);
                         bk[u] = key > bk[u] ? key : bk[u];
                     }
             }
+            // (only the level's nseg segments are reduced: nseg is the same for the whole block)
 #pragma unroll
             for (int u = 0; u < kFewSegs; u++) {
+                if (u >= nseg) break;
 #pragma unroll
                 for (int o = 16; o; o >>= 1) {
                     const unsigned long long ot = __shfl_xor_sync(0xffffffffu, bk[u], o);
@@ -616,6 +639,7 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
             if (warp == 0) {
 #pragma unroll
                 for (int u = 0; u < kFewSegs; u++) {
+                    if (u >= nseg) break;
                     unsigned long long v = lane < T / 32 ? s_wbest[u][lane] : 0ull;
 #pragma unroll
                     for (int o = 16; o; o >>= 1) {
@@ -666,8 +690,8 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
             }
             const int2 sg = sa[lo];
             const int i = sg.x + 1 + (g - pref[lo]);
-            const float d = seg_dist((float)pts[i].x, (float)pts[i].y, (float)pts[sg.x].x, (float)pts[sg.x].y,
-                                     (float)pts[sg.y].x, (float)pts[sg.y].y);
+            const SegC c = seg_c((float)pts[sg.x].x, (float)pts[sg.x].y, (float)pts[sg.y].x, (float)pts[sg.y].y);
+            const float d = seg_dist(c, (float)pts[i].x, (float)pts[i].y);
             atomicMax(best + lo, dp_key(d, i));
         }
         if (tid == 0) s_next = 0;

@@ -38,6 +38,7 @@ struct UmmaP {
     int64_t y_n = 0, y_pix = 0, ldy = 0;
     int out_vec = 0;              // 16-byte aligned output rows: float4 stores
     int tma_y = 0;                // y rows (M x N, 16-byte aligned) written by TMA tensor stores
+    uint32_t ntn_m = 1, ntn_l = 0;  // tile index / N tiles as a multiply-high and a shift (per launch)
     const float *res = nullptr;
     int64_t res_n = 0, res_pix = 0;
     int scatter = 0, scat_cout = 0;
