@@ -52,12 +52,13 @@ def parse():
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--cpu-sample", type=int, default=2, help="pages of the CPU-baseline sample")
     p.add_argument("--workload", default="pp4",
-                   choices=["pp4", "pp4ink", "ocrs2", "ocrs2ink", "det1", "rec0", "pp3", "ppdet4", "ppdb4", "pplines",
-                            "words1"],
+                   choices=["pp4", "pp4ink", "ocrs2", "ocrs2ink", "det1", "rec0", "pp3", "ctc3", "ppdet4", "ppdb4",
+                            "pplines", "words1"],
                    help="pp4 (default, the driver's line): config 4, the full PP-OCRv6 page pipeline (pp4ink: "
                         "with a hand-set ink detector, hundreds of lines a page); ocrs2: config 2, the full ocrs page "
                         "pipeline (ocrs2ink: with a hand-set ink detector, 36 lines a page); det1: config 1 detection; rec0 / "
-                        "pp3 / ppdet4: configs 0, 3 and 4 through their public calls; ppdb4: config 4 with the DB "
+                        "pp3 / ppdet4: configs 0, 3 and 4 through their public calls; ctc3: config 3's CTC head alone over "
+                        "all its steps' rows; ppdb4: config 4 with the DB "
                         "mask and box scores on the device; pplines: PP line extraction; words1: word rectangles "
                         "of config 1 detection masks (secondary measurements)")
     p.add_argument("--lanes", type=int, default=4,
@@ -738,6 +739,28 @@ def run_workload(args):
             logits = ref.run_onnx(model, data, stop_before_softmax=True)
             ref.argmax(logits.reshape(-1, logits.shape[-1]))
             return n, f"{n} lines (the narrowest batch)"
+    elif args.workload == "ctc3":
+        # the CTC head of config 3 (120 -> 18,709 with the fused arg-max, classes only as the
+        # reference's argmax) once over the rows of all 16 width batches (sum of lines x steps)
+        batches, _ = synth.pp_batches(synth.pp_lines(2, n=256))
+        rows = sum(n_ * (w_ // 8) for _, n_, w_ in batches)
+        b_ = synth._Builder(2)
+        model = b_.model("x", b_.linear("x", 120, 18709))
+        handle = wocr.NdGraph(gpu, model)
+        xin = pinned(np.random.default_rng(5).standard_normal((1, rows, 120)).astype(np.float32))
+        units, unit, workload = rows, "rows/s", (f"config 3 CTC head alone: Linear 120 -> 18709 (random init, seed 2) "
+                                                 f"with the fused row arg-max over {rows} rows (the 256 lines' steps "
+                                                 f"of all width batches at once), classes read back")
+        h2d, d2h = xin.nbytes, rows * 8
+
+        def step():
+            handle.argmax(xin, lse=False)
+
+        def cpu():
+            sub = np.ascontiguousarray(xin[:, :512])
+            logits = ref.run_onnx(model, sub)
+            ref.argmax(logits.reshape(-1, logits.shape[-1]))
+            return 512, "512 rows through the CPU oracle (matmul + arg-max)"
     elif args.workload == "pplines":
         handle = None
         npg = 12

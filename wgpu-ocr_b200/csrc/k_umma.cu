@@ -230,6 +230,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long bud = p.budget > 0 ? p.budget : kWaitBudget;  // every wait's clock budget
     const int nk = p.Kpad / BK;
     const int ntn = (p.N + BN - 1) / BN;
     const int64_t ntiles = ((p.M + BM - 1) / BM) * ntn;
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     load_pair(r, kb2, nxt);
                 }
                 const int s = it % STAGES;
-                if (!warp_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 11)) break;
+                if (!warp_wait(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 11, bud)) break;
                 uint8_t *rhi = smem + s * Lay::stage_bytes + (row >> 3) * 1024 + (row & 7) * 128;
                 uint8_t *rlo = rhi + Smem::a_bytes;
 #pragma unroll
@@ -313,7 +314,8 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 }
                 fence_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&afull[s]);  // one arrival per warp
+                // (a wait test leaves the first stage without its arrivals)
+                if (lane == 0 && !(p.test_stall && it == 0)) mbar_arrive(&afull[s]);  // one arrival per warp
                 it++;
                 if (!more) break;
                 t = t2;
@@ -333,7 +335,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 const int n0 = (int)((uint32_t)t - tile_row(p, t) * (uint32_t)ntn) * BN;
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % STAGES;
-                    if (!mbar_wait_spin(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 12)) {
+                    if (!mbar_wait_spin(&empty[s], ((it / STAGES) & 1) ^ 1, p.status, abort_flag, 12, bud)) {
                         ok = false;
                         break;
                     }
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             // drain: the last STAGES issued copies land before the CTA may exit (bounded)
             for (int j = (it > STAGES ? it - STAGES : 0); j < it; j++) {
                 long long t0 = clock64();
-                while (!mbar_try(&bfull[j % STAGES], (j / STAGES) & 1) && clock64() - t0 < kWaitBudget) {
+                while (!mbar_try(&bfull[j % STAGES], (j / STAGES) & 1) && clock64() - t0 < bud) {
                 }
             }
         }
@@ -360,14 +362,14 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, lt++) {
                 const int ab = lt % NACC;
                 const uint32_t dcol = tmem + ab * TCOLS;
-                ok = mbar_wait_spin(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 16);
+                ok = mbar_wait_spin(&tempty[ab], ((lt / NACC) & 1) ^ 1, p.status, abort_flag, 16, bud);
                 if (!ok) break;
                 tc_fence_after();
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % STAGES;
                     const uint32_t par = (it / STAGES) & 1;
-                    ok = mbar_wait_spin(&afull[s], par, p.status, abort_flag, 13) &&
-                         mbar_wait_spin(&bfull[s], par, p.status, abort_flag, 14);
+                    ok = mbar_wait_spin(&afull[s], par, p.status, abort_flag, 13, bud) &&
+                         mbar_wait_spin(&bfull[s], par, p.status, abort_flag, 14, bud);
                     if (!ok) break;
                     tc_fence_after();
                     uint8_t *base = smem + s * Lay::stage_bytes;
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             // every issued MMA completes before the shared and tensor memory go away (bounded)
             umma_commit(drain);
             long long t0 = clock64();
-            while (!mbar_try(drain, 0) && clock64() - t0 < kWaitBudget) {
+            while (!mbar_try(drain, 0) && clock64() - t0 < bud) {
             }
         }
     } else {
@@ -425,7 +427,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 eb[j] = p.bias && col < p.N ? p.bias[bc] : 0.f;
             }
             __syncwarp();
-            if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 15)) break;
+            if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 15, bud)) break;
             tc_fence_after();
             int ox = 0, oy = 0, nb = 0;
             int64_t pix = 0;
@@ -722,6 +724,8 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
         WOCR_CUDA(cudaMemsetAsync(c->status, 0, 16, c->stream));
     }
     p.status = c->status;
+    if (const char *b = std::getenv("WOCR_WAIT_BUDGET")) p.budget = std::atoll(b);
+    p.test_stall = std::getenv("WOCR_TEST_STALL_FIRST_STAGE") != nullptr;
     const bool al = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0;
     p.out_vec = p.mode == 1 ? (al && p.y_pix % 4 == 0 && p.y_n % 4 == 0) : (al && p.ldy % 4 == 0);
     // TMA tensor stores of the output: rows of y at a fixed stride (a convolution's pixels
@@ -736,7 +740,10 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
     p.Kpad = w.Kpad;
     p.N = w.N;
     double flops = 2.0 * (double)p.M * w.N * w.K;
-    double bytes = 4.0 * ((double)p.M * w.K / (p.mode == 1 ? (double)p.kh * p.kw : 1.0) + (double)p.M * w.N) +
+    // fp32 A (its pixels once for a convolution), the output (or the arg-max partials: 12 bytes a
+    // slot), the split weights (4 bytes a weight)
+    const double out_bytes = p.part_max ? 12.0 * (double)p.M * p.part_ld : 4.0 * (double)p.M * w.N;
+    double bytes = 4.0 * (double)p.M * w.K / (p.mode == 1 ? (double)p.kh * p.kw : 1.0) + out_bytes +
                    4.0 * (double)w.N * w.Kpad;
     Prof pf(c, p.scatter ? "umma_convt" : (p.mode == 1 ? "umma_conv" : "umma_linear"), flops, bytes);
     // few row tiles (short inputs): 64- or 32-column tiles put more SMs on the launch, with the

@@ -84,11 +84,11 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t *bar, uint32_t parity) {
 // Bounded wait: false (and an error code in *status) when the budget runs out or another role
 // has already given up.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
-                                          int code) {
+                                          int code, long long budget = kWaitBudget) {
     long long t0 = clock64();
     while (!mbar_try_sleep(bar, parity)) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitBudget) {
+        if (clock64() - t0 > budget) {
             *abort_flag = 1;
             atomicCAS(status, 0, code);
             return false;
@@ -115,12 +115,12 @@ __device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
 // limit passes) instead of a test_wait spin whose instructions take issue slots from the
 // epilogue warps on the same scheduler; bounded alike.
 __device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
-                                               int code) {
+                                               int code, long long budget = kWaitBudget) {
     if (mbar_test(bar, parity)) return true;
     long long t0 = clock64();
     while (!mbar_try(bar, parity)) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > kWaitBudget) {
+        if (clock64() - t0 > budget) {
             *abort_flag = 1;
             atomicCAS(status, 0, code);
             return false;
@@ -131,9 +131,9 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t *bar, uint32_t parity, i
 
 // One lane polls, the warp follows: a warp-uniform outcome for warp-wide code after the wait.
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int *status, volatile int *abort_flag,
-                                          int code) {
+                                          int code, long long budget = kWaitBudget) {
     int ok = 1;
-    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, abort_flag, code);
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, status, abort_flag, code, budget);
     return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 

@@ -39,6 +39,10 @@ struct UmmaP {
     int out_vec = 0;              // 16-byte aligned output rows: float4 stores
     int tma_y = 0;                // y rows (M x N, 16-byte aligned) written by TMA tensor stores
     uint32_t ntn_m = 1, ntn_l = 0;  // tile index / N tiles as a multiply-high and a shift (per launch)
+    // tests of the bounded waits: a budget in clock cycles (0: the default of about 2 s) and a
+    // first A stage whose producers do not arrive (its wait then runs out)
+    long long budget = 0;
+    int test_stall = 0;
     const float *res = nullptr;
     int64_t res_n = 0, res_pix = 0;
     int scatter = 0, scat_cout = 0;
