@@ -13,7 +13,7 @@
 //   3. a foreground component is external (its outer border's parent is the frame) exactly when
 //      the background left of that pixel belongs to the frame's component (or the pixel is in
 //      column 0);
-//   4. one thread per external component follows its outer border from that pixel with
+//   4. one warp per external component follows its outer border from that pixel with
 //      Algorithm 1's steps (3.1)-(3.5) (count, then write); a block per component then runs
 //      Douglas-Peucker, the convex hull and the minimum-area rectangle on its points.
 // Every floating-point step uses the round-to-nearest intrinsics in the order of the C
@@ -312,93 +312,118 @@ __global__ void k_ext_list(const int *__restrict__ run_x, const uint8_t *__restr
 
 // ---- border following ------------------------------------------------------------------------
 
-// Columns wx0 .. wx0 + 31 of row y as bits (pixels off the page read 0).
-__device__ __forceinline__ uint32_t row_win(const uint32_t *m, int words, int w, int h, int y, int wx0) {
-    if ((unsigned)y >= (unsigned)h) return 0u;
+// Columns wx0 .. wx0 + 63 of row y as bits (pixels off the page read 0).
+__device__ __forceinline__ uint64_t row_win64(const uint32_t *m, int words, int w, int h, int y, int wx0) {
+    if ((unsigned)y >= (unsigned)h) return 0ull;
     const uint32_t *row = m + (int64_t)y * words;
     const int j = wx0 >> 5;  // floor, also for wx0 < 0
-    const uint32_t lo = (unsigned)j < (unsigned)words ? __ldg(row + j) : 0u;
-    const uint32_t hi = (unsigned)(j + 1) < (unsigned)words ? __ldg(row + j + 1) : 0u;
-    uint32_t v = __funnelshift_r(lo, hi, wx0 & 31);
+    const uint32_t a = (unsigned)j < (unsigned)words ? __ldg(row + j) : 0u;
+    const uint32_t b = (unsigned)(j + 1) < (unsigned)words ? __ldg(row + j + 1) : 0u;
+    const uint32_t c = (unsigned)(j + 2) < (unsigned)words ? __ldg(row + j + 2) : 0u;
+    uint64_t v = ((uint64_t)__funnelshift_r(b, c, wx0 & 31) << 32) | __funnelshift_r(a, b, wx0 & 31);
     const int valid = w - wx0;
-    if (valid < 32) v &= valid <= 0 ? 0u : (1u << valid) - 1u;
+    if (valid < 64) v &= valid <= 0 ? 0ull : (1ull << valid) - 1ull;
     return v;
 }
 
-// Algorithm 1 (3.1)-(3.5) from the outer-border start (x, y) entered from its left neighbour:
-// the number of border points; with WRITE, the points go to out.  The rows y - 1 .. y + 1 of the
-// current point, columns wx0 .. wx0 + 31, stay in registers: a step down or up loads one row, a
-// step that leaves the columns reloads the three.  (3.1) takes the first set neighbour clockwise
-// from the left one, (3.3) the first counterclockwise from the one after the previous point: a
-// rotate of the 8 neighbour bits (bit d = neighbour d) and a leading-zero count.  A border is at
-// most 4 points a pixel; past that the status word is set and the trace stops.
-// Points are written to out while their index is below wcap (0: count only).
-__device__ int follow(const uint32_t *m, int words, int w, int h, int x, int y, short2 *out, int wcap, int *status) {
-    int wx0 = x - 16;
-    uint32_t up = row_win(m, words, w, h, y - 1, wx0), mid = row_win(m, words, w, h, y, wx0),
-             dn = row_win(m, words, w, h, y + 1, wx0);
-    auto nbits = [&](int xx) -> uint32_t {
-        const int b = xx - 1 - wx0;
-        const uint32_t u = up >> b & 7u, c = mid >> b & 7u, d = dn >> b & 7u;
-        return (c & 1u) | (u & 1u) << 1 | (u >> 1 & 1u) << 2 | (u >> 2 & 1u) << 3 | (c >> 2 & 1u) << 4 |
-               (d >> 2 & 1u) << 5 | (d >> 1 & 1u) << 6 | (d & 1u) << 7;
+// Step (3.3)-(3.4) of Algorithm 1 as a table: for the direction e from the current point back to
+// the previous one and the 3 x 3 block around the current point (bits 0-2 the row above, 3-5 its
+// own row, 6-8 the row below, each left to right), the first set neighbour counterclockwise from
+// e - 1: (dx + 1) | (dy + 1) << 2 | (its direction back to the current point) << 4, or 0x80 when
+// no neighbour is set.
+struct StepLut {
+    uint8_t v[8 * 512];
+};
+
+constexpr StepLut make_step_lut() {
+    StepLut t{};
+    for (int e = 0; e < 8; e++)
+        for (int b = 0; b < 512; b++) {
+            const uint32_t u = b & 7, c = b >> 3 & 7, d = b >> 6 & 7;
+            const uint32_t nb = (c & 1u) | (u & 1u) << 1 | (u >> 1 & 1u) << 2 | (u >> 2 & 1u) << 3 |
+                                (c >> 2 & 1u) << 4 | (d >> 2 & 1u) << 5 | (d >> 1 & 1u) << 6 | (d & 1u) << 7;
+            int d4 = -1;
+            for (int k = 1; k <= 8 && d4 < 0; k++)
+                if (nb >> ((e - k) & 7) & 1u) d4 = (e - k) & 7;
+            t.v[e * 512 + b] = d4 < 0 ? (uint8_t)0x80
+                                      : (uint8_t)((kNbX >> (2 * d4) & 3u) | (kNbY >> (2 * d4) & 3u) << 2 |
+                                                  (uint32_t)((d4 + 4) & 7) << 4);
+        }
+    return t;
+}
+
+__constant__ StepLut kStep = make_step_lut();
+
+// Algorithm 1 (3.1)-(3.5) from the outer-border start (x, y) entered from its left neighbour,
+// run by a whole warp: the number of border points, the points written to out while their index
+// is below wcap (0: count only).  The warp holds a 32-row x 64-column window of the mask, lane l
+// row wy0 + l, in registers; every lane runs the same steps, and the three neighbour rows of the
+// current point come from their lanes by shuffles, so a step reads no memory until the point
+// leaves the window (then every lane loads its row of a window re-centred on it, in parallel).
+// (3.1) takes the first set neighbour clockwise from the left one, (3.3) the first
+// counterclockwise from the one after the previous point (StepLut).  A border is at most 4 points
+// a pixel; past that the status word is set and the trace stops.  Must be called by all 32 lanes
+// of a warp.
+__device__ int follow_warp(const uint32_t *m, int words, int w, int h, int x, int y, short2 *out, int wcap,
+                           int *status) {
+    const int lane = threadIdx.x & 31;
+    int wx0 = x - 32, wy0 = y - 16;
+    uint64_t win = row_win64(m, words, w, h, wy0 + lane, wx0);
+    // the 3 x 3 block around (xx, yy) (StepLut's bit order): xx - 1 - wx0 in 0 .. 61, yy - wy0 in 1 .. 30
+    auto block = [&](int xx, int yy) -> uint32_t {
+        const uint32_t t = (uint32_t)(win >> (xx - 1 - wx0)) & 7u;
+        const int r = yy - wy0;
+        const uint32_t u = __shfl_sync(0xffffffffu, t, r - 1), c = __shfl_sync(0xffffffffu, t, r),
+                       d = __shfl_sync(0xffffffffu, t, r + 1);
+        return u | c << 3 | d << 6;
     };
-    uint32_t nb = nbits(x);
-    if (nb == 0) {
-        if (wcap > 0) out[0] = make_short2((short)x, (short)y);
+    uint32_t blk = block(x, y);
+    // (3.1): the first set neighbour clockwise from the left one (bit d = neighbour d)
+    const uint32_t nb0 = (blk >> 3 & 1u) | (blk & 1u) << 1 | (blk >> 1 & 1u) << 2 | (blk >> 2 & 1u) << 3 |
+                         (blk >> 5 & 1u) << 4 | (blk >> 8 & 1u) << 5 | (blk >> 7 & 1u) << 6 | (blk >> 6 & 1u) << 7;
+    if (nb0 == 0) {
+        if (wcap > 0 && lane == 0) out[0] = make_short2((short)x, (short)y);
         return 1;
     }
-    const int d1 = __ffs(nb) - 1;
+    const int d1 = __ffs(nb0) - 1;
     const int x1 = x + nb_dx(d1), y1 = y + nb_dy(d1);
     int x3 = x, y3 = y, e = d1, n = 0;
     const int64_t cap = 4 * (int64_t)w * h + 8;
     for (;;) {
-        if (n < wcap) out[n] = make_short2((short)x3, (short)y3);
+        if (lane == 0 && n < wcap) out[n] = make_short2((short)x3, (short)y3);
         n++;
-        // counterclockwise from e - 1: bit t -> 7, t - 1 -> 6, ...; the first set is the highest
-        const int t = (e - 1) & 7;
-        const uint32_t rot = ((nb << (7 - t)) | (nb >> (t + 1))) & 0xffu;
-        if (rot == 0u || n >= cap) {  // the previous point is always set: a broken mask read
-            atomicExch(status, 40);
+        const uint32_t v = kStep.v[e << 9 | blk];
+        if ((v & 0x80u) || n >= cap) {  // the previous point is always set: a broken mask read
+            if (lane == 0) atomicExch(status, 40);
             break;
         }
-        const int d4 = (t - (7 - (31 - __clz(rot)))) & 7;
-        const int x4 = x3 + nb_dx(d4), y4 = y3 + nb_dy(d4);
+        const int x4 = x3 + (int)(v & 3u) - 1, y4 = y3 + (int)(v >> 2 & 3u) - 1;
         if (x4 == x && y4 == y && x3 == x1 && y3 == y1) break;
-        e = (d4 + 4) & 7;  // from the new (i3, j3) back to the old one
-        if (x4 - 1 < wx0 || x4 + 1 > wx0 + 31) {
-            wx0 = x4 - 16;
-            up = row_win(m, words, w, h, y4 - 1, wx0);
-            mid = row_win(m, words, w, h, y4, wx0);
-            dn = row_win(m, words, w, h, y4 + 1, wx0);
-        } else if (y4 > y3) {
-            up = mid;
-            mid = dn;
-            dn = row_win(m, words, w, h, y4 + 1, wx0);
-        } else if (y4 < y3) {
-            dn = mid;
-            mid = up;
-            up = row_win(m, words, w, h, y4 - 1, wx0);
+        e = (int)(v >> 4);  // from the new (i3, j3) back to the old one
+        if (x4 - 1 < wx0 || x4 + 1 > wx0 + 63 || y4 - 1 < wy0 || y4 + 1 > wy0 + 31) {
+            wx0 = x4 - 32;
+            wy0 = y4 - 16;
+            win = row_win64(m, words, w, h, wy0 + lane, wx0);
         }
         x3 = x4;
         y3 = y4;
-        nb = nbits(x3);
+        blk = block(x3, y3);
     }
     return n;
 }
 
-// A warp per component, lane 0 tracing: lanes of one warp would wait on each other's loads.  The
-// first cache_cap points go to the component's cache slot, so borders no longer than that are
-// not followed a second time.
+// A warp per component.  The first cache_cap points go to the component's cache slot, so borders
+// no longer than that are not followed a second time.
 __global__ void __launch_bounds__(32) k_trace_len(const uint32_t *__restrict__ mask, int words, int w, int h,
                                                   const int *__restrict__ run_x, const int *__restrict__ run_row,
                                                   const int *__restrict__ comp_run, int C, int *__restrict__ len,
                                                   short2 *__restrict__ cache, int cache_cap, int *status) {
     const int k = blockIdx.x;
-    if (k >= C || threadIdx.x != 0) return;
+    if (k >= C) return;
     const int r = comp_run[k], row = run_row[r];
     const uint32_t *m = mask + (int64_t)(row / h) * h * words;
-    len[k] = follow(m, words, w, h, run_x[r], row % h, cache + (int64_t)k * cache_cap, cache_cap, status);
+    const int n = follow_warp(m, words, w, h, run_x[r], row % h, cache + (int64_t)k * cache_cap, cache_cap, status);
+    if (threadIdx.x == 0) len[k] = n;
 }
 
 // Block sizes of k_word_rect: components of more than kBigLen border points get kWTBig threads.
@@ -534,18 +559,23 @@ __device__ __forceinline__ unsigned long long dp_key(float d, int i) {
     return ((unsigned long long)__float_as_uint(d) << 32) | (0xffffffffu - (uint32_t)i);
 }
 
-// a point strictly inside the octagon of extreme points cannot be a hull vertex
+// The octagon of extreme points (in x, y, x + y, x - y) has points of the set on the hull as its
+// vertices, so a point of the closed octagon that is not one of its vertices lies strictly inside
+// the hull or on a hull edge strictly between two hull points, and the monotone chain (which
+// drops collinear points) never returns it.  (A degenerate, collinear octagon keeps its two ends.)
 __device__ __forceinline__ bool in_octagon(const uint32_t *oct, int noct, uint32_t q) {
     if (noct < 3) return false;
     for (int i = 0; i < 8; i++) {
         const uint32_t a = oct[i], b = oct[(i + 1) & 7];
+        if (q == a) return false;
         if (a == b) continue;
-        if (cross3(a, b, q) <= 0) return false;
+        if (cross3(a, b, q) < 0) return false;
     }
     return true;
 }
 
-// One block per external component: border following (one thread), Douglas-Peucker by levels
+// One block per external component: border following (one warp, when the length pass could not
+// keep the border), Douglas-Peucker by levels
 // (every point of every open segment at once, argmax per segment by a 64-bit atomicMax: the
 // largest distance, then the smallest index, as the sequential search finds it), the hull of
 // the kept points (octagon filter, sort, monotone chain) and the minimum-area rectangle (an
@@ -570,21 +600,21 @@ __global__ void __launch_bounds__(T) k_word_rect(WordP p) {
         const short2 *src = p.cache + (int64_t)k * p.cache_cap;
         for (int i = tid; i < L; i += T) pts[i] = src[i];
     }
-    if (tid == 0) {
+    if (warp == 0) {
         int nb = L;
-        if (L <= p.cache_cap) {
-            pts[nb] = p.cache[(int64_t)k * p.cache_cap];
-        } else {
+        if (L > p.cache_cap) {
             const uint32_t *m = p.mask + (int64_t)(row / p.h) * p.h * p.words;
-            nb = follow(m, p.words, p.w, p.h, p.run_x[r], row % p.h, pts, 0x7fffffff, p.status);
-            pts[nb] = pts[0];
+            nb = follow_warp(m, p.words, p.w, p.h, p.run_x[r], row % p.h, pts, 0x7fffffff, p.status);
         }
-        s_n = nb + 1;
-        s_nseg = 0;
-        if (nb + 1 > 2) {
-            p.seg_a[base] = make_int2(0, nb);
-            s_few[0][0] = make_int2(0, nb);
-            s_nseg = 1;
+        if (lane == 0) {
+            pts[nb] = L > p.cache_cap ? pts[0] : p.cache[(int64_t)k * p.cache_cap];
+            s_n = nb + 1;
+            s_nseg = 0;
+            if (nb + 1 > 2) {
+                p.seg_a[base] = make_int2(0, nb);
+                s_few[0][0] = make_int2(0, nb);
+                s_nseg = 1;
+            }
         }
     }
     __syncthreads();
