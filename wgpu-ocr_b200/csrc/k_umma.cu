@@ -212,7 +212,8 @@ __device__ __forceinline__ uint32_t tile_row(const UmmaP &p, int64_t t) {
 template <int BN, int STAGES, int CHAINS>
 __global__ void __launch_bounds__(kAllThreads, 1)
     k_umma(const __grid_constant__ CUtensorMap tm_hi, const __grid_constant__ CUtensorMap tm_lo,
-           const __grid_constant__ CUtensorMap tm_y, UmmaP p) {
+           const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_ahi,
+           const __grid_constant__ CUtensorMap tm_alo, UmmaP p) {
     using Lay = Layout<BN, STAGES>;
     // CHAINS: accumulation chains per tile (0: Acc<BN>'s choice); one chain sums in the order of
     // the 128- and 256-column tiles, so a narrowed launch gives their results to the bit
@@ -267,6 +268,9 @@ __global__ void __launch_bounds__(kAllThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp < kProdWarps) {
+        if (p.a_tma) {
+            // A arrives pre-split with the weights (the TMA warp): nothing to build
+        } else {
         // ---------------- A producers: four threads per tile row, 2 chunks of 8 k each ----------------
         // Software-pipelined: the loads of the next k block are issued before waiting for a free
         // stage and converting the current one, so two k blocks of loads are in flight.
@@ -326,8 +330,9 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     for (int e = 0; e < 8; e++) cur[c][e] = nxt[c][e];
             }
         }
+        }
     } else if (warp == kTmaWarp) {
-        // ---------------- B loader: TMA of the pre-split weight tiles ----------------
+        // ---------------- B loader: TMA of the pre-split weight tiles (and of A, pre-split) ----------------
         if (lane == 0) {
             int it = 0;
             bool ok = true;
@@ -341,9 +346,15 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                     }
                     uint8_t *bhi = smem + s * Lay::stage_bytes + 2 * Smem::a_bytes;
                     uint8_t *blo = bhi + Lay::b_bytes;
-                    mbar_expect_tx(&bfull[s], 2 * Lay::b_bytes);
+                    mbar_expect_tx(&bfull[s], 2 * Lay::b_bytes + (p.a_tma ? 2 * Smem::a_bytes : 0));
                     tma_load_2d(bhi, &tm_hi, &bfull[s], kb * BK, n0);
                     tma_load_2d(blo, &tm_lo, &bfull[s], kb * BK, n0);
+                    if (p.a_tma) {  // the tile's rows, in the layout the producers would write
+                        uint8_t *ahi = smem + s * Lay::stage_bytes;
+                        const int m0 = (int)(tile_row(p, t) * BM);
+                        tma_load_2d(ahi, &tm_ahi, &bfull[s], kb * BK, m0);
+                        tma_load_2d(ahi + Smem::a_bytes, &tm_alo, &bfull[s], kb * BK, m0);
+                    }
                 }
             }
             // drain: the last STAGES issued copies land before the CTA may exit (bounded)
@@ -368,7 +379,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                 for (int kb = 0; kb < nk; kb++, it++) {
                     const int s = it % STAGES;
                     const uint32_t par = (it / STAGES) & 1;
-                    ok = mbar_wait_spin(&afull[s], par, p.status, abort_flag, 13, bud) &&
+                    ok = (p.a_tma || mbar_wait_spin(&afull[s], par, p.status, abort_flag, 13, bud)) &&
                          mbar_wait_spin(&bfull[s], par, p.status, abort_flag, 14, bud);
                     if (!ok) break;
                     tc_fence_after();
@@ -490,28 +501,28 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                             if (n0 + c0 + j >= p.N) o[j] = -INFINITY;
                     }
                     if (ci < nck) {
-                        // pass 1: the chunk's maximum and first column by a 4-level select tree
-                        // (the right side wins only when strictly greater), then against the row's
+                        // pass 1: the chunk's maximum by a tree of fmaxf (NaN never wins, as K30's
+                        // search from -inf); only a chunk that beats the row's maximum so far looks
+                        // for its first column holding that value (an earlier column keeps a tie)
                         float m8[8];
-                        int i8[8];
 #pragma unroll
-                        for (int t = 0; t < 8; t++) {
-                            const bool g = o[2 * t + 1] > o[2 * t];
-                            m8[t] = g ? o[2 * t + 1] : o[2 * t];
-                            i8[t] = 2 * t + (g ? 1 : 0);
-                        }
+                        for (int t = 0; t < 8; t++) m8[t] = fmaxf(o[2 * t], o[2 * t + 1]);
 #pragma unroll
                         for (int w = 4; w >= 1; w >>= 1) {
 #pragma unroll
-                            for (int t = 0; t < w; t++) {
-                                const bool g = m8[2 * t + 1] > m8[2 * t];
-                                m8[t] = g ? m8[2 * t + 1] : m8[2 * t];
-                                i8[t] = g ? i8[2 * t + 1] : i8[2 * t];
-                            }
+                            for (int t = 0; t < w; t++) m8[t] = fmaxf(m8[2 * t], m8[2 * t + 1]);
                         }
                         if (m8[0] > amx) {
-                            amx = m8[0];
-                            aidx = (uint32_t)(n0 + c0 + i8[0]);
+                            int first = 15;
+                            float fv = o[15];  // the value itself (a zero keeps its sign)
+#pragma unroll
+                            for (int j = 14; j >= 0; j--)
+                                if (o[j] == m8[0]) {
+                                    first = j;
+                                    fv = o[j];
+                                }
+                            amx = fv;
+                            aidx = (uint32_t)(n0 + c0 + first);
                         }
                     } else {
                         // pass 2: exponentials against the row's maximum, e^(o - max) as
@@ -617,6 +628,23 @@ __global__ void __launch_bounds__(kAllThreads, 1)
     }
 }
 
+// A (mode 0, fp32 [M][lda]) as the producers split it: per row, bf16 hi = bf16(v) and lo =
+// bf16(v - hi) of the first K values, zeros up to Kpad; a thread per 8 values.
+__global__ void k_split_rows(const float *__restrict__ x, int64_t lda, int64_t M, int K, int Kpad,
+                             uint4 *__restrict__ hi, uint4 *__restrict__ lo) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, per = Kpad / 8;
+    if (g >= M * per) return;
+    const int64_t m = g / per;
+    const int k0 = (int)(g - m * per) * 8;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = k0 + i < K ? __ldg(x + m * lda + k0 + i) : 0.f;
+    uint4 h, l;
+    split8(v, h, l);
+    hi[g] = h;
+    lo[g] = l;
+}
+
 // ---- host side ------------------------------------------------------------------------------
 
 // The output map of a TMA-store epilogue: fp32 [M][N] rows `stride` floats apart, 16 x 32 boxes
@@ -647,7 +675,8 @@ void make_map(CUtensorMap *map, void *base, int N, int Kpad, int bn) {
 }
 
 template <int BN, int STAGES, int CHAINS = 0>
-void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const CUtensorMap &map_y, const UmmaP &p) {
+void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const CUtensorMap &map_y, const UmmaP &p,
+            const CUtensorMap &map_ahi = CUtensorMap{}, const CUtensorMap &map_alo = CUtensorMap{}) {
     using Lay = Layout<BN, STAGES>;
     static std::atomic<bool> set[64];
     if (!set[c->device]) {
@@ -662,7 +691,7 @@ void launch(Ctx *c, const CUtensorMap &map_hi, const CUtensorMap &map_lo, const 
     q.ntn_m = fd.m;
     q.ntn_l = fd.l;
     unsigned grid = (unsigned)std::min<int64_t>(tiles, c->sm_count);
-    k_umma<BN, STAGES, CHAINS><<<grid, kAllThreads, Lay::total, c->stream>>>(map_hi, map_lo, map_y, q);
+    k_umma<BN, STAGES, CHAINS><<<grid, kAllThreads, Lay::total, c->stream>>>(map_hi, map_lo, map_y, map_ahi, map_alo, q);
     WOCR_LAUNCHED(c);
 }
 
@@ -767,12 +796,29 @@ void umma_gemm(Ctx *c, const UmmaW &w, UmmaP p) {
             return;
         }
     }
+    // Many N tiles over the same rows (the CTC head: 74): the producers would split each A tile
+    // once per N tile; instead A is split once into bf16 hi / lo rows and the TMA warp loads the
+    // tiles with the weights' (same 128-byte swizzled K-major layout, zeros past M and K)
+    CUtensorMap mahi{}, malo{};
+    BufP ahi, alo;
+    if (p.mode == 0 && !p.test_stall && umma_ntiles(w) >= 8 && p.M >= BM && !std::getenv("WOCR_NO_A_TMA")) {
+        const size_t abytes = (size_t)p.M * w.Kpad * 2;
+        ahi = alloc(c, abytes);
+        alo = alloc(c, abytes);
+        const int64_t n8 = p.M * (w.Kpad / 8);
+        k_split_rows<<<(unsigned)((n8 + 255) / 256), 256, 0, c->stream>>>(p.x, p.lda, p.M, w.K, w.Kpad,
+                                                                          (uint4 *)ahi->p, (uint4 *)alo->p);
+        WOCR_LAUNCHED(c);
+        make_map(&mahi, ahi->p, (int)p.M, w.Kpad, BM);
+        make_map(&malo, alo->p, (int)p.M, w.Kpad, BM);
+        p.a_tma = 1;
+    }
     switch (w.bn) {
-    case 16: launch<16, 5>(c, w.map_hi, w.map_lo, my, p); break;
-    case 32: launch<32, 5>(c, w.map_hi, w.map_lo, my, p); break;
-    case 64: launch<64, 4>(c, w.map_hi, w.map_lo, my, p); break;
-    case 128: launch<128, 3>(c, w.map_hi, w.map_lo, my, p); break;
-    default: launch<256, 2>(c, w.map_hi, w.map_lo, my, p); break;
+    case 16: launch<16, 5>(c, w.map_hi, w.map_lo, my, p, mahi, malo); break;
+    case 32: launch<32, 5>(c, w.map_hi, w.map_lo, my, p, mahi, malo); break;
+    case 64: launch<64, 4>(c, w.map_hi, w.map_lo, my, p, mahi, malo); break;
+    case 128: launch<128, 3>(c, w.map_hi, w.map_lo, my, p, mahi, malo); break;
+    default: launch<256, 2>(c, w.map_hi, w.map_lo, my, p, mahi, malo); break;
     }
     c->flops += flops;
 }

@@ -38,6 +38,7 @@ struct UmmaP {
     int64_t y_n = 0, y_pix = 0, ldy = 0;
     int out_vec = 0;              // 16-byte aligned output rows: float4 stores
     int tma_y = 0;                // y rows (M x N, 16-byte aligned) written by TMA tensor stores
+    int a_tma = 0;                // mode 0: A pre-split into bf16 hi / lo rows, loaded by the TMA warp
     uint32_t ntn_m = 1, ntn_l = 0;  // tile index / N tiles as a multiply-high and a shift (per launch)
     // tests of the bounded waits: a budget in clock cycles (0: the default of about 2 s) and a
     // first A stage whose producers do not arrive (its wait then runs out)
