@@ -464,6 +464,67 @@ __global__ void __launch_bounds__(kAllThreads, 1)
             const bool amax = BN >= 64 && p.part_max;  // arg-max partials (64-column tiles or wider)
             const int nck_all = amax && p.part_sum ? 2 * nck : nck;  // no sums wanted: pass 1 only
             const bool full_tile = n0 + BN <= p.N;
+            // a chunk's maximum by a tree of fmaxf (NaN never wins, as K30's search from -inf); only a
+            // chunk that beats the row's maximum so far looks for its first column holding that value
+            // (an earlier column keeps a tie)
+            auto amax_tree = [&](const float (&o)[16], int c0) {
+                float m8[8];
+#pragma unroll
+                for (int t = 0; t < 8; t++) m8[t] = fmaxf(o[2 * t], o[2 * t + 1]);
+#pragma unroll
+                for (int w = 4; w >= 1; w >>= 1) {
+#pragma unroll
+                    for (int t = 0; t < w; t++) m8[t] = fmaxf(m8[2 * t], m8[2 * t + 1]);
+                }
+                if (m8[0] > amx) {
+                    int first = 15;
+                    float fv = o[15];  // the value itself (a zero keeps its sign)
+#pragma unroll
+                    for (int j = 14; j >= 0; j--)
+                        if (o[j] == m8[0]) {
+                            first = j;
+                            fv = o[j];
+                        }
+                    amx = fv;
+                    aidx = (uint32_t)(n0 + c0 + first);
+                }
+            };
+            auto amax_chunk = [&](float (&o)[16], int c0) {
+                if (m >= p.M || n0 + c0 >= p.N) return;
+                add_bias16(o, eb + (c0 - ck0 * 16));
+                if (!full_tile) {
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (n0 + c0 + j >= p.N) o[j] = -INFINITY;
+                }
+                amax_tree(o, c0);
+            };
+            if (amax && !p.part_sum && NCH == 1) {
+                // classes and maxima only, one accumulation chain: two chunks' loads before one
+                // wait (a load and its wait are a round trip that the scheduler's two epilogue
+                // warps cannot hide)
+#pragma unroll 1
+                for (int ci = 0; ci < nck; ci += 2) {
+                    const int c0 = (ck0 + ci) * 16;
+                    uint32_t a[16], b[16];
+                    float va[16];
+                    tmem_ld16_async(trow + c0, a);
+                    if (ci + 1 < nck) {  // (warp-uniform)
+                        tmem_ld16_async(trow + c0 + 16, b);
+                        tmem_wait16x2(a, b);
+                    } else {
+                        tmem_wait16(a);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; j++) va[j] = __uint_as_float(a[j]);
+                    amax_chunk(va, c0);
+                    if (ci + 1 < nck) {
+#pragma unroll
+                        for (int j = 0; j < 16; j++) va[j] = __uint_as_float(b[j]);
+                        amax_chunk(va, c0 + 16);
+                    }
+                }
+            } else
 #pragma unroll 1
             for (int ci = 0; ci < nck_all; ci++) {
                 float v[16];
@@ -501,29 +562,7 @@ __global__ void __launch_bounds__(kAllThreads, 1)
                             if (n0 + c0 + j >= p.N) o[j] = -INFINITY;
                     }
                     if (ci < nck) {
-                        // pass 1: the chunk's maximum by a tree of fmaxf (NaN never wins, as K30's
-                        // search from -inf); only a chunk that beats the row's maximum so far looks
-                        // for its first column holding that value (an earlier column keeps a tie)
-                        float m8[8];
-#pragma unroll
-                        for (int t = 0; t < 8; t++) m8[t] = fmaxf(o[2 * t], o[2 * t + 1]);
-#pragma unroll
-                        for (int w = 4; w >= 1; w >>= 1) {
-#pragma unroll
-                            for (int t = 0; t < w; t++) m8[t] = fmaxf(m8[2 * t], m8[2 * t + 1]);
-                        }
-                        if (m8[0] > amx) {
-                            int first = 15;
-                            float fv = o[15];  // the value itself (a zero keeps its sign)
-#pragma unroll
-                            for (int j = 14; j >= 0; j--)
-                                if (o[j] == m8[0]) {
-                                    first = j;
-                                    fv = o[j];
-                                }
-                            amx = fv;
-                            aidx = (uint32_t)(n0 + c0 + first);
-                        }
+                        amax_tree(v, c0);  // pass 1
                     } else {
                         // pass 2: exponentials against the row's maximum, e^(o - max) as
                         // 2^(o log2(e) - max log2(e)) (exp(-inf) = 0 past N)
