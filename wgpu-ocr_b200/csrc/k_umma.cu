@@ -424,18 +424,27 @@ __global__ void __launch_bounds__(kAllThreads, 1)
         // pieces through the load/store unit (which bounds the epilogue)
         const bool tma_y = p.tma_y && !p.part_max && !p.scatter;
         int lt = 0;
+        int eb_n0_0 = -1, eb_n0_1 = -1;  // the N tile whose bias columns each slot holds
         for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x, lt++) {
             const int ab = lt % NACC;
             const uint32_t trow_i = tile_row(p, t);
             const int64_t m = (int64_t)trow_i * BM + row, qrow0 = m - lane;  // qrow0: the quadrant's first row
             const int n0 = (int)((uint32_t)t - trow_i * (uint32_t)ntn) * BN;
             // the tile's bias columns (scatter tiles: per output channel) into this warp's slot while
-            // the MMAs run, so no chunk below waits on a global load
+            // the MMAs run, so no chunk below waits on a global load.  A slot that already holds
+            // this N tile's columns is kept (a CTA whose tiles step by a multiple of the N tile
+            // count, as 148 CTAs over 74 N tiles, keeps one N tile): when the epilogue is what
+            // bounds the kernel, these loads would otherwise sit on every tile's path.
             float *eb = ebias + (lt & 1) * Lay::ecols;
-            for (int j = lane; j < nck * 16; j += 32) {
-                const int col = n0 + ck0 * 16 + j;
-                const int bc = p.scatter ? col % p.scat_cout : col;
-                eb[j] = p.bias && col < p.N ? p.bias[bc] : 0.f;
+            int &eb_n0 = (lt & 1) ? eb_n0_1 : eb_n0_0;
+            if (eb_n0 != n0) {
+                eb_n0 = n0;
+#pragma unroll 4
+                for (int j = lane; j < nck * 16; j += 32) {
+                    const int col = n0 + ck0 * 16 + j;
+                    const int bc = p.scatter ? col % p.scat_cout : col;
+                    eb[j] = p.bias && col < p.N ? p.bias[bc] : 0.f;
+                }
             }
             __syncwarp();
             if (!warp_wait(&tfull[ab], (lt / NACC) & 1, p.status, abort_flag, 15, bud)) break;
