@@ -113,6 +113,30 @@ def test_svtr_block(gpu):
     close(run_nd(gpu, m, x, stop=True), ref.run_onnx(m, x, stop_before_softmax=True))
 
 
+def test_linear_pre_split_rows(gpu, monkeypatch):
+    """A linear layer whose input rows are read by many N tiles (18,709 classes: 74 tiles of 256)
+    splits them once into bf16 hi / lo rows that the TMA engine loads; its results equal those of
+    the producer warps' own split (WOCR_NO_A_TMA) exactly: the output, and the fused arg-max's
+    classes, maxima and log-sum-exp.  The output also matches the oracle's fp32 GEMM."""
+    b = _Builder(15)
+    m = b.model("x", b.linear("x", 120, 18709))
+    x = rnd(1, 300, 120)
+    g = wocr.NdGraph(gpu, m)
+    try:
+        monkeypatch.setenv("WOCR_NO_GRAPH", "1")  # every call launches, reading the variable
+        out = g.run(x)
+        best, mx, lse, shape = g.argmax(x)
+        monkeypatch.setenv("WOCR_NO_A_TMA", "1")
+        out2 = g.run(x)
+        best2, mx2, lse2, shape2 = g.argmax(x)
+    finally:
+        g.close()
+    assert shape == shape2 == (1, 300, 18709)
+    assert np.array_equal(out, out2)
+    assert np.array_equal(best, best2) and np.array_equal(mx, mx2) and np.array_equal(lse, lse2)
+    close(out, ref.run_onnx(m, x), tol=5e-5)
+
+
 @pytest.mark.parametrize("classes", [37, 700, 1031])
 def test_linear_argmax_fused(gpu, classes, monkeypatch):
     """A final linear layer with the row arg-max in its epilogue (per N tile partials merged):
